@@ -1,0 +1,90 @@
+"""Loader for the sm_100a extension ``granite_switch_b200._C``.
+
+The extension is built in place (``python setup.py build_ext --inplace`` or
+``__graft_entry__.build()``). On a CUDA device every op in
+:mod:`granite_switch_b200.ops` calls it; when it is missing there, the op
+raises instead of silently running a slower PyTorch path.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+_lock = threading.Lock()
+_C = None
+_err_buffers: dict[int, torch.Tensor] = {}
+
+# Bits of the device error word (csrc/common.cuh, enum ErrorBits).
+ERR_GEMM_WAIT = 1 << 0
+ERR_ATTN_WAIT = 1 << 1
+ERR_PEER_WAIT = 1 << 2
+ERR_BAD_SHAPE = 1 << 3
+ERR_SHRINK_WAIT = 1 << 4
+
+
+class NativeExtensionMissing(RuntimeError):
+    pass
+
+
+def native():
+    """Return the loaded extension module, importing it on first use."""
+    global _C
+    if _C is None:
+        with _lock:
+            if _C is None:
+                try:
+                    from . import _C as mod  # type: ignore[attr-defined]
+                except ImportError as e:  # pragma: no cover - depends on build state
+                    raise NativeExtensionMissing(
+                        "granite_switch_b200._C is not built; run "
+                        "`python setup.py build_ext --inplace` in the repository root"
+                    ) from e
+                _C = mod
+    return _C
+
+
+def available() -> bool:
+    try:
+        native()
+        return True
+    except NativeExtensionMissing:
+        return False
+
+
+def err_buffer(device: torch.device) -> torch.Tensor:
+    """Per-device int32[4] word that bounded device waits report into.
+
+    Allocated on first use; call once per device before CUDA-graph capture.
+    """
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _err_buffers.get(idx)
+    if buf is None:
+        buf = torch.zeros(4, dtype=torch.int32, device=torch.device("cuda", idx))
+        _err_buffers[idx] = buf
+    return buf
+
+
+def read_errors(device: torch.device, clear: bool = True) -> int:
+    """Synchronise and return (optionally clearing) the device error word."""
+    buf = err_buffer(device)
+    val = int(buf[0].item())
+    if clear and val:
+        buf.zero_()
+    return val
+
+
+def check_errors(device: torch.device) -> None:
+    val = read_errors(device)
+    if val:
+        names = []
+        for bit, name in (
+            (ERR_GEMM_WAIT, "gemm-wait-timeout"),
+            (ERR_ATTN_WAIT, "attention-wait-timeout"),
+            (ERR_PEER_WAIT, "peer-wait-timeout"),
+            (ERR_BAD_SHAPE, "bad-shape"),
+            (ERR_SHRINK_WAIT, "shrink-wait-timeout"),
+        ):
+            if val & bit:
+                names.append(name)
+        raise RuntimeError(f"device kernels reported errors: {', '.join(names)} (0x{val:x})")

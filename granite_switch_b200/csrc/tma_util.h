@@ -1,0 +1,76 @@
+// Host-side helpers: TMA tensor-map encoding through the driver entry point
+// (so the extension does not link libcuda directly and still imports on a
+// machine without a GPU), plus argument checks shared by the launchers.
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+#include <string>
+
+namespace gsb {
+
+// Message building avoids <sstream>: the toolchain's libstdc++ differs from
+// the one loaded at run time, and iostream objects crossed that boundary badly.
+inline void gsb_str_append(std::string& s, const char* v) { s += v; }
+inline void gsb_str_append(std::string& s, const std::string& v) { s += v; }
+template <typename T>
+inline void gsb_str_append(std::string& s, const T& v) { s += std::to_string(v); }
+template <typename... Ts>
+inline std::string gsb_str(const Ts&... vs) {
+  std::string s;
+  (gsb_str_append(s, vs), ...);
+  return s;
+}
+
+#define GSB_CHECK(cond, ...)                                                     \
+  do {                                                                           \
+    if (!(cond)) {                                                               \
+      throw std::runtime_error(::gsb::gsb_str("granite_switch_b200: ", __VA_ARGS__, \
+                                              " (", __FILE__, ":", __LINE__, ")")); \
+    }                                                                            \
+  } while (0)
+
+#define GSB_CUDA_CHECK(expr)                                                  \
+  do {                                                                        \
+    cudaError_t _e = (expr);                                                  \
+    GSB_CHECK(_e == cudaSuccess, "CUDA error ", cudaGetErrorString(_e), " in " #expr); \
+  } while (0)
+
+inline PFN_cuTensorMapEncodeTiled_v12000 tma_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    GSB_CHECK(e == cudaSuccess && p != nullptr && q == cudaDriverEntryPointSuccess,
+              "cuTensorMapEncodeTiled is not available from the driver");
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with the given row
+// stride (elements). The box is [box_rows, box_cols]; box_cols * 2 bytes must
+// equal the swizzle span (128 B for SW128, 64 B for SW64).
+inline CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t cols,
+                                     uint64_t row_stride_elems, uint32_t box_cols,
+                                     uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  GSB_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
+  GSB_CHECK((row_stride_elems * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = tma_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr),
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  GSB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r, " rows=",
+            rows, " cols=", cols, " box=", box_rows, "x", box_cols);
+  return m;
+}
+
+}  // namespace gsb

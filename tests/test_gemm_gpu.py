@@ -1,0 +1,115 @@
+"""tcgen05 switched GEMM vs the fp32 PyTorch oracle (GPU)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rand(*shape, scale=1.0, dev="cuda"):
+    return (torch.randn(*shape, device=dev) * scale).to(torch.bfloat16)
+
+
+def _close(a, b, tol=2e-2):
+    a = a.float()
+    b = b.float()
+    err = (a - b).abs().max().item()
+    ref = b.abs().max().item() + 1e-6
+    assert err <= tol * ref + 1e-2, f"max err {err} vs max |ref| {ref}"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA")
+    from granite_switch_b200 import _native
+
+    _native.native()  # fail loudly if the extension is missing
+
+
+@pytest.mark.parametrize("m", [1, 77, 128, 300])
+@pytest.mark.parametrize("bn", [64, 128, 256])
+def test_plain_store(m, bn):
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(0)
+    n, k = 512, 320
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.05)
+    out = G.switched_gemm(x, w, bn=bn)
+    torch.cuda.synchronize()
+    _close(out, G.switched_gemm_reference(x, w))
+    from granite_switch_b200._native import check_errors
+
+    check_errors(x.device)
+
+
+@pytest.mark.parametrize("bn", [64, 256])
+def test_f32_and_resadd(bn):
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(1)
+    m, n, k = 200, 256, 256
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.05)
+    out = G.switched_gemm(x, w, epi=G.EPI_F32, scale=0.5, bn=bn)
+    _close(out, G.switched_gemm_reference(x, w, epi=G.EPI_F32, scale=0.5))
+    res = _rand(m, n)
+    res_copy = res.clone()
+    G.switched_gemm(x, w, res, epi=G.EPI_RESADD, residual=res, scale=0.22, bn=bn)
+    _close(res, G.switched_gemm_reference(x, w, epi=G.EPI_RESADD, residual=res_copy, scale=0.22))
+
+
+@pytest.mark.parametrize("m", [5, 130])
+def test_lora_expand_fused(m):
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(2)
+    k, na, rank = 256, 3, 32
+    bounds = [0, 256, 384, 512]  # q | k | v slices
+    n = bounds[-1]
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.05)
+    row_adapter = torch.randint(0, na + 1, (m,), device="cuda", dtype=torch.int32)
+    a_all = torch.zeros(320, k, device="cuda", dtype=torch.bfloat16)  # 288 rows padded to 64
+    a_all[:3 * na * rank] = _rand(3 * na * rank, k, scale=0.05)
+    s = G.lora_shrink(x, a_all, row_adapter, rank, na)
+    s_ref = G.switched_gemm_reference(x, a_all, epi=G.EPI_MASK_ADAPTER, row_adapter=row_adapter,
+                                      mask_rank=rank, mask_num_adapters=na)
+    _close(s[:, :288], s_ref[:, :288])
+    lb = _rand(n, na * rank, scale=0.05)
+    tiles = (m + 127) // 128
+    mask = torch.zeros(tiles, dtype=torch.int64, device="cuda")
+    for t in range(tiles):
+        ids = row_adapter[t * 128:(t + 1) * 128]
+        bits = 0
+        for a in ids.unique().tolist():
+            if a > 0:
+                bits |= 1 << (a - 1)
+        mask[t] = bits
+    out = G.switched_gemm(x, w, s=s, lb=lb, tile_mask=mask, rank=rank, num_adapters=na,
+                          slice_bounds=bounds, bn=128)
+    ref = G.switched_gemm_reference(x, w, s=s, lb=lb, rank=rank, num_adapters=na,
+                                    slice_bounds=bounds)
+    _close(out, ref)
+
+
+def test_swiglu_split_lora():
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(3)
+    m, k, na, rank, bn = 150, 128, 2, 32, 128
+    n = 512
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.05)
+    row_adapter = torch.randint(0, na + 1, (m,), device="cuda", dtype=torch.int32)
+    s = _rand(m, 2 * na * rank, scale=0.5)
+    # zero columns not owned by the row's adapter, as the shrink would
+    cols = torch.arange(2 * na * rank, device="cuda")
+    keep = ((cols // rank) % na + 1).unsqueeze(0) == row_adapter.long().unsqueeze(1)
+    s = (s.float() * keep).to(torch.bfloat16)
+    lb = _rand(n, na * rank, scale=0.05)
+    out = G.switched_gemm(x, w, epi=G.EPI_SWIGLU, s=s, lb=lb, rank=rank, num_adapters=na,
+                          slice_bounds=[0, n], bn=bn)
+    ref = G.switched_gemm_reference(x, w, epi=G.EPI_SWIGLU, s=s, lb=lb, rank=rank,
+                                    num_adapters=na, swiglu_tile=bn)
+    _close(out, ref)
