@@ -9,4 +9,10 @@
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "granite_switch_b200 sm_100a kernels";
   m.def("switched_gemm", &gsb_switched_gemm, "tcgen05 GEMM with fused switched-LoRA expand");
+  m.def("rmsnorm", &gsb_rmsnorm, "RMSNorm (optionally gathering rows)");
+  m.def("embed", &gsb_embed, "embedding gather with token exchange and multiplier");
+  m.def("rope_kv", &gsb_rope_kv, "RoPE on q/k fused with the paged KV-cache write");
+  m.def("argmax", &gsb_argmax, "greedy argmax over fp32 logits");
+  m.def("routing", &gsb_routing, "latest-wins routing, token exchange and LoRA tile metadata");
+  m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode)");
 }

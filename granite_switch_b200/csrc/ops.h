@@ -14,3 +14,25 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
                        int64_t num_adapters, std::vector<int64_t> slice_bounds,
                        const c10::optional<at::Tensor>& row_adapter, int64_t mask_rank,
                        int64_t mask_num_adapters, const at::Tensor& err);
+
+void gsb_rmsnorm(const at::Tensor& x, const at::Tensor& w, const at::Tensor& out,
+                 const c10::optional<at::Tensor>& rows, double eps);
+void gsb_embed(const at::Tensor& ids, const at::Tensor& table, const c10::optional<at::Tensor>& lut,
+               double mult, const at::Tensor& out, const at::Tensor& err);
+void gsb_rope_kv(const at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& cos_sin,
+                 const c10::optional<at::Tensor>& k_cache, const c10::optional<at::Tensor>& v_cache,
+                 const c10::optional<at::Tensor>& slots, int64_t num_q_heads, int64_t num_kv_heads,
+                 int64_t head_dim, const at::Tensor& err);
+void gsb_argmax(const at::Tensor& logits, const at::Tensor& out);
+void gsb_routing(const at::Tensor& ids, const at::Tensor& seq_starts, const c10::optional<at::Tensor>& carry_in,
+                 const at::Tensor& expert_tbl, const c10::optional<at::Tensor>& lut,
+                 const c10::optional<at::Tensor>& kind_lut, int64_t num_adapters,
+                 const c10::optional<at::Tensor>& remap, const at::Tensor& adapter_idx,
+                 const at::Tensor& lora_idx, const at::Tensor& modified_ids,
+                 const c10::optional<at::Tensor>& carry_out, const c10::optional<at::Tensor>& row_adapter,
+                 const c10::optional<at::Tensor>& tile_mask);
+void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                         const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
+                         const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t rows_per_tile,
+                         int64_t num_q_heads, double scale, const at::Tensor& out, int64_t nsplit,
+                         const c10::optional<at::Tensor>& ws_o, const c10::optional<at::Tensor>& ws_lse);

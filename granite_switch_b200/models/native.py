@@ -1,0 +1,385 @@
+"""The decoder on the native sm_100a kernels: one engine step = one ``forward``.
+
+Per step: routing + LoRA metadata (one launch) -> embedding with token
+exchange -> per layer [RMSNorm -> qkv shrink + switched GEMM -> RoPE + paged
+KV write -> paged attention -> o_proj switched GEMM with the residual add in
+its epilogue -> RMSNorm -> gate/up switched GEMM with SwiGLU in its epilogue
+-> down switched GEMM with residual add] -> final RMSNorm on the rows that
+need logits -> LM head GEMM (fp32, / logits_scaling).
+
+Tensor parallelism (``tp_size > 1``): heads and the FFN are sharded; the
+row-parallel o/down projections write ``residual + partial`` on rank 0 and
+``partial`` elsewhere, and one all-reduce per projection sums them (the
+reference does the same reduction after its expand,
+src/granite_switch/vllm/core/lora.py:568-586). When a symmetric-memory
+communicator is attached, that reduction runs in the fused kernels of
+:mod:`granite_switch_b200.parallel.fused` instead of NCCL.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .._native import err_buffer, native
+from ..config import GraniteSwitchConfig
+from ..ops import attention as A
+from ..ops import elementwise as E
+from ..ops import gemm as G
+from ..routing.scan import expert_table
+from .packing import PackedLinear, choose_swiglu_tile, pack_linear
+
+
+@dataclass
+class LayerWeights:
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+    qkv: PackedLinear
+    o: PackedLinear
+    gu: PackedLinear
+    down: PackedLinear
+
+
+@dataclass
+class AttnPlan:
+    work_seq: torch.Tensor
+    work_row0: torch.Tensor
+    rows: int
+    nsplit: int
+
+
+@dataclass
+class StepBatch:
+    """Device-side inputs of one engine step (flattened request chunks)."""
+
+    num_tokens: int
+    num_seqs: int
+    ids: torch.Tensor          # [T] int64 original ids (control tokens included)
+    positions: torch.Tensor    # [T] int64
+    slots: torch.Tensor        # [T] int64 KV slot of each token
+    seq_starts: torch.Tensor   # [S+1] int32
+    carry_in: torch.Tensor     # [S] int32 routing carry at chunk start
+    kv_lens: torch.Tensor      # [S] int32 cached + new tokens
+    block_table: torch.Tensor  # [S, max_blocks] int32
+    logit_rows: torch.Tensor   # [B] int64 rows whose logits are needed
+    plans: list                # [AttnPlan]
+
+
+class NativeGraniteSwitch:
+    """Kernel-layout weights + persistent activation buffers + the step forward."""
+
+    def __init__(self, config: GraniteSwitchConfig, device: torch.device, max_tokens: int,
+                 num_kv_blocks: int, tp_rank: int = 0, tp_size: int = 1, tp_group=None,
+                 max_seqs: int = 512):
+        self.cfg = config
+        self.device = device
+        self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
+        self.hidden = config.hidden_size
+        self.head_dim = config.head_dim_eff
+        assert config.num_attention_heads % tp_size == 0
+        self.num_q = config.num_attention_heads // tp_size
+        self.num_kv = max(1, config.num_key_value_heads // tp_size)
+        self.inter = config.shared_intermediate_size // tp_size
+        self.vocab = config.vocab_size
+        self.num_layers = config.num_decoder_layers
+        self.max_tokens = max_tokens
+        self.max_seqs = max_seqs
+        self.num_kv_blocks = num_kv_blocks
+        self.layers: list[LayerWeights] = []
+        self.remaps: torch.Tensor | None = None
+        self.comm = None  # optional fused-collective communicator
+        self.err = err_buffer(device)
+        na = config.num_adapters
+        self.num_adapters = na
+        tbl = expert_table(config.adapter_token_ids or [], na, 1)
+        self.expert_tbl = tbl.to(device)
+        self.lut = None
+        self.kind_lut = None
+        self.cos_sin = E.rope_cos_sin_table(min(config.max_position_embeddings, 1 << 17), self.head_dim,
+                                            config.rope_theta, device)
+
+    # ------------------------------------------------------------------ weights
+    def _finish_weights(self, embed: torch.Tensor, final_norm: torch.Tensor, lm_head: torch.Tensor | None):
+        self.embed_w = embed
+        self.final_norm = final_norm
+        self.lm_head_w = lm_head if lm_head is not None else embed
+        # LM head is vocab-parallel under TP
+        if self.tp_size > 1:
+            v = self.lm_head_w.shape[0]
+            per = (v + self.tp_size - 1) // self.tp_size
+            per = (per + 255) // 256 * 256
+            lo = self.tp_rank * per
+            shard = torch.zeros(per, self.hidden, dtype=self.lm_head_w.dtype, device=self.device)
+            hi = min(v, lo + per)
+            if hi > lo:
+                shard[: hi - lo] = self.lm_head_w[lo:hi]
+            self.lm_vocab_lo, self.lm_vocab_hi = lo, hi
+            self.lm_head_w = shard
+        else:
+            v = self.lm_head_w.shape[0]
+            pad = (v + 255) // 256 * 256
+            if pad != v:
+                w = torch.zeros(pad, self.hidden, dtype=self.lm_head_w.dtype, device=self.device)
+                w[:v] = self.lm_head_w
+                self.lm_head_w = w
+            self.lm_vocab_lo, self.lm_vocab_hi = 0, v
+        # remap tables (deduplicated) for the routing kernel
+        maps: list[list[int]] = []
+        for lw in self.layers:
+            for pl in (lw.qkv, lw.o, lw.gu, lw.down):
+                if pl.has_lora:
+                    if pl.remap not in maps:
+                        maps.append(pl.remap)
+                    pl.map_id = maps.index(pl.remap)
+        self.remaps = torch.tensor(maps, dtype=torch.int32, device=self.device) if maps else None
+        self.n_maps = len(maps)
+        self._alloc_buffers()
+
+    @classmethod
+    def from_state_dict(cls, config: GraniteSwitchConfig, sd, device, max_tokens: int, num_kv_blocks: int,
+                        tp_rank: int = 0, tp_size: int = 1, tp_group=None, max_seqs: int = 512):
+        """Pack a composed checkpoint (``sd``: name -> tensor, or a lazy getter)."""
+        self = cls(config, device, max_tokens, num_kv_blocks, tp_rank, tp_size, tp_group, max_seqs)
+        get = sd.__getitem__ if isinstance(sd, dict) else sd
+        has = (lambda k: k in sd) if isinstance(sd, dict) else (lambda k: True)
+        na = config.num_adapters
+        h, d = config.hidden_size, config.head_dim_eff
+        q, kv = config.num_attention_heads * d, config.num_key_value_heads * d
+        inter = config.shared_intermediate_size
+        tiles = choose_swiglu_tile(inter // tp_size)
+
+        def lin(prefix, slices, parallel, swiglu=0):
+            base = prefix + ".base_layer.weight"
+            if has(base):
+                w = get(base)
+                ns = len(slices)
+                if ns > 1:
+                    la = [get(f"{prefix}.lora_A_slices.{s}") for s in range(ns)]
+                    lb = [get(f"{prefix}.lora_B_slices.{s}") for s in range(ns)]
+                else:
+                    la, lb = [get(prefix + ".lora_A")], [get(prefix + ".lora_B")]
+            else:
+                w, la, lb = get(prefix + ".weight"), None, None
+            return pack_linear(w, la, lb, slices, na, device, swiglu_tile=swiglu, tp_rank=tp_rank,
+                               tp_size=tp_size, parallel=parallel)
+
+        for i in range(config.num_decoder_layers):
+            p = f"model.layers.{i}."
+            self.layers.append(LayerWeights(
+                in_norm=get(p + "input_layernorm.weight").to(device, torch.bfloat16),
+                post_norm=get(p + "post_attention_layernorm.weight").to(device, torch.bfloat16),
+                qkv=lin(p + "self_attn.qkv_proj", [q, kv, kv], "column"),
+                o=lin(p + "self_attn.o_proj", [h], "row"),
+                gu=lin(p + "shared_mlp.input_linear", [inter, inter], "column", swiglu=tiles),
+                down=lin(p + "shared_mlp.output_linear", [h], "row"),
+            ))
+        embed = get("model.embed_tokens.weight").to(device, torch.bfloat16)
+        lm = None
+        if not config.tie_word_embeddings and has("lm_head.weight"):
+            lm = get("lm_head.weight").to(device, torch.bfloat16)
+        if has("model.switch.control_to_substitute_lut"):
+            self.lut = get("model.switch.control_to_substitute_lut").to(device, torch.long)
+        if has("model.switch.adapter_kind_lut"):
+            self.kind_lut = get("model.switch.adapter_kind_lut").to(device, torch.bool)
+        self._finish_weights(embed, get("model.norm.weight").to(device, torch.bfloat16), lm)
+        return self
+
+    @classmethod
+    def from_random(cls, config: GraniteSwitchConfig, device, max_tokens: int, num_kv_blocks: int,
+                    lora_modules=("qkv",), rank: int = 32, seed: int = 0, std: float = 0.02,
+                    tp_rank: int = 0, tp_size: int = 1, tp_group=None, max_seqs: int = 512):
+        """Random-init weights of the architecture, generated directly in kernel layout on the GPU.
+
+        Every rank draws the full (unsharded) tensors from the same seed and keeps
+        its shard, so TP runs are numerically the same model as TP=1.
+        """
+        self = cls(config, device, max_tokens, num_kv_blocks, tp_rank, tp_size, tp_group, max_seqs)
+        g = torch.Generator(device=device).manual_seed(seed)
+        na = config.num_adapters
+        h, d = config.hidden_size, config.head_dim_eff
+        q, kv = config.num_attention_heads * d, config.num_key_value_heads * d
+        inter = config.shared_intermediate_size
+        tiles = choose_swiglu_tile(inter // tp_size)
+        scale = 2.0  # alpha / r
+
+        def rnd(*shape, s=std):
+            return (torch.randn(*shape, generator=g, device=device) * s).to(torch.bfloat16)
+
+        def lin(n_out_slices, k, parallel, lora, swiglu=0):
+            n = sum(n_out_slices)
+            w = rnd(n, k)
+            la = lb = None
+            if lora and na > 0:
+                la = [rnd(na, 1, rank, k, s=0.02) for _ in n_out_slices]
+                lb = [rnd(na, 1, ns, rank, s=0.01 * scale) for ns in n_out_slices]
+            return pack_linear(w, la, lb, n_out_slices, na, device, swiglu_tile=swiglu, tp_rank=tp_rank,
+                               tp_size=tp_size, parallel=parallel)
+
+        for _ in range(config.num_decoder_layers):
+            self.layers.append(LayerWeights(
+                in_norm=torch.ones(h, dtype=torch.bfloat16, device=device),
+                post_norm=torch.ones(h, dtype=torch.bfloat16, device=device),
+                qkv=lin([q, kv, kv], h, "column", "qkv" in lora_modules),
+                o=lin([h], q, "row", "o" in lora_modules),
+                gu=lin([inter, inter], h, "column", "gu" in lora_modules, swiglu=tiles),
+                down=lin([h], inter, "row", "down" in lora_modules),
+            ))
+        embed = rnd(config.vocab_size, h)
+        if config.adapter_token_ids:
+            from ..routing.token_exchange import build_control_to_substitute_lut
+
+            lut = build_control_to_substitute_lut(config)
+            self.lut = lut.to(device) if lut is not None else None
+        self._finish_weights(embed, torch.ones(h, dtype=torch.bfloat16, device=device), None)
+        return self
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc_buffers(self):
+        t, dev = self.max_tokens, self.device
+        bf = torch.bfloat16
+        qkv_n = (self.num_q + 2 * self.num_kv) * self.head_dim
+        self.kv_cache = torch.zeros(self.num_layers, 2, self.num_kv_blocks, self.num_kv, 16, self.head_dim,
+                                    dtype=bf, device=dev)
+        self.h = torch.empty(t, self.hidden, dtype=bf, device=dev)
+        self.h2 = torch.empty(t, self.hidden, dtype=bf, device=dev) if self.tp_size > 1 else None
+        self.x = torch.empty(t, self.hidden, dtype=bf, device=dev)
+        self.qkv = torch.empty(t, qkv_n, dtype=bf, device=dev)
+        self.attn = torch.empty(t, self.num_q * self.head_dim, dtype=bf, device=dev)
+        self.act = torch.empty(t, self.inter, dtype=bf, device=dev)
+        s_cols = 64
+        for lw in self.layers:
+            for pl in (lw.qkv, lw.o, lw.gu, lw.down):
+                if pl.has_lora:
+                    s_cols = max(s_cols, pl.a_all.shape[0])
+        self.s_buf = torch.empty(t, s_cols, dtype=bf, device=dev)
+        self.adapter_idx = torch.empty(t, dtype=torch.int32, device=dev)
+        self.lora_idx = torch.empty(t, dtype=torch.int32, device=dev)
+        self.mod_ids = torch.empty(t, dtype=torch.long, device=dev)
+        self.carry_out = torch.empty(self.max_seqs, dtype=torch.int32, device=dev)
+        n_tiles = (t + 127) // 128
+        self.row_adapter = torch.empty(max(self.n_maps, 1), t, dtype=torch.int32, device=dev)
+        self.tile_mask = torch.empty(max(self.n_maps, 1), n_tiles, dtype=torch.int64, device=dev)
+        self.max_logit_rows = self.max_seqs
+        self.xf = torch.empty(self.max_seqs, self.hidden, dtype=bf, device=dev)
+        self.logits = torch.empty(self.max_seqs, self.lm_head_w.shape[0], dtype=torch.float32, device=dev)
+        max_split = 32
+        self.ws_o = torch.empty(max_split * min(t, 4 * self.max_seqs) * self.num_q * self.head_dim,
+                                dtype=torch.float32, device=dev)
+        self.ws_lse = torch.empty(max_split * min(t, 4 * self.max_seqs) * self.num_q, dtype=torch.float32, device=dev)
+        self.ws_tokens = min(t, 4 * self.max_seqs)
+
+    def kv_cache_bytes(self) -> int:
+        return self.kv_cache.numel() * self.kv_cache.element_size()
+
+    # ------------------------------------------------------------------ forward pieces
+    def _proj(self, pl: PackedLinear, x: torch.Tensor, out: torch.Tensor, epi=G.EPI_STORE, residual=None,
+              scale=1.0):
+        m = x.shape[0]
+        if pl.has_lora:
+            ra = self.row_adapter[pl.map_id, :m]
+            s = self.s_buf[:m, : pl.a_all.shape[0]]
+            G.lora_shrink(x, pl.a_all, ra, pl.rank, pl.n_local, out=s)
+            tm = self.tile_mask[pl.map_id, : (m + 127) // 128]
+            bn = pl.swiglu_tile if epi == G.EPI_SWIGLU else None
+            G.switched_gemm(x, pl.w, out, epi=epi, residual=residual, scale=scale, s=s, lb=pl.lb, tile_mask=tm,
+                            rank=pl.rank, num_adapters=pl.n_local,
+                            slice_bounds=[0, pl.n] if epi == G.EPI_SWIGLU else pl.slice_bounds, bn=bn)
+        else:
+            bn = pl.swiglu_tile if epi == G.EPI_SWIGLU else None
+            G.switched_gemm(x, pl.w, out, epi=epi, residual=residual, scale=scale, bn=bn)
+        return out
+
+    def _row_parallel(self, pl: PackedLinear, x: torch.Tensor, h: torch.Tensor, mult: float):
+        """h <- h + x @ W^T * mult, summed over TP ranks."""
+        m = x.shape[0]
+        if self.tp_size == 1:
+            self._proj(pl, x, h, epi=G.EPI_RESADD, residual=h, scale=mult)
+            return
+        if self.comm is not None:
+            self.comm.row_parallel(self, pl, x, h, mult)
+            return
+        y = self.h2[:m]
+        if self.tp_rank == 0:
+            self._proj(pl, x, y, epi=G.EPI_RESADD, residual=h, scale=mult)
+        else:
+            self._proj(pl, x, y, epi=G.EPI_STORE, scale=mult)
+        torch.distributed.all_reduce(y, group=self.tp_group)
+        h.copy_(y)
+
+    @torch.no_grad()
+    def forward(self, b: StepBatch) -> torch.Tensor:
+        """Run one step; returns fp32 logits ``[B, vocab(_shard)]`` for ``b.logit_rows``."""
+        cfg = self.cfg
+        t = b.num_tokens
+        nat = native()
+        if self.n_maps:
+            nat.routing(b.ids, b.seq_starts, b.carry_in, self.expert_tbl, None, self.kind_lut,
+                        self.num_adapters, self.remaps, self.adapter_idx[:t], self.lora_idx[:t],
+                        self.mod_ids[:t], self.carry_out[: b.num_seqs], self.row_adapter[:, :t],
+                        self.tile_mask[:, : (t + 127) // 128])
+            E.embed(b.ids, self.embed_w, self.lut, cfg.embedding_multiplier, out=self.h[:t])
+        else:
+            E.embed(b.ids, self.embed_w, self.lut, cfg.embedding_multiplier, out=self.h[:t])
+        h, x = self.h[:t], self.x[:t]
+        qkv, attn, act = self.qkv[:t], self.attn[:t], self.act[:t]
+        mult = float(cfg.residual_multiplier)
+        scale = float(cfg.attention_multiplier)
+        for li, lw in enumerate(self.layers):
+            E.rmsnorm(h, lw.in_norm, cfg.rms_norm_eps, out=x)
+            self._proj(lw.qkv, x, qkv)
+            kc, vc = self.kv_cache[li, 0], self.kv_cache[li, 1]
+            E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
+            for plan in b.plans:
+                A.paged_attention(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
+                                  plan.work_row0, plan.rows, self.num_q, scale, attn, plan.nsplit,
+                                  self.ws_o, self.ws_lse)
+            self._row_parallel(lw.o, attn, h, mult)
+            E.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps, out=x)
+            self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
+            self._row_parallel(lw.down, act, h, mult)
+        nb = b.logit_rows.numel()
+        xf = self.xf[:nb]
+        E.rmsnorm(h, self.final_norm, cfg.rms_norm_eps, out=xf, rows=b.logit_rows)
+        logits = self.logits[:nb]
+        G.switched_gemm(xf, self.lm_head_w, logits, epi=G.EPI_F32, scale=1.0 / float(cfg.logits_scaling))
+        return logits
+
+    def attention_plans(self, q_lens: list[int], kv_lens: list[int]) -> list[tuple[list[int], list[int], int, int]]:
+        """Split requests into decode-layout and prefill-layout CTA work lists."""
+        g = self.num_q // self.num_kv
+        dec = [i for i, ql in enumerate(q_lens) if ql * g <= 16]
+        pre = [i for i, ql in enumerate(q_lens) if ql * g > 16]
+        plans = []
+        for idx, rows in ((dec, 16), (pre, 64)):
+            if not idx:
+                continue
+            ws, wr = [], []
+            for i in idx:
+                for r0 in range(0, q_lens[i] * g, rows):
+                    ws.append(i)
+                    wr.append(r0)
+            n_ctas = len(ws) * self.num_kv
+            max_kv = max(kv_lens[i] for i in idx)
+            ns = A.choose_splits(n_ctas, max_kv) if rows == 16 else 1
+            tot = sum(q_lens)
+            if ns > 1 and tot > self.ws_tokens:
+                ns = 1
+            plans.append((ws, wr, rows, ns))
+        return plans
+
+
+def default_num_kv_blocks(model_bytes: int, cfg: GraniteSwitchConfig, tp_size: int, mem_fraction: float = 0.85,
+                          device=None, reserve_bytes: int = 6 << 30, cap_blocks: int | None = None) -> int:
+    free, total = torch.cuda.mem_get_info(device)
+    d = cfg.head_dim_eff
+    kv_heads = max(1, cfg.num_key_value_heads // tp_size)
+    per_block = cfg.num_decoder_layers * 2 * kv_heads * 16 * d * 2
+    budget = int(total * mem_fraction) - (total - free) - reserve_bytes
+    n = max(64, budget // per_block)
+    if cap_blocks is not None:
+        n = min(n, cap_blocks)
+    return int(n)
+
+
+__all__ = ["NativeGraniteSwitch", "StepBatch", "AttnPlan", "default_num_kv_blocks", "math"]

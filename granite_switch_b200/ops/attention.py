@@ -1,0 +1,66 @@
+"""Paged causal GQA attention (native, sm_100a) and its PyTorch oracle."""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .._native import native
+
+NUM_SMS = 148
+
+
+def build_work(q_lens: list[int], group: int, rows_per_tile: int) -> tuple[list[int], list[int]]:
+    """(request, first row) per CTA tile; a request contributes ceil(q_len*G / rows) tiles."""
+    seqs, rows = [], []
+    for i, ql in enumerate(q_lens):
+        n = ql * group
+        for r0 in range(0, n, rows_per_tile):
+            seqs.append(i)
+            rows.append(r0)
+    return seqs, rows
+
+
+def choose_splits(n_ctas: int, max_kv: int, min_keys_per_split: int = 256) -> int:
+    """Flash-decoding split count: fill ~2 waves of SMs without splits shorter than 256 keys."""
+    if n_ctas >= 2 * NUM_SMS:
+        return 1
+    want = max(1, (2 * NUM_SMS + n_ctas - 1) // max(n_ctas, 1))
+    cap = max(1, max_kv // min_keys_per_split)
+    return int(max(1, min(want, cap, 32)))
+
+
+def paged_attention(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
+                    rows_per_tile: int, num_q_heads: int, scale: float, out, nsplit: int = 1,
+                    ws_o=None, ws_lse=None):
+    native().paged_attention(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
+                             rows_per_tile, num_q_heads, float(scale), out, nsplit, ws_o, ws_lse)
+    return out
+
+
+def paged_attention_reference(q, k_cache, v_cache, block_table, q_lens, kv_lens, num_q_heads, scale):
+    """fp32 oracle. q ``[T, Hq*D]`` (flat, requests back to back); returns ``[T, Hq*D]`` fp32."""
+    _, hkv, page, d = k_cache.shape
+    g = num_q_heads // hkv
+    outs = []
+    off = 0
+    for i, (ql, kl) in enumerate(zip(q_lens, kv_lens)):
+        nblk = (kl + page - 1) // page
+        blocks = block_table[i, :nblk].long()
+        k = k_cache[blocks].permute(0, 2, 1, 3).reshape(-1, hkv, d)[:kl].float()  # [kl, hkv, d]
+        v = v_cache[blocks].permute(0, 2, 1, 3).reshape(-1, hkv, d)[:kl].float()
+        qi = q[off:off + ql, : num_q_heads * d].float().view(ql, num_q_heads, d)
+        k = k.repeat_interleave(g, dim=1)
+        v = v.repeat_interleave(g, dim=1)
+        att = torch.einsum("qhd,khd->hqk", qi, k) * scale
+        pos = torch.arange(kl - ql, kl, device=q.device)
+        mask = torch.arange(kl, device=q.device).unsqueeze(0) <= pos.unsqueeze(1)
+        att = att.masked_fill(~mask.unsqueeze(0), float("-inf"))
+        p = torch.softmax(att, dim=-1)
+        o = torch.einsum("hqk,khd->qhd", p, v).reshape(ql, num_q_heads * d)
+        outs.append(o)
+        off += ql
+    return torch.cat(outs, 0)
+
+
+__all__ = ["paged_attention", "paged_attention_reference", "build_work", "choose_splits", "math"]

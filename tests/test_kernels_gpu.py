@@ -1,0 +1,182 @@
+"""Native norm / embedding / RoPE+KV / argmax / routing / attention vs PyTorch fp32 oracles (GPU)."""
+import random
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA")
+    from granite_switch_b200 import _native
+
+    _native.native()
+
+
+def _check(dev="cuda"):
+    from granite_switch_b200._native import check_errors
+
+    check_errors(torch.device(dev))
+
+
+@pytest.mark.parametrize("h", [64, 2048, 4096])
+def test_rmsnorm(h):
+    from granite_switch_b200.ops import elementwise as E
+
+    x = torch.randn(37, h, device="cuda").bfloat16()
+    w = (1 + 0.1 * torch.randn(h, device="cuda")).bfloat16()
+    out = E.rmsnorm(x, w, 1e-5)
+    ref = E.rmsnorm_reference(x, w, 1e-5)
+    assert (out.float() - ref.float()).abs().max() <= 0.02 * ref.float().abs().max()
+    rows = torch.tensor([3, 0, 36], device="cuda")
+    out2 = E.rmsnorm(x, w, 1e-5, rows=rows)
+    assert torch.equal(out2, out[rows])
+
+
+def test_embed_exchange():
+    from granite_switch_b200.ops import elementwise as E
+
+    table = torch.randn(300, 64, device="cuda").bfloat16()
+    lut = torch.full((302,), -1, dtype=torch.long, device="cuda")
+    lut[300], lut[301] = 5, 7
+    ids = torch.tensor([1, 300, 2, 301, 299], device="cuda")
+    table2 = torch.cat([table, torch.zeros(2, 64, device="cuda").bfloat16()])
+    out = E.embed(ids, table2, lut, 12.0)
+    ref = E.embed_reference(ids, table2, lut, 12.0)
+    assert torch.equal(out, ref)
+    _check()
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_rope_kv_write(d):
+    from granite_switch_b200.ops import elementwise as E
+
+    hq, hkv, t = 8, 2, 20
+    cs = E.rope_cos_sin_table(4096, d, 10000.0, "cuda")
+    qkv = torch.randn(t, (hq + 2 * hkv) * d, device="cuda").bfloat16()
+    pos = torch.randint(0, 4000, (t,), device="cuda")
+    kc = torch.zeros(8, hkv, 16, d, device="cuda").bfloat16()
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(8 * 16, device="cuda")[:t]
+    orig = qkv.clone()
+    E.rope_kv(qkv, pos, cs, hq, hkv, d, kc, vc, slots)
+    q_ref = E.rope_reference(orig[:, : hq * d].view(t, hq, d), pos, cs)
+    k_ref = E.rope_reference(orig[:, hq * d:(hq + hkv) * d].view(t, hkv, d), pos, cs)
+    v_ref = orig[:, (hq + hkv) * d:].view(t, hkv, d)
+    assert (qkv[:, : hq * d].view(t, hq, d).float() - q_ref.float()).abs().max() < 2e-2
+    for i in range(t):
+        b, o = int(slots[i]) // 16, int(slots[i]) % 16
+        assert (kc[b, :, o].float() - k_ref[i].float()).abs().max() < 2e-2
+        assert torch.equal(vc[b, :, o], v_ref[i])
+    _check()
+
+
+def test_argmax():
+    from granite_switch_b200.ops import elementwise as E
+
+    x = torch.randn(9, 49155, device="cuda")
+    x[3, 17] = 100.0
+    assert torch.equal(E.argmax(x), x.argmax(dim=1))
+
+
+def test_routing_kernel_matches_scan():
+    from granite_switch_b200.ops.routing import route_device, tile_masks_reference
+    from granite_switch_b200.routing.scan import expert_table, route_flat
+
+    rng = random.Random(0)
+    na = 5
+    ctrl = [1000 + i for i in range(na)]
+    tbl = expert_table(ctrl, na, 1100)
+    lens = [rng.randrange(1, 700) for _ in range(7)] + [1, 1, 1]
+    ids = []
+    for n in lens:
+        ids += [rng.choice(ctrl) if rng.random() < 0.02 else rng.randrange(0, 1000) for _ in range(n)]
+    starts = [0]
+    for n in lens:
+        starts.append(starts[-1] + n)
+    carries = [rng.randrange(0, na + 1) for _ in lens]
+    ref, ref_c = route_flat(torch.tensor(ids), starts, carries, tbl)
+    T = len(ids)
+    dev = "cuda"
+    lut = torch.full((1100,), -1, dtype=torch.long)
+    for i, c in enumerate(ctrl):
+        lut[c] = i
+    kind = torch.zeros(na + 1, dtype=torch.bool)
+    kind[3] = True  # slot 3 is a probe
+    remap = torch.tensor([[0, 1, 2, 3, 4, 5], [0, 0, 1, 0, 0, 2]], dtype=torch.int32)
+    out_a = torch.empty(T, dtype=torch.int32, device=dev)
+    out_l = torch.empty(T, dtype=torch.int32, device=dev)
+    out_ids = torch.empty(T, dtype=torch.long, device=dev)
+    out_c = torch.empty(len(lens), dtype=torch.int32, device=dev)
+    ra = torch.empty(2, T, dtype=torch.int32, device=dev)
+    tm = torch.empty(2, (T + 127) // 128, dtype=torch.int64, device=dev)
+    route_device(torch.tensor(ids, device=dev), torch.tensor(starts, dtype=torch.int32, device=dev),
+                 torch.tensor(carries, dtype=torch.int32, device=dev), tbl.to(dev), lut.to(dev), kind.to(dev),
+                 na, remap.to(dev), out_a, out_l, out_ids, out_c, ra, tm)
+    assert out_a.cpu().tolist() == ref.tolist()
+    assert out_c.cpu().tolist() == ref_c
+    lora = torch.where(ref == 3, torch.zeros_like(ref), ref)
+    assert out_l.cpu().tolist() == lora.tolist()
+    ex = torch.tensor(ids)
+    ex = torch.where(lut[ex] >= 0, lut[ex], ex)
+    assert out_ids.cpu().tolist() == ex.tolist()
+    for m in range(2):
+        want = remap[m][lora].int()
+        assert ra[m].cpu().tolist() == want.tolist()
+        assert tm[m].cpu().tolist() == tile_masks_reference(want).tolist()
+
+
+def _make_cache(lens, hkv, d, seed=0):
+    torch.manual_seed(seed)
+    nblk = sum((l + 15) // 16 for l in lens) + 3
+    kc = torch.randn(nblk, hkv, 16, d, device="cuda").bfloat16()
+    vc = torch.randn(nblk, hkv, 16, d, device="cuda").bfloat16()
+    perm = torch.randperm(nblk).tolist()
+    maxb = max((l + 15) // 16 for l in lens)
+    bt = torch.zeros(len(lens), maxb, dtype=torch.int32)
+    p = 0
+    for i, l in enumerate(lens):
+        for j in range((l + 15) // 16):
+            bt[i, j] = perm[p]
+            p += 1
+    return kc, vc, bt.cuda()
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("mode", ["prefill", "decode"])
+@pytest.mark.parametrize("nsplit", [1, 3])
+def test_paged_attention(d, mode, nsplit):
+    from granite_switch_b200.ops import attention as A
+
+    hq, hkv = 8, 2
+    g = hq // hkv
+    if mode == "decode":
+        q_lens = [1, 1, 2, 1, 4]
+        kv_lens = [1, 37, 300, 1025, 64]
+        rows = 16
+    else:
+        q_lens = [5, 64, 130, 1]
+        kv_lens = [5, 200, 130, 77]
+        rows = 64
+    kc, vc, bt = _make_cache(kv_lens, hkv, d)
+    T = sum(q_lens)
+    q = torch.randn(T, (hq + 2 * hkv) * d, device="cuda").bfloat16()  # qkv buffer, q at the front
+    out = torch.zeros(T, hq * d, device="cuda").bfloat16()
+    qs = [0]
+    for l in q_lens:
+        qs.append(qs[-1] + l)
+    ws, wr = A.build_work(q_lens, g, rows)
+    dev = "cuda"
+    ws_o = torch.empty(nsplit * T * hq * d, device=dev)
+    ws_l = torch.empty(nsplit * T * hq, device=dev)
+    A.paged_attention(q, kc, vc, bt, torch.tensor(qs, dtype=torch.int32, device=dev),
+                      torch.tensor(kv_lens, dtype=torch.int32, device=dev),
+                      torch.tensor(ws, dtype=torch.int32, device=dev), torch.tensor(wr, dtype=torch.int32, device=dev),
+                      rows, hq, 0.125, out, nsplit, ws_o, ws_l)
+    ref = A.paged_attention_reference(q, kc, vc, bt, q_lens, kv_lens, hq, 0.125)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 3e-2, err
+    _check()
