@@ -1,0 +1,270 @@
+#!/usr/bin/env python
+"""Headline benchmark: multi-aLoRA serving throughput on the Granite-8B shape.
+
+Metric: output tok/s + p50 TTFT for the multi-adapter
+Granite-8B-shape workload (40 layers, d_model 4096, 32 q / 8 kv heads,
+head_dim 128, FFN 12800, vocab 49152, random init; 12 aLoRA adapters of rank 32
+on q/k/v/o), with the KV prefix-hit rate. Conversations arrive by a Poisson
+process; each holds a 4096-token context followed by 8 chained adapter calls
+(16-64-token invocation, 32-128 generated tokens).
+
+``python bench.py --gpus N --steps K --warmup W`` serves the workload with
+tensor parallelism over N GPUs (one process per GPU under torchrun). A step is
+one engine iteration (one batched forward over every running request). After
+an untimed ramp that fills the server to its steady concurrency, W untimed
+warm-up steps run, then exactly K steps are timed with CUDA events bracketed
+by a barrier and a device synchronise; the reported time is the max over
+ranks. ``value`` is whole-job generated tokens per second over the timed
+steps. ``e2e`` is the same metric measured by the host clock around the same
+K steps of the public engine API, whose every step copies its inputs from
+pinned host memory and reads the sampled ids back.
+
+``--impl reference`` runs the unmodified reference (granite-switch's vLLM
+plugin from baseline/_ref) on the same workload and prints the same line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+METRIC = "output tok/s + p50 TTFT, multi-aLoRA 8B-shape, TP1/2/4/8; KV prefix-hit rate"
+BASELINE_VALUE = None  # BASELINE.md publishes no number for this workload on any B200
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=120)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["native", "reference"], default="native")
+    p.add_argument("--preset", default="granite-8b")
+    p.add_argument("--layers", type=int, default=None, help="override layer count (debug only; invalid for the metric)")
+    p.add_argument("--rate", type=float, default=16.0, help="conversation arrivals per second (Poisson)")
+    p.add_argument("--conversations", type=int, default=2048)
+    p.add_argument("--context-len", type=int, default=4096)
+    p.add_argument("--calls", type=int, default=8)
+    p.add_argument("--max-num-seqs", type=int, default=128)
+    p.add_argument("--max-num-batched-tokens", type=int, default=8192)
+    p.add_argument("--ramp-steps", type=int, default=400, help="max untimed steps to reach steady concurrency")
+    p.add_argument("--mode", choices=["alora", "lora"], default="alora")
+    p.add_argument("--fused-comm", action="store_true", help="fused GEMM+collective kernels for TP")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--kv-blocks", type=int, default=None)
+    return p.parse_args()
+
+
+def emit(obj):
+    print(json.dumps(obj), flush=True)
+
+
+# ----------------------------------------------------------------------------- config
+def model_config(args):
+    sys.path.insert(0, ROOT)
+    from granite_switch_b200.composer.synthetic import base_config
+    from granite_switch_b200.config import GraniteSwitchConfig
+
+    base = base_config(args.preset)
+    if args.layers:
+        base["num_hidden_layers"] = args.layers
+    na = 12
+    v = base["vocab_size"]
+    cfg = dict(base)
+    cfg.update(num_adapters=na, adapter_token_ids=list(range(v, v + na)),
+               adapter_substitute_token_ids=[1] * na, adapter_names=[f"adapter_{i}" for i in range(na)],
+               adapter_ranks=[32] * na, max_lora_rank=32, lora_target_modules=["qkv_proj", "o_proj"],
+               num_hidden_layers=base["num_hidden_layers"] + 2, vocab_size=v + na)
+    return GraniteSwitchConfig(**cfg), base
+
+
+# ----------------------------------------------------------------------------- native arm
+def run_native(args):
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    from granite_switch_b200 import _native
+    from granite_switch_b200.engine import LLM, EngineConfig, SamplingParams
+    from granite_switch_b200.utils.timing import ClockSampler, local_rank, max_over_ranks
+    from granite_switch_b200.utils.workload import WorkloadConfig, advance, call_prompt, make_workload
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank())
+    group = None
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank()))
+        group = dist.group.WORLD
+    _native.native()
+    config, base = model_config(args)
+    ecfg = EngineConfig(max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
+                        max_model_len=args.context_len + args.calls * 200 + 256, tensor_parallel_size=world,
+                        num_kv_blocks=args.kv_blocks, fused_tp_comm=args.fused_comm, seed=args.seed)
+    llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
+              random_init=dict(lora_modules=("qkv", "o"), rank=32, seed=args.seed), tp_rank=rank, tp_group=group)
+    eng = llm.engine
+    wl = WorkloadConfig(num_conversations=args.conversations, rate=args.rate, context_len=args.context_len,
+                        calls=args.calls, vocab=base["vocab_size"], num_adapters=12, seed=args.seed, mode=args.mode)
+    convs = make_workload(wl)
+    ctrl = config.adapter_token_ids
+    by_req = {}
+    submit_times = {}
+
+    def submit(conv, now):
+        prompt = call_prompt(conv, ctrl, args.mode)
+        gen = conv.calls[conv.next_call].gen_len
+        r = eng.add_request(prompt, SamplingParams(max_tokens=gen, ignore_eos=True), arrival_time=now)
+        by_req[r.request_id] = conv
+        submit_times[r.request_id] = now
+
+    def on_finish(req):
+        conv = by_req.pop(req.request_id)
+        if advance(conv, req.prompt_ids, req.output_ids, args.mode):
+            submit(conv, time.perf_counter())
+
+    eng.on_finish = on_finish
+    t0 = time.perf_counter()
+    next_conv = 0
+    arrived = torch.zeros(1, dtype=torch.long, device="cuda")
+
+    def admit():
+        nonlocal next_conv
+        now = time.perf_counter() - t0
+        if (rank == 0 and not eng.has_unfinished() and next_conv < len(convs)
+                and convs[next_conv].arrival > now):
+            time.sleep(convs[next_conv].arrival - now)  # idle server: wait for the next arrival
+            now = time.perf_counter() - t0
+        n = next_conv
+        while n < len(convs) and convs[n].arrival <= now:
+            n += 1
+        if world > 1:
+            arrived.fill_(n)
+            dist.broadcast(arrived, src=0, group=group)
+            n = int(arrived.item())
+        while next_conv < n:
+            submit(convs[next_conv], time.perf_counter())
+            next_conv += 1
+
+    finished_log = []
+    eng_step = eng.step
+
+    def step():
+        admit()
+        fin = eng_step()
+        finished_log.extend(fin)
+        return fin
+
+    # ---- ramp: fill the server to steady concurrency
+    ramp = 0
+    target = int(0.9 * args.max_num_seqs)
+    while ramp < args.ramp_steps:
+        step()
+        ramp += 1
+        if len(eng.scheduler.running) >= target and eng.stats.finished >= 1:
+            break
+    # ---- warm-up
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(group=group)
+    gen0 = eng.stats.generated_tokens
+    q0, h0 = eng.blocks.queries, eng.blocks.hits
+    ex = eng.executor
+    h2d0, d2h0 = ex.h2d_bytes, ex.d2h_bytes
+    launches0 = _native.launch_count()
+    first_tok_before = {r.request_id for r in finished_log}
+    start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank()) as clocks:
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        start_ev.record()
+        for _ in range(args.steps):
+            step()
+        end_ev.record()
+        torch.cuda.synchronize()
+        w1 = time.perf_counter()
+    if world > 1:
+        dist.barrier(group=group)
+    dev_ms = max_over_ranks(start_ev.elapsed_time(end_ev), group)
+    wall_s = max_over_ranks(w1 - w0, group)
+    gen = eng.stats.generated_tokens - gen0
+    launches = _native.launch_count() - launches0
+    # TTFT of calls whose first token landed in the timed window
+    ttfts = []
+    for r in finished_log:
+        if r.first_token_time is not None and w0 <= r.first_token_time <= w1:
+            ttfts.append(r.first_token_time - r.arrival_time)
+    for r in eng.scheduler.running:
+        if r.first_token_time is not None and w0 <= r.first_token_time <= w1:
+            ttfts.append(r.first_token_time - r.arrival_time)
+    dq, dh = eng.blocks.queries - q0, eng.blocks.hits - h0
+    value = gen / (dev_ms / 1e3)
+    e2e = gen / wall_s
+    clk = clocks.summary()
+    if rank == 0:
+        emit({
+            "metric": METRIC, "value": round(value, 2), "unit": "output tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": (round(value / BASELINE_VALUE, 4) if BASELINE_VALUE else None),
+            "dtype": "bf16", "data": "synthetic (random prompts, random-init base and adapter weights)",
+            "impl": "native",
+            "p50_ttft_s": round(statistics.median(ttfts), 4) if ttfts else None,
+            "ttft_samples": len(ttfts),
+            "prefix_hit_rate": round(dh / dq, 4) if dq else None,
+            "prefix_hit_rate_overall": round(eng.prefix_cache_hit_rate(), 4),
+            "config": {"model": f"{args.preset}-shape" + (f"-L{args.layers}" if args.layers else ""),
+                       "global_batch": args.max_num_seqs, "seq_len": args.context_len,
+                       "parallelism": f"tp{world}", "adapters": "12 aLoRA r32 q/k/v/o",
+                       "workload": f"poisson {args.rate}/s, {args.calls} chained calls, inv 16-64, gen 32-128",
+                       "mode": args.mode, "max_num_batched_tokens": args.max_num_batched_tokens,
+                       "ramp_steps": ramp, "l2": "inputs larger than L2 (each step streams all weights)",
+                       "fused_comm": bool(args.fused_comm)},
+            "e2e": {"value": round(e2e, 2), "unit": "output tok/s", "h2d_bytes_per_step": (ex.h2d_bytes - h2d0) // args.steps,
+                    "d2h_bytes_per_step": (ex.d2h_bytes - d2h0) // args.steps},
+            "gpu_launches": launches,
+            "clocks": clk,
+            "kv_blocks": eng.blocks.num_blocks,
+            "running_at_end": len(eng.scheduler.running),
+        })
+    if world > 1:
+        dist.barrier(group=group)
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "granite_switch")):
+        if rank == 0:
+            emit({"impl": "reference", "unavailable": "baseline/_ref is not installed"})
+        return
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    from reference_arm import run as ref_run  # baseline/reference_arm.py
+
+    ref_run(args, emit, METRIC)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_native(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -27,8 +27,40 @@ class NativeExtensionMissing(RuntimeError):
     pass
 
 
+class _Counted:
+    """Proxy over the extension that counts op calls (one call = one or two kernel launches).
+
+    ``launch_count()`` lets benchmarks report how many native kernels ran in a
+    timed region.
+    """
+
+    def __init__(self, mod):
+        self._mod = mod
+        self._fns = {}
+
+    def __getattr__(self, name):
+        fn = self._fns.get(name)
+        if fn is None:
+            raw = getattr(self._mod, name)
+
+            def fn(*a, _raw=raw, **k):
+                global _LAUNCHES
+                _LAUNCHES += 1
+                return _raw(*a, **k)
+
+            self._fns[name] = fn
+        return fn
+
+
+_LAUNCHES = 0
+
+
+def launch_count() -> int:
+    return _LAUNCHES
+
+
 def native():
-    """Return the loaded extension module, importing it on first use."""
+    """Return the loaded extension (through the counting proxy), importing it on first use."""
     global _C
     if _C is None:
         with _lock:
@@ -40,7 +72,7 @@ def native():
                         "granite_switch_b200._C is not built; run "
                         "`python setup.py build_ext --inplace` in the repository root"
                     ) from e
-                _C = mod
+                _C = _Counted(mod)
     return _C
 
 

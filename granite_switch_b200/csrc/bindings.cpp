@@ -14,5 +14,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_kv", &gsb_rope_kv, "RoPE on q/k fused with the paged KV-cache write");
   m.def("argmax", &gsb_argmax, "greedy argmax over fp32 logits");
   m.def("routing", &gsb_routing, "latest-wins routing, token exchange and LoRA tile metadata");
+  m.def("sample", &gsb_sample, "temperature / top-k / top-p sampling (Gumbel-max, Philox)");
   m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode)");
 }

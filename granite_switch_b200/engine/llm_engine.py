@@ -1,0 +1,250 @@
+"""Serving engine: continuous batching over a paged, prefix-cached KV cache.
+
+``LLMEngine`` is the step loop (add requests, ``step()``, collect finished
+requests). ``LLM`` is the offline entry point: ``LLM(model_dir).generate(...)``.
+Both run the same scheduler on every tensor-parallel rank (SPMD); ranks stay in
+lockstep because every input to a scheduling decision (arrivals, sampled
+tokens) is identical on all ranks.
+"""
+from __future__ import annotations
+
+import os
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from ..config import GraniteSwitchConfig
+from ..routing.scan import expert_table
+from .kv_cache import BLOCK_SIZE, BlockManager
+from .request import Request, RequestOutput, SamplingParams
+from .scheduler import Scheduler
+
+
+@dataclass
+class EngineConfig:
+    max_num_seqs: int = 256
+    max_num_batched_tokens: int = 8192
+    max_model_len: int = 8192
+    num_kv_blocks: int | None = None       # None: size from free GPU memory
+    gpu_memory_utilization: float = 0.88
+    enable_prefix_caching: bool = True
+    enable_chunked_prefill: bool = True
+    tensor_parallel_size: int = 1
+    use_cuda_graphs: bool = False
+    dtype: str = "bfloat16"
+    seed: int = 0
+    fused_tp_comm: bool = False            # symmetric-memory fused GEMM + reduction kernels
+
+
+@dataclass
+class EngineStats:
+    steps: int = 0
+    prompt_tokens: int = 0
+    generated_tokens: int = 0
+    finished: int = 0
+    ttfts: list = field(default_factory=list)
+    latencies: list = field(default_factory=list)
+
+
+class HostRouter:
+    """Host copy of the routing rule, used to carry routing state across chunks."""
+
+    def __init__(self, config: GraniteSwitchConfig):
+        self.map = {}
+        if config.num_adapters > 0 and config.adapter_token_ids:
+            tbl = expert_table(config.adapter_token_ids, config.num_adapters)
+            for tok in config.adapter_token_ids:
+                self.map[tok] = int(tbl[tok])
+
+    def __call__(self, ids: list[int], carry: int) -> int:
+        m = self.map
+        if not m:
+            return carry
+        for t in reversed(ids):
+            e = m.get(t)
+            if e is not None:
+                return e
+        return carry
+
+
+class LLMEngine:
+    def __init__(self, config: GraniteSwitchConfig, executor, num_blocks: int, engine_config: EngineConfig | None = None):
+        self.config = config
+        self.ecfg = engine_config or EngineConfig()
+        self.executor = executor
+        self.blocks = BlockManager(num_blocks, self.ecfg.enable_prefix_caching)
+        self.router = HostRouter(config)
+        self.scheduler = Scheduler(self.blocks, self.ecfg.max_num_seqs, self.ecfg.max_num_batched_tokens,
+                                   self.ecfg.enable_chunked_prefill, route_fn=self.router)
+        self.stats = EngineStats()
+        self.requests: dict[str, Request] = {}
+        self.eos = config.eos_token_id if isinstance(config.eos_token_id, int) else None
+        self.on_finish = None  # optional callback(req)
+
+    # -------------------------------------------------------------- requests
+    def add_request(self, prompt_ids: list[int], sampling: SamplingParams | None = None,
+                    request_id: str | None = None, arrival_time: float | None = None, user_data=None) -> Request:
+        if len(prompt_ids) == 0:
+            raise ValueError("empty prompt")
+        sp = sampling or SamplingParams()
+        if len(prompt_ids) + sp.max_tokens > self.ecfg.max_model_len:
+            raise ValueError(f"prompt ({len(prompt_ids)}) + max_tokens ({sp.max_tokens}) exceeds "
+                             f"max_model_len {self.ecfg.max_model_len}")
+        req = Request(list(prompt_ids), sp, eos_token_id=self.eos, user_data=user_data)
+        if request_id is not None:
+            req.request_id = request_id
+        if arrival_time is not None:
+            req.arrival_time = arrival_time
+        self.requests[req.request_id] = req
+        self.scheduler.add(req)
+        self.stats.prompt_tokens += len(prompt_ids)
+        return req
+
+    def abort_request(self, request_id: str) -> bool:
+        return self.scheduler.abort(request_id)
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_work()
+
+    # -------------------------------------------------------------- step
+    def step(self) -> list[Request]:
+        out = self.scheduler.schedule()
+        if not out.chunks:
+            return []
+        tokens = self.executor.execute(out)
+        now = time.perf_counter()
+        finished = []
+        j = 0
+        for c in out.chunks:
+            r = c.req
+            r.carry = self.router(r.all_ids[c.start:c.start + c.num_tokens], r.carry)
+            r.num_computed = c.start + c.num_tokens
+            self.blocks.register_full_blocks(r)
+            if not c.needs_sample:
+                continue
+            tok = int(tokens[j])
+            j += 1
+            r.output_ids.append(tok)
+            self.stats.generated_tokens += 1
+            if r.first_token_time is None:
+                r.first_token_time = now
+            reason = self._stop_reason(r, tok)
+            if reason:
+                r.finish_time = now
+                self.scheduler.finish(r, reason)
+                finished.append(r)
+                self.stats.finished += 1
+                if r.ttft() is not None:
+                    self.stats.ttfts.append(r.ttft())
+                self.stats.latencies.append(r.finish_time - r.arrival_time)
+                self.requests.pop(r.request_id, None)
+                if self.on_finish is not None:
+                    self.on_finish(r)
+        self.stats.steps += 1
+        return finished
+
+    def _stop_reason(self, r: Request, tok: int) -> str | None:
+        sp = r.sampling
+        n = len(r.output_ids)
+        if n >= sp.max_tokens:
+            return "length"
+        if n >= sp.min_tokens:
+            if tok in sp.stop_token_ids:
+                return "stop"
+            if not sp.ignore_eos and r.eos_token_id is not None and tok == r.eos_token_id:
+                return "stop"
+        return None
+
+    # -------------------------------------------------------------- metrics
+    def prefix_cache_hit_rate(self) -> float:
+        return self.blocks.hits / max(1, self.blocks.queries)
+
+    def metrics(self) -> dict:
+        return {
+            "num_requests_running": len(self.scheduler.running),
+            "num_requests_waiting": len(self.scheduler.waiting),
+            "prefix_cache_queries_total": self.blocks.queries,
+            "prefix_cache_hits_total": self.blocks.hits,
+            "generation_tokens_total": self.stats.generated_tokens,
+            "prompt_tokens_total": self.stats.prompt_tokens,
+            "kv_cache_usage_perc": self.blocks.usage(),
+            "num_preemptions_total": self.scheduler.num_preemptions,
+        }
+
+
+def _to_output(r: Request) -> RequestOutput:
+    return RequestOutput(r.request_id, r.prompt_ids, r.output_ids, r.finish_reason, r.num_cached_tokens,
+                         r.ttft(), None if r.finish_time is None else r.finish_time - r.arrival_time)
+
+
+class LLM:
+    """Offline generation over a composed checkpoint (or a random-init config).
+
+    ``LLM(path)`` loads a composed Granite Switch directory; on a CUDA device it
+    runs the native kernels, on CPU the PyTorch reference executor.
+    """
+
+    def __init__(self, model: str | GraniteSwitchConfig, device: str | None = None,
+                 engine_config: EngineConfig | None = None, random_init: dict | None = None,
+                 tp_rank: int = 0, tp_group=None):
+        ecfg = engine_config or EngineConfig()
+        self.ecfg = ecfg
+        if device is None:
+            device = "cuda" if torch.cuda.is_available() else "cpu"
+        self.device = torch.device(device)
+        if isinstance(model, GraniteSwitchConfig):
+            config, path = model, None
+        else:
+            config, path = GraniteSwitchConfig.from_pretrained(model), model
+        self.config = config
+        tp = ecfg.tensor_parallel_size
+        if self.device.type == "cuda":
+            from ..models.native import NativeGraniteSwitch, default_num_kv_blocks
+            from .executor import NativeExecutor
+
+            max_tokens = max(ecfg.max_num_batched_tokens, ecfg.max_num_seqs)
+            nb = ecfg.num_kv_blocks or 64
+            if path is not None:
+                from ..checkpoint import load_state_dict
+
+                sd = load_state_dict(path)
+                nm = NativeGraniteSwitch.from_state_dict(config, sd, self.device, max_tokens, 1, tp_rank, tp,
+                                                         tp_group, ecfg.max_num_seqs)
+                del sd
+            else:
+                ri = dict(random_init or {})
+                nm = NativeGraniteSwitch.from_random(config, self.device, max_tokens, 1, tp_rank=tp_rank,
+                                                     tp_size=tp, tp_group=tp_group, max_seqs=ecfg.max_num_seqs, **ri)
+            if ecfg.num_kv_blocks is None:
+                torch.cuda.synchronize()
+                nb = default_num_kv_blocks(0, config, tp, ecfg.gpu_memory_utilization, self.device)
+            nm.num_kv_blocks = nb
+            nm._alloc_buffers()
+            self.model = nm
+            executor = NativeExecutor(nm, ecfg.max_model_len, tp_group, tp, ecfg.use_cuda_graphs)
+            if ecfg.fused_tp_comm and tp > 1:
+                from ..parallel.fused import attach_fused_comm
+
+                attach_fused_comm(nm, tp_group)
+        else:
+            from ..models.reference import GraniteSwitchForCausalLM
+            from .executor import ReferenceExecutor
+
+            if path is None:
+                raise ValueError("the CPU executor needs a checkpoint directory")
+            ref = GraniteSwitchForCausalLM.from_pretrained(path).eval()
+            nb = ecfg.num_kv_blocks or 256
+            executor = ReferenceExecutor(ref, nb)
+            self.model = ref
+        self.engine = LLMEngine(config, executor, nb, ecfg)
+
+    def generate(self, prompts: list[list[int]], sampling: SamplingParams | list[SamplingParams] | None = None) -> list[RequestOutput]:
+        sps = sampling if isinstance(sampling, list) else [sampling or SamplingParams()] * len(prompts)
+        reqs = [self.engine.add_request(p, sp) for p, sp in zip(prompts, sps)]
+        while self.engine.has_unfinished():
+            self.engine.step()
+        return [_to_output(r) for r in reqs]
+
+
+__all__ = ["LLM", "LLMEngine", "EngineConfig", "SamplingParams", "BLOCK_SIZE", "os"]

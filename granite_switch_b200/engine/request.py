@@ -1,0 +1,84 @@
+"""Request state and sampling parameters of the serving engine."""
+from __future__ import annotations
+
+import enum
+import itertools
+import time
+from dataclasses import dataclass, field
+
+_ids = itertools.count()
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 16
+    temperature: float = 0.0          # 0 = greedy
+    top_k: int = 0                    # 0 = off
+    top_p: float = 1.0
+    seed: int | None = None
+    stop_token_ids: tuple[int, ...] = ()
+    ignore_eos: bool = False
+    min_tokens: int = 0
+
+    @property
+    def greedy(self) -> bool:
+        return self.temperature <= 0.0
+
+
+class RequestStatus(enum.Enum):
+    WAITING = 0
+    RUNNING = 1
+    PREEMPTED = 2
+    FINISHED = 3
+
+
+@dataclass
+class Request:
+    prompt_ids: list[int]
+    sampling: SamplingParams = field(default_factory=SamplingParams)
+    request_id: str = field(default_factory=lambda: f"req-{next(_ids)}")
+    arrival_time: float = field(default_factory=time.perf_counter)
+    eos_token_id: int | None = None
+    output_ids: list[int] = field(default_factory=list)
+    status: RequestStatus = RequestStatus.WAITING
+    num_computed: int = 0              # tokens whose KV is in the cache
+    block_ids: list[int] = field(default_factory=list)
+    block_hashes: list[int] = field(default_factory=list)  # chained hashes of full blocks
+    num_registered_blocks: int = 0     # full blocks published to the prefix cache
+    num_cached_tokens: int = 0         # prefix-cache hit at admission
+    carry: int = 0                     # routing carry after num_computed tokens
+    matched: bool = False              # prefix cache consulted for the current admission
+    first_token_time: float | None = None
+    finish_time: float | None = None
+    finish_reason: str | None = None
+    user_data: object = None
+
+    @property
+    def all_ids(self) -> list[int]:
+        return self.prompt_ids + self.output_ids
+
+    @property
+    def num_tokens(self) -> int:
+        return len(self.prompt_ids) + len(self.output_ids)
+
+    @property
+    def prefilling(self) -> bool:
+        return self.num_computed < len(self.prompt_ids)
+
+    @property
+    def finished(self) -> bool:
+        return self.status == RequestStatus.FINISHED
+
+    def ttft(self) -> float | None:
+        return None if self.first_token_time is None else self.first_token_time - self.arrival_time
+
+
+@dataclass
+class RequestOutput:
+    request_id: str
+    prompt_ids: list[int]
+    output_ids: list[int]
+    finish_reason: str | None
+    num_cached_tokens: int
+    ttft: float | None
+    latency: float | None

@@ -1,0 +1,139 @@
+"""Continuous batching with chunked prefill (one token budget per step).
+
+Each step: running requests first (one decode token, or their next prefill
+chunk), then waiting requests in arrival order while the token budget, the
+sequence cap and free KV blocks allow. A new request first acquires its
+longest cached prefix. When a running request cannot get a block, the most
+recently admitted running request is preempted (its blocks are freed; it
+recomputes later, largely from the prefix cache).
+"""
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass, field
+
+from .kv_cache import BlockManager
+from .request import Request, RequestStatus
+
+
+@dataclass
+class ScheduledChunk:
+    req: Request
+    start: int        # first token position computed in this step
+    num_tokens: int
+
+    @property
+    def needs_sample(self) -> bool:
+        return self.start + self.num_tokens >= self.req.num_tokens
+
+
+@dataclass
+class SchedulerOutput:
+    chunks: list[ScheduledChunk] = field(default_factory=list)
+    preempted: list[Request] = field(default_factory=list)
+
+    @property
+    def num_tokens(self) -> int:
+        return sum(c.num_tokens for c in self.chunks)
+
+    @property
+    def is_decode_only(self) -> bool:
+        return all(c.num_tokens == 1 and not c.req.prefilling for c in self.chunks)
+
+
+class Scheduler:
+    def __init__(self, blocks: BlockManager, max_num_seqs: int = 256, max_num_batched_tokens: int = 8192,
+                 enable_chunked_prefill: bool = True, route_fn=None):
+        self.blocks = blocks
+        self.max_num_seqs = max_num_seqs
+        self.max_num_batched_tokens = max_num_batched_tokens
+        self.chunked = enable_chunked_prefill
+        self.waiting: deque[Request] = deque()
+        self.running: list[Request] = []
+        self.route_fn = route_fn  # (ids, carry) -> carry after ids
+        self.num_preemptions = 0
+
+    def add(self, req: Request) -> None:
+        req.status = RequestStatus.WAITING
+        self.waiting.append(req)
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def _preempt(self, req: Request, out: SchedulerOutput) -> None:
+        self.running.remove(req)
+        self.blocks.free_request(req)
+        req.num_computed = 0
+        req.carry = 0
+        req.matched = False
+        req.status = RequestStatus.PREEMPTED
+        self.waiting.appendleft(req)
+        out.preempted.append(req)
+        self.num_preemptions += 1
+
+    def schedule(self) -> SchedulerOutput:
+        out = SchedulerOutput()
+        budget = self.max_num_batched_tokens
+        scheduled = set()
+        # ---- running requests
+        i = 0
+        while i < len(self.running) and budget > 0:
+            req = self.running[i]
+            remaining = req.num_tokens - req.num_computed
+            n = min(remaining, budget) if self.chunked else remaining
+            if n <= 0 or n > budget:
+                i += 1
+                continue
+            while not self.blocks.allocate(req, req.num_computed + n):
+                victim = self.running[-1]
+                if victim is req:
+                    self._preempt(req, out)
+                    req = None
+                    break
+                self._preempt(victim, out)
+            if req is None:
+                continue
+            out.chunks.append(ScheduledChunk(req, req.num_computed, n))
+            scheduled.add(id(req))
+            budget -= n
+            i += 1
+        # ---- waiting requests
+        while self.waiting and budget > 0 and len(self.running) < self.max_num_seqs:
+            req = self.waiting[0]
+            if not req.matched:
+                req.matched = True
+                hit = self.blocks.match_prefix(req)
+                req.num_computed = hit
+                req.num_cached_tokens = hit
+                req.carry = self.route_fn(req.prompt_ids[:hit], 0) if (self.route_fn and hit) else 0
+            remaining = req.num_tokens - req.num_computed
+            n = min(remaining, budget) if self.chunked else remaining
+            if n > budget or not self.blocks.allocate(req, req.num_computed + n):
+                break  # keep arrival order; retry next step
+            self.waiting.popleft()
+            req.status = RequestStatus.RUNNING
+            self.running.append(req)
+            out.chunks.append(ScheduledChunk(req, req.num_computed, n))
+            budget -= n
+        return out
+
+    def finish(self, req: Request, reason: str) -> None:
+        req.status = RequestStatus.FINISHED
+        req.finish_reason = reason
+        if req in self.running:
+            self.running.remove(req)
+        self.blocks.free_request(req)
+
+    def abort(self, request_id: str) -> bool:
+        for q in (self.running, self.waiting):
+            for r in list(q):
+                if r.request_id == request_id:
+                    if r in self.running:
+                        self.running.remove(r)
+                    else:
+                        self.waiting.remove(r)
+                    self.blocks.free_request(r)
+                    r.status = RequestStatus.FINISHED
+                    r.finish_reason = "abort"
+                    return True
+        return False

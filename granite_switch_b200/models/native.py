@@ -339,6 +339,8 @@ class NativeGraniteSwitch:
             self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
             self._row_parallel(lw.down, act, h, mult)
         nb = b.logit_rows.numel()
+        if nb == 0:
+            return None
         xf = self.xf[:nb]
         E.rmsnorm(h, self.final_norm, cfg.rms_norm_eps, out=xf, rows=b.logit_rows)
         logits = self.logits[:nb]
