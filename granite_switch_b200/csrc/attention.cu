@@ -1,21 +1,23 @@
 // Paged causal GQA attention over the KV cache, for chunked prefill and decode.
 //
-// One CTA owns a tile of "rows" of one request and one KV head, where a row is
-// a (query token, query head of that KV group) pair: GQA heads that share a
-// KV head are packed into the M dimension so every K/V page is read once per
-// group. Queries at absolute position p attend keys [0, p] (the KV of the
-// already-cached prefix plus this chunk), so a chunk that hits the prefix
-// cache attends its cached context directly.
+// A CTA owns a tile of "rows" of one request and one KV head, where a row is a
+// (query token, query head of that KV group) pair: the GQA heads that share a
+// KV head are packed into the M dimension, so every K/V page is read once per
+// group. A query at absolute position p attends keys [0, p] (the cached prefix
+// plus this chunk), so a chunk that hits the prefix cache attends its cached
+// context directly.
 //
-//  * WARPS_M = 4: four warps x 16 rows (prefill tiles of 64 rows);
-//  * WARPS_M = 1: 16 rows, the four warps split every 64-key tile and merge
-//    their softmax states at the end (decode: a request has G rows);
-//  * nsplit > 1 additionally splits the key range across CTAs (flash-decoding)
-//    and a second kernel merges the partial results by log-sum-exp.
-//
-// K/V tiles are staged with cp.async into XOR-swizzled shared memory (double
-// buffered) and multiplied with mma.sync m16n8k16 bf16 -> fp32; the online
-// softmax runs in registers. KV cache layout: [num_blocks, Hkv, 16, D].
+// K/V pages ([num_blocks, Hkv, 16, D] bf16) are fetched by TMA: the cache is
+// viewed as a 2-D tensor of 16-token page rows, each page half (64 columns)
+// is one [16 x 64] box with 128-byte swizzle, and one producer thread issues
+// all boxes of a key tile against an mbarrier. STAGES tiles are in flight.
+// The math is mma.sync m16n8k16 (bf16 -> fp32) with the online softmax in
+// registers:
+//  * prefill layout: WARPS_M warps x 16 rows, every warp walks every key;
+//  * decode layout: 16 rows, the four warps split each key tile and merge
+//    their softmax states at the end;
+//  * nsplit > 1 splits the key range across CTAs (flash-decoding) and a merge
+//    kernel combines the partial results by log-sum-exp.
 // (reference: attention comes from vLLM's backends, called at
 // src/granite_switch/vllm/decoder/lora/decoder.py:146-174.)
 #include "common.cuh"
@@ -29,16 +31,14 @@ namespace gsb {
 
 namespace attn {
 
-constexpr int KT = 64;   // keys per tile
-constexpr int PAGE = 16; // tokens per KV page
+constexpr int PAGE = 16;  // tokens per KV page
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   const int n = valid ? 16 : 0;
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c, uint32_t& d) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -56,35 +56,46 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// byte offset of 16-byte chunk `c` of row `r` in a [rows][D] bf16 tile
-template <int D>
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-  return (uint32_t)(r * (D * 2) + ((c ^ (r & 7)) << 4));
+// Byte offset of 16-byte chunk `ch` (of D/8) of row `r` in a tile stored as
+// [D/64 halves][ROWS][64 bf16] with the TMA 128-byte swizzle (chunk ^ row%8).
+template <int ROWS>
+__device__ __forceinline__ uint32_t sw(int r, int ch) {
+  return (uint32_t)((ch >> 3) * (ROWS * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
 }  // namespace attn
 
-template <int D, int WARPS_M>
-__global__ void __launch_bounds__(128)
-    paged_attn_kernel(const __nv_bfloat16* __restrict__ q, int64_t q_stride,
-                      const __nv_bfloat16* __restrict__ k_cache, const __nv_bfloat16* __restrict__ v_cache,
+template <int D, int WARPS_M, int KT, int STAGES>
+struct AttnCfg {
+  static constexpr int WARPS = (WARPS_M == 1) ? 4 : WARPS_M;
+  static constexpr int THREADS = WARPS * 32;
+  static constexpr int ROWS = 16 * WARPS_M;
+  static constexpr int WARPS_N = (WARPS_M == 1) ? 4 : 1;
+  static constexpr int KPW = KT / WARPS_N;        // keys per warp per tile
+  static constexpr int TILE_BYTES = KT * D * 2;   // one of K or V
+  static constexpr int Q_BYTES = ROWS * D * 2;
+  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * TILE_BYTES + 256;
+};
+
+template <int D, int WARPS_M, int KT, int STAGES>
+__global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
+    paged_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                      const __nv_bfloat16* __restrict__ q, int64_t q_stride,
                       const int32_t* __restrict__ block_table, int bt_stride,
                       const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
                       const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0,
                       int Hq, int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out,
                       int64_t out_stride, float* __restrict__ ws_o, float* __restrict__ ws_lse,
-                      int nsplit, int T) {
+                      int nsplit, int T, uint32_t* err) {
   using namespace attn;
-  constexpr int ROWS = 16 * WARPS_M;
-  constexpr int WARPS_N = 4 / WARPS_M;
-  constexpr int KPW = KT / WARPS_N;  // keys per warp per tile
-  constexpr int NB = KPW / 8;        // S n-blocks per warp
-  constexpr int DC = D / 8;          // 16-byte chunks per row
-  constexpr int OB = D / 8;          // O n-blocks
-  extern __shared__ __align__(128) uint8_t smem[];
+  using C = AttnCfg<D, WARPS_M, KT, STAGES>;
+  constexpr int ROWS = C::ROWS, WARPS_N = C::WARPS_N, KPW = C::KPW, NB = KPW / 8;
+  constexpr int DC = D / 8, OB = D / 8, PAGES = KT / PAGE;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
-  uint8_t* sK = sQ + ROWS * D * 2;
-  uint8_t* sV = sK + 2 * KT * D * 2;
+  uint8_t* sKV = smem + C::Q_BYTES;  // [STAGES][K tile | V tile]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sKV + STAGES * 2 * C::TILE_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wm = (WARPS_M == 1) ? 0 : warp;
@@ -96,62 +107,75 @@ __global__ void __launch_bounds__(128)
   const int qs = q_start[seq];
   const int q_len = q_start[seq + 1] - qs;
   const int kv_len = kv_len_arr[seq];
-  const int ctx = kv_len - q_len;  // keys before the first query of this chunk
+  const int ctx = kv_len - q_len;
   const int n_rows = q_len * G;
   const int32_t* bt = block_table + (int64_t)seq * bt_stride;
 
-  // key range of this CTA: causal limit of its last row, then its split share
   const int last_row = min(row0 + ROWS, n_rows) - 1;
-  const int k_limit = min(kv_len, ctx + last_row / G + 1);
+  const int k_limit = max(0, min(kv_len, ctx + last_row / G + 1));
   int per_split = (k_limit + nsplit - 1) / nsplit;
   per_split = (per_split + KT - 1) / KT * KT;
   const int k_begin = split * per_split;
   const int k_end = min(k_limit, k_begin + per_split);
+  const int n_tiles = (k_end > k_begin) ? (k_end - k_begin + KT - 1) / KT : 0;
 
-  // ---- load Q tile
-  for (int c = threadIdx.x; c < ROWS * DC; c += blockDim.x) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  // ---- Q tile via cp.async into the swizzled [half][row][64] layout
+  for (int c = threadIdx.x; c < ROWS * DC; c += C::THREADS) {
     const int r = c / DC, ch = c % DC;
     const int gr = row0 + r;
     const bool valid = gr < n_rows;
     const int tok = valid ? gr / G : 0;
     const int head = kvh * G + (valid ? gr % G : 0);
     const __nv_bfloat16* src = q + (int64_t)(qs + tok) * q_stride + head * D + ch * 8;
-    cp_async16(smem_u32(sQ) + swz<D>(r, ch), valid ? (const void*)src : (const void*)q, valid);
+    cp_async16(smem_u32(sQ) + sw<ROWS>(r, ch), valid ? (const void*)src : (const void*)q, valid);
   }
   cp_commit();
+  __syncthreads();  // barrier init visible
 
-  auto load_kv = [&](int tile_start, int buf) {
-    for (int c = threadIdx.x; c < KT * DC; c += blockDim.x) {
-      const int r = c / DC, ch = c % DC;
-      const int j = tile_start + r;
-      const bool valid = j < k_end;
-      int64_t off = 0;
-      if (valid) {
-        const int page = bt[j / PAGE];
-        off = (((int64_t)page * Hkv + kvh) * PAGE + (j % PAGE)) * D + ch * 8;
+  // producer: one thread issues every box of a key tile
+  const int first_page = bt[0];
+  auto issue = [&](int it) {
+    const int s = it % STAGES;
+    uint8_t* dK = sKV + s * 2 * C::TILE_BYTES;
+    uint8_t* dV = dK + C::TILE_BYTES;
+    const int tile_start = k_begin + it * KT;
+    mbar_arrive_expect_tx(&full[s], 2 * C::TILE_BYTES);
+#pragma unroll
+    for (int p = 0; p < PAGES; ++p) {
+      const int j = tile_start + p * PAGE;
+      // pages past the key range still load a valid page (masked later) so no
+      // uninitialised smem (possibly NaN) ever meets a zero probability
+      const int page = (j < k_end) ? bt[j / PAGE] : first_page;
+      const int row = (page * Hkv + kvh) * PAGE;
+#pragma unroll
+      for (int h = 0; h < D / 64; ++h) {
+        tma_load_2d(dK + h * (KT * 128) + p * PAGE * 128, &tm_k, &full[s], h * 64, row);
+        tma_load_2d(dV + h * (KT * 128) + p * PAGE * 128, &tm_v, &full[s], h * 64, row);
       }
-      cp_async16(smem_u32(sK + buf * KT * D * 2) + swz<D>(r, ch), k_cache + off, valid);
-      cp_async16(smem_u32(sV + buf * KT * D * 2) + swz<D>(r, ch), v_cache + off, valid);
     }
-    cp_commit();
   };
+  int issued = 0;  // tiles whose loads were issued (thread 0 only)
+  if (threadIdx.x == 0) {
+    for (int it = 0; it < min(n_tiles, STAGES - 1); ++it) issue(it);
+    issued = min(n_tiles, STAGES - 1);
+  }
 
   float o[OB][4];
 #pragma unroll
   for (int i = 0; i < OB; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
-
   const int g = lane >> 2, t4 = lane & 3;
-  // rows (within the CTA tile) owned by this thread
   const int rA = wm * 16 + g, rB = rA + 8;
-  const int posA = ctx + (row0 + rA) / G;  // absolute position of the row's query token
+  const int posA = ctx + (row0 + rA) / G;
   const int posB = ctx + (row0 + rB) / G;
 
-  const int n_tiles = (k_end > k_begin) ? (k_end - k_begin + KT - 1) / KT : 0;
-  if (n_tiles > 0) load_kv(k_begin, 0);
-
-  // Q fragments (after the Q copy lands)
-  cp_wait<0>();
+  cp_wait_all();
   __syncthreads();
   uint32_t qf[D / 16][4];
   {
@@ -159,27 +183,26 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       const int ch = kk * 2 + (lane >> 4);
-      ldsm_x4(smem_u32(sQ) + swz<D>(r, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      ldsm_x4(smem_u32(sQ) + sw<ROWS>(r, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
     }
   }
 
+  bool ok = true;
+  int consumed = 0;
   for (int it = 0; it < n_tiles; ++it) {
-    const int tile_start = k_begin + it * KT;
-    const int buf = it & 1;
-    if (it + 1 < n_tiles) {
-      load_kv(tile_start + KT, buf ^ 1);
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
+    const int s = it % STAGES;
+    if (threadIdx.x == 0 && it + STAGES - 1 < n_tiles) {
+      issue(it + STAGES - 1);
+      issued = it + STAGES;
     }
-    __syncthreads();
-    const uint32_t kbase = smem_u32(sK + buf * KT * D * 2);
-    const uint32_t vbase = smem_u32(sV + buf * KT * D * 2);
+    const bool landed = mbar_wait(&full[s], (it / STAGES) & 1, err, kErrAttnWait);
+    const int tile_start = k_begin + it * KT;
+    const uint32_t kbase = smem_u32(sKV + s * 2 * C::TILE_BYTES);
+    const uint32_t vbase = kbase + C::TILE_BYTES;
 
-    // ---- S = Q K^T for this warp's keys
-    float s[NB][4];
+    float sacc[NB][4];
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb) s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
+    for (int nb = 0; nb < NB; ++nb) sacc[nb][0] = sacc[nb][1] = sacc[nb][2] = sacc[nb][3] = 0.f;
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
 #pragma unroll
@@ -187,12 +210,11 @@ __global__ void __launch_bounds__(128)
         const int key = wn * KPW + nb2 * 16 + (lane & 7) + ((lane >> 4) << 3);
         const int ch = kk * 2 + ((lane >> 3) & 1);
         uint32_t b0, b1, b2, b3;
-        ldsm_x4(kbase + swz<D>(key, ch), b0, b1, b2, b3);
-        mma16816(s[2 * nb2], qf[kk], b0, b1);
-        mma16816(s[2 * nb2 + 1], qf[kk], b2, b3);
+        ldsm_x4(kbase + sw<KT>(key, ch), b0, b1, b2, b3);
+        mma16816(sacc[2 * nb2], qf[kk], b0, b1);
+        mma16816(sacc[2 * nb2 + 1], qf[kk], b2, b3);
       }
     }
-    // ---- mask + online softmax (log2 domain)
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
@@ -200,9 +222,9 @@ __global__ void __launch_bounds__(128)
       for (int e = 0; e < 4; ++e) {
         const int j = tile_start + wn * KPW + nb * 8 + 2 * t4 + (e & 1);
         const int pos = (e < 2) ? posA : posB;
-        float v = s[nb][e] * scale_log2;
+        float v = sacc[nb][e] * scale_log2;
         if (j >= k_end || j > pos) v = -INFINITY;
-        s[nb][e] = v;
+        sacc[nb][e] = v;
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
     }
@@ -221,8 +243,8 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float mm = m_r[e >> 1];
-        const float p = (mm == -INFINITY) ? 0.f : exp2f(s[nb][e] - mm);
-        s[nb][e] = p;
+        const float p = (mm == -INFINITY) ? 0.f : exp2f(sacc[nb][e] - mm);
+        sacc[nb][e] = p;
         rs[e >> 1] += p;
       }
     }
@@ -239,32 +261,45 @@ __global__ void __launch_bounds__(128)
       o[i][2] *= corr[1];
       o[i][3] *= corr[1];
     }
-    // ---- O += P V
 #pragma unroll
     for (int kk = 0; kk < KPW / 16; ++kk) {
       uint32_t pa[4];
-      pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
-      pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
-      pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      pa[0] = pack_bf16x2(sacc[2 * kk][0], sacc[2 * kk][1]);
+      pa[1] = pack_bf16x2(sacc[2 * kk][2], sacc[2 * kk][3]);
+      pa[2] = pack_bf16x2(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+      pa[3] = pack_bf16x2(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
 #pragma unroll
       for (int db = 0; db < D / 16; ++db) {
         const int key = wn * KPW + kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
         const int ch = db * 2 + (lane >> 4);
         uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vbase + swz<D>(key, ch), b0, b1, b2, b3);
+        ldsm_x4_t(vbase + sw<KT>(key, ch), b0, b1, b2, b3);
         mma16816(o[2 * db], pa, b0, b1);
         mma16816(o[2 * db + 1], pa, b2, b3);
       }
     }
+    // every warp is done with stage s before it is refilled; a lost TMA
+    // completion in any thread stops every thread at the same point
+    if (!__syncthreads_and(landed)) {
+      ok = false;
+      break;
+    }
+    consumed = it + 1;
+  }
+  if (!ok) {
+    // drain the copies that may still land in our shared memory, then leave
+    if (threadIdx.x == 0)
+      for (int it = consumed; it < issued; ++it)
+        mbar_wait(&full[it % STAGES], (it / STAGES) & 1, err, kErrAttnWait);
     __syncthreads();
+    return;
   }
 
   // ---- merge the key-split warps (decode layout)
   if (WARPS_N > 1) {
-    float* sm = reinterpret_cast<float*>(sK);       // [WARPS_N][16] max
-    float* sl = sm + WARPS_N * 16;                  // [WARPS_N][16] sum
-    float* so = sl + WARPS_N * 16;                  // [WARPS_N][16][D]
+    float* sm = reinterpret_cast<float*>(sKV);
+    float* sl = sm + WARPS_N * 16;
+    float* so = sl + WARPS_N * 16;  // [WARPS_N][16][D]
     if (t4 == 0) {
       sm[wn * 16 + g] = m_r[0];
       sm[wn * 16 + g + 8] = m_r[1];
@@ -272,17 +307,12 @@ __global__ void __launch_bounds__(128)
       sl[wn * 16 + g + 8] = l_r[1];
     }
     __syncthreads();
-    float mt[2], lt[2] = {0.f, 0.f}, my[2];
+    float my[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int r = g + 8 * h;
       float m = -INFINITY;
       for (int k = 0; k < WARPS_N; ++k) m = fmaxf(m, sm[k * 16 + r]);
-      mt[h] = m;
-      for (int k = 0; k < WARPS_N; ++k) {
-        const float mk = sm[k * 16 + r];
-        lt[h] += (mk == -INFINITY) ? 0.f : sl[k * 16 + r] * exp2f(mk - m);
-      }
       my[h] = (m_r[h] == -INFINITY) ? 0.f : exp2f(m_r[h] - m);
     }
 #pragma unroll
@@ -294,19 +324,19 @@ __global__ void __launch_bounds__(128)
       so[(wn * 16 + g + 8) * D + col + 1] = o[i][3] * my[1];
     }
     __syncthreads();
-    // every thread finalises a slice of the 16 x D tile
-    for (int idx = threadIdx.x; idx < 16 * D; idx += blockDim.x) {
+    for (int idx = threadIdx.x; idx < 16 * D; idx += C::THREADS) {
       const int r = idx / D, col = idx % D;
-      float acc = 0.f;
-      for (int k = 0; k < WARPS_N; ++k) acc += so[(k * 16 + r) * D + col];
-      float m = -INFINITY, l = 0.f;
-      for (int k = 0; k < WARPS_N; ++k) m = fmaxf(m, sm[k * 16 + r]);
+      const int gr = row0 + r;
+      if (gr >= n_rows) continue;
+      float acc = 0.f, m = -INFINITY, l = 0.f;
+      for (int k = 0; k < WARPS_N; ++k) {
+        acc += so[(k * 16 + r) * D + col];
+        m = fmaxf(m, sm[k * 16 + r]);
+      }
       for (int k = 0; k < WARPS_N; ++k) {
         const float mk = sm[k * 16 + r];
         l += (mk == -INFINITY) ? 0.f : sl[k * 16 + r] * exp2f(mk - m);
       }
-      const int gr = row0 + r;
-      if (gr >= n_rows) continue;
       const int tok = qs + gr / G, head = kvh * G + gr % G;
       const float val = (l > 0.f) ? acc / l : 0.f;
       if (nsplit == 1) {
@@ -317,12 +347,9 @@ __global__ void __launch_bounds__(128)
           ws_lse[((int64_t)split * T + tok) * Hq + head] = (l > 0.f) ? (m + log2f(l)) : -INFINITY;
       }
     }
-    (void)mt;
-    (void)lt;
     return;
   }
 
-  // ---- write (WARPS_M = 4 layout: each warp owns its 16 rows)
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int r = wm * 16 + g + 8 * h;
@@ -346,17 +373,15 @@ __global__ void __launch_bounds__(128)
         wp[col + 1] = o[i][2 * h + 1] * inv;
       }
       if (t4 == 0)
-        ws_lse[((int64_t)split * T + tok) * Hq + head] =
-            (l_r[h] > 0.f) ? (m_r[h] + log2f(l_r[h])) : -INFINITY;
+        ws_lse[((int64_t)split * T + tok) * Hq + head] = (l_r[h] > 0.f) ? (m_r[h] + log2f(l_r[h])) : -INFINITY;
     }
   }
 }
 
 // Merge flash-decoding partials: out = sum_s 2^(lse_s - M) o_s / sum_s 2^(lse_s - M).
 template <int D>
-__global__ void attn_merge_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse,
-                                  int nsplit, int T, int Hq, __nv_bfloat16* __restrict__ out,
-                                  int64_t out_stride) {
+__global__ void attn_merge_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, int nsplit,
+                                  int T, int Hq, __nv_bfloat16* __restrict__ out, int64_t out_stride) {
   const int tok = blockIdx.x, head = blockIdx.y;
   float m = -INFINITY;
   for (int s = 0; s < nsplit; ++s) m = fmaxf(m, ws_lse[((int64_t)s * T + tok) * Hq + head]);
@@ -377,45 +402,44 @@ __global__ void attn_merge_kernel(const float* __restrict__ ws_o, const float* _
 
 using namespace gsb;
 
-template <int D, int WM>
-static void launch_attn(dim3 grid, cudaStream_t st, const at::Tensor& q, const at::Tensor& kc,
-                        const at::Tensor& vc, const at::Tensor& bt, const at::Tensor& q_start,
-                        const at::Tensor& kv_len, const at::Tensor& work_seq, const at::Tensor& work_row0,
-                        int Hq, int Hkv, float scale_log2, const at::Tensor& out, float* wso, float* wsl,
-                        int nsplit, int T) {
-  constexpr int ROWS = 16 * WM;
-  const int smem = ROWS * D * 2 + 2 * 2 * attn::KT * D * 2;
-  auto kfn = paged_attn_kernel<D, WM>;
+template <int D, int WM, int KT, int ST>
+static void launch_attn(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const CUtensorMap& tv,
+                        const at::Tensor& q, const at::Tensor& bt, const at::Tensor& q_start, const at::Tensor& kv_len,
+                        const at::Tensor& work_seq, const at::Tensor& work_row0, int Hq, int Hkv, float scale_log2,
+                        const at::Tensor& out, float* wso, float* wsl, int nsplit, int T, uint32_t* err) {
+  using C = AttnCfg<D, WM, KT, ST>;
+  auto kfn = paged_attn_kernel<D, WM, KT, ST>;
   static bool configured = false;
   if (!configured) {
-    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured = true;
   }
-  kfn<<<grid, 128, smem, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
-      reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()),
-      bt.data_ptr<int32_t>(), (int)bt.stride(0), q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
-      work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv, scale_log2,
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), wso, wsl, nsplit, T);
+  kfn<<<grid, C::THREADS, C::SMEM, st>>>(
+      tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), bt.data_ptr<int32_t>(),
+      (int)bt.stride(0), q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(), work_seq.data_ptr<int32_t>(),
+      work_row0.data_ptr<int32_t>(), Hq, Hkv, scale_log2, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+      out.stride(0), wso, wsl, nsplit, T, err);
   GSB_CUDA_CHECK(cudaGetLastError());
 }
 
 // q: [T, >= Hq*D] bf16 (row stride q.stride(0)); caches [num_blocks, Hkv, 16, D];
 // block_table [S, max_blocks] int32; q_start [S+1] int32 (token offsets of each
 // request chunk in q); kv_len [S] int32 (cached + new keys); work_seq/work_row0
-// [n_work] int32: the (request, first row) of each CTA tile; rows_per_tile
-// selects the layout (64: prefill, 16: decode); out [T, Hq*D] bf16.
+// [n_work] int32: the (request, first row) of each CTA tile. rows_per_tile
+// selects the layout: 128 (prefill, 8 warps), 64 (prefill, 4 warps) or 16
+// (decode, warps split keys). out [T, Hq*D] bf16.
 void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                          const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
                          const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t rows_per_tile,
                          int64_t num_q_heads, double scale, const at::Tensor& out, int64_t nsplit,
-                         const c10::optional<at::Tensor>& ws_o, const c10::optional<at::Tensor>& ws_lse) {
+                         const c10::optional<at::Tensor>& ws_o, const c10::optional<at::Tensor>& ws_lse,
+                         const at::Tensor& err) {
   GSB_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16 &&
                 out.scalar_type() == at::kBFloat16,
             "attention: bf16 tensors required");
   GSB_CHECK(k_cache.dim() == 4 && k_cache.size(2) == attn::PAGE && k_cache.is_contiguous() &&
-                v_cache.is_contiguous(),
-            "attention: cache must be contiguous [num_blocks, Hkv, 16, D]");
+                v_cache.is_contiguous() && v_cache.sizes() == k_cache.sizes(),
+            "attention: caches must be contiguous [num_blocks, Hkv, 16, D]");
   GSB_CHECK(block_table.scalar_type() == at::kInt && q_start.scalar_type() == at::kInt &&
                 kv_len.scalar_type() == at::kInt && work_seq.scalar_type() == at::kInt &&
                 work_row0.scalar_type() == at::kInt,
@@ -439,27 +463,30 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
     wso = ws_o->data_ptr<float>();
     wsl = ws_lse->data_ptr<float>();
   }
+  const int64_t page_rows = k_cache.size(0) * (int64_t)Hkv * attn::PAGE;
+  GSB_CHECK(page_rows < (int64_t(1) << 31), "attention: cache too large for 32-bit TMA coordinates");
   c10::cuda::CUDAGuard guard(q.device());
   auto st = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
+  CUtensorMap tk = make_tmap_bf16_2d(k_cache.data_ptr(), page_rows, D, D, 64, attn::PAGE, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, attn::PAGE, CU_TENSOR_MAP_SWIZZLE_128B);
+  uint32_t* ep = reinterpret_cast<uint32_t*>(err.data_ptr());
   const float scale_log2 = (float)(scale * 1.4426950408889634);
   dim3 grid(n_work, Hkv, (unsigned)nsplit);
+#define GSB_ATTN(DD, WM, KT, ST)                                                                              \
+  launch_attn<DD, WM, KT, ST>(grid, st, tk, tv, q, block_table, q_start, kv_len, work_seq, work_row0, Hq, Hkv, \
+                              scale_log2, out, wso, wsl, (int)nsplit, T, ep)
   if (D == 128) {
-    if (rows_per_tile == 64)
-      launch_attn<128, 4>(grid, st, q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0, Hq,
-                          Hkv, scale_log2, out, wso, wsl, (int)nsplit, T);
-    else
-      launch_attn<128, 1>(grid, st, q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0, Hq,
-                          Hkv, scale_log2, out, wso, wsl, (int)nsplit, T);
+    if (rows_per_tile == 128) GSB_ATTN(128, 8, 64, 2);
+    else if (rows_per_tile == 64) GSB_ATTN(128, 4, 64, 2);
+    else GSB_ATTN(128, 1, 64, 3);
   } else if (D == 64) {
-    if (rows_per_tile == 64)
-      launch_attn<64, 4>(grid, st, q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0, Hq,
-                         Hkv, scale_log2, out, wso, wsl, (int)nsplit, T);
-    else
-      launch_attn<64, 1>(grid, st, q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0, Hq,
-                         Hkv, scale_log2, out, wso, wsl, (int)nsplit, T);
+    if (rows_per_tile == 128) GSB_ATTN(64, 8, 64, 3);
+    else if (rows_per_tile == 64) GSB_ATTN(64, 4, 64, 3);
+    else GSB_ATTN(64, 1, 64, 6);
   } else {
     GSB_CHECK(false, "attention: head_dim must be 64 or 128, got ", D);
   }
+#undef GSB_ATTN
   if (nsplit > 1) {
     dim3 g2(T, Hq);
     if (D == 128)

@@ -26,6 +26,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 
+#include <algorithm>
+
 namespace gsb {
 
 enum EpiKind : int {
@@ -65,10 +67,51 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;     // BN * 128 B
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int TMEM_COLS = 2 * BN;        // two accumulator buffers
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// Tile order: groups of 16 M-tiles, M fastest inside a group, so the CTAs that
+// run at the same time share weight tiles (B) in L2 and touch a bounded slice
+// of activations (A).
+__device__ __forceinline__ void gemm_tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
+  constexpr int GM = 16;
+  const int group = t / (GM * n_tiles);
+  const int first_m = group * GM;
+  const int gm = min(GM, m_tiles - first_m);
+  const int r = t - group * GM * n_tiles;
+  mt = first_m + r % gm;
+  nt = r / gm;
+}
+
+struct LoraTile {
+  uint64_t amask;
+  int s_base0, s_base1;
+  int blocks;
+};
+
+template <bool SPLIT>
+__device__ __forceinline__ LoraTile lora_tile(const GemmLoraArgs& lora, int m_tile, int n0) {
+  LoraTile lt{0, 0, 0, 0};
+  if (!lora.enabled) return lt;
+  lt.amask = lora.tile_mask ? lora.tile_mask[m_tile]
+                            : ((lora.num_adapters >= 64) ? ~0ull : ((1ull << lora.num_adapters) - 1));
+  const int slice_cols = lora.num_adapters * lora.rank_blocks * 32;
+  if (SPLIT) {
+    lt.s_base1 = slice_cols;
+  } else {
+    int s = 0;
+    for (int i = 0; i < lora.num_slices; ++i)
+      if (n0 >= lora.slice_bounds[i]) s = i;
+    lt.s_base0 = s * slice_cols;
+  }
+  lt.blocks = __popcll(lt.amask) * lora.rank_blocks;
+  return lt;
+}
+
+// Persistent: one CTA per SM walks tiles t = blockIdx.x, +gridDim.x, ...
+// TMEM holds two accumulators so the epilogue of tile i overlaps the
+// mainloop of tile i+1.
 template <int BN, int EPI, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
     switched_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
@@ -82,45 +125,27 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
   uint64_t* empty_bar = full_bar + C::STAGES;
-  uint64_t* tmem_full_bar = empty_bar + C::STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_full_bar + 1);
+  uint64_t* tfull_bar = empty_bar + C::STAGES;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;          // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int n_tile = blockIdx.x;
-  const int m_tile = blockIdx.y;
-  const int n0 = n_tile * BN;
-  const int m0 = m_tile * C::BM;
-
-  // ---- LoRA schedule for this tile -------------------------------------------
-  uint64_t amask = 0;
-  int s_base0 = 0, s_base1 = 0;
-  if (lora.enabled) {
-    amask = lora.tile_mask ? lora.tile_mask[m_tile]
-                           : ((lora.num_adapters >= 64) ? ~0ull
-                                                        : ((1ull << lora.num_adapters) - 1));
-    const int slice_cols = lora.num_adapters * lora.rank_blocks * 32;
-    if (SPLIT) {
-      s_base0 = 0;
-      s_base1 = slice_cols;
-    } else {
-      int s = 0;
-      for (int i = 0; i < lora.num_slices; ++i)
-        if (n0 >= lora.slice_bounds[i]) s = i;
-      s_base0 = s * slice_cols;
-    }
-  }
+  const int m_tiles = (M + C::BM - 1) / C::BM;
+  const int n_tiles = N / BN;
+  const int num_tiles = m_tiles * n_tiles;
   const int main_blocks = K / C::BK;
-  const int lora_blocks = __popcll(amask) * lora.rank_blocks;
-  const int total_blocks = main_blocks + (lora.enabled ? lora_blocks : 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(tmem_full_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 4);  // one arrive per epilogue warp
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -144,43 +169,49 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int issued = 0;
-      int a_iter = 0, rb_iter = 0;  // LoRA cursor: adapter bit index, rank block
-      uint64_t rem = amask;
-      for (int i = 0; i < total_blocks; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
-        if (*abort_flag || !mbar_wait(&empty_bar[s], ph ^ 1, err, kErrGemmWait)) {
-          *abort_flag = 1;
-          break;
-        }
-        uint8_t* sa = smem + s * C::STAGE_BYTES;
-        uint8_t* sb = sa + C::A_BYTES;
-        if (i < main_blocks) {
-          mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
-          tma_load_2d(sa, &tm_a, &full_bar[s], i * C::BK, m0);
-          tma_load_2d(sb, &tm_b, &full_bar[s], i * C::BK, n0);
-        } else {
-          if (rb_iter == 0) {
-            a_iter = __ffsll((long long)rem) - 1;  // adapter bit (kernel-local id - 1)
+      uint32_t kb = 0;  // k-blocks issued by this CTA (ring position)
+      bool stop = false;
+      for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x) {
+        int mt, nt;
+        gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
+        const int m0 = mt * C::BM, n0 = nt * BN;
+        const LoraTile lt = lora_tile<SPLIT>(lora, mt, n0);
+        const int total = main_blocks + lt.blocks;
+        uint64_t rem = lt.amask;
+        int a_bit = 0, rb = 0;
+        for (int i = 0; i < total; ++i, ++kb) {
+          const int s = kb % C::STAGES;
+          const uint32_t ph = (kb / C::STAGES) & 1;
+          if (*abort_flag || !mbar_wait(&empty_bar[s], ph ^ 1, err, kErrGemmWait)) {
+            *abort_flag = 1;
+            stop = true;
+            break;
           }
-          const int kcol = a_iter * lora.rank_blocks * 32 + rb_iter * 32;
-          const int nsub = SPLIT ? 2 : 1;
-          const uint32_t bytes = nsub * (C::BM * 32 * 2) + BN * 32 * 2;
-          mbar_arrive_expect_tx(&full_bar[s], bytes);
-          tma_load_2d(sa, &tm_s, &full_bar[s], s_base0 + kcol, m0);
-          if (SPLIT) tma_load_2d(sa + C::BM * 64, &tm_s, &full_bar[s], s_base1 + kcol, m0);
-          tma_load_2d(sb, &tm_lb, &full_bar[s], kcol, n0);
-          if (++rb_iter == lora.rank_blocks) {
-            rb_iter = 0;
-            rem &= rem - 1;
+          uint8_t* sa = smem + s * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          if (i < main_blocks) {
+            mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+            tma_load_2d(sa, &tm_a, &full_bar[s], i * C::BK, m0);
+            tma_load_2d(sb, &tm_b, &full_bar[s], i * C::BK, n0);
+          } else {
+            if (rb == 0) a_bit = __ffsll((long long)rem) - 1;
+            const int kcol = a_bit * lora.rank_blocks * 32 + rb * 32;
+            constexpr int nsub = SPLIT ? 2 : 1;
+            mbar_arrive_expect_tx(&full_bar[s], nsub * (C::BM * 32 * 2) + BN * 32 * 2);
+            tma_load_2d(sa, &tm_s, &full_bar[s], lt.s_base0 + kcol, m0);
+            if (SPLIT) tma_load_2d(sa + C::BM * 64, &tm_s, &full_bar[s], lt.s_base1 + kcol, m0);
+            tma_load_2d(sb, &tm_lb, &full_bar[s], kcol, n0);
+            if (++rb == lora.rank_blocks) {
+              rb = 0;
+              rem &= rem - 1;
+            }
           }
         }
-        ++issued;
       }
-      // Drain: make sure no TMA write is still in flight into our smem.
       if (*abort_flag) {
-        for (int j = (issued > C::STAGES ? issued - C::STAGES : 0); j < issued; ++j)
+        // drain: no TMA write may still be in flight into our smem at exit
+        const uint32_t first = kb > (uint32_t)C::STAGES ? kb - C::STAGES : 0;
+        for (uint32_t j = first; j < kb; ++j)
           mbar_wait(&full_bar[j % C::STAGES], (j / C::STAGES) & 1, err, kErrGemmWait);
       }
     }
@@ -189,55 +220,74 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       const uint32_t idesc_full = umma_idesc_bf16(128, BN);
       const uint32_t idesc_half = umma_idesc_bf16(128, SPLIT ? BN / 2 : BN);
-      bool ok = true;
-      for (int i = 0; i < total_blocks; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
-        if (*abort_flag || !mbar_wait(&full_bar[s], ph, err, kErrGemmWait)) {
+      uint32_t kb = 0;
+      int ltile = 0;
+      bool stop = false;
+      for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x, ++ltile) {
+        int mt, nt;
+        gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
+        const LoraTile lt = lora_tile<SPLIT>(lora, mt, nt * BN);
+        const int total = main_blocks + lt.blocks;
+        const int acc = ltile & 1;
+        if (*abort_flag || !mbar_wait(&tempty_bar[acc], ((ltile >> 1) & 1) ^ 1, err, kErrGemmWait)) {
           *abort_flag = 1;
-          ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
-        const uint32_t sb = sa + C::A_BYTES;
-        if (i < main_blocks) {
-          const uint64_t ad = umma_desc_sw128(sa);
-          const uint64_t bd = umma_desc_sw128(sb);
+        const uint32_t tacc = tmem_base + acc * BN;
+        for (int i = 0; i < total; ++i, ++kb) {
+          const int s = kb % C::STAGES;
+          const uint32_t ph = (kb / C::STAGES) & 1;
+          if (*abort_flag || !mbar_wait(&full_bar[s], ph, err, kErrGemmWait)) {
+            *abort_flag = 1;
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+          if (i < main_blocks) {
+            const uint64_t ad = umma_desc_sw128(sa);
+            const uint64_t bd = umma_desc_sw128(sb);
 #pragma unroll
-          for (int kk = 0; kk < C::BK / 16; ++kk)
-            umma_bf16(tmem_base, ad + 2 * kk, bd + 2 * kk, idesc_full, (i | kk) != 0);
-        } else {
-          if (SPLIT) {
+            for (int kk = 0; kk < C::BK / 16; ++kk)
+              umma_bf16(tacc, ad + 2 * kk, bd + 2 * kk, idesc_full, (i | kk) != 0);
+          } else if (SPLIT) {
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const uint64_t ad = umma_desc_sw64(sa + u * C::BM * 64);
               const uint64_t bd = umma_desc_sw64(sb + u * (BN / 2) * 64);
 #pragma unroll
               for (int kk = 0; kk < 2; ++kk)
-                umma_bf16(tmem_base + u * (BN / 2), ad + 2 * kk, bd + 2 * kk, idesc_half, 1);
+                umma_bf16(tacc + u * (BN / 2), ad + 2 * kk, bd + 2 * kk, idesc_half, 1);
             }
           } else {
             const uint64_t ad = umma_desc_sw64(sa);
             const uint64_t bd = umma_desc_sw64(sb);
 #pragma unroll
-            for (int kk = 0; kk < 2; ++kk)
-              umma_bf16(tmem_base, ad + 2 * kk, bd + 2 * kk, idesc_full, 1);
+            for (int kk = 0; kk < 2; ++kk) umma_bf16(tacc, ad + 2 * kk, bd + 2 * kk, idesc_full, 1);
           }
+          umma_commit(&empty_bar[s]);
         }
-        umma_commit(&empty_bar[s]);
+        umma_commit(&tfull_bar[acc]);
       }
-      (void)ok;
-      umma_commit(tmem_full_bar);
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = m0 + q * 32 + lane;
-    const bool ok = mbar_wait(tmem_full_bar, 0, err, kErrGemmWait);
-    tc_fence_after();
-    if (ok && !*abort_flag) {
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16);
+    int ltile = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++ltile) {
+      int mt, nt;
+      gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
+      const int m0 = mt * C::BM, n0 = nt * BN;
+      const int acc = ltile & 1;
+      if (*abort_flag || !mbar_wait(&tfull_bar[acc], (ltile >> 1) & 1, err, kErrGemmWait)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
       if (EPI == kEpiSwiGLU) {
         for (int c = 0; c < BN / 2; c += 32) {
           uint32_t g[32], u[32];
@@ -245,23 +295,21 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld32(tbase + BN / 2 + c, u);
           tmem_wait_ld();
           if (row < M) {
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(epi.out) + (int64_t)row * epi.ldo +
-                               (n0 / 2) + c;
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(epi.out) + (int64_t)row * epi.ldo + (n0 / 2) + c;
             uint32_t pk[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              // The gate/up pre-activations are rounded to bf16 first, as the
-              // unfused path stores them in bf16 before the activation.
-              float g0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * j]) * epi.scale));
-              float g1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * j + 1]) * epi.scale));
-              float u0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[2 * j]) * epi.scale));
-              float u1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[2 * j + 1]) * epi.scale));
-              pk[j] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+              // gate/up pre-activations are rounded to bf16 first, as the
+              // unfused path stores them in bf16 before the activation
+              const float g0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * j])));
+              const float g1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * j + 1])));
+              const float u0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[2 * j])));
+              const float u1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[2 * j + 1])));
+              pk[j] = pack_bf16x2(__fdividef(g0, 1.f + __expf(-g0)) * u0, __fdividef(g1, 1.f + __expf(-g1)) * u1);
             }
             uint4* o4 = reinterpret_cast<uint4*>(o);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            for (int j = 0; j < 4; ++j) o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
           }
         }
       } else {
@@ -274,57 +322,53 @@ __global__ void __launch_bounds__(192, 1)
           if (row >= M) continue;
           const int col = n0 + c;
           if (EPI == kEpiF32) {
-            float* o = reinterpret_cast<float*>(epi.out) + (int64_t)row * epi.ldo + col;
-            float4* o4 = reinterpret_cast<float4*>(o);
+            float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(epi.out) + (int64_t)row * epi.ldo + col);
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              o4[j] = make_float4(__uint_as_float(r[4 * j]) * epi.scale,
-                                  __uint_as_float(r[4 * j + 1]) * epi.scale,
-                                  __uint_as_float(r[4 * j + 2]) * epi.scale,
-                                  __uint_as_float(r[4 * j + 3]) * epi.scale);
+              o4[j] = make_float4(__uint_as_float(r[4 * j]) * epi.scale, __uint_as_float(r[4 * j + 1]) * epi.scale,
+                                  __uint_as_float(r[4 * j + 2]) * epi.scale, __uint_as_float(r[4 * j + 3]) * epi.scale);
           } else {
             float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * epi.scale;
-            if (EPI == kEpiMaskAdapter) {
-              // Columns of this chunk belong to one adapter when rank >= 32;
-              // evaluate per column to also cover rank 16 groups.
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int a = ((col + j) / epi.mask_rank) % epi.mask_num_adapters + 1;
-                if (a != radapter) v[j] = 0.f;
-              }
-            }
             if (EPI == kEpiResAdd) {
-              const uint4* r4 = reinterpret_cast<const uint4*>(epi.residual +
-                                                               (int64_t)row * epi.ldr + col);
+              const uint4* r4 = reinterpret_cast<const uint4*>(epi.residual + (int64_t)row * epi.ldr + col);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
-                uint4 w = r4[j];
-                uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+                const uint4 w = r4[j];
+                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                  // Round the projection to bf16 before the residual add, as
-                  // the unfused path materialises it in bf16.
-                  float2 f = unpack_bf16x2(ww[t]);
-                  float p0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * j + 2 * t])));
-                  float p1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * j + 2 * t + 1])));
-                  v[8 * j + 2 * t] = f.x + p0 * epi.scale;
-                  v[8 * j + 2 * t + 1] = f.y + p1 * epi.scale;
+                for (int tt = 0; tt < 4; ++tt) {
+                  // the projection is rounded to bf16 before the residual add, as
+                  // the unfused path materialises it in bf16
+                  const float2 f = unpack_bf16x2(ww[tt]);
+                  const float p0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * j + 2 * tt])));
+                  const float p1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * j + 2 * tt + 1])));
+                  v[8 * j + 2 * tt] = f.x + p0 * epi.scale;
+                  v[8 * j + 2 * tt + 1] = f.y + p1 * epi.scale;
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * epi.scale;
+              if (EPI == kEpiMaskAdapter) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const int a = ((col + j) / epi.mask_rank) % epi.mask_num_adapters + 1;
+                  if (a != radapter) v[j] = 0.f;
                 }
               }
             }
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(epi.out) + (int64_t)row * epi.ldo + col;
-            uint4* o4 = reinterpret_cast<uint4*>(o);
+            uint4* o4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(epi.out) + (int64_t)row * epi.ldo + col);
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-              o4[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]),
-                                 pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
-                                 pack_bf16x2(v[8 * j + 4], v[8 * j + 5]),
-                                 pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+              o4[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                                 pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
           }
         }
       }
+      // accumulator drained: hand the TMEM buffer back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
     }
   }
 
@@ -336,10 +380,20 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-
 // ---------------------------------------------------------------------------
 // Host launcher
 // ---------------------------------------------------------------------------
+static int num_sms_for_current_device() {
+  static int cached[64] = {0};
+  int dev = 0;
+  GSB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int n = 0;
+  GSB_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
 template <int BN, int EPI, bool SPLIT>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ts,
                         const CUtensorMap& tlb, int M, int N, int K, const GemmLoraArgs& lora,
@@ -348,11 +402,11 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   auto kfn = switched_gemm_kernel<BN, EPI, SPLIT>;
   static bool configured = false;  // per instantiation; attribute is per-function
   if (!configured) {
-    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        C::SMEM_BYTES));
+    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     configured = true;
   }
-  dim3 grid(N / BN, (M + C::BM - 1) / C::BM);
+  const int tiles = (N / BN) * ((M + C::BM - 1) / C::BM);
+  const int grid = std::min(tiles, num_sms_for_current_device());
   kfn<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, M, N, K, lora, epi, err);
   GSB_CUDA_CHECK(cudaGetLastError());
 }

@@ -5,7 +5,7 @@ import math
 
 import torch
 
-from .._native import native
+from .._native import err_buffer, native
 
 NUM_SMS = 148
 
@@ -34,7 +34,8 @@ def paged_attention(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq,
                     rows_per_tile: int, num_q_heads: int, scale: float, out, nsplit: int = 1,
                     ws_o=None, ws_lse=None):
     native().paged_attention(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
-                             rows_per_tile, num_q_heads, float(scale), out, nsplit, ws_o, ws_lse)
+                             rows_per_tile, num_q_heads, float(scale), out, nsplit, ws_o, ws_lse,
+                             err_buffer(q.device))
     return out
 
 

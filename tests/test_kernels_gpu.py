@@ -146,7 +146,7 @@ def _make_cache(lens, hkv, d, seed=0):
 
 
 @pytest.mark.parametrize("d", [64, 128])
-@pytest.mark.parametrize("mode", ["prefill", "decode"])
+@pytest.mark.parametrize("mode", ["prefill", "prefill128", "decode"])
 @pytest.mark.parametrize("nsplit", [1, 3])
 def test_paged_attention(d, mode, nsplit):
     from granite_switch_b200.ops import attention as A
@@ -158,9 +158,9 @@ def test_paged_attention(d, mode, nsplit):
         kv_lens = [1, 37, 300, 1025, 64]
         rows = 16
     else:
-        q_lens = [5, 64, 130, 1]
-        kv_lens = [5, 200, 130, 77]
-        rows = 64
+        q_lens = [5, 64, 130, 1, 40]
+        kv_lens = [5, 200, 130, 77, 1000]
+        rows = 128 if mode == "prefill128" else 64
     kc, vc, bt = _make_cache(kv_lens, hkv, d)
     T = sum(q_lens)
     q = torch.randn(T, (hq + 2 * hkv) * d, device="cuda").bfloat16()  # qkv buffer, q at the front
