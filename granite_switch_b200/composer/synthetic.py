@@ -114,3 +114,81 @@ def compose_synthetic(out_dir: str, preset: str | dict = "tiny", num_adapters: i
                              technology=technology, seed=seed + 1)
     return compose_checkpoint(cfg, base, ads, out_dir, dtype=dtype, base_reset=base_reset,
                               base_model_name=f"synthetic-{preset if isinstance(preset, str) else 'custom'}")
+
+
+def write_random_checkpoint(out_dir: str, config, device="cuda", seed: int = 0, std: float = 0.02,
+                            lora_groups=("qkv_proj", "o_proj"), rank: int = 32,
+                            max_shard_bytes: int = 4 * 1024 ** 3) -> None:
+    """Write a composed checkpoint of ``config`` with random weights, generated on ``device``.
+
+    For large shapes (the Granite-8B benchmark model) where composing from a
+    random base on the CPU would be slow: tensors are drawn in bf16 directly
+    in the composed layout and written shard by shard.
+    """
+    import json
+    import os
+
+    from safetensors.torch import save_file
+
+    from ..routing.codebook import KerdockDGCodeGenerator
+    from ..routing.token_exchange import build_control_to_substitute_lut
+
+    os.makedirs(out_dir, exist_ok=True)
+    g = torch.Generator(device=device).manual_seed(seed)
+    h, d = config.hidden_size, config.head_dim_eff
+    q, kv = config.num_attention_heads * d, config.num_key_value_heads * d
+    inter = config.shared_intermediate_size
+    na, r = config.num_adapters, config.max_lora_rank
+
+    def rnd(*shape, s=std):
+        return (torch.randn(*shape, generator=g, device=device) * s).to(torch.bfloat16)
+
+    shards, cur, size = [], {}, 0
+
+    def put(name, t):
+        nonlocal cur, size
+        n = t.numel() * t.element_size()
+        if cur and size + n > max_shard_bytes:
+            shards.append(cur)
+            cur, size = {}, 0
+        cur[name] = t.cpu()
+        size += n
+
+    put("model.embed_tokens.weight", rnd(config.vocab_size, h))
+    put("model.norm.weight", torch.ones(h, dtype=torch.bfloat16))
+    if not config.tie_word_embeddings:
+        put("lm_head.weight", rnd(config.vocab_size, h))
+    groups = {"qkv_proj": ("self_attn.qkv_proj", [q, kv, kv], h), "o_proj": ("self_attn.o_proj", [h], q),
+              "shared_input_linear": ("shared_mlp.input_linear", [inter, inter], h),
+              "shared_output_linear": ("shared_mlp.output_linear", [h], inter)}
+    for i in range(config.num_decoder_layers):
+        p = f"model.layers.{i}."
+        put(p + "input_layernorm.weight", torch.ones(h, dtype=torch.bfloat16))
+        put(p + "post_attention_layernorm.weight", torch.ones(h, dtype=torch.bfloat16))
+        for gname, (mod, sizes, k) in groups.items():
+            lora = gname in config.lora_target_modules
+            put(p + mod + (".base_layer.weight" if lora else ".weight"), rnd(sum(sizes), k))
+            if not lora:
+                continue
+            if len(sizes) > 1:
+                for s, n in enumerate(sizes):
+                    put(f"{p}{mod}.lora_A_slices.{s}", rnd(na, 1, r, k, s=0.02))
+                    put(f"{p}{mod}.lora_B_slices.{s}", rnd(na, 1, n, r, s=0.02))
+            else:
+                put(f"{p}{mod}.lora_A", rnd(na, 1, r, k, s=0.02))
+                put(f"{p}{mod}.lora_B", rnd(na, 1, sizes[0], r, s=0.02))
+    if na > 0:
+        put("model.switch.codebook", KerdockDGCodeGenerator(config.ms_code_m, config.ms_code_type)
+            .precompute_codebook(torch.float32))
+        put("model.switch.control_to_substitute_lut", build_control_to_substitute_lut(config))
+    if cur:
+        shards.append(cur)
+    weight_map = {}
+    for i, sh in enumerate(shards):
+        name = f"model-{i + 1:05d}-of-{len(shards):05d}.safetensors"
+        save_file(sh, os.path.join(out_dir, name), metadata={"format": "pt"})
+        for k in sh:
+            weight_map[k] = name
+    with open(os.path.join(out_dir, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {}, "weight_map": weight_map}, f)
+    config.save_pretrained(out_dir)

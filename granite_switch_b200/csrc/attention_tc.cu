@@ -1,0 +1,383 @@
+// Prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// One CTA owns 128 query rows of one request and one KV head (a row is a
+// (query token, query head of the GQA group) pair, as in attention.cu) and
+// walks the request's paged K/V in tiles of 128 keys:
+//
+//   S_j  = Q . K_j^T        tcgen05.mma M=128 N=128 K=D, S_j in TMEM (2 buffers)
+//   P_j  = softmax rows      softmax warps: tcgen05.ld one S row per thread,
+//                            mask, running max/sum in registers, P_j -> smem
+//   O   += P_j . V_j         tcgen05.mma M=128 N=D K=128, O in TMEM; V is read
+//                            straight from its [key][d] tile as an MN-major B
+//
+// Warp roles (192 threads): warp 0 issues the K/V page boxes by TMA
+// (double-buffered), warp 1 owns TMEM and issues every MMA from one thread,
+// warps 2..5 run the softmax, rescale O in TMEM when a row maximum grows, and
+// write the normalised output. S_{j+1} is issued before P_j . V_j so the tensor
+// core computes the next scores while the softmax of the current tile runs.
+// Every mbarrier wait is bounded; the error word reports a timeout.
+// (reference: attention comes from vLLM's backends, called at
+// src/granite_switch/vllm/decoder/lora/decoder.py:146-174.)
+#include "common.cuh"
+#include "tma_util.h"
+
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+namespace gsb {
+
+template <int D>
+struct FaCfg {
+  static constexpr int BM = 128;
+  static constexpr int KT = 128;
+  static constexpr int PAGE = 16;
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = KT * D * 2;      // one of K or V
+  static constexpr int STAGES = 2;
+  static constexpr int P_BYTES = BM * KT * 2;
+  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + P_BYTES + 512;
+  static constexpr int TMEM_COLS = 512;            // S0 | S1 | O
+  static constexpr int S_COL0 = 0, S_COL1 = 128, O_COL = 256;
+};
+
+// byte offset of 16-byte chunk `ch` of row `r` in a [D/64][rows][64] SW128 tile
+template <int ROWS>
+__device__ __forceinline__ uint32_t fa_sw(int r, int ch) {
+  return (uint32_t)((ch >> 3) * (ROWS * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+}
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                      const __nv_bfloat16* __restrict__ q, int64_t q_stride,
+                      const int32_t* __restrict__ block_table, int bt_stride,
+                      const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
+                      const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0, int Hq,
+                      int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out, int64_t out_stride,
+                      uint32_t* err) {
+  using C = FaCfg<D>;
+  constexpr int KT = C::KT, BM = C::BM, PAGE = C::PAGE;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + C::Q_BYTES;                       // [STAGES][K | V]
+  uint8_t* sP = sKV + C::STAGES * 2 * C::KV_BYTES;
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(sP + C::P_BYTES);  // [2]
+  uint64_t* kv_empty = kv_full + 2;                     // [2]
+  uint64_t* s_full = kv_empty + 2;                      // [2]
+  uint64_t* s_empty = s_full + 2;                       // [2]
+  uint64_t* p_full = s_empty + 2;                       // [1]
+  uint64_t* o_done = p_full + 1;                        // [1]
+  uint64_t* q_ready = o_done + 1;                       // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int w = blockIdx.x, kvh = blockIdx.y;
+  const int seq = work_seq[w];
+  const int row0 = work_row0[w];
+  const int G = Hq / Hkv;
+  const int qs = q_start[seq];
+  const int q_len = q_start[seq + 1] - qs;
+  const int kv_len = kv_len_arr[seq];
+  const int ctx = kv_len - q_len;
+  const int n_rows = q_len * G;
+  const int32_t* bt = block_table + (int64_t)seq * bt_stride;
+  const int last_row = min(row0 + BM, n_rows) - 1;
+  const int k_end = max(0, min(kv_len, ctx + last_row / G + 1));
+  const int n_tiles = (k_end + KT - 1) / KT;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    mbar_init(q_ready, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  // Q tile: every thread copies part of it (cp.async), then the proxy fence
+  // makes it visible to the tensor core.
+  for (int c = threadIdx.x; c < BM * (D / 8); c += blockDim.x) {
+    const int r = c / (D / 8), ch = c % (D / 8);
+    const int gr = row0 + r;
+    const bool valid = gr < n_rows;
+    const int tok = valid ? gr / G : 0;
+    const int head = kvh * G + (valid ? gr % G : 0);
+    const __nv_bfloat16* src = q + (int64_t)(qs + tok) * q_stride + head * D + ch * 8;
+    const uint32_t dst = smem_u32(sQ) + fa_sw<BM>(r, ch);
+    const int nbytes = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
+                 "l"(valid ? (const void*)src : (const void*)q), "r"(nbytes)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- K/V producer ----------------
+    if (lane == 0) {
+      const int first_page = bt[0];
+      int issued = 0;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int s = j & 1;
+        if (*abort_flag || !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, err, kErrAttnWait)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* dK = sKV + s * 2 * C::KV_BYTES;
+        uint8_t* dV = dK + C::KV_BYTES;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * C::KV_BYTES);
+#pragma unroll 1
+        for (int p = 0; p < KT / PAGE; ++p) {
+          const int key = j * KT + p * PAGE;
+          const int page = (key < k_end) ? bt[key / PAGE] : first_page;
+          const int row = (page * Hkv + kvh) * PAGE;
+#pragma unroll
+          for (int h = 0; h < D / 64; ++h) {
+            tma_load_2d(dK + h * (KT * 128) + p * PAGE * 128, &tm_k, &kv_full[s], h * 64, row);
+            tma_load_2d(dV + h * (KT * 128) + p * PAGE * 128, &tm_v, &kv_full[s], h * 64, row);
+          }
+        }
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
+          mbar_wait(&kv_full[j & 1], (j >> 1) & 1, err, kErrAttnWait);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t idesc_s = umma_idesc_bf16(128, KT);
+      const uint32_t idesc_o = umma_idesc_bf16_bmn(128, D);
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t p_addr = smem_u32(sP);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (*abort_flag || !mbar_wait(&kv_full[s], (j >> 1) & 1, err, kErrAttnWait)) return false;
+        if (!mbar_wait(&s_empty[s], ((j >> 1) & 1) ^ 1, err, kErrAttnWait)) return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sKV + s * 2 * C::KV_BYTES);
+        const uint32_t tS = tmem + (s ? C::S_COL1 : C::S_COL0);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * 0 + (kk & 3) * 32;
+          const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (BM * 128) + off);
+          const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * (KT * 128) + off);
+          umma_bf16(tS, ad, bd, idesc_s, kk != 0);
+        }
+        umma_commit(&s_full[s]);
+        return true;
+      };
+      bool ok = issue_s(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles) ok = issue_s(j + 1);
+        if (!ok) break;
+        // O += P_j . V_j once the softmax has written P_j (and rescaled O)
+        if (*abort_flag || !mbar_wait(p_full, j & 1, err, kErrAttnWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sKV + (j & 1) * 2 * C::KV_BYTES + C::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32);
+          // V tile as MN-major B: d groups of 64 are KT*128 bytes apart,
+          // 8-key groups 1024 bytes apart; 16 keys per step = 2048 bytes
+          const uint64_t bd = umma_desc_sw128_mn(v_addr + kk * 2048, KT * 128, 1024);
+          umma_bf16(tmem + C::O_COL, ad, bd, idesc_o, (j | kk) != 0);
+        }
+        umma_commit(o_done);
+        umma_commit(&kv_empty[j & 1]);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ---------------- softmax + epilogue (warps 2..5) ----------------
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;                 // row within the tile
+    const int gr = row0 + r;
+    const int pos = ctx + gr / G;                 // absolute position of this row's query
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j & 1;
+      if (*abort_flag || !mbar_wait(&s_full[s], (j >> 1) & 1, err, kErrAttnWait)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[KT];
+      {
+        const uint32_t tS = tmem + lane_base + (s ? C::S_COL1 : C::S_COL0);
+#pragma unroll
+        for (int c = 0; c < KT / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(tS + c * 32, rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(rr[i]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[s]);
+      // mask (causal + key range) and running max in the log2 domain
+      const int kbase = j * KT;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < KT; ++i) {
+        const int key = kbase + i;
+        float v = sv[i] * scale_log2;
+        if (key > pos || key >= k_end) v = -INFINITY;
+        sv[i] = v;
+        mt = fmaxf(mt, v);
+      }
+      const float m_new = fmaxf(m, mt);
+      // P_{j-1} . V_{j-1} must be complete before O is rescaled or P is overwritten
+      if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, err, kErrAttnWait)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (j > 0 && m_new > m && m != -INFINITY) {
+        const float f = exp2f(m - m_new);
+        l *= f;
+        const uint32_t tO = tmem + lane_base + C::O_COL;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(tO + c * 32, rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * f);
+          tmem_st32(tO + c * 32, rr);
+        }
+        tmem_wait_st();
+      }
+      m = m_new;
+      // P = 2^(s - m) as bf16 into the SW128 K-major P tile; l accumulates
+      float rs = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < KT / 8; ++ch) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a = (m == -INFINITY) ? 0.f : exp2f(sv[ch * 8 + 2 * e] - m);
+          const float b = (m == -INFINITY) ? 0.f : exp2f(sv[ch * 8 + 2 * e + 1] - m);
+          rs += a + b;
+          pk[e] = pack_bf16x2(a, b);
+        }
+        *reinterpret_cast<uint4*>(sP + fa_sw<BM>(r, ch)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      l += rs;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    // ---- epilogue: O / l -> out
+    if (ok && n_tiles > 0 && !*abort_flag) {
+      if (mbar_wait(o_done, (n_tiles - 1) & 1, err, kErrAttnWait)) {
+        tc_fence_after();
+        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+        const bool valid = gr < n_rows;
+        const int tok = qs + (valid ? gr / G : 0);
+        const int head = kvh * G + (valid ? gr % G : 0);
+        __nv_bfloat16* op = out + (int64_t)tok * out_stride + head * D;
+        const uint32_t tO = tmem + lane_base + C::O_COL;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(tO + c * 32, rr);
+          tmem_wait_ld();
+          if (valid) {
+            uint4* o4 = reinterpret_cast<uint4*>(op + c * 32);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              o4[e] = make_uint4(pack_bf16x2(__uint_as_float(rr[8 * e]) * inv, __uint_as_float(rr[8 * e + 1]) * inv),
+                                 pack_bf16x2(__uint_as_float(rr[8 * e + 2]) * inv, __uint_as_float(rr[8 * e + 3]) * inv),
+                                 pack_bf16x2(__uint_as_float(rr[8 * e + 4]) * inv, __uint_as_float(rr[8 * e + 5]) * inv),
+                                 pack_bf16x2(__uint_as_float(rr[8 * e + 6]) * inv, __uint_as_float(rr[8 * e + 7]) * inv));
+          }
+        }
+      } else {
+        *abort_flag = 1;
+      }
+    } else if (n_tiles == 0 && gr < n_rows) {
+      __nv_bfloat16* op = out + (int64_t)(qs + gr / G) * out_stride + (kvh * G + gr % G) * D;
+      for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(op + c) = make_uint4(0, 0, 0, 0);
+    }
+    if (!ok) *abort_flag = 1;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace gsb
+
+using namespace gsb;
+
+// Same metadata contract as gsb_paged_attention (rows_per_tile = 128), no key split.
+void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                              const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
+                              const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t num_q_heads,
+                              double scale, const at::Tensor& out, const at::Tensor& err) {
+  GSB_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16 &&
+                out.scalar_type() == at::kBFloat16,
+            "attention_tc: bf16 tensors required");
+  GSB_CHECK(k_cache.dim() == 4 && k_cache.size(2) == 16 && k_cache.is_contiguous() && v_cache.is_contiguous(),
+            "attention_tc: caches must be contiguous [num_blocks, Hkv, 16, D]");
+  const int Hkv = (int)k_cache.size(1), D = (int)k_cache.size(3), Hq = (int)num_q_heads;
+  GSB_CHECK(D == 128, "attention_tc: head_dim 128 only (64 uses the mma.sync kernel)");
+  GSB_CHECK(Hq % Hkv == 0, "attention_tc: Hq must be a multiple of Hkv");
+  GSB_CHECK(q.stride(1) == 1 && (q.stride(0) % 8) == 0 && out.stride(1) == 1 && (out.stride(0) % 8) == 0,
+            "attention_tc: q/out rows must be 16-byte aligned");
+  const int n_work = (int)work_seq.numel();
+  if (n_work == 0) return;
+  const int64_t page_rows = k_cache.size(0) * (int64_t)Hkv * 16;
+  GSB_CHECK(page_rows < (int64_t(1) << 31), "attention_tc: cache too large for 32-bit TMA coordinates");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto st = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
+  CUtensorMap tk = make_tmap_bf16_2d(k_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+  using C = FaCfg<128>;
+  auto kfn = fa_prefill_kernel<128>;
+  static bool configured = false;
+  if (!configured) {
+    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured = true;
+  }
+  dim3 grid(n_work, Hkv);
+  kfn<<<grid, 192, C::SMEM, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
+                                  block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
+                                  q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
+                                  work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv,
+                                  (float)(scale * 1.4426950408889634),
+                                  reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
+                                  reinterpret_cast<uint32_t*>(err.data_ptr()));
+  GSB_CUDA_CHECK(cudaGetLastError());
+}

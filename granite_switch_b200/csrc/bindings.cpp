@@ -15,5 +15,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &gsb_argmax, "greedy argmax over fp32 logits");
   m.def("routing", &gsb_routing, "latest-wins routing, token exchange and LoRA tile metadata");
   m.def("sample", &gsb_sample, "temperature / top-k / top-p sampling (Gumbel-max, Philox)");
+  m.def("prefill_attention_tc", &gsb_prefill_attention_tc, "tcgen05/TMEM prefill attention (128-row tiles)");
   m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode)");
 }

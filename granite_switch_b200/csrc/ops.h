@@ -39,3 +39,7 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
                          const at::Tensor& err);
 void gsb_sample(const at::Tensor& logits, const at::Tensor& temperature, const at::Tensor& top_k,
                 const at::Tensor& top_p, const at::Tensor& seeds, const at::Tensor& offsets, const at::Tensor& out);
+void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                              const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
+                              const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t num_q_heads,
+                              double scale, const at::Tensor& out, const at::Tensor& err);

@@ -39,6 +39,14 @@ def paged_attention(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq,
     return out
 
 
+def prefill_attention_tc(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
+                         num_q_heads: int, scale: float, out):
+    """tcgen05 prefill attention; work tiles must be built with ``rows_per_tile=128``."""
+    native().prefill_attention_tc(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
+                                  num_q_heads, float(scale), out, err_buffer(q.device))
+    return out
+
+
 def paged_attention_reference(q, k_cache, v_cache, block_table, q_lens, kv_lens, num_q_heads, scale):
     """fp32 oracle. q ``[T, Hq*D]`` (flat, requests back to back); returns ``[T, Hq*D]`` fp32."""
     _, hkv, page, d = k_cache.shape

@@ -1,0 +1,164 @@
+"""OpenAI-compatible HTTP server over the serving engine.
+
+Endpoints: ``POST /v1/completions`` (text or token-id prompts; token ids are
+the form the multi-adapter prefix cache needs), ``POST /v1/chat/completions``
+(rendered with the checkpoint's chat template; ``chat_template_kwargs`` such as
+``adapter_name`` and ``documents`` select the adapter and its inputs),
+``GET /v1/models``, ``GET /health`` and ``GET /metrics`` (Prometheus text with
+the vLLM metric names: ``vllm:prefix_cache_queries_total``,
+``vllm:prefix_cache_hits_total``, ``vllm:time_to_first_token_seconds``,
+``vllm:e2e_request_latency_seconds``, ``vllm:num_requests_running/waiting``).
+
+Run: ``python -m granite_switch_b200.server --model <composed dir> --port 8000``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import time
+import uuid
+
+from ..engine.request import SamplingParams
+from .async_engine import AsyncEngine
+
+
+def _sampling(body: dict, default_max: int = 16) -> SamplingParams:
+    stop_ids = tuple(body.get("stop_token_ids") or ())
+    return SamplingParams(max_tokens=int(body.get("max_tokens") or default_max),
+                          temperature=float(body.get("temperature", 0.0) or 0.0),
+                          top_k=int(body.get("top_k", 0) or 0), top_p=float(body.get("top_p", 1.0) or 1.0),
+                          seed=body.get("seed"), stop_token_ids=stop_ids,
+                          ignore_eos=bool(body.get("ignore_eos", False)),
+                          min_tokens=int(body.get("min_tokens", 0) or 0))
+
+
+def build_app(async_engine: AsyncEngine, tokenizer=None, model_name: str = "granite-switch"):
+    from fastapi import FastAPI, HTTPException
+    from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+    app = FastAPI(title="granite_switch_b200")
+
+    def encode_prompt(prompt):
+        if isinstance(prompt, list) and all(isinstance(t, int) for t in prompt):
+            return [list(prompt)]
+        if isinstance(prompt, list) and prompt and isinstance(prompt[0], list):
+            return [list(p) for p in prompt]
+        if tokenizer is None:
+            raise HTTPException(400, "this server has no tokenizer: send the prompt as token ids")
+        texts = prompt if isinstance(prompt, list) else [prompt]
+        return [tokenizer(t, add_special_tokens=False)["input_ids"] for t in texts]
+
+    def decode(ids):
+        if tokenizer is None:
+            return ""
+        return tokenizer.decode(ids, skip_special_tokens=True)
+
+    def usage(reqs):
+        p = sum(len(r.prompt_ids) for r in reqs)
+        c = sum(len(r.output_ids) for r in reqs)
+        cached = sum(r.num_cached_tokens for r in reqs)
+        return {"prompt_tokens": p, "completion_tokens": c, "total_tokens": p + c,
+                "prompt_tokens_details": {"cached_tokens": cached}}
+
+    @app.get("/health")
+    async def health():
+        return {"status": "ok"}
+
+    @app.get("/v1/models")
+    async def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "granite_switch_b200"}]}
+
+    @app.get("/metrics")
+    async def metrics():
+        return PlainTextResponse(async_engine.metrics_text())
+
+    @app.post("/v1/completions")
+    async def completions(body: dict):
+        prompts = encode_prompt(body.get("prompt"))
+        sp = _sampling(body)
+        rid = f"cmpl-{uuid.uuid4().hex[:24]}"
+        created = int(time.time())
+        if body.get("stream"):
+            if len(prompts) != 1:
+                raise HTTPException(400, "streaming supports one prompt")
+
+            async def gen():
+                async for item in async_engine.stream(prompts[0], sp):
+                    if isinstance(item, list):
+                        chunk = {"id": rid, "object": "text_completion", "created": created, "model": model_name,
+                                 "choices": [{"index": 0, "text": decode(item), "token_ids": item,
+                                              "finish_reason": None}]}
+                    else:
+                        chunk = {"id": rid, "object": "text_completion", "created": created, "model": model_name,
+                                 "choices": [{"index": 0, "text": "", "token_ids": [],
+                                              "finish_reason": item.finish_reason}], "usage": usage([item])}
+                    yield f"data: {json.dumps(chunk)}\n\n"
+                yield "data: [DONE]\n\n"
+
+            return StreamingResponse(gen(), media_type="text/event-stream")
+        try:
+            reqs = [await async_engine.generate(p, sp) for p in prompts]
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
+        choices = [{"index": i, "text": decode(r.output_ids), "token_ids": r.output_ids,
+                    "finish_reason": r.finish_reason, "logprobs": None} for i, r in enumerate(reqs)]
+        return JSONResponse({"id": rid, "object": "text_completion", "created": created, "model": model_name,
+                             "choices": choices, "usage": usage(reqs)})
+
+    @app.post("/v1/chat/completions")
+    async def chat(body: dict):
+        if tokenizer is None:
+            raise HTTPException(400, "chat completions need the checkpoint's tokenizer")
+        kwargs = dict(body.get("chat_template_kwargs") or {})
+        text = tokenizer.apply_chat_template(body["messages"], add_generation_prompt=True, tokenize=False, **kwargs)
+        ids = tokenizer(text, add_special_tokens=False)["input_ids"]
+        sp = _sampling(body)
+        try:
+            r = await async_engine.generate(ids, sp)
+        except ValueError as e:
+            raise HTTPException(400, str(e)) from e
+        return JSONResponse({
+            "id": f"chatcmpl-{uuid.uuid4().hex[:24]}", "object": "chat.completion", "created": int(time.time()),
+            "model": model_name,
+            "choices": [{"index": 0, "message": {"role": "assistant", "content": decode(r.output_ids)},
+                         "finish_reason": r.finish_reason}],
+            "usage": usage([r])})
+
+    return app
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description="granite_switch_b200 OpenAI-compatible server")
+    ap.add_argument("--model", required=True, help="composed Granite Switch checkpoint directory")
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--served-model-name", default=None)
+    ap.add_argument("--max-num-seqs", type=int, default=256)
+    ap.add_argument("--max-num-batched-tokens", type=int, default=8192)
+    ap.add_argument("--max-model-len", type=int, default=8192)
+    ap.add_argument("--gpu-memory-utilization", type=float, default=0.88)
+    ap.add_argument("--no-prefix-caching", action="store_true")
+    ap.add_argument("--device", default=None)
+    args = ap.parse_args(argv)
+    import uvicorn
+
+    from ..engine import LLM, EngineConfig
+
+    ecfg = EngineConfig(max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
+                        max_model_len=args.max_model_len, gpu_memory_utilization=args.gpu_memory_utilization,
+                        enable_prefix_caching=not args.no_prefix_caching)
+    llm = LLM(args.model, device=args.device, engine_config=ecfg)
+    tok = None
+    try:
+        from transformers import AutoTokenizer
+
+        tok = AutoTokenizer.from_pretrained(args.model)
+    except Exception:
+        tok = None
+    name = args.served_model_name or args.model.rstrip("/").split("/")[-1]
+    ae = AsyncEngine(llm.engine, name)
+    uvicorn.run(build_app(ae, tok, name), host=args.host, port=args.port, log_level="warning")
+
+
+if __name__ == "__main__":
+    main()

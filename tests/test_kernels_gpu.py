@@ -180,3 +180,34 @@ def test_paged_attention(d, mode, nsplit):
     err = (out.float() - ref).abs().max().item()
     assert err < 3e-2, err
     _check()
+
+
+@pytest.mark.parametrize("case", ["fresh", "cached_prefix", "mixed"])
+def test_prefill_attention_tcgen05(case):
+    from granite_switch_b200.ops import attention as A
+
+    hq, hkv, d = 8, 2, 128
+    g = hq // hkv
+    if case == "fresh":
+        q_lens, kv_lens = [130, 64, 5], [130, 64, 5]
+    elif case == "cached_prefix":
+        q_lens, kv_lens = [40, 100], [300, 1100]
+    else:
+        q_lens, kv_lens = [1, 257, 33], [77, 257, 700]
+    kc, vc, bt = _make_cache(kv_lens, hkv, d, seed=3)
+    T = sum(q_lens)
+    q = torch.randn(T, (hq + 2 * hkv) * d, device="cuda").bfloat16()
+    out = torch.zeros(T, hq * d, device="cuda").bfloat16()
+    qs = [0]
+    for l in q_lens:
+        qs.append(qs[-1] + l)
+    ws, wr = A.build_work(q_lens, g, 128)
+    dev = "cuda"
+    A.prefill_attention_tc(q, kc, vc, bt, torch.tensor(qs, dtype=torch.int32, device=dev),
+                           torch.tensor(kv_lens, dtype=torch.int32, device=dev),
+                           torch.tensor(ws, dtype=torch.int32, device=dev),
+                           torch.tensor(wr, dtype=torch.int32, device=dev), hq, 0.088, out)
+    ref = A.paged_attention_reference(q, kc, vc, bt, q_lens, kv_lens, hq, 0.088)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 3e-2, err
+    _check()
