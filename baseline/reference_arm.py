@@ -131,7 +131,8 @@ def _run(args, emit, metric, world):
     while ramp < args.ramp_steps:
         step()
         ramp += 1
-        if len(live) >= target and stats["gen"] > 0:
+        decoding = sum(1 for rid in live if rid in first_tok)
+        if decoding >= target:
             break
     for _ in range(args.warmup):
         step()
@@ -145,13 +146,21 @@ def _run(args, emit, metric, world):
     gen = tok_after - tok_before
     win = [t for (ts, t) in ttfts if w0 <= ts <= w1]
     dp, dc = stats["prompt"] - p0, stats["cached"] - c0
+    hit = None
+    try:  # vLLM's own prefix-cache counters, when this version exposes them
+        for mt in llm.get_metrics():
+            if mt.name in ("vllm:prefix_cache_hits", "vllm:prefix_cache_queries"):
+                hit = hit or {}
+                hit[mt.name] = getattr(mt, "value", None)
+    except Exception:
+        pass
     emit({"metric": metric, "value": round(gen / (w1 - w0), 2), "unit": "output tok/s", "n_gpus": world,
           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round((w1 - w0) * 1e3 / args.steps, 3),
           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
           "data": "synthetic (random prompts, random-init base and adapter weights)", "impl": "reference",
           "timing": "host clock (vLLM runs the model in its own engine process)",
           "p50_ttft_s": round(statistics.median(win), 4) if win else None, "ttft_samples": len(win),
-          "prefix_hit_rate": round(dc / dp, 4) if dp else None,
+          "prefix_hit_rate": round(dc / dp, 4) if dp else None, "vllm_prefix_cache_counters": hit,
           "config": {"model": f"{args.preset}-shape", "global_batch": args.max_num_seqs, "seq_len": args.context_len,
                      "parallelism": f"tp{world}", "adapters": "12 aLoRA r32 q/k/v/o",
                      "workload": f"poisson {args.rate}/s, {args.calls} chained calls, inv 16-64, gen 32-128",

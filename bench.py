@@ -171,7 +171,8 @@ def run_native(args):
     while ramp < args.ramp_steps:
         step()
         ramp += 1
-        if len(eng.scheduler.running) >= target and eng.stats.finished >= 1:
+        decoding = sum(1 for r in eng.scheduler.running if r.first_token_time is not None)
+        if decoding >= target:
             break
     # ---- warm-up
     for _ in range(args.warmup):

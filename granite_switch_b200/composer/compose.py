@@ -74,7 +74,8 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
                        reserved_output_row: int | None = None, default_substitute: int | None = None,
                        base_model_name: str = "synthetic", ms_code_m: int = 6, ms_memory_gain: float = 28.0,
                        switch_head_dim: int = 32, extra_config: dict | None = None,
-                       max_shard_bytes: int = 5 * 1024 ** 3) -> GraniteSwitchConfig:
+                       max_shard_bytes: int = 5 * 1024 ** 3,
+                       control_token_ids: list[int] | None = None) -> GraniteSwitchConfig:
     na = len(adapters)
     cfg = dict(base_config)
     base_vocab = int(cfg["vocab_size"])
@@ -96,7 +97,12 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
 
     # ---- control tokens and substitutes
     n_ctrl = na + (1 if base_reset else 0)
-    ctrl_ids = list(range(base_vocab, base_vocab + n_ctrl))
+    if control_token_ids is not None:
+        if len(control_token_ids) != n_ctrl:
+            raise ValueError(f"{len(control_token_ids)} control token ids for {n_ctrl} control tokens")
+        ctrl_ids = [int(t) for t in control_token_ids]
+    else:
+        ctrl_ids = list(range(base_vocab, base_vocab + n_ctrl))
     subs = []
     if base_reset:
         subs.append(default_substitute if default_substitute is not None else 0)
@@ -107,7 +113,7 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
             subs.append(int(a.invocation_tokens[0]))
         else:
             subs.append(default_substitute if default_substitute is not None else 0)
-    new_vocab = base_vocab + n_ctrl
+    new_vocab = max(base_vocab, max(ctrl_ids) + 1) if ctrl_ids else base_vocab
     ranks = [a.max_rank() if a.kind == "lora" else 1 for a in adapters]
     max_rank = max(ranks) if ranks else 8
     kinds = [a.kind for a in adapters]
@@ -160,14 +166,19 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
         for i in range(n_layers):
             sd[f"model.layers.{i}.cross_stream.base_layer.weight"] = torch.zeros(h, h)
 
-    # grow embeddings; control-token output rows come from a reserved row
-    emb = sd["model.embed_tokens.weight"]
+    # grow embeddings to cover the control ids; every control-token output row is
+    # a copy of a reserved (never emitted) row, so the model does not emit them
     reserved = reserved_output_row if reserved_output_row is not None else base_vocab - 1
-    grow = emb[reserved:reserved + 1].expand(n_ctrl, -1).clone()
-    sd["model.embed_tokens.weight"] = torch.cat([emb, grow], 0)
-    if "lm_head.weight" in sd:
-        lm = sd["lm_head.weight"]
-        sd["lm_head.weight"] = torch.cat([lm, lm[reserved:reserved + 1].expand(n_ctrl, -1).clone()], 0)
+    for key in ("model.embed_tokens.weight", "lm_head.weight"):
+        if key not in sd:
+            continue
+        t = sd[key]
+        if new_vocab > t.shape[0]:
+            t = torch.cat([t, t[reserved:reserved + 1].expand(new_vocab - t.shape[0], -1).clone()], 0)
+        else:
+            t = t.clone()
+        t[torch.tensor(ctrl_ids, dtype=torch.long)] = t[reserved].clone()
+        sd[key] = t
 
     if any(k == "probe" for k in kinds):
         lmax = config.max_probe_labels

@@ -33,8 +33,12 @@ GROUP_SLICES = {"qkv_proj": 3, "o_proj": 1, "shared_input_linear": 2, "shared_ou
 
 _PEFT_RE = re.compile(
     r"(?:base_model\.model\.)?model\.layers\.(\d+)\.(?:self_attn|mlp|shared_mlp)?\.?"
-    r"(q_proj|k_proj|v_proj|o_proj|gate_proj|up_proj|down_proj|cross_stream)\.lora_([AB])(?:\.default)?\.weight$"
+    r"(q_proj|k_proj|v_proj|o_proj|gate_proj|up_proj|down_proj|input_linear|output_linear|cross_stream)"
+    r"\.lora_([AB])(?:\.default)?\.weight$"
 )
+# PEFT modules of a fused MoE-hybrid shared MLP: input_linear (gate|up) is split into
+# two slices (A duplicated, B chunked on its output dim), output_linear is down.
+FUSED_SPLIT = {"input_linear": ("shared_input_linear", 2), "output_linear": ("shared_output_linear", 1)}
 
 
 def parse_peft_name(name: str):
@@ -46,6 +50,10 @@ def parse_peft_name(name: str):
 
 
 def module_group(module: str) -> tuple[str, int | None]:
+    if module == "input_linear":
+        return "shared_input_linear", -1  # both slices
+    if module == "output_linear":
+        return "shared_output_linear", None
     if module in ATTN_SLICES:
         return ATTN_SLICES[module]
     if module in MLP_SLICES:
@@ -149,6 +157,11 @@ def stack_adapters(adapters: list[dict], num_layers: int, slice_sizes: dict[str,
             if s is None:
                 out[pre + ".lora_A"][a, 0, :r] = A
                 out[pre + ".lora_B"][a, 0, :, :r] = B * scale
+            elif s == -1:  # fused gate|up: duplicate A, chunk B
+                half = B.shape[0] // 2
+                for si in range(2):
+                    out[pre + f".lora_A_slices.{si}"][a, 0, :r] = A
+                    out[pre + f".lora_B_slices.{si}"][a, 0, :, :r] = B[si * half:(si + 1) * half] * scale
             else:
                 out[pre + f".lora_A_slices.{s}"][a, 0, :r] = A
                 out[pre + f".lora_B_slices.{s}"][a, 0, :, :r] = B * scale

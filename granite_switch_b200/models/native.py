@@ -18,6 +18,7 @@ communicator is attached, that reduction runs in the fused kernels of
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -89,6 +90,8 @@ class NativeGraniteSwitch:
         self.layers: list[LayerWeights] = []
         self.remaps: torch.Tensor | None = None
         self.comm = None  # optional fused-collective communicator
+        # prefill attention on tcgen05 (head_dim 128); GSB_ATTN_TC=0 selects the mma.sync kernel
+        self.use_tc_attention = os.environ.get("GSB_ATTN_TC", "1") != "0"
         self.err = err_buffer(device)
         na = config.num_adapters
         self.num_adapters = na
@@ -331,9 +334,13 @@ class NativeGraniteSwitch:
             kc, vc = self.kv_cache[li, 0], self.kv_cache[li, 1]
             E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
             for plan in b.plans:
-                A.paged_attention(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
-                                  plan.work_row0, plan.rows, self.num_q, scale, attn, plan.nsplit,
-                                  self.ws_o, self.ws_lse)
+                if plan.rows == 128:
+                    A.prefill_attention_tc(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
+                                           plan.work_row0, self.num_q, scale, attn)
+                else:
+                    A.paged_attention(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
+                                      plan.work_row0, plan.rows, self.num_q, scale, attn, plan.nsplit,
+                                      self.ws_o, self.ws_lse)
             self._row_parallel(lw.o, attn, h, mult)
             E.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps, out=x)
             self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
@@ -353,7 +360,8 @@ class NativeGraniteSwitch:
         dec = [i for i, ql in enumerate(q_lens) if ql * g <= 16]
         pre = [i for i, ql in enumerate(q_lens) if ql * g > 16]
         plans = []
-        for idx, rows in ((dec, 16), (pre, 64)):
+        pre_rows = 128 if (self.head_dim == 128 and self.use_tc_attention) else 64
+        for idx, rows in ((dec, 16), (pre, pre_rows)):
             if not idx:
                 continue
             ws, wr = [], []
