@@ -27,18 +27,22 @@
 
 namespace gsb {
 
-template <int D>
+template <int D, int KT_ = 64>
 struct FaCfg {
   static constexpr int BM = 128;
-  static constexpr int KT = 128;
+  static constexpr int KT = KT_;
   static constexpr int PAGE = 16;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = KT * D * 2;      // one of K or V
   static constexpr int STAGES = 2;
+  // P_j is written over K_j (same size when BM == D): S_j has consumed K_j
+  // by the time the softmax writes P_j, and the stage is refilled only after
+  // P_j . V_j completes.
   static constexpr int P_BYTES = BM * KT * 2;
-  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + P_BYTES + 512;
-  static constexpr int TMEM_COLS = 512;            // S0 | S1 | O
-  static constexpr int S_COL0 = 0, S_COL1 = 128, O_COL = 256;
+  static_assert(P_BYTES <= KV_BYTES, "P must fit in the K tile it replaces");
+  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + 512;
+  static constexpr int TMEM_COLS = (2 * KT + D) <= 256 ? 256 : 512;  // S0 | S1 | O
+  static constexpr int S_COL0 = 0, S_COL1 = KT, O_COL = 2 * KT;
 };
 
 // byte offset of 16-byte chunk `ch` of row `r` in a [D/64][rows][64] SW128 tile
@@ -47,23 +51,31 @@ __device__ __forceinline__ uint32_t fa_sw(int r, int ch) {
   return (uint32_t)((ch >> 3) * (ROWS * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
-template <int D>
-__global__ void __launch_bounds__(192, 1)
+template <int D, int KT_>
+__global__ void __launch_bounds__(192, 2)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __nv_bfloat16* __restrict__ q, int64_t q_stride,
                       const int32_t* __restrict__ block_table, int bt_stride,
                       const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
                       const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0, int Hq,
                       int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out, int64_t out_stride,
-                      uint32_t* err) {
-  using C = FaCfg<D>;
+                      uint32_t* err, volatile int* dbg) {
+  using C = FaCfg<D, KT_>;
   constexpr int KT = C::KT, BM = C::BM, PAGE = C::PAGE;
+  const bool report = (dbg != nullptr);
+  volatile int* my_dbg = report ? dbg + (blockIdx.y * gridDim.x + blockIdx.x) * 16 : nullptr;
+#define FA_PROGRESS(slot, code)            \
+  do {                                     \
+    if (report) {                          \
+      my_dbg[(slot)] = (code);             \
+      __threadfence_system();              \
+    }                                      \
+  } while (0)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + C::Q_BYTES;                       // [STAGES][K | V]
-  uint8_t* sP = sKV + C::STAGES * 2 * C::KV_BYTES;
-  uint64_t* kv_full = reinterpret_cast<uint64_t*>(sP + C::P_BYTES);  // [2]
+  uint64_t* kv_full = reinterpret_cast<uint64_t*>(sKV + C::STAGES * 2 * C::KV_BYTES);  // [2]
   uint64_t* kv_empty = kv_full + 2;                     // [2]
   uint64_t* s_full = kv_empty + 2;                      // [2]
   uint64_t* s_empty = s_full + 2;                       // [2]
@@ -104,8 +116,10 @@ __global__ void __launch_bounds__(192, 1)
     tma_prefetch_desc(&tm_v);
   }
   if (warp == 1) {
+    if (lane == 0) FA_PROGRESS(0, 1);
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
+    if (lane == 0) FA_PROGRESS(0, 2);
   }
   // Q tile: every thread copies part of it (cp.async), then the proxy fence
   // makes it visible to the tensor core.
@@ -128,6 +142,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) FA_PROGRESS(0, 3);
 
   if (warp == 0) {
     // ---------------- K/V producer ----------------
@@ -155,6 +170,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
         issued = j + 1;
+        FA_PROGRESS(1, issued);
       }
       if (*abort_flag) {
         for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
@@ -167,7 +183,6 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t idesc_s = umma_idesc_bf16(128, KT);
       const uint32_t idesc_o = umma_idesc_bf16_bmn(128, D);
       const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
         if (*abort_flag || !mbar_wait(&kv_full[s], (j >> 1) & 1, err, kErrAttnWait)) return false;
@@ -183,6 +198,7 @@ __global__ void __launch_bounds__(192, 1)
           umma_bf16(tS, ad, bd, idesc_s, kk != 0);
         }
         umma_commit(&s_full[s]);
+        FA_PROGRESS(2, 100 + j);
         return true;
       };
       bool ok = issue_s(0);
@@ -195,10 +211,11 @@ __global__ void __launch_bounds__(192, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sKV + (j & 1) * 2 * C::KV_BYTES + C::KV_BYTES);
+        const uint32_t p_addr = smem_u32(sKV + (j & 1) * 2 * C::KV_BYTES);  // P_j over K_j
+        const uint32_t v_addr = p_addr + C::KV_BYTES;
 #pragma unroll
         for (int kk = 0; kk < KT / 16; ++kk) {
-          const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32);
+          const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32);  // P: [KT/64][BM][64]
           // V tile as MN-major B: d groups of 64 are KT*128 bytes apart,
           // 8-key groups 1024 bytes apart; 16 keys per step = 2048 bytes
           const uint64_t bd = umma_desc_sw128_mn(v_addr + kk * 2048, KT * 128, 1024);
@@ -206,6 +223,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         umma_commit(o_done);
         umma_commit(&kv_empty[j & 1]);
+        FA_PROGRESS(3, 200 + j);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -220,7 +238,8 @@ __global__ void __launch_bounds__(192, 1)
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j & 1;
-      if (*abort_flag || !mbar_wait(&s_full[s], (j >> 1) & 1, err, kErrAttnWait)) {
+      const bool got_s = !*abort_flag && mbar_wait(&s_full[s], (j >> 1) & 1, err, kErrAttnWait);
+      if (!__all_sync(0xffffffffu, got_s)) {  // warp-uniform: the tcgen05.ld below is warp-collective
         ok = false;
         break;
       }
@@ -240,6 +259,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[s]);
+      if (lane == 0) FA_PROGRESS(4 + qd, 300 + j);
       // mask (causal + key range) and running max in the log2 domain
       const int kbase = j * KT;
       float mt = -INFINITY;
@@ -253,13 +273,17 @@ __global__ void __launch_bounds__(192, 1)
       }
       const float m_new = fmaxf(m, mt);
       // P_{j-1} . V_{j-1} must be complete before O is rescaled or P is overwritten
-      if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, err, kErrAttnWait)) {
+      const bool got_o = (j == 0) || mbar_wait(o_done, (j - 1) & 1, err, kErrAttnWait);
+      if (!__all_sync(0xffffffffu, got_o)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (j > 0 && m_new > m && m != -INFINITY) {
-        const float f = exp2f(m - m_new);
+      // tcgen05.ld/st are warp-collective: the whole warp rescales when any of
+      // its rows needs it (factor 1 for the others)
+      const bool grow = (j > 0 && m_new > m && m != -INFINITY);
+      if (__any_sync(0xffffffffu, grow)) {
+        const float f = grow ? exp2f(m - m_new) : 1.f;
         l *= f;
         const uint32_t tO = tmem + lane_base + C::O_COL;
 #pragma unroll
@@ -286,17 +310,20 @@ __global__ void __launch_bounds__(192, 1)
           rs += a + b;
           pk[e] = pack_bf16x2(a, b);
         }
-        *reinterpret_cast<uint4*>(sP + fa_sw<BM>(r, ch)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        *reinterpret_cast<uint4*>(sKV + s * 2 * C::KV_BYTES + fa_sw<BM>(r, ch)) =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
       l += rs;
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) FA_PROGRESS(4 + qd, 400 + j);
     }
     // ---- epilogue: O / l -> out
-    if (ok && n_tiles > 0 && !*abort_flag) {
-      if (mbar_wait(o_done, (n_tiles - 1) & 1, err, kErrAttnWait)) {
+    const bool go = ok && n_tiles > 0 && !*abort_flag;
+    if (__all_sync(0xffffffffu, go)) {
+      if (__all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, err, kErrAttnWait))) {
         tc_fence_after();
         const float inv = (l > 0.f) ? 1.f / l : 0.f;
         const bool valid = gr < n_rows;
@@ -329,12 +356,15 @@ __global__ void __launch_bounds__(192, 1)
     if (!ok) *abort_flag = 1;
   }
 
+  if (lane == 0) FA_PROGRESS(8 + warp, 500);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+    if (lane == 0) FA_PROGRESS(0, 4);
   }
+#undef FA_PROGRESS
 }
 
 }  // namespace gsb
@@ -345,7 +375,10 @@ using namespace gsb;
 void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                               const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
                               const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t num_q_heads,
-                              double scale, const at::Tensor& out, const at::Tensor& err) {
+                              double scale, const at::Tensor& out, const at::Tensor& err, int64_t dbg_ptr) {
+  // dbg_ptr: optional device-visible address of mapped host memory (>= 16 ints)
+  // where CTA (0, 0) records its progress; 0 disables reporting.
+  volatile int* dbg = reinterpret_cast<volatile int*>(dbg_ptr);
   GSB_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16 &&
                 out.scalar_type() == at::kBFloat16,
             "attention_tc: bf16 tensors required");
@@ -364,8 +397,8 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
   auto st = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
   CUtensorMap tk = make_tmap_bf16_2d(k_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
-  using C = FaCfg<128>;
-  auto kfn = fa_prefill_kernel<128>;
+  using C = FaCfg<128, 64>;
+  auto kfn = fa_prefill_kernel<128, 64>;
   static bool configured = false;
   if (!configured) {
     GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
@@ -378,6 +411,6 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
                                   work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv,
                                   (float)(scale * 1.4426950408889634),
                                   reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
-                                  reinterpret_cast<uint32_t*>(err.data_ptr()));
+                                  reinterpret_cast<uint32_t*>(err.data_ptr()), dbg);
   GSB_CUDA_CHECK(cudaGetLastError());
 }

@@ -42,4 +42,4 @@ void gsb_sample(const at::Tensor& logits, const at::Tensor& temperature, const a
 void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                               const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
                               const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t num_q_heads,
-                              double scale, const at::Tensor& out, const at::Tensor& err);
+                              double scale, const at::Tensor& out, const at::Tensor& err, int64_t dbg_ptr);
