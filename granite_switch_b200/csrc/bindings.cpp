@@ -16,5 +16,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("routing", &gsb_routing, "latest-wins routing, token exchange and LoRA tile metadata");
   m.def("sample", &gsb_sample, "temperature / top-k / top-p sampling (Gumbel-max, Philox)");
   m.def("prefill_attention_tc", &gsb_prefill_attention_tc, "tcgen05/TMEM prefill attention (128-row tiles)");
+  m.def("peer_barrier", &gsb_peer_barrier, "bounded cross-rank barrier over P2P signal pads");
+  m.def("multimem_allreduce_bf16", &gsb_multimem_allreduce_bf16, "NVLS one-shot all-reduce (multimem)");
+  m.def("rmsnorm_residual_from", &gsb_rmsnorm_residual_from, "h <- y; x <- rmsnorm(y); y <- 0");
   m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode)");
 }

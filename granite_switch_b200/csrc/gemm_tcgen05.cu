@@ -36,7 +36,18 @@ enum EpiKind : int {
   kEpiSwiGLU = 2,    // out(bf16)[:, n/2] = silu(gate) * up, gate/up interleaved per tile
   kEpiMaskAdapter = 3,  // shrink: keep column j only where row's adapter == (j/r)%NA+1
   kEpiF32 = 4,       // out(fp32) = acc * scale
+  // out = multicast address of a symmetric bf16 buffer: every rank adds
+  // (residual +) acc * scale into all ranks' copies through NVSwitch
+  // (multimem.red), tile by tile as accumulators drain
+  kEpiMultimemRed = 5,
 };
+
+__device__ __forceinline__ void multimem_red_add_v4_bf16x2(void* mc, uint32_t a, uint32_t b, uint32_t c,
+                                                           uint32_t d) {
+  asm volatile("multimem.red.relaxed.sys.global.add.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(mc), "r"(a), "r"(b),
+               "r"(c), "r"(d)
+               : "memory");
+}
 
 struct GemmLoraArgs {
   int enabled;            // 0: plain GEMM
@@ -329,7 +340,7 @@ __global__ void __launch_bounds__(192, 1)
                                   __uint_as_float(r[4 * j + 2]) * epi.scale, __uint_as_float(r[4 * j + 3]) * epi.scale);
           } else {
             float v[32];
-            if (EPI == kEpiResAdd) {
+            if (EPI == kEpiResAdd || (EPI == kEpiMultimemRed && epi.residual != nullptr)) {
               const uint4* r4 = reinterpret_cast<const uint4*>(epi.residual + (int64_t)row * epi.ldr + col);
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
@@ -346,6 +357,9 @@ __global__ void __launch_bounds__(192, 1)
                   v[8 * j + 2 * tt + 1] = f.y + p1 * epi.scale;
                 }
               }
+            } else if (EPI == kEpiMultimemRed) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[j]))) * epi.scale;
             } else {
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * epi.scale;
@@ -358,13 +372,23 @@ __global__ void __launch_bounds__(192, 1)
               }
             }
             uint4* o4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(epi.out) + (int64_t)row * epi.ldo + col);
+            if (EPI == kEpiMultimemRed) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              o4[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
-                                 pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+              for (int j = 0; j < 4; ++j)
+                multimem_red_add_v4_bf16x2(o4 + j, pack_bf16x2(v[8 * j], v[8 * j + 1]),
+                                           pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                                           pack_bf16x2(v[8 * j + 4], v[8 * j + 5]),
+                                           pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                o4[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                                   pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+            }
           }
         }
       }
+      if (EPI == kEpiMultimemRed) __threadfence_system();  // this tile's reductions precede the next barrier
       // accumulator drained: hand the TMEM buffer back to the MMA warp
       tc_fence_before();
       __syncwarp();
@@ -422,6 +446,7 @@ static void dispatch_epi(int epi_kind, const CUtensorMap& ta, const CUtensorMap&
     case kEpiSwiGLU: launch_gemm<BN, kEpiSwiGLU, true>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
     case kEpiMaskAdapter: launch_gemm<BN, kEpiMaskAdapter, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
     case kEpiF32: launch_gemm<BN, kEpiF32, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
+    case kEpiMultimemRed: launch_gemm<BN, kEpiMultimemRed, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
     default: GSB_CHECK(false, "unknown epilogue kind ", epi_kind);
   }
 }
@@ -438,7 +463,7 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
                        const c10::optional<at::Tensor>& tile_mask, int64_t rank,
                        int64_t num_adapters, std::vector<int64_t> slice_bounds,
                        const c10::optional<at::Tensor>& row_adapter, int64_t mask_rank,
-                       int64_t mask_num_adapters, const at::Tensor& err) {
+                       int64_t mask_num_adapters, const at::Tensor& err, int64_t mc_out) {
   using namespace gsb;
   GSB_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "tensors must be on CUDA");
   GSB_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
@@ -495,11 +520,19 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     }
   }
   GemmEpiArgs epi{};
-  epi.out = out.data_ptr();
+  epi.out = (epi_kind == kEpiMultimemRed && mc_out != 0) ? reinterpret_cast<void*>(mc_out) : out.data_ptr();
   epi.ldo = out.stride(0);
   epi.scale = (float)scale;
   epi.residual = nullptr;
   epi.ldr = 0;
+  if (epi_kind == kEpiMultimemRed) {
+    GSB_CHECK(mc_out != 0, "multimem epilogue needs the multicast address of the output");
+    GSB_CHECK((mc_out & 15) == 0, "multicast address must be 16-byte aligned");
+    if (residual.has_value()) {
+      epi.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+      epi.ldr = residual->stride(0);
+    }
+  }
   if (epi_kind == kEpiResAdd) {
     GSB_CHECK(residual.has_value(), "residual required");
     epi.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());

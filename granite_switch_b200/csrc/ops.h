@@ -13,7 +13,7 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
                        const c10::optional<at::Tensor>& tile_mask, int64_t rank,
                        int64_t num_adapters, std::vector<int64_t> slice_bounds,
                        const c10::optional<at::Tensor>& row_adapter, int64_t mask_rank,
-                       int64_t mask_num_adapters, const at::Tensor& err);
+                       int64_t mask_num_adapters, const at::Tensor& err, int64_t mc_out);
 
 void gsb_rmsnorm(const at::Tensor& x, const at::Tensor& w, const at::Tensor& out,
                  const c10::optional<at::Tensor>& rows, double eps);
@@ -43,3 +43,8 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
                               const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
                               const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t num_q_heads,
                               double scale, const at::Tensor& out, const at::Tensor& err, int64_t dbg_ptr);
+void gsb_peer_barrier(const at::Tensor& pad_ptrs_dev, int64_t rank, int64_t tp, int64_t epoch, int64_t budget_ns,
+                      const at::Tensor& err);
+void gsb_multimem_allreduce_bf16(int64_t mc_ptr, int64_t nbytes, int64_t rank, int64_t tp, const at::Tensor& like);
+void gsb_rmsnorm_residual_from(const at::Tensor& y, const at::Tensor& h, const at::Tensor& w, const at::Tensor& x,
+                               double eps);

@@ -277,7 +277,7 @@ class NativeGraniteSwitch:
 
     # ------------------------------------------------------------------ forward pieces
     def _proj(self, pl: PackedLinear, x: torch.Tensor, out: torch.Tensor, epi=G.EPI_STORE, residual=None,
-              scale=1.0):
+              scale=1.0, mc_out: int = 0):
         m = x.shape[0]
         if pl.has_lora:
             ra = self.row_adapter[pl.map_id, :m]
@@ -287,10 +287,11 @@ class NativeGraniteSwitch:
             bn = pl.swiglu_tile if epi == G.EPI_SWIGLU else None
             G.switched_gemm(x, pl.w, out, epi=epi, residual=residual, scale=scale, s=s, lb=pl.lb, tile_mask=tm,
                             rank=pl.rank, num_adapters=pl.n_local,
-                            slice_bounds=[0, pl.n] if epi == G.EPI_SWIGLU else pl.slice_bounds, bn=bn)
+                            slice_bounds=[0, pl.n] if epi == G.EPI_SWIGLU else pl.slice_bounds, bn=bn,
+                            mc_out=mc_out)
         else:
             bn = pl.swiglu_tile if epi == G.EPI_SWIGLU else None
-            G.switched_gemm(x, pl.w, out, epi=epi, residual=residual, scale=scale, bn=bn)
+            G.switched_gemm(x, pl.w, out, epi=epi, residual=residual, scale=scale, bn=bn, mc_out=mc_out)
         return out
 
     def _row_parallel(self, pl: PackedLinear, x: torch.Tensor, h: torch.Tensor, mult: float):
@@ -298,9 +299,6 @@ class NativeGraniteSwitch:
         m = x.shape[0]
         if self.tp_size == 1:
             self._proj(pl, x, h, epi=G.EPI_RESADD, residual=h, scale=mult)
-            return
-        if self.comm is not None:
-            self.comm.row_parallel(self, pl, x, h, mult)
             return
         y = self.h2[:m]
         if self.tp_rank == 0:
@@ -328,8 +326,12 @@ class NativeGraniteSwitch:
         qkv, attn, act = self.qkv[:t], self.attn[:t], self.act[:t]
         mult = float(cfg.residual_multiplier)
         scale = float(cfg.attention_multiplier)
+        comm = self.comm
+        if comm is not None:
+            E.rmsnorm(h, self.layers[0].in_norm, cfg.rms_norm_eps, out=x)
         for li, lw in enumerate(self.layers):
-            E.rmsnorm(h, lw.in_norm, cfg.rms_norm_eps, out=x)
+            if comm is None:
+                E.rmsnorm(h, lw.in_norm, cfg.rms_norm_eps, out=x)
             self._proj(lw.qkv, x, qkv)
             kc, vc = self.kv_cache[li, 0], self.kv_cache[li, 1]
             E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
@@ -341,10 +343,19 @@ class NativeGraniteSwitch:
                     A.paged_attention(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
                                       plan.work_row0, plan.rows, self.num_q, scale, attn, plan.nsplit,
                                       self.ws_o, self.ws_lse)
-            self._row_parallel(lw.o, attn, h, mult)
-            E.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps, out=x)
+            if comm is not None:
+                y = comm.row_parallel(self, lw.o, attn, h, mult)
+                comm.finish(y, h, lw.post_norm, x, cfg.rms_norm_eps)
+            else:
+                self._row_parallel(lw.o, attn, h, mult)
+                E.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps, out=x)
             self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
-            self._row_parallel(lw.down, act, h, mult)
+            if comm is not None:
+                y = comm.row_parallel(self, lw.down, act, h, mult)
+                nxt = self.layers[li + 1].in_norm if li + 1 < len(self.layers) else self.final_norm
+                comm.finish(y, h, nxt, x, cfg.rms_norm_eps)
+            else:
+                self._row_parallel(lw.down, act, h, mult)
         nb = b.logit_rows.numel()
         if nb == 0:
             return None

@@ -17,6 +17,7 @@ EPI_RESADD = 1
 EPI_SWIGLU = 2
 EPI_MASK_ADAPTER = 3
 EPI_F32 = 4
+EPI_MULTIMEM_RED = 5
 
 
 def pick_bn(m: int, n: int, candidates=(256, 128, 64)) -> int:
@@ -53,6 +54,7 @@ def switched_gemm(
     mask_rank: int = 0,
     mask_num_adapters: int = 0,
     bn: int | None = None,
+    mc_out: int = 0,
 ) -> torch.Tensor:
     m, _ = x.shape
     n = w.shape[0]
@@ -71,7 +73,7 @@ def switched_gemm(
     native().switched_gemm(
         x, w, out, epi, bn, residual, float(scale), s, lb, tile_mask, rank, num_adapters,
         list(slice_bounds) if slice_bounds is not None else [0, n], row_adapter, mask_rank,
-        mask_num_adapters, err_buffer(x.device),
+        mask_num_adapters, err_buffer(x.device), int(mc_out),
     )
     return out
 

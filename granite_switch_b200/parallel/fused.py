@@ -1,0 +1,88 @@
+"""Fused tensor-parallel collectives over NVSwitch symmetric memory.
+
+Row-parallel projections (o_proj, down) are computed by the switched GEMM with
+the ``EPI_MULTIMEM_RED`` epilogue: as each output tile's accumulator drains,
+its epilogue adds the tile into a symmetric bf16 buffer ``y`` through the
+NVLink multicast address (``multimem.red``), so the NVSwitch sums the ranks'
+partials and every rank's copy receives the total while other tiles are still
+being computed. Rank 0 folds the residual stream into its contribution. A
+bounded peer barrier then orders the reductions before the consumer, and one
+kernel moves the sum into the residual stream and applies the next RMSNorm
+(``h <- y; x <- RMSNorm(y); y <- 0``).
+
+This replaces the reference's ``tensor_model_parallel_all_reduce`` after the
+expand (reference: src/granite_switch/vllm/core/lora.py:568-586) and the
+separate residual add / norm kernels. Because the reduction result is
+multicast to all ranks, the next column-parallel GEMM (qkv, gate/up) reads its
+full input from local memory: the all-gather happens inside the switch.
+
+Requires NVLS multicast (``has_multicast_support``); without it the model keeps
+the NCCL all-reduce path. Buffers come from ``torch.distributed._symmetric_memory``.
+"""
+from __future__ import annotations
+
+import torch
+
+from .._native import err_buffer, native
+from ..ops import gemm as G
+
+BARRIER_BUDGET_NS = 5_000_000_000
+
+
+class FusedTPComm:
+    def __init__(self, group, device: torch.device, max_tokens: int, hidden: int):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = device
+        # two buffers, alternated per projection: a buffer is zeroed by its consumer
+        # one projection (and so one barrier) before any rank adds into it again
+        self.max_tokens, self.hidden = max_tokens, hidden
+        self.y = symm_mem.empty(2, max_tokens, hidden, dtype=torch.bfloat16, device=device)
+        self.y.zero_()
+        self.turn = 0
+        self.y_handle = symm_mem.rendezvous(self.y, group)
+        self.mc = int(self.y_handle.multicast_ptr) if self.y_handle.has_multicast_support() else 0
+        self.pads = symm_mem.empty(64, dtype=torch.int32, device=device)
+        self.pads.zero_()
+        self.pad_handle = symm_mem.rendezvous(self.pads, group)
+        self.pad_ptrs = torch.tensor(list(self.pad_handle.buffer_ptrs), dtype=torch.int64, device=device)
+        self.epoch = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+
+    @property
+    def supported(self) -> bool:
+        return self.mc != 0
+
+    def barrier(self, budget_ns: int = BARRIER_BUDGET_NS) -> None:
+        self.epoch += 1
+        native().peer_barrier(self.pad_ptrs, self.rank, self.world, self.epoch, budget_ns, err_buffer(self.device))
+
+    def row_parallel(self, model, pl, x: torch.Tensor, h: torch.Tensor, mult: float) -> torch.Tensor:
+        """Reduce ``x @ W_shard^T * mult`` (+ ``h`` once) over the group into ``y``; returns ``y[:m]``."""
+        m = x.shape[0]
+        b = self.turn
+        self.turn ^= 1
+        y = self.y[b, :m]
+        resid = h if self.rank == 0 else None
+        mc = self.mc + b * self.max_tokens * self.hidden * 2
+        model._proj(pl, x, y, epi=G.EPI_MULTIMEM_RED, residual=resid, scale=mult, mc_out=mc)
+        self.barrier()
+        return y
+
+    def finish(self, y: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor, x: torch.Tensor, eps: float) -> None:
+        """``h <- y; x <- RMSNorm(y) * norm_w; y <- 0``."""
+        native().rmsnorm_residual_from(y, h, norm_w, x, float(eps))
+
+
+def attach_fused_comm(model, group) -> bool:
+    """Attach a :class:`FusedTPComm` to a native model; False (NCCL path kept) without multicast."""
+    comm = FusedTPComm(group, model.device, model.max_tokens, model.hidden)
+    if not comm.supported:
+        return False
+    model.comm = comm
+    return True

@@ -1,0 +1,123 @@
+"""Tensor-parallel self-check: TP=N logits (NCCL and fused) against TP=1 on the same random model.
+
+Run under torchrun, one process per GPU::
+
+    torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m granite_switch_b200.parallel.tp_check
+
+Every rank builds the same seeded random model, keeps its shard, runs one
+prefill step and two decode steps through the native executor, and gathers
+the logits. Rank 0 also builds the unsharded model alone and compares. Prints
+one JSON line per checked mode on rank 0 and exits non-zero on a mismatch.
+"""
+from __future__ import annotations
+
+import datetime
+import json
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+
+def _config():
+    from ..composer.synthetic import base_config
+    from ..config import GraniteSwitchConfig
+
+    base = base_config(dict(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=3,
+                            num_attention_heads=8, num_key_value_heads=4, head_dim=128, rope_theta=10000.0))
+    na = 4
+    v = base["vocab_size"]
+    cfg = dict(base)
+    cfg.update(num_adapters=na, adapter_token_ids=list(range(v, v + na)), adapter_substitute_token_ids=[1] * na,
+               adapter_ranks=[16] * na, max_lora_rank=16, lora_target_modules=["qkv_proj", "o_proj"],
+               num_hidden_layers=base["num_hidden_layers"] + 2, vocab_size=v + na)
+    return GraniteSwitchConfig(**cfg)
+
+
+def _run(config, device, tp, rank, group, fused):
+    from ..engine import EngineConfig
+    from ..engine.executor import NativeExecutor
+    from ..engine.kv_cache import BlockManager
+    from ..engine.llm_engine import HostRouter
+    from ..engine.request import Request, SamplingParams
+    from ..engine.scheduler import Scheduler
+    from ..models.native import NativeGraniteSwitch
+
+    m = NativeGraniteSwitch.from_random(config, device, max_tokens=512, num_kv_blocks=256,
+                                        lora_modules=("qkv", "o"), rank=16, seed=7, tp_rank=rank, tp_size=tp,
+                                        tp_group=group, max_seqs=16)
+    if fused:
+        from .fused import attach_fused_comm
+
+        if not attach_fused_comm(m, group):
+            return None
+    ex = NativeExecutor(m, 1024, group, tp)
+    bm = BlockManager(256)
+    router = HostRouter(config)
+    sch = Scheduler(bm, 8, 512, True, route_fn=router)
+    g = torch.Generator().manual_seed(3)
+    ctrl = config.adapter_token_ids
+    for i in range(3):
+        ids = torch.randint(5, 2000, (40 + 17 * i,), generator=g).tolist() + [ctrl[i], 9, 10]
+        sch.add(Request(ids, SamplingParams(max_tokens=3)))
+    outs = []
+    for _ in range(3):
+        out = sch.schedule()
+        _, logits = ex.compute_logits(out)
+        outs.append(logits.float().cpu())
+        toks = logits.argmax(dim=-1).tolist()
+        j = 0
+        for c in out.chunks:
+            r = c.req
+            r.carry = router(r.all_ids[c.start:c.start + c.num_tokens], r.carry)
+            r.num_computed = c.start + c.num_tokens
+            if c.needs_sample:
+                r.output_ids.append(toks[j])
+                j += 1
+    from .._native import read_errors
+
+    errs = read_errors(device)
+    return outs, errs
+
+
+def main() -> int:
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    group = dist.group.WORLD
+    config = _config()
+    results = {}
+    nccl = _run(config, device, world, rank, group, fused=False)
+    results["nccl"] = nccl
+    dist.barrier()
+    fused = _run(config, device, world, rank, group, fused=True)
+    results["fused"] = fused
+    dist.barrier()
+    ok = True
+    if rank == 0:
+        ref, _ = _run(config, device, 1, 0, None, fused=False)
+        for mode, res in results.items():
+            if res is None:
+                print(json.dumps({"mode": mode, "skipped": "no NVLS multicast support"}), flush=True)
+                continue
+            outs, errs = res
+            worst = max(((a - b).abs().max() / b.abs().max()).item() for a, b in zip(outs, ref))
+            agree = sum(int((a.argmax(-1) == b.argmax(-1)).sum()) for a, b in zip(outs, ref))
+            total = sum(b.shape[0] for b in ref)
+            good = worst < 0.05 and agree >= total - 1 and errs == 0
+            ok &= good
+            print(json.dumps({"mode": mode, "tp": world, "max_rel_err": round(worst, 5), "argmax_agree": agree,
+                              "rows": total, "device_errors": errs, "ok": good}), flush=True)
+    flag = torch.tensor([1 if ok else 0], device=device)
+    dist.broadcast(flag, 0)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0 if int(flag.item()) else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
