@@ -54,7 +54,8 @@ def parse_args():
     p.add_argument("--max-num-batched-tokens", type=int, default=8192)
     p.add_argument("--ramp-steps", type=int, default=400, help="max untimed steps to reach steady concurrency")
     p.add_argument("--mode", choices=["alora", "lora"], default="alora")
-    p.add_argument("--fused-comm", action="store_true", help="fused GEMM+collective kernels for TP")
+    p.add_argument("--no-fused-comm", dest="fused_comm", action="store_false",
+                   help="use NCCL all-reduce instead of the fused GEMM+multimem collectives for TP")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-blocks", type=int, default=None)
     return p.parse_args()
@@ -103,7 +104,7 @@ def run_native(args):
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank()))
         group = dist.group.WORLD
     _native.native()
@@ -232,7 +233,7 @@ def run_native(args):
                        "workload": f"poisson {args.rate}/s, {args.calls} chained calls, inv 16-64, gen 32-128",
                        "mode": args.mode, "max_num_batched_tokens": args.max_num_batched_tokens,
                        "ramp_steps": ramp, "l2": "inputs larger than L2 (each step streams all weights)",
-                       "fused_comm": bool(args.fused_comm)},
+                       "fused_comm": bool(getattr(llm.model, "comm", None) is not None)},
             "e2e": {"value": round(e2e, 2), "unit": "output tok/s", "h2d_bytes_per_step": (ex.h2d_bytes - h2d0) // args.steps,
                     "d2h_bytes_per_step": (ex.d2h_bytes - d2h0) // args.steps},
             "gpu_launches": launches,

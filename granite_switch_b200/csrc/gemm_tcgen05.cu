@@ -68,7 +68,20 @@ struct GemmEpiArgs {
   const int32_t* row_adapter;  // kEpiMaskAdapter: kernel-local adapter id per row
   int mask_rank;               // kEpiMaskAdapter: rank (columns per adapter)
   int mask_num_adapters;
+  const uint64_t* skip_mask;   // kEpiMaskAdapter: adapters present per 128-row tile; tiles
+                               // whose columns belong only to absent adapters are skipped
 };
+
+// A shrink tile is skipped when none of the adapters owning its columns has a
+// row in its 128-row tile: the expand never reads those columns for that tile.
+template <int BN>
+__device__ __forceinline__ bool shrink_tile_skipped(const GemmEpiArgs& epi, int mt, int n0) {
+  if (epi.skip_mask == nullptr) return false;
+  uint64_t need = 0;
+  for (int c = 0; c < BN; c += epi.mask_rank)
+    need |= 1ull << (((n0 + c) / epi.mask_rank) % epi.mask_num_adapters);
+  return (epi.skip_mask[mt] & need) == 0;
+}
 
 template <int BN>
 struct GemmCfg {
@@ -186,6 +199,7 @@ __global__ void __launch_bounds__(192, 1)
         int mt, nt;
         gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
         const int m0 = mt * C::BM, n0 = nt * BN;
+        if (EPI == kEpiMaskAdapter && shrink_tile_skipped<BN>(epi, mt, n0)) continue;
         const LoraTile lt = lora_tile<SPLIT>(lora, mt, n0);
         const int total = main_blocks + lt.blocks;
         uint64_t rem = lt.amask;
@@ -234,9 +248,10 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t kb = 0;
       int ltile = 0;
       bool stop = false;
-      for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x, ++ltile) {
+      for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x) {
         int mt, nt;
         gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
+        if (EPI == kEpiMaskAdapter && shrink_tile_skipped<BN>(epi, mt, nt * BN)) continue;
         const LoraTile lt = lora_tile<SPLIT>(lora, mt, nt * BN);
         const int total = main_blocks + lt.blocks;
         const int acc = ltile & 1;
@@ -281,16 +296,18 @@ __global__ void __launch_bounds__(192, 1)
           umma_commit(&empty_bar[s]);
         }
         umma_commit(&tfull_bar[acc]);
+        ++ltile;  // only tiles that use an accumulator advance the buffer sequence
       }
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int ltile = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++ltile) {
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int mt, nt;
       gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
       const int m0 = mt * C::BM, n0 = nt * BN;
+      if (EPI == kEpiMaskAdapter && shrink_tile_skipped<BN>(epi, mt, n0)) continue;
       const int acc = ltile & 1;
       if (*abort_flag || !mbar_wait(&tfull_bar[acc], (ltile >> 1) & 1, err, kErrGemmWait)) {
         *abort_flag = 1;
@@ -393,6 +410,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      ++ltile;
     }
   }
 
@@ -557,6 +575,13 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     epi.row_adapter = row_adapter->data_ptr<int32_t>();
     epi.mask_rank = (int)mask_rank;
     epi.mask_num_adapters = (int)mask_num_adapters;
+    epi.skip_mask = nullptr;
+    if (tile_mask.has_value()) {  // for the shrink, tile_mask selects the tiles to compute
+      GSB_CHECK(tile_mask->scalar_type() == at::kLong && tile_mask->numel() >= (M + 127) / 128,
+                "tile_mask must be int64 [ceil(M/128)]");
+      epi.skip_mask = reinterpret_cast<const uint64_t*>(tile_mask->data_ptr());
+      GSB_CHECK(mask_num_adapters <= 64, "at most 64 adapters per module");
+    }
     GSB_CHECK(mask_rank > 0 && mask_num_adapters > 0, "mask_rank and mask_num_adapters required");
   }
   uint32_t* errp = reinterpret_cast<uint32_t*>(err.data_ptr());

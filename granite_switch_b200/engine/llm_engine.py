@@ -81,6 +81,7 @@ class LLMEngine:
         self.requests: dict[str, Request] = {}
         self.eos = config.eos_token_id if isinstance(config.eos_token_id, int) else None
         self.on_finish = None  # optional callback(req)
+        self.health = None     # optional parallel.health.Heartbeat (multi-rank)
 
     # -------------------------------------------------------------- requests
     def add_request(self, prompt_ids: list[int], sampling: SamplingParams | None = None,
@@ -112,7 +113,11 @@ class LLMEngine:
         out = self.scheduler.schedule()
         if not out.chunks:
             return []
+        if self.health is not None:
+            self.health.check()  # a dead peer is reported here, not inside a collective
         tokens = self.executor.execute(out)
+        if self.health is not None:
+            self.health.beat()
         now = time.perf_counter()
         finished = []
         j = 0

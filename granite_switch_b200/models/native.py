@@ -282,8 +282,8 @@ class NativeGraniteSwitch:
         if pl.has_lora:
             ra = self.row_adapter[pl.map_id, :m]
             s = self.s_buf[:m, : pl.a_all.shape[0]]
-            G.lora_shrink(x, pl.a_all, ra, pl.rank, pl.n_local, out=s)
             tm = self.tile_mask[pl.map_id, : (m + 127) // 128]
+            G.lora_shrink(x, pl.a_all, ra, pl.rank, pl.n_local, out=s, tile_mask=tm)
             bn = pl.swiglu_tile if epi == G.EPI_SWIGLU else None
             G.switched_gemm(x, pl.w, out, epi=epi, residual=residual, scale=scale, s=s, lb=pl.lb, tile_mask=tm,
                             rank=pl.rank, num_adapters=pl.n_local,

@@ -79,14 +79,21 @@ def switched_gemm(
 
 
 def lora_shrink(x: torch.Tensor, a_all: torch.Tensor, row_adapter: torch.Tensor, rank: int,
-                num_adapters: int, out: torch.Tensor | None = None) -> torch.Tensor:
-    """``S = mask(x @ a_all.T)``: row ``m`` keeps only its adapter's columns."""
+                num_adapters: int, out: torch.Tensor | None = None,
+                tile_mask: torch.Tensor | None = None) -> torch.Tensor:
+    """``S = mask(x @ a_all.T)``: row ``m`` keeps only its adapter's columns.
+
+    With ``tile_mask`` (adapters present per 128-row tile) only the column
+    blocks of present adapters are computed; the expand reads nothing else.
+    """
     n = a_all.shape[0]
     if n % 64:
         raise ValueError(f"a_all must have a multiple of 64 rows (pad with zeros), got {n}")
+    bn = pick_bn(x.shape[0], n, (128, 64))
+    if bn > rank * num_adapters:
+        bn = 64
     return switched_gemm(x, a_all, out, epi=EPI_MASK_ADAPTER, row_adapter=row_adapter,
-                         mask_rank=rank, mask_num_adapters=num_adapters,
-                         bn=pick_bn(x.shape[0], n, (128, 64)))
+                         mask_rank=rank, mask_num_adapters=num_adapters, tile_mask=tile_mask, bn=bn)
 
 
 # ---------------------------------------------------------------- oracle

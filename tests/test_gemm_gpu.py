@@ -91,6 +91,12 @@ def test_lora_expand_fused(m):
     ref = G.switched_gemm_reference(x, w, s=s, lb=lb, rank=rank, num_adapters=na,
                                     slice_bounds=bounds)
     _close(out, ref)
+    # shrink restricted to the adapters present per tile gives the same projection
+    s2 = torch.full_like(s, float("nan"))
+    G.lora_shrink(x, a_all, row_adapter, rank, na, out=s2, tile_mask=mask)
+    out2 = G.switched_gemm(x, w, s=s2, lb=lb, tile_mask=mask, rank=rank, num_adapters=na,
+                           slice_bounds=bounds, bn=128)
+    _close(out2, ref)
 
 
 def test_swiglu_split_lora():
