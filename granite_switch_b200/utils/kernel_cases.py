@@ -1,0 +1,94 @@
+"""One launch of each native kernel on a representative shape, for profiler captures.
+
+``python -m granite_switch_b200.utils.kernel_cases <case>`` with case in
+gemm, swiglu, decode_gemm, attn_prefill, attn_decode, rmsnorm, rope, embed,
+routing, sample (or ``all``). Pair it with ``ncu -k regex:<kernel> -c 1``.
+"""
+import sys
+
+import torch
+
+from granite_switch_b200.ops import gemm as G, elementwise as E, attention as A
+from granite_switch_b200._native import native, err_buffer, check_errors
+from granite_switch_b200.ops.routing import route_device
+from granite_switch_b200.routing.scan import expert_table
+from granite_switch_b200.engine.sampling import sample
+from granite_switch_b200.engine.request import SamplingParams, Request
+dev = "cuda"
+torch.manual_seed(0)
+err_buffer(torch.device(dev))
+which = sys.argv[1] if len(sys.argv) > 1 else "all"
+def want(n): return which in ("all", n)
+H, I, T = 4096, 12800, 4096
+if want("gemm"):  # qkv-shape prefill GEMM with fused LoRA expand (12 adapters r32, 3 slices)
+    x = torch.randn(T, H, device=dev).bfloat16()
+    w = (torch.randn(6144, H, device=dev) * 0.02).bfloat16()
+    na, r = 12, 32
+    ra = torch.randint(0, na + 1, (T,), device=dev, dtype=torch.int32)
+    a_all = (torch.randn(3 * na * r, H, device=dev) * 0.02).bfloat16()
+    lb = (torch.randn(6144, na * r, device=dev) * 0.02).bfloat16()
+    tm = torch.full(((T + 127) // 128,), (1 << na) - 1, dtype=torch.int64, device=dev)
+    s = G.lora_shrink(x, a_all, ra, r, na, tile_mask=tm)
+    out = G.switched_gemm(x, w, s=s, lb=lb, tile_mask=tm, rank=r, num_adapters=na, slice_bounds=[0, 4096, 5120, 6144])
+if want("swiglu"):
+    x = torch.randn(T, H, device=dev).bfloat16()
+    w = (torch.randn(2 * I, H, device=dev) * 0.02).bfloat16()
+    out = G.switched_gemm(x, w, epi=G.EPI_SWIGLU, bn=256)
+if want("decode_gemm"):
+    x = torch.randn(128, H, device=dev).bfloat16()
+    w = (torch.randn(H, I, device=dev) * 0.02).bfloat16()
+    x2 = torch.randn(128, I, device=dev).bfloat16()
+    h = torch.randn(128, H, device=dev).bfloat16()
+    G.switched_gemm(x2, w, h, epi=G.EPI_RESADD, residual=h, scale=0.5)
+if want("attn_prefill") or want("attn_decode"):
+    hq, hkv, d = 32, 8, 128
+    def setup(q_lens, kv_lens):
+        nblk = sum((l + 15)//16 for l in kv_lens) + 4
+        kc = torch.randn(nblk, hkv, 16, d, device=dev).bfloat16(); vc = torch.randn_like(kc)
+        maxb = max((l+15)//16 for l in kv_lens)
+        bt = torch.arange(nblk, dtype=torch.int32)[: len(kv_lens) * maxb].view(len(kv_lens), maxb) if nblk >= len(kv_lens)*maxb else None
+        bt = torch.zeros(len(kv_lens), maxb, dtype=torch.int32); p = 0
+        for i, l in enumerate(kv_lens):
+            for j in range((l+15)//16): bt[i, j] = p; p += 1
+        Tq = sum(q_lens)
+        q = torch.randn(Tq, (hq+2*hkv)*d, device=dev).bfloat16()
+        out = torch.empty(Tq, hq*d, device=dev).bfloat16()
+        qs = [0]
+        for l in q_lens: qs.append(qs[-1]+l)
+        return kc, vc, bt.to(dev), q, out, torch.tensor(qs, dtype=torch.int32, device=dev), torch.tensor(kv_lens, dtype=torch.int32, device=dev)
+    if want("attn_prefill"):
+        q_lens = [4096]; kc, vc, bt, q, out, qs, kvl = setup(q_lens, q_lens)
+        ws, wr = [torch.tensor(v, dtype=torch.int32, device=dev) for v in A.build_work(q_lens, 4, 128)]
+        A.prefill_attention_tc(q, kc, vc, bt, qs, kvl, ws, wr, hq, 0.088, out)
+    if want("attn_decode"):
+        q_lens = [1] * 128; kv = [4200] * 128; kc, vc, bt, q, out, qs, kvl = setup(q_lens, kv)
+        ws, wr = [torch.tensor(v, dtype=torch.int32, device=dev) for v in A.build_work(q_lens, 4, 16)]
+        A.paged_attention(q, kc, vc, bt, qs, kvl, ws, wr, 16, hq, 0.088, out, 1)
+if want("rmsnorm"):
+    x = torch.randn(16384, H, device=dev).bfloat16(); w = torch.ones(H, device=dev).bfloat16()
+    E.rmsnorm(x, w, 1e-5)
+if want("rope"):
+    cs = E.rope_cos_sin_table(8192, 128, 1e4, dev)
+    qkv = torch.randn(8192, 48 * 128, device=dev).bfloat16(); pos = torch.arange(8192, device=dev)
+    kc = torch.zeros(512, 8, 16, 128, device=dev).bfloat16(); vc = torch.zeros_like(kc)
+    E.rope_kv(qkv, pos, cs, 32, 8, 128, kc, vc, torch.arange(8192, device=dev))
+if want("embed"):
+    tab = torch.randn(49164, H, device=dev).bfloat16(); ids = torch.randint(0, 49164, (8192,), device=dev)
+    E.embed(ids, tab, None, 12.0)
+if want("routing"):
+    tbl = expert_table(list(range(49152, 49164)), 12, 49164).to(dev)
+    T2 = 8192; ids = torch.randint(0, 49164, (T2,), device=dev)
+    starts = torch.arange(0, T2 + 1, 64, dtype=torch.int32, device=dev); S = starts.numel() - 1
+    remap = torch.arange(13, dtype=torch.int32, device=dev).view(1, 13)
+    route_device(ids, starts, torch.zeros(S, dtype=torch.int32, device=dev), tbl, None, None, 12, remap,
+                 torch.empty(T2, dtype=torch.int32, device=dev), torch.empty(T2, dtype=torch.int32, device=dev),
+                 torch.empty(T2, dtype=torch.long, device=dev), torch.empty(S, dtype=torch.int32, device=dev),
+                 torch.empty(1, T2, dtype=torch.int32, device=dev), torch.empty(1, (T2 + 127)//128, dtype=torch.int64, device=dev))
+if want("sample"):
+    logits = torch.randn(128, 49164, device=dev)
+    reqs = [Request([1]) for _ in range(128)]
+    sample(logits, [SamplingParams(temperature=0.8, top_k=50, top_p=0.9, seed=i) for i in range(128)], reqs)
+    E.argmax(logits)
+torch.cuda.synchronize()
+check_errors(torch.device(dev))
+print("ok", which)
