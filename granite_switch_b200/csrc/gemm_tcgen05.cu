@@ -18,7 +18,8 @@
 // memory ring, warp 1 owns the TMEM allocation and issues tcgen05.mma from
 // one thread, warps 2..5 drain the fp32 accumulator with tcgen05.ld and run
 // the epilogue (store / residual add / SwiGLU / adapter mask / fp32 logits).
-// No cluster multicast is used, so the kernel is safe on every GPU count.
+// Every TMA load is a plain single-CTA copy from this GPU's memory, so the
+// kernel is safe on every GPU count.
 #include "common.cuh"
 #include "tma_util.h"
 
