@@ -498,3 +498,162 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
     GSB_CUDA_CHECK(cudaGetLastError());
   }
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free split-KV decode attention (declared in noalloc_attention.h;
+// no counterpart in the reference). Same kernels as the nsplit > 1 decode path
+// of gsb_paged_attention, but the fp32 partial outputs and log-sum-exps live
+// in a fixed static device array instead of caller-allocated workspaces, and
+// the entry point takes raw pointers so a caller without PyTorch (or one that
+// may not allocate) can use it.
+// ---------------------------------------------------------------------------
+#include "noalloc_attention.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+namespace gsb {
+namespace noalloc {
+
+constexpr int64_t kScratchFloats = GSB_NOALLOC_SCRATCH_FLOATS;
+constexpr int kMaxDevices = 64;
+
+// Shared by every call on a device; see the header for the sharing rules.
+static __device__ __align__(256) float g_scratch[kScratchFloats];
+
+__global__ void fill_neg_inf_kernel(float* __restrict__ p, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = -INFINITY;
+}
+
+struct DeviceState {
+  bool ready = false;
+  float* scratch = nullptr;
+};
+static std::mutex g_mu;
+static DeviceState g_state[kMaxDevices];
+
+static int fail(char* msg, size_t len, int code, const char* fmt, ...) {
+  if (msg != nullptr && len > 0) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(msg, len, fmt, ap);
+    va_end(ap);
+  }
+  return code;
+}
+
+// Once per device, with that device current: the scratch array's address and
+// the kernels' shared-memory limits.
+static int setup(int dev, float** scratch, char* msg, size_t len) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& s = g_state[dev];
+  if (!s.ready) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(msg, len, GSB_NOALLOC_ECUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    e = cudaFuncSetAttribute(paged_attn_kernel<128, 1, 64, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             AttnCfg<128, 1, 64, 3>::SMEM);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(paged_attn_kernel<64, 1, 64, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               AttnCfg<64, 1, 64, 6>::SMEM);
+    if (e != cudaSuccess)
+      return fail(msg, len, GSB_NOALLOC_ECUDA, "cudaFuncSetAttribute failed on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    s.scratch = static_cast<float*>(p);
+    s.ready = true;
+  }
+  *scratch = s.scratch;
+  return GSB_NOALLOC_OK;
+}
+
+template <int D, int ST>
+static void launch_decode(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const CUtensorMap& tv, const void* q,
+                          int64_t q_stride, const int32_t* bt, int64_t bt_stride, const int32_t* q_start,
+                          const int32_t* kv_len, const int32_t* work_seq, const int32_t* work_row0, int Hq, int Hkv,
+                          float scale_log2, void* out, int64_t out_stride, float* wso, float* wsl, int nsplit, int T,
+                          uint32_t* err) {
+  using C = AttnCfg<D, 1, 64, ST>;
+  paged_attn_kernel<D, 1, 64, ST><<<grid, C::THREADS, C::SMEM, st>>>(
+      tk, tv, reinterpret_cast<const __nv_bfloat16*>(q), q_stride, bt, (int)bt_stride, q_start, kv_len, work_seq,
+      work_row0, Hq, Hkv, scale_log2, reinterpret_cast<__nv_bfloat16*>(out), out_stride, wso, wsl, nsplit, T, err);
+  if (nsplit > 1)
+    attn_merge_kernel<D><<<dim3(T, Hq), D, 0, st>>>(wso, wsl, nsplit, T, Hq, reinterpret_cast<__nv_bfloat16*>(out),
+                                                    out_stride);
+}
+
+}  // namespace noalloc
+}  // namespace gsb
+
+extern "C" int gsb_decode_attention_noalloc(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                                            int64_t num_blocks, int num_kv_heads, int head_dim,
+                                            const int32_t* block_table, int64_t block_table_stride,
+                                            const int32_t* q_start, const int32_t* kv_len, const int32_t* work_seq,
+                                            const int32_t* work_row0, int num_work, int num_tokens, int num_q_heads,
+                                            float scale, int nsplit, void* out, int64_t out_stride, uint32_t* err,
+                                            cudaStream_t stream, char* msg, size_t msg_len) {
+  using namespace gsb::noalloc;
+  if (msg != nullptr && msg_len > 0) msg[0] = '\0';
+  if (!q || !k_cache || !v_cache || !block_table || !q_start || !kv_len || !work_seq || !work_row0 || !out || !err)
+    return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "null pointer argument");
+  const int D = head_dim, Hq = num_q_heads, Hkv = num_kv_heads, T = num_tokens;
+  if (D != 64 && D != 128) return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "head_dim must be 64 or 128, got %d", D);
+  if (Hkv <= 0 || Hq <= 0 || Hq % Hkv != 0)
+    return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "num_q_heads (%d) must be a positive multiple of num_kv_heads (%d)",
+                Hq, Hkv);
+  if (num_work < 0 || T <= 0 || num_blocks <= 0 || block_table_stride <= 0)
+    return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "sizes must be positive");
+  if (nsplit < 1 || nsplit > 64) return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "nsplit must be in [1, 64], got %d", nsplit);
+  if ((reinterpret_cast<uintptr_t>(q) & 15) || q_stride < (int64_t)Hq * D || q_stride % 8 != 0)
+    return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "q must be 16-byte aligned with a row stride >= Hq*D, multiple of 8");
+  if ((reinterpret_cast<uintptr_t>(out) & 3) || out_stride < (int64_t)Hq * D || out_stride % 2 != 0)
+    return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "out must be 4-byte aligned with an even row stride >= Hq*D");
+  if ((reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15))
+    return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "k_cache and v_cache must be 16-byte aligned");
+  const int64_t page_rows = num_blocks * (int64_t)Hkv * attn::PAGE;
+  if (page_rows >= (int64_t(1) << 31))
+    return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "cache too large for 32-bit TMA coordinates");
+  const int64_t o_floats = (int64_t)nsplit * T * Hq * D;
+  const int64_t lse_off = (o_floats + 63) / 64 * 64;  // 256-byte aligned LSE region
+  const int64_t need = (nsplit > 1) ? lse_off + (int64_t)nsplit * T * Hq : 0;
+  if (need > kScratchFloats)
+    return fail(msg, msg_len, GSB_NOALLOC_ETOOBIG,
+                "split partials need %lld fp32 values (nsplit %d x tokens %d x heads %d x (head_dim %d + 1)), "
+                "over the fixed scratch of %lld; lower nsplit or split the batch",
+                (long long)need, nsplit, T, Hq, D, (long long)kScratchFloats);
+  if (num_work == 0) return GSB_NOALLOC_OK;
+
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(msg, msg_len, GSB_NOALLOC_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "device %d out of range", dev);
+  float* scratch = nullptr;
+  const int rc = setup(dev, &scratch, msg, msg_len);
+  if (rc != GSB_NOALLOC_OK) return rc;
+  try {
+    const CUtensorMap tk = gsb::make_tmap_bf16_2d(k_cache, page_rows, D, D, 64, attn::PAGE, CU_TENSOR_MAP_SWIZZLE_128B);
+    const CUtensorMap tv = gsb::make_tmap_bf16_2d(v_cache, page_rows, D, D, 64, attn::PAGE, CU_TENSOR_MAP_SWIZZLE_128B);
+    float* wso = (nsplit > 1) ? scratch : nullptr;
+    float* wsl = (nsplit > 1) ? scratch + lse_off : nullptr;
+    if (nsplit > 1) {
+      const int64_t n = (int64_t)nsplit * T * Hq;
+      fill_neg_inf_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148), 256, 0, stream>>>(wsl, n);
+    }
+    const float scale_log2 = (float)(scale * 1.4426950408889634);
+    const dim3 grid(num_work, Hkv, nsplit);
+    if (D == 128)
+      launch_decode<128, 3>(grid, stream, tk, tv, q, q_stride, block_table, block_table_stride, q_start, kv_len,
+                            work_seq, work_row0, Hq, Hkv, scale_log2, out, out_stride, wso, wsl, nsplit, T, err);
+    else
+      launch_decode<64, 6>(grid, stream, tk, tv, q, q_stride, block_table, block_table_stride, q_start, kv_len,
+                           work_seq, work_row0, Hq, Hkv, scale_log2, out, out_stride, wso, wsl, nsplit, T, err);
+  } catch (const std::exception& ex) {
+    return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "%s", ex.what());
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(msg, msg_len, GSB_NOALLOC_ECUDA, "launch failed: %s", cudaGetErrorString(e));
+  return GSB_NOALLOC_OK;
+}
