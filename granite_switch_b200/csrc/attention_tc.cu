@@ -2,18 +2,20 @@
 //
 // One CTA owns 128 query rows of one request and one KV head (a row is a
 // (query token, query head of the GQA group) pair, as in attention.cu) and
-// walks the request's paged K/V in tiles of 128 keys:
+// walks the request's paged K/V in tiles of 64 keys:
 //
-//   S_j  = Q . K_j^T        tcgen05.mma M=128 N=128 K=D, S_j in TMEM (2 buffers)
+//   S_j  = Q . K_j^T        tcgen05.mma M=128 N=64 K=D, S_j in TMEM (2 buffers)
 //   P_j  = softmax rows      softmax warps: tcgen05.ld one S row per thread,
 //                            mask, running max/sum in registers, P_j -> smem
-//   O   += P_j . V_j         tcgen05.mma M=128 N=D K=128, O in TMEM; V is read
+//                            over the K_j tile that S_j consumed
+//   O   += P_j . V_j         tcgen05.mma M=128 N=D K=64, O in TMEM; V is read
 //                            straight from its [key][d] tile as an MN-major B
 //
 // Warp roles (192 threads): warp 0 issues the K/V page boxes by TMA
 // (double-buffered), warp 1 owns TMEM and issues every MMA from one thread,
-// warps 2..5 run the softmax, rescale O in TMEM when a row maximum grows, and
-// write the normalised output. S_{j+1} is issued before P_j . V_j so the tensor
+// warps 2..5 run the softmax, rescale O in TMEM when a row maximum grows by
+// more than 2^8, and write the normalised output. Two CTAs share an SM, so one
+// CTA's softmax overlaps the other's MMAs; work tiles arrive heaviest first. S_{j+1} is issued before P_j . V_j so the tensor
 // core computes the next scores while the softmax of the current tile runs.
 // Every mbarrier wait is bounded; the error word reports a timeout.
 // (reference: attention comes from vLLM's backends, called at
@@ -79,14 +81,14 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* kv_empty = kv_full + 2;                     // [2]
   uint64_t* s_full = kv_empty + 2;                      // [2]
   uint64_t* s_empty = s_full + 2;                       // [2]
-  uint64_t* p_full = s_empty + 2;                       // [1]
-  uint64_t* o_done = p_full + 1;                        // [1]
-  uint64_t* q_ready = o_done + 1;                       // [1]
+  uint64_t* p_full = s_empty + 2;                       // [2] by tile parity
+  uint64_t* o_done = p_full + 2;                        // [2] by tile parity
+  uint64_t* q_ready = o_done + 2;                       // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int w = blockIdx.x, kvh = blockIdx.y;
+  const int kvh = blockIdx.x, w = blockIdx.y;  // KV heads fastest: the heaviest work tiles launch first
   const int seq = work_seq[w];
   const int row0 = work_row0[w];
   const int G = Hq / Hkv;
@@ -106,9 +108,9 @@ __global__ void __launch_bounds__(192, 2)
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(o_done, 1);
     mbar_init(q_ready, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -206,7 +208,7 @@ __global__ void __launch_bounds__(192, 2)
         if (j + 1 < n_tiles) ok = issue_s(j + 1);
         if (!ok) break;
         // O += P_j . V_j once the softmax has written P_j (and rescaled O)
-        if (*abort_flag || !mbar_wait(p_full, j & 1, err, kErrAttnWait)) {
+        if (*abort_flag || !mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, kErrAttnWait)) {
           ok = false;
           break;
         }
@@ -221,7 +223,7 @@ __global__ void __launch_bounds__(192, 2)
           const uint64_t bd = umma_desc_sw128_mn(v_addr + kk * 2048, KT * 128, 1024);
           umma_bf16(tmem + C::O_COL, ad, bd, idesc_o, (j | kk) != 0);
         }
-        umma_commit(o_done);
+        umma_commit(&o_done[j & 1]);
         umma_commit(&kv_empty[j & 1]);
         FA_PROGRESS(3, 200 + j);
       }
@@ -229,6 +231,12 @@ __global__ void __launch_bounds__(192, 2)
     }
   } else {
     // ---------------- softmax + epilogue (warps 2..5) ----------------
+    // Each thread owns one row. The running max m (log2 domain) is allowed to
+    // lag the true maximum by up to kLazyLog2: P = 2^(s - m) then stays below
+    // 2^kLazyLog2, which bf16 P and fp32 O / l represent exactly as well, and
+    // O in TMEM is rescaled only when some row's max grows by more than that.
+    // Without a rescale the warp never waits for the previous P.V.
+    constexpr float kLazyLog2 = 8.f;
     const int qd = warp & 3;
     const int r = qd * 32 + lane;                 // row within the tile
     const int gr = row0 + r;
@@ -244,46 +252,46 @@ __global__ void __launch_bounds__(192, 2)
         break;
       }
       tc_fence_after();
-      float sv[KT];
+      uint32_t sv[KT];
       {
         const uint32_t tS = tmem + lane_base + (s ? C::S_COL1 : C::S_COL0);
 #pragma unroll
-        for (int c = 0; c < KT / 32; ++c) {
-          uint32_t rr[32];
-          tmem_ld32(tS + c * 32, rr);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(rr[i]);
-        }
+        for (int c = 0; c < KT / 32; ++c) tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t(&)[32]>(sv[c * 32]));
+        tmem_wait_ld();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[s]);
       if (lane == 0) FA_PROGRESS(4 + qd, 300 + j);
-      // mask (causal + key range) and running max in the log2 domain
+      // causal / key-range mask, only on tiles that cross this warp's diagonal or k_end
       const int kbase = j * KT;
-      float mt = -INFINITY;
+      if (__any_sync(0xffffffffu, kbase + KT - 1 > pos || kbase + KT > k_end)) {
 #pragma unroll
-      for (int i = 0; i < KT; ++i) {
-        const int key = kbase + i;
-        float v = sv[i] * scale_log2;
-        if (key > pos || key >= k_end) v = -INFINITY;
-        sv[i] = v;
-        mt = fmaxf(mt, v);
+        for (int i = 0; i < KT; ++i) {
+          const int key = kbase + i;
+          if (key > pos || key >= k_end) sv[i] = 0xff800000u;  // -inf
+        }
       }
-      const float m_new = fmaxf(m, mt);
-      // P_{j-1} . V_{j-1} must be complete before O is rescaled or P is overwritten
-      const bool got_o = (j == 0) || mbar_wait(o_done, (j - 1) & 1, err, kErrAttnWait);
-      if (!__all_sync(0xffffffffu, got_o)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // tcgen05.ld/st are warp-collective: the whole warp rescales when any of
-      // its rows needs it (factor 1 for the others)
-      const bool grow = (j > 0 && m_new > m && m != -INFINITY);
-      if (__any_sync(0xffffffffu, grow)) {
-        const float f = grow ? exp2f(m - m_new) : 1.f;
+      // tile max of the raw scores (scale > 0 commutes with max), 8 independent chains
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(sv[i]);
+#pragma unroll
+      for (int i = 8; i < KT; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sv[i]));
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale_log2;
+      const bool grow = mt > m + kLazyLog2;      // also true for the first finite max (m = -inf)
+      const bool rescale = grow && m != -INFINITY && j > 0;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // P_{j-1} . V_{j-1} must be complete before O is rescaled (o_done by tile parity:
+        // S_j complete implies P_{j-2} . V_{j-2} complete, so the parity is unambiguous)
+        const bool got_o = mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, err, kErrAttnWait);
+        if (!__all_sync(0xffffffffu, got_o)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float f = rescale ? ex2_approx(m - mt) : 1.f;
         l *= f;
         const uint32_t tO = tmem + lane_base + C::O_COL;
 #pragma unroll
@@ -297,33 +305,35 @@ __global__ void __launch_bounds__(192, 2)
         }
         tmem_wait_st();
       }
-      m = m_new;
-      // P = 2^(s - m) as bf16 into the SW128 K-major P tile; l accumulates
-      float rs = 0.f;
+      if (grow) m = mt;
+      // P = 2^(s * scale - m) as bf16 into the SW128 K-major P tile over K_j; l accumulates
+      const float mb = (m == -INFINITY) ? 0.f : m;  // fully masked row so far: every P is 0
+      float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ch = 0; ch < KT / 8; ++ch) {
         uint32_t pk[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float a = (m == -INFINITY) ? 0.f : exp2f(sv[ch * 8 + 2 * e] - m);
-          const float b = (m == -INFINITY) ? 0.f : exp2f(sv[ch * 8 + 2 * e + 1] - m);
-          rs += a + b;
+          const float a = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + 2 * e]), scale_log2, -mb));
+          const float b = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + 2 * e + 1]), scale_log2, -mb));
+          rs[e] += a + b;
           pk[e] = pack_bf16x2(a, b);
         }
         *reinterpret_cast<uint4*>(sKV + s * 2 * C::KV_BYTES + fa_sw<BM>(r, ch)) =
             make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
-      l += rs;
+      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[s]);
       if (lane == 0) FA_PROGRESS(4 + qd, 400 + j);
     }
     // ---- epilogue: O / l -> out
     const bool go = ok && n_tiles > 0 && !*abort_flag;
     if (__all_sync(0xffffffffu, go)) {
-      if (__all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, err, kErrAttnWait))) {
+      const int jl = n_tiles - 1;
+      if (__all_sync(0xffffffffu, mbar_wait(&o_done[jl & 1], (jl >> 1) & 1, err, kErrAttnWait))) {
         tc_fence_after();
         const float inv = (l > 0.f) ? 1.f / l : 0.f;
         const bool valid = gr < n_rows;
@@ -404,7 +414,8 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
     GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured = true;
   }
-  dim3 grid(n_work, Hkv);
+  GSB_CHECK(n_work < 65536, "attention_tc: too many work tiles");
+  dim3 grid(Hkv, n_work);
   kfn<<<grid, 192, C::SMEM, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
                                   block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
                                   q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),

@@ -375,11 +375,9 @@ class NativeGraniteSwitch:
         for idx, rows in ((dec, 16), (pre, pre_rows)):
             if not idx:
                 continue
-            ws, wr = [], []
-            for i in idx:
-                for r0 in range(0, q_lens[i] * g, rows):
-                    ws.append(i)
-                    wr.append(r0)
+            sub_q = [q_lens[i] for i in idx]
+            sw, wr = A.build_work(sub_q, g, rows, [kv_lens[i] for i in idx] if rows != 16 else None)
+            ws = [idx[t] for t in sw]
             n_ctas = len(ws) * self.num_kv
             max_kv = max(kv_lens[i] for i in idx)
             ns = A.choose_splits(n_ctas, max_kv) if rows == 16 else 1

@@ -10,14 +10,28 @@ from .._native import err_buffer, native
 NUM_SMS = 148
 
 
-def build_work(q_lens: list[int], group: int, rows_per_tile: int) -> tuple[list[int], list[int]]:
-    """(request, first row) per CTA tile; a request contributes ceil(q_len*G / rows) tiles."""
+def build_work(q_lens: list[int], group: int, rows_per_tile: int,
+               kv_lens: list[int] | None = None) -> tuple[list[int], list[int]]:
+    """(request, first row) per CTA tile; a request contributes ceil(q_len*G / rows) tiles.
+
+    With ``kv_lens`` the tiles are ordered by the number of keys they attend
+    (causal), heaviest first, so the last wave of CTAs is short.
+    """
     seqs, rows = [], []
     for i, ql in enumerate(q_lens):
         n = ql * group
         for r0 in range(0, n, rows_per_tile):
             seqs.append(i)
             rows.append(r0)
+    if kv_lens is not None and len(seqs) > 1:
+        def keys(t):
+            i, r0 = seqs[t], rows[t]
+            last = min(r0 + rows_per_tile, q_lens[i] * group) - 1
+            return min(kv_lens[i], kv_lens[i] - q_lens[i] + last // group + 1)
+
+        order = sorted(range(len(seqs)), key=keys, reverse=True)
+        seqs = [seqs[t] for t in order]
+        rows = [rows[t] for t in order]
     return seqs, rows
 
 

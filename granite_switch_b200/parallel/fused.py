@@ -29,6 +29,15 @@ from ..ops import gemm as G
 BARRIER_BUDGET_NS = 5_000_000_000
 
 
+def _multicast_supported(device: torch.device) -> bool:
+    """NVLink multicast (NVLS) objects can be created on this device."""
+    from torch._C._autograd import DeviceType
+    from torch._C._distributed_c10d import _SymmetricMemory
+
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    return bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, idx))
+
+
 class FusedTPComm:
     def __init__(self, group, device: torch.device, max_tokens: int, hidden: int):
         import torch.distributed as dist
@@ -45,7 +54,7 @@ class FusedTPComm:
         self.y.zero_()
         self.turn = 0
         self.y_handle = symm_mem.rendezvous(self.y, group)
-        self.mc = int(self.y_handle.multicast_ptr) if self.y_handle.has_multicast_support() else 0
+        self.mc = int(self.y_handle.multicast_ptr) if _multicast_supported(device) else 0
         self.pads = symm_mem.empty(64, dtype=torch.int32, device=device)
         self.pads.zero_()
         self.pad_handle = symm_mem.rendezvous(self.pads, group)
