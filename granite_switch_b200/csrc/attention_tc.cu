@@ -6,17 +6,21 @@
 //
 //   S_j  = Q . K_j^T        tcgen05.mma M=128 N=64 K=D, S_j in TMEM (2 buffers)
 //   P_j  = softmax rows      softmax warps: tcgen05.ld one S row per thread,
-//                            mask, running max/sum in registers, P_j -> smem
-//                            over the K_j tile that S_j consumed
-//   O   += P_j . V_j         tcgen05.mma M=128 N=D K=64, O in TMEM; V is read
-//                            straight from its [key][d] tile as an MN-major B
+//                            mask, running max/sum in registers, P_j (bf16,
+//                            two per column) tcgen05.st over S_j's columns
+//   O   += P_j . V_j         tcgen05.mma M=128 N=D K=64 with A = P_j read from
+//                            TMEM, O in TMEM; V is read straight from its
+//                            [key][d] tile as an MN-major B
 //
-// Warp roles (192 threads): warp 0 issues the K/V page boxes by TMA
-// (double-buffered), warp 1 owns TMEM and issues every MMA from one thread,
-// warps 2..5 run the softmax, rescale O in TMEM when a row maximum grows by
-// more than 2^8, and write the normalised output. Two CTAs share an SM, so one
-// CTA's softmax overlaps the other's MMAs; work tiles arrive heaviest first. S_{j+1} is issued before P_j . V_j so the tensor
-// core computes the next scores while the softmax of the current tile runs.
+// Warp roles (192 threads): warp 0 issues the K/V page boxes by TMA, warp 1
+// owns TMEM and issues every MMA from one thread, warps 2..5 run the softmax,
+// rescale O in TMEM when a row maximum grows by more than 2^8, and write the
+// normalised output. K and V have separate two-stage rings: a K stage is
+// released when S_j completes (P never touches shared memory), a V stage when
+// P_j . V_j completes, and K runs one tile ahead of V. S_{j+1} is issued
+// before P_j . V_j, so the tensor core computes the next scores while the
+// softmax of the current tile runs, and two CTAs share an SM so one CTA's
+// softmax overlaps the other's MMAs. Work tiles arrive heaviest first.
 // Every mbarrier wait is bounded; the error word reports a timeout.
 // (reference: attention comes from vLLM's backends, called at
 // src/granite_switch/vllm/decoder/lora/decoder.py:146-174.)
@@ -37,11 +41,6 @@ struct FaCfg {
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = KT * D * 2;      // one of K or V
   static constexpr int STAGES = 2;
-  // P_j is written over K_j (same size when BM == D): S_j has consumed K_j
-  // by the time the softmax writes P_j, and the stage is refilled only after
-  // P_j . V_j completes.
-  static constexpr int P_BYTES = BM * KT * 2;
-  static_assert(P_BYTES <= KV_BYTES, "P must fit in the K tile it replaces");
   static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + 512;
   static constexpr int TMEM_COLS = (2 * KT + D) <= 256 ? 256 : 512;  // S0 | S1 | O
   static constexpr int S_COL0 = 0, S_COL1 = KT, O_COL = 2 * KT;
@@ -56,39 +55,32 @@ __device__ __forceinline__ uint32_t fa_sw(int r, int ch) {
 template <int D, int KT_>
 __global__ void __launch_bounds__(192, 2)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                      const __nv_bfloat16* __restrict__ q, int64_t q_stride,
-                      const int32_t* __restrict__ block_table, int bt_stride,
-                      const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
-                      const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0, int Hq,
-                      int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out, int64_t out_stride,
-                      uint32_t* err, volatile int* dbg) {
+                             const __nv_bfloat16* __restrict__ q, int64_t q_stride,
+                             const int32_t* __restrict__ block_table, int bt_stride,
+                             const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
+                             const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0, int Hq,
+                             int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out, int64_t out_stride,
+                             uint32_t* err) {
   using C = FaCfg<D, KT_>;
   constexpr int KT = C::KT, BM = C::BM, PAGE = C::PAGE;
-  const bool report = (dbg != nullptr);
-  volatile int* my_dbg = report ? dbg + (blockIdx.y * gridDim.x + blockIdx.x) * 16 : nullptr;
-#define FA_PROGRESS(slot, code)            \
-  do {                                     \
-    if (report) {                          \
-      my_dbg[(slot)] = (code);             \
-      __threadfence_system();              \
-    }                                      \
-  } while (0)
+  static_assert(KT == 64, "the P store below writes 32 TMEM columns (64 keys)");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + C::Q_BYTES;                       // [STAGES][K | V]
-  uint64_t* kv_full = reinterpret_cast<uint64_t*>(sKV + C::STAGES * 2 * C::KV_BYTES);  // [2]
-  uint64_t* kv_empty = kv_full + 2;                     // [2]
-  uint64_t* s_full = kv_empty + 2;                      // [2]
-  uint64_t* s_empty = s_full + 2;                       // [2]
-  uint64_t* p_full = s_empty + 2;                       // [2] by tile parity
-  uint64_t* o_done = p_full + 2;                        // [2] by tile parity
-  uint64_t* q_ready = o_done + 2;                       // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
+  uint8_t* sK = sQ + C::Q_BYTES;                  // [2][KT x D]
+  uint8_t* sV = sK + 2 * C::KV_BYTES;             // [2][KT x D]
+  uint64_t* k_full = reinterpret_cast<uint64_t*>(sV + 2 * C::KV_BYTES);
+  uint64_t* k_empty = k_full + 2;
+  uint64_t* v_full = k_empty + 2;
+  uint64_t* v_empty = v_full + 2;
+  uint64_t* s_full = v_empty + 2;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kvh = blockIdx.x, w = blockIdx.y;  // KV heads fastest: the heaviest work tiles launch first
+  const int kvh = blockIdx.x, w = blockIdx.y;
   const int seq = work_seq[w];
   const int row0 = work_row0[w];
   const int G = Hq / Hkv;
@@ -104,27 +96,23 @@ __global__ void __launch_bounds__(192, 2)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
     }
-    mbar_init(q_ready, 1);
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
   }
   if (warp == 1) {
-    if (lane == 0) FA_PROGRESS(0, 1);
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
-    if (lane == 0) FA_PROGRESS(0, 2);
   }
-  // Q tile: every thread copies part of it (cp.async), then the proxy fence
-  // makes it visible to the tensor core.
   for (int c = threadIdx.x; c < BM * (D / 8); c += blockDim.x) {
     const int r = c / (D / 8), ch = c % (D / 8);
     const int gr = row0 + r;
@@ -144,39 +132,49 @@ __global__ void __launch_bounds__(192, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (threadIdx.x == 0) FA_PROGRESS(0, 3);
 
   if (warp == 0) {
-    // ---------------- K/V producer ----------------
-    if (lane == 0) {
+    // ---------------- K/V producer: K runs one tile ahead of V ----------------
+    if (lane == 0 && n_tiles > 0) {
       const int first_page = bt[0];
-      int issued = 0;
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j & 1;
-        if (*abort_flag || !mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, err, kErrAttnWait)) {
-          *abort_flag = 1;
-          break;
-        }
-        uint8_t* dK = sKV + s * 2 * C::KV_BYTES;
-        uint8_t* dV = dK + C::KV_BYTES;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * C::KV_BYTES);
+      auto load = [&](uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, int j) {
+        mbar_arrive_expect_tx(bar, C::KV_BYTES);
 #pragma unroll 1
         for (int p = 0; p < KT / PAGE; ++p) {
           const int key = j * KT + p * PAGE;
           const int page = (key < k_end) ? bt[key / PAGE] : first_page;
           const int row = (page * Hkv + kvh) * PAGE;
 #pragma unroll
-          for (int h = 0; h < D / 64; ++h) {
-            tma_load_2d(dK + h * (KT * 128) + p * PAGE * 128, &tm_k, &kv_full[s], h * 64, row);
-            tma_load_2d(dV + h * (KT * 128) + p * PAGE * 128, &tm_v, &kv_full[s], h * 64, row);
-          }
+          for (int h = 0; h < D / 64; ++h) tma_load_2d(dst + h * (KT * 128) + p * PAGE * 128, tm, bar, h * 64, row);
         }
-        issued = j + 1;
-        FA_PROGRESS(1, issued);
+      };
+      int k_issued = 0, v_issued = 0;
+      bool ok = true;
+      auto issue_k = [&](int j) {
+        const int s = j & 1;
+        if (*abort_flag || !mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, err, kErrAttnWait)) return false;
+        load(sK + s * C::KV_BYTES, &tm_k, &k_full[s], j);
+        k_issued = j + 1;
+        return true;
+      };
+      ok = issue_k(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles && !(ok = issue_k(j + 1))) break;
+        const int s = j & 1;
+        if (*abort_flag || !mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, err, kErrAttnWait)) {
+          ok = false;
+          break;
+        }
+        load(sV + s * C::KV_BYTES, &tm_v, &v_full[s], j);
+        v_issued = j + 1;
       }
-      if (*abort_flag) {
-        for (int j = (issued > 2 ? issued - 2 : 0); j < issued; ++j)
-          mbar_wait(&kv_full[j & 1], (j >> 1) & 1, err, kErrAttnWait);
+      if (!ok) {
+        *abort_flag = 1;
+        // drain this CTA's own copies still in flight before the CTA exits
+        for (int j = (k_issued > 2 ? k_issued - 2 : 0); j < k_issued; ++j)
+          mbar_wait(&k_full[j & 1], (j >> 1) & 1, err, kErrAttnWait);
+        for (int j = (v_issued > 2 ? v_issued - 2 : 0); j < v_issued; ++j)
+          mbar_wait(&v_full[j & 1], (j >> 1) & 1, err, kErrAttnWait);
       }
     }
   } else if (warp == 1) {
@@ -187,92 +185,80 @@ __global__ void __launch_bounds__(192, 2)
       const uint32_t q_addr = smem_u32(sQ);
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
-        if (*abort_flag || !mbar_wait(&kv_full[s], (j >> 1) & 1, err, kErrAttnWait)) return false;
-        if (!mbar_wait(&s_empty[s], ((j >> 1) & 1) ^ 1, err, kErrAttnWait)) return false;
+        if (*abort_flag || !mbar_wait(&k_full[s], (j >> 1) & 1, err, kErrAttnWait)) return false;
+        // S_j reuses the TMEM columns of S_{j-2} / P_{j-2}: P_{j-2} . V_{j-2} must be done
+        if (j >= 2 && !mbar_wait(&o_done[s], ((j - 2) >> 1) & 1, err, kErrAttnWait)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sKV + s * 2 * C::KV_BYTES);
+        const uint32_t k_addr = smem_u32(sK + s * C::KV_BYTES);
         const uint32_t tS = tmem + (s ? C::S_COL1 : C::S_COL0);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 0 + (kk & 3) * 32;
-          const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (BM * 128) + off);
-          const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * (KT * 128) + off);
+          const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32);
+          const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * (KT * 128) + (kk & 3) * 32);
           umma_bf16(tS, ad, bd, idesc_s, kk != 0);
         }
         umma_commit(&s_full[s]);
-        FA_PROGRESS(2, 100 + j);
+        umma_commit(&k_empty[s]);
         return true;
       };
       bool ok = issue_s(0);
       for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles) ok = issue_s(j + 1);
-        if (!ok) break;
-        // O += P_j . V_j once the softmax has written P_j (and rescaled O)
-        if (*abort_flag || !mbar_wait(&p_full[j & 1], (j >> 1) & 1, err, kErrAttnWait)) {
+        if (j + 1 < n_tiles && !(ok = issue_s(j + 1))) break;
+        const int s = j & 1;
+        if (*abort_flag || !mbar_wait(&p_full[s], (j >> 1) & 1, err, kErrAttnWait) ||
+            !mbar_wait(&v_full[s], (j >> 1) & 1, err, kErrAttnWait)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sKV + (j & 1) * 2 * C::KV_BYTES);  // P_j over K_j
-        const uint32_t v_addr = p_addr + C::KV_BYTES;
+        const uint32_t tP = tmem + (s ? C::S_COL1 : C::S_COL0);
+        const uint32_t v_addr = smem_u32(sV + s * C::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < KT / 16; ++kk) {
-          const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32);  // P: [KT/64][BM][64]
-          // V tile as MN-major B: d groups of 64 are KT*128 bytes apart,
-          // 8-key groups 1024 bytes apart; 16 keys per step = 2048 bytes
           const uint64_t bd = umma_desc_sw128_mn(v_addr + kk * 2048, KT * 128, 1024);
-          umma_bf16(tmem + C::O_COL, ad, bd, idesc_o, (j | kk) != 0);
+          umma_bf16_tmem_a(tmem + C::O_COL, tP + kk * 8, bd, idesc_o, (j | kk) != 0);
         }
-        umma_commit(&o_done[j & 1]);
-        umma_commit(&kv_empty[j & 1]);
-        FA_PROGRESS(3, 200 + j);
+        umma_commit(&o_done[s]);
+        umma_commit(&v_empty[s]);
       }
       if (!ok) *abort_flag = 1;
     }
   } else {
     // ---------------- softmax + epilogue (warps 2..5) ----------------
-    // Each thread owns one row. The running max m (log2 domain) is allowed to
-    // lag the true maximum by up to kLazyLog2: P = 2^(s - m) then stays below
-    // 2^kLazyLog2, which bf16 P and fp32 O / l represent exactly as well, and
-    // O in TMEM is rescaled only when some row's max grows by more than that.
-    // Without a rescale the warp never waits for the previous P.V.
+    // Each thread owns one row. The running max m (log2 domain) may lag the
+    // true maximum by up to kLazyLog2: P = 2^(s - m) then stays below
+    // 2^kLazyLog2, which bf16 P and fp32 O / l represent as well as P <= 1,
+    // and O in TMEM is rescaled only when some row's max grows by more than
+    // that. Without a rescale the warp never waits for the previous P.V.
     constexpr float kLazyLog2 = 8.f;
     const int qd = warp & 3;
-    const int r = qd * 32 + lane;                 // row within the tile
+    const int r = qd * 32 + lane;
     const int gr = row0 + r;
-    const int pos = ctx + gr / G;                 // absolute position of this row's query
+    const int pos = ctx + gr / G;
     const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j & 1;
       const bool got_s = !*abort_flag && mbar_wait(&s_full[s], (j >> 1) & 1, err, kErrAttnWait);
-      if (!__all_sync(0xffffffffu, got_s)) {  // warp-uniform: the tcgen05.ld below is warp-collective
+      if (!__all_sync(0xffffffffu, got_s)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      const uint32_t tS = tmem + lane_base + (s ? C::S_COL1 : C::S_COL0);
       uint32_t sv[KT];
-      {
-        const uint32_t tS = tmem + lane_base + (s ? C::S_COL1 : C::S_COL0);
 #pragma unroll
-        for (int c = 0; c < KT / 32; ++c) tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t(&)[32]>(sv[c * 32]));
-        tmem_wait_ld();
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[s]);
-      if (lane == 0) FA_PROGRESS(4 + qd, 300 + j);
-      // causal / key-range mask, only on tiles that cross this warp's diagonal or k_end
+      for (int c = 0; c < KT / 32; ++c) tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t(&)[32]>(sv[c * 32]));
+      tmem_wait_ld();
       const int kbase = j * KT;
       if (__any_sync(0xffffffffu, kbase + KT - 1 > pos || kbase + KT > k_end)) {
 #pragma unroll
         for (int i = 0; i < KT; ++i) {
           const int key = kbase + i;
-          if (key > pos || key >= k_end) sv[i] = 0xff800000u;  // -inf
+          if (key > pos || key >= k_end) sv[i] = 0xff800000u;
         }
       }
-      // tile max of the raw scores (scale > 0 commutes with max), 8 independent chains
       float mx[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(sv[i]);
@@ -280,11 +266,9 @@ __global__ void __launch_bounds__(192, 2)
       for (int i = 8; i < KT; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sv[i]));
       const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                              fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale_log2;
-      const bool grow = mt > m + kLazyLog2;      // also true for the first finite max (m = -inf)
+      const bool grow = mt > m + kLazyLog2;
       const bool rescale = grow && m != -INFINITY && j > 0;
       if (__any_sync(0xffffffffu, rescale)) {
-        // P_{j-1} . V_{j-1} must be complete before O is rescaled (o_done by tile parity:
-        // S_j complete implies P_{j-2} . V_{j-2} complete, so the parity is unambiguous)
         const bool got_o = mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, err, kErrAttnWait);
         if (!__all_sync(0xffffffffu, got_o)) {
           ok = false;
@@ -303,33 +287,25 @@ __global__ void __launch_bounds__(192, 2)
           for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * f);
           tmem_st32(tO + c * 32, rr);
         }
-        tmem_wait_st();
       }
       if (grow) m = mt;
-      // P = 2^(s * scale - m) as bf16 into the SW128 K-major P tile over K_j; l accumulates
-      const float mb = (m == -INFINITY) ? 0.f : m;  // fully masked row so far: every P is 0
+      const float mb = (m == -INFINITY) ? 0.f : m;
+      uint32_t pk[KT / 2];
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int ch = 0; ch < KT / 8; ++ch) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float a = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + 2 * e]), scale_log2, -mb));
-          const float b = ex2_approx(fmaf(__uint_as_float(sv[ch * 8 + 2 * e + 1]), scale_log2, -mb));
-          rs[e] += a + b;
-          pk[e] = pack_bf16x2(a, b);
-        }
-        *reinterpret_cast<uint4*>(sKV + s * 2 * C::KV_BYTES + fa_sw<BM>(r, ch)) =
-            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      for (int i = 0; i < KT / 2; ++i) {
+        const float a = ex2_approx(fmaf(__uint_as_float(sv[2 * i]), scale_log2, -mb));
+        const float b = ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), scale_log2, -mb));
+        rs[i & 3] += a + b;
+        pk[i] = pack_bf16x2(a, b);
       }
       l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
-      fence_proxy_async_smem();
+      tmem_st32(tS, pk);  // P_j over the first 32 columns of S_j
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[s]);
-      if (lane == 0) FA_PROGRESS(4 + qd, 400 + j);
     }
-    // ---- epilogue: O / l -> out
     const bool go = ok && n_tiles > 0 && !*abort_flag;
     if (__all_sync(0xffffffffu, go)) {
       const int jl = n_tiles - 1;
@@ -365,16 +341,12 @@ __global__ void __launch_bounds__(192, 2)
     }
     if (!ok) *abort_flag = 1;
   }
-
-  if (lane == 0) FA_PROGRESS(8 + warp, 500);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
-    if (lane == 0) FA_PROGRESS(0, 4);
   }
-#undef FA_PROGRESS
 }
 
 }  // namespace gsb
@@ -385,10 +357,7 @@ using namespace gsb;
 void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                               const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
                               const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t num_q_heads,
-                              double scale, const at::Tensor& out, const at::Tensor& err, int64_t dbg_ptr) {
-  // dbg_ptr: optional device-visible address of mapped host memory (>= 16 ints)
-  // where CTA (0, 0) records its progress; 0 disables reporting.
-  volatile int* dbg = reinterpret_cast<volatile int*>(dbg_ptr);
+                              double scale, const at::Tensor& out, const at::Tensor& err) {
   GSB_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16 &&
                 out.scalar_type() == at::kBFloat16,
             "attention_tc: bf16 tensors required");
@@ -408,20 +377,20 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
   CUtensorMap tk = make_tmap_bf16_2d(k_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   using C = FaCfg<128, 64>;
+  GSB_CHECK(n_work < 65536, "attention_tc: too many work tiles");
+  dim3 grid(Hkv, n_work);
   auto kfn = fa_prefill_kernel<128, 64>;
   static bool configured = false;
   if (!configured) {
     GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured = true;
   }
-  GSB_CHECK(n_work < 65536, "attention_tc: too many work tiles");
-  dim3 grid(Hkv, n_work);
   kfn<<<grid, 192, C::SMEM, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
                                   block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
                                   q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
                                   work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv,
                                   (float)(scale * 1.4426950408889634),
                                   reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
-                                  reinterpret_cast<uint32_t*>(err.data_ptr()), dbg);
+                                  reinterpret_cast<uint32_t*>(err.data_ptr()));
   GSB_CUDA_CHECK(cudaGetLastError());
 }

@@ -54,10 +54,10 @@ def paged_attention(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq,
 
 
 def prefill_attention_tc(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
-                         num_q_heads: int, scale: float, out, dbg_ptr: int = 0):
+                         num_q_heads: int, scale: float, out):
     """tcgen05 prefill attention; work tiles must be built with ``rows_per_tile=128``."""
     native().prefill_attention_tc(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
-                                  num_q_heads, float(scale), out, err_buffer(q.device), int(dbg_ptr))
+                                  num_q_heads, float(scale), out, err_buffer(q.device))
     return out
 
 
