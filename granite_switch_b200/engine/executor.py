@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import math
 
+import numpy as np
 import torch
 
 from ..routing.scan import route_flat
@@ -20,28 +21,82 @@ from .kv_cache import BLOCK_SIZE
 from .scheduler import SchedulerOutput
 
 
+def _req_tokens(r, upto: int) -> np.ndarray:
+    """int64 mirror of ``r.all_ids`` with at least ``upto`` valid entries (extended in place)."""
+    a, n = r._np_tok, r._np_tok_n
+    if a is None or a.shape[0] < upto:
+        cap = max(upto, len(r.prompt_ids) + r.sampling.max_tokens)
+        b = np.empty(cap, np.int64)
+        if a is not None and n:
+            b[:n] = a[:n]
+        a = r._np_tok = b
+    if n < upto:
+        a[n:upto] = r.all_ids[n:upto]
+        r._np_tok_n = upto
+    return a
+
+
+def _req_blocks(r) -> tuple[np.ndarray, int]:
+    """int32 mirror of ``r.block_ids`` (appended incrementally; rebuilt when the list is replaced)."""
+    src = r.block_ids
+    a = r._np_bt
+    n = r._np_bt_n if r._np_bt_src is src else 0
+    r._np_bt_src = src
+    ln = len(src)
+    if a is None or a.shape[0] < ln:
+        b = np.empty(max(ln, 64, 2 * (a.shape[0] if a is not None else 0)), np.int32)
+        if a is not None and n:
+            b[:n] = a[:n]
+        a = r._np_bt = b
+    if n < ln:
+        a[n:ln] = src[n:ln]
+    r._np_bt_n = ln
+    return a, ln
+
+
 class HostBatch:
-    """Flattened host-side description of one step."""
+    """Flattened host-side description of one step (numpy arrays).
+
+    ``ids``/``pos``/``slots`` are per token; ``starts`` (chunk offsets plus the
+    total), ``carry``, ``q_lens``, ``kv_lens`` per chunk; ``bt`` is the step's
+    block table ``[chunks, width]``; ``rows`` the flat rows that sample. Token
+    ids and block ids come from per-request numpy mirrors that grow with the
+    request, so packing costs a few vector operations per chunk instead of a
+    Python loop per token.
+    """
 
     def __init__(self, out: SchedulerOutput):
-        ids, pos, slots, starts, carry, kv_lens, rows, q_lens = [], [], [], [0], [], [], [], []
-        self.chunks = out.chunks
-        for c in out.chunks:
+        chunks = out.chunks
+        self.chunks = chunks
+        s = len(chunks)
+        start = np.fromiter((c.start for c in chunks), np.int64, s)
+        count = np.fromiter((c.num_tokens for c in chunks), np.int64, s)
+        cu = np.zeros(s + 1, np.int64)
+        np.cumsum(count, out=cu[1:])
+        t = int(cu[-1])
+        ids = np.empty(t, np.int64)
+        blocks = []
+        width = 1
+        for i, c in enumerate(chunks):
             r = c.req
-            toks = r.all_ids[c.start:c.start + c.num_tokens]
-            ids.extend(toks)
-            for p in range(c.start, c.start + c.num_tokens):
-                pos.append(p)
-                slots.append(r.block_ids[p // BLOCK_SIZE] * BLOCK_SIZE + p % BLOCK_SIZE)
-            starts.append(starts[-1] + c.num_tokens)
-            carry.append(r.carry)
-            kv_lens.append(c.start + c.num_tokens)
-            q_lens.append(c.num_tokens)
-            if c.needs_sample:
-                rows.append(starts[-1] - 1)
-        self.ids, self.pos, self.slots, self.starts = ids, pos, slots, starts
-        self.carry, self.kv_lens, self.rows, self.q_lens = carry, kv_lens, rows, q_lens
-        self.block_lists = [c.req.block_ids for c in out.chunks]
+            end = c.start + c.num_tokens
+            ids[cu[i]:cu[i + 1]] = _req_tokens(r, end)[c.start:end]
+            bl = _req_blocks(r)
+            blocks.append(bl)
+            width = max(width, bl[1])
+        bt = np.zeros((s, width), np.int32)
+        for i, (bl, ln) in enumerate(blocks):
+            bt[i, :ln] = bl[:ln]
+        seq_of = np.repeat(np.arange(s), count)
+        pos = np.arange(t, dtype=np.int64) - cu[:-1][seq_of] + start[seq_of]
+        slots = bt[seq_of, pos // BLOCK_SIZE].astype(np.int64) * BLOCK_SIZE + pos % BLOCK_SIZE
+        sample = np.fromiter((c.needs_sample for c in chunks), bool, s)
+        self.ids, self.pos, self.slots, self.bt = ids, pos, slots, bt
+        self.starts = cu
+        self.carry = np.fromiter((c.req.carry for c in chunks), np.int64, s)
+        self.q_lens = count.tolist()
+        self.kv_lens = (start + count).tolist()
+        self.rows = (cu[1:] - 1)[sample]
 
 
 class NativeExecutor:
@@ -65,6 +120,9 @@ class NativeExecutor:
         self.d_work = torch.empty(4, 4 * t + 4 * s, dtype=torch.int32, device=dev)
         self.h_work = torch.empty(4, 4 * t + 4 * s, dtype=torch.int32, **pin)
         self.d_tokens = torch.empty(s, dtype=torch.long, device=dev)
+        # numpy views of the pinned staging buffers (same memory)
+        self.np_i64, self.np_i32 = self.h_i64.numpy(), self.h_i32.numpy()
+        self.np_bt, self.np_rows, self.np_work = self.h_bt.numpy(), self.h_rows.numpy(), self.h_work.numpy()
         self.copy_event = torch.cuda.Event()
         self.h2d_event = torch.cuda.Event()
         self.h2d_pending = False
@@ -82,23 +140,23 @@ class NativeExecutor:
         # host staging (pinned): the previous step's async copies must have landed
         if self.h2d_pending:
             self.h2d_event.synchronize()
-        self.h_i64[:t] = torch.tensor(hb.ids, dtype=torch.long)
-        self.h_i64[t:2 * t] = torch.tensor(hb.pos, dtype=torch.long)
-        self.h_i64[2 * t:3 * t] = torch.tensor(hb.slots, dtype=torch.long)
-        self.h_i32[: s + 1] = torch.tensor(hb.starts, dtype=torch.int32)
-        self.h_i32[s + 1:2 * s + 1] = torch.tensor(hb.carry, dtype=torch.int32)
-        self.h_i32[2 * s + 1:3 * s + 1] = torch.tensor(hb.kv_lens, dtype=torch.int32)
-        width = max(len(b) for b in hb.block_lists)
-        bt = torch.zeros(s, width, dtype=torch.int32)
-        for i, bl in enumerate(hb.block_lists):
-            bt[i, : len(bl)] = torch.tensor(bl, dtype=torch.int32)
-        self.h_bt[:s, :width] = bt
+        i64, i32 = self.np_i64, self.np_i32
+        i64[:t] = hb.ids
+        i64[t:2 * t] = hb.pos
+        i64[2 * t:3 * t] = hb.slots
+        i32[: s + 1] = hb.starts
+        i32[s + 1:2 * s + 1] = hb.carry
+        i32[2 * s + 1:3 * s + 1] = hb.kv_lens
+        width = hb.bt.shape[1]
+        if width > self.max_blocks:
+            raise ValueError(f"block table width {width} exceeds max_model_len blocks {self.max_blocks}")
+        self.np_bt[:s, :width] = hb.bt
         nb = len(hb.rows)
-        self.h_rows[:nb] = torch.tensor(hb.rows, dtype=torch.long)
+        self.np_rows[:nb] = hb.rows
         plans_host = m.attention_plans(hb.q_lens, hb.kv_lens)
         for pi, (ws, wr, rows, ns) in enumerate(plans_host):
-            self.h_work[2 * pi, : len(ws)] = torch.tensor(ws, dtype=torch.int32)
-            self.h_work[2 * pi + 1, : len(wr)] = torch.tensor(wr, dtype=torch.int32)
+            self.np_work[2 * pi, : len(ws)] = ws
+            self.np_work[2 * pi + 1, : len(wr)] = wr
         # H2D (one copy per staging buffer)
         self.d_i64[: 3 * t].copy_(self.h_i64[: 3 * t], non_blocking=True)
         self.d_i32[: 3 * s + 1].copy_(self.h_i32[: 3 * s + 1], non_blocking=True)
@@ -130,7 +188,7 @@ class NativeExecutor:
         hb = HostBatch(out)
         batch = self._stage(hb)
         logits = self.model.forward(batch)
-        if not hb.rows or logits is None:
+        if not len(hb.rows) or logits is None:
             return hb, None
         return hb, self._gather_logits(logits)
 
@@ -189,23 +247,20 @@ class ReferenceExecutor:
 
         cfg = self.cfg
         hb = HostBatch(out)
-        ids = torch.tensor(hb.ids, dtype=torch.long)
+        ids = torch.from_numpy(hb.ids)
         if self.table is not None:
-            idx, _ = route_flat(ids, hb.starts, hb.carry, self.table)
+            idx, _ = route_flat(ids, hb.starts.tolist(), hb.carry.tolist(), self.table)
             lora_idx, _ = self.m.model.switch.split_indices(idx)
             lut = self.m.model.switch.control_to_substitute_lut
         else:
             lora_idx = torch.zeros_like(ids)
             lut = None
         mod = apply_token_exchange(lut, ids)
-        pos = torch.tensor(hb.pos, dtype=torch.long)
-        slots = torch.tensor(hb.slots, dtype=torch.long)
+        pos = torch.from_numpy(hb.pos)
+        slots = torch.from_numpy(hb.slots)
         h = self.m.model.embed_tokens(mod) * cfg.embedding_multiplier
         cos, sin = rope_cos_sin(pos.unsqueeze(0), cfg.head_dim_eff, cfg.rope_theta, h.dtype)
-        width = max(len(b) for b in hb.block_lists)
-        bt = torch.zeros(len(hb.block_lists), width, dtype=torch.int32)
-        for i, bl in enumerate(hb.block_lists):
-            bt[i, : len(bl)] = torch.tensor(bl, dtype=torch.int32)
+        bt = torch.from_numpy(hb.bt)
         blk, off = slots // BLOCK_SIZE, slots % BLOCK_SIZE
         for li, layer in enumerate(self.m.model.layers):
             att = layer.self_attn
@@ -219,9 +274,9 @@ class ReferenceExecutor:
             h = h + att.out(o.to(h.dtype).unsqueeze(0), lora_idx.unsqueeze(0))[0] * layer.residual_multiplier
             x = layer.post_attention_layernorm(h)
             h = h + layer.mlp(x.unsqueeze(0), lora_idx.unsqueeze(0))[0] * layer.residual_multiplier
-        if not hb.rows:
+        if not len(hb.rows):
             return hb, None
-        hf = self.m.model.norm(h[torch.tensor(hb.rows)])
+        hf = self.m.model.norm(h[torch.from_numpy(hb.rows)])
         return hb, self.m.lm_head(hf).float() / cfg.logits_scaling
 
 

@@ -12,6 +12,7 @@ import os
 import time
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 from ..config import GraniteSwitchConfig
@@ -48,21 +49,34 @@ class EngineStats:
 
 
 class HostRouter:
-    """Host copy of the routing rule, used to carry routing state across chunks."""
+    """Host copy of the routing rule, used to carry routing state across chunks.
+
+    Long chunks (prefill) are scanned with a vectorised lookup table; short
+    ones (decode) with a dict.
+    """
 
     def __init__(self, config: GraniteSwitchConfig):
         self.map = {}
+        self.lut = None
         if config.num_adapters > 0 and config.adapter_token_ids:
             tbl = expert_table(config.adapter_token_ids, config.num_adapters)
             for tok in config.adapter_token_ids:
                 self.map[tok] = int(tbl[tok])
+            self.lut = tbl.numpy().astype(np.int64)
 
-    def __call__(self, ids: list[int], carry: int) -> int:
+    def __call__(self, ids, carry: int) -> int:
         m = self.map
         if not m:
             return carry
+        if len(ids) > 32:
+            a = np.asarray(ids, dtype=np.int64)
+            lut = self.lut
+            inside = a < lut.shape[0]
+            e = np.where(inside, lut[np.where(inside, a, 0)], -1)
+            hit = np.flatnonzero(e >= 0)
+            return int(e[hit[-1]]) if hit.size else carry
         for t in reversed(ids):
-            e = m.get(t)
+            e = m.get(int(t))
             if e is not None:
                 return e
         return carry
@@ -123,7 +137,9 @@ class LLMEngine:
         j = 0
         for c in out.chunks:
             r = c.req
-            r.carry = self.router(r.all_ids[c.start:c.start + c.num_tokens], r.carry)
+            end = c.start + c.num_tokens
+            toks = r._np_tok[c.start:end] if r._np_tok_n >= end else r.all_ids[c.start:end]
+            r.carry = self.router(toks, r.carry)
             r.num_computed = c.start + c.num_tokens
             self.blocks.register_full_blocks(r)
             if not c.needs_sample:

@@ -52,10 +52,33 @@ class Request:
     finish_time: float | None = None
     finish_reason: str | None = None
     user_data: object = None
+    _all: list = field(default=None, init=False, repr=False, compare=False)
+    # host step-packing mirrors (numpy), maintained by engine.executor.HostBatch
+    _np_tok: object = field(default=None, init=False, repr=False, compare=False)
+    _np_tok_n: int = field(default=0, init=False, repr=False, compare=False)
+    _np_bt: object = field(default=None, init=False, repr=False, compare=False)
+    _np_bt_n: int = field(default=0, init=False, repr=False, compare=False)
+    _np_bt_src: object = field(default=None, init=False, repr=False, compare=False)
 
     @property
     def all_ids(self) -> list[int]:
-        return self.prompt_ids + self.output_ids
+        """Prompt followed by the generated tokens (a maintained list; do not mutate).
+
+        Kept incrementally instead of concatenating on every access: the engine
+        reads a slice of it for every scheduled chunk of every step.
+        """
+        a = self._all
+        p = len(self.prompt_ids)
+        if a is None or len(a) < p:
+            a = self._all = list(self.prompt_ids)
+        k = len(a) - p
+        n_out = len(self.output_ids)
+        if k != n_out:
+            if k > n_out:
+                del a[p + n_out:]
+            else:
+                a.extend(self.output_ids[k:])
+        return a
 
     @property
     def num_tokens(self) -> int:
