@@ -28,6 +28,7 @@
 #include <c10/cuda/CUDAStream.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace gsb {
 
@@ -99,8 +100,8 @@ struct GemmCfg {
 // Tile order: groups of 16 M-tiles, M fastest inside a group, so the CTAs that
 // run at the same time share weight tiles (B) in L2 and touch a bounded slice
 // of activations (A).
+template <int GM = 16>
 __device__ __forceinline__ void gemm_tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
-  constexpr int GM = 16;
   const int group = t / (GM * n_tiles);
   const int first_m = group * GM;
   const int gm = min(GM, m_tiles - first_m);
@@ -115,12 +116,19 @@ struct LoraTile {
   int blocks;
 };
 
+// `m_tile` counts 128-row tiles; a CTA pair covers `span` of them (1 or 2)
+// and runs the expand for the union of their adapters.
 template <bool SPLIT>
-__device__ __forceinline__ LoraTile lora_tile(const GemmLoraArgs& lora, int m_tile, int n0) {
+__device__ __forceinline__ LoraTile lora_tile(const GemmLoraArgs& lora, int m_tile, int n0, int span = 1,
+                                              int m_tiles128 = 0) {
   LoraTile lt{0, 0, 0, 0};
   if (!lora.enabled) return lt;
-  lt.amask = lora.tile_mask ? lora.tile_mask[m_tile]
-                            : ((lora.num_adapters >= 64) ? ~0ull : ((1ull << lora.num_adapters) - 1));
+  if (lora.tile_mask) {
+    lt.amask = lora.tile_mask[m_tile];
+    if (span == 2 && m_tile + 1 < m_tiles128) lt.amask |= lora.tile_mask[m_tile + 1];
+  } else {
+    lt.amask = (lora.num_adapters >= 64) ? ~0ull : ((1ull << lora.num_adapters) - 1);
+  }
   const int slice_cols = lora.num_adapters * lora.rank_blocks * 32;
   if (SPLIT) {
     lt.s_base1 = slice_cols;
@@ -132,6 +140,103 @@ __device__ __forceinline__ LoraTile lora_tile(const GemmLoraArgs& lora, int m_ti
   }
   lt.blocks = __popcll(lt.amask) * lora.rank_blocks;
   return lt;
+}
+
+// Drains one 128 x BN fp32 accumulator from TMEM and applies the epilogue.
+// Called by each of the four epilogue warps: the warp reads TMEM lanes
+// [32q, 32q + 32) (`tbase` already points there) and thread `lane` owns output
+// row `row`; columns n0 .. n0 + BN - 1.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmEpiArgs& epi, uint32_t tbase, int row, int M, int n0) {
+  if (EPI == kEpiSwiGLU) {
+    for (int c = 0; c < BN / 2; c += 32) {
+      uint32_t g[32], u[32];
+      tmem_ld32(tbase + c, g);
+      tmem_ld32(tbase + BN / 2 + c, u);
+      tmem_wait_ld();
+      if (row < M) {
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(epi.out) + (int64_t)row * epi.ldo + (n0 / 2) + c;
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          // gate/up pre-activations are rounded to bf16 first, as the
+          // unfused path stores them in bf16 before the activation
+          const float g0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * j])));
+          const float g1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * j + 1])));
+          const float u0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[2 * j])));
+          const float u1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[2 * j + 1])));
+          pk[j] = pack_bf16x2(__fdividef(g0, 1.f + __expf(-g0)) * u0, __fdividef(g1, 1.f + __expf(-g1)) * u1);
+        }
+        uint4* o4 = reinterpret_cast<uint4*>(o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+      }
+    }
+  } else {
+    int radapter = 0;
+    if (EPI == kEpiMaskAdapter && row < M) radapter = epi.row_adapter[row];
+    for (int c = 0; c < BN; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(tbase + c, r);
+      tmem_wait_ld();
+      if (row >= M) continue;
+      const int col = n0 + c;
+      if (EPI == kEpiF32) {
+        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(epi.out) + (int64_t)row * epi.ldo + col);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          o4[j] = make_float4(__uint_as_float(r[4 * j]) * epi.scale, __uint_as_float(r[4 * j + 1]) * epi.scale,
+                              __uint_as_float(r[4 * j + 2]) * epi.scale, __uint_as_float(r[4 * j + 3]) * epi.scale);
+      } else {
+        float v[32];
+        if (EPI == kEpiResAdd || (EPI == kEpiMultimemRed && epi.residual != nullptr)) {
+          const uint4* r4 = reinterpret_cast<const uint4*>(epi.residual + (int64_t)row * epi.ldr + col);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 w = r4[j];
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int tt = 0; tt < 4; ++tt) {
+              // the projection is rounded to bf16 before the residual add, as
+              // the unfused path materialises it in bf16
+              const float2 f = unpack_bf16x2(ww[tt]);
+              const float p0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * j + 2 * tt])));
+              const float p1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * j + 2 * tt + 1])));
+              v[8 * j + 2 * tt] = f.x + p0 * epi.scale;
+              v[8 * j + 2 * tt + 1] = f.y + p1 * epi.scale;
+            }
+          }
+        } else if (EPI == kEpiMultimemRed) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[j]))) * epi.scale;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * epi.scale;
+          if (EPI == kEpiMaskAdapter) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int a = ((col + j) / epi.mask_rank) % epi.mask_num_adapters + 1;
+              if (a != radapter) v[j] = 0.f;
+            }
+          }
+        }
+        uint4* o4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(epi.out) + (int64_t)row * epi.ldo + col);
+        if (EPI == kEpiMultimemRed) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            multimem_red_add_v4_bf16x2(o4 + j, pack_bf16x2(v[8 * j], v[8 * j + 1]),
+                                       pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                                       pack_bf16x2(v[8 * j + 4], v[8 * j + 5]),
+                                       pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            o4[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                               pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+        }
+      }
+    }
+  }
 }
 
 // Persistent: one CTA per SM walks tiles t = blockIdx.x, +gridDim.x, ...
@@ -317,95 +422,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
-      if (EPI == kEpiSwiGLU) {
-        for (int c = 0; c < BN / 2; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld32(tbase + c, g);
-          tmem_ld32(tbase + BN / 2 + c, u);
-          tmem_wait_ld();
-          if (row < M) {
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(epi.out) + (int64_t)row * epi.ldo + (n0 / 2) + c;
-            uint32_t pk[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              // gate/up pre-activations are rounded to bf16 first, as the
-              // unfused path stores them in bf16 before the activation
-              const float g0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * j])));
-              const float g1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * j + 1])));
-              const float u0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[2 * j])));
-              const float u1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[2 * j + 1])));
-              pk[j] = pack_bf16x2(__fdividef(g0, 1.f + __expf(-g0)) * u0, __fdividef(g1, 1.f + __expf(-g1)) * u1);
-            }
-            uint4* o4 = reinterpret_cast<uint4*>(o);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) o4[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-          }
-        }
-      } else {
-        int radapter = 0;
-        if (EPI == kEpiMaskAdapter && row < M) radapter = epi.row_adapter[row];
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c, r);
-          tmem_wait_ld();
-          if (row >= M) continue;
-          const int col = n0 + c;
-          if (EPI == kEpiF32) {
-            float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(epi.out) + (int64_t)row * epi.ldo + col);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              o4[j] = make_float4(__uint_as_float(r[4 * j]) * epi.scale, __uint_as_float(r[4 * j + 1]) * epi.scale,
-                                  __uint_as_float(r[4 * j + 2]) * epi.scale, __uint_as_float(r[4 * j + 3]) * epi.scale);
-          } else {
-            float v[32];
-            if (EPI == kEpiResAdd || (EPI == kEpiMultimemRed && epi.residual != nullptr)) {
-              const uint4* r4 = reinterpret_cast<const uint4*>(epi.residual + (int64_t)row * epi.ldr + col);
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const uint4 w = r4[j];
-                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int tt = 0; tt < 4; ++tt) {
-                  // the projection is rounded to bf16 before the residual add, as
-                  // the unfused path materialises it in bf16
-                  const float2 f = unpack_bf16x2(ww[tt]);
-                  const float p0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * j + 2 * tt])));
-                  const float p1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * j + 2 * tt + 1])));
-                  v[8 * j + 2 * tt] = f.x + p0 * epi.scale;
-                  v[8 * j + 2 * tt + 1] = f.y + p1 * epi.scale;
-                }
-              }
-            } else if (EPI == kEpiMultimemRed) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[j]))) * epi.scale;
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * epi.scale;
-              if (EPI == kEpiMaskAdapter) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                  const int a = ((col + j) / epi.mask_rank) % epi.mask_num_adapters + 1;
-                  if (a != radapter) v[j] = 0.f;
-                }
-              }
-            }
-            uint4* o4 = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(epi.out) + (int64_t)row * epi.ldo + col);
-            if (EPI == kEpiMultimemRed) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                multimem_red_add_v4_bf16x2(o4 + j, pack_bf16x2(v[8 * j], v[8 * j + 1]),
-                                           pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
-                                           pack_bf16x2(v[8 * j + 4], v[8 * j + 5]),
-                                           pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
-            } else {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                o4[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
-                                   pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
-            }
-          }
-        }
-      }
+      epilogue_tile<BN, EPI>(epi, tbase, row, M, n0);
       if (EPI == kEpiMultimemRed) __threadfence_system();  // this tile's reductions precede the next barrier
       // accumulator drained: hand the TMEM buffer back to the MMA warp
       tc_fence_before();
@@ -420,6 +437,249 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2): a cluster of two CTAs on neighbouring SMs
+// computes a 256 x 256 tile. Each CTA stages its own 128 rows of X and its own
+// 128 rows of W per K block; the leader CTA's MMA thread issues
+// tcgen05.mma.cta_group::2 over both CTAs' shared memory, and each CTA's
+// TMEM receives its 128 x 256 accumulator. Per SM this moves half the W bytes
+// of the single-CTA 128 x 256 tile through L2 and shared memory for the same
+// tensor work. Both CTAs load with plain (non-multicast) TMA copies whose
+// completion is counted on the leader's barrier; only the leader sets the
+// expected byte count, for both CTAs. MMA completion is signalled to both
+// CTAs' barriers by one commit with a two-CTA mask.
+// ---------------------------------------------------------------------------
+struct PairCfg {
+  static constexpr int BM = 128;                   // rows per CTA (tile: 256)
+  static constexpr int BN = 256;                   // tile columns (each CTA stages BN/2 rows of W)
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;      // 16 KB
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = 7;                 // 224 KB of the 227 KB a CTA may use
+  static constexpr int TMEM_COLS = 2 * BN;         // two 256-column accumulators = all 512 columns
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+template <int EPI, bool SPLIT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    switched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a,
+                              const __grid_constant__ CUtensorMap tm_b,
+                              const __grid_constant__ CUtensorMap tm_s,
+                              const __grid_constant__ CUtensorMap tm_lb, int M, int N, int K,
+                              GemmLoraArgs lora, GemmEpiArgs epi, uint32_t* err) {
+  using C = PairCfg;
+  constexpr int BN = C::BN;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);  // leader's are used
+  uint64_t* empty_bar = full_bar + C::STAGES;
+  uint64_t* tfull_bar = empty_bar + C::STAGES;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;          // [2], leader's are used
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int m_tiles128 = (M + C::BM - 1) / C::BM;
+  const int m_tiles = (M + 2 * C::BM - 1) / (2 * C::BM);
+  const int n_tiles = N / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int main_blocks = K / C::BK;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 8);  // one arrive per epilogue warp of both CTAs
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+    if (lora.enabled) {
+      tma_prefetch_desc(&tm_s);
+      tma_prefetch_desc(&tm_lb);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers are initialised before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t full_bar_leader = mapa_shared(smem_u32(full_bar), 0);
+  const uint32_t tempty_bar_leader = mapa_shared(smem_u32(tempty_bar), 0);
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      uint32_t kb = 0;
+      bool stop = false;
+      for (int t = cluster_id; t < num_tiles && !stop; t += num_clusters) {
+        int mt, nt;
+        gemm_tile_coords<8>(t, m_tiles, n_tiles, mt, nt);
+        const int m0 = mt * 2 * C::BM + (int)rank * C::BM;  // this CTA's X rows
+        const int n0 = nt * BN;
+        const LoraTile lt = lora_tile<SPLIT>(lora, 2 * mt, n0, 2, m_tiles128);
+        const int total = main_blocks + lt.blocks;
+        uint64_t rem = lt.amask;
+        int a_bit = 0, rb = 0;
+        for (int i = 0; i < total; ++i, ++kb) {
+          const int s = kb % C::STAGES;
+          const uint32_t ph = (kb / C::STAGES) & 1;
+          if (*abort_flag || !mbar_wait(&empty_bar[s], ph ^ 1, err, kErrGemmWait)) {
+            *abort_flag = 1;
+            stop = true;
+            break;
+          }
+          uint8_t* sa = smem + s * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          const uint32_t fb = full_bar_leader + s * 8;
+          if (i < main_blocks) {
+            if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * C::STAGE_BYTES);
+            tma_load_2d_pair(sa, &tm_a, fb, i * C::BK, m0);
+            tma_load_2d_pair(sb, &tm_b, fb, i * C::BK, n0 + (int)rank * (BN / 2));
+          } else {
+            if (rb == 0) a_bit = __ffsll((long long)rem) - 1;
+            const int kcol = a_bit * lora.rank_blocks * 32 + rb * 32;
+            constexpr int nsub = SPLIT ? 2 : 1;
+            // per CTA: nsub S tiles of 128 x 32, and BN/2 rows x 32 of packed B
+            if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * (nsub * (C::BM * 32 * 2) + (BN / 2) * 32 * 2));
+            tma_load_2d_pair(sa, &tm_s, fb, lt.s_base0 + kcol, m0);
+            if (SPLIT) {
+              tma_load_2d_pair(sa + C::BM * 64, &tm_s, fb, lt.s_base1 + kcol, m0);
+              // gate rows [n0 + 64r, +64) and up rows [n0 + 128 + 64r, +64): the
+              // two N = 128 pair MMAs each take 64 rows from either CTA
+              tma_load_2d_pair(sb, &tm_lb, fb, kcol, n0 + (int)rank * 64);
+              tma_load_2d_pair(sb + 64 * 64, &tm_lb, fb, kcol, n0 + BN / 2 + (int)rank * 64);
+            } else {
+              tma_load_2d_pair(sb, &tm_lb, fb, kcol, n0 + (int)rank * (BN / 2));
+            }
+            if (++rb == lora.rank_blocks) {
+              rb = 0;
+              rem &= rem - 1;
+            }
+          }
+        }
+      }
+      // every stage this CTA filled has been released by the pair MMA before
+      // the CTA may exit (the release arrives in this CTA's shared memory)
+      const uint32_t first = kb > (uint32_t)C::STAGES ? kb - C::STAGES : 0;
+      for (uint32_t j = first; j < kb && !*abort_flag; ++j)
+        if (!mbar_wait(&empty_bar[j % C::STAGES], (j / C::STAGES) & 1, err, kErrGemmWait)) *abort_flag = 1;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only) ----------------
+    if (leader && lane == 0) {
+      const uint32_t idesc_full = umma_idesc_bf16(256, BN);
+      const uint32_t idesc_half = umma_idesc_bf16(256, BN / 2);
+      uint32_t kb = 0;
+      int ltile = 0;
+      bool stop = false;
+      for (int t = cluster_id; t < num_tiles && !stop; t += num_clusters) {
+        int mt, nt;
+        gemm_tile_coords<8>(t, m_tiles, n_tiles, mt, nt);
+        const LoraTile lt = lora_tile<SPLIT>(lora, 2 * mt, nt * BN, 2, m_tiles128);
+        const int total = main_blocks + lt.blocks;
+        const int acc = ltile & 1;
+        if (*abort_flag || !mbar_wait(&tempty_bar[acc], ((ltile >> 1) & 1) ^ 1, err, kErrGemmWait)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tacc = tmem_base + acc * BN;
+        for (int i = 0; i < total; ++i, ++kb) {
+          const int s = kb % C::STAGES;
+          const uint32_t ph = (kb / C::STAGES) & 1;
+          if (*abort_flag || !mbar_wait(&full_bar[s], ph, err, kErrGemmWait)) {
+            *abort_flag = 1;
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+          const uint32_t sb = sa + C::A_BYTES;
+          if (i < main_blocks) {
+            const uint64_t ad = umma_desc_sw128(sa);
+            const uint64_t bd = umma_desc_sw128(sb);
+#pragma unroll
+            for (int kk = 0; kk < C::BK / 16; ++kk)
+              umma_bf16_pair(tacc, ad + 2 * kk, bd + 2 * kk, idesc_full, (i | kk) != 0);
+          } else if (SPLIT) {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const uint64_t ad = umma_desc_sw64(sa + u * C::BM * 64);
+              const uint64_t bd = umma_desc_sw64(sb + u * 64 * 64);
+#pragma unroll
+              for (int kk = 0; kk < 2; ++kk)
+                umma_bf16_pair(tacc + u * (BN / 2), ad + 2 * kk, bd + 2 * kk, idesc_half, 1);
+            }
+          } else {
+            const uint64_t ad = umma_desc_sw64(sa);
+            const uint64_t bd = umma_desc_sw64(sb);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) umma_bf16_pair(tacc, ad + 2 * kk, bd + 2 * kk, idesc_full, 1);
+          }
+          umma_commit_pair(&empty_bar[s], 0x3);
+        }
+        if (stop) break;
+        umma_commit_pair(&tfull_bar[acc], 0x3);
+        ++ltile;
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int q = warp & 3;
+    int ltile = 0;
+    for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+      int mt, nt;
+      gemm_tile_coords<8>(t, m_tiles, n_tiles, mt, nt);
+      const int acc = ltile & 1;
+      if (*abort_flag || !mbar_wait(&tfull_bar[acc], (ltile >> 1) & 1, err, kErrGemmWait)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = mt * 2 * C::BM + (int)rank * C::BM + q * 32 + lane;
+      const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
+      epilogue_tile<BN, EPI>(epi, tbase, row, M, nt * BN);
+      if (EPI == kEpiMultimemRed) __threadfence_system();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_bar_leader + acc * 8);
+      ++ltile;
+    }
+  }
+
+  if (*abort_flag) {
+    // error path: give copies that may still be in flight into this CTA's
+    // shared memory time to land before the CTA exits (bounded, ~1 ms)
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 1000000ull) {
+    }
+  }
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -452,6 +712,73 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   const int grid = std::min(tiles, num_sms_for_current_device());
   kfn<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, M, N, K, lora, epi, err);
   GSB_CUDA_CHECK(cudaGetLastError());
+}
+
+// Clusters of two that fit at once for the pair kernel (queried once per device).
+template <int EPI, bool SPLIT>
+static int pair_max_clusters() {
+  static int cached[64] = {0};
+  int dev = 0;
+  GSB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 64 && cached[dev]) return cached[dev];
+  auto kfn = switched_gemm_pair_kernel<EPI, SPLIT>;
+  GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::SMEM_BYTES));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 148, 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = PairCfg::SMEM_BYTES;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  GSB_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kfn, &cfg));
+  if (n <= 0) n = num_sms_for_current_device() / 2;
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+template <int EPI, bool SPLIT>
+static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ts,
+                             const CUtensorMap& tlb, int M, int N, int K, const GemmLoraArgs& lora,
+                             const GemmEpiArgs& epi, uint32_t* err, cudaStream_t stream) {
+  auto kfn = switched_gemm_pair_kernel<EPI, SPLIT>;
+  const int clusters = pair_max_clusters<EPI, SPLIT>();  // also sets the shared-memory attribute
+  const int tiles = (N / PairCfg::BN) * ((M + 255) / 256);
+  const int grid = 2 * std::min(tiles, clusters);
+  kfn<<<grid, 192, PairCfg::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, M, N, K, lora, epi, err);
+  GSB_CUDA_CHECK(cudaGetLastError());
+}
+
+static void dispatch_epi_pair(int epi_kind, const CUtensorMap& ta, const CUtensorMap& tb,
+                              const CUtensorMap& ts, const CUtensorMap& tlb, int M, int N, int K,
+                              const GemmLoraArgs& lora, const GemmEpiArgs& epi, uint32_t* err,
+                              cudaStream_t st) {
+  switch (epi_kind) {
+    case kEpiStore: launch_gemm_pair<kEpiStore, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
+    case kEpiResAdd: launch_gemm_pair<kEpiResAdd, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
+    case kEpiSwiGLU: launch_gemm_pair<kEpiSwiGLU, true>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
+    case kEpiMultimemRed: launch_gemm_pair<kEpiMultimemRed, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
+    default: GSB_CHECK(false, "no pair kernel for epilogue kind ", epi_kind);
+  }
+}
+
+// The pair kernel serves 256-wide tiles of large-M GEMMs: M >= the threshold
+// below (GSB_GEMM_PAIR_MIN_M, default 512; GSB_GEMM_PAIR=0 or a negative
+// threshold keeps every GEMM on the single-CTA kernel).
+static int g_pair_min_m = []() {
+  const char* off = getenv("GSB_GEMM_PAIR");
+  if (off != nullptr && off[0] == '0') return -1;
+  const char* v = getenv("GSB_GEMM_PAIR_MIN_M");
+  return v != nullptr ? atoi(v) : 512;
+}();
+
+static bool pair_enabled(int M, int bn, int epi_kind) {
+  if (g_pair_min_m < 0 || bn != 256 || M < g_pair_min_m) return false;
+  return epi_kind == kEpiStore || epi_kind == kEpiResAdd || epi_kind == kEpiSwiGLU || epi_kind == kEpiMultimemRed;
 }
 
 template <int BN>
@@ -500,7 +827,9 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
 
   CUtensorMap ta = make_tmap_bf16_2d(x.data_ptr(), M, K, x.stride(0), 64, 128,
                                      CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tb = make_tmap_bf16_2d(w.data_ptr(), N, K, w.stride(0), 64, (uint32_t)bn,
+  const bool pair = pair_enabled(M, (int)bn, (int)epi_kind);
+  // the pair kernel stages half of the 256-row W tile in each CTA
+  CUtensorMap tb = make_tmap_bf16_2d(w.data_ptr(), N, K, w.stride(0), 64, (uint32_t)(pair ? bn / 2 : bn),
                                      CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap ts = ta, tlb = tb;  // placeholders when LoRA is off
   GemmLoraArgs lora{};
@@ -516,7 +845,10 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     GSB_CHECK(num_adapters <= 64, "at most 64 adapters per module");
     ts = make_tmap_bf16_2d(S.data_ptr(), M, S.size(1), S.stride(0), 32, 128,
                            CU_TENSOR_MAP_SWIZZLE_64B);
-    tlb = make_tmap_bf16_2d(LB.data_ptr(), N, LB.size(1), LB.stride(0), 32, (uint32_t)bn,
+    // pair kernel: each CTA stages 128 of the tile's 256 rows of packed B, or
+    // (SwiGLU) 64 gate rows and 64 up rows
+    const uint32_t lb_rows = pair ? (epi_kind == kEpiSwiGLU ? 64u : 128u) : (uint32_t)bn;
+    tlb = make_tmap_bf16_2d(LB.data_ptr(), N, LB.size(1), LB.stride(0), 32, lb_rows,
                             CU_TENSOR_MAP_SWIZZLE_64B);
     lora.enabled = 1;
     lora.rank_blocks = (int)(rank / 32);
@@ -586,9 +918,21 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     GSB_CHECK(mask_rank > 0 && mask_num_adapters > 0, "mask_rank and mask_num_adapters required");
   }
   uint32_t* errp = reinterpret_cast<uint32_t*>(err.data_ptr());
+  if (pair) {
+    dispatch_epi_pair((int)epi_kind, ta, tb, ts, tlb, M, N, K, lora, epi, errp, stream);
+    return;
+  }
   switch (bn) {
     case 64: dispatch_epi<64>((int)epi_kind, ta, tb, ts, tlb, M, N, K, lora, epi, errp, stream); break;
     case 128: dispatch_epi<128>((int)epi_kind, ta, tb, ts, tlb, M, N, K, lora, epi, errp, stream); break;
     case 256: dispatch_epi<256>((int)epi_kind, ta, tb, ts, tlb, M, N, K, lora, epi, errp, stream); break;
   }
+}
+
+// Sets the smallest M served by the CTA-pair kernel (negative: never); returns
+// the previous value.
+int64_t gsb_gemm_pair_min_m(int64_t m) {
+  const int64_t old = gsb::g_pair_min_m;
+  gsb::g_pair_min_m = (int)m;
+  return old;
 }

@@ -15,6 +15,8 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
                        const c10::optional<at::Tensor>& row_adapter, int64_t mask_rank,
                        int64_t mask_num_adapters, const at::Tensor& err, int64_t mc_out);
 
+int64_t gsb_gemm_pair_min_m(int64_t m);
+
 void gsb_rmsnorm(const at::Tensor& x, const at::Tensor& w, const at::Tensor& out,
                  const c10::optional<at::Tensor>& rows, double eps);
 void gsb_embed(const at::Tensor& ids, const at::Tensor& table, const c10::optional<at::Tensor>& lut,

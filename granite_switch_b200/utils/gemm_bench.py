@@ -1,0 +1,139 @@
+"""Switched-LoRA GEMM microbenchmark (the kernel sweep of the benchmark configs).
+
+``python -m granite_switch_b200.utils.gemm_bench [--quick] [--pair-min-m M]``
+
+For every point (M tokens, N x K, rank r, number of adapters) the per-token
+adapter ids are drawn uniformly over the adapters, then an activation mask
+sends every token before a uniformly drawn invocation start to the base model
+(id 0), as activated LoRA does. Timed per point, with CUDA events after
+warm-up and an L2 flush (a 256 MB write) before every launch:
+
+* ``native``  - LoRA shrink + tcgen05 switched GEMM with the expand fused in
+  the mainloop (what a projection costs in the engine),
+* ``base``    - the same tcgen05 GEMM with no adapters,
+* ``cublas``  - ``torch.matmul`` of the base weight (the library bar).
+
+TFLOP/s count the base product only (2 M N K), so the three columns compare
+directly. One JSON line per point on stdout.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from .._native import check_errors, err_buffer, native
+from ..ops import gemm as G
+
+SHAPES = [(4096, 4096), (12800, 4096), (4096, 12800)]  # N x K
+MS = [16, 256, 4096]
+RANKS = [8, 32, 64]
+ADAPTERS = [1, 4, 12, 32]
+
+
+def _flush_buffer(dev):
+    return torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+
+def time_launches(fn, flush, iters=20, warmup=3) -> float:
+    """Median device time (ms) of ``fn`` over ``iters`` launches, L2 flushed before each."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def make_case(m, n, k, rank, na, dev, seed=0):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = (torch.randn(m, k, device=dev, generator=g)).bfloat16()
+    w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+    rp = (rank + 31) // 32 * 32  # the kernel pads ranks to multiples of 32
+    ids = torch.randint(1, na + 1, (m,), device=dev, generator=g, dtype=torch.int32)
+    start = int(torch.randint(0, m, (1,), generator=torch.Generator().manual_seed(seed)).item())
+    ids[:start] = 0  # activated LoRA: tokens before the invocation run the base weights
+    a_rows = (na * rp + 63) // 64 * 64
+    a_all = torch.zeros(a_rows, k, device=dev, dtype=torch.bfloat16)
+    a_all[: na * rp] = (torch.randn(na * rp, k, device=dev, generator=g) * 0.02).bfloat16()
+    lb = (torch.randn(n, na * rp, device=dev, generator=g) * 0.02).bfloat16()
+    tiles = (m + 127) // 128
+    mask = torch.zeros(tiles, dtype=torch.int64)
+    ids_h = ids.cpu()
+    for t in range(tiles):
+        bits = 0
+        for a in ids_h[t * 128:(t + 1) * 128].unique().tolist():
+            if a > 0:
+                bits |= 1 << (a - 1)
+        mask[t] = bits if bits < (1 << 63) else bits - (1 << 64)
+    return dict(x=x, w=w, ids=ids, a_all=a_all, lb=lb, mask=mask.to(dev), rank=rp, na=na)
+
+
+def run_point(m, n, k, rank, na, flush, dev, iters=20, compare_pair=False):
+    c = make_case(m, n, k, rank, na, dev)
+    x, w = c["x"], c["w"]
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    s = torch.empty(m, max(64, c["a_all"].shape[0]), dtype=torch.bfloat16, device=dev)[:, : c["a_all"].shape[0]]
+
+    def native_fn():
+        G.lora_shrink(x, c["a_all"], c["ids"], c["rank"], c["na"], out=s, tile_mask=c["mask"])
+        G.switched_gemm(x, w, out, s=s, lb=c["lb"], tile_mask=c["mask"], rank=c["rank"], num_adapters=c["na"],
+                        slice_bounds=[0, n])
+
+    def base_fn():
+        G.switched_gemm(x, w, out)
+
+    def cublas_fn():
+        torch.matmul(x, w.t(), out=out)
+
+    res = {}
+    fns = [("native", native_fn, None), ("base", base_fn, None), ("cublas", cublas_fn, None)]
+    if compare_pair:  # same point on the CTA-pair and the single-CTA kernel, interleaved
+        fns = [("native_pair", native_fn, 1), ("native_single", native_fn, -1), ("base_pair", base_fn, 1),
+               ("base_single", base_fn, -1), ("cublas", cublas_fn, None)]
+    nat = native()
+    for name, fn, pair in fns:
+        old = nat.gemm_pair_min_m(pair) if pair is not None else None
+        ms = time_launches(fn, flush, iters)
+        if old is not None:
+            nat.gemm_pair_min_m(old)
+        res[name] = dict(ms=round(ms, 4), tflops=round(2 * m * n * k / ms / 1e9, 1))
+    check_errors(x.device)
+    return res
+
+
+def main():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--quick", action="store_true", help="r=32, 12 adapters only")
+    p.add_argument("--ms", type=int, nargs="*", default=None)
+    p.add_argument("--pair-min-m", type=int, default=None, help="smallest M of the CTA-pair kernel (<0: off)")
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--compare-pair", action="store_true", help="time CTA-pair and single-CTA tiles side by side")
+    args = p.parse_args()
+    dev = torch.device("cuda", 0)
+    err_buffer(dev)
+    nat = native()
+    if args.pair_min_m is not None:
+        nat.gemm_pair_min_m(args.pair_min_m)
+    flush = _flush_buffer(dev)
+    ranks = [32] if args.quick else RANKS
+    adapters = [12] if args.quick else ADAPTERS
+    for m in args.ms or MS:
+        for n, k in SHAPES:
+            for r in ranks:
+                for na in adapters:
+                    res = run_point(m, n, k, r, na, flush, dev, args.iters, args.compare_pair)
+                    print(json.dumps(dict(m=m, n=n, k=k, rank=r, adapters=na, **res)), flush=True)
+
+
+if __name__ == "__main__":
+    main()

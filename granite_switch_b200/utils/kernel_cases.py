@@ -1,7 +1,7 @@
 """One launch of each native kernel on a representative shape, for profiler captures.
 
 ``python -m granite_switch_b200.utils.kernel_cases <case>`` with case in
-gemm, swiglu, decode_gemm, attn_prefill, attn_decode, rmsnorm, rope, embed,
+gemm, gemm_pair, swiglu, decode_gemm, attn_prefill, attn_decode, rmsnorm, rope, embed,
 routing, sample (or ``all``). Pair it with ``ncu -k regex:<kernel> -c 1``.
 """
 import sys
@@ -30,6 +30,10 @@ if want("gemm"):  # qkv-shape prefill GEMM with fused LoRA expand (12 adapters r
     tm = torch.full(((T + 127) // 128,), (1 << na) - 1, dtype=torch.int64, device=dev)
     s = G.lora_shrink(x, a_all, ra, r, na, tile_mask=tm)
     out = G.switched_gemm(x, w, s=s, lb=lb, tile_mask=tm, rank=r, num_adapters=na, slice_bounds=[0, 4096, 5120, 6144])
+if want("gemm_pair"):  # base GEMM on CTA-pair tiles (M >= 512 selects them)
+    x = torch.randn(T, H, device=dev).bfloat16()
+    w = (torch.randn(I, H, device=dev) * 0.02).bfloat16()
+    out = G.switched_gemm(x, w, bn=256)
 if want("swiglu"):
     x = torch.randn(T, H, device=dev).bfloat16()
     w = (torch.randn(2 * I, H, device=dev) * 0.02).bfloat16()

@@ -119,3 +119,115 @@ def test_swiglu_split_lora():
     ref = G.switched_gemm_reference(x, w, epi=G.EPI_SWIGLU, s=s, lb=lb, rank=rank,
                                     num_adapters=na, swiglu_tile=bn)
     _close(out, ref)
+
+
+def _tile_mask(row_adapter, m):
+    tiles = (m + 127) // 128
+    mask = torch.zeros(tiles, dtype=torch.int64, device="cuda")
+    for t in range(tiles):
+        bits = 0
+        for a in row_adapter[t * 128:(t + 1) * 128].unique().tolist():
+            if a > 0:
+                bits |= 1 << (a - 1)
+        mask[t] = bits
+    return mask
+
+
+class _PairMinM:
+    """Temporarily route GEMMs with M >= m to the CTA-pair kernel (m < 0: never)."""
+
+    def __init__(self, m):
+        self.m = m
+
+    def __enter__(self):
+        from granite_switch_b200._native import native
+
+        self.old = native().gemm_pair_min_m(self.m)
+
+    def __exit__(self, *a):
+        from granite_switch_b200._native import native
+
+        native().gemm_pair_min_m(self.old)
+
+
+@pytest.mark.parametrize("m", [256, 300, 513, 1000])
+def test_pair_store_and_resadd(m):
+    """CTA-pair (cta_group::2) tiles, including a pair whose second CTA is past M."""
+    from granite_switch_b200._native import check_errors
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(4)
+    n, k = 768, 512
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.05)
+    with _PairMinM(1):
+        out = G.switched_gemm(x, w, bn=256)
+        res = _rand(m, n)
+        res_copy = res.clone()
+        G.switched_gemm(x, w, res, epi=G.EPI_RESADD, residual=res, scale=0.22, bn=256)
+    torch.cuda.synchronize()
+    check_errors(x.device)
+    _close(out, G.switched_gemm_reference(x, w))
+    _close(res, G.switched_gemm_reference(x, w, epi=G.EPI_RESADD, residual=res_copy, scale=0.22))
+    with _PairMinM(-1):
+        single = G.switched_gemm(x, w, bn=256)
+    assert torch.equal(out, single), "pair and single-CTA tiles must agree bit for bit"
+
+
+@pytest.mark.parametrize("m", [384, 700])
+def test_pair_lora_expand(m):
+    from granite_switch_b200._native import check_errors
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(5)
+    k, na, rank = 256, 5, 32
+    bounds = [0, 512, 768, 1024]
+    n = bounds[-1]
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.05)
+    row_adapter = torch.randint(0, na + 1, (m,), device="cuda", dtype=torch.int32)
+    row_adapter[:128] = 0  # one all-base tile next to mixed tiles
+    cols = 3 * na * rank
+    s = _rand(m, cols, scale=0.5)
+    keep = ((torch.arange(cols, device="cuda") // rank) % na + 1).unsqueeze(0) == row_adapter.long().unsqueeze(1)
+    s = (s.float() * keep).to(torch.bfloat16)
+    lb = _rand(n, na * rank, scale=0.05)
+    mask = _tile_mask(row_adapter, m)
+    with _PairMinM(1):
+        out = G.switched_gemm(x, w, s=s, lb=lb, tile_mask=mask, rank=rank, num_adapters=na,
+                              slice_bounds=bounds, bn=256)
+    torch.cuda.synchronize()
+    check_errors(x.device)
+    ref = G.switched_gemm_reference(x, w, s=s, lb=lb, rank=rank, num_adapters=na, slice_bounds=bounds)
+    _close(out, ref)
+
+
+@pytest.mark.parametrize("m", [256, 650])
+def test_pair_swiglu_split_lora(m):
+    from granite_switch_b200._native import check_errors
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(6)
+    k, na, rank, bn = 256, 3, 64, 256
+    n = 1024
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.05)
+    row_adapter = torch.randint(0, na + 1, (m,), device="cuda", dtype=torch.int32)
+    s = _rand(m, 2 * na * rank, scale=0.5)
+    cols = torch.arange(2 * na * rank, device="cuda")
+    keep = ((cols // rank) % na + 1).unsqueeze(0) == row_adapter.long().unsqueeze(1)
+    s = (s.float() * keep).to(torch.bfloat16)
+    lb = _rand(n, na * rank, scale=0.05)
+    mask = _tile_mask(row_adapter, m)
+    with _PairMinM(1):
+        out = G.switched_gemm(x, w, epi=G.EPI_SWIGLU, s=s, lb=lb, tile_mask=mask, rank=rank,
+                              num_adapters=na, slice_bounds=[0, n], bn=bn)
+    torch.cuda.synchronize()
+    check_errors(x.device)
+    ref = G.switched_gemm_reference(x, w, epi=G.EPI_SWIGLU, s=s, lb=lb, rank=rank, num_adapters=na,
+                                    swiglu_tile=bn)
+    _close(out, ref)
+    with _PairMinM(-1):
+        single = G.switched_gemm(x, w, epi=G.EPI_SWIGLU, s=s, lb=lb, tile_mask=mask, rank=rank,
+                                 num_adapters=na, slice_bounds=[0, n], bn=bn)
+    _close(out, single, tol=1e-2)
