@@ -72,6 +72,8 @@ struct GemmEpiArgs {
   int mask_num_adapters;
   const uint64_t* skip_mask;   // kEpiMaskAdapter: adapters present per 128-row tile; tiles
                                // whose columns belong only to absent adapters are skipped
+  int diag;                    // pair kernel diagnostics (GSB_GEMM_DIAG): bit 0 skips the
+                               // epilogue stores, bit 1 re-reads K block 0 (L2-resident)
 };
 
 // A shrink tile is skipped when none of the adapters owning its columns has a
@@ -85,6 +87,10 @@ __device__ __forceinline__ bool shrink_tile_skipped(const GemmEpiArgs& epi, int 
   return (epi.skip_mask[mt] & need) == 0;
 }
 
+// Shared memory of the staged epilogue: two 4 KB buffers (32 rows x 64 bf16,
+// 128-byte swizzled) per epilogue warp.
+constexpr int kEpiStageBytes = 4 * 2 * 4096;
+
 template <int BN>
 struct GemmCfg {
   static constexpr int BM = 128;
@@ -94,7 +100,9 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN;        // two accumulator buffers
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STAGING_OFF = STAGES * STAGE_BYTES;   // epilogue staging (1024-aligned)
+  static constexpr int BAR_OFF = STAGING_OFF + kEpiStageBytes;
+  static constexpr int SMEM_BYTES = BAR_OFF + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 // Tile order: groups of 16 M-tiles, M fastest inside a group, so the CTAs that
@@ -239,6 +247,109 @@ __device__ __forceinline__ void epilogue_tile(const GemmEpiArgs& epi, uint32_t t
   }
 }
 
+// Epilogues whose bf16 output goes out through shared memory and TMA stores
+// (output tiles a multiple of 64 columns wide).
+__host__ __device__ constexpr bool epi_staged(int epi, int bn) {
+  return (epi == kEpiStore || epi == kEpiResAdd || epi == kEpiSwiGLU) && ((epi == kEpiSwiGLU ? bn / 2 : bn) % 64 == 0);
+}
+__device__ __forceinline__ uint32_t swz128(int row, int chunk) {
+  return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
+}
+
+// Staged epilogue of one 128 x BN accumulator, 64 output columns at a time.
+// Each warp owns 32 rows (TMEM lanes): thread `lane` converts its row's 64
+// values to bf16 (after SwiGLU, or adding the residual) and writes them as
+// eight 16-byte chunks into a swizzled 32 x 128-byte buffer; lane 0 then
+// stores the whole 32 x 64 box with one TMA store, which runs asynchronously
+// while the warp moves on to the next buffer. The residual (kEpiResAdd) is
+// read with coalesced 16-byte loads (eight threads per 128-byte row) through
+// the same buffer. Rows at or past M are dropped by the tensor map bounds.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile_staged(const GemmEpiArgs& epi, const CUtensorMap* tm_out,
+                                                     uint32_t tbase, int row0, int M, int n0,
+                                                     uint8_t* stage, int& sbuf) {
+  const int lane = threadIdx.x & 31;
+  constexpr int OUT_COLS = (EPI == kEpiSwiGLU) ? BN / 2 : BN;
+  const int out_col0 = (EPI == kEpiSwiGLU) ? n0 / 2 : n0;
+#pragma unroll 1
+  for (int c = 0; c < OUT_COLS; c += 64) {
+    uint8_t* buf = stage + sbuf * 4096;
+    // the TMA store that last used this buffer must have read it
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    uint32_t pk[32];  // 64 bf16 of this thread's row, chunk-major
+    if (EPI == kEpiSwiGLU) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t g[32], u[32];
+        tmem_ld32(tbase + c + 32 * h, g);
+        tmem_ld32(tbase + BN / 2 + c + 32 * h, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          // gate/up pre-activations are rounded to bf16 first, as the
+          // unfused path stores them in bf16 before the activation
+          const float g0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * j])));
+          const float g1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * j + 1])));
+          const float u0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[2 * j])));
+          const float u1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(u[2 * j + 1])));
+          pk[16 * h + j] = pack_bf16x2(__fdividef(g0, 1.f + __expf(-g0)) * u0, __fdividef(g1, 1.f + __expf(-g1)) * u1);
+        }
+      }
+    } else {
+      uint32_t r[64];
+      tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld32(tbase + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      if (EPI == kEpiResAdd) {
+        // coalesced residual read of the warp's 32 x 64 box into the buffer
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int rr = 4 * j + (lane >> 3), ch = lane & 7;
+          const int grow = row0 + rr;
+          uint4 v = make_uint4(0u, 0u, 0u, 0u);
+          if (grow < M)
+            v = *reinterpret_cast<const uint4*>(epi.residual + (int64_t)grow * epi.ldr + n0 + c + ch * 8);
+          *reinterpret_cast<uint4*>(buf + swz128(rr, ch)) = v;
+        }
+        __syncwarp();
+      }
+      tmem_wait_ld();
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        if (EPI == kEpiResAdd) {
+          const uint4 w = *reinterpret_cast<const uint4*>(buf + swz128(lane, ch));
+          const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            // the projection is rounded to bf16 before the residual add, as
+            // the unfused path materialises it in bf16
+            const float2 f = unpack_bf16x2(ww[t]);
+            const float p0 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * ch + 2 * t])));
+            const float p1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * ch + 2 * t + 1])));
+            pk[4 * ch + t] = pack_bf16x2(f.x + p0 * epi.scale, f.y + p1 * epi.scale);
+          }
+        } else {
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            pk[4 * ch + t] = pack_bf16x2(__uint_as_float(r[8 * ch + 2 * t]) * epi.scale,
+                                         __uint_as_float(r[8 * ch + 2 * t + 1]) * epi.scale);
+        }
+      }
+    }
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch)
+      *reinterpret_cast<uint4*>(buf + swz128(lane, ch)) =
+          make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && row0 < M) {
+      tma_store_2d(tm_out, buf, out_col0 + c, row0);
+      bulk_commit_group();
+    }
+    sbuf ^= 1;
+  }
+}
+
 // Persistent: one CTA per SM walks tiles t = blockIdx.x, +gridDim.x, ...
 // TMEM holds two accumulators so the epilogue of tile i overlaps the
 // mainloop of tile i+1.
@@ -247,13 +358,15 @@ __global__ void __launch_bounds__(192, 1)
     switched_gemm_kernel(const __grid_constant__ CUtensorMap tm_a,
                          const __grid_constant__ CUtensorMap tm_b,
                          const __grid_constant__ CUtensorMap tm_s,
-                         const __grid_constant__ CUtensorMap tm_lb, int M, int N, int K,
+                         const __grid_constant__ CUtensorMap tm_lb,
+                         const __grid_constant__ CUtensorMap tm_out, int M, int N, int K,
                          GemmLoraArgs lora, GemmEpiArgs epi, uint32_t* err) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* staging = smem + C::STAGING_OFF;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
   uint64_t* empty_bar = full_bar + C::STAGES;
   uint64_t* tfull_bar = empty_bar + C::STAGES;   // [2]
   uint64_t* tempty_bar = tfull_bar + 2;          // [2]
@@ -409,6 +522,7 @@ __global__ void __launch_bounds__(192, 1)
     // ---------------- epilogue (warps 2..5) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int ltile = 0;
+    int sbuf = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       int mt, nt;
       gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
@@ -422,7 +536,10 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
-      epilogue_tile<BN, EPI>(epi, tbase, row, M, n0);
+      if constexpr (epi_staged(EPI, BN))
+        epilogue_tile_staged<BN, EPI>(epi, &tm_out, tbase, m0 + q * 32, M, n0, staging + q * 8192, sbuf);
+      else
+        epilogue_tile<BN, EPI>(epi, tbase, row, M, n0);
       if (EPI == kEpiMultimemRed) __threadfence_system();  // this tile's reductions precede the next barrier
       // accumulator drained: hand the TMEM buffer back to the MMA warp
       tc_fence_before();
@@ -430,6 +547,7 @@ __global__ void __launch_bounds__(192, 1)
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       ++ltile;
     }
+    if (epi_staged(EPI, BN) && lane == 0) bulk_wait_group_all();  // stores done before the CTA exits
   }
 
   tc_fence_before();
@@ -460,9 +578,11 @@ struct PairCfg {
   static constexpr int A_BYTES = BM * BK * 2;      // 16 KB
   static constexpr int B_BYTES = (BN / 2) * BK * 2;  // 16 KB
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = 7;                 // 224 KB of the 227 KB a CTA may use
+  static constexpr int STAGES = 6;
   static constexpr int TMEM_COLS = 2 * BN;         // two 256-column accumulators = all 512 columns
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int STAGING_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = STAGING_OFF + kEpiStageBytes;
+  static constexpr int SMEM_BYTES = BAR_OFF + 1024 + 256;   // 225.25 KB of the 227 KB a CTA may use
 };
 
 template <int EPI, bool SPLIT>
@@ -470,14 +590,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     switched_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a,
                               const __grid_constant__ CUtensorMap tm_b,
                               const __grid_constant__ CUtensorMap tm_s,
-                              const __grid_constant__ CUtensorMap tm_lb, int M, int N, int K,
+                              const __grid_constant__ CUtensorMap tm_lb,
+                              const __grid_constant__ CUtensorMap tm_out, int M, int N, int K,
                               GemmLoraArgs lora, GemmEpiArgs epi, uint32_t* err) {
   using C = PairCfg;
   constexpr int BN = C::BN;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);  // leader's are used
+  uint8_t* staging = smem + C::STAGING_OFF;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);  // leader's are used
   uint64_t* empty_bar = full_bar + C::STAGES;
   uint64_t* tfull_bar = empty_bar + C::STAGES;   // [2]
   uint64_t* tempty_bar = tfull_bar + 2;          // [2], leader's are used
@@ -541,6 +663,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         const int total = main_blocks + lt.blocks;
         uint64_t rem = lt.amask;
         int a_bit = 0, rb = 0;
+        // The pair expands the union of both CTAs' adapters. With a tile mask,
+        // the shrink leaves S columns of adapters absent from a 128-row tile
+        // unwritten; for those the CTA loads S rows past M, which TMA fills
+        // with zeros (same byte count), so the other adapter's delta is exact.
+        const int own_tile = 2 * mt + (int)rank;
+        const uint64_t own_mask = (lora.tile_mask == nullptr) ? ~0ull
+                                  : (own_tile < m_tiles128 ? lora.tile_mask[own_tile] : 0ull);
+        const int zero_row = m_tiles128 * C::BM;  // first row of an all-out-of-bounds box
         for (int i = 0; i < total; ++i, ++kb) {
           const int s = kb % C::STAGES;
           const uint32_t ph = (kb / C::STAGES) & 1;
@@ -554,17 +684,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           const uint32_t fb = full_bar_leader + s * 8;
           if (i < main_blocks) {
             if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * C::STAGE_BYTES);
-            tma_load_2d_pair(sa, &tm_a, fb, i * C::BK, m0);
-            tma_load_2d_pair(sb, &tm_b, fb, i * C::BK, n0 + (int)rank * (BN / 2));
+            const int kx = (epi.diag & 2) ? 0 : i * C::BK;
+            tma_load_2d_pair(sa, &tm_a, fb, kx, m0);
+            tma_load_2d_pair(sb, &tm_b, fb, kx, n0 + (int)rank * (BN / 2));
           } else {
             if (rb == 0) a_bit = __ffsll((long long)rem) - 1;
             const int kcol = a_bit * lora.rank_blocks * 32 + rb * 32;
             constexpr int nsub = SPLIT ? 2 : 1;
             // per CTA: nsub S tiles of 128 x 32, and BN/2 rows x 32 of packed B
             if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * (nsub * (C::BM * 32 * 2) + (BN / 2) * 32 * 2));
-            tma_load_2d_pair(sa, &tm_s, fb, lt.s_base0 + kcol, m0);
+            const int ys = ((own_mask >> a_bit) & 1ull) ? m0 : zero_row;
+            tma_load_2d_pair(sa, &tm_s, fb, lt.s_base0 + kcol, ys);
             if (SPLIT) {
-              tma_load_2d_pair(sa + C::BM * 64, &tm_s, fb, lt.s_base1 + kcol, m0);
+              tma_load_2d_pair(sa + C::BM * 64, &tm_s, fb, lt.s_base1 + kcol, ys);
               // gate rows [n0 + 64r, +64) and up rows [n0 + 128 + 64r, +64): the
               // two N = 128 pair MMAs each take 64 rows from either CTA
               tma_load_2d_pair(sb, &tm_lb, fb, kcol, n0 + (int)rank * 64);
@@ -648,6 +780,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int q = warp & 3;
     int ltile = 0;
+    int sbuf = 0;
     for (int t = cluster_id; t < num_tiles; t += num_clusters) {
       int mt, nt;
       gemm_tile_coords<8>(t, m_tiles, n_tiles, mt, nt);
@@ -659,13 +792,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       tc_fence_after();
       const int row = mt * 2 * C::BM + (int)rank * C::BM + q * 32 + lane;
       const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
-      epilogue_tile<BN, EPI>(epi, tbase, row, M, nt * BN);
+      if (!(epi.diag & 1)) {
+        if constexpr (epi_staged(EPI, BN))
+          epilogue_tile_staged<BN, EPI>(epi, &tm_out, tbase, row - lane, M, nt * BN, staging + q * 8192, sbuf);
+        else
+          epilogue_tile<BN, EPI>(epi, tbase, row, M, nt * BN);
+      }
       if (EPI == kEpiMultimemRed) __threadfence_system();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_bar_leader + acc * 8);
       ++ltile;
     }
+    if (epi_staged(EPI, BN) && lane == 0) bulk_wait_group_all();
   }
 
   if (*abort_flag) {
@@ -699,7 +838,7 @@ static int num_sms_for_current_device() {
 
 template <int BN, int EPI, bool SPLIT>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ts,
-                        const CUtensorMap& tlb, int M, int N, int K, const GemmLoraArgs& lora,
+                        const CUtensorMap& tlb, const CUtensorMap& to, int M, int N, int K, const GemmLoraArgs& lora,
                         const GemmEpiArgs& epi, uint32_t* err, cudaStream_t stream) {
   using C = GemmCfg<BN>;
   auto kfn = switched_gemm_kernel<BN, EPI, SPLIT>;
@@ -710,7 +849,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   }
   const int tiles = (N / BN) * ((M + C::BM - 1) / C::BM);
   const int grid = std::min(tiles, num_sms_for_current_device());
-  kfn<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, M, N, K, lora, epi, err);
+  kfn<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err);
   GSB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -743,25 +882,27 @@ static int pair_max_clusters() {
 
 template <int EPI, bool SPLIT>
 static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ts,
-                             const CUtensorMap& tlb, int M, int N, int K, const GemmLoraArgs& lora,
+                             const CUtensorMap& tlb, const CUtensorMap& to, int M, int N, int K,
+                             const GemmLoraArgs& lora,
                              const GemmEpiArgs& epi, uint32_t* err, cudaStream_t stream) {
   auto kfn = switched_gemm_pair_kernel<EPI, SPLIT>;
   const int clusters = pair_max_clusters<EPI, SPLIT>();  // also sets the shared-memory attribute
   const int tiles = (N / PairCfg::BN) * ((M + 255) / 256);
   const int grid = 2 * std::min(tiles, clusters);
-  kfn<<<grid, 192, PairCfg::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, M, N, K, lora, epi, err);
+  kfn<<<grid, 192, PairCfg::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err);
   GSB_CUDA_CHECK(cudaGetLastError());
 }
 
 static void dispatch_epi_pair(int epi_kind, const CUtensorMap& ta, const CUtensorMap& tb,
-                              const CUtensorMap& ts, const CUtensorMap& tlb, int M, int N, int K,
+                              const CUtensorMap& ts, const CUtensorMap& tlb, const CUtensorMap& to,
+                              int M, int N, int K,
                               const GemmLoraArgs& lora, const GemmEpiArgs& epi, uint32_t* err,
                               cudaStream_t st) {
   switch (epi_kind) {
-    case kEpiStore: launch_gemm_pair<kEpiStore, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
-    case kEpiResAdd: launch_gemm_pair<kEpiResAdd, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
-    case kEpiSwiGLU: launch_gemm_pair<kEpiSwiGLU, true>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
-    case kEpiMultimemRed: launch_gemm_pair<kEpiMultimemRed, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
+    case kEpiStore: launch_gemm_pair<kEpiStore, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
+    case kEpiResAdd: launch_gemm_pair<kEpiResAdd, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
+    case kEpiSwiGLU: launch_gemm_pair<kEpiSwiGLU, true>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
+    case kEpiMultimemRed: launch_gemm_pair<kEpiMultimemRed, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
     default: GSB_CHECK(false, "no pair kernel for epilogue kind ", epi_kind);
   }
 }
@@ -783,16 +924,17 @@ static bool pair_enabled(int M, int bn, int epi_kind) {
 
 template <int BN>
 static void dispatch_epi(int epi_kind, const CUtensorMap& ta, const CUtensorMap& tb,
-                         const CUtensorMap& ts, const CUtensorMap& tlb, int M, int N, int K,
+                         const CUtensorMap& ts, const CUtensorMap& tlb, const CUtensorMap& to,
+                         int M, int N, int K,
                          const GemmLoraArgs& lora, const GemmEpiArgs& epi, uint32_t* err,
                          cudaStream_t st) {
   switch (epi_kind) {
-    case kEpiStore: launch_gemm<BN, kEpiStore, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
-    case kEpiResAdd: launch_gemm<BN, kEpiResAdd, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
-    case kEpiSwiGLU: launch_gemm<BN, kEpiSwiGLU, true>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
-    case kEpiMaskAdapter: launch_gemm<BN, kEpiMaskAdapter, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
-    case kEpiF32: launch_gemm<BN, kEpiF32, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
-    case kEpiMultimemRed: launch_gemm<BN, kEpiMultimemRed, false>(ta, tb, ts, tlb, M, N, K, lora, epi, err, st); break;
+    case kEpiStore: launch_gemm<BN, kEpiStore, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
+    case kEpiResAdd: launch_gemm<BN, kEpiResAdd, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
+    case kEpiSwiGLU: launch_gemm<BN, kEpiSwiGLU, true>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
+    case kEpiMaskAdapter: launch_gemm<BN, kEpiMaskAdapter, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
+    case kEpiF32: launch_gemm<BN, kEpiF32, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
+    case kEpiMultimemRed: launch_gemm<BN, kEpiMultimemRed, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
     default: GSB_CHECK(false, "unknown epilogue kind ", epi_kind);
   }
 }
@@ -871,6 +1013,11 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     }
   }
   GemmEpiArgs epi{};
+  static const int diag = []() {
+    const char* v = getenv("GSB_GEMM_DIAG");
+    return v != nullptr ? atoi(v) : 0;
+  }();
+  epi.diag = diag;
   epi.out = (epi_kind == kEpiMultimemRed && mc_out != 0) ? reinterpret_cast<void*>(mc_out) : out.data_ptr();
   epi.ldo = out.stride(0);
   epi.scale = (float)scale;
@@ -917,15 +1064,19 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     }
     GSB_CHECK(mask_rank > 0 && mask_num_adapters > 0, "mask_rank and mask_num_adapters required");
   }
+  // staged epilogues store 32-row x 64-column boxes of the bf16 output by TMA
+  CUtensorMap to = ta;
+  if (epi_staged((int)epi_kind, pair ? 256 : (int)bn))
+    to = make_tmap_bf16_2d(out.data_ptr(), M, out.size(1), out.stride(0), 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   uint32_t* errp = reinterpret_cast<uint32_t*>(err.data_ptr());
   if (pair) {
-    dispatch_epi_pair((int)epi_kind, ta, tb, ts, tlb, M, N, K, lora, epi, errp, stream);
+    dispatch_epi_pair((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, errp, stream);
     return;
   }
   switch (bn) {
-    case 64: dispatch_epi<64>((int)epi_kind, ta, tb, ts, tlb, M, N, K, lora, epi, errp, stream); break;
-    case 128: dispatch_epi<128>((int)epi_kind, ta, tb, ts, tlb, M, N, K, lora, epi, errp, stream); break;
-    case 256: dispatch_epi<256>((int)epi_kind, ta, tb, ts, tlb, M, N, K, lora, epi, errp, stream); break;
+    case 64: dispatch_epi<64>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, errp, stream); break;
+    case 128: dispatch_epi<128>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, errp, stream); break;
+    case 256: dispatch_epi<256>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, errp, stream); break;
   }
 }
 

@@ -1,7 +1,7 @@
 """One launch of each native kernel on a representative shape, for profiler captures.
 
 ``python -m granite_switch_b200.utils.kernel_cases <case>`` with case in
-gemm, gemm_pair, swiglu, decode_gemm, attn_prefill, attn_decode, rmsnorm, rope, embed,
+gemm, gemm_pair, gemm_single, cublas, swiglu, decode_gemm, attn_prefill, attn_decode, rmsnorm, rope, embed,
 routing, sample (or ``all``). Pair it with ``ncu -k regex:<kernel> -c 1``.
 """
 import sys
@@ -34,6 +34,15 @@ if want("gemm_pair"):  # base GEMM on CTA-pair tiles (M >= 512 selects them)
     x = torch.randn(T, H, device=dev).bfloat16()
     w = (torch.randn(I, H, device=dev) * 0.02).bfloat16()
     out = G.switched_gemm(x, w, bn=256)
+if want("gemm_single"):  # the same GEMM on single-CTA 128x256 tiles
+    native().gemm_pair_min_m(-1)
+    x = torch.randn(T, H, device=dev).bfloat16()
+    w = (torch.randn(I, H, device=dev) * 0.02).bfloat16()
+    out = G.switched_gemm(x, w, bn=256)
+if want("cublas"):  # library bar for the same shape (torch.matmul -> cuBLAS)
+    x = torch.randn(T, H, device=dev).bfloat16()
+    w = (torch.randn(I, H, device=dev) * 0.02).bfloat16()
+    out = torch.matmul(x, w.t())
 if want("swiglu"):
     x = torch.randn(T, H, device=dev).bfloat16()
     w = (torch.randn(2 * I, H, device=dev) * 0.02).bfloat16()

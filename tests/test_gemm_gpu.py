@@ -231,3 +231,102 @@ def test_pair_swiglu_split_lora(m):
         single = G.switched_gemm(x, w, epi=G.EPI_SWIGLU, s=s, lb=lb, tile_mask=mask, rank=rank,
                                  num_adapters=na, slice_bounds=[0, n], bn=bn)
     _close(out, single, tol=1e-2)
+
+
+@pytest.mark.parametrize("pair", [1, -1])
+def test_many_tiles_per_cta(pair):
+    """Enough tiles that every CTA drains several accumulators through its staging buffers."""
+    from granite_switch_b200._native import check_errors
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(7)
+    m, n, k = 2304, 2048, 256
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.05)
+    with _PairMinM(pair):
+        out = G.switched_gemm(x, w, bn=256)
+        res = _rand(m, n)
+        res_copy = res.clone()
+        G.switched_gemm(x, w, res, epi=G.EPI_RESADD, residual=res, scale=0.5, bn=256)
+        wg = _rand(2 * n, k, scale=0.05)
+        act = G.switched_gemm(x, wg, epi=G.EPI_SWIGLU, bn=256)
+    torch.cuda.synchronize()
+    check_errors(x.device)
+    _close(out, G.switched_gemm_reference(x, w))
+    _close(res, G.switched_gemm_reference(x, w, epi=G.EPI_RESADD, residual=res_copy, scale=0.5))
+    _close(act, G.switched_gemm_reference(x, wg, epi=G.EPI_SWIGLU, swiglu_tile=256))
+
+
+@pytest.mark.parametrize("pair", [1, -1])
+@pytest.mark.parametrize("m", [600, 1100])
+def test_swiglu_lora_engine_layout(pair, m):
+    """gate/up as the engine runs it: rank 32 (one LoRA K block), S a strided view of a wider
+    buffer, base-only tiles before the adapter rows."""
+    from granite_switch_b200._native import check_errors
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(8)
+    k, na, rank, bn, n = 256, 3, 32, 256, 1024
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.05)
+    row_adapter = torch.zeros(m, device="cuda", dtype=torch.int32)
+    row_adapter[m // 2:] = torch.randint(0, na + 1, (m - m // 2,), device="cuda", dtype=torch.int32)
+    cols = 2 * na * rank
+    s_buf = torch.zeros(m, 320, device="cuda", dtype=torch.bfloat16)
+    s = s_buf[:, :cols]
+    sv = _rand(m, cols, scale=0.5)
+    keep = ((torch.arange(cols, device="cuda") // rank) % na + 1).unsqueeze(0) == row_adapter.long().unsqueeze(1)
+    s.copy_((sv.float() * keep).to(torch.bfloat16))
+    lb = _rand(n, na * rank, scale=0.05)
+    mask = _tile_mask(row_adapter, m)
+    with _PairMinM(pair):
+        out = G.switched_gemm(x, w, epi=G.EPI_SWIGLU, s=s, lb=lb, tile_mask=mask, rank=rank,
+                              num_adapters=na, slice_bounds=[0, n], bn=bn)
+    torch.cuda.synchronize()
+    check_errors(x.device)
+    ref = G.switched_gemm_reference(x, w, epi=G.EPI_SWIGLU, s=s.contiguous(), lb=lb, rank=rank,
+                                    num_adapters=na, swiglu_tile=bn)
+    _close(out, ref)
+
+
+@pytest.mark.parametrize("epi", ["store", "swiglu"])
+def test_pair_expand_with_tile_restricted_shrink(epi):
+    """The tile-restricted shrink leaves S columns of absent adapters unwritten (NaN here);
+    a pair whose two 128-row tiles hold different adapters must not read them."""
+    from granite_switch_b200._native import check_errors
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(9)
+    m, k, na, rank = 700, 256, 3, 32
+    n = 1024
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.05)
+    row_adapter = torch.zeros(m, device="cuda", dtype=torch.int32)
+    row_adapter[128:256] = 1          # tile 1: adapter 1 only (its pair partner, tile 0, is base)
+    row_adapter[256:384] = 2          # tiles 2 / 3 hold different adapters
+    row_adapter[400:500] = 3
+    row_adapter[640:] = 2             # a partial last tile
+    mask = _tile_mask(row_adapter, m)
+    slices = 2 if epi == "swiglu" else 1
+    a_rows = (slices * na * rank + 63) // 64 * 64
+    a_all = torch.zeros(a_rows, k, device="cuda", dtype=torch.bfloat16)
+    a_all[: slices * na * rank] = _rand(slices * na * rank, k, scale=0.05)
+    s = torch.full((m, a_rows), float("nan"), device="cuda", dtype=torch.bfloat16)
+    G.lora_shrink(x, a_all, row_adapter, rank, na, out=s, tile_mask=mask)
+    s_full = G.lora_shrink(x, a_all, row_adapter, rank, na)
+    lb = _rand(n, na * rank, scale=0.05)
+    kw = dict(s=s, lb=lb, tile_mask=mask, rank=rank, num_adapters=na, bn=256)
+    with _PairMinM(1):
+        if epi == "swiglu":
+            out = G.switched_gemm(x, w, epi=G.EPI_SWIGLU, slice_bounds=[0, n], **kw)
+        else:
+            out = G.switched_gemm(x, w, slice_bounds=[0, n], **kw)
+    torch.cuda.synchronize()
+    check_errors(x.device)
+    if epi == "swiglu":
+        ref = G.switched_gemm_reference(x, w, epi=G.EPI_SWIGLU, s=s_full, lb=lb, rank=rank, num_adapters=na,
+                                        swiglu_tile=256)
+    else:
+        ref = G.switched_gemm_reference(x, w, s=s_full, lb=lb, rank=rank, num_adapters=na, slice_bounds=[0, n])
+    assert not torch.isnan(out.float()).any()
+    _close(out, ref)
