@@ -250,7 +250,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmEpiArgs& epi, uint32_t t
 // Epilogues whose bf16 output goes out through shared memory and TMA stores
 // (output tiles a multiple of 64 columns wide).
 __host__ __device__ constexpr bool epi_staged(int epi, int bn) {
-  return (epi == kEpiStore || epi == kEpiResAdd || epi == kEpiSwiGLU) && ((epi == kEpiSwiGLU ? bn / 2 : bn) % 64 == 0);
+  return (epi == kEpiStore || epi == kEpiResAdd || epi == kEpiSwiGLU || epi == kEpiMultimemRed) &&
+         ((epi == kEpiSwiGLU ? bn / 2 : bn) % 64 == 0);
+}
+// Staged epilogues whose output leaves by TMA store (the multimem one leaves by
+// row-contiguous multimem reductions instead).
+__host__ __device__ constexpr bool epi_tma_store(int epi, int bn) {
+  return epi_staged(epi, bn) && epi != kEpiMultimemRed;
 }
 __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4));
@@ -300,7 +306,8 @@ __device__ __forceinline__ void epilogue_tile_staged(const GemmEpiArgs& epi, con
       uint32_t r[64];
       tmem_ld32(tbase + c, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
       tmem_ld32(tbase + c + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-      if (EPI == kEpiResAdd) {
+      const bool has_res = (EPI == kEpiResAdd) || (EPI == kEpiMultimemRed && epi.residual != nullptr);
+      if (has_res) {
         // coalesced residual read of the warp's 32 x 64 box into the buffer
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -316,7 +323,7 @@ __device__ __forceinline__ void epilogue_tile_staged(const GemmEpiArgs& epi, con
       tmem_wait_ld();
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
-        if (EPI == kEpiResAdd) {
+        if (has_res) {
           const uint4 w = *reinterpret_cast<const uint4*>(buf + swz128(lane, ch));
           const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -328,6 +335,13 @@ __device__ __forceinline__ void epilogue_tile_staged(const GemmEpiArgs& epi, con
             const float p1 = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * ch + 2 * t + 1])));
             pk[4 * ch + t] = pack_bf16x2(f.x + p0 * epi.scale, f.y + p1 * epi.scale);
           }
+        } else if (EPI == kEpiMultimemRed) {
+          // partial projection rounded to bf16 before scaling, as the unfused path
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            pk[4 * ch + t] =
+                pack_bf16x2(__bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * ch + 2 * t]))) * epi.scale,
+                            __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[8 * ch + 2 * t + 1]))) * epi.scale);
         } else {
 #pragma unroll
           for (int t = 0; t < 4; ++t)
@@ -340,11 +354,28 @@ __device__ __forceinline__ void epilogue_tile_staged(const GemmEpiArgs& epi, con
     for (int ch = 0; ch < 8; ++ch)
       *reinterpret_cast<uint4*>(buf + swz128(lane, ch)) =
           make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0 && row0 < M) {
-      tma_store_2d(tm_out, buf, out_col0 + c, row0);
-      bulk_commit_group();
+    if (EPI == kEpiMultimemRed) {
+      // read the box back row-contiguously (eight lanes per 128-byte row, four
+      // rows per instruction) and add it into every rank's copy through the
+      // multicast address: full-line NVLink transfers instead of 16-byte ones
+      __syncwarp();
+      __nv_bfloat16* mc = reinterpret_cast<__nv_bfloat16*>(epi.out);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int rr = 4 * j + (lane >> 3), ch = lane & 7;
+        if (row0 + rr < M) {
+          const uint4 v = *reinterpret_cast<const uint4*>(buf + swz128(rr, ch));
+          multimem_red_add_v4_bf16x2(mc + (int64_t)(row0 + rr) * epi.ldo + out_col0 + c + ch * 8, v.x, v.y, v.z, v.w);
+        }
+      }
+      __syncwarp();  // the buffer is rewritten two boxes later
+    } else {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && row0 < M) {
+        tma_store_2d(tm_out, buf, out_col0 + c, row0);
+        bulk_commit_group();
+      }
     }
     sbuf ^= 1;
   }
@@ -547,7 +578,7 @@ __global__ void __launch_bounds__(192, 1)
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       ++ltile;
     }
-    if (epi_staged(EPI, BN) && lane == 0) bulk_wait_group_all();  // stores done before the CTA exits
+    if (epi_tma_store(EPI, BN) && lane == 0) bulk_wait_group_all();  // stores done before the CTA exits
   }
 
   tc_fence_before();
@@ -804,7 +835,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       if (lane == 0) mbar_arrive_cluster(tempty_bar_leader + acc * 8);
       ++ltile;
     }
-    if (epi_staged(EPI, BN) && lane == 0) bulk_wait_group_all();
+    if (epi_tma_store(EPI, BN) && lane == 0) bulk_wait_group_all();
   }
 
   if (*abort_flag) {
@@ -1066,7 +1097,7 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
   }
   // staged epilogues store 32-row x 64-column boxes of the bf16 output by TMA
   CUtensorMap to = ta;
-  if (epi_staged((int)epi_kind, pair ? 256 : (int)bn))
+  if (epi_tma_store((int)epi_kind, pair ? 256 : (int)bn))
     to = make_tmap_bf16_2d(out.data_ptr(), M, out.size(1), out.stride(0), 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   uint32_t* errp = reinterpret_cast<uint32_t*>(err.data_ptr());
   if (pair) {

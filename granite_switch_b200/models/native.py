@@ -17,6 +17,7 @@ communicator is attached, that reduction runs in the fused kernels of
 """
 from __future__ import annotations
 
+import contextlib
 import math
 import os
 from dataclasses import dataclass
@@ -90,6 +91,7 @@ class NativeGraniteSwitch:
         self.layers: list[LayerWeights] = []
         self.remaps: torch.Tensor | None = None
         self.comm = None  # optional fused-collective communicator
+        self.prof = None  # optional per-op CUDA-event profiler (utils.step_profile.StepProfiler)
         # prefill attention on tcgen05 (head_dim 128); GSB_ATTN_TC=0 selects the mma.sync kernel
         self.use_tc_attention = os.environ.get("GSB_ATTN_TC", "1") != "0"
         self.err = err_buffer(device)
@@ -275,6 +277,9 @@ class NativeGraniteSwitch:
     def kv_cache_bytes(self) -> int:
         return self.kv_cache.numel() * self.kv_cache.element_size()
 
+    def _region(self, name: str):
+        return self.prof.region(name) if self.prof is not None else contextlib.nullcontext()
+
     # ------------------------------------------------------------------ forward pieces
     def _proj(self, pl: PackedLinear, x: torch.Tensor, out: torch.Tensor, epi=G.EPI_STORE, residual=None,
               scale=1.0, mc_out: int = 0):
@@ -314,13 +319,13 @@ class NativeGraniteSwitch:
         cfg = self.cfg
         t = b.num_tokens
         nat = native()
-        if self.n_maps:
-            nat.routing(b.ids, b.seq_starts, b.carry_in, self.expert_tbl, None, self.kind_lut,
-                        self.num_adapters, self.remaps, self.adapter_idx[:t], self.lora_idx[:t],
-                        self.mod_ids[:t], self.carry_out[: b.num_seqs], self.row_adapter[:, :t],
-                        self.tile_mask[:, : (t + 127) // 128])
-            E.embed(b.ids, self.embed_w, self.lut, cfg.embedding_multiplier, out=self.h[:t])
-        else:
+        R = self._region
+        with R("routing+embed"):
+            if self.n_maps:
+                nat.routing(b.ids, b.seq_starts, b.carry_in, self.expert_tbl, None, self.kind_lut,
+                            self.num_adapters, self.remaps, self.adapter_idx[:t], self.lora_idx[:t],
+                            self.mod_ids[:t], self.carry_out[: b.num_seqs], self.row_adapter[:, :t],
+                            self.tile_mask[:, : (t + 127) // 128])
             E.embed(b.ids, self.embed_w, self.lut, cfg.embedding_multiplier, out=self.h[:t])
         h, x = self.h[:t], self.x[:t]
         qkv, attn, act = self.qkv[:t], self.attn[:t], self.act[:t]
@@ -328,41 +333,56 @@ class NativeGraniteSwitch:
         scale = float(cfg.attention_multiplier)
         comm = self.comm
         if comm is not None:
-            E.rmsnorm(h, self.layers[0].in_norm, cfg.rms_norm_eps, out=x)
+            with R("rmsnorm"):
+                E.rmsnorm(h, self.layers[0].in_norm, cfg.rms_norm_eps, out=x)
         for li, lw in enumerate(self.layers):
             if comm is None:
-                E.rmsnorm(h, lw.in_norm, cfg.rms_norm_eps, out=x)
-            self._proj(lw.qkv, x, qkv)
+                with R("rmsnorm"):
+                    E.rmsnorm(h, lw.in_norm, cfg.rms_norm_eps, out=x)
+            with R("qkv"):
+                self._proj(lw.qkv, x, qkv)
             kc, vc = self.kv_cache[li, 0], self.kv_cache[li, 1]
-            E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
+            with R("rope+kv"):
+                E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
             for plan in b.plans:
                 if plan.rows == 128:
-                    A.prefill_attention_tc(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
-                                           plan.work_row0, self.num_q, scale, attn)
+                    with R("attn_prefill"):
+                        A.prefill_attention_tc(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
+                                               plan.work_row0, self.num_q, scale, attn)
                 else:
-                    A.paged_attention(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
-                                      plan.work_row0, plan.rows, self.num_q, scale, attn, plan.nsplit,
-                                      self.ws_o, self.ws_lse)
+                    with R("attn_decode" if plan.rows == 16 else "attn_prefill"):
+                        A.paged_attention(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
+                                          plan.work_row0, plan.rows, self.num_q, scale, attn, plan.nsplit,
+                                          self.ws_o, self.ws_lse)
             if comm is not None:
-                y = comm.row_parallel(self, lw.o, attn, h, mult)
-                comm.finish(y, h, lw.post_norm, x, cfg.rms_norm_eps)
+                with R("o+reduce"):
+                    y = comm.row_parallel(self, lw.o, attn, h, mult)
+                with R("finish+rmsnorm"):
+                    comm.finish(y, h, lw.post_norm, x, cfg.rms_norm_eps)
             else:
-                self._row_parallel(lw.o, attn, h, mult)
-                E.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps, out=x)
-            self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
+                with R("o"):
+                    self._row_parallel(lw.o, attn, h, mult)
+                with R("rmsnorm"):
+                    E.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps, out=x)
+            with R("gate_up+swiglu"):
+                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
             if comm is not None:
-                y = comm.row_parallel(self, lw.down, act, h, mult)
+                with R("down+reduce"):
+                    y = comm.row_parallel(self, lw.down, act, h, mult)
                 nxt = self.layers[li + 1].in_norm if li + 1 < len(self.layers) else self.final_norm
-                comm.finish(y, h, nxt, x, cfg.rms_norm_eps)
+                with R("finish+rmsnorm"):
+                    comm.finish(y, h, nxt, x, cfg.rms_norm_eps)
             else:
-                self._row_parallel(lw.down, act, h, mult)
+                with R("down"):
+                    self._row_parallel(lw.down, act, h, mult)
         nb = b.logit_rows.numel()
         if nb == 0:
             return None
         xf = self.xf[:nb]
-        E.rmsnorm(h, self.final_norm, cfg.rms_norm_eps, out=xf, rows=b.logit_rows)
-        logits = self.logits[:nb]
-        G.switched_gemm(xf, self.lm_head_w, logits, epi=G.EPI_F32, scale=1.0 / float(cfg.logits_scaling))
+        with R("lm_head"):
+            E.rmsnorm(h, self.final_norm, cfg.rms_norm_eps, out=xf, rows=b.logit_rows)
+            logits = self.logits[:nb]
+            G.switched_gemm(xf, self.lm_head_w, logits, epi=G.EPI_F32, scale=1.0 / float(cfg.logits_scaling))
         return logits
 
     def attention_plans(self, q_lens: list[int], kv_lens: list[int]) -> list[tuple[list[int], list[int], int, int]]:

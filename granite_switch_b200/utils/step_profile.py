@@ -1,0 +1,159 @@
+"""Per-op device time of one representative engine step (CUDA events, no profiler).
+
+``python -m granite_switch_b200.utils.step_profile [--preset granite-8b] [--prefill 4096 4096]
+[--decode 120 --decode-ctx 4400]``; under torchrun (one process per GPU) it
+runs the tensor-parallel model, with the fused NVSwitch collectives unless
+``--no-fused-comm``.
+
+The step is built the way the serving engine builds one: prefill chunks (a
+fresh prompt, or a chunk after a cached prefix) next to single-token decode
+rows, flattened into one batch, KV pages from the block manager. After
+warm-up steps, each op of the forward is bracketed by CUDA events (one pair
+per launch group) over ``--steps`` steps; the table gives the mean device
+milliseconds per step for each op summed over layers, and the share of the
+event-timed step. Rank 0 prints one JSON line; with several ranks every op
+is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import contextlib
+import json
+import os
+from collections import defaultdict
+
+import torch
+
+
+class StepProfiler:
+    """Collects (name, start event, end event) for regions of the forward."""
+
+    def __init__(self):
+        self.events = []
+
+    @contextlib.contextmanager
+    def region(self, name: str):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        try:
+            yield
+        finally:
+            b.record()
+            self.events.append((name, a, b))
+
+    def totals(self) -> dict[str, float]:
+        torch.cuda.synchronize()
+        out = defaultdict(float)
+        for name, a, b in self.events:
+            out[name] += a.elapsed_time(b)
+        self.events = []
+        return dict(out)
+
+
+def build_step(engine, prefill: list[int], decode: int, decode_ctx: int, vocab: int, seed: int = 0):
+    """Scheduler output with ``prefill`` chunks and ``decode`` single-token rows."""
+    from ..engine.request import Request, SamplingParams
+    from ..engine.scheduler import ScheduledChunk, SchedulerOutput
+
+    g = torch.Generator().manual_seed(seed)
+    bm = engine.blocks
+    out = SchedulerOutput()
+    for n in prefill:
+        r = Request(torch.randint(0, vocab, (n,), generator=g).tolist(), SamplingParams(max_tokens=8))
+        assert bm.allocate(r, n)
+        out.chunks.append(ScheduledChunk(r, 0, n))
+    for _ in range(decode):
+        r = Request(torch.randint(0, vocab, (decode_ctx,), generator=g).tolist(), SamplingParams(max_tokens=8))
+        r.output_ids.append(1)
+        assert bm.allocate(r, decode_ctx + 1)
+        r.num_computed = decode_ctx
+        out.chunks.append(ScheduledChunk(r, decode_ctx, 1))
+    return out
+
+
+def main():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--preset", default="granite-8b")
+    p.add_argument("--layers", type=int, default=None)
+    p.add_argument("--prefill", type=int, nargs="*", default=[4096, 3968])
+    p.add_argument("--decode", type=int, default=128)
+    p.add_argument("--decode-ctx", type=int, default=4400)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--no-fused-comm", dest="fused", action="store_false")
+    args = p.parse_args()
+
+    import torch.distributed as dist
+
+    from .. import _native
+    from ..engine import LLM, EngineConfig
+    from .timing import local_rank
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(local_rank())
+    group = None
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank()))
+        group = dist.group.WORLD
+    _native.native()
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+    import bench
+
+    bargs = argparse.Namespace(preset=args.preset, layers=args.layers)
+    config, base = bench.model_config(bargs)
+    tokens = sum(args.prefill) + args.decode
+    need_blocks = sum((n + 15) // 16 for n in args.prefill) + args.decode * ((args.decode_ctx + 16) // 16) + 64
+    ecfg = EngineConfig(max_num_seqs=max(8, len(args.prefill) + args.decode), max_num_batched_tokens=tokens,
+                        max_model_len=max(args.prefill + [args.decode_ctx + 1]) + 16, tensor_parallel_size=world,
+                        num_kv_blocks=need_blocks, fused_tp_comm=args.fused)
+    llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
+              random_init=dict(lora_modules=("qkv", "o"), rank=32), tp_rank=rank, tp_group=group)
+    eng = llm.engine
+    out = build_step(eng, args.prefill, args.decode, args.decode_ctx, base["vocab_size"])
+    ex = eng.executor
+    model = llm.model
+    for _ in range(args.warmup):
+        ex.compute_logits(out)
+    torch.cuda.synchronize()
+    prof = StepProfiler()
+    sums = defaultdict(float)
+    step_ms = 0.0
+    for _ in range(args.steps):
+        if group is not None:
+            dist.barrier(group=group)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        model.prof = prof
+        a.record()
+        ex.compute_logits(out)
+        b.record()
+        model.prof = None
+        for k, v in prof.totals().items():
+            sums[k] += v
+        step_ms += a.elapsed_time(b)
+    ops = {k: v / args.steps for k, v in sums.items()}
+    step_ms /= args.steps
+    if group is not None:
+        names = sorted(ops)
+        t = torch.tensor([ops[n] for n in names] + [step_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        ops = dict(zip(names, t[:-1].tolist()))
+        step_ms = float(t[-1])
+    if rank == 0:
+        table = {k: dict(ms=round(v, 3), share=round(v / step_ms, 3)) for k, v in sorted(ops.items(), key=lambda kv: -kv[1])}
+        print(json.dumps(dict(preset=args.preset, tp=world, fused_comm=bool(getattr(model, "comm", None)),
+                              tokens=tokens, prefill=args.prefill, decode=args.decode, decode_ctx=args.decode_ctx,
+                              step_ms=round(step_ms, 3), ops=table)), flush=True)
+    if group is not None:
+        dist.barrier(group=group)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
