@@ -76,7 +76,8 @@ def random_base_state(cfg: dict, seed: int = 0, std: float = 0.02, dtype=torch.f
 
 
 def random_peft_adapter(cfg: dict, rank: int, targets=("q", "k", "v"), seed: int = 1, std_a: float = 0.02,
-                        std_b: float = 0.01, dtype=torch.float32) -> dict[str, torch.Tensor]:
+                        std_b: float = 0.01, dtype=torch.float32, cross_rank: int = 0) -> dict[str, torch.Tensor]:
+    """PEFT-named random LoRA tensors; ``cross_rank > 0`` adds a Shadow-Residual ``cross_stream``."""
     g = torch.Generator().manual_seed(seed)
     shp = _shapes(cfg)
     out = {}
@@ -86,18 +87,43 @@ def random_peft_adapter(cfg: dict, rank: int, targets=("q", "k", "v"), seed: int
             pre = f"base_model.model.model.layers.{i}.{_MODS[t]}"
             out[pre + ".lora_A.weight"] = (torch.randn(rank, n_in, generator=g) * std_a).to(dtype)
             out[pre + ".lora_B.weight"] = (torch.randn(n_out, rank, generator=g) * std_b).to(dtype)
+        if cross_rank:
+            h = cfg["hidden_size"]
+            pre = f"base_model.model.model.layers.{i}.cross_stream"
+            out[pre + ".lora_A.weight"] = (torch.randn(cross_rank, h, generator=g) * std_a).to(dtype)
+            out[pre + ".lora_B.weight"] = (torch.randn(h, cross_rank, generator=g) * std_b).to(dtype)
+    return out
+
+
+def synthetic_probes(cfg: dict, n: int, num_labels: int = 3, read_layers=None, seed: int = 7) -> list[AdapterSpec]:
+    """``n`` probe slots: random label token ids and a random linear head each.
+
+    ``read_layers[i]`` is the decoder layer whose output the probe reads, or
+    ``None`` for the final-norm hidden state.
+    """
+    g = torch.Generator().manual_seed(seed)
+    h = cfg["hidden_size"]
+    out = []
+    for i in range(n):
+        labels = torch.randperm(cfg["vocab_size"] - 2, generator=g)[:num_labels].add(1).tolist()
+        layer = read_layers[i] if read_layers is not None else None
+        out.append(AdapterSpec(
+            name=f"probe_{i}", tensors={}, r=1, alpha=1.0, technology="lora", kind="probe",
+            probe_label_token_ids=labels, probe_read_layer=layer,
+            probe_weight=torch.randn(num_labels, h, generator=g) * 0.1, probe_bias=torch.randn(num_labels, generator=g)))
     return out
 
 
 def synthetic_adapters(cfg: dict, n: int, rank: int, targets=("q", "k", "v"), alpha: float | None = None,
                        invocation_len: int = 4, technology: str = "alora", seed: int = 1,
-                       std_a: float = 0.02, std_b: float = 0.01) -> list[AdapterSpec]:
+                       std_a: float = 0.02, std_b: float = 0.01, cross_rank: int = 0) -> list[AdapterSpec]:
     g = torch.Generator().manual_seed(seed + 1000)
     out = []
     for a in range(n):
         inv = torch.randint(1, cfg["vocab_size"] - 1, (invocation_len,), generator=g).tolist()
         out.append(AdapterSpec(
-            name=f"adapter_{a}", tensors=random_peft_adapter(cfg, rank, targets, seed + a, std_a, std_b),
+            name=f"adapter_{a}",
+            tensors=random_peft_adapter(cfg, rank, targets, seed + a, std_a, std_b, cross_rank=cross_rank),
             r=rank, alpha=alpha if alpha is not None else 2.0 * rank, technology=technology,
             invocation_tokens=inv))
     return out
@@ -106,12 +132,19 @@ def synthetic_adapters(cfg: dict, n: int, rank: int, targets=("q", "k", "v"), al
 def compose_synthetic(out_dir: str, preset: str | dict = "tiny", num_adapters: int = 3, rank: int = 8,
                       targets=("q", "k", "v"), seed: int = 0, dtype=torch.float32, invocation_len: int = 4,
                       base_reset: bool = False, technology: str = "alora", alpha: float | None = None,
-                      **cfg_overrides):
-    """Write a composed checkpoint with random base + random adapters; returns the config."""
+                      num_probes: int = 0, probe_read_layers=None, probe_labels: int = 3, cross_rank: int = 0,
+                      std_b: float = 0.01, **cfg_overrides):
+    """Write a composed checkpoint with random base + random adapters; returns the config.
+
+    ``num_probes`` appends probe slots after the LoRA slots; ``cross_rank > 0``
+    makes every adapter a Shadow-Residual one (dual-stream checkpoint).
+    """
     cfg = base_config(preset, **cfg_overrides)
     base = random_base_state(cfg, seed=seed)
     ads = synthetic_adapters(cfg, num_adapters, rank, targets, alpha=alpha, invocation_len=invocation_len,
-                             technology=technology, seed=seed + 1)
+                             technology=technology, seed=seed + 1, cross_rank=cross_rank, std_b=std_b)
+    if num_probes:
+        ads += synthetic_probes(cfg, num_probes, probe_labels, probe_read_layers, seed=seed + 7)
     return compose_checkpoint(cfg, base, ads, out_dir, dtype=dtype, base_reset=base_reset,
                               base_model_name=f"synthetic-{preset if isinstance(preset, str) else 'custom'}")
 
