@@ -20,5 +20,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_barrier", &gsb_peer_barrier, "bounded cross-rank barrier over P2P signal pads");
   m.def("multimem_allreduce_bf16", &gsb_multimem_allreduce_bf16, "NVLS one-shot all-reduce (multimem)");
   m.def("rmsnorm_residual_from", &gsb_rmsnorm_residual_from, "h <- y; x <- rmsnorm(y); y <- 0");
+  m.def("probe_verdict", &gsb_probe_verdict, "probe-head scores at marker rows");
+  m.def("probe_rewrite", &gsb_probe_rewrite, "replace marker logit rows by the probe verdict");
   m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode)");
 }

@@ -50,3 +50,8 @@ void gsb_peer_barrier(const at::Tensor& pad_ptrs_dev, int64_t rank, int64_t tp, 
 void gsb_multimem_allreduce_bf16(int64_t mc_ptr, int64_t nbytes, int64_t rank, int64_t tp, const at::Tensor& like);
 void gsb_rmsnorm_residual_from(const at::Tensor& y, const at::Tensor& h, const at::Tensor& w, const at::Tensor& x,
                                double eps);
+void gsb_probe_verdict(const at::Tensor& hidden, const at::Tensor& rows, const at::Tensor& slots,
+                       const at::Tensor& out_rows, const at::Tensor& w, const at::Tensor& bias,
+                       const at::Tensor& verdict);
+void gsb_probe_rewrite(const at::Tensor& logits, int64_t vocab_lo, const at::Tensor& out_rows,
+                       const at::Tensor& slots, const at::Tensor& labels, const at::Tensor& verdict);

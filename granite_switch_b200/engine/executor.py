@@ -170,10 +170,30 @@ class NativeExecutor:
         self.h2d_bytes += 8 * 3 * t + 4 * (3 * s + 1) + 4 * s * width + 8 * nb + 4 * 2 * len(plans_host) * nw
         plans = [AttnPlan(self.d_work[2 * pi, : len(ws)], self.d_work[2 * pi + 1, : len(ws)], rows, ns)
                  for pi, (ws, wr, rows, ns) in enumerate(plans_host)]
+        probe_groups = probe_all = None
+        if m.probe_w is not None:
+            marks = probe_markers(m.cfg, hb)
+            if marks:
+                # rare (probe calls only): small synchronous copies
+                read = m.cfg.probe_read_layers or [None] * m.cfg.num_adapters
+                dev = self.device
+                groups = {}
+                for j, r, slot in marks:
+                    groups.setdefault(read[slot - 1], []).append((j, r, slot))
+                probe_groups = []
+                for layer, ms in groups.items():
+                    rows = [r for _, r, _ in ms] if layer is not None else [j for j, _, _ in ms]
+                    probe_groups.append((layer, torch.tensor(rows, dtype=torch.int32, device=dev),
+                                         torch.tensor([sl for _, _, sl in ms], dtype=torch.int32, device=dev),
+                                         torch.tensor([j for j, _, _ in ms], dtype=torch.int32, device=dev)))
+                probe_all = (torch.tensor([j for j, _, _ in marks], dtype=torch.int32, device=dev),
+                             torch.tensor([sl for _, _, sl in marks], dtype=torch.int32, device=dev))
+                self.h2d_bytes += 4 * 5 * len(marks)
         return StepBatch(num_tokens=t, num_seqs=s, ids=self.d_i64[:t], positions=self.d_i64[t:2 * t],
                          slots=self.d_i64[2 * t:3 * t], seq_starts=self.d_i32[: s + 1],
                          carry_in=self.d_i32[s + 1:2 * s + 1], kv_lens=self.d_i32[2 * s + 1:3 * s + 1],
-                         block_table=self.d_bt[:s, :width], logit_rows=self.d_rows[:nb], plans=plans)
+                         block_table=self.d_bt[:s, :width], logit_rows=self.d_rows[:nb], plans=plans,
+                         probe_groups=probe_groups, probe_all=probe_all)
 
     def _gather_logits(self, logits: torch.Tensor) -> torch.Tensor:
         if self.tp_size == 1:
@@ -241,7 +261,7 @@ class ReferenceExecutor:
 
     @torch.no_grad()
     def compute_logits(self, out: SchedulerOutput):
-        from ..models.layers import apply_rope, rope_cos_sin
+        from ..models.layers import rope_cos_sin
         from ..ops.attention import paged_attention_reference
         from ..routing.token_exchange import apply_token_exchange
 
@@ -250,10 +270,10 @@ class ReferenceExecutor:
         ids = torch.from_numpy(hb.ids)
         if self.table is not None:
             idx, _ = route_flat(ids, hb.starts.tolist(), hb.carry.tolist(), self.table)
-            lora_idx, _ = self.m.model.switch.split_indices(idx)
+            lora_idx, probe_idx = self.m.model.switch.split_indices(idx)
             lut = self.m.model.switch.control_to_substitute_lut
         else:
-            lora_idx = torch.zeros_like(ids)
+            lora_idx = probe_idx = torch.zeros_like(ids)
             lut = None
         mod = apply_token_exchange(lut, ids)
         pos = torch.from_numpy(hb.pos)
@@ -262,22 +282,85 @@ class ReferenceExecutor:
         cos, sin = rope_cos_sin(pos.unsqueeze(0), cfg.head_dim_eff, cfg.rope_theta, h.dtype)
         bt = torch.from_numpy(hb.bt)
         blk, off = slots // BLOCK_SIZE, slots % BLOCK_SIZE
+        markers = probe_markers(cfg, hb, probe_idx)
+        verdict = {}
+        head = self.m.model.probe_head
+        read = cfg.probe_read_layers or [None] * cfg.num_adapters
+
+        def score(layer, hidden):
+            for j, r, slot in markers:
+                if read[slot - 1] == layer:
+                    verdict[j] = head(hidden[r].unsqueeze(0), torch.tensor([slot]))[0]
+
+        n = len(hb.ids)
+        li_b = lora_idx.unsqueeze(0)
+        dual = bool(cfg.dual_stream)
+        hbase = h if dual else None
+
+        def attend(q, li, att):
+            return paged_attention_reference(q[0].reshape(n, -1), self.kv[li, 0], self.kv[li, 1], bt, hb.q_lens,
+                                             hb.kv_lens, cfg.num_attention_heads, att.scaling)
+
         for li, layer in enumerate(self.m.model.layers):
             att = layer.self_attn
-            x = layer.input_layernorm(h)
-            q, k, v = att.project_qkv(x.unsqueeze(0), lora_idx.unsqueeze(0), cos, sin)
-            q, k, v = q[0], k[0], v[0]
-            self.kv[li, 0, blk, :, off] = k.to(self.kv.dtype)
-            self.kv[li, 1, blk, :, off] = v.to(self.kv.dtype)
-            o = paged_attention_reference(q.reshape(len(hb.ids), -1), self.kv[li, 0], self.kv[li, 1], bt,
-                                          hb.q_lens, hb.kv_lens, cfg.num_attention_heads, att.scaling)
-            h = h + att.out(o.to(h.dtype).unsqueeze(0), lora_idx.unsqueeze(0))[0] * layer.residual_multiplier
-            x = layer.post_attention_layernorm(h)
-            h = h + layer.mlp(x.unsqueeze(0), lora_idx.unsqueeze(0))[0] * layer.residual_multiplier
+            rm = layer.residual_multiplier
+            if dual:
+                # Shadow Residual: the base stream writes K/V; the adapter stream's
+                # queries attend to that base K/V (its own K/V are never used)
+                xb = layer.input_layernorm(hbase).unsqueeze(0)
+                xa = layer.input_layernorm(h).unsqueeze(0)
+                qb, k, v = att.project_qkv(xb, None, cos, sin)
+                qa, _, _ = att.project_qkv(xa, li_b, cos, sin)
+                self.kv[li, 0, blk, :, off] = k[0].to(self.kv.dtype)
+                self.kv[li, 1, blk, :, off] = v[0].to(self.kv.dtype)
+                ob, oa = attend(qb, li, att), attend(qa, li, att)
+                hbase = hbase + att.out(ob.to(h.dtype).unsqueeze(0), None)[0] * rm
+                h = h + att.out(oa.to(h.dtype).unsqueeze(0), li_b)[0] * rm
+                xb = layer.post_attention_layernorm(hbase).unsqueeze(0)
+                xa = layer.post_attention_layernorm(h).unsqueeze(0)
+                routing = layer.block_sparse_moe.route(xb) if layer.block_sparse_moe is not None else None
+                hbase = hbase + layer.mlp(xb, None, routing)[0] * rm
+                h = h + layer.mlp(xa, li_b, routing)[0] * rm
+                h = h + layer.cross_stream(hbase.unsqueeze(0), li_b)[0]
+            else:
+                x = layer.input_layernorm(h)
+                q, k, v = att.project_qkv(x.unsqueeze(0), li_b, cos, sin)
+                self.kv[li, 0, blk, :, off] = k[0].to(self.kv.dtype)
+                self.kv[li, 1, blk, :, off] = v[0].to(self.kv.dtype)
+                o = attend(q, li, att)
+                h = h + att.out(o.to(h.dtype).unsqueeze(0), li_b)[0] * rm
+                x = layer.post_attention_layernorm(h)
+                h = h + layer.mlp(x.unsqueeze(0), li_b)[0] * rm
+            score(li, h)
         if not len(hb.rows):
             return hb, None
         hf = self.m.model.norm(h[torch.from_numpy(hb.rows)])
-        return hb, self.m.lm_head(hf).float() / cfg.logits_scaling
+        logits = self.m.lm_head(hf).float() / cfg.logits_scaling
+        for j, _r, slot in markers:
+            if read[slot - 1] is None:
+                verdict[j] = head(hf[j].unsqueeze(0), torch.tensor([slot]))[0]
+            labels = cfg.probe_label_token_ids[slot - 1]
+            logits[j] = float("-inf")
+            logits[j, torch.tensor(labels)] = verdict[j][: len(labels)].float()
+        return hb, logits
 
 
-__all__ = ["NativeExecutor", "ReferenceExecutor", "HostBatch", "math"]
+def probe_markers(cfg, hb: HostBatch, probe_idx=None) -> list[tuple[int, int, int]]:
+    """``(logit row j, flat token row, probe slot)`` for sampled rows that hold a probe control token.
+
+    A probe's control token must be its request's last token, so a marker is
+    always a row that samples (reference: src/granite_switch/hf/modeling_granite_switch.py:482-531).
+    """
+    ids = cfg.probe_control_token_ids or []
+    if not ids or not len(hb.rows):
+        return []
+    tok = hb.ids[hb.rows]
+    hit = np.flatnonzero(np.isin(tok, np.asarray(ids)))
+    if not hit.size:
+        return []
+    off = len(cfg.adapter_token_ids or []) - cfg.num_adapters
+    slot_of = {int(t): i - off + 1 for i, t in enumerate(cfg.adapter_token_ids or []) if i >= off}
+    return [(int(j), int(hb.rows[j]), slot_of[int(tok[j])]) for j in hit]
+
+
+__all__ = ["NativeExecutor", "ReferenceExecutor", "HostBatch", "probe_markers", "math"]

@@ -41,6 +41,7 @@ class LayerWeights:
     o: PackedLinear
     gu: PackedLinear
     down: PackedLinear
+    cross: PackedLinear | None = None   # Shadow Residual cross-stream LoRA (no base weight)
 
 
 @dataclass
@@ -66,6 +67,10 @@ class StepBatch:
     block_table: torch.Tensor  # [S, max_blocks] int32
     logit_rows: torch.Tensor   # [B] int64 rows whose logits are needed
     plans: list                # [AttnPlan]
+    # probe markers: per read layer (None = final norm) the device tensors
+    # (flat rows, slots, logit rows); plus (logit rows, slots) of all markers
+    probe_groups: list | None = None
+    probe_all: tuple | None = None
 
 
 class NativeGraniteSwitch:
@@ -103,6 +108,10 @@ class NativeGraniteSwitch:
         self.kind_lut = None
         self.cos_sin = E.rope_cos_sin_table(min(config.max_position_embeddings, 1 << 17), self.head_dim,
                                             config.rope_theta, device)
+        # Shadow Residual (dual stream): base stream + adapter stream over base-only K/V
+        self.dual = bool(getattr(config, "dual_stream", False))
+        # probe heads: weight [NA, L, H] bf16, bias [NA, L] fp32, label ids [NA, L] int32 (-1 pad)
+        self.probe_w = self.probe_b = self.probe_labels = None
 
     # ------------------------------------------------------------------ weights
     def _finish_weights(self, embed: torch.Tensor, final_norm: torch.Tensor, lm_head: torch.Tensor | None):
@@ -132,14 +141,38 @@ class NativeGraniteSwitch:
         # remap tables (deduplicated) for the routing kernel
         maps: list[list[int]] = []
         for lw in self.layers:
-            for pl in (lw.qkv, lw.o, lw.gu, lw.down):
-                if pl.has_lora:
+            for pl in (lw.qkv, lw.o, lw.gu, lw.down, lw.cross):
+                if pl is not None and pl.has_lora:
                     if pl.remap not in maps:
                         maps.append(pl.remap)
                     pl.map_id = maps.index(pl.remap)
         self.remaps = torch.tensor(maps, dtype=torch.int32, device=self.device) if maps else None
         self.n_maps = len(maps)
         self._alloc_buffers()
+
+    def _set_probes(self, weight: torch.Tensor, bias: torch.Tensor) -> None:
+        cfg = self.cfg
+        na, lmax = weight.shape[0], weight.shape[1]
+        labels = torch.full((na, lmax), -1, dtype=torch.int32)
+        for i, ids in enumerate(cfg.probe_label_token_ids or []):
+            if ids:
+                labels[i, : len(ids)] = torch.tensor(ids, dtype=torch.int32)
+        self.probe_w = weight.to(self.device, torch.bfloat16).contiguous()
+        self.probe_b = bias.to(self.device, torch.float32).contiguous()
+        self.probe_labels = labels.to(self.device)
+
+    def _pack_cross(self, la: torch.Tensor, lb: torch.Tensor) -> PackedLinear:
+        """Cross-stream LoRA (replicated under TP). Its base weight is all zeros and
+        never multiplied; ``lb`` is padded to the shrink width so the expand is one
+        plain GEMM ``S @ lb^T`` over every adapter column."""
+        h = self.hidden
+        pl = pack_linear(torch.zeros(h, h), [la], [lb], [h], self.num_adapters, self.device)
+        pl.w = None
+        if pl.has_lora:
+            pad = torch.zeros(h, pl.a_all.shape[0], dtype=pl.lb.dtype, device=self.device)
+            pad[:, : pl.lb.shape[1]] = pl.lb
+            pl.lb = pad
+        return pl
 
     @classmethod
     def from_state_dict(cls, config: GraniteSwitchConfig, sd, device, max_tokens: int, num_kv_blocks: int,
@@ -179,6 +212,12 @@ class NativeGraniteSwitch:
                 gu=lin(p + "shared_mlp.input_linear", [inter, inter], "column", swiglu=tiles),
                 down=lin(p + "shared_mlp.output_linear", [h], "row"),
             ))
+        if self.dual:
+            for i, lw in enumerate(self.layers):
+                p = f"model.layers.{i}.cross_stream."
+                lw.cross = self._pack_cross(get(p + "lora_A"), get(p + "lora_B"))
+        if has("model.probe_head.weight"):
+            self._set_probes(get("model.probe_head.weight"), get("model.probe_head.bias"))
         embed = get("model.embed_tokens.weight").to(device, torch.bfloat16)
         lm = None
         if not config.tie_word_embeddings and has("lm_head.weight"):
@@ -230,6 +269,13 @@ class NativeGraniteSwitch:
                 gu=lin([inter, inter], h, "column", "gu" in lora_modules, swiglu=tiles),
                 down=lin([h], inter, "row", "down" in lora_modules),
             ))
+        if self.dual and na > 0:
+            rc = int(config.cross_stream_rank or 32)
+            for lw in self.layers:
+                lw.cross = self._pack_cross(rnd(na, 1, rc, h).float().cpu(), rnd(na, 1, h, rc, s=0.01).float().cpu())
+        if config.probe_control_token_ids:
+            lmax = max(1, config.max_probe_labels)
+            self._set_probes(rnd(na, lmax, h, s=0.1), torch.randn(na, lmax, generator=g, device=device))
         embed = rnd(config.vocab_size, h)
         if config.adapter_token_ids:
             from ..routing.token_exchange import build_control_to_substitute_lut
@@ -254,10 +300,16 @@ class NativeGraniteSwitch:
         self.act = torch.empty(t, self.inter, dtype=bf, device=dev)
         s_cols = 64
         for lw in self.layers:
-            for pl in (lw.qkv, lw.o, lw.gu, lw.down):
-                if pl.has_lora:
+            for pl in (lw.qkv, lw.o, lw.gu, lw.down, lw.cross):
+                if pl is not None and pl.has_lora:
                     s_cols = max(s_cols, pl.a_all.shape[0])
         self.s_buf = torch.empty(t, s_cols, dtype=bf, device=dev)
+        if self.dual:
+            self.hbase = torch.empty(t, self.hidden, dtype=bf, device=dev)
+            self.hbase2 = torch.empty(t, self.hidden, dtype=bf, device=dev) if self.tp_size > 1 else None
+            self.qa = torch.empty(t, self.num_q * self.head_dim, dtype=bf, device=dev)
+        if self.probe_w is not None:
+            self.verdict = torch.zeros(self.max_seqs, self.probe_w.shape[1], dtype=torch.float32, device=dev)
         self.adapter_idx = torch.empty(t, dtype=torch.int32, device=dev)
         self.lora_idx = torch.empty(t, dtype=torch.int32, device=dev)
         self.mod_ids = torch.empty(t, dtype=torch.long, device=dev)
@@ -282,36 +334,71 @@ class NativeGraniteSwitch:
 
     # ------------------------------------------------------------------ forward pieces
     def _proj(self, pl: PackedLinear, x: torch.Tensor, out: torch.Tensor, epi=G.EPI_STORE, residual=None,
-              scale=1.0, mc_out: int = 0):
+              scale=1.0, mc_out: int = 0, lora: bool = True, n_rows: int | None = None):
+        """``out <- epi(x @ W^T (+ switched LoRA))``.
+
+        ``lora=False`` runs the base weight only (the Shadow-Residual base
+        stream); ``n_rows`` restricts the projection to the first output rows
+        of ``W``, which must be the first slice (the adapter stream's Q).
+        """
         m = x.shape[0]
-        if pl.has_lora:
+        w, lb, bounds = pl.w, pl.lb, pl.slice_bounds
+        if n_rows is not None:
+            assert n_rows == pl.slice_bounds[1], "n_rows must cover exactly the first slice"
+            w, bounds = w[:n_rows], [0, n_rows]
+            lb = lb[:n_rows] if lb is not None else None
+        bn = pl.swiglu_tile if epi == G.EPI_SWIGLU else None
+        if pl.has_lora and lora:
             ra = self.row_adapter[pl.map_id, :m]
-            s = self.s_buf[:m, : pl.a_all.shape[0]]
             tm = self.tile_mask[pl.map_id, : (m + 127) // 128]
-            G.lora_shrink(x, pl.a_all, ra, pl.rank, pl.n_local, out=s, tile_mask=tm)
-            bn = pl.swiglu_tile if epi == G.EPI_SWIGLU else None
-            G.switched_gemm(x, pl.w, out, epi=epi, residual=residual, scale=scale, s=s, lb=pl.lb, tile_mask=tm,
+            a_all = pl.a_all
+            if n_rows is not None:  # shrink of the first slice only
+                a_all = a_all[: (pl.n_local * pl.rank + 63) // 64 * 64]
+            s = self.s_buf[:m, : a_all.shape[0]]
+            G.lora_shrink(x, a_all, ra, pl.rank, pl.n_local, out=s, tile_mask=tm)
+            G.switched_gemm(x, w, out, epi=epi, residual=residual, scale=scale, s=s, lb=lb, tile_mask=tm,
                             rank=pl.rank, num_adapters=pl.n_local,
-                            slice_bounds=[0, pl.n] if epi == G.EPI_SWIGLU else pl.slice_bounds, bn=bn,
+                            slice_bounds=[0, pl.n] if epi == G.EPI_SWIGLU else bounds, bn=bn,
                             mc_out=mc_out)
         else:
-            bn = pl.swiglu_tile if epi == G.EPI_SWIGLU else None
-            G.switched_gemm(x, pl.w, out, epi=epi, residual=residual, scale=scale, bn=bn, mc_out=mc_out)
+            G.switched_gemm(x, w, out, epi=epi, residual=residual, scale=scale, bn=bn, mc_out=mc_out)
         return out
 
-    def _row_parallel(self, pl: PackedLinear, x: torch.Tensor, h: torch.Tensor, mult: float):
+    def _row_parallel(self, pl: PackedLinear, x: torch.Tensor, h: torch.Tensor, mult: float, lora: bool = True,
+                      partial: torch.Tensor | None = None):
         """h <- h + x @ W^T * mult, summed over TP ranks."""
         m = x.shape[0]
         if self.tp_size == 1:
-            self._proj(pl, x, h, epi=G.EPI_RESADD, residual=h, scale=mult)
+            self._proj(pl, x, h, epi=G.EPI_RESADD, residual=h, scale=mult, lora=lora)
             return
-        y = self.h2[:m]
+        y = (partial if partial is not None else self.h2)[:m]
         if self.tp_rank == 0:
-            self._proj(pl, x, y, epi=G.EPI_RESADD, residual=h, scale=mult)
+            self._proj(pl, x, y, epi=G.EPI_RESADD, residual=h, scale=mult, lora=lora)
         else:
-            self._proj(pl, x, y, epi=G.EPI_STORE, scale=mult)
+            self._proj(pl, x, y, epi=G.EPI_STORE, scale=mult, lora=lora)
         torch.distributed.all_reduce(y, group=self.tp_group)
         h.copy_(y)
+
+    def _cross_stream(self, pl: PackedLinear, hbase: torch.Tensor, h: torch.Tensor) -> None:
+        """Shadow Residual injection ``h <- h + (hbase A_a^T) B_a^T`` on rows routed to adapter a.
+
+        The shrink is computed for every column (no tile mask), so S is exactly
+        zero outside each row's own adapter, and the expand is one plain GEMM
+        over all adapter columns (reference K4: kernels/switch_lora_kernel.py:883-1091).
+        """
+        if pl is None or not pl.has_lora:
+            return
+        m = hbase.shape[0]
+        ra = self.row_adapter[pl.map_id, :m]
+        s = self.s_buf[:m, : pl.a_all.shape[0]]
+        G.lora_shrink(hbase, pl.a_all, ra, pl.rank, pl.n_local, out=s)
+        G.switched_gemm(s, pl.lb, h, epi=G.EPI_RESADD, residual=h, scale=1.0)
+
+    def _probe_layer(self, b: StepBatch, layer, hidden: torch.Tensor) -> None:
+        """Probe scores of the markers that read ``layer`` (None: the final-norm rows)."""
+        for lay, rows, slots, outj in b.probe_groups:
+            if lay == layer:
+                native().probe_verdict(hidden, rows, slots, outj, self.probe_w, self.probe_b, self.verdict)
 
     @torch.no_grad()
     def forward(self, b: StepBatch) -> torch.Tensor:
@@ -332,49 +419,46 @@ class NativeGraniteSwitch:
         mult = float(cfg.residual_multiplier)
         scale = float(cfg.attention_multiplier)
         comm = self.comm
-        if comm is not None:
-            with R("rmsnorm"):
-                E.rmsnorm(h, self.layers[0].in_norm, cfg.rms_norm_eps, out=x)
-        for li, lw in enumerate(self.layers):
-            if comm is None:
+        probes = bool(b.probe_groups)
+        if self.dual:
+            self._forward_dual(b, h, x, qkv, attn, act, mult, scale)
+        else:
+            if comm is not None:
                 with R("rmsnorm"):
-                    E.rmsnorm(h, lw.in_norm, cfg.rms_norm_eps, out=x)
-            with R("qkv"):
-                self._proj(lw.qkv, x, qkv)
-            kc, vc = self.kv_cache[li, 0], self.kv_cache[li, 1]
-            with R("rope+kv"):
-                E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
-            for plan in b.plans:
-                if plan.rows == 128:
-                    with R("attn_prefill"):
-                        A.prefill_attention_tc(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
-                                               plan.work_row0, self.num_q, scale, attn)
+                    E.rmsnorm(h, self.layers[0].in_norm, cfg.rms_norm_eps, out=x)
+            for li, lw in enumerate(self.layers):
+                if comm is None:
+                    with R("rmsnorm"):
+                        E.rmsnorm(h, lw.in_norm, cfg.rms_norm_eps, out=x)
+                with R("qkv"):
+                    self._proj(lw.qkv, x, qkv)
+                kc, vc = self.kv_cache[li, 0], self.kv_cache[li, 1]
+                with R("rope+kv"):
+                    E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
+                self._attention(b, qkv, kc, vc, attn, scale)
+                if comm is not None:
+                    with R("o+reduce"):
+                        y = comm.row_parallel(self, lw.o, attn, h, mult)
+                    with R("finish+rmsnorm"):
+                        comm.finish(y, h, lw.post_norm, x, cfg.rms_norm_eps)
                 else:
-                    with R("attn_decode" if plan.rows == 16 else "attn_prefill"):
-                        A.paged_attention(qkv, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
-                                          plan.work_row0, plan.rows, self.num_q, scale, attn, plan.nsplit,
-                                          self.ws_o, self.ws_lse)
-            if comm is not None:
-                with R("o+reduce"):
-                    y = comm.row_parallel(self, lw.o, attn, h, mult)
-                with R("finish+rmsnorm"):
-                    comm.finish(y, h, lw.post_norm, x, cfg.rms_norm_eps)
-            else:
-                with R("o"):
-                    self._row_parallel(lw.o, attn, h, mult)
-                with R("rmsnorm"):
-                    E.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps, out=x)
-            with R("gate_up+swiglu"):
-                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
-            if comm is not None:
-                with R("down+reduce"):
-                    y = comm.row_parallel(self, lw.down, act, h, mult)
-                nxt = self.layers[li + 1].in_norm if li + 1 < len(self.layers) else self.final_norm
-                with R("finish+rmsnorm"):
-                    comm.finish(y, h, nxt, x, cfg.rms_norm_eps)
-            else:
-                with R("down"):
-                    self._row_parallel(lw.down, act, h, mult)
+                    with R("o"):
+                        self._row_parallel(lw.o, attn, h, mult)
+                    with R("rmsnorm"):
+                        E.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps, out=x)
+                with R("gate_up+swiglu"):
+                    self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
+                if comm is not None:
+                    with R("down+reduce"):
+                        y = comm.row_parallel(self, lw.down, act, h, mult)
+                    nxt = self.layers[li + 1].in_norm if li + 1 < len(self.layers) else self.final_norm
+                    with R("finish+rmsnorm"):
+                        comm.finish(y, h, nxt, x, cfg.rms_norm_eps)
+                else:
+                    with R("down"):
+                        self._row_parallel(lw.down, act, h, mult)
+                if probes:
+                    self._probe_layer(b, li, h)
         nb = b.logit_rows.numel()
         if nb == 0:
             return None
@@ -383,7 +467,83 @@ class NativeGraniteSwitch:
             E.rmsnorm(h, self.final_norm, cfg.rms_norm_eps, out=xf, rows=b.logit_rows)
             logits = self.logits[:nb]
             G.switched_gemm(xf, self.lm_head_w, logits, epi=G.EPI_F32, scale=1.0 / float(cfg.logits_scaling))
+        if probes:
+            self._probe_layer(b, None, xf)
+            outj, slots = b.probe_all
+            native().probe_rewrite(logits, self.lm_vocab_lo, outj, slots, self.probe_labels, self.verdict)
         return logits
+
+    def _attention(self, b: StepBatch, q: torch.Tensor, kc, vc, attn: torch.Tensor, scale: float) -> None:
+        R = self._region
+        for plan in b.plans:
+            if plan.rows == 128:
+                with R("attn_prefill"):
+                    A.prefill_attention_tc(q, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
+                                           plan.work_row0, self.num_q, scale, attn)
+            else:
+                with R("attn_decode" if plan.rows == 16 else "attn_prefill"):
+                    A.paged_attention(q, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
+                                      plan.work_row0, plan.rows, self.num_q, scale, attn, plan.nsplit,
+                                      self.ws_o, self.ws_lse)
+
+    def _forward_dual(self, b: StepBatch, h, x, qkv, attn, act, mult: float, scale: float) -> None:
+        """Shadow Residual layers (reference: src/granite_switch/vllm/decoder/shadow_residual/decoder.py:88-364).
+
+        ``hbase`` is the base stream (no LoRA anywhere; it alone writes K/V),
+        ``h`` the adapter stream: its queries (LoRA on the Q slice) attend to
+        the base K/V, its o/MLP projections run the switched LoRA, and after
+        the MLP it receives the cross-stream delta computed from ``hbase``.
+        Logits are read from the adapter stream. Under tensor parallelism both
+        streams are reduced over NCCL; the cross stream is replicated.
+        """
+        cfg = self.cfg
+        R = self._region
+        t = b.num_tokens
+        hb = self.hbase[:t]
+        hb.copy_(h)
+        qa = self.qa[:t]
+        q_n = self.num_q * self.head_dim
+        eps = cfg.rms_norm_eps
+        hb2 = self.hbase2[:t] if self.hbase2 is not None else None
+        for li, lw in enumerate(self.layers):
+            kc, vc = self.kv_cache[li, 0], self.kv_cache[li, 1]
+            # base stream: q, k, v without LoRA; k/v go to the cache
+            with R("rmsnorm"):
+                E.rmsnorm(hb, lw.in_norm, eps, out=x)
+            with R("qkv"):
+                self._proj(lw.qkv, x, qkv, lora=False)
+            with R("rope+kv"):
+                E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
+            self._attention(b, qkv, kc, vc, attn, scale)
+            with R("o"):
+                self._row_parallel(lw.o, attn, hb, mult, lora=False, partial=hb2)
+            # adapter stream: switched Q only, same base K/V
+            with R("rmsnorm"):
+                E.rmsnorm(h, lw.in_norm, eps, out=x)
+            with R("qkv"):
+                self._proj(lw.qkv, x, qa, n_rows=q_n)
+            with R("rope+kv"):
+                E.rope_kv(qa, b.positions, self.cos_sin, self.num_q, 0, self.head_dim)
+            self._attention(b, qa, kc, vc, attn, scale)
+            with R("o"):
+                self._row_parallel(lw.o, attn, h, mult)
+            # MLPs: base stream first (its output feeds the cross stream)
+            with R("rmsnorm"):
+                E.rmsnorm(hb, lw.post_norm, eps, out=x)
+            with R("gate_up+swiglu"):
+                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU, lora=False)
+            with R("down"):
+                self._row_parallel(lw.down, act, hb, mult, lora=False, partial=hb2)
+            with R("rmsnorm"):
+                E.rmsnorm(h, lw.post_norm, eps, out=x)
+            with R("gate_up+swiglu"):
+                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
+            with R("down"):
+                self._row_parallel(lw.down, act, h, mult)
+            with R("cross_stream"):
+                self._cross_stream(lw.cross, hb, h)
+            if b.probe_groups:
+                self._probe_layer(b, li, h)
 
     def attention_plans(self, q_lens: list[int], kv_lens: list[int]) -> list[tuple[list[int], list[int], int, int]]:
         """Split requests into decode-layout and prefill-layout CTA work lists."""

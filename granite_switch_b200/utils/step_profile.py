@@ -11,7 +11,9 @@ rows, flattened into one batch, KV pages from the block manager. After
 warm-up steps, each op of the forward is bracketed by CUDA events (one pair
 per launch group) over ``--steps`` steps; the table gives the mean device
 milliseconds per step for each op summed over layers, and the share of the
-event-timed step. Rank 0 prints one JSON line; with several ranks every op
+event-timed step. ``step_ms`` is the step without the per-op events and
+``host_enqueue_ms`` the host time to stage the inputs and enqueue every
+launch of the step. Rank 0 prints one JSON line; with several ranks every op
 is the max over ranks.
 """
 from __future__ import annotations
@@ -122,6 +124,28 @@ def main():
     for _ in range(args.warmup):
         ex.compute_logits(out)
     torch.cuda.synchronize()
+    # host time to enqueue one step (no profiler regions): staging + every launch
+    import time
+
+    host_ms = 0.0
+    for _ in range(args.steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ex.compute_logits(out)
+        host_ms += (time.perf_counter() - t0) * 1e3
+    host_ms /= args.steps
+    torch.cuda.synchronize()
+    plain = 0.0
+    for _ in range(args.steps):
+        if group is not None:
+            dist.barrier(group=group)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ex.compute_logits(out)
+        b.record()
+        b.synchronize()
+        plain += a.elapsed_time(b)
+    plain /= args.steps
     prof = StepProfiler()
     sums = defaultdict(float)
     step_ms = 0.0
@@ -141,15 +165,16 @@ def main():
     step_ms /= args.steps
     if group is not None:
         names = sorted(ops)
-        t = torch.tensor([ops[n] for n in names] + [step_ms], device="cuda")
+        t = torch.tensor([ops[n] for n in names] + [step_ms, plain, host_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
-        ops = dict(zip(names, t[:-1].tolist()))
-        step_ms = float(t[-1])
+        ops = dict(zip(names, t[:-3].tolist()))
+        step_ms, plain, host_ms = float(t[-3]), float(t[-2]), float(t[-1])
     if rank == 0:
         table = {k: dict(ms=round(v, 3), share=round(v / step_ms, 3)) for k, v in sorted(ops.items(), key=lambda kv: -kv[1])}
         print(json.dumps(dict(preset=args.preset, tp=world, fused_comm=bool(getattr(model, "comm", None)),
                               tokens=tokens, prefill=args.prefill, decode=args.decode, decode_ctx=args.decode_ctx,
-                              step_ms=round(step_ms, 3), ops=table)), flush=True)
+                              step_ms=round(plain, 3), step_ms_with_regions=round(step_ms, 3),
+                              host_enqueue_ms=round(host_ms, 3), ops=table)), flush=True)
     if group is not None:
         dist.barrier(group=group)
         dist.destroy_process_group()

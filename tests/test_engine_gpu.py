@@ -89,3 +89,110 @@ def test_native_step_logits_match_reference(tiny_dir, budget):
     assert total == 25
     assert worst < 0.05, worst
     assert agree >= total - 2
+
+
+@pytest.fixture(scope="module")
+def sr_dir(tmp_path_factory):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA")
+    from granite_switch_b200.composer.synthetic import compose_synthetic
+
+    d = str(tmp_path_factory.mktemp("eng_gpu_sr"))
+    compose_synthetic(d, "tiny", num_adapters=3, rank=8, targets=("q", "k", "v", "o", "gate", "up", "down"),
+                      seed=1, dtype=torch.float32, invocation_len=4, alpha=16.0, num_hidden_layers=2,
+                      cross_rank=16, std_b=0.03)
+    return d
+
+
+@pytest.fixture(scope="module")
+def probe_dir(tmp_path_factory):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA")
+    from granite_switch_b200.composer.synthetic import compose_synthetic
+
+    d = str(tmp_path_factory.mktemp("eng_gpu_probe"))
+    compose_synthetic(d, "tiny", num_adapters=3, rank=8, targets=("q", "k", "v", "o"), seed=2,
+                      dtype=torch.float32, invocation_len=4, alpha=16.0, num_hidden_layers=2,
+                      num_probes=2, probe_read_layers=[0, None])
+    return d
+
+
+def _compare_engine(d, prompts, budget, max_tokens=4):
+    """Native executor vs the CPU oracle on the same schedule; returns (worst rel err, agree, total, rows)."""
+    from granite_switch_b200.checkpoint import load_state_dict
+    from granite_switch_b200.config import GraniteSwitchConfig
+    from granite_switch_b200.engine.executor import NativeExecutor, ReferenceExecutor
+    from granite_switch_b200.engine.kv_cache import BlockManager
+    from granite_switch_b200.engine.llm_engine import HostRouter
+    from granite_switch_b200.engine.request import Request, SamplingParams
+    from granite_switch_b200.engine.scheduler import Scheduler
+    from granite_switch_b200.models import GraniteSwitchForCausalLM
+    from granite_switch_b200.models.native import NativeGraniteSwitch
+    from granite_switch_b200._native import check_errors
+
+    cfg = GraniteSwitchConfig.from_pretrained(d)
+    dev = torch.device("cuda")
+    nb = 128
+    nm = NativeGraniteSwitch.from_state_dict(cfg, load_state_dict(d), dev, max_tokens=2048, num_kv_blocks=nb,
+                                             max_seqs=16)
+    nat = NativeExecutor(nm, 1024)
+    ref = ReferenceExecutor(GraniteSwitchForCausalLM.from_pretrained(d).eval(), nb)
+    bm = BlockManager(nb)
+    router = HostRouter(cfg)
+    sch = Scheduler(bm, 8, budget, True, route_fn=router)
+    for p in prompts:
+        sch.add(Request(p, SamplingParams(max_tokens=max_tokens)))
+    worst, agree, total, rows = 0.0, 0, 0, []
+    steps = 0
+    while sch.has_work() and steps < 200:
+        out = sch.schedule()
+        _, ln = nat.compute_logits(out)
+        _, lr = ref.compute_logits(out)
+        torch.cuda.synchronize()
+        j = 0
+        for c in out.chunks:
+            r = c.req
+            r.carry = router(r.all_ids[c.start:c.start + c.num_tokens], r.carry)
+            r.num_computed = c.start + c.num_tokens
+            bm.register_full_blocks(r)
+            if c.needs_sample:
+                a, b = ln[j].float().cpu(), lr[j].float()
+                fin = torch.isfinite(b)
+                assert torch.equal(fin, torch.isfinite(a)), "-inf pattern differs"
+                worst = max(worst, ((a[fin] - b[fin]).abs().max() / b[fin].abs().max()).item())
+                tok = int(b.argmax())
+                agree += int(int(a.argmax()) == tok)
+                total += 1
+                rows.append((a, b))
+                r.output_ids.append(tok)
+                j += 1
+                if len(r.output_ids) >= r.sampling.max_tokens:
+                    sch.finish(r, "length")
+        steps += 1
+    check_errors(dev)
+    return worst, agree, total, rows
+
+
+@pytest.mark.parametrize("budget", [40, 2048])
+def test_native_shadow_residual_matches_reference(sr_dir, budget):
+    worst, agree, total, _ = _compare_engine(sr_dir, _prompts(sr_dir, 4, seed=3), budget)
+    assert total == 16
+    assert worst < 0.05, worst
+    assert agree >= total - 1
+
+
+def test_native_probe_verdict_matches_reference(probe_dir):
+    from granite_switch_b200.config import GraniteSwitchConfig
+
+    cfg = GraniteSwitchConfig.from_pretrained(probe_dir)
+    g = torch.Generator().manual_seed(4)
+    prompts = _prompts(probe_dir, 2, seed=5)
+    for slot in (0, 1, 1):
+        ids = torch.randint(0, 1000, (int(torch.randint(20, 90, (1,), generator=g)),), generator=g).tolist()
+        prompts.append(ids + [cfg.probe_control_token_ids[slot]])
+    worst, agree, total, rows = _compare_engine(probe_dir, prompts, 256, max_tokens=1)
+    assert total == 5
+    assert worst < 0.05, worst
+    assert agree == total
+    n_probe_rows = sum(1 for a, b in rows if torch.isinf(b).any())
+    assert n_probe_rows == 3

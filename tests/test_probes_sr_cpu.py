@@ -102,3 +102,53 @@ def test_sr_kv_is_base_only(sr_dir):
     # before the control token the outputs agree; from it on the adapter stream differs
     torch.testing.assert_close(a.logits[0, :12], b.logits[0, :12], rtol=1e-5, atol=1e-5)
     assert (a.logits[0, 12:] - b.logits[0, 12:]).abs().max() > 1e-3
+
+
+def _sr_prompts(d, n, seed=0):
+    idx = json.load(open(os.path.join(d, "adapter_index.json")))
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for i in range(n):
+        ids = torch.randint(1, 1000, (int(torch.randint(20, 50, (1,), generator=g)),), generator=g).tolist()
+        a = i % 2
+        ids += [idx["adapters"][a]["control_token"]["id"]] + idx["adapters"][a]["invocation_token_ids"][1:]
+        out.append(ids)
+    return out
+
+
+@pytest.mark.parametrize("budget", [16, 512])
+def test_engine_sr_matches_generate(sr_dir, budget):
+    """The paged engine runs the dual stream like the HF-style model (chunked prefill included)."""
+    from granite_switch_b200.engine import LLM, EngineConfig, SamplingParams
+    from granite_switch_b200.models.reference import GraniteSwitchForCausalLM
+
+    prompts = _sr_prompts(sr_dir, 4)
+    llm = LLM(sr_dir, device="cpu", engine_config=EngineConfig(max_num_seqs=3, max_num_batched_tokens=budget,
+                                                               num_kv_blocks=64, max_model_len=256))
+    outs = llm.generate(prompts, SamplingParams(max_tokens=5))
+    m = GraniteSwitchForCausalLM.from_pretrained(sr_dir).eval()
+    for o, p in zip(outs, prompts):
+        ref = m.generate(torch.tensor([p]), max_new_tokens=5)[0, len(p):].tolist()
+        assert o.output_ids == ref
+
+
+def test_engine_probe_verdict(probe_dir):
+    """A request ending in a probe's control token samples from the verdict (one of its labels),
+    exactly as the HF-style model's rewritten logits."""
+    from granite_switch_b200.engine import LLM, EngineConfig, SamplingParams
+    from granite_switch_b200.models.reference import GraniteSwitchForCausalLM
+
+    m = GraniteSwitchForCausalLM.from_pretrained(probe_dir).eval()
+    cfg = m.config
+    g = torch.Generator().manual_seed(11)
+    prompts = []
+    for slot in (0, 1, 0):
+        ids = torch.randint(1, 1000, (int(torch.randint(10, 40, (1,), generator=g)),), generator=g).tolist()
+        prompts.append(ids + [cfg.probe_control_token_ids[slot]])
+    llm = LLM(probe_dir, device="cpu", engine_config=EngineConfig(max_num_seqs=4, max_num_batched_tokens=64,
+                                                                  num_kv_blocks=64, max_model_len=256))
+    outs = llm.generate(prompts, SamplingParams(max_tokens=1))
+    for o, p, slot in zip(outs, prompts, (0, 1, 0)):
+        logits = m(torch.tensor([p])).logits[0, -1]
+        assert o.output_ids == [int(logits.argmax())]
+        assert o.output_ids[0] in cfg.probe_label_token_ids[2 + slot]
