@@ -220,12 +220,16 @@ class NativeExecutor:
         nb = len(hb.rows)
         if nb == 0:
             return []
-        params = [c.req.sampling for c in hb.chunks if c.needs_sample]
         toks = self.d_tokens[:nb]
-        if all(p.greedy for p in params):
-            E.argmax(logits, out=toks)
-        else:
-            sample(logits, params, [c.req for c in hb.chunks if c.needs_sample], out=toks)
+        pipe = self.model.pipeline
+        if pipe is None or self.model.last_stage:
+            params = [c.req.sampling for c in hb.chunks if c.needs_sample]
+            if all(p.greedy for p in params):
+                E.argmax(logits, out=toks)
+            else:
+                sample(logits, params, [c.req for c in hb.chunks if c.needs_sample], out=toks)
+        if pipe is not None:
+            pipe.broadcast_tokens(toks)  # every stage's scheduler sees the sampled ids
         self.h_out[:nb].copy_(toks, non_blocking=True)
         self.copy_event.record()
         self.copy_event.synchronize()

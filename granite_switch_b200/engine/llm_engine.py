@@ -32,6 +32,7 @@ class EngineConfig:
     enable_prefix_caching: bool = True
     enable_chunked_prefill: bool = True
     tensor_parallel_size: int = 1
+    pipeline_parallel_size: int = 1
     use_cuda_graphs: bool = False
     dtype: str = "bfloat16"
     seed: int = 0
@@ -208,7 +209,7 @@ class LLM:
 
     def __init__(self, model: str | GraniteSwitchConfig, device: str | None = None,
                  engine_config: EngineConfig | None = None, random_init: dict | None = None,
-                 tp_rank: int = 0, tp_group=None):
+                 tp_rank: int = 0, tp_group=None, pipeline=None):
         ecfg = engine_config or EngineConfig()
         self.ecfg = ecfg
         if device is None:
@@ -231,20 +232,22 @@ class LLM:
 
                 sd = load_state_dict(path)
                 nm = NativeGraniteSwitch.from_state_dict(config, sd, self.device, max_tokens, 1, tp_rank, tp,
-                                                         tp_group, ecfg.max_num_seqs)
+                                                         tp_group, ecfg.max_num_seqs, pipeline)
                 del sd
             else:
                 ri = dict(random_init or {})
                 nm = NativeGraniteSwitch.from_random(config, self.device, max_tokens, 1, tp_rank=tp_rank,
-                                                     tp_size=tp, tp_group=tp_group, max_seqs=ecfg.max_num_seqs, **ri)
+                                                     tp_size=tp, tp_group=tp_group, max_seqs=ecfg.max_num_seqs,
+                                                     pipeline=pipeline, **ri)
             if ecfg.num_kv_blocks is None:
                 torch.cuda.synchronize()
-                nb = default_num_kv_blocks(0, config, tp, ecfg.gpu_memory_utilization, self.device)
+                nb = default_num_kv_blocks(0, config, tp, ecfg.gpu_memory_utilization, self.device,
+                                           num_layers=nm.num_layers)
             nm.num_kv_blocks = nb
             nm._alloc_buffers()
             self.model = nm
             executor = NativeExecutor(nm, ecfg.max_model_len, tp_group, tp, ecfg.use_cuda_graphs)
-            if ecfg.fused_tp_comm and tp > 1:
+            if ecfg.fused_tp_comm and tp > 1 and pipeline is None:
                 from ..parallel.fused import attach_fused_comm
 
                 attach_fused_comm(nm, tp_group)

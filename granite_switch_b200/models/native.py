@@ -78,7 +78,7 @@ class NativeGraniteSwitch:
 
     def __init__(self, config: GraniteSwitchConfig, device: torch.device, max_tokens: int,
                  num_kv_blocks: int, tp_rank: int = 0, tp_size: int = 1, tp_group=None,
-                 max_seqs: int = 512):
+                 max_seqs: int = 512, pipeline=None):
         self.cfg = config
         self.device = device
         self.tp_rank, self.tp_size, self.tp_group = tp_rank, tp_size, tp_group
@@ -89,7 +89,15 @@ class NativeGraniteSwitch:
         self.num_kv = max(1, config.num_key_value_heads // tp_size)
         self.inter = config.shared_intermediate_size // tp_size
         self.vocab = config.vocab_size
-        self.num_layers = config.num_decoder_layers
+        # pipeline parallelism: this stage owns decoder layers [layer_lo, layer_hi)
+        self.pipeline = pipeline
+        if pipeline is not None:
+            self.layer_lo, self.layer_hi = split_layers(config.num_decoder_layers, pipeline.rank, pipeline.size)
+        else:
+            self.layer_lo, self.layer_hi = 0, config.num_decoder_layers
+        self.first_stage = pipeline is None or pipeline.rank == 0
+        self.last_stage = pipeline is None or pipeline.rank == pipeline.size - 1
+        self.num_layers = self.layer_hi - self.layer_lo
         self.max_tokens = max_tokens
         self.max_seqs = max_seqs
         self.num_kv_blocks = num_kv_blocks
@@ -176,9 +184,12 @@ class NativeGraniteSwitch:
 
     @classmethod
     def from_state_dict(cls, config: GraniteSwitchConfig, sd, device, max_tokens: int, num_kv_blocks: int,
-                        tp_rank: int = 0, tp_size: int = 1, tp_group=None, max_seqs: int = 512):
-        """Pack a composed checkpoint (``sd``: name -> tensor, or a lazy getter)."""
-        self = cls(config, device, max_tokens, num_kv_blocks, tp_rank, tp_size, tp_group, max_seqs)
+                        tp_rank: int = 0, tp_size: int = 1, tp_group=None, max_seqs: int = 512, pipeline=None):
+        """Pack a composed checkpoint (``sd``: name -> tensor, or a lazy getter).
+
+        With ``pipeline`` only this stage's decoder layers are read.
+        """
+        self = cls(config, device, max_tokens, num_kv_blocks, tp_rank, tp_size, tp_group, max_seqs, pipeline)
         get = sd.__getitem__ if isinstance(sd, dict) else sd
         has = (lambda k: k in sd) if isinstance(sd, dict) else (lambda k: True)
         na = config.num_adapters
@@ -202,7 +213,7 @@ class NativeGraniteSwitch:
             return pack_linear(w, la, lb, slices, na, device, swiglu_tile=swiglu, tp_rank=tp_rank,
                                tp_size=tp_size, parallel=parallel)
 
-        for i in range(config.num_decoder_layers):
+        for i in range(self.layer_lo, self.layer_hi):
             p = f"model.layers.{i}."
             self.layers.append(LayerWeights(
                 in_norm=get(p + "input_layernorm.weight").to(device, torch.bfloat16),
@@ -213,7 +224,7 @@ class NativeGraniteSwitch:
                 down=lin(p + "shared_mlp.output_linear", [h], "row"),
             ))
         if self.dual:
-            for i, lw in enumerate(self.layers):
+            for i, lw in zip(range(self.layer_lo, self.layer_hi), self.layers):
                 p = f"model.layers.{i}.cross_stream."
                 lw.cross = self._pack_cross(get(p + "lora_A"), get(p + "lora_B"))
         if has("model.probe_head.weight"):
@@ -232,13 +243,14 @@ class NativeGraniteSwitch:
     @classmethod
     def from_random(cls, config: GraniteSwitchConfig, device, max_tokens: int, num_kv_blocks: int,
                     lora_modules=("qkv",), rank: int = 32, seed: int = 0, std: float = 0.02,
-                    tp_rank: int = 0, tp_size: int = 1, tp_group=None, max_seqs: int = 512):
+                    tp_rank: int = 0, tp_size: int = 1, tp_group=None, max_seqs: int = 512, pipeline=None):
         """Random-init weights of the architecture, generated directly in kernel layout on the GPU.
 
-        Every rank draws the full (unsharded) tensors from the same seed and keeps
-        its shard, so TP runs are numerically the same model as TP=1.
+        Every rank draws the full (unsharded) tensors of every layer from the same
+        seed and keeps its shard (and, under pipeline parallelism, its stage's
+        layers), so TP / PP runs are numerically the same model as one GPU.
         """
-        self = cls(config, device, max_tokens, num_kv_blocks, tp_rank, tp_size, tp_group, max_seqs)
+        self = cls(config, device, max_tokens, num_kv_blocks, tp_rank, tp_size, tp_group, max_seqs, pipeline)
         g = torch.Generator(device=device).manual_seed(seed)
         na = config.num_adapters
         h, d = config.hidden_size, config.head_dim_eff
@@ -260,19 +272,23 @@ class NativeGraniteSwitch:
             return pack_linear(w, la, lb, n_out_slices, na, device, swiglu_tile=swiglu, tp_rank=tp_rank,
                                tp_size=tp_size, parallel=parallel)
 
-        for _ in range(config.num_decoder_layers):
-            self.layers.append(LayerWeights(
+        for i in range(config.num_decoder_layers):
+            lw = LayerWeights(
                 in_norm=torch.ones(h, dtype=torch.bfloat16, device=device),
                 post_norm=torch.ones(h, dtype=torch.bfloat16, device=device),
                 qkv=lin([q, kv, kv], h, "column", "qkv" in lora_modules),
                 o=lin([h], q, "row", "o" in lora_modules),
                 gu=lin([inter, inter], h, "column", "gu" in lora_modules, swiglu=tiles),
                 down=lin([h], inter, "row", "down" in lora_modules),
-            ))
+            )
+            if self.layer_lo <= i < self.layer_hi:
+                self.layers.append(lw)
         if self.dual and na > 0:
             rc = int(config.cross_stream_rank or 32)
-            for lw in self.layers:
-                lw.cross = self._pack_cross(rnd(na, 1, rc, h).float().cpu(), rnd(na, 1, h, rc, s=0.01).float().cpu())
+            for i in range(config.num_decoder_layers):
+                cross = self._pack_cross(rnd(na, 1, rc, h).float().cpu(), rnd(na, 1, h, rc, s=0.01).float().cpu())
+                if self.layer_lo <= i < self.layer_hi:
+                    self.layers[i - self.layer_lo].cross = cross
         if config.probe_control_token_ids:
             lmax = max(1, config.max_probe_labels)
             self._set_probes(rnd(na, lmax, h, s=0.1), torch.randn(na, lmax, generator=g, device=device))
@@ -408,12 +424,18 @@ class NativeGraniteSwitch:
         nat = native()
         R = self._region
         with R("routing+embed"):
+            # every pipeline stage recomputes the routing metadata from the ids
             if self.n_maps:
                 nat.routing(b.ids, b.seq_starts, b.carry_in, self.expert_tbl, None, self.kind_lut,
                             self.num_adapters, self.remaps, self.adapter_idx[:t], self.lora_idx[:t],
                             self.mod_ids[:t], self.carry_out[: b.num_seqs], self.row_adapter[:, :t],
                             self.tile_mask[:, : (t + 127) // 128])
-            E.embed(b.ids, self.embed_w, self.lut, cfg.embedding_multiplier, out=self.h[:t])
+            if self.first_stage:
+                E.embed(b.ids, self.embed_w, self.lut, cfg.embedding_multiplier, out=self.h[:t])
+        if not self.first_stage:
+            with R("pp_recv"):
+                self.pipeline.recv(self.h[:t], self.hbase[:t] if self.dual else None,
+                                   self.verdict if self.probe_w is not None else None)
         h, x = self.h[:t], self.x[:t]
         qkv, attn, act = self.qkv[:t], self.attn[:t], self.act[:t]
         mult = float(cfg.residual_multiplier)
@@ -458,7 +480,12 @@ class NativeGraniteSwitch:
                     with R("down"):
                         self._row_parallel(lw.down, act, h, mult)
                 if probes:
-                    self._probe_layer(b, li, h)
+                    self._probe_layer(b, self.layer_lo + li, h)
+        if not self.last_stage:
+            with R("pp_send"):
+                self.pipeline.send(h, self.hbase[:t] if self.dual else None,
+                                   self.verdict if self.probe_w is not None else None)
+            return None
         nb = b.logit_rows.numel()
         if nb == 0:
             return None
@@ -500,7 +527,8 @@ class NativeGraniteSwitch:
         R = self._region
         t = b.num_tokens
         hb = self.hbase[:t]
-        hb.copy_(h)
+        if self.first_stage:
+            hb.copy_(h)  # both streams start from the embedding
         qa = self.qa[:t]
         q_n = self.num_q * self.head_dim
         eps = cfg.rms_norm_eps
@@ -543,7 +571,7 @@ class NativeGraniteSwitch:
             with R("cross_stream"):
                 self._cross_stream(lw.cross, hb, h)
             if b.probe_groups:
-                self._probe_layer(b, li, h)
+                self._probe_layer(b, self.layer_lo + li, h)
 
     def attention_plans(self, q_lens: list[int], kv_lens: list[int]) -> list[tuple[list[int], list[int], int, int]]:
         """Split requests into decode-layout and prefill-layout CTA work lists."""
@@ -568,12 +596,20 @@ class NativeGraniteSwitch:
         return plans
 
 
+def split_layers(num_layers: int, stage: int, stages: int) -> tuple[int, int]:
+    """Contiguous layer range of a pipeline stage; earlier stages take the remainder."""
+    base, extra = divmod(num_layers, stages)
+    lo = stage * base + min(stage, extra)
+    return lo, lo + base + (1 if stage < extra else 0)
+
+
 def default_num_kv_blocks(model_bytes: int, cfg: GraniteSwitchConfig, tp_size: int, mem_fraction: float = 0.85,
-                          device=None, reserve_bytes: int = 6 << 30, cap_blocks: int | None = None) -> int:
+                          device=None, reserve_bytes: int = 6 << 30, cap_blocks: int | None = None,
+                          num_layers: int | None = None) -> int:
     free, total = torch.cuda.mem_get_info(device)
     d = cfg.head_dim_eff
     kv_heads = max(1, cfg.num_key_value_heads // tp_size)
-    per_block = cfg.num_decoder_layers * 2 * kv_heads * 16 * d * 2
+    per_block = (num_layers or cfg.num_decoder_layers) * 2 * kv_heads * 16 * d * 2
     budget = int(total * mem_fraction) - (total - free) - reserve_bytes
     n = max(64, budget // per_block)
     if cap_blocks is not None:
@@ -581,4 +617,4 @@ def default_num_kv_blocks(model_bytes: int, cfg: GraniteSwitchConfig, tp_size: i
     return int(n)
 
 
-__all__ = ["NativeGraniteSwitch", "StepBatch", "AttnPlan", "default_num_kv_blocks", "math"]
+__all__ = ["NativeGraniteSwitch", "StepBatch", "AttnPlan", "default_num_kv_blocks", "split_layers", "math"]

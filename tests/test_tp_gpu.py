@@ -45,3 +45,17 @@ def test_tp2_matches_tp1():
     print(r.stdout[-4000:], r.stderr[-4000:])
     assert r.returncode == 0, r.stderr[-2000:]
     assert '"mode": "nccl"' in r.stdout
+
+
+@pytest.mark.multigpu
+def test_pp2_matches_single_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29535", "-m",
+           "granite_switch_b200.parallel.pp_check"]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)
+    print(r.stdout[-4000:], r.stderr[-4000:])
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert '"ok": true' in r.stdout

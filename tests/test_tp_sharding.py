@@ -100,3 +100,13 @@ def test_adapter_not_touching_module_is_dropped():
     lb[0][1] = 0.5
     pl = pack_linear(torch.randn(n, k), la, lb, [n], na, "cpu", dtype=torch.float32)
     assert pl.n_local == 1 and pl.remap == [0, 0, 1, 0]
+
+
+def test_pipeline_layer_split():
+    from granite_switch_b200.models.native import split_layers
+
+    assert [split_layers(40, s, 2) for s in range(2)] == [(0, 20), (20, 40)]
+    assert [split_layers(10, s, 3) for s in range(3)] == [(0, 4), (4, 7), (7, 10)]
+    spans = [split_layers(7, s, 4) for s in range(4)]
+    assert spans[0][0] == 0 and spans[-1][1] == 7
+    assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
