@@ -59,6 +59,12 @@ def launch_count() -> int:
     return _LAUNCHES
 
 
+def add_launches(n: int) -> None:
+    """Account for ``n`` kernel launches issued by a CUDA-graph replay."""
+    global _LAUNCHES
+    _LAUNCHES += n
+
+
 def native():
     """Return the loaded extension (through the counting proxy), importing it on first use."""
     global _C

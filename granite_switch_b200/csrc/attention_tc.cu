@@ -1,4 +1,5 @@
-// Prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+// Prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA),
+// head_dim 64 or 128.
 //
 // One CTA owns 128 query rows of one request and one KV head (a row is a
 // (query token, query head of the GQA group) pair, as in attention.cu) and
@@ -364,7 +365,7 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
   GSB_CHECK(k_cache.dim() == 4 && k_cache.size(2) == 16 && k_cache.is_contiguous() && v_cache.is_contiguous(),
             "attention_tc: caches must be contiguous [num_blocks, Hkv, 16, D]");
   const int Hkv = (int)k_cache.size(1), D = (int)k_cache.size(3), Hq = (int)num_q_heads;
-  GSB_CHECK(D == 128, "attention_tc: head_dim 128 only (64 uses the mma.sync kernel)");
+  GSB_CHECK(D == 128 || D == 64, "attention_tc: head_dim must be 64 or 128, got ", D);
   GSB_CHECK(Hq % Hkv == 0, "attention_tc: Hq must be a multiple of Hkv");
   GSB_CHECK(q.stride(1) == 1 && (q.stride(0) % 8) == 0 && out.stride(1) == 1 && (out.stride(0) % 8) == 0,
             "attention_tc: q/out rows must be 16-byte aligned");
@@ -376,16 +377,16 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
   auto st = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
   CUtensorMap tk = make_tmap_bf16_2d(k_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
-  using C = FaCfg<128, 64>;
   GSB_CHECK(n_work < 65536, "attention_tc: too many work tiles");
   dim3 grid(Hkv, n_work);
-  auto kfn = fa_prefill_kernel<128, 64>;
-  static bool configured = false;
-  if (!configured) {
-    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    configured = true;
+  auto kfn = (D == 128) ? fa_prefill_kernel<128, 64> : fa_prefill_kernel<64, 64>;
+  const int smem = (D == 128) ? FaCfg<128, 64>::SMEM : FaCfg<64, 64>::SMEM;
+  static bool configured[2] = {false, false};
+  if (!configured[D == 128]) {
+    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured[D == 128] = true;
   }
-  kfn<<<grid, 192, C::SMEM, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
+  kfn<<<grid, 192, smem, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
                                   block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
                                   q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
                                   work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv,

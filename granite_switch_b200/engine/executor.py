@@ -99,7 +99,26 @@ class HostBatch:
         self.rows = (cu[1:] - 1)[sample]
 
 
+GRAPH_BUCKETS = (8, 16, 32, 64, 128, 256, 512)
+
+
+class _DecodeGraph:
+    """One captured decode step for a padded batch of ``size`` single-token rows."""
+
+    def __init__(self, size: int, graph, logits, launches: int, work):
+        self.size, self.graph, self.logits, self.launches, self.work = size, graph, logits, launches, work
+
+
 class NativeExecutor:
+    """Stages a scheduler step into persistent device buffers and runs the native model.
+
+    With ``use_cuda_graphs``, decode-only steps (every chunk one token) on one
+    GPU replay a CUDA graph captured per padded batch size (8, 16, ... up to
+    ``max_seqs``): the inputs are staged into the same device buffers, padding
+    rows point at a scratch KV page and are not sampled, and the whole forward
+    (routing, every layer, LM head) is one graph launch. Other steps run eagerly.
+    """
+
     def __init__(self, model, max_model_len: int, tp_group=None, tp_size: int = 1, use_cuda_graphs: bool = False):
         self.model = model
         self.device = model.device
@@ -129,6 +148,90 @@ class NativeExecutor:
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.gather_buf = None
+        self.use_cuda_graphs = bool(use_cuda_graphs) and tp_size == 1 and model.pipeline is None
+        self.graphs: dict[int, _DecodeGraph] = {}
+        self.graph_replays = 0
+
+    # ------------------------------------------------------------------ CUDA graphs
+    def _graph_bucket(self, out: SchedulerOutput) -> int | None:
+        if not self.use_cuda_graphs or not out.is_decode_only:
+            return None
+        n = len(out.chunks)
+        for b in GRAPH_BUCKETS:
+            if n <= b <= self.model.max_seqs and b <= self.model.max_tokens:
+                return b
+        return None
+
+    def _stage_graph(self, hb: HostBatch, p: int) -> None:
+        """Stage a decode step padded to ``p`` rows at the fixed offsets the graphs read."""
+        s = len(hb.ids)
+        m = self.model
+        if self.h2d_pending:
+            self.h2d_event.synchronize()
+        i64, i32 = self.np_i64, self.np_i32
+        scratch = m.scratch_block * BLOCK_SIZE
+        i64[:s] = hb.ids
+        i64[s:p] = 0
+        i64[p:p + s] = hb.pos
+        i64[p + s:2 * p] = 0
+        i64[2 * p:2 * p + s] = hb.slots
+        i64[2 * p + s:3 * p] = scratch
+        i32[: p + 1] = np.arange(p + 1, dtype=np.int32)
+        i32[p + 1:p + 1 + s] = hb.carry
+        i32[p + 1 + s:2 * p + 1] = 0
+        i32[2 * p + 1:2 * p + 1 + s] = hb.kv_lens
+        i32[2 * p + 1 + s:3 * p + 1] = 1
+        width = hb.bt.shape[1]
+        if width > self.max_blocks:
+            raise ValueError(f"block table width {width} exceeds max_model_len blocks {self.max_blocks}")
+        self.np_bt[:s, :width] = hb.bt
+        self.np_bt[:s, width:] = 0
+        self.np_bt[s:p, :] = m.scratch_block
+        self.np_rows[:p] = np.arange(p)
+        self.d_i64[: 3 * p].copy_(self.h_i64[: 3 * p], non_blocking=True)
+        self.d_i32[: 3 * p + 1].copy_(self.h_i32[: 3 * p + 1], non_blocking=True)
+        self.d_bt[:p].copy_(self.h_bt[:p], non_blocking=True)
+        self.d_rows[:p].copy_(self.h_rows[:p], non_blocking=True)
+        self.h2d_event.record()
+        self.h2d_pending = True
+        self.h2d_bytes += 8 * 3 * p + 4 * (3 * p + 1) + 4 * p * self.max_blocks + 8 * p
+
+    def _graph_batch(self, p: int, work):
+        from ..models.native import AttnPlan, StepBatch
+
+        return StepBatch(num_tokens=p, num_seqs=p, ids=self.d_i64[:p], positions=self.d_i64[p:2 * p],
+                         slots=self.d_i64[2 * p:3 * p], seq_starts=self.d_i32[: p + 1],
+                         carry_in=self.d_i32[p + 1:2 * p + 1], kv_lens=self.d_i32[2 * p + 1:3 * p + 1],
+                         block_table=self.d_bt[:p], logit_rows=self.d_rows[:p],
+                         plans=[AttnPlan(work[0], work[1], 16, work[2])])
+
+    def _run_graph(self, hb: HostBatch, p: int) -> torch.Tensor:
+        from .. import _native
+        from ..ops import attention as A
+
+        self._stage_graph(hb, p)
+        g = self.graphs.get(p)
+        if g is None:
+            m = self.model
+            ws, wr = A.build_work([1] * p, m.num_q // m.num_kv, 16)
+            ns = A.choose_splits(p * m.num_kv, self.max_blocks * BLOCK_SIZE)
+            if ns > 1 and p > m.ws_tokens:
+                ns = 1
+            work = (torch.tensor(ws, dtype=torch.int32, device=self.device),
+                    torch.tensor(wr, dtype=torch.int32, device=self.device), ns)
+            batch = self._graph_batch(p, work)
+            m.forward(batch)  # eager warm-up: one-time kernel set-up happens outside the capture
+            torch.cuda.synchronize(self.device)
+            graph = torch.cuda.CUDAGraph()
+            before = _native.launch_count()
+            with torch.cuda.graph(graph):
+                logits = m.forward(batch)
+            launches = _native.launch_count() - before
+            g = self.graphs[p] = _DecodeGraph(p, graph, logits, launches, work)
+        g.graph.replay()
+        _native.add_launches(g.launches)
+        self.graph_replays += 1
+        return g.logits[: len(hb.rows)]
 
     def _stage(self, hb: HostBatch):
         from ..models.native import AttnPlan, StepBatch
@@ -206,6 +309,10 @@ class NativeExecutor:
     def compute_logits(self, out: SchedulerOutput):
         """Run the step; returns ``(HostBatch, fp32 logits [B, vocab])`` for rows that sample."""
         hb = HostBatch(out)
+        p = self._graph_bucket(out)
+        if p is not None:
+            logits = self._run_graph(hb, p)
+            return hb, self._gather_logits(logits)
         batch = self._stage(hb)
         logits = self.model.forward(batch)
         if not len(hb.rows) or logits is None:

@@ -263,7 +263,18 @@ class LLM:
             self.model = ref
         self.engine = LLMEngine(config, executor, nb, ecfg)
 
-    def generate(self, prompts: list[list[int]], sampling: SamplingParams | list[SamplingParams] | None = None) -> list[RequestOutput]:
+    def generate(self, prompts: list[list[int]], sampling: SamplingParams | list[SamplingParams] | None = None,
+                 audios: list | None = None, audio_processor=None) -> list[RequestOutput]:
+        """Generate for token-id prompts.
+
+        ``audios[i]`` (with ``audio_processor``, an
+        :class:`~granite_switch_b200.audio.AudioPromptProcessor`) lists prompt
+        ``i``'s clips; each ``<|audio|>`` marker is replaced by its transcript.
+        """
+        if audios is not None:
+            if audio_processor is None:
+                raise ValueError("audios given without an audio_processor")
+            prompts = [audio_processor.expand(p, a) for p, a in zip(prompts, audios)]
         sps = sampling if isinstance(sampling, list) else [sampling or SamplingParams()] * len(prompts)
         reqs = [self.engine.add_request(p, sp) for p, sp in zip(prompts, sps)]
         while self.engine.has_unfinished():

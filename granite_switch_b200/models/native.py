@@ -105,7 +105,7 @@ class NativeGraniteSwitch:
         self.remaps: torch.Tensor | None = None
         self.comm = None  # optional fused-collective communicator
         self.prof = None  # optional per-op CUDA-event profiler (utils.step_profile.StepProfiler)
-        # prefill attention on tcgen05 (head_dim 128); GSB_ATTN_TC=0 selects the mma.sync kernel
+        # prefill attention on tcgen05 (head_dim 64 / 128); GSB_ATTN_TC=0 selects the mma.sync kernel
         self.use_tc_attention = os.environ.get("GSB_ATTN_TC", "1") != "0"
         self.err = err_buffer(device)
         na = config.num_adapters
@@ -306,7 +306,10 @@ class NativeGraniteSwitch:
         t, dev = self.max_tokens, self.device
         bf = torch.bfloat16
         qkv_n = (self.num_q + 2 * self.num_kv) * self.head_dim
-        self.kv_cache = torch.zeros(self.num_layers, 2, self.num_kv_blocks, self.num_kv, 16, self.head_dim,
+        # one extra block past the managed ones: a scratch page for padding rows of
+        # CUDA-graph decode steps (the block manager never hands it out)
+        self.scratch_block = self.num_kv_blocks
+        self.kv_cache = torch.zeros(self.num_layers, 2, self.num_kv_blocks + 1, self.num_kv, 16, self.head_dim,
                                     dtype=bf, device=dev)
         self.h = torch.empty(t, self.hidden, dtype=bf, device=dev)
         self.h2 = torch.empty(t, self.hidden, dtype=bf, device=dev) if self.tp_size > 1 else None
@@ -579,7 +582,7 @@ class NativeGraniteSwitch:
         dec = [i for i, ql in enumerate(q_lens) if ql * g <= 16]
         pre = [i for i, ql in enumerate(q_lens) if ql * g > 16]
         plans = []
-        pre_rows = 128 if (self.head_dim == 128 and self.use_tc_attention) else 64
+        pre_rows = 128 if (self.head_dim in (64, 128) and self.use_tc_attention) else 64
         for idx, rows in ((dec, 16), (pre, pre_rows)):
             if not idx:
                 continue

@@ -84,6 +84,7 @@ def main():
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--no-fused-comm", dest="fused", action="store_false")
+    p.add_argument("--lora", nargs="*", default=["qkv", "o"], help="projections with adapters")
     args = p.parse_args()
 
     import torch.distributed as dist
@@ -116,7 +117,7 @@ def main():
                         max_model_len=max(args.prefill + [args.decode_ctx + 1]) + 16, tensor_parallel_size=world,
                         num_kv_blocks=need_blocks, fused_tp_comm=args.fused)
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
-              random_init=dict(lora_modules=("qkv", "o"), rank=32), tp_rank=rank, tp_group=group)
+              random_init=dict(lora_modules=tuple(args.lora), rank=32), tp_rank=rank, tp_group=group)
     eng = llm.engine
     out = build_step(eng, args.prefill, args.decode, args.decode_ctx, base["vocab_size"])
     ex = eng.executor

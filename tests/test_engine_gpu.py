@@ -196,3 +196,20 @@ def test_native_probe_verdict_matches_reference(probe_dir):
     assert agree == total
     n_probe_rows = sum(1 for a, b in rows if torch.isinf(b).any())
     assert n_probe_rows == 3
+
+
+def test_cuda_graph_decode_matches_eager(tiny_dir):
+    """Decode steps replayed from CUDA graphs (padded batch buckets) give the eager engine's tokens."""
+    from granite_switch_b200.engine import LLM, EngineConfig, SamplingParams
+
+    prompts = _prompts(tiny_dir, 11, seed=9)
+    outs = {}
+    for graphs in (False, True):
+        ecfg = EngineConfig(max_num_seqs=16, max_num_batched_tokens=512, num_kv_blocks=256, max_model_len=512,
+                            use_cuda_graphs=graphs)
+        llm = LLM(tiny_dir, device="cuda:0", engine_config=ecfg)
+        outs[graphs] = [o.output_ids for o in llm.generate(prompts, SamplingParams(max_tokens=12))]
+        if graphs:
+            ex = llm.engine.executor
+            assert ex.graph_replays > 0 and set(ex.graphs) <= {8, 16}
+    assert outs[True] == outs[False]

@@ -182,11 +182,12 @@ def test_paged_attention(d, mode, nsplit):
     _check()
 
 
+@pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("case", ["fresh", "cached_prefix", "mixed"])
-def test_prefill_attention_tcgen05(case):
+def test_prefill_attention_tcgen05(case, d):
     from granite_switch_b200.ops import attention as A
 
-    hq, hkv, d = 8, 2, 128
+    hq, hkv = 8, 2
     g = hq // hkv
     if case == "fresh":
         q_lens, kv_lens = [130, 64, 5], [130, 64, 5]
