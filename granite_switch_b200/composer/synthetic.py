@@ -46,6 +46,14 @@ def base_config(preset: str | dict, **overrides) -> dict:
     return cfg
 
 
+def _mlp_size(cfg: dict) -> int:
+    """Width of the dense (shared) MLP: intermediate_size for dense bases; for
+    mixture-of-experts bases shared_intermediate_size (0 = no shared MLP)."""
+    if int(cfg.get("num_local_experts", 0) or 0):
+        return int(cfg.get("shared_intermediate_size") or 0)
+    return int(cfg["intermediate_size"])
+
+
 def _shapes(cfg: dict) -> dict[str, tuple[int, int]]:
     h, hd = cfg["hidden_size"], cfg["head_dim"]
     q, kv, i = cfg["num_attention_heads"] * hd, cfg["num_key_value_heads"] * hd, cfg["intermediate_size"]
@@ -65,13 +73,25 @@ def random_base_state(cfg: dict, seed: int = 0, std: float = 0.02, dtype=torch.f
     if not cfg.get("tie_word_embeddings", True):
         sd["lm_head.weight"] = rnd(cfg["vocab_size"], cfg["hidden_size"])
     sd["model.norm.weight"] = torch.ones(cfg["hidden_size"], dtype=dtype)
-    shp = _shapes(cfg)
+    n_exp = int(cfg.get("num_local_experts", 0) or 0)
+    h = cfg["hidden_size"]
+    # mixture-of-experts bases: experts use intermediate_size, the optional shared
+    # MLP (dense mlp.* names) uses shared_intermediate_size
+    shared = _mlp_size(cfg)
+    shp = _shapes(dict(cfg, intermediate_size=shared)) if shared else _shapes(cfg)
     for i in range(cfg["num_hidden_layers"]):
         p = f"model.layers.{i}."
-        sd[p + "input_layernorm.weight"] = torch.ones(cfg["hidden_size"], dtype=dtype)
-        sd[p + "post_attention_layernorm.weight"] = torch.ones(cfg["hidden_size"], dtype=dtype)
+        sd[p + "input_layernorm.weight"] = torch.ones(h, dtype=dtype)
+        sd[p + "post_attention_layernorm.weight"] = torch.ones(h, dtype=dtype)
         for k, mod in _MODS.items():
+            if k in ("gate", "up", "down") and not shared:
+                continue
             sd[p + mod + ".weight"] = rnd(*shp[k])
+        if n_exp:
+            ie = cfg["intermediate_size"]
+            sd[p + "block_sparse_moe.experts.gate_up_proj"] = rnd(n_exp, 2 * ie, h)
+            sd[p + "block_sparse_moe.experts.down_proj"] = rnd(n_exp, h, ie)
+            sd[p + "block_sparse_moe.router.weight"] = rnd(n_exp, h) * 10.0
     return sd
 
 
@@ -79,7 +99,10 @@ def random_peft_adapter(cfg: dict, rank: int, targets=("q", "k", "v"), seed: int
                         std_b: float = 0.01, dtype=torch.float32, cross_rank: int = 0) -> dict[str, torch.Tensor]:
     """PEFT-named random LoRA tensors; ``cross_rank > 0`` adds a Shadow-Residual ``cross_stream``."""
     g = torch.Generator().manual_seed(seed)
-    shp = _shapes(cfg)
+    shared = _mlp_size(cfg)
+    shp = _shapes(dict(cfg, intermediate_size=shared or cfg["intermediate_size"]))
+    if not shared:  # no dense MLP to adapt
+        targets = [t for t in targets if t not in ("gate", "up", "down")]
     out = {}
     for i in range(cfg["num_hidden_layers"]):
         for t in targets:

@@ -22,5 +22,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_residual_from", &gsb_rmsnorm_residual_from, "h <- y; x <- rmsnorm(y); y <- 0");
   m.def("probe_verdict", &gsb_probe_verdict, "probe-head scores at marker rows");
   m.def("probe_rewrite", &gsb_probe_rewrite, "replace marker logit rows by the probe verdict");
+  m.def("moe_route", &gsb_moe_route, "MoE top-k routing, softmax and per-expert segment plan");
+  m.def("moe_scatter", &gsb_moe_scatter, "MoE token rows into their experts' segments");
+  m.def("moe_combine", &gsb_moe_combine, "MoE weighted sum of expert outputs (+ shared MLP, residual)");
+  m.def("residual_axpy", &gsb_residual_axpy, "h <- h + y * scale");
   m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode)");
 }

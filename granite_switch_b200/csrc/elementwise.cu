@@ -327,3 +327,31 @@ void gsb_argmax(const at::Tensor& logits, const at::Tensor& out) {
                                                    (int)logits.size(1), out.data_ptr<int64_t>());
   GSB_CUDA_CHECK(cudaGetLastError());
 }
+
+namespace gsb {
+__global__ void residual_axpy_kernel(__nv_bfloat16* __restrict__ h, int64_t ldh, const __nv_bfloat16* __restrict__ y,
+                                     int64_t ldy, int H, float scale) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x * 2; c < H; c += blockDim.x * 2) {
+    uint32_t* hp = reinterpret_cast<uint32_t*>(h + (int64_t)t * ldh + c);
+    const float2 a = unpack_bf16x2(*hp);
+    const float2 b = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(y + (int64_t)t * ldy + c));
+    *hp = pack_bf16x2(a.x + b.x * scale, a.y + b.y * scale);
+  }
+}
+}  // namespace gsb
+
+// h <- h + y * scale (bf16 rows; the residual add after a reduced MLP output).
+void gsb_residual_axpy(const at::Tensor& h, const at::Tensor& y, double scale) {
+  using namespace gsb;
+  GSB_CHECK(h.scalar_type() == at::kBFloat16 && y.scalar_type() == at::kBFloat16 && h.sizes() == y.sizes() &&
+                h.size(1) % 2 == 0 && h.stride(1) == 1 && y.stride(1) == 1,
+            "residual_axpy: matching bf16 [T, H] tensors required");
+  const int T = (int)h.size(0);
+  if (T == 0) return;
+  c10::cuda::CUDAGuard g(h.device());
+  residual_axpy_kernel<<<T, 256, 0, cur_stream(h)>>>(reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), h.stride(0),
+                                                     reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
+                                                     (int)h.size(1), (float)scale);
+  GSB_CUDA_CHECK(cudaGetLastError());
+}

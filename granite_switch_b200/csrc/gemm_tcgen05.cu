@@ -76,6 +76,12 @@ struct GemmEpiArgs {
                                // epilogue stores, bit 1 re-reads K block 0 (L2-resident)
 };
 
+// Grouped mode (mixture-of-experts): W is a stack [E, N, K] and every 128-row
+// tile of X belongs to one expert (tile_expert[mt]; -1 = no rows, skipped).
+struct GemmGroupArgs {
+  const int32_t* tile_expert;  // null: plain GEMM
+};
+
 // A shrink tile is skipped when none of the adapters owning its columns has a
 // row in its 128-row tile: the expand never reads those columns for that tile.
 template <int BN>
@@ -85,6 +91,12 @@ __device__ __forceinline__ bool shrink_tile_skipped(const GemmEpiArgs& epi, int 
   for (int c = 0; c < BN; c += epi.mask_rank)
     need |= 1ull << (((n0 + c) / epi.mask_rank) % epi.mask_num_adapters);
   return (epi.skip_mask[mt] & need) == 0;
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ bool tile_skipped(const GemmEpiArgs& epi, const GemmGroupArgs& grp, int mt, int n0) {
+  if (grp.tile_expert != nullptr && grp.tile_expert[mt] < 0) return true;
+  return EPI == kEpiMaskAdapter && shrink_tile_skipped<BN>(epi, mt, n0);
 }
 
 // Shared memory of the staged epilogue: two 4 KB buffers (32 rows x 64 bf16,
@@ -391,7 +403,7 @@ __global__ void __launch_bounds__(192, 1)
                          const __grid_constant__ CUtensorMap tm_s,
                          const __grid_constant__ CUtensorMap tm_lb,
                          const __grid_constant__ CUtensorMap tm_out, int M, int N, int K,
-                         GemmLoraArgs lora, GemmEpiArgs epi, uint32_t* err) {
+                         GemmLoraArgs lora, GemmEpiArgs epi, GemmGroupArgs grp, uint32_t* err) {
   using C = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -449,7 +461,7 @@ __global__ void __launch_bounds__(192, 1)
         int mt, nt;
         gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
         const int m0 = mt * C::BM, n0 = nt * BN;
-        if (EPI == kEpiMaskAdapter && shrink_tile_skipped<BN>(epi, mt, n0)) continue;
+        if (tile_skipped<BN, EPI>(epi, grp, mt, n0)) continue;
         const LoraTile lt = lora_tile<SPLIT>(lora, mt, n0);
         const int total = main_blocks + lt.blocks;
         uint64_t rem = lt.amask;
@@ -467,7 +479,10 @@ __global__ void __launch_bounds__(192, 1)
           if (i < main_blocks) {
             mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
             tma_load_2d(sa, &tm_a, &full_bar[s], i * C::BK, m0);
-            tma_load_2d(sb, &tm_b, &full_bar[s], i * C::BK, n0);
+            if (grp.tile_expert != nullptr)
+              tma_load_3d(sb, &tm_b, &full_bar[s], i * C::BK, n0, grp.tile_expert[mt]);
+            else
+              tma_load_2d(sb, &tm_b, &full_bar[s], i * C::BK, n0);
           } else {
             if (rb == 0) a_bit = __ffsll((long long)rem) - 1;
             const int kcol = a_bit * lora.rank_blocks * 32 + rb * 32;
@@ -501,7 +516,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x) {
         int mt, nt;
         gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
-        if (EPI == kEpiMaskAdapter && shrink_tile_skipped<BN>(epi, mt, nt * BN)) continue;
+        if (tile_skipped<BN, EPI>(epi, grp, mt, nt * BN)) continue;
         const LoraTile lt = lora_tile<SPLIT>(lora, mt, nt * BN);
         const int total = main_blocks + lt.blocks;
         const int acc = ltile & 1;
@@ -558,7 +573,7 @@ __global__ void __launch_bounds__(192, 1)
       int mt, nt;
       gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
       const int m0 = mt * C::BM, n0 = nt * BN;
-      if (EPI == kEpiMaskAdapter && shrink_tile_skipped<BN>(epi, mt, n0)) continue;
+      if (tile_skipped<BN, EPI>(epi, grp, mt, n0)) continue;
       const int acc = ltile & 1;
       if (*abort_flag || !mbar_wait(&tfull_bar[acc], (ltile >> 1) & 1, err, kErrGemmWait)) {
         *abort_flag = 1;
@@ -870,7 +885,7 @@ static int num_sms_for_current_device() {
 template <int BN, int EPI, bool SPLIT>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ts,
                         const CUtensorMap& tlb, const CUtensorMap& to, int M, int N, int K, const GemmLoraArgs& lora,
-                        const GemmEpiArgs& epi, uint32_t* err, cudaStream_t stream) {
+                        const GemmEpiArgs& epi, const GemmGroupArgs& grp, uint32_t* err, cudaStream_t stream) {
   using C = GemmCfg<BN>;
   auto kfn = switched_gemm_kernel<BN, EPI, SPLIT>;
   static bool configured = false;  // per instantiation; attribute is per-function
@@ -880,7 +895,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   }
   const int tiles = (N / BN) * ((M + C::BM - 1) / C::BM);
   const int grid = std::min(tiles, num_sms_for_current_device());
-  kfn<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err);
+  kfn<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, err);
   GSB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -957,15 +972,15 @@ template <int BN>
 static void dispatch_epi(int epi_kind, const CUtensorMap& ta, const CUtensorMap& tb,
                          const CUtensorMap& ts, const CUtensorMap& tlb, const CUtensorMap& to,
                          int M, int N, int K,
-                         const GemmLoraArgs& lora, const GemmEpiArgs& epi, uint32_t* err,
+                         const GemmLoraArgs& lora, const GemmEpiArgs& epi, const GemmGroupArgs& grp, uint32_t* err,
                          cudaStream_t st) {
   switch (epi_kind) {
-    case kEpiStore: launch_gemm<BN, kEpiStore, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
-    case kEpiResAdd: launch_gemm<BN, kEpiResAdd, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
-    case kEpiSwiGLU: launch_gemm<BN, kEpiSwiGLU, true>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
-    case kEpiMaskAdapter: launch_gemm<BN, kEpiMaskAdapter, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
-    case kEpiF32: launch_gemm<BN, kEpiF32, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
-    case kEpiMultimemRed: launch_gemm<BN, kEpiMultimemRed, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err, st); break;
+    case kEpiStore: launch_gemm<BN, kEpiStore, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, err, st); break;
+    case kEpiResAdd: launch_gemm<BN, kEpiResAdd, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, err, st); break;
+    case kEpiSwiGLU: launch_gemm<BN, kEpiSwiGLU, true>(ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, err, st); break;
+    case kEpiMaskAdapter: launch_gemm<BN, kEpiMaskAdapter, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, err, st); break;
+    case kEpiF32: launch_gemm<BN, kEpiF32, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, err, st); break;
+    case kEpiMultimemRed: launch_gemm<BN, kEpiMultimemRed, false>(ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, err, st); break;
     default: GSB_CHECK(false, "unknown epilogue kind ", epi_kind);
   }
 }
@@ -982,15 +997,26 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
                        const c10::optional<at::Tensor>& tile_mask, int64_t rank,
                        int64_t num_adapters, std::vector<int64_t> slice_bounds,
                        const c10::optional<at::Tensor>& row_adapter, int64_t mask_rank,
-                       int64_t mask_num_adapters, const at::Tensor& err, int64_t mc_out) {
+                       int64_t mask_num_adapters, const at::Tensor& err, int64_t mc_out,
+                       const c10::optional<at::Tensor>& tile_expert) {
   using namespace gsb;
   GSB_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "tensors must be on CUDA");
   GSB_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
             "x and w must be bf16");
-  GSB_CHECK(x.dim() == 2 && w.dim() == 2 && x.stride(1) == 1 && w.stride(1) == 1,
-            "x and w must be 2-D with unit inner stride");
-  const int M = (int)x.size(0), K = (int)x.size(1), N = (int)w.size(0);
-  GSB_CHECK(w.size(1) == K, "K mismatch");
+  const bool grouped = tile_expert.has_value();
+  GSB_CHECK(x.dim() == 2 && w.dim() == (grouped ? 3 : 2) && x.stride(1) == 1 && w.stride(-1) == 1,
+            "x must be 2-D and w 2-D (3-D [E, N, K] with tile_expert) with unit inner stride");
+  const int M = (int)x.size(0), K = (int)x.size(1), N = (int)w.size(grouped ? 1 : 0);
+  GSB_CHECK(w.size(-1) == K, "K mismatch");
+  GemmGroupArgs grp{};
+  grp.tile_expert = nullptr;
+  if (grouped) {
+    GSB_CHECK(w.is_contiguous(), "grouped GEMM: w must be a contiguous [E, N, K] stack");
+    GSB_CHECK(tile_expert->scalar_type() == at::kInt && tile_expert->numel() >= (M + 127) / 128,
+              "grouped GEMM: tile_expert must be int32 [ceil(M/128)]");
+    GSB_CHECK(!s.has_value(), "grouped GEMM: no LoRA operands");
+    grp.tile_expert = tile_expert->data_ptr<int32_t>();
+  }
   GSB_CHECK(bn == 64 || bn == 128 || bn == 256, "bn must be 64, 128 or 256");
   GSB_CHECK(N % bn == 0, "N=", N, " must be a multiple of bn=", bn);
   GSB_CHECK(K % 64 == 0, "K=", K, " must be a multiple of 64");
@@ -1000,10 +1026,12 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
 
   CUtensorMap ta = make_tmap_bf16_2d(x.data_ptr(), M, K, x.stride(0), 64, 128,
                                      CU_TENSOR_MAP_SWIZZLE_128B);
-  const bool pair = pair_enabled(M, (int)bn, (int)epi_kind);
+  const bool pair = !grouped && pair_enabled(M, (int)bn, (int)epi_kind);
   // the pair kernel stages half of the 256-row W tile in each CTA
-  CUtensorMap tb = make_tmap_bf16_2d(w.data_ptr(), N, K, w.stride(0), 64, (uint32_t)(pair ? bn / 2 : bn),
-                                     CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tb = grouped ? make_tmap_bf16_3d(w.data_ptr(), w.size(0), N, K, 64, (uint32_t)bn,
+                                               CU_TENSOR_MAP_SWIZZLE_128B)
+                           : make_tmap_bf16_2d(w.data_ptr(), N, K, w.stride(0), 64, (uint32_t)(pair ? bn / 2 : bn),
+                                               CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap ts = ta, tlb = tb;  // placeholders when LoRA is off
   GemmLoraArgs lora{};
   lora.enabled = 0;
@@ -1105,9 +1133,9 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     return;
   }
   switch (bn) {
-    case 64: dispatch_epi<64>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, errp, stream); break;
-    case 128: dispatch_epi<128>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, errp, stream); break;
-    case 256: dispatch_epi<256>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, errp, stream); break;
+    case 64: dispatch_epi<64>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, errp, stream); break;
+    case 128: dispatch_epi<128>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, errp, stream); break;
+    case 256: dispatch_epi<256>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, errp, stream); break;
   }
 }
 

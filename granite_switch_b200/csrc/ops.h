@@ -13,7 +13,8 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
                        const c10::optional<at::Tensor>& tile_mask, int64_t rank,
                        int64_t num_adapters, std::vector<int64_t> slice_bounds,
                        const c10::optional<at::Tensor>& row_adapter, int64_t mask_rank,
-                       int64_t mask_num_adapters, const at::Tensor& err, int64_t mc_out);
+                       int64_t mask_num_adapters, const at::Tensor& err, int64_t mc_out,
+                       const c10::optional<at::Tensor>& tile_expert);
 
 int64_t gsb_gemm_pair_min_m(int64_t m);
 
@@ -55,3 +56,12 @@ void gsb_probe_verdict(const at::Tensor& hidden, const at::Tensor& rows, const a
                        const at::Tensor& verdict);
 void gsb_probe_rewrite(const at::Tensor& logits, int64_t vocab_lo, const at::Tensor& out_rows,
                        const at::Tensor& slots, const at::Tensor& labels, const at::Tensor& verdict);
+void gsb_moe_route(const at::Tensor& logits, int64_t num_experts, int64_t top_k, const at::Tensor& ids,
+                   const at::Tensor& wts, const at::Tensor& counts, const at::Tensor& offsets, const at::Tensor& cursor,
+                   const at::Tensor& tile_expert);
+void gsb_moe_scatter(const at::Tensor& x, const at::Tensor& ids, const at::Tensor& offsets, const at::Tensor& cursor,
+                     const at::Tensor& slot, const at::Tensor& xp);
+void gsb_moe_combine(const at::Tensor& yp, const at::Tensor& slot, const at::Tensor& wts, int64_t top_k,
+                     const c10::optional<at::Tensor>& shared, const c10::optional<at::Tensor>& residual, double scale,
+                     const at::Tensor& out);
+void gsb_residual_axpy(const at::Tensor& h, const at::Tensor& y, double scale);

@@ -73,4 +73,22 @@ inline CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t co
   return m;
 }
 
+// 3-D bf16 tensor map over a stack of row-major matrices [planes, rows, cols]
+// (contiguous); box [1, box_rows, box_cols].
+inline CUtensorMap make_tmap_bf16_3d(const void* ptr, uint64_t planes, uint64_t rows, uint64_t cols,
+                                     uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  GSB_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
+  GSB_CHECK((cols * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {cols, rows, planes};
+  cuuint64_t strides[2] = {cols * 2, rows * cols * 2};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = tma_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides,
+                               box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  GSB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (3-D) failed with code ", (int)r);
+  return m;
+}
+
 }  // namespace gsb

@@ -30,7 +30,7 @@ from ..ops import attention as A
 from ..ops import elementwise as E
 from ..ops import gemm as G
 from ..routing.scan import expert_table
-from .packing import PackedLinear, choose_swiglu_tile, pack_linear
+from .packing import PackedLinear, PackedMoE, choose_swiglu_tile, pack_linear, pack_moe
 
 
 @dataclass
@@ -39,9 +39,10 @@ class LayerWeights:
     post_norm: torch.Tensor
     qkv: PackedLinear
     o: PackedLinear
-    gu: PackedLinear
-    down: PackedLinear
+    gu: PackedLinear | None             # shared MLP (None for pure mixture-of-experts bases)
+    down: PackedLinear | None
     cross: PackedLinear | None = None   # Shadow Residual cross-stream LoRA (no base weight)
+    moe: PackedMoE | None = None        # frozen expert bank
 
 
 @dataclass
@@ -88,6 +89,11 @@ class NativeGraniteSwitch:
         self.num_q = config.num_attention_heads // tp_size
         self.num_kv = max(1, config.num_key_value_heads // tp_size)
         self.inter = config.shared_intermediate_size // tp_size
+        self.has_shared_mlp = config.shared_intermediate_size > 0
+        self.has_moe = int(getattr(config, "num_local_experts", 0) or 0) > 0
+        if self.has_moe and getattr(config, "dual_stream", False):
+            raise NotImplementedError("Shadow-Residual adapters over a mixture-of-experts base are served by the "
+                                      "HF-style model only")
         self.vocab = config.vocab_size
         # pipeline parallelism: this stage owns decoder layers [layer_lo, layer_hi)
         self.pipeline = pipeline
@@ -196,7 +202,7 @@ class NativeGraniteSwitch:
         h, d = config.hidden_size, config.head_dim_eff
         q, kv = config.num_attention_heads * d, config.num_key_value_heads * d
         inter = config.shared_intermediate_size
-        tiles = choose_swiglu_tile(inter // tp_size)
+        tiles = choose_swiglu_tile(inter // tp_size) if inter > 0 else 0
 
         def lin(prefix, slices, parallel, swiglu=0):
             base = prefix + ".base_layer.weight"
@@ -215,14 +221,19 @@ class NativeGraniteSwitch:
 
         for i in range(self.layer_lo, self.layer_hi):
             p = f"model.layers.{i}."
-            self.layers.append(LayerWeights(
+            lw = LayerWeights(
                 in_norm=get(p + "input_layernorm.weight").to(device, torch.bfloat16),
                 post_norm=get(p + "post_attention_layernorm.weight").to(device, torch.bfloat16),
                 qkv=lin(p + "self_attn.qkv_proj", [q, kv, kv], "column"),
                 o=lin(p + "self_attn.o_proj", [h], "row"),
-                gu=lin(p + "shared_mlp.input_linear", [inter, inter], "column", swiglu=tiles),
-                down=lin(p + "shared_mlp.output_linear", [h], "row"),
-            ))
+                gu=lin(p + "shared_mlp.input_linear", [inter, inter], "column", swiglu=tiles) if inter > 0 else None,
+                down=lin(p + "shared_mlp.output_linear", [h], "row") if inter > 0 else None,
+            )
+            if self.has_moe:
+                e = p + "block_sparse_moe."
+                lw.moe = pack_moe(get(e + "experts.gate_up_proj"), get(e + "experts.down_proj"),
+                                  get(e + "router.weight"), config.num_experts_per_tok, device, tp_rank, tp_size)
+            self.layers.append(lw)
         if self.dual:
             for i, lw in zip(range(self.layer_lo, self.layer_hi), self.layers):
                 p = f"model.layers.{i}.cross_stream."
@@ -256,8 +267,9 @@ class NativeGraniteSwitch:
         h, d = config.hidden_size, config.head_dim_eff
         q, kv = config.num_attention_heads * d, config.num_key_value_heads * d
         inter = config.shared_intermediate_size
-        tiles = choose_swiglu_tile(inter // tp_size)
+        tiles = choose_swiglu_tile(inter // tp_size) if inter > 0 else 0
         scale = 2.0  # alpha / r
+        n_exp = int(getattr(config, "num_local_experts", 0) or 0)
 
         def rnd(*shape, s=std):
             return (torch.randn(*shape, generator=g, device=device) * s).to(torch.bfloat16)
@@ -278,9 +290,13 @@ class NativeGraniteSwitch:
                 post_norm=torch.ones(h, dtype=torch.bfloat16, device=device),
                 qkv=lin([q, kv, kv], h, "column", "qkv" in lora_modules),
                 o=lin([h], q, "row", "o" in lora_modules),
-                gu=lin([inter, inter], h, "column", "gu" in lora_modules, swiglu=tiles),
-                down=lin([h], inter, "row", "down" in lora_modules),
+                gu=lin([inter, inter], h, "column", "gu" in lora_modules, swiglu=tiles) if inter > 0 else None,
+                down=lin([h], inter, "row", "down" in lora_modules) if inter > 0 else None,
             )
+            if n_exp:
+                ie = config.intermediate_size
+                lw.moe = pack_moe(rnd(n_exp, 2 * ie, h), rnd(n_exp, h, ie), rnd(n_exp, h),
+                                  config.num_experts_per_tok, device, tp_rank, tp_size)
             if self.layer_lo <= i < self.layer_hi:
                 self.layers.append(lw)
         if self.dual and na > 0:
@@ -316,7 +332,25 @@ class NativeGraniteSwitch:
         self.x = torch.empty(t, self.hidden, dtype=bf, device=dev)
         self.qkv = torch.empty(t, qkv_n, dtype=bf, device=dev)
         self.attn = torch.empty(t, self.num_q * self.head_dim, dtype=bf, device=dev)
-        self.act = torch.empty(t, self.inter, dtype=bf, device=dev)
+        self.act = torch.empty(t, max(self.inter, 1), dtype=bf, device=dev)
+        moe = next((lw.moe for lw in self.layers if lw.moe is not None), None)
+        if moe is not None:
+            e, k = moe.num_experts, moe.top_k
+            self.moe_pmax = (t * k + 127 * e + 127) // 128 * 128   # worst case of the padded segments
+            self.moe_logits = torch.empty(t, moe.router.shape[0], dtype=torch.float32, device=dev)
+            self.moe_ids = torch.empty(t * k, dtype=torch.int32, device=dev)
+            self.moe_wts = torch.empty(t * k, dtype=torch.float32, device=dev)
+            self.moe_slot = torch.empty(t * k, dtype=torch.int32, device=dev)
+            self.moe_counts = torch.zeros(e, dtype=torch.int32, device=dev)
+            self.moe_offsets = torch.empty(e, dtype=torch.int32, device=dev)
+            self.moe_cursor = torch.empty(e, dtype=torch.int32, device=dev)
+            self.moe_tiles = torch.empty(self.moe_pmax // 128, dtype=torch.int32, device=dev)
+            self.moe_xp = torch.zeros(self.moe_pmax, self.hidden, dtype=bf, device=dev)
+            self.moe_ap = torch.zeros(self.moe_pmax, moe.inter, dtype=bf, device=dev)
+            self.moe_yp = torch.zeros(self.moe_pmax, self.hidden, dtype=bf, device=dev)
+            self.moe_y = torch.empty(t, self.hidden, dtype=bf, device=dev)
+        self.x2 = (torch.empty(t, self.hidden, dtype=bf, device=dev)
+                   if moe is not None and self.has_shared_mlp else None)
         s_cols = 64
         for lw in self.layers:
             for pl in (lw.qkv, lw.o, lw.gu, lw.down, lw.cross):
@@ -413,6 +447,48 @@ class NativeGraniteSwitch:
         G.lora_shrink(hbase, pl.a_all, ra, pl.rank, pl.n_local, out=s)
         G.switched_gemm(s, pl.lb, h, epi=G.EPI_RESADD, residual=h, scale=1.0)
 
+    def _mlp(self, lw: LayerWeights, x: torch.Tensor, act: torch.Tensor, h: torch.Tensor, mult: float) -> None:
+        """``h <- h + MLP(x) * mult``: shared MLP, expert bank, or their sum (summed over TP ranks)."""
+        R = self._region
+        if lw.moe is None:
+            with R("gate_up+swiglu"):
+                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
+            with R("down"):
+                self._row_parallel(lw.down, act, h, mult)
+            return
+        m = x.shape[0]
+        moe = lw.moe
+        nat = native()
+        with R("moe_route"):
+            logits = self.moe_logits[:m]
+            G.switched_gemm(x, moe.router, logits, epi=G.EPI_F32)
+            k = moe.top_k
+            nat.moe_route(logits, moe.num_experts, k, self.moe_ids[: m * k], self.moe_wts[: m * k],
+                          self.moe_counts, self.moe_offsets, self.moe_cursor, self.moe_tiles)
+            nat.moe_scatter(x, self.moe_ids[: m * k], self.moe_offsets, self.moe_cursor, self.moe_slot[: m * k],
+                            self.moe_xp)
+        rows = min(self.moe_pmax, (m * k + 127 * moe.num_experts + 127) // 128 * 128)
+        tiles = self.moe_tiles[: rows // 128]
+        with R("moe_experts"):
+            G.switched_gemm(self.moe_xp[:rows], moe.gate_up, self.moe_ap[:rows], epi=G.EPI_SWIGLU,
+                            bn=moe.swiglu_tile, tile_expert=tiles)
+            G.switched_gemm(self.moe_ap[:rows], moe.down, self.moe_yp[:rows], tile_expert=tiles)
+        shared = None
+        if lw.gu is not None:
+            with R("gate_up+swiglu"):
+                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
+            with R("down"):
+                shared = self.x2[:m]
+                self._proj(lw.down, act, shared, epi=G.EPI_STORE)
+        with R("moe_combine"):
+            if self.tp_size == 1:
+                nat.moe_combine(self.moe_yp, self.moe_slot[: m * k], self.moe_wts[: m * k], k, shared, h, mult, h)
+            else:
+                y = self.moe_y[:m]
+                nat.moe_combine(self.moe_yp, self.moe_slot[: m * k], self.moe_wts[: m * k], k, shared, None, 1.0, y)
+                torch.distributed.all_reduce(y, group=self.tp_group)
+                E.residual_axpy(h, y, mult)
+
     def _probe_layer(self, b: StepBatch, layer, hidden: torch.Tensor) -> None:
         """Probe scores of the markers that read ``layer`` (None: the final-norm rows)."""
         for lay, rows, slots, outj in b.probe_groups:
@@ -471,17 +547,16 @@ class NativeGraniteSwitch:
                         self._row_parallel(lw.o, attn, h, mult)
                     with R("rmsnorm"):
                         E.rmsnorm(h, lw.post_norm, cfg.rms_norm_eps, out=x)
-                with R("gate_up+swiglu"):
-                    self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
                 if comm is not None:
+                    with R("gate_up+swiglu"):
+                        self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
                     with R("down+reduce"):
                         y = comm.row_parallel(self, lw.down, act, h, mult)
                     nxt = self.layers[li + 1].in_norm if li + 1 < len(self.layers) else self.final_norm
                     with R("finish+rmsnorm"):
                         comm.finish(y, h, nxt, x, cfg.rms_norm_eps)
                 else:
-                    with R("down"):
-                        self._row_parallel(lw.down, act, h, mult)
+                    self._mlp(lw, x, act, h, mult)
                 if probes:
                     self._probe_layer(b, self.layer_lo + li, h)
         if not self.last_stage:

@@ -158,3 +158,42 @@ def choose_swiglu_tile(inter_local: int) -> int:
         if inter_local % (bn // 2) == 0:
             return bn
     raise ValueError(f"intermediate size {inter_local} is not a multiple of 32")
+
+
+@dataclass
+class PackedMoE:
+    """Frozen expert bank in kernel layout (never a LoRA target).
+
+    ``router`` ``[pad64(E), H]`` bf16 (zero rows past E); ``gate_up``
+    ``[E, 2 I_local, H]`` with gate/up rows interleaved per SwiGLU tile;
+    ``down`` ``[E, H, I_local]``. Under tensor parallelism every rank holds
+    ``I / tp`` of each expert (gate/up column-parallel, down row-parallel)
+    and the router is replicated.
+    """
+    router: torch.Tensor
+    gate_up: torch.Tensor
+    down: torch.Tensor
+    num_experts: int
+    top_k: int
+    inter: int
+    swiglu_tile: int
+
+
+def pack_moe(gate_up: torch.Tensor, down: torch.Tensor, router: torch.Tensor, top_k: int, device,
+             tp_rank: int = 0, tp_size: int = 1, dtype=torch.bfloat16) -> PackedMoE:
+    """``gate_up [E, 2I, H]`` (gate rows then up rows), ``down [E, H, I]``, ``router [E, H]``."""
+    e, two_i, h = gate_up.shape
+    i = two_i // 2
+    assert i % tp_size == 0, f"expert intermediate size {i} not divisible by tp {tp_size}"
+    il = i // tp_size
+    lo, hi = tp_rank * il, (tp_rank + 1) * il
+    gu = torch.cat([gate_up[:, lo:hi], gate_up[:, i + lo:i + hi]], dim=1)
+    tile = choose_swiglu_tile(il)
+    gu = torch.stack([interleave_gate_up(gu[k], tile) for k in range(e)])
+    dn = down[:, :, lo:hi]
+    r = torch.zeros(_pad_to(e, 64), h, dtype=router.dtype, device=router.device)
+    r[:e] = router
+    return PackedMoE(router=r.to(device=device, dtype=dtype).contiguous(),
+                     gate_up=gu.to(device=device, dtype=dtype).contiguous(),
+                     down=dn.to(device=device, dtype=dtype).contiguous(),
+                     num_experts=e, top_k=int(top_k), inter=il, swiglu_tile=tile)

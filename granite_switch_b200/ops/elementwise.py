@@ -67,3 +67,8 @@ def argmax(logits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
         out = torch.empty(logits.shape[0], dtype=torch.long, device=logits.device)
     native().argmax(logits, out)
     return out
+
+
+def residual_axpy(h: torch.Tensor, y: torch.Tensor, scale: float) -> None:
+    """``h <- h + y * scale`` (bf16)."""
+    native().residual_axpy(h, y, float(scale))

@@ -55,9 +55,12 @@ def switched_gemm(
     mask_num_adapters: int = 0,
     bn: int | None = None,
     mc_out: int = 0,
+    tile_expert: torch.Tensor | None = None,
 ) -> torch.Tensor:
+    """``tile_expert`` selects grouped mode: ``w`` is a stack ``[E, N, K]`` and
+    128-row tile ``t`` of ``x`` multiplies expert ``tile_expert[t]`` (-1: skipped)."""
     m, _ = x.shape
-    n = w.shape[0]
+    n = w.shape[-2]
     if out is None:
         if epi == EPI_SWIGLU:
             out = torch.empty((m, n // 2), dtype=torch.bfloat16, device=x.device)
@@ -73,7 +76,7 @@ def switched_gemm(
     native().switched_gemm(
         x, w, out, epi, bn, residual, float(scale), s, lb, tile_mask, rank, num_adapters,
         list(slice_bounds) if slice_bounds is not None else [0, n], row_adapter, mask_rank,
-        mask_num_adapters, err_buffer(x.device), int(mc_out),
+        mask_num_adapters, err_buffer(x.device), int(mc_out), tile_expert,
     )
     return out
 

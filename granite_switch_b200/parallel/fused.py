@@ -90,8 +90,8 @@ class FusedTPComm:
 
 def attach_fused_comm(model, group) -> bool:
     """Attach a :class:`FusedTPComm` to a native model; False (NCCL path kept) without multicast."""
-    if getattr(model, "dual", False):
-        return False  # Shadow-Residual models reduce both streams over NCCL
+    if getattr(model, "dual", False) or getattr(model, "has_moe", False):
+        return False  # Shadow-Residual and expert-bank models reduce over NCCL
     comm = FusedTPComm(group, model.device, model.max_tokens, model.hidden)
     if not comm.supported:
         return False

@@ -99,6 +99,8 @@ def run_reference(args):
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "granite_switch")):
         return dict(impl="reference", unavailable="baseline/_ref is not installed")
+    # vLLM inspects model classes in subprocesses: they must find the reference package too
+    os.environ["PYTHONPATH"] = ref + os.pathsep + os.environ.get("PYTHONPATH", "")
     sys.path.insert(0, ref)
     import torch
 

@@ -213,3 +213,27 @@ def test_cuda_graph_decode_matches_eager(tiny_dir):
             ex = llm.engine.executor
             assert ex.graph_replays > 0 and set(ex.graphs) <= {8, 16}
     assert outs[True] == outs[False]
+
+
+@pytest.fixture(scope="module", params=["moe", "moe_shared"])
+def moe_dir(request, tmp_path_factory):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA")
+    from granite_switch_b200.composer.synthetic import compose_synthetic
+
+    d = str(tmp_path_factory.mktemp("eng_gpu_" + request.param))
+    extra = dict(shared_intermediate_size=512) if request.param == "moe_shared" else {}
+    targets = ("q", "k", "v", "o", "gate", "up", "down") if extra else ("q", "k", "v", "o")
+    compose_synthetic(d, "tiny", num_adapters=3, rank=8, targets=targets, seed=6, dtype=torch.float32,
+                      invocation_len=4, alpha=16.0, num_hidden_layers=2, num_local_experts=8,
+                      num_experts_per_tok=2, intermediate_size=256, **extra)
+    return d
+
+
+@pytest.mark.parametrize("budget", [48, 2048])
+def test_native_moe_matches_reference(moe_dir, budget):
+    """Frozen expert bank (grouped tcgen05 GEMMs, per-expert 128-row segments) vs the CPU oracle."""
+    worst, agree, total, _ = _compare_engine(moe_dir, _prompts(moe_dir, 5, seed=7), budget)
+    assert total == 20
+    assert worst < 0.05, worst
+    assert agree >= total - 1

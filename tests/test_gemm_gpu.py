@@ -330,3 +330,34 @@ def test_pair_expand_with_tile_restricted_shrink(epi):
         ref = G.switched_gemm_reference(x, w, s=s_full, lb=lb, rank=rank, num_adapters=na, slice_bounds=[0, n])
     assert not torch.isnan(out.float()).any()
     _close(out, ref)
+
+
+@pytest.mark.parametrize("epi", ["store", "swiglu"])
+def test_grouped_gemm(epi):
+    """Grouped mode: each 128-row tile multiplies its expert's weights; -1 tiles are left untouched."""
+    from granite_switch_b200._native import check_errors
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(10)
+    e, n, k = 5, 512, 256
+    tiles = torch.tensor([3, 0, 0, 4, -1, 2, -1], dtype=torch.int32, device="cuda")
+    m = 128 * tiles.numel()
+    x = _rand(m, k)
+    w = _rand(e, n, k, scale=0.05)
+    out = torch.full((m, n // 2 if epi == "swiglu" else n), 7.0, device="cuda", dtype=torch.bfloat16)
+    if epi == "swiglu":
+        G.switched_gemm(x, w, out, epi=G.EPI_SWIGLU, bn=256, tile_expert=tiles)
+    else:
+        G.switched_gemm(x, w, out, tile_expert=tiles)
+    torch.cuda.synchronize()
+    check_errors(x.device)
+    for t, ex in enumerate(tiles.tolist()):
+        rows = slice(128 * t, 128 * (t + 1))
+        if ex < 0:
+            assert bool((out[rows].float() == 7.0).all())
+            continue
+        if epi == "swiglu":
+            ref = G.switched_gemm_reference(x[rows], w[ex], epi=G.EPI_SWIGLU, swiglu_tile=256)
+        else:
+            ref = G.switched_gemm_reference(x[rows], w[ex])
+        _close(out[rows], ref)
