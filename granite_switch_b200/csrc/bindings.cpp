@@ -26,5 +26,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_scatter", &gsb_moe_scatter, "MoE token rows into their experts' segments");
   m.def("moe_combine", &gsb_moe_combine, "MoE weighted sum of expert outputs (+ shared MLP, residual)");
   m.def("residual_axpy", &gsb_residual_axpy, "h <- h + y * scale");
+  m.def("allreduce_ldreduce_p2p", &gsb_allreduce_ldreduce_p2p,
+        "switch-summed slices written to every rank by P2P stores");
   m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode)");
 }

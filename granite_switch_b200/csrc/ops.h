@@ -65,3 +65,5 @@ void gsb_moe_combine(const at::Tensor& yp, const at::Tensor& slot, const at::Ten
                      const c10::optional<at::Tensor>& shared, const c10::optional<at::Tensor>& residual, double scale,
                      const at::Tensor& out);
 void gsb_residual_axpy(const at::Tensor& h, const at::Tensor& y, double scale);
+void gsb_allreduce_ldreduce_p2p(int64_t mc_ptr, const at::Tensor& peer_ptrs, int64_t offset, int64_t nbytes,
+                                int64_t rank, int64_t tp);

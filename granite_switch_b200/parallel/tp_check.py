@@ -6,7 +6,8 @@ Run under torchrun, one process per GPU::
 
 Every rank builds the same seeded random model, keeps its shard, runs one
 prefill step and two decode steps through the native executor, and gathers
-the logits. Rank 0 also builds the unsharded model alone and compares. Prints
+the logits: over NCCL, with the fused reductions, and with every fused
+reduction on the large-step path. Rank 0 also builds the unsharded model alone and compares. Prints
 one JSON line per checked mode on rank 0 and exits non-zero on a mismatch.
 """
 from __future__ import annotations
@@ -35,7 +36,7 @@ def _config():
     return GraniteSwitchConfig(**cfg)
 
 
-def _run(config, device, tp, rank, group, fused):
+def _run(config, device, tp, rank, group, fused, red_max_tokens=None):
     from ..engine import EngineConfig
     from ..engine.executor import NativeExecutor
     from ..engine.kv_cache import BlockManager
@@ -52,6 +53,8 @@ def _run(config, device, tp, rank, group, fused):
 
         if not attach_fused_comm(m, group):
             return None
+        if red_max_tokens is not None:
+            m.comm.red_max_tokens = red_max_tokens
     ex = NativeExecutor(m, 1024, group, tp)
     bm = BlockManager(256)
     router = HostRouter(config)
@@ -81,6 +84,66 @@ def _run(config, device, tp, rank, group, fused):
     return outs, errs
 
 
+def _check_primitives(device, group, rank, world) -> dict:
+    """Each fused-collective primitive against an NCCL all-reduce of the same data."""
+    from .._native import native
+    from ..ops import gemm as G
+    from .fused import FusedTPComm
+
+    m, h, k = 200, 512, 256
+    comm = FusedTPComm(group, device, m, h)
+    out = {}
+    g = torch.Generator(device=device).manual_seed(11 + rank)
+    x = torch.randn(m, k, device=device, generator=g).bfloat16()
+    w = (torch.randn(h, k, device=device, generator=g) * 0.05).bfloat16()
+    part = G.switched_gemm(x, w)
+    want = part.clone()
+    dist.all_reduce(want, group=group)
+    mc0 = comm.mc
+    for name in ("plain_store+allreduce", "gemm_store+allreduce", "gemm_multimem_red"):
+        y = comm.y[0, :m]
+        y.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        if name == "plain_store+allreduce":
+            y.copy_(part)
+        elif name == "gemm_store+allreduce":
+            G.switched_gemm(x, w, y)
+        else:
+            G.switched_gemm(x, w, y, epi=G.EPI_MULTIMEM_RED, mc_out=mc0)
+        comm.barrier()
+        if name != "gemm_multimem_red":
+            native().allreduce_ldreduce_p2p(mc0, comm.y_ptrs, 0, m * h * 2, rank, world)
+            comm.barrier()
+        torch.cuda.synchronize()
+        err = ((y.float() - want.float()).abs().max() / want.float().abs().max()).item()
+        out[name] = round(err, 5)
+    # the model's sequence: three projections back to back through row_parallel + finish
+    # (alternating buffers, rank 0 folds in the residual), no host synchronisation
+    class _M:
+        def _proj(self, pl, xx, yy, epi=G.EPI_STORE, residual=None, scale=1.0, mc_out=0):
+            return G.switched_gemm(xx, pl, yy, epi=epi, residual=residual, scale=scale, mc_out=mc_out)
+
+    for red in (10 ** 6, 0):
+        comm.red_max_tokens = red
+        hres = torch.randn(m, h, device=device, generator=torch.Generator(device=device).manual_seed(5)).bfloat16()
+        nw = torch.ones(h, device=device, dtype=torch.bfloat16)
+        xs = [torch.randn(m, k, device=device, generator=g).bfloat16() for _ in range(3)]
+        hh, xx = hres.clone(), torch.empty(m, h, device=device, dtype=torch.bfloat16)
+        ref = hres.clone()
+        for xi in xs:
+            y = comm.row_parallel(_M(), w, xi, hh, 0.5)
+            comm.finish(y, hh, nw, xx, 1e-5)
+        for xi in xs:
+            p = G.switched_gemm(xi, w, scale=0.5)
+            dist.all_reduce(p, group=group)
+            ref = (ref.float() + p.float()).bfloat16()
+        torch.cuda.synchronize()
+        err = ((hh.float() - ref.float()).abs().max() / ref.float().abs().max()).item()
+        out["row_parallel_" + ("red" if red else "allreduce")] = round(err, 5)
+    return out
+
+
 def main() -> int:
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
@@ -90,12 +153,19 @@ def main() -> int:
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
     group = dist.group.WORLD
     config = _config()
+    prim = _check_primitives(device, group, rank, world)
+    if rank == 0:
+        print(json.dumps({"primitives": prim}), flush=True)
+    dist.barrier()
     results = {}
     nccl = _run(config, device, world, rank, group, fused=False)
     results["nccl"] = nccl
     dist.barrier()
     fused = _run(config, device, world, rank, group, fused=True)
     results["fused"] = fused
+    dist.barrier()
+    # every reduction on the large-step path (partial stored, NCCL all-reduce)
+    results["fused_allreduce"] = _run(config, device, world, rank, group, fused=True, red_max_tokens=0)
     dist.barrier()
     ok = True
     if rank == 0:
