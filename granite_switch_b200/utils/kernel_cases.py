@@ -1,7 +1,7 @@
 """One launch of each native kernel on a representative shape, for profiler captures.
 
 ``python -m granite_switch_b200.utils.kernel_cases <case>`` with case in
-gemm, gemm_pair, gemm_single, cublas, swiglu, decode_gemm, attn_prefill, attn_decode, rmsnorm, rope, embed,
+gemm, gemm_pair, gemm_single, cublas, swiglu, attn_prefill64, moe, probe, decode_gemm, attn_prefill, attn_decode, rmsnorm, rope, embed,
 routing, sample (or ``all``). Pair it with ``ncu -k regex:<kernel> -c 1``.
 """
 import sys
@@ -77,6 +77,46 @@ if want("attn_prefill") or want("attn_decode"):
         q_lens = [1] * 128; kv = [4200] * 128; kc, vc, bt, q, out, qs, kvl = setup(q_lens, kv)
         ws, wr = [torch.tensor(v, dtype=torch.int32, device=dev) for v in A.build_work(q_lens, 4, 16)]
         A.paged_attention(q, kc, vc, bt, qs, kvl, ws, wr, 16, hq, 0.088, out, 1)
+if want("attn_prefill64"):  # tcgen05 prefill attention, head_dim 64 (3B shape: 32 q / 8 kv heads)
+    hq, hkv, d = 32, 8, 64
+    q_lens = [2048, 2048]
+    nblk = sum((l + 15) // 16 for l in q_lens) + 4
+    kc = torch.randn(nblk, hkv, 16, d, device=dev).bfloat16(); vc = torch.randn_like(kc)
+    bt = torch.arange(nblk - 4, dtype=torch.int32, device=dev).view(len(q_lens), -1)
+    q = torch.randn(sum(q_lens), (hq + 2 * hkv) * d, device=dev).bfloat16()
+    out = torch.empty(sum(q_lens), hq * d, device=dev).bfloat16()
+    qs = torch.tensor([0, 2048, 4096], dtype=torch.int32, device=dev)
+    ws, wr = [torch.tensor(v, dtype=torch.int32, device=dev) for v in A.build_work(q_lens, 4, 128, q_lens)]
+    A.prefill_attention_tc(q, kc, vc, bt, qs, torch.tensor(q_lens, dtype=torch.int32, device=dev), ws, wr, hq,
+                           0.125, out)
+if want("moe"):  # expert bank: 8192 tokens, 40 experts top-8, H 1536, expert FFN 512
+    Hm, Im, Em, Km, Tm = 1536, 512, 40, 8, 8192
+    from granite_switch_b200.models.packing import pack_moe
+    moe = pack_moe((torch.randn(Em, 2 * Im, Hm) * 0.02).bfloat16(), (torch.randn(Em, Hm, Im) * 0.02).bfloat16(),
+                   torch.randn(Em, Hm).bfloat16(), Km, dev)
+    x = torch.randn(Tm, Hm, device=dev).bfloat16()
+    pmax = (Tm * Km + 127 * Em + 127) // 128 * 128
+    logits = torch.empty(Tm, moe.router.shape[0], device=dev)
+    ids = torch.empty(Tm * Km, dtype=torch.int32, device=dev); wts = torch.empty(Tm * Km, device=dev)
+    cnt = torch.zeros(Em, dtype=torch.int32, device=dev); off = torch.empty_like(cnt); cur = torch.empty_like(cnt)
+    tiles = torch.empty(pmax // 128, dtype=torch.int32, device=dev); slot = torch.empty_like(ids)
+    xp = torch.zeros(pmax, Hm, device=dev).bfloat16(); ap = torch.zeros(pmax, Im, device=dev).bfloat16()
+    yp = torch.zeros(pmax, Hm, device=dev).bfloat16(); h = torch.randn(Tm, Hm, device=dev).bfloat16()
+    G.switched_gemm(x, moe.router, logits, epi=G.EPI_F32)
+    native().moe_route(logits, Em, Km, ids, wts, cnt, off, cur, tiles)
+    native().moe_scatter(x, ids, off, cur, slot, xp)
+    G.switched_gemm(xp, moe.gate_up, ap, epi=G.EPI_SWIGLU, bn=moe.swiglu_tile, tile_expert=tiles)
+    G.switched_gemm(ap, moe.down, yp, tile_expert=tiles)
+    native().moe_combine(yp, slot, wts, Km, None, h, 1.0, h)
+if want("probe"):
+    hid = torch.randn(4096, H, device=dev).bfloat16()
+    pw = torch.randn(4, 8, H, device=dev).bfloat16(); pb = torch.randn(4, 8, device=dev)
+    rows = torch.arange(0, 4096, 32, dtype=torch.int32, device=dev); n = rows.numel()
+    slots = (torch.arange(n, dtype=torch.int32, device=dev) % 4) + 1; outj = torch.arange(n, dtype=torch.int32, device=dev)
+    verdict = torch.zeros(n, 8, device=dev); logits = torch.randn(n, 49152, device=dev)
+    labels = torch.randint(0, 49152, (4, 8), dtype=torch.int32, device=dev)
+    native().probe_verdict(hid, rows, slots, outj, pw, pb, verdict)
+    native().probe_rewrite(logits, 0, outj, slots, labels, verdict)
 if want("rmsnorm"):
     x = torch.randn(16384, H, device=dev).bfloat16(); w = torch.ones(H, device=dev).bfloat16()
     E.rmsnorm(x, w, 1e-5)
