@@ -74,7 +74,10 @@ struct AttnCfg {
   static constexpr int KPW = KT / WARPS_N;        // keys per warp per tile
   static constexpr int TILE_BYTES = KT * D * 2;   // one of K or V
   static constexpr int Q_BYTES = ROWS * D * 2;
-  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * TILE_BYTES + 256;
+  // page ids of the CTA's key range, staged in shared memory once (past this
+  // many pages the loop falls back to reading the block table in global memory)
+  static constexpr int PT_CAP = 2048;
+  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * TILE_BYTES + 256 + PT_CAP * 4;
 };
 
 template <int D, int WARPS_M, int KT, int STAGES>
@@ -125,6 +128,12 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
   }
+  // ---- page ids of [k_begin, k_end) into shared memory: the producer thread
+  // then issues each tile's page loads without a dependent global read
+  int32_t* s_pages = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full) + 256);
+  const int pg0 = k_begin / PAGE;
+  const int n_cached = (n_tiles > 0) ? min((k_end + PAGE - 1) / PAGE - pg0, C::PT_CAP) : 0;
+  for (int i = threadIdx.x; i < n_cached; i += C::THREADS) s_pages[i] = bt[pg0 + i];
   // ---- Q tile via cp.async into the swizzled [half][row][64] layout
   for (int c = threadIdx.x; c < ROWS * DC; c += C::THREADS) {
     const int r = c / DC, ch = c % DC;
@@ -151,7 +160,8 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
       const int j = tile_start + p * PAGE;
       // pages past the key range still load a valid page (masked later) so no
       // uninitialised smem (possibly NaN) ever meets a zero probability
-      const int page = (j < k_end) ? bt[j / PAGE] : first_page;
+      const int pi = j / PAGE - pg0;
+      const int page = (j < k_end) ? (pi < n_cached ? s_pages[pi] : bt[j / PAGE]) : first_page;
       const int row = (page * Hkv + kvh) * PAGE;
 #pragma unroll
       for (int h = 0; h < D / 64; ++h) {

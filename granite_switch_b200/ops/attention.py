@@ -35,11 +35,16 @@ def build_work(q_lens: list[int], group: int, rows_per_tile: int,
     return seqs, rows
 
 
-def choose_splits(n_ctas: int, max_kv: int, min_keys_per_split: int = 256) -> int:
-    """Flash-decoding split count: fill ~2 waves of SMs without splits shorter than 256 keys."""
-    if n_ctas >= 2 * NUM_SMS:
+def choose_splits(n_ctas: int, max_kv: int, min_keys_per_split: int = 512) -> int:
+    """Flash-decoding split count: split the key range only while there are fewer
+    (request, KV head) CTAs than SMs, aiming at one CTA per SM, never below 512
+    keys per split. Measured on B200 (d=128, 32 q / 8 kv heads): at 256 or more
+    CTAs one split is fastest (4.1-5.1 TB/s); a second split costs 10-20%
+    (fp32 partials, merge, per-CTA set-up over shorter ranges).
+    """
+    if n_ctas >= NUM_SMS:
         return 1
-    want = max(1, (2 * NUM_SMS + n_ctas - 1) // max(n_ctas, 1))
+    want = max(1, (NUM_SMS + n_ctas - 1) // max(n_ctas, 1))
     cap = max(1, max_kv // min_keys_per_split)
     return int(max(1, min(want, cap, 32)))
 
