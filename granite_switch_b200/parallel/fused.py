@@ -67,6 +67,9 @@ class FusedTPComm:
         # from the collective sweep: always at TP=2, small steps only at TP=4 / 8
         default = {2: 1 << 20, 4: 1024}.get(self.world, 256)
         self.red_max_tokens = int(os.environ.get("GSB_TP_RED_MAX_TOKENS", str(default)))
+        # large steps reduce through NCCL; GSB_TP_SWITCH_ALLREDUCE=1 selects the switch
+        # all-reduce kernel instead (under investigation, see the TP self-check)
+        self.switch_allreduce = os.environ.get("GSB_TP_SWITCH_ALLREDUCE", "0") == "1"
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
 
@@ -103,7 +106,13 @@ class FusedTPComm:
                 model._proj(pl, x, y, epi=G.EPI_RESADD, residual=resid, scale=mult)
             else:
                 model._proj(pl, x, y, epi=G.EPI_STORE, scale=mult)
-            torch.distributed.all_reduce(y, group=self.group)
+            if self.switch_allreduce:
+                self.barrier()
+                native().allreduce_ldreduce_p2p(self.mc, self.y_ptrs, b * self.max_tokens * self.hidden * 2,
+                                                m * self.hidden * 2, self.rank, self.world)
+                self.barrier()
+            else:
+                torch.distributed.all_reduce(y, group=self.group)
         return y
 
     def finish(self, y: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor, x: torch.Tensor, eps: float) -> None:

@@ -45,8 +45,9 @@ def _run(config, device, tp, rank, group, fused, red_max_tokens=None):
     from ..engine.scheduler import Scheduler
     from ..models.native import NativeGraniteSwitch
 
+    lora = tuple(x for x in os.environ.get("GSB_TPCHECK_LORA", "qkv,o").split(",") if x)
     m = NativeGraniteSwitch.from_random(config, device, max_tokens=512, num_kv_blocks=256,
-                                        lora_modules=("qkv", "o"), rank=16, seed=7, tp_rank=rank, tp_size=tp,
+                                        lora_modules=lora, rank=16, seed=7, tp_rank=rank, tp_size=tp,
                                         tp_group=group, max_seqs=16)
     if fused:
         from .fused import attach_fused_comm
