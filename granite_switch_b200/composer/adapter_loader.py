@@ -82,7 +82,8 @@ def load_adapter(path: str, name: str | None = None, technology: str | None = No
         name=nm, tensors=tensors, r=int(cfg.get("r", 8)), alpha=float(cfg.get("lora_alpha", cfg.get("r", 8))),
         technology=tech, invocation_tokens=list(inv) if inv else None, kind=kind,
         rank_pattern=dict(cfg.get("rank_pattern") or {}), alpha_pattern=dict(cfg.get("alpha_pattern") or {}),
-        io_config=io, source=path)
+        io_config=io, source=path, last_context_token=cfg.get("last_context_token"),
+        last_context_token_id=cfg.get("last_context_token_id"))
 
 
 def empty_adapter(name: str, rank: int, alpha: float | None = None) -> AdapterSpec:

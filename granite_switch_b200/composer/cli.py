@@ -101,13 +101,12 @@ def _probe_adapter(found, tokenizer) -> AdapterSpec:
     ph = os.path.join(found.path, "probe_head.safetensors")
     sd = load_file(ph) if os.path.exists(ph) else {}
     labels = found.labels or []
-    label_ids = []
-    for lab in labels:
-        if tokenizer is not None:
-            ids = tokenizer(lab, add_special_tokens=False)["input_ids"]
-            label_ids.append(int(ids[0]))
-        else:
-            label_ids.append(int(lab))
+    if tokenizer is not None:
+        from .tokenizer_setup import resolve_label_token_ids
+
+        label_ids = resolve_label_token_ids(tokenizer, [str(x) for x in labels])
+    else:
+        label_ids = [int(lab) for lab in labels]
     return AdapterSpec(name=found.name, tensors={}, r=1, alpha=1.0, technology="lora", kind="probe",
                        probe_label_token_ids=label_ids, probe_read_layer=found.layer,
                        probe_weight=sd.get("weight"), probe_bias=sd.get("bias"), source=found.path)
@@ -151,13 +150,19 @@ def compose_main(argv=None) -> int:
     adapters.sort(key=lambda a: 1 if a.kind == "probe" else 0)
     base_cfg, base_sd = load_base(base_path)
     ctrl_ids = None
+    reserved_row = default_sub = None
+    extra_ids: list[int] = []
     if tokenizer is not None:
-        from .tokenizer_setup import configure_tokenizer
+        from .tokenizer_setup import configure_tokenizer, find_reserved_never_emitted_token_id
 
-        ctrl_ids = configure_tokenizer(tokenizer, adapters, args.base_reset_token)
+        ctrl_ids, setup = configure_tokenizer(tokenizer, adapters, args.base_reset_token, audio=args.enable_audio)
+        reserved_row = find_reserved_never_emitted_token_id(tokenizer)
         if args.enable_audio:
-            tokenizer.add_special_tokens({"additional_special_tokens":
-                                          list(tokenizer.additional_special_tokens) + ["<|audio|>"]})
+            extra_ids = [int(tokenizer.convert_tokens_to_ids("<|audio|>"))]
+        if setup is not None:
+            default_sub = setup.lora_substitute
+            print(f"chat template: {setup.format.name}; placements: "
+                  + ", ".join(f"{n}={p.mode}" for n, p in setup.placements.items()))
     extra = {}
     if args.enable_audio:
         extra.update(asr_enabled=True, asr_model_id=args.asr_model or DEFAULT_ASR_MODEL_ID,
@@ -174,7 +179,8 @@ def compose_main(argv=None) -> int:
                                 base_reset=args.base_reset_token, base_model_name=args.base_model,
                                 ms_code_m=args.ms_code_m or 6, ms_memory_gain=args.ms_memory_gain or 28.0,
                                 switch_head_dim=args.switch_head_dim or 32, extra_config=extra,
-                                control_token_ids=ctrl_ids)
+                                control_token_ids=ctrl_ids, reserved_output_row=reserved_row,
+                                default_substitute=default_sub, extra_token_ids=extra_ids)
     if tokenizer is not None:
         tokenizer.save_pretrained(args.output)
     io_dir = os.path.join(args.output, "io_configs")

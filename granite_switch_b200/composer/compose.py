@@ -49,6 +49,8 @@ class AdapterSpec:
     probe_bias: torch.Tensor | None = None     # [L]
     io_config: dict | None = None
     source: str | None = None
+    last_context_token: str | None = None      # Shadow Residual activation anchor
+    last_context_token_id: int | None = None
 
     def target_groups(self) -> set[str]:
         groups = set()
@@ -75,7 +77,10 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
                        base_model_name: str = "synthetic", ms_code_m: int = 6, ms_memory_gain: float = 28.0,
                        switch_head_dim: int = 32, extra_config: dict | None = None,
                        max_shard_bytes: int = 5 * 1024 ** 3,
-                       control_token_ids: list[int] | None = None) -> GraniteSwitchConfig:
+                       control_token_ids: list[int] | None = None,
+                       extra_token_ids: list[int] | None = None) -> GraniteSwitchConfig:
+    """``extra_token_ids``: other added tokens that need an embedding row and a
+    never-emitted output row (the audio marker), like the control tokens."""
     na = len(adapters)
     cfg = dict(base_config)
     base_vocab = int(cfg["vocab_size"])
@@ -113,7 +118,8 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
             subs.append(int(a.invocation_tokens[0]))
         else:
             subs.append(default_substitute if default_substitute is not None else 0)
-    new_vocab = max(base_vocab, max(ctrl_ids) + 1) if ctrl_ids else base_vocab
+    extra_ids = [int(t) for t in (extra_token_ids or [])]
+    new_vocab = max([base_vocab] + [t + 1 for t in ctrl_ids + extra_ids])
     ranks = [a.max_rank() if a.kind == "lora" else 1 for a in adapters]
     max_rank = max(ranks) if ranks else 8
     kinds = [a.kind for a in adapters]
@@ -177,7 +183,8 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
             t = torch.cat([t, t[reserved:reserved + 1].expand(new_vocab - t.shape[0], -1).clone()], 0)
         else:
             t = t.clone()
-        t[torch.tensor(ctrl_ids, dtype=torch.long)] = t[reserved].clone()
+        if ctrl_ids or extra_ids:
+            t[torch.tensor(ctrl_ids + extra_ids, dtype=torch.long)] = t[reserved].clone()
         sd[key] = t
 
     if any(k == "probe" for k in kinds):

@@ -104,3 +104,47 @@ def test_list_adapters(lib, capsys):
     _, root, _ = lib
     assert compose_main(["--adapters", root, "--target-model", "base", "--list-adapters"]) == 0
     assert "citations" in capsys.readouterr().out
+
+
+def test_compose_cli_with_tokenizer_and_audio(lib, tmp_path):
+    """Base directory with a tokenizer: control tokens, substitutes and the
+    adapter-aware chat template are written with the checkpoint."""
+    from transformers import AutoTokenizer
+
+    from tests.tokenizer_stub import granite_template, make_tokenizer
+
+    base, root, cfg = lib
+    make_tokenizer(granite_template("4.1")).save_pretrained(base)
+    out = str(tmp_path / "out_tok")
+    rc = compose_main(["--adapters", root, "--base-model", base, "--target-model", "base", "--output", out,
+                       "--dtype", "float32", "--enable-audio"])
+    assert rc == 0
+    c = GraniteSwitchConfig.from_pretrained(out)
+    tok = AutoTokenizer.from_pretrained(out)
+    ctrl = dict(zip(c.adapter_names, c.adapter_token_ids))
+    sub = dict(zip(c.adapter_token_ids, c.adapter_substitute_token_ids))
+    assert [tok.convert_ids_to_tokens(ctrl[n]) for n in c.adapter_names] == [f"<|{n}|>" for n in c.adapter_names]
+    marker = tok.convert_tokens_to_ids("<|start_of_role|>")
+    assert sub[ctrl["query_rewrite"]] == marker                       # LoRA: position-0 token
+    inv = json.load(open(os.path.join(root, "answerability", "base", "alora", "adapter_config.json")))
+    assert sub[ctrl["answerability"]] == inv["alora_invocation_tokens"][0]
+    audio = tok.convert_tokens_to_ids("<|audio|>")
+    assert audio < c.vocab_size
+    msgs = [{"role": "user", "content": [{"type": "text", "text": "hi"}, {"type": "audio", "audio": None}]}]
+    plain = tok.apply_chat_template(msgs, tokenize=False, add_generation_prompt=True)
+    assert "hi<|audio|>" in plain
+    lora = tok.apply_chat_template(msgs, tokenize=False, add_generation_prompt=True, adapter_name="query_rewrite")
+    ids = tok.encode(lora, add_special_tokens=False)
+    assert ids[0] == ctrl["query_rewrite"]
+    assert [sub.get(i, i) for i in ids] == tok.encode(plain, add_special_tokens=False)
+    # control and audio rows: never-emitted output rows copied from the reserved token
+    from safetensors.torch import load_file
+
+    sd = {}
+    for f in os.listdir(out):
+        if f.endswith(".safetensors"):
+            sd.update(load_file(os.path.join(out, f)))
+    emb = sd["model.embed_tokens.weight"]
+    reserved = tok.convert_tokens_to_ids("<|unused_1|>")
+    for t in list(ctrl.values()) + [audio]:
+        torch.testing.assert_close(emb[t], emb[reserved])
