@@ -28,6 +28,8 @@ from ..config import SWITCH_CACHE_LAYERS, GraniteSwitchConfig
 from ..routing.codebook import KerdockDGCodeGenerator
 from ..routing.probe_routing import build_adapter_kind_lut
 from ..routing.token_exchange import build_control_to_substitute_lut, validate_control_lut
+from .arch import resolve_arch
+from .validators import audit_saved_checkpoint, validate_cross_stream_population, validate_parameters
 from .weight_transfer import GROUP_PREFIX, fuse_base_weights, module_group, parse_peft_name, stack_adapters
 
 
@@ -96,6 +98,12 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
     dual = any("cross_stream" in a.target_groups() for a in lora_adapters)
     if dual and any("cross_stream" not in a.target_groups() for a in lora_adapters):
         raise ValueError("Shadow Residual and plain LoRA/aLoRA adapters cannot be composed together")
+    arch = resolve_arch(base_config, dual_stream=dual)
+    for a in lora_adapters:
+        arch.check_adapter_modules(a.name, {p[1] for n in a.tensors if (p := parse_peft_name(n))})
+        if dual and {p[1] for n in a.tensors if (p := parse_peft_name(n))} & {"k_proj", "v_proj"}:
+            raise ValueError(f"Shadow Residual adapter {a.name!r} trains k/v: the adapter stream reuses the "
+                             f"base stream's K/V, so k/v LoRA would never apply")
     groups.discard("cross_stream")
     order = ["qkv_proj", "o_proj", "shared_input_linear", "shared_output_linear"]
     target_modules = [g for g in order if g in groups]
@@ -156,13 +164,8 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
 
     # ---- weights
     sd = fuse_base_weights(base_state, n_layers, target_modules)
-    sizes = {"qkv_proj": [nh * hd, nkv * hd, nkv * hd], "o_proj": [h],
-             "shared_input_linear": [inter, inter], "shared_output_linear": [h]}
-    in_sizes = {"qkv_proj": h, "o_proj": nh * hd, "shared_input_linear": h, "shared_output_linear": inter}
-    slice_sizes = {g: sizes[g] for g in target_modules}
-    if dual:
-        slice_sizes["cross_stream"] = [h]
-        in_sizes["cross_stream"] = h
+    sizes, in_sizes = arch.sizes(cfg)
+    slice_sizes = {g: sizes[g] for g in target_modules + (["cross_stream"] if dual else [])}
     padded = [AdapterSpec(a.name, a.tensors, a.r, a.alpha, rank_pattern=a.rank_pattern,
                           alpha_pattern=a.alpha_pattern) if a.kind == "lora"
               else AdapterSpec(a.name, {}, 1, 1.0) for a in adapters]
@@ -212,9 +215,14 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
     if config.tie_word_embeddings:
         sd.pop("lm_head.weight", None)
 
+    validation = validate_parameters(sd, config, arch, adapters, cfg)
+    validation["cross_stream_layers"] = validate_cross_stream_population(sd, config, adapters)
     os.makedirs(out_dir, exist_ok=True)
     config.save_pretrained(out_dir)
     save_state_dict(sd, out_dir, max_shard_bytes=max_shard_bytes)
+    validation["saved_tensors"] = audit_saved_checkpoint(out_dir, sd)
+    validation["arch"] = arch.model_type
+    config.compose_validation = validation
     write_adapter_index(out_dir, config, adapters, base_model_name)
     write_generation_config(out_dir, config)
     return config

@@ -103,6 +103,8 @@ def random_peft_adapter(cfg: dict, rank: int, targets=("q", "k", "v"), seed: int
     shp = _shapes(dict(cfg, intermediate_size=shared or cfg["intermediate_size"]))
     if not shared:  # no dense MLP to adapt
         targets = [t for t in targets if t not in ("gate", "up", "down")]
+    if cross_rank:  # the Shadow-Residual adapter stream reads the base stream's K/V
+        targets = [t for t in targets if t not in ("k", "v")]
     out = {}
     for i in range(cfg["num_hidden_layers"]):
         for t in targets:
