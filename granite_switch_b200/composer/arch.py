@@ -24,19 +24,19 @@ from dataclasses import dataclass
 @dataclass(frozen=True)
 class ModuleGroup:
     name: str                       # composed group key
-    peft_modules: tuple[str, ...]   # PEFT module names feeding the group
+    sources: tuple[tuple[str, int | None], ...]   # (PEFT module name, slice it writes)
     prefix: str                     # composed module path inside a layer
     slices: int
     base_sources: tuple[str, ...]   # base weights concatenated (in order) into the base layer
 
+    @property
+    def peft_modules(self) -> tuple[str, ...]:
+        return tuple(m for m, _ in self.sources)
+
     def slice_of(self, peft_module: str) -> int | None:
         """Slice a PEFT module writes; None for single-slice groups, -1 for a fused
         module that feeds every slice (A duplicated, B chunked)."""
-        if self.slices == 1:
-            return None
-        if len(self.peft_modules) == 1:
-            return -1
-        return self.peft_modules.index(peft_module)
+        return dict(self.sources)[peft_module]
 
 
 @dataclass(frozen=True)
@@ -87,22 +87,25 @@ class ArchSpec:
 
 
 _ATTN = (
-    ModuleGroup("qkv_proj", ("q_proj", "k_proj", "v_proj"), "self_attn.qkv_proj", 3,
+    ModuleGroup("qkv_proj", (("q_proj", 0), ("k_proj", 1), ("v_proj", 2)), "self_attn.qkv_proj", 3,
                 ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight")),
-    ModuleGroup("o_proj", ("o_proj",), "self_attn.o_proj", 1, ("self_attn.o_proj.weight",)),
+    ModuleGroup("o_proj", (("o_proj", None),), "self_attn.o_proj", 1, ("self_attn.o_proj.weight",)),
 )
 _DENSE_MLP = (
-    ModuleGroup("shared_input_linear", ("gate_proj", "up_proj"), "shared_mlp.input_linear", 2,
+    ModuleGroup("shared_input_linear", (("gate_proj", 0), ("up_proj", 1)), "shared_mlp.input_linear", 2,
                 ("mlp.gate_proj.weight", "mlp.up_proj.weight")),
-    ModuleGroup("shared_output_linear", ("down_proj",), "shared_mlp.output_linear", 1, ("mlp.down_proj.weight",)),
+    ModuleGroup("shared_output_linear", (("down_proj", None),), "shared_mlp.output_linear", 1,
+                ("mlp.down_proj.weight",)),
 )
+# GraniteMoeHybrid adapters train the fused input_linear (gate|up); adapters
+# trained on the split names map onto the same slices
 _SHARED_MLP = (
-    ModuleGroup("shared_input_linear", ("input_linear",), "shared_mlp.input_linear", 2,
-                ("shared_mlp.input_linear.weight",)),
-    ModuleGroup("shared_output_linear", ("output_linear",), "shared_mlp.output_linear", 1,
-                ("shared_mlp.output_linear.weight",)),
+    ModuleGroup("shared_input_linear", (("input_linear", -1), ("gate_proj", 0), ("up_proj", 1)),
+                "shared_mlp.input_linear", 2, ("shared_mlp.input_linear.weight",)),
+    ModuleGroup("shared_output_linear", (("output_linear", None), ("down_proj", None)), "shared_mlp.output_linear",
+                1, ("shared_mlp.output_linear.weight",)),
 )
-_CROSS = (ModuleGroup("cross_stream", ("cross_stream",), "cross_stream", 1, ()),)
+_CROSS = (ModuleGroup("cross_stream", (("cross_stream", None),), "cross_stream", 1, ()),)
 
 
 def _spec(model_type: str, cfg: dict, dual: bool) -> ArchSpec:
@@ -110,7 +113,9 @@ def _spec(model_type: str, cfg: dict, dual: bool) -> ArchSpec:
     if model_type == "granite":
         groups, shared = _ATTN + _DENSE_MLP, True
     elif model_type == "granitemoehybrid":
-        shared = int(cfg.get("shared_intermediate_size", 1) or 0) > 0
+        # with experts the shared MLP exists only when shared_intermediate_size > 0;
+        # without experts it carries the dense MLP
+        shared = int(cfg.get("shared_intermediate_size") or 0) > 0 if experts else True
         groups = _ATTN + (_SHARED_MLP if shared else ())
     elif model_type == "granitemoe":
         groups, shared, experts = _ATTN, False, True

@@ -17,6 +17,7 @@ import numpy as np
 import torch
 
 from ..routing.scan import route_flat
+from ..utils.tracing import nvtx_range
 from .kv_cache import BLOCK_SIZE
 from .scheduler import SchedulerOutput
 
@@ -149,6 +150,8 @@ class NativeExecutor:
         self.d2h_bytes = 0
         self.gather_buf = None
         self.use_cuda_graphs = bool(use_cuda_graphs) and tp_size == 1 and model.pipeline is None
+        self.routing_trace = None  # utils.tracing.RoutingTrace: per-step routing records
+        self.nvtx = False          # NVTX range per step (regions: model.prof = NvtxRanges())
         self.graphs: dict[int, _DecodeGraph] = {}
         self.graph_replays = 0
 
@@ -309,15 +312,32 @@ class NativeExecutor:
     def compute_logits(self, out: SchedulerOutput):
         """Run the step; returns ``(HostBatch, fp32 logits [B, vocab])`` for rows that sample."""
         hb = HostBatch(out)
-        p = self._graph_bucket(out)
-        if p is not None:
-            logits = self._run_graph(hb, p)
+        with nvtx_range(f"step {len(hb.ids)} tokens", self.nvtx):
+            p = self._graph_bucket(out)
+            if p is not None:
+                logits = self._run_graph(hb, p)
+            else:
+                logits = self.model.forward(self._stage(hb))
+                if not len(hb.rows):
+                    logits = None
+            if self.routing_trace is not None:
+                self._trace(hb)
+            if logits is None:
+                return hb, None
             return hb, self._gather_logits(logits)
-        batch = self._stage(hb)
-        logits = self.model.forward(batch)
-        if not len(hb.rows) or logits is None:
-            return hb, None
-        return hb, self._gather_logits(logits)
+
+    def _trace(self, hb: HostBatch) -> None:
+        """Record this step's routing from the model's static buffers (valid after a graph replay too)."""
+        t = len(hb.ids)
+        m = self.model
+        if m.n_maps:
+            adapter = m.adapter_idx[:t].to("cpu", torch.int64)
+            lora = m.lora_idx[:t].to("cpu", torch.int64)
+        else:
+            adapter = lora = torch.zeros(t, dtype=torch.int64)
+        rec = self.routing_trace.record([c.req.request_id for c in hb.chunks], hb.ids, hb.pos, adapter, lora,
+                                        torch.where(adapter != lora, adapter, 0))
+        rec["spans"] = [(int(hb.starts[i]), int(hb.starts[i + 1])) for i in range(len(hb.chunks))]
 
     def execute(self, out: SchedulerOutput) -> list[int]:
         from ..ops import elementwise as E
@@ -357,6 +377,7 @@ class ReferenceExecutor:
         sw = ref_model.model.switch
         self.table = sw._table if sw is not None else None
         self.h2d_bytes = self.d2h_bytes = 0
+        self.routing_trace = None
 
     @torch.no_grad()
     def execute(self, out: SchedulerOutput) -> list[int]:
@@ -384,8 +405,12 @@ class ReferenceExecutor:
             lora_idx, probe_idx = self.m.model.switch.split_indices(idx)
             lut = self.m.model.switch.control_to_substitute_lut
         else:
-            lora_idx = probe_idx = torch.zeros_like(ids)
+            idx = lora_idx = probe_idx = torch.zeros_like(ids)
             lut = None
+        if self.routing_trace is not None:
+            rec = self.routing_trace.record([c.req.request_id for c in hb.chunks], hb.ids, hb.pos, idx, lora_idx,
+                                            probe_idx)
+            rec["spans"] = [(int(hb.starts[i]), int(hb.starts[i + 1])) for i in range(len(hb.chunks))]
         mod = apply_token_exchange(lut, ids)
         pos = torch.from_numpy(hb.pos)
         slots = torch.from_numpy(hb.slots)

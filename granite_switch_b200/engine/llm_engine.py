@@ -262,6 +262,22 @@ class LLM:
             executor = ReferenceExecutor(ref, nb)
             self.model = ref
         self.engine = LLMEngine(config, executor, nb, ecfg)
+        # tracing toggles: NVTX ranges per step and forward region; per-step routing records
+        if os.environ.get("GSB_NVTX", "0") == "1" and hasattr(executor, "nvtx"):
+            from ..utils.tracing import NvtxRanges
+
+            executor.nvtx = True
+            executor.model.prof = NvtxRanges(executor.model.prof)
+        if os.environ.get("GSB_ROUTING_TRACE"):
+            self.enable_routing_trace(os.environ["GSB_ROUTING_TRACE"])
+
+    def enable_routing_trace(self, path: str | None = None):
+        """Record each step's routing (ids, positions, adapter / LoRA / probe index per token);
+        returns the :class:`~granite_switch_b200.utils.tracing.RoutingTrace`."""
+        from ..utils.tracing import RoutingTrace
+
+        self.engine.executor.routing_trace = RoutingTrace(path)
+        return self.engine.executor.routing_trace
 
     def generate(self, prompts: list[list[int]], sampling: SamplingParams | list[SamplingParams] | None = None,
                  audios: list | None = None, audio_processor=None) -> list[RequestOutput]:

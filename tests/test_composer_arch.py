@@ -116,3 +116,14 @@ def test_moe_base_rejects_mlp_adapters(tmp_path):
     t = random_peft_adapter(dict(cfg, shared_intermediate_size=64, model_type="granite"), 8, ("q", "gate"), seed=2)
     with pytest.raises(ValueError, match="gate_proj"):
         compose_checkpoint(cfg, random_base_state(cfg), [AdapterSpec("m", t, 8, 16.0)], str(tmp_path / "m"))
+
+
+@pytest.mark.parametrize("shared", [0, 64])
+def test_compose_moe_bases(tmp_path, shared):
+    extra = dict(shared_intermediate_size=shared) if shared else {}
+    config = compose_synthetic(str(tmp_path / f"moe{shared}"), "tiny", num_adapters=2, rank=8,
+                               targets=("q", "v", "gate", "up", "down"), num_local_experts=4,
+                               num_experts_per_tok=2, **extra)
+    v = config.compose_validation
+    assert v["arch"] == "granitemoehybrid"
+    assert ("shared_input_linear" in config.lora_target_modules) == bool(shared)

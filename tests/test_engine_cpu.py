@@ -99,3 +99,25 @@ def test_block_manager_lru_and_hashes():
     r3 = Request([9] * 70)
     bm.match_prefix(r3)
     assert not bm.allocate(r3, 70)  # 5 blocks > 4
+
+
+def test_routing_trace(tiny_dir, tmp_path):
+    """Per-step routing records: positions run 0..n-1 per request and the adapter index switches
+    on at the control token (aLoRA), across chunked-prefill and decode steps."""
+    idx = json.load(open(os.path.join(tiny_dir, "adapter_index.json")))
+    prompts = _prompts(tiny_dir, 3)
+    ecfg = EngineConfig(max_num_seqs=3, max_num_batched_tokens=16, num_kv_blocks=64, max_model_len=256)
+    llm = LLM(tiny_dir, device="cpu", engine_config=ecfg)
+    path = str(tmp_path / "trace.jsonl")
+    trace = llm.enable_routing_trace(path)
+    outs = llm.generate(prompts, SamplingParams(max_tokens=3))
+    for i, (p, o) in enumerate(zip(prompts, outs)):
+        pos = trace.of_request(o.request_id, "positions")
+        ids = trace.of_request(o.request_id, "ids")
+        assert pos == list(range(len(pos))) and ids == (p + o.output_ids)[:len(ids)]
+        ctrl = p.index(idx["adapters"][i % 3]["control_token"]["id"])
+        adapter = trace.of_request(o.request_id, "adapter")
+        assert adapter == [0] * ctrl + [i % 3 + 1] * (len(adapter) - ctrl)
+    trace.flush()
+    lines = open(path).read().splitlines()
+    assert len(lines) == trace.step and json.loads(lines[0])["spans"]

@@ -203,16 +203,21 @@ def test_cuda_graph_decode_matches_eager(tiny_dir):
     from granite_switch_b200.engine import LLM, EngineConfig, SamplingParams
 
     prompts = _prompts(tiny_dir, 11, seed=9)
-    outs = {}
+    outs, routes = {}, {}
     for graphs in (False, True):
         ecfg = EngineConfig(max_num_seqs=16, max_num_batched_tokens=512, num_kv_blocks=256, max_model_len=512,
                             use_cuda_graphs=graphs)
         llm = LLM(tiny_dir, device="cuda:0", engine_config=ecfg)
-        outs[graphs] = [o.output_ids for o in llm.generate(prompts, SamplingParams(max_tokens=12))]
+        trace = llm.enable_routing_trace()
+        res = llm.generate(prompts, SamplingParams(max_tokens=12))
+        outs[graphs] = [o.output_ids for o in res]
+        # the routing trace reads the static buffers, so graph replays are traced too
+        routes[graphs] = [trace.of_request(o.request_id, "adapter") for o in res]
         if graphs:
             ex = llm.engine.executor
             assert ex.graph_replays > 0 and set(ex.graphs) <= {8, 16}
     assert outs[True] == outs[False]
+    assert routes[True] == routes[False] and all(len(r) == len(p) + 11 for r, p in zip(routes[True], prompts))
 
 
 @pytest.fixture(scope="module", params=["moe", "moe_shared"])
