@@ -103,17 +103,30 @@ def err_buffer(device: torch.device) -> torch.Tensor:
     return buf
 
 
+# Sites of bad-index reports (csrc/common.cuh, enum BadIndexSite): err[1] holds the
+# first report's site, err[2] its index.
+BAD_INDEX_SITES = {1: "embedding token id", 2: "rotary position", 3: "KV slot", 4: "attention page id",
+                   5: "tcgen05 attention page id"}
+
+
 def read_errors(device: torch.device, clear: bool = True) -> int:
     """Synchronise and return (optionally clearing) the device error word."""
+    return read_error_detail(device, clear)[0]
+
+
+def read_error_detail(device: torch.device, clear: bool = True) -> tuple[int, str | None, int | None]:
+    """``(error word, site of the first bad index or None, that index)``."""
     buf = err_buffer(device)
-    val = int(buf[0].item())
-    if clear and val:
+    w, site, idx = (int(v) for v in buf[:3].tolist())
+    if clear and (w or site):
         buf.zero_()
-    return val
+    if not site:
+        return w, None, None
+    return w, BAD_INDEX_SITES.get(site, f"site {site}"), idx
 
 
 def check_errors(device: torch.device) -> None:
-    val = read_errors(device)
+    val, site, idx = read_error_detail(device)
     if val:
         names = []
         for bit, name in (
@@ -125,4 +138,5 @@ def check_errors(device: torch.device) -> None:
         ):
             if val & bit:
                 names.append(name)
-        raise RuntimeError(f"device kernels reported errors: {', '.join(names)} (0x{val:x})")
+        where = f"; first bad index: {site} = {idx}" if site else ""
+        raise RuntimeError(f"device kernels reported errors: {', '.join(names)} (0x{val:x}){where}")

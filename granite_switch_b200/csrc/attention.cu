@@ -84,7 +84,7 @@ template <int D, int WARPS_M, int KT, int STAGES>
 __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
     paged_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                       const __nv_bfloat16* __restrict__ q, int64_t q_stride,
-                      const int32_t* __restrict__ block_table, int bt_stride,
+                      const int32_t* __restrict__ block_table, int bt_stride, int num_blocks,
                       const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
                       const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0,
                       int Hq, int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out,
@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
   int32_t* s_pages = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full) + 256);
   const int pg0 = k_begin / PAGE;
   const int n_cached = (n_tiles > 0) ? min((k_end + PAGE - 1) / PAGE - pg0, C::PT_CAP) : 0;
-  for (int i = threadIdx.x; i < n_cached; i += C::THREADS) s_pages[i] = bt[pg0 + i];
+  for (int i = threadIdx.x; i < n_cached; i += C::THREADS) s_pages[i] = checked_index(bt[pg0 + i], num_blocks, err, kSitePage);
   // ---- Q tile via cp.async into the swizzled [half][row][64] layout
   for (int c = threadIdx.x; c < ROWS * DC; c += C::THREADS) {
     const int r = c / DC, ch = c % DC;
@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
   __syncthreads();  // barrier init visible
 
   // producer: one thread issues every box of a key tile
-  const int first_page = bt[0];
+  const int first_page = checked_index(bt[0], num_blocks, err, kSitePage);
   auto issue = [&](int it) {
     const int s = it % STAGES;
     uint8_t* dK = sKV + s * 2 * C::TILE_BYTES;
@@ -161,7 +161,9 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
       // pages past the key range still load a valid page (masked later) so no
       // uninitialised smem (possibly NaN) ever meets a zero probability
       const int pi = j / PAGE - pg0;
-      const int page = (j < k_end) ? (pi < n_cached ? s_pages[pi] : bt[j / PAGE]) : first_page;
+      const int page = (j < k_end) ? (pi < n_cached ? s_pages[pi] : checked_index(bt[j / PAGE], num_blocks, err,
+                                                                                  kSitePage))
+                                   : first_page;
       const int row = (page * Hkv + kvh) * PAGE;
 #pragma unroll
       for (int h = 0; h < D / 64; ++h) {
@@ -414,7 +416,8 @@ using namespace gsb;
 
 template <int D, int WM, int KT, int ST>
 static void launch_attn(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const CUtensorMap& tv,
-                        const at::Tensor& q, const at::Tensor& bt, const at::Tensor& q_start, const at::Tensor& kv_len,
+                        const at::Tensor& q, const at::Tensor& bt, int num_blocks, const at::Tensor& q_start,
+                        const at::Tensor& kv_len,
                         const at::Tensor& work_seq, const at::Tensor& work_row0, int Hq, int Hkv, float scale_log2,
                         const at::Tensor& out, float* wso, float* wsl, int nsplit, int T, uint32_t* err) {
   using C = AttnCfg<D, WM, KT, ST>;
@@ -426,7 +429,8 @@ static void launch_attn(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const
   }
   kfn<<<grid, C::THREADS, C::SMEM, st>>>(
       tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), bt.data_ptr<int32_t>(),
-      (int)bt.stride(0), q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(), work_seq.data_ptr<int32_t>(),
+      (int)bt.stride(0), num_blocks, q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
+      work_seq.data_ptr<int32_t>(),
       work_row0.data_ptr<int32_t>(), Hq, Hkv, scale_log2, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
       out.stride(0), wso, wsl, nsplit, T, err);
   GSB_CUDA_CHECK(cudaGetLastError());
@@ -483,7 +487,8 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
   const float scale_log2 = (float)(scale * 1.4426950408889634);
   dim3 grid(n_work, Hkv, (unsigned)nsplit);
 #define GSB_ATTN(DD, WM, KT, ST)                                                                              \
-  launch_attn<DD, WM, KT, ST>(grid, st, tk, tv, q, block_table, q_start, kv_len, work_seq, work_row0, Hq, Hkv, \
+  launch_attn<DD, WM, KT, ST>(grid, st, tk, tv, q, block_table, (int)k_cache.size(0), q_start, kv_len, work_seq, \
+                              work_row0, Hq, Hkv, \
                               scale_log2, out, wso, wsl, (int)nsplit, T, ep)
   if (D == 128) {
     if (rows_per_tile == 128) GSB_ATTN(128, 8, 64, 2);
@@ -582,14 +587,15 @@ static int setup(int dev, float** scratch, char* msg, size_t len) {
 
 template <int D, int ST>
 static void launch_decode(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const CUtensorMap& tv, const void* q,
-                          int64_t q_stride, const int32_t* bt, int64_t bt_stride, const int32_t* q_start,
+                          int64_t q_stride, const int32_t* bt, int64_t bt_stride, int num_blocks, const int32_t* q_start,
                           const int32_t* kv_len, const int32_t* work_seq, const int32_t* work_row0, int Hq, int Hkv,
                           float scale_log2, void* out, int64_t out_stride, float* wso, float* wsl, int nsplit, int T,
                           uint32_t* err) {
   using C = AttnCfg<D, 1, 64, ST>;
   paged_attn_kernel<D, 1, 64, ST><<<grid, C::THREADS, C::SMEM, st>>>(
-      tk, tv, reinterpret_cast<const __nv_bfloat16*>(q), q_stride, bt, (int)bt_stride, q_start, kv_len, work_seq,
-      work_row0, Hq, Hkv, scale_log2, reinterpret_cast<__nv_bfloat16*>(out), out_stride, wso, wsl, nsplit, T, err);
+      tk, tv, reinterpret_cast<const __nv_bfloat16*>(q), q_stride, bt, (int)bt_stride, num_blocks, q_start, kv_len,
+      work_seq, work_row0, Hq, Hkv, scale_log2, reinterpret_cast<__nv_bfloat16*>(out), out_stride, wso, wsl, nsplit,
+      T, err);
   if (nsplit > 1)
     attn_merge_kernel<D><<<dim3(T, Hq), D, 0, st>>>(wso, wsl, nsplit, T, Hq, reinterpret_cast<__nv_bfloat16*>(out),
                                                     out_stride);
@@ -655,10 +661,12 @@ extern "C" int gsb_decode_attention_noalloc(const void* q, int64_t q_stride, con
     const float scale_log2 = (float)(scale * 1.4426950408889634);
     const dim3 grid(num_work, Hkv, nsplit);
     if (D == 128)
-      launch_decode<128, 3>(grid, stream, tk, tv, q, q_stride, block_table, block_table_stride, q_start, kv_len,
+      launch_decode<128, 3>(grid, stream, tk, tv, q, q_stride, block_table, block_table_stride, (int)num_blocks,
+                            q_start, kv_len,
                             work_seq, work_row0, Hq, Hkv, scale_log2, out, out_stride, wso, wsl, nsplit, T, err);
     else
-      launch_decode<64, 6>(grid, stream, tk, tv, q, q_stride, block_table, block_table_stride, q_start, kv_len,
+      launch_decode<64, 6>(grid, stream, tk, tv, q, q_stride, block_table, block_table_stride, (int)num_blocks,
+                           q_start, kv_len,
                            work_seq, work_row0, Hq, Hkv, scale_log2, out, out_stride, wso, wsl, nsplit, T, err);
   } catch (const std::exception& ex) {
     return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "%s", ex.what());

@@ -57,7 +57,7 @@ template <int D, int KT_>
 __global__ void __launch_bounds__(192, 2)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                              const __nv_bfloat16* __restrict__ q, int64_t q_stride,
-                             const int32_t* __restrict__ block_table, int bt_stride,
+                             const int32_t* __restrict__ block_table, int bt_stride, int num_blocks,
                              const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
                              const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0, int Hq,
                              int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out, int64_t out_stride,
@@ -137,13 +137,13 @@ __global__ void __launch_bounds__(192, 2)
   if (warp == 0) {
     // ---------------- K/V producer: K runs one tile ahead of V ----------------
     if (lane == 0 && n_tiles > 0) {
-      const int first_page = bt[0];
+      const int first_page = checked_index(bt[0], num_blocks, err, kSiteTcPage);
       auto load = [&](uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, int j) {
         mbar_arrive_expect_tx(bar, C::KV_BYTES);
 #pragma unroll 1
         for (int p = 0; p < KT / PAGE; ++p) {
           const int key = j * KT + p * PAGE;
-          const int page = (key < k_end) ? bt[key / PAGE] : first_page;
+          const int page = (key < k_end) ? checked_index(bt[key / PAGE], num_blocks, err, kSiteTcPage) : first_page;
           const int row = (page * Hkv + kvh) * PAGE;
 #pragma unroll
           for (int h = 0; h < D / 64; ++h) tma_load_2d(dst + h * (KT * 128) + p * PAGE * 128, tm, bar, h * 64, row);
@@ -387,7 +387,7 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
     configured[D == 128] = true;
   }
   kfn<<<grid, 192, smem, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
-                                  block_table.data_ptr<int32_t>(), (int)block_table.stride(0),
+                                  block_table.data_ptr<int32_t>(), (int)block_table.stride(0), (int)k_cache.size(0),
                                   q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
                                   work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv,
                                   (float)(scale * 1.4426950408889634),

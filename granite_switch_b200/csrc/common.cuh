@@ -41,6 +41,31 @@ __device__ __forceinline__ void raise_error(uint32_t* err, uint32_t bits) {
   if (err != nullptr) atomicOr(err, bits);
 }
 
+// Data-dependent indices (token ids, positions, KV slots, page ids) are
+// checked against their tensor's extent; a bad one is replaced by a safe value
+// (its access skipped or pointed at entry 0), kErrBadShape is set, and the
+// first report's site and index land in err[1] / err[2] for the host.
+enum BadIndexSite : uint32_t {
+  kSiteEmbedId = 1,    // token id >= embedding rows
+  kSiteRopePos = 2,    // position >= rotary table rows
+  kSiteKvSlot = 3,     // KV slot >= cache slots
+  kSitePage = 4,       // block-table page id >= cache blocks (paged attention)
+  kSiteTcPage = 5,     // same, tcgen05 prefill attention
+};
+
+__device__ __forceinline__ void report_bad_index(uint32_t* err, uint32_t site, int64_t idx) {
+  if (err == nullptr) return;
+  atomicOr(err, (uint32_t)kErrBadShape);
+  if (atomicCAS(err + 1, 0u, site) == 0u) err[2] = (uint32_t)idx;
+}
+
+// ``v`` if 0 <= v < n, else 0 after a report.
+__device__ __forceinline__ int checked_index(int v, int n, uint32_t* err, uint32_t site) {
+  if ((unsigned)v < (unsigned)n) return v;
+  report_bad_index(err, site, v);
+  return 0;
+}
+
 // ---- small math -------------------------------------------------------------
 __device__ __forceinline__ float bf2f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16_rn(v); }

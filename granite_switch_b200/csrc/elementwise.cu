@@ -87,7 +87,7 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat1
     if (s >= 0) id = s;
   }
   if (id < 0 || id >= vocab) {
-    if (threadIdx.x == 0) raise_error(err, kErrBadShape);
+    if (threadIdx.x == 0) report_bad_index(err, kSiteEmbedId, id);
     id = 0;
   }
   const uint4* src = reinterpret_cast<const uint4*>(table + id * (int64_t)H);
@@ -118,7 +118,7 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ldq,
   const int t = blockIdx.x;
   int64_t pos = positions[t];
   if (pos < 0 || pos >= max_pos) {
-    if (threadIdx.x == 0) raise_error(err, kErrBadShape);
+    if (threadIdx.x == 0) report_bad_index(err, kSiteRopePos, pos);
     pos = 0;
   }
   const float* cs = cos_sin + pos * D;
@@ -158,7 +158,7 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ldq,
       *reinterpret_cast<uint4*>(v_cache + ((blk * Hkv + kh) * BS + off) * D + d0) = q;
     }
   } else if (slot >= num_slots && threadIdx.x == 0) {
-    raise_error(err, kErrBadShape);
+    report_bad_index(err, kSiteKvSlot, slot);
   }
 }
 

@@ -25,8 +25,6 @@ nvcc_flags = [
     "--expt-relaxed-constexpr",
     "-DNDEBUG",
 ]
-if os.environ.get("GSB_DEBUG_BOUNDS") == "1":
-    nvcc_flags.append("-DGSB_DEBUG_BOUNDS=1")
 if os.environ.get("GSB_PTXAS_VERBOSE") == "1":
     nvcc_flags.append("-Xptxas=-v")
 

@@ -212,3 +212,43 @@ def test_prefill_attention_tcgen05(case, d):
     err = (out.float() - ref).abs().max().item()
     assert err < 3e-2, err
     _check()
+
+
+def test_bad_indices_reported_not_faulted():
+    """A token id or page id outside its tensor is replaced by entry 0 and reported with its
+    site and value. The tensors given to the kernels are prefix views of larger allocations,
+    so even an unchecked access would stay inside allocated memory."""
+    from granite_switch_b200._native import read_error_detail
+    from granite_switch_b200.ops import attention as A
+    from granite_switch_b200.ops import elementwise as E
+
+    dev = torch.device("cuda", 0)
+    read_error_detail(dev)  # start clean
+    table = torch.randn(300, 64, device="cuda").bfloat16()
+    view = table[:290]
+    out = E.embed(torch.tensor([1, 295, 2], device="cuda"), view, None, 1.0)
+    w, site, idx = read_error_detail(dev)
+    assert w & 8 and site == "embedding token id" and idx == 295
+    assert torch.equal(out[1], view[0]) and torch.equal(out[0], view[1])
+
+    hq, hkv, d = 8, 2, 128
+    kv_lens = [300, 500]
+    kc, vc, bt = _make_cache(kv_lens, hkv, d)
+    n_ok = kc.shape[0] - 3
+    assert int(bt.max()) >= n_ok  # some pages fall outside the view
+    q_lens = [1, 1]
+    q = torch.randn(2, (hq + 2 * hkv) * d, device="cuda").bfloat16()
+    out = torch.zeros(2, hq * d, device="cuda").bfloat16()
+    ws, wr = A.build_work(q_lens, hq // hkv, 16)
+    i32 = dict(dtype=torch.int32, device="cuda")
+    args = (torch.tensor([0, 1, 2], **i32), torch.tensor(kv_lens, **i32), torch.tensor(ws, **i32),
+            torch.tensor(wr, **i32))
+    A.paged_attention(q, kc[:n_ok], vc[:n_ok], bt, *args, 16, hq, 0.1, out)
+    w, site, idx = read_error_detail(dev)
+    assert w & 8 and site == "attention page id" and idx >= n_ok
+    ws, wr = A.build_work(q_lens, hq // hkv, 128)
+    args = args[:2] + (torch.tensor(ws, **i32), torch.tensor(wr, **i32))
+    A.prefill_attention_tc(q, kc[:n_ok], vc[:n_ok], bt, *args, hq, 0.1, out)
+    w, site, idx = read_error_detail(dev)
+    assert w & 8 and site == "tcgen05 attention page id" and idx >= n_ok
+    assert torch.isfinite(out.float()).all()
