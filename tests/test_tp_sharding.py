@@ -110,3 +110,28 @@ def test_pipeline_layer_split():
     spans = [split_layers(7, s, 4) for s in range(4)]
     assert spans[0][0] == 0 and spans[-1][1] == 7
     assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+
+
+@pytest.mark.parametrize("fault", ["lora_a_wrong_shard", "lora_b_wrong_shard", "skip_row_reduce", "base_wrong_shard"])
+def test_sharding_faults_are_detected(fault):
+    """Sensitivity guard (reference: tests/vllm/_tp_integration_worker.py:56-144, GS_TP_FAULT):
+    the row-parallel comparison must fail when a shard or the reduction is wrong."""
+    torch.manual_seed(3)
+    tp, k, n, na, r = 2, 64, 48, 2, 8
+    w = torch.randn(n, k)
+    la = [torch.randn(na, 1, r, k) * 0.3]
+    lb = [torch.randn(na, 1, n, r) * 0.3]
+    x = torch.randn(5, k)
+    idx = torch.tensor([1, 0, 2, 2, 1])
+    ref = _full(w, la, lb, x, idx, [n])
+    pls = [pack_linear(w, la, lb, [n], na, "cpu", dtype=torch.float32, tp_rank=rk, tp_size=tp, parallel="row")
+           for rk in range(tp)]
+    if fault == "lora_a_wrong_shard":
+        pls[0].a_all, pls[1].a_all = pls[1].a_all, pls[0].a_all
+    elif fault == "lora_b_wrong_shard":
+        pls[0].lb = pls[0].lb * 0.5
+    elif fault == "base_wrong_shard":
+        pls[0].w, pls[1].w = pls[1].w, pls[0].w
+    parts = [_apply(pl, x[:, rk * (k // tp):(rk + 1) * (k // tp)], idx) for rk, pl in enumerate(pls)]
+    total = parts[0] if fault == "skip_row_reduce" else parts[0] + parts[1]
+    assert not torch.allclose(total, ref, rtol=1e-3, atol=1e-3)
