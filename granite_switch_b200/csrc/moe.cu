@@ -133,9 +133,13 @@ __global__ void moe_scatter_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   const int t = w / K;
   int pos = 0;
   if (lane == 0) {
-    const int e = ids[w];
-    pos = offsets[e] + atomicAdd(&cursor[e], 1);
-    slot[w] = pos;
+    if (cursor != nullptr) {
+      const int e = ids[w];
+      pos = offsets[e] + atomicAdd(&cursor[e], 1);
+      slot[w] = pos;
+    } else {
+      pos = slot[w];  // slots of an earlier scatter with the same routing
+    }
   }
   pos = __shfl_sync(0xffffffffu, pos, 0);
   const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)t * ldx);
@@ -233,6 +237,27 @@ void gsb_moe_scatter(const at::Tensor& x, const at::Tensor& ids, const at::Tenso
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), T, K, H, ids.data_ptr<int32_t>(),
       offsets.data_ptr<int32_t>(), cursor.data_ptr<int32_t>(), slot.data_ptr<int32_t>(),
       reinterpret_cast<__nv_bfloat16*>(xp.data_ptr()), xp.stride(0));
+  GSB_CUDA_CHECK(cudaGetLastError());
+}
+
+// Scatter x's rows to the slots an earlier gsb_moe_scatter assigned (same routing,
+// another stream of hidden states: the Shadow-Residual adapter stream reuses the
+// base stream's expert choice). slot [T*K] int32.
+void gsb_moe_scatter_slots(const at::Tensor& x, const at::Tensor& slot, int64_t top_k, const at::Tensor& xp) {
+  using namespace gsb;
+  const int T = (int)x.size(0), H = (int)x.size(1), K = (int)top_k;
+  if (T == 0) return;
+  GSB_CHECK(x.scalar_type() == at::kBFloat16 && xp.scalar_type() == at::kBFloat16 && H % 8 == 0 &&
+                x.stride(0) % 8 == 0 && xp.stride(0) % 8 == 0 && xp.size(1) == H,
+            "moe_scatter_slots: bf16 rows of equal, 16-byte aligned width required");
+  GSB_CHECK(slot.scalar_type() == at::kInt && slot.numel() >= (int64_t)T * K && K >= 1 && K <= kMoeMaxK,
+            "moe_scatter_slots: int32 slot [T * k] required");
+  c10::cuda::CUDAGuard g(x.device());
+  const int threads = 256;
+  const int64_t warps = (int64_t)T * K;
+  moe_scatter_kernel<<<(unsigned)((warps * 32 + threads - 1) / threads), threads, 0, moe_stream(x)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), T, K, H, nullptr, nullptr, nullptr,
+      slot.data_ptr<int32_t>(), reinterpret_cast<__nv_bfloat16*>(xp.data_ptr()), xp.stride(0));
   GSB_CUDA_CHECK(cudaGetLastError());
 }
 

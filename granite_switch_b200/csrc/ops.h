@@ -61,6 +61,7 @@ void gsb_moe_route(const at::Tensor& logits, int64_t num_experts, int64_t top_k,
                    const at::Tensor& tile_expert);
 void gsb_moe_scatter(const at::Tensor& x, const at::Tensor& ids, const at::Tensor& offsets, const at::Tensor& cursor,
                      const at::Tensor& slot, const at::Tensor& xp);
+void gsb_moe_scatter_slots(const at::Tensor& x, const at::Tensor& slot, int64_t top_k, const at::Tensor& xp);
 void gsb_moe_combine(const at::Tensor& yp, const at::Tensor& slot, const at::Tensor& wts, int64_t top_k,
                      const c10::optional<at::Tensor>& shared, const c10::optional<at::Tensor>& residual, double scale,
                      const at::Tensor& out);

@@ -91,9 +91,6 @@ class NativeGraniteSwitch:
         self.inter = config.shared_intermediate_size // tp_size
         self.has_shared_mlp = config.shared_intermediate_size > 0
         self.has_moe = int(getattr(config, "num_local_experts", 0) or 0) > 0
-        if self.has_moe and getattr(config, "dual_stream", False):
-            raise NotImplementedError("Shadow-Residual adapters over a mixture-of-experts base are served by the "
-                                      "HF-style model only")
         self.vocab = config.vocab_size
         # pipeline parallelism: this stage owns decoder layers [layer_lo, layer_hi)
         self.pipeline = pipeline
@@ -447,26 +444,36 @@ class NativeGraniteSwitch:
         G.lora_shrink(hbase, pl.a_all, ra, pl.rank, pl.n_local, out=s)
         G.switched_gemm(s, pl.lb, h, epi=G.EPI_RESADD, residual=h, scale=1.0)
 
-    def _mlp(self, lw: LayerWeights, x: torch.Tensor, act: torch.Tensor, h: torch.Tensor, mult: float) -> None:
-        """``h <- h + MLP(x) * mult``: shared MLP, expert bank, or their sum (summed over TP ranks)."""
+    def _mlp(self, lw: LayerWeights, x: torch.Tensor, act: torch.Tensor, h: torch.Tensor, mult: float,
+             lora: bool = True, reuse_routing: bool = False, partial: torch.Tensor | None = None) -> None:
+        """``h <- h + MLP(x) * mult``: shared MLP, expert bank, or their sum (summed over TP ranks).
+
+        ``lora=False`` runs base weights only; ``reuse_routing`` sends ``x`` to the
+        experts (and slots) chosen by the previous call, which is how the
+        Shadow-Residual adapter stream shares the base stream's routing
+        (reference: src/granite_switch/hf/modeling_granite_switch.py:232-340).
+        """
         R = self._region
         if lw.moe is None:
             with R("gate_up+swiglu"):
-                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
+                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU, lora=lora)
             with R("down"):
-                self._row_parallel(lw.down, act, h, mult)
+                self._row_parallel(lw.down, act, h, mult, lora=lora, partial=partial)
             return
         m = x.shape[0]
         moe = lw.moe
         nat = native()
+        k = moe.top_k
         with R("moe_route"):
-            logits = self.moe_logits[:m]
-            G.switched_gemm(x, moe.router, logits, epi=G.EPI_F32)
-            k = moe.top_k
-            nat.moe_route(logits, moe.num_experts, k, self.moe_ids[: m * k], self.moe_wts[: m * k],
-                          self.moe_counts, self.moe_offsets, self.moe_cursor, self.moe_tiles)
-            nat.moe_scatter(x, self.moe_ids[: m * k], self.moe_offsets, self.moe_cursor, self.moe_slot[: m * k],
-                            self.moe_xp)
+            if reuse_routing:
+                nat.moe_scatter_slots(x, self.moe_slot[: m * k], k, self.moe_xp)
+            else:
+                logits = self.moe_logits[:m]
+                G.switched_gemm(x, moe.router, logits, epi=G.EPI_F32)
+                nat.moe_route(logits, moe.num_experts, k, self.moe_ids[: m * k], self.moe_wts[: m * k],
+                              self.moe_counts, self.moe_offsets, self.moe_cursor, self.moe_tiles)
+                nat.moe_scatter(x, self.moe_ids[: m * k], self.moe_offsets, self.moe_cursor,
+                                self.moe_slot[: m * k], self.moe_xp)
         rows = min(self.moe_pmax, (m * k + 127 * moe.num_experts + 127) // 128 * 128)
         tiles = self.moe_tiles[: rows // 128]
         with R("moe_experts"):
@@ -476,10 +483,10 @@ class NativeGraniteSwitch:
         shared = None
         if lw.gu is not None:
             with R("gate_up+swiglu"):
-                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
+                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU, lora=lora)
             with R("down"):
                 shared = self.x2[:m]
-                self._proj(lw.down, act, shared, epi=G.EPI_STORE)
+                self._proj(lw.down, act, shared, epi=G.EPI_STORE, lora=lora)
         with R("moe_combine"):
             if self.tp_size == 1:
                 nat.moe_combine(self.moe_yp, self.moe_slot[: m * k], self.moe_wts[: m * k], k, shared, h, mult, h)
@@ -633,19 +640,14 @@ class NativeGraniteSwitch:
             self._attention(b, qa, kc, vc, attn, scale)
             with R("o"):
                 self._row_parallel(lw.o, attn, h, mult)
-            # MLPs: base stream first (its output feeds the cross stream)
+            # MLPs: base stream first (its output feeds the cross stream; with
+            # experts, its routing is the adapter stream's too)
             with R("rmsnorm"):
                 E.rmsnorm(hb, lw.post_norm, eps, out=x)
-            with R("gate_up+swiglu"):
-                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU, lora=False)
-            with R("down"):
-                self._row_parallel(lw.down, act, hb, mult, lora=False, partial=hb2)
+            self._mlp(lw, x, act, hb, mult, lora=False, partial=hb2)
             with R("rmsnorm"):
                 E.rmsnorm(h, lw.post_norm, eps, out=x)
-            with R("gate_up+swiglu"):
-                self._proj(lw.gu, x, act, epi=G.EPI_SWIGLU)
-            with R("down"):
-                self._row_parallel(lw.down, act, h, mult)
+            self._mlp(lw, x, act, h, mult, reuse_routing=True)
             with R("cross_stream"):
                 self._cross_stream(lw.cross, hb, h)
             if b.probe_groups:

@@ -220,14 +220,16 @@ def test_cuda_graph_decode_matches_eager(tiny_dir):
     assert routes[True] == routes[False] and all(len(r) == len(p) + 11 for r, p in zip(routes[True], prompts))
 
 
-@pytest.fixture(scope="module", params=["moe", "moe_shared"])
+@pytest.fixture(scope="module", params=["moe", "moe_shared", "moe_sr"])
 def moe_dir(request, tmp_path_factory):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA")
     from granite_switch_b200.composer.synthetic import compose_synthetic
 
     d = str(tmp_path_factory.mktemp("eng_gpu_" + request.param))
-    extra = dict(shared_intermediate_size=512) if request.param == "moe_shared" else {}
+    extra = dict(shared_intermediate_size=512) if request.param != "moe" else {}
+    if request.param == "moe_sr":  # Shadow Residual: the adapter stream shares the base stream's routing
+        extra.update(cross_rank=16, std_b=0.03)
     targets = ("q", "k", "v", "o", "gate", "up", "down") if extra else ("q", "k", "v", "o")
     compose_synthetic(d, "tiny", num_adapters=3, rank=8, targets=targets, seed=6, dtype=torch.float32,
                       invocation_len=4, alpha=16.0, num_hidden_layers=2, num_local_experts=8,
