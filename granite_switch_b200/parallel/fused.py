@@ -70,6 +70,9 @@ class FusedTPComm:
         # large steps reduce through NCCL; GSB_TP_SWITCH_ALLREDUCE=1 selects the switch
         # all-reduce kernel instead (under investigation, see the TP self-check)
         self.switch_allreduce = os.environ.get("GSB_TP_SWITCH_ALLREDUCE", "0") == "1"
+        # diagnostics: compare every switch all-reduce with NCCL on a copy of the partial
+        self.debug_compare = os.environ.get("GSB_TP_DEBUG_COMPARE", "0") == "1"
+        self.calls = 0
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
 
@@ -107,13 +110,32 @@ class FusedTPComm:
             else:
                 model._proj(pl, x, y, epi=G.EPI_STORE, scale=mult)
             if self.switch_allreduce:
+                chk = y.clone() if self.debug_compare else None
                 self.barrier()
                 native().allreduce_ldreduce_p2p(self.mc, self.y_ptrs, b * self.max_tokens * self.hidden * 2,
                                                 m * self.hidden * 2, self.rank, self.world)
                 self.barrier()
+                if chk is not None:
+                    self._compare(y, chk, b)
             else:
                 torch.distributed.all_reduce(y, group=self.group)
         return y
+
+    def _compare(self, y: torch.Tensor, partial: torch.Tensor, b: int) -> None:
+        """Diagnostics: this rank's switch all-reduce result vs NCCL's sum of the same
+        partials, and this rank's result vs rank 0's (every rank must hold the same sum)."""
+        import torch.distributed as dist
+
+        dist.all_reduce(partial, group=self.group)
+        d = (y.float() - partial.float()).abs()
+        bad = (d > 1e-2 * partial.float().abs().amax() + 1e-3).nonzero()
+        y0 = y.clone()
+        dist.broadcast(y0, src=dist.get_global_rank(self.group, 0), group=self.group)
+        first = bad[0].tolist() if len(bad) else None
+        print(f"[tp-compare] rank {self.rank} call {self.calls} buf {b} m {y.shape[0]} "
+              f"max_diff_vs_nccl {float(d.max()):.4g} bad {len(bad)} first {first} "
+              f"max_diff_vs_rank0 {float((y.float() - y0.float()).abs().max()):.4g}", flush=True)
+        self.calls += 1
 
     def finish(self, y: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor, x: torch.Tensor, eps: float) -> None:
         """``h <- y; x <- RMSNorm(y) * norm_w; y <- 0``."""
