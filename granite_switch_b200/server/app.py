@@ -110,19 +110,24 @@ def build_app(async_engine: AsyncEngine, tokenizer=None, model_name: str = "gran
         if tokenizer is None:
             raise HTTPException(400, "chat completions need the checkpoint's tokenizer")
         kwargs = dict(body.get("chat_template_kwargs") or {})
-        text = tokenizer.apply_chat_template(body["messages"], add_generation_prompt=True, tokenize=False, **kwargs)
+        kwargs.setdefault("add_generation_prompt", bool(body.get("add_generation_prompt", True)))
+        text = tokenizer.apply_chat_template(body["messages"], tokenize=False, **kwargs)
         ids = tokenizer(text, add_special_tokens=False)["input_ids"]
         sp = _sampling(body)
         try:
             r = await async_engine.generate(ids, sp)
         except ValueError as e:
             raise HTTPException(400, str(e)) from e
-        return JSONResponse({
+        out = {
             "id": f"chatcmpl-{uuid.uuid4().hex[:24]}", "object": "chat.completion", "created": int(time.time()),
             "model": model_name,
             "choices": [{"index": 0, "message": {"role": "assistant", "content": decode(r.output_ids)},
                          "finish_reason": r.finish_reason}],
-            "usage": usage([r])})
+            "usage": usage([r])}
+        if body.get("return_token_ids"):
+            out["prompt_token_ids"] = list(ids)
+            out["choices"][0]["token_ids"] = r.output_ids
+        return JSONResponse(out)
 
     return app
 

@@ -58,3 +58,46 @@ def test_streaming(client):
     for l in lines[:-1]:
         toks += json.loads(l[6:])["choices"][0]["token_ids"]
     assert len(toks) == 3
+
+
+def test_chat_completions_place_the_control_token(tmp_path):
+    """Chat requests render the composed chat template: ``chat_template_kwargs.adapter_name``
+    puts the adapter's control token in the prompt, and the prompt shares its prefix with the
+    base render (aLoRA at the assistant boundary)."""
+    from fastapi.testclient import TestClient
+
+    from granite_switch_b200.composer.compose import compose_checkpoint
+    from granite_switch_b200.composer.synthetic import base_config, random_base_state, synthetic_adapters
+    from granite_switch_b200.composer.tokenizer_setup import configure_tokenizer, encode
+    from granite_switch_b200.engine import LLM, EngineConfig
+    from granite_switch_b200.server.app import build_app
+    from granite_switch_b200.server.async_engine import AsyncEngine
+    from tests.tokenizer_stub import granite_template, make_tokenizer
+
+    tok = make_tokenizer(granite_template("4.1"))
+    cfg = base_config("tiny", num_hidden_layers=2)
+    ads = synthetic_adapters(cfg, 2, 8, ("q", "k", "v", "o"), seed=1)
+    for a in ads:
+        a.invocation_tokens = encode(tok, "<|start_of_role|>assistant<|end_of_role|>")
+    ids, setup = configure_tokenizer(tok, ads)
+    d = str(tmp_path / "chat")
+    compose_checkpoint(cfg, random_base_state(cfg), ads, d, dtype=torch.float32, control_token_ids=ids,
+                       default_substitute=setup.lora_substitute)
+    llm = LLM(d, device="cpu", engine_config=EngineConfig(max_num_seqs=4, max_num_batched_tokens=256,
+                                                          num_kv_blocks=64, max_model_len=512))
+    ae = AsyncEngine(llm.engine, "tiny")
+    msgs = [{"role": "user", "content": "Is the sky blue?"}]
+    try:
+        with TestClient(build_app(ae, tok, "tiny")) as c:
+            plain = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 2, "return_token_ids": True})
+            assert plain.status_code == 200, plain.text
+            r = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 2, "return_token_ids": True,
+                                                     "chat_template_kwargs": {"adapter_name": "adapter_1"}})
+            assert r.status_code == 200, r.text
+            p0, p1 = plain.json()["prompt_token_ids"], r.json()["prompt_token_ids"]
+            assert ids[1] in p1 and ids[1] not in p0
+            cut = p1.index(ids[1])
+            assert p1[:cut] == p0[:cut] and len(p1) == len(p0)
+            assert r.json()["usage"]["prompt_tokens_details"]["cached_tokens"] >= 16 * (cut // 16) > 0
+    finally:
+        ae.shutdown()
