@@ -90,8 +90,9 @@ def filter_adapters(found: list[FoundAdapter], include=None, exclude=None, techn
     return out
 
 
-def resolve(sources: list[str], target_model: str | None = None, technology: str | None = None) -> list[FoundAdapter]:
-    """Resolve each ``--adapters`` source (library dir, adapter dir, YAML file, or a cached HF repo)."""
+def resolve(sources: list[str], target_model: str | None = None, technology: str | None = None,
+            include=None, exclude=None) -> list[FoundAdapter]:
+    """Resolve each ``--adapters`` source (library dir, adapter dir, YAML file, or a Hugging Face repo)."""
     found: list[FoundAdapter] = []
     for src in sources:
         if src.endswith((".yaml", ".yml")) and os.path.isfile(src):
@@ -99,18 +100,40 @@ def resolve(sources: list[str], target_model: str | None = None, technology: str
         elif os.path.isdir(src):
             found += discover_library(src, target_model, technology)
         else:
-            local = _hf_snapshot(src)
+            local = _hf_snapshot(src, target_model, include, exclude, technology)
             if local is None:
                 raise FileNotFoundError(
-                    f"adapter source {src!r} is neither a local path nor a locally cached Hugging Face repo")
+                    f"adapter source {src!r} is neither a local path nor a reachable or cached Hugging Face repo")
             found += discover_library(local, target_model, technology)
     return found
 
 
-def _hf_snapshot(repo: str) -> str | None:
+def hf_patterns(target_model: str | None, include=None, exclude=None, technology: str | None = None):
+    """``(allow_patterns, ignore_patterns)`` for a selective download of an adapter library laid
+    out ``<adapter>/<model>/<technology>/...`` (reference: adapter_discovery.py:488-571): only
+    the target model's adapters, the requested technology and the included names."""
+    if not target_model:
+        allow = None
+    else:
+        techs = [technology] if technology in ("alora", "lora") else ["alora", "lora"]
+        short = target_model.rstrip("/").split("/")[-1]  # library dirs use the model's short name
+        allow = [f"{n}/{short}/{t}/*" for n in (include or ["*"]) for t in techs]
+        allow += ["*.yaml", "*.yml", "README*"]
+    ignore = [f"{e}/*" for e in (exclude or [])] or None
+    return allow, ignore
+
+
+def _hf_snapshot(repo: str, target_model=None, include=None, exclude=None, technology=None) -> str | None:
+    """Download (selectively) or find in the local cache; None when neither works."""
     try:
         from huggingface_hub import snapshot_download
-
-        return snapshot_download(repo, local_files_only=True)
-    except Exception:
+    except ImportError:
         return None
+    allow, ignore = hf_patterns(target_model, include, exclude, technology)
+    offline = os.environ.get("HF_HUB_OFFLINE", "0") not in ("0", "", "false")
+    for local_only in ((True,) if offline else (False, True)):
+        try:
+            return snapshot_download(repo, allow_patterns=allow, ignore_patterns=ignore, local_files_only=local_only)
+        except Exception:
+            continue
+    return None

@@ -116,7 +116,8 @@ def compose_main(argv=None) -> int:
     args = build_argparser().parse_args(argv)
     base_path = _resolve_local(args.base_model) if not args.list_adapters else args.base_model
     target = args.target_model or args.base_model
-    found = resolve(args.adapters, target, None) if args.adapters else []
+    found = resolve(args.adapters, target, args.technology_filter, args.include_adapters,
+                    args.exclude_adapters) if args.adapters else []
     found = filter_adapters(found, args.include_adapters, args.exclude_adapters, args.technology_filter)
     if args.list_adapters:
         for a in found:

@@ -148,3 +148,27 @@ def test_compose_cli_with_tokenizer_and_audio(lib, tmp_path):
     reserved = tok.convert_tokens_to_ids("<|unused_1|>")
     for t in list(ctrl.values()) + [audio]:
         torch.testing.assert_close(emb[t], emb[reserved])
+
+
+def test_hf_repo_selective_download(lib, monkeypatch, tmp_path):
+    """A repo id resolves through huggingface_hub with patterns limited to the target model,
+    the included adapters and the technology (no network here: the download is faked)."""
+    import huggingface_hub
+
+    from granite_switch_b200.composer.adapter_discovery import hf_patterns, resolve
+
+    _, root, _ = lib
+    calls = []
+
+    def fake(repo, allow_patterns=None, ignore_patterns=None, local_files_only=False):
+        calls.append((repo, allow_patterns, ignore_patterns, local_files_only))
+        return root
+
+    monkeypatch.setattr(huggingface_hub, "snapshot_download", fake)
+    monkeypatch.delenv("HF_HUB_OFFLINE", raising=False)
+    found = resolve(["org/granitelib"], "base", "alora", include=["ans*", "cit*"], exclude=["cit*"])
+    assert calls[0][0] == "org/granitelib" and calls[0][3] is False
+    assert calls[0][1][:2] == ["ans*/base/alora/*", "cit*/base/alora/*"] and calls[0][2] == ["cit*/*"]
+    assert {f.name for f in found} == {"answerability", "citations"}
+    assert hf_patterns(None) == (None, None)
+    assert hf_patterns("ibm-granite/granite-4.1-3b", technology="lora")[0][0] == "*/granite-4.1-3b/lora/*"
