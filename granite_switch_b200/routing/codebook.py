@@ -161,7 +161,16 @@ class KerdockDGCodeGenerator:
         vec = (1.0 - 2.0 * bits) / np.sqrt(self.N)
         return torch.tensor(vec, dtype=dtype)
 
+    #: largest codebook written into a checkpoint (the buffer ships with every model)
+    MAX_CODEBOOK_BYTES = 128 * 1024 * 1024
+
     def precompute_codebook(self, dtype=torch.float32) -> torch.Tensor:
+        """All ``[capacity, N]`` code vectors; raises for codebooks above 128 MB (DG(8, 1):
+        4.2M vectors of dimension 256), which would have to be generated on the fly."""
+        size = self.capacity * self.N * 4
+        if size > self.MAX_CODEBOOK_BYTES:
+            raise ValueError(f"codebook of {self.capacity} x {self.N} fp32 is {size / 2**20:.0f} MB, above the "
+                             f"{self.MAX_CODEBOOK_BYTES // 2**20} MB a checkpoint carries")
         return self.generate_code_vectors_batch(range(self.capacity), dtype=dtype)
 
 

@@ -116,3 +116,16 @@ def test_token_exchange_and_probe_split():
     kind = build_adapter_kind_lut(_Cfg)
     lora, probe = split_adapter_indices(kind, torch.tensor([0, 1, 2, 1]))
     assert lora.tolist() == [0, 1, 0, 1] and probe.tolist() == [0, 0, 2, 0]
+
+
+def test_codebook_size_limit():
+    """DG(6, 1) (65,536 x 64, coherence 1/4) is written; DG(8, 1) (4.2M x 256, 4 GB) is refused."""
+    import pytest
+    import torch
+
+    from granite_switch_b200.routing.codebook import KerdockDGCodeGenerator
+
+    cb = KerdockDGCodeGenerator(m=6, code_type="dg1").precompute_codebook(torch.float32)
+    assert tuple(cb.shape) == (65536, 64)
+    with pytest.raises(ValueError, match="MB"):
+        KerdockDGCodeGenerator(m=8, code_type="dg1").precompute_codebook(torch.float32)
