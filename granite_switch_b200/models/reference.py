@@ -474,8 +474,15 @@ class GraniteSwitchForCausalLM(nn.Module):
 
     @classmethod
     def from_pretrained(cls, path: str, dtype: torch.dtype = torch.float32, device="cpu",
-                        strict: bool = True) -> "GraniteSwitchForCausalLM":
+                        strict: bool = True, **hf_kwargs) -> "GraniteSwitchForCausalLM":
+        """Load a composed directory. ``hf_kwargs`` are what ``AutoModelForCausalLM``
+        passes (``config``, ``torch_dtype`` / ``dtype``, hub options): a dtype among them
+        is honoured, the rest is ignored since the checkpoint is read locally."""
         from ..checkpoint import load_state_dict
+
+        hf_dtype = hf_kwargs.get("torch_dtype", hf_kwargs.get("dtype"))
+        if isinstance(hf_dtype, torch.dtype):
+            dtype = hf_dtype
 
         config = GraniteSwitchConfig.from_pretrained(path)
         model = cls(config)

@@ -137,3 +137,18 @@ def test_config_validation_errors():
     assert c.has_base_reset and c.lora_target_modules[:2] == ["qkv_proj", "o_proj"]
     d = GraniteSwitchConfig.from_dict(c.to_dict())
     assert d == c
+
+
+def test_transformers_auto_classes(tiny_dir):
+    """Importing granite_switch_b200.hf registers model_type granite_switch with transformers' Auto classes."""
+    import granite_switch_b200.hf  # noqa: F401
+    from transformers import AutoConfig, AutoModelForCausalLM
+
+    cfg = AutoConfig.from_pretrained(tiny_dir)
+    assert cfg.model_type == "granite_switch"
+    assert cfg.to_native().adapter_token_ids == GraniteSwitchConfig.from_pretrained(tiny_dir).adapter_token_ids
+    m = AutoModelForCausalLM.from_pretrained(tiny_dir)
+    assert isinstance(m, GraniteSwitchForCausalLM)
+    ids = torch.randint(1, 900, (1, 12))
+    with torch.no_grad():
+        torch.testing.assert_close(m(ids).logits, GraniteSwitchForCausalLM.from_pretrained(tiny_dir)(ids).logits)
