@@ -383,6 +383,25 @@ class GraniteSwitchModel(nn.Module):
         self._last["probe"] = None if markers is None else (*markers, verdict)
         return h, cache
 
+    # routing introspection of the last forward, under the reference's attribute names
+    # (src/granite_switch/hf/modeling_granite_switch.py:679-681,704,756-762)
+    @property
+    def _last_adapter_indices(self):
+        return getattr(self, "_last", {}).get("adapter_indices")
+
+    @property
+    def _last_lora_indices(self):
+        return getattr(self, "_last", {}).get("lora_indices")
+
+    @property
+    def _last_probe_indices(self):
+        return getattr(self, "_last", {}).get("probe_indices")
+
+    @property
+    def _last_probe_verdict(self):
+        probe = getattr(self, "_last", {}).get("probe")
+        return None if probe is None else probe[-1]
+
     def _locate_markers(self, input_ids, probe_idx, valid):
         if self.probe_head is None:
             return None
