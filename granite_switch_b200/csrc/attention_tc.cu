@@ -26,6 +26,7 @@
 // (reference: attention comes from vLLM's backends, called at
 // src/granite_switch/vllm/decoder/lora/decoder.py:146-174.)
 #include "common.cuh"
+#include <cstdlib>
 #include "tma_util.h"
 
 #include <ATen/ATen.h>
@@ -53,7 +54,7 @@ __device__ __forceinline__ uint32_t fa_sw(int r, int ch) {
   return (uint32_t)((ch >> 3) * (ROWS * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
-template <int D, int KT_>
+template <int D, int KT_, bool POLY>
 __global__ void __launch_bounds__(192, 2)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                              const __nv_bfloat16* __restrict__ q, int64_t q_stride,
@@ -296,7 +297,9 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
       for (int i = 0; i < KT / 2; ++i) {
         const float a = ex2_approx(fmaf(__uint_as_float(sv[2 * i]), scale_log2, -mb));
-        const float b = ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), scale_log2, -mb));
+        const float xb = fmaf(__uint_as_float(sv[2 * i + 1]), scale_log2, -mb);
+        // POLY: one exponential in four on the FMA pipe (balances it against MUFU)
+        const float b = (POLY && (i & 1)) ? exp2_poly(xb) : ex2_approx(xb);
         rs[i & 3] += a + b;
         pk[i] = pack_bf16x2(a, b);
       }
@@ -354,6 +357,19 @@ __global__ void __launch_bounds__(192, 2)
 
 using namespace gsb;
 
+// Softmax exponentials: 0 = all on MUFU (ex2.approx), 1 = one in four on the FMA
+// pipe (exp2_poly). Env GSB_ATTN_POLY_EXP sets the start value.
+static int g_attn_poly_exp = [] {
+  const char* e = std::getenv("GSB_ATTN_POLY_EXP");
+  return e ? std::atoi(e) : 1;
+}();
+
+int64_t gsb_attn_poly_exp(int64_t v) {
+  const int64_t old = g_attn_poly_exp;
+  if (v >= 0) g_attn_poly_exp = (int)v;
+  return old;
+}
+
 // Same metadata contract as gsb_paged_attention (rows_per_tile = 128), no key split.
 void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                               const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
@@ -379,12 +395,15 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
   CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   GSB_CHECK(n_work < 65536, "attention_tc: too many work tiles");
   dim3 grid(Hkv, n_work);
-  auto kfn = (D == 128) ? fa_prefill_kernel<128, 64> : fa_prefill_kernel<64, 64>;
+  const bool poly = g_attn_poly_exp != 0;
+  auto kfn = (D == 128) ? (poly ? fa_prefill_kernel<128, 64, true> : fa_prefill_kernel<128, 64, false>)
+                        : (poly ? fa_prefill_kernel<64, 64, true> : fa_prefill_kernel<64, 64, false>);
   const int smem = (D == 128) ? FaCfg<128, 64>::SMEM : FaCfg<64, 64>::SMEM;
-  static bool configured[2] = {false, false};
-  if (!configured[D == 128]) {
+  static bool configured[4] = {false, false, false, false};
+  const int variant = (D == 128) * 2 + poly;
+  if (!configured[variant]) {
     GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured[D == 128] = true;
+    configured[variant] = true;
   }
   kfn<<<grid, 192, smem, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
                                   block_table.data_ptr<int32_t>(), (int)block_table.stride(0), (int)k_cache.size(0),

@@ -81,6 +81,21 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 2^x on the FMA/ALU pipes, to take part of a softmax's exponentials off the
+// MUFU unit. Method: split x = n + f with n = floor(x), f in [0, 1); 2^f by a
+// degree-3 polynomial whose coefficients were fitted (iteratively reweighted
+// least squares) for the smallest maximum relative error on [0, 1), 7.5e-5,
+// well below the 2^-9 rounding of the bf16 probabilities it feeds; 2^n is
+// added to the exponent field. Returns +0 for x <= -127 (masked scores are -inf).
+__device__ __forceinline__ float exp2_poly(float x) {
+  const float xc = fmaxf(x, -127.f);
+  const float n = floorf(xc);
+  const float f = xc - n;
+  const float p = fmaf(fmaf(fmaf(0.07802403f, f, 0.22606707f), f, 0.69583398f), f, 0.99992514f);
+  const float r = __int_as_float(__float_as_int(p) + ((int)n << 23));
+  return x <= -127.f ? 0.f : r;
+}
+
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
   __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&v);
   return __bfloat1622float2(h);
