@@ -54,7 +54,7 @@ __device__ __forceinline__ uint32_t fa_sw(int r, int ch) {
   return (uint32_t)((ch >> 3) * (ROWS * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
-template <int D, int KT_, bool POLY>
+template <int D, int KT_, bool PACKED>
 __global__ void __launch_bounds__(192, 2)
     fa_prefill_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                              const __nv_bfloat16* __restrict__ q, int64_t q_stride,
@@ -293,17 +293,32 @@ __global__ void __launch_bounds__(192, 2)
       if (grow) m = mt;
       const float mb = (m == -INFINITY) ? 0.f : m;
       uint32_t pk[KT / 2];
-      float rs[4] = {0.f, 0.f, 0.f, 0.f};
+      if constexpr (PACKED) {
+        // the scale-and-shift and the row sum on packed fp32 pairs (one f32x2
+        // instruction per two scores): fewer issue slots per score for the
+        // softmax warps, which share each SM sub-partition with the other CTA
+        const uint64_t sc2 = f32x2_pack(scale_log2, scale_log2), nm2 = f32x2_pack(-mb, -mb);
+        uint64_t acc[2] = {0ull, 0ull};
 #pragma unroll
-      for (int i = 0; i < KT / 2; ++i) {
-        const float a = ex2_approx(fmaf(__uint_as_float(sv[2 * i]), scale_log2, -mb));
-        const float xb = fmaf(__uint_as_float(sv[2 * i + 1]), scale_log2, -mb);
-        // POLY: one exponential in four on the FMA pipe (balances it against MUFU)
-        const float b = (POLY && (i & 1)) ? exp2_poly(xb) : ex2_approx(xb);
-        rs[i & 3] += a + b;
-        pk[i] = pack_bf16x2(a, b);
+        for (int i = 0; i < KT / 2; ++i) {
+          const uint64_t y = f32x2_fma(f32x2_pack_bits(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
+          const float a = ex2_approx(f32x2_lo(y)), b = ex2_approx(f32x2_hi(y));
+          acc[i & 1] = f32x2_add(acc[i & 1], f32x2_pack(a, b));
+          pk[i] = pack_bf16x2(a, b);
+        }
+        const uint64_t t = f32x2_add(acc[0], acc[1]);
+        l += f32x2_lo(t) + f32x2_hi(t);
+      } else {
+        float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < KT / 2; ++i) {
+          const float a = ex2_approx(fmaf(__uint_as_float(sv[2 * i]), scale_log2, -mb));
+          const float b = ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), scale_log2, -mb));
+          rs[i & 3] += a + b;
+          pk[i] = pack_bf16x2(a, b);
+        }
+        l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       }
-      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
       tmem_st32(tS, pk);  // P_j over the first 32 columns of S_j
       tmem_wait_st();
       tc_fence_before();
@@ -357,18 +372,18 @@ __global__ void __launch_bounds__(192, 2)
 
 using namespace gsb;
 
-// Softmax exponentials: 0 = all on MUFU (ex2.approx), 1 = one in four on the FMA
-// pipe (exp2_poly). Env GSB_ATTN_POLY_EXP sets the start value. Measured on B200
-// (d=128, 32/8 heads): 530 vs 518 TFLOP/s causal 4k, 516 vs 502 for 8 x 512 over
-// 3.5k cached keys, so MUFU is not this kernel's limit and 0 is the default.
-static int g_attn_poly_exp = [] {
-  const char* e = std::getenv("GSB_ATTN_POLY_EXP");
-  return e ? std::atoi(e) : 0;
+// Softmax arithmetic: 0 = scalar fp32, 1 = packed f32x2 scale-and-shift and row
+// sums (env GSB_ATTN_PACKED sets the start value). Taking a quarter of the
+// exponentials off MUFU with a polynomial was measured slower on B200 (530 vs
+// 518 TFLOP/s causal 4k), so the exponentials stay on ex2.approx.
+static int g_attn_packed = [] {
+  const char* e = std::getenv("GSB_ATTN_PACKED");
+  return e ? std::atoi(e) : 1;
 }();
 
-int64_t gsb_attn_poly_exp(int64_t v) {
-  const int64_t old = g_attn_poly_exp;
-  if (v >= 0) g_attn_poly_exp = (int)v;
+int64_t gsb_attn_packed(int64_t v) {
+  const int64_t old = g_attn_packed;
+  if (v >= 0) g_attn_packed = (int)v;
   return old;
 }
 
@@ -397,12 +412,12 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
   CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   GSB_CHECK(n_work < 65536, "attention_tc: too many work tiles");
   dim3 grid(Hkv, n_work);
-  const bool poly = g_attn_poly_exp != 0;
-  auto kfn = (D == 128) ? (poly ? fa_prefill_kernel<128, 64, true> : fa_prefill_kernel<128, 64, false>)
-                        : (poly ? fa_prefill_kernel<64, 64, true> : fa_prefill_kernel<64, 64, false>);
+  const bool packed = g_attn_packed != 0;
+  auto kfn = (D == 128) ? (packed ? fa_prefill_kernel<128, 64, true> : fa_prefill_kernel<128, 64, false>)
+                        : (packed ? fa_prefill_kernel<64, 64, true> : fa_prefill_kernel<64, 64, false>);
   const int smem = (D == 128) ? FaCfg<128, 64>::SMEM : FaCfg<64, 64>::SMEM;
   static bool configured[4] = {false, false, false, false};
-  const int variant = (D == 128) * 2 + poly;
+  const int variant = (D == 128) * 2 + packed;
   if (!configured[variant]) {
     GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[variant] = true;

@@ -81,19 +81,26 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x on the FMA/ALU pipes, to take part of a softmax's exponentials off the
-// MUFU unit. Method: split x = n + f with n = floor(x), f in [0, 1); 2^f by a
-// degree-3 polynomial whose coefficients were fitted (iteratively reweighted
-// least squares) for the smallest maximum relative error on [0, 1), 7.5e-5,
-// well below the 2^-9 rounding of the bf16 probabilities it feeds; 2^n is
-// added to the exponent field. Returns +0 for x <= -127 (masked scores are -inf).
-__device__ __forceinline__ float exp2_poly(float x) {
-  const float xc = fmaxf(x, -127.f);
-  const float n = floorf(xc);
-  const float f = xc - n;
-  const float p = fmaf(fmaf(fmaf(0.07802403f, f, 0.22606707f), f, 0.69583398f), f, 0.99992514f);
-  const float r = __int_as_float(__float_as_int(p) + ((int)n << 23));
-  return x <= -127.f ? 0.f : r;
+// Packed fp32 pairs (sm_100a f32x2 arithmetic): the low word holds the first value.
+__device__ __forceinline__ uint64_t f32x2_pack_bits(uint32_t lo, uint32_t hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t f32x2_pack(float lo, float hi) {
+  return f32x2_pack_bits(__float_as_uint(lo), __float_as_uint(hi));
+}
+__device__ __forceinline__ float f32x2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f32x2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f32x2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
 }
 
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {

@@ -68,4 +68,4 @@ void gsb_moe_combine(const at::Tensor& yp, const at::Tensor& slot, const at::Ten
 void gsb_residual_axpy(const at::Tensor& h, const at::Tensor& y, double scale);
 void gsb_allreduce_ldreduce_p2p(int64_t mc_ptr, const at::Tensor& peer_ptrs, int64_t offset, int64_t nbytes,
                                 int64_t rank, int64_t tp);
-int64_t gsb_attn_poly_exp(int64_t v);
+int64_t gsb_attn_packed(int64_t v);

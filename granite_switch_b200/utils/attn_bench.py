@@ -66,11 +66,11 @@ def main():
         # causal FLOPs: each query attends to (ctx + its index + 1) keys; 4 flop per (q, k, d)
         pairs = sum(ql * (kl - ql) + ql * (ql + 1) // 2 for ql, kl in zip(q_lens, kv_lens))
         flops = 4.0 * pairs * hq * d
-        for poly in (0, 1):  # softmax exponentials all on MUFU / one in four on the FMA pipe
-            old = _native.native().attn_poly_exp(poly)
+        for packed in (0, 1):  # softmax on scalar / packed f32x2 arithmetic
+            old = _native.native().attn_packed(packed)
             ms = _time(lambda: A.prefill_attention_tc(q, kc, vc, bt, qs, kvl, ws, wr, hq, 0.088, out), args.iters)
-            _native.native().attn_poly_exp(old)
-            print(json.dumps({"case": name, "poly_exp": poly, "ms": round(ms, 4),
+            _native.native().attn_packed(old)
+            print(json.dumps({"case": name, "packed": packed, "ms": round(ms, 4),
                               "tflops": round(flops / ms / 1e9, 1)}), flush=True)
     q_lens, kv_lens = [1] * 128, [4200] * 128
     kc, vc, bt, q, out, qs, kvl = _setup(q_lens, kv_lens)

@@ -182,14 +182,14 @@ def test_paged_attention(d, mode, nsplit):
     _check()
 
 
-@pytest.mark.parametrize("poly", [0, 1])
+@pytest.mark.parametrize("packed", [0, 1])
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("case", ["fresh", "cached_prefix", "mixed"])
-def test_prefill_attention_tcgen05(case, d, poly):
+def test_prefill_attention_tcgen05(case, d, packed):
     from granite_switch_b200._native import native
     from granite_switch_b200.ops import attention as A
 
-    old = native().attn_poly_exp(poly)  # softmax exponentials: all on MUFU, or one in four on the FMA pipe
+    old = native().attn_packed(packed)  # softmax on scalar or packed f32x2 arithmetic
 
     hq, hkv = 8, 2
     g = hq // hkv
@@ -212,7 +212,7 @@ def test_prefill_attention_tcgen05(case, d, poly):
                            torch.tensor(kv_lens, dtype=torch.int32, device=dev),
                            torch.tensor(ws, dtype=torch.int32, device=dev),
                            torch.tensor(wr, dtype=torch.int32, device=dev), hq, 0.088, out)
-    native().attn_poly_exp(old)
+    native().attn_packed(old)
     ref = A.paged_attention_reference(q, kc, vc, bt, q_lens, kv_lens, hq, 0.088)
     err = (out.float() - ref).abs().max().item()
     assert err < 3e-2, err
