@@ -144,15 +144,46 @@ def main(argv=None):
     ap.add_argument("--gpu-memory-utilization", type=float, default=0.88)
     ap.add_argument("--no-prefix-caching", action="store_true")
     ap.add_argument("--device", default=None)
+    ap.add_argument("--tensor-parallel-size", type=int, default=1)
+    ap.add_argument("--pipeline-parallel-size", type=int, default=1)
+    ap.add_argument("--no-fused-tp-comm", action="store_true", help="reduce with NCCL only")
     args = ap.parse_args(argv)
     import uvicorn
 
     from ..engine import LLM, EngineConfig
 
+    tp, pp = args.tensor_parallel_size, args.pipeline_parallel_size
     ecfg = EngineConfig(max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
                         max_model_len=args.max_model_len, gpu_memory_utilization=args.gpu_memory_utilization,
-                        enable_prefix_caching=not args.no_prefix_caching)
-    llm = LLM(args.model, device=args.device, engine_config=ecfg)
+                        enable_prefix_caching=not args.no_prefix_caching, tensor_parallel_size=tp,
+                        pipeline_parallel_size=pp, fused_tp_comm=not args.no_fused_tp_comm)
+    sync = None
+    if tp * pp > 1:
+        # one process per GPU (torchrun); rank 0 serves HTTP and drives the others in lock step
+        import datetime
+        import os
+
+        import torch
+        import torch.distributed as dist
+
+        from ..parallel.pipeline import init_parallel_groups
+        from .async_engine import StepSync, follow
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        control = dist.new_group(backend="gloo")
+        tp_rank, tp_group, pipe = init_parallel_groups(tp, pp)
+        llm = LLM(args.model, device=f"cuda:{local}", engine_config=ecfg, tp_rank=tp_rank, tp_group=tp_group,
+                  pipeline=pipe)
+        if dist.get_rank() != 0:
+            follow(llm.engine, control)
+            dist.destroy_process_group()
+            return
+        sync = StepSync(control)
+    else:
+        llm = LLM(args.model, device=args.device, engine_config=ecfg)
     tok = None
     try:
         from transformers import AutoTokenizer
@@ -161,8 +192,11 @@ def main(argv=None):
     except Exception:
         tok = None
     name = args.served_model_name or args.model.rstrip("/").split("/")[-1]
-    ae = AsyncEngine(llm.engine, name)
-    uvicorn.run(build_app(ae, tok, name), host=args.host, port=args.port, log_level="warning")
+    ae = AsyncEngine(llm.engine, name, sync=sync)
+    try:
+        uvicorn.run(build_app(ae, tok, name), host=args.host, port=args.port, log_level="warning")
+    finally:
+        ae.shutdown()
 
 
 if __name__ == "__main__":

@@ -60,10 +60,72 @@ _LAT_BUCKETS = (0.001, 0.005, 0.01, 0.02, 0.04, 0.06, 0.08, 0.1, 0.25, 0.5, 0.75
                 20.0, 40.0, 80.0)
 
 
+class StepSync:
+    """Lock-step control channel of a multi-rank engine (tensor / pipeline parallel).
+
+    Every rank runs the same scheduler, so every rank must see the same
+    requests in the same order before each step: rank 0 (the one serving
+    HTTP) publishes, over a CPU process group, the requests it added and
+    aborted since the last step and whether to step; the other ranks replay
+    that in :func:`follow` and step with it, so the collectives inside the step
+    line up. An idle rank 0 publishes a heartbeat every ``heartbeat_s``.
+    """
+
+    def __init__(self, group, heartbeat_s: float = 1.0):
+        import torch.distributed as dist
+
+        self.group = group
+        self.src = dist.get_global_rank(group, 0) if group is not None else 0
+        self.heartbeat_s = heartbeat_s
+        self.adds: list[tuple] = []
+        self.aborts: list[str] = []
+        self.last = time.perf_counter()
+
+    def add(self, req: Request) -> None:
+        from dataclasses import asdict
+
+        self.adds.append((list(req.prompt_ids), asdict(req.sampling), req.request_id, req.arrival_time))
+
+    def abort(self, request_id: str) -> None:
+        self.aborts.append(request_id)
+
+    def publish(self, step: bool, stop: bool = False) -> None:
+        import torch.distributed as dist
+
+        pkt = [{"add": self.adds, "abort": self.aborts, "step": step, "stop": stop}]
+        dist.broadcast_object_list(pkt, src=self.src, group=self.group)
+        self.adds, self.aborts = [], []
+        self.last = time.perf_counter()
+
+    def idle(self) -> None:
+        if time.perf_counter() - self.last >= self.heartbeat_s:
+            self.publish(step=False)
+
+
+def follow(engine, group) -> None:
+    """Loop of a rank other than 0: replay rank 0's request changes and step with it until told to stop."""
+    import torch.distributed as dist
+
+    src = dist.get_global_rank(group, 0) if group is not None else 0
+    while True:
+        pkt = [None]
+        dist.broadcast_object_list(pkt, src=src, group=group)
+        p = pkt[0]
+        for ids, sp, rid, arrival in p["add"]:
+            engine.add_request(ids, SamplingParams(**sp), request_id=rid, arrival_time=arrival)
+        for rid in p["abort"]:
+            engine.abort_request(rid)
+        if p["stop"]:
+            return
+        if p["step"]:
+            engine.step()
+
+
 class AsyncEngine:
-    def __init__(self, engine, model_name: str = "granite-switch"):
+    def __init__(self, engine, model_name: str = "granite-switch", sync: StepSync | None = None):
         self.engine = engine
         self.model_name = model_name
+        self.sync = sync
         self._inbox: list[_Pending] = []
         self._lock = threading.Lock()
         self._wake = threading.Event()
@@ -103,6 +165,8 @@ class AsyncEngine:
         self._stop = True
         self._wake.set()
         self._thread.join(timeout=10)
+        if self.sync is not None:
+            self.sync.publish(step=False, stop=True)  # release the follower ranks
 
     # ------------------------------------------------------------ engine thread
     def _run(self):
@@ -115,20 +179,28 @@ class AsyncEngine:
                     req = self.engine.add_request(p.prompt_ids, p.sampling, arrival_time=p.submitted)
                     p.request_id = req.request_id
                     self._live[req.request_id] = p
+                    if self.sync is not None:
+                        self.sync.add(req)
                     self.prompt_tokens.observe(len(p.prompt_ids))
                 except Exception as e:  # invalid request: fail only this one
                     self.errors += 1
                     p.loop.call_soon_threadsafe(_set_exc, p.future, e)
             if not self.engine.has_unfinished():
+                if self.sync is not None:
+                    self.sync.idle()
                 self._wake.wait(timeout=0.05)
                 self._wake.clear()
                 continue
             try:
+                if self.sync is not None:
+                    self.sync.publish(step=True)
                 finished = self.engine.step()
             except Exception as e:  # a failing step aborts the requests it carried
                 self.errors += 1
                 for rid, p in list(self._live.items()):
                     self.engine.abort_request(rid)
+                    if self.sync is not None:
+                        self.sync.abort(rid)
                     p.loop.call_soon_threadsafe(_set_exc, p.future, e)
                 self._live.clear()
                 continue

@@ -101,3 +101,60 @@ def test_chat_completions_place_the_control_token(tmp_path):
             assert r.json()["usage"]["prompt_tokens_details"]["cached_tokens"] >= 16 * (cut // 16) > 0
     finally:
         ae.shutdown()
+
+
+def _lockstep_worker(rank, world, port, model_dir, prompts, q):
+    import asyncio
+
+    import torch.distributed as dist
+
+    from granite_switch_b200.engine import LLM, EngineConfig, SamplingParams
+    from granite_switch_b200.server.async_engine import AsyncEngine, StepSync, follow
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    llm = LLM(model_dir, device="cpu", engine_config=EngineConfig(max_num_seqs=2, max_num_batched_tokens=64,
+                                                                  num_kv_blocks=64, max_model_len=512))
+    done = {}
+    if rank == 0:
+        ae = AsyncEngine(llm.engine, "tiny", sync=StepSync(dist.group.WORLD, heartbeat_s=0.05))
+
+        async def run():
+            reqs = await asyncio.gather(*[ae.generate(p, SamplingParams(max_tokens=5)) for p in prompts])
+            return {r.request_id: r.output_ids for r in reqs}
+
+        done = asyncio.run(run())
+        ae.shutdown()
+    else:
+        llm.engine.on_finish = lambda r: done.__setitem__(r.request_id, list(r.output_ids))
+        follow(llm.engine, dist.group.WORLD)
+    out = [None] * world
+    dist.all_gather_object(out, done)
+    if rank == 0:
+        q.put(out)
+    dist.destroy_process_group()
+
+
+def test_multi_rank_lockstep_serving(client):
+    """Rank 0 serves and publishes each step's new requests; the follower rank replays them and
+    takes the same scheduling decisions (gloo ranks on CPU)."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    idx = json.load(open(os.path.join(client.model_dir, "adapter_index.json")))
+    ctrl = idx["adapters"][1]["control_token"]["id"]
+    prompts = [list(range(5, 40)), list(range(7, 30)) + [ctrl, 3], list(range(50, 90)), [9, 8, 7, ctrl, 6]]
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_lockstep_worker, args=(r, 2, port, client.model_dir, prompts, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+    assert all(p.exitcode == 0 for p in procs)
+    lead, follower = out
+    assert len(lead) == len(prompts) and lead == follower
