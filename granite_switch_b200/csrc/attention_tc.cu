@@ -368,6 +368,347 @@ __global__ void __launch_bounds__(192, 2)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Two query tiles per CTA ("ping-pong"): 256 rows of one request and KV head,
+// 128-key tiles, one CTA per SM.
+//
+//   TMEM (512 columns): S_A [0,128) | S_B [128,256) | O_A | O_B (D columns each)
+//   warp 0: K/V TMA producer, warp 1: TMEM owner + MMA issuer,
+//   warps 2..5: softmax of tile A, warps 6..9: softmax of tile B.
+//
+// Each K/V tile in shared memory serves both query tiles (half the K/V traffic
+// per query row of the one-tile kernel), and each S tile holds 128 keys, so a
+// softmax pass does twice the work per TMEM round trip. The MMA issuer runs
+//   S_A(0) S_B(0) | PV_A(0) S_A(1) PV_B(0) S_B(1) | PV_A(1) S_A(2) ...
+// so the tensor core computes one tile's products while the other tile's
+// softmax runs. S_t(j+1) reuses S_t's columns (P_t(j) lives in the first 64
+// of them): it is issued after PV_t(j) by the same thread, and tcgen05.mma
+// operations from one thread execute in issue order. Every wait is bounded.
+template <int D>
+struct FaPPCfg {
+  static constexpr int BM = 128;            // rows per query tile
+  static constexpr int KT = 128;            // keys per tile
+  static constexpr int PAGE = 16;
+  static constexpr int Q_BYTES = BM * D * 2;  // one query tile
+  static constexpr int KV_BYTES = KT * D * 2;  // one K (or V) tile
+  static constexpr int STAGES = 2;
+  static constexpr int SMEM = 1024 + 2 * Q_BYTES + STAGES * 2 * KV_BYTES + 512;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int S_COL = 0;           // + t * KT
+  static constexpr int O_COL = 2 * KT;      // + t * D
+};
+
+template <int D, bool PACKED>
+__global__ void __launch_bounds__(320, 1)
+    fa_pingpong_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                       const __nv_bfloat16* __restrict__ q, int64_t q_stride,
+                       const int32_t* __restrict__ block_table, int bt_stride, int num_blocks,
+                       const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
+                       const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0, int Hq,
+                       int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out, int64_t out_stride,
+                       uint32_t* err) {
+  using C = FaPPCfg<D>;
+  constexpr int KT = C::KT, BM = C::BM, PAGE = C::PAGE, ST = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sQ = smem;                               // [2][D/64][BM][64]
+  uint8_t* sK = sQ + 2 * C::Q_BYTES;                // [ST][D/64][KT][64]
+  uint8_t* sV = sK + ST * C::KV_BYTES;              // [ST][D/64][KT][64]
+  uint64_t* k_full = reinterpret_cast<uint64_t*>(sV + ST * C::KV_BYTES);
+  uint64_t* k_empty = k_full + ST;
+  uint64_t* v_full = k_empty + ST;
+  uint64_t* v_empty = v_full + ST;
+  uint64_t* s_full = v_empty + ST;   // [2] per query tile
+  uint64_t* p_full = s_full + 2;     // [2]
+  uint64_t* o_done = p_full + 2;     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.x, w = blockIdx.y;
+  const int seq = work_seq[w];
+  const int row0 = work_row0[w];
+  const int G = Hq / Hkv;
+  const int qs = q_start[seq];
+  const int q_len = q_start[seq + 1] - qs;
+  const int kv_len = kv_len_arr[seq];
+  const int ctx = kv_len - q_len;
+  const int n_rows = q_len * G;
+  const int32_t* bt = block_table + (int64_t)seq * bt_stride;
+  const int last_row = min(row0 + 2 * BM, n_rows) - 1;
+  const int k_end = max(0, min(kv_len, ctx + last_row / G + 1));
+  const int n_tiles = (k_end + KT - 1) / KT;
+  const int nq = (row0 + BM < n_rows) ? 2 : 1;   // query tiles with any valid row
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < ST; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&o_done[t], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  for (int c = threadIdx.x; c < 2 * BM * (D / 8); c += blockDim.x) {
+    const int rr = c / (D / 8), ch = c % (D / 8);
+    const int t = rr / BM, r = rr % BM;
+    const int gr = row0 + rr;
+    const bool valid = gr < n_rows;
+    const int tok = valid ? gr / G : 0;
+    const int head = kvh * G + (valid ? gr % G : 0);
+    const __nv_bfloat16* src = q + (int64_t)(qs + tok) * q_stride + head * D + ch * 8;
+    const uint32_t dst = smem_u32(sQ + t * C::Q_BYTES) + fa_sw<BM>(r, ch);
+    const int nbytes = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
+                 "l"(valid ? (const void*)src : (const void*)q), "r"(nbytes)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- K/V producer: K runs one tile ahead of V ----------------
+    if (lane == 0 && n_tiles > 0) {
+      const int first_page = checked_index(bt[0], num_blocks, err, kSiteTcPage);
+      auto load = [&](uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, int j) {
+        mbar_arrive_expect_tx(bar, C::KV_BYTES);
+#pragma unroll 1
+        for (int p = 0; p < KT / PAGE; ++p) {
+          const int key = j * KT + p * PAGE;
+          const int page = (key < k_end) ? checked_index(bt[key / PAGE], num_blocks, err, kSiteTcPage) : first_page;
+          const int row = (page * Hkv + kvh) * PAGE;
+#pragma unroll
+          for (int h = 0; h < D / 64; ++h) tma_load_2d(dst + h * (KT * 128) + p * PAGE * 128, tm, bar, h * 64, row);
+        }
+      };
+      int k_issued = 0, v_issued = 0;
+      bool ok = true;
+      auto issue_k = [&](int j) {
+        const int st = j % ST;
+        if (*abort_flag || !mbar_wait(&k_empty[st], ((j / ST) & 1) ^ 1, err, kErrAttnWait)) return false;
+        load(sK + st * C::KV_BYTES, &tm_k, &k_full[st], j);
+        k_issued = j + 1;
+        return true;
+      };
+      ok = issue_k(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles && !(ok = issue_k(j + 1))) break;
+        const int st = j % ST;
+        if (*abort_flag || !mbar_wait(&v_empty[st], ((j / ST) & 1) ^ 1, err, kErrAttnWait)) {
+          ok = false;
+          break;
+        }
+        load(sV + st * C::KV_BYTES, &tm_v, &v_full[st], j);
+        v_issued = j + 1;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        for (int j = (k_issued > ST ? k_issued - ST : 0); j < k_issued; ++j)
+          mbar_wait(&k_full[j % ST], (j / ST) & 1, err, kErrAttnWait);
+        for (int j = (v_issued > ST ? v_issued - ST : 0); j < v_issued; ++j)
+          mbar_wait(&v_full[j % ST], (j / ST) & 1, err, kErrAttnWait);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && n_tiles > 0) {
+      const uint32_t idesc_s = umma_idesc_bf16(128, KT);
+      const uint32_t idesc_o = umma_idesc_bf16_bmn(128, D);
+      auto issue_s = [&](int t, int j) -> bool {
+        const int st = j % ST;
+        if (t == 0 && (*abort_flag || !mbar_wait(&k_full[st], (j / ST) & 1, err, kErrAttnWait))) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + t * C::Q_BYTES);
+        const uint32_t k_addr = smem_u32(sK + st * C::KV_BYTES);
+        const uint32_t tS = tmem + C::S_COL + t * KT;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32);
+          const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * (KT * 128) + (kk & 3) * 32);
+          umma_bf16(tS, ad, bd, idesc_s, kk != 0);
+        }
+        umma_commit(&s_full[t]);
+        if (t == nq - 1) umma_commit(&k_empty[st]);
+        return true;
+      };
+      auto issue_pv = [&](int t, int j) -> bool {
+        const int st = j % ST;
+        if (*abort_flag || (t == 0 && !mbar_wait(&v_full[st], (j / ST) & 1, err, kErrAttnWait)) ||
+            !mbar_wait(&p_full[t], j & 1, err, kErrAttnWait))
+          return false;
+        tc_fence_after();
+        const uint32_t tP = tmem + C::S_COL + t * KT;
+        const uint32_t v_addr = smem_u32(sV + st * C::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk) {
+          const uint64_t bd = umma_desc_sw128_mn(v_addr + kk * 2048, KT * 128, 1024);
+          umma_bf16_tmem_a(tmem + C::O_COL + t * D, tP + kk * 8, bd, idesc_o, (j | kk) != 0);
+        }
+        umma_commit(&o_done[t]);
+        if (t == nq - 1) umma_commit(&v_empty[st]);
+        return true;
+      };
+      bool ok = issue_s(0, 0) && (nq < 2 || issue_s(1, 0));
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        for (int t = 0; t < nq && ok; ++t) {
+          ok = issue_pv(t, j);
+          if (ok && j + 1 < n_tiles) ok = issue_s(t, j + 1);
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ---------------- softmax + epilogue: warps 2..5 tile A, 6..9 tile B ----------------
+    constexpr float kLazyLog2 = 8.f;
+    const int t = (warp - 2) >> 2;
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;
+    const int gr = row0 + t * BM + r;
+    const int pos = ctx + gr / G;
+    const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+    const uint32_t tS = tmem + lane_base + C::S_COL + t * KT;
+    const uint32_t tO = tmem + lane_base + C::O_COL + t * D;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    const bool live = t < nq;
+    for (int j = 0; live && j < n_tiles; ++j) {
+      const bool got_s = !*abort_flag && mbar_wait(&s_full[t], j & 1, err, kErrAttnWait);
+      if (!__all_sync(0xffffffffu, got_s)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[KT];
+#pragma unroll
+      for (int c = 0; c < KT / 32; ++c) tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t(&)[32]>(sv[c * 32]));
+      tmem_wait_ld();
+      const int kbase = j * KT;
+      if (__any_sync(0xffffffffu, kbase + KT - 1 > pos || kbase + KT > k_end)) {
+#pragma unroll
+        for (int i = 0; i < KT; ++i) {
+          const int key = kbase + i;
+          if (key > pos || key >= k_end) sv[i] = 0xff800000u;
+        }
+      }
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(sv[i]);
+#pragma unroll
+      for (int i = 8; i < KT; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sv[i]));
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                             fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale_log2;
+      const bool grow = mt > m + kLazyLog2;
+      const bool rescale = grow && m != -INFINITY && j > 0;
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O_t must hold P_t(j-1) . V(j-1) before it is scaled
+        const bool got_o = mbar_wait(&o_done[t], (j - 1) & 1, err, kErrAttnWait);
+        if (!__all_sync(0xffffffffu, got_o)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float f = rescale ? ex2_approx(m - mt) : 1.f;
+        l *= f;
+#pragma unroll 1
+        for (int c = 0; c < D / 16; ++c) {  // 16 columns at a time: the 128 scores stay in registers
+          uint32_t rr[16];
+          tmem_ld16(tO + c * 16, rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * f);
+          tmem_st16(tO + c * 16, rr);
+        }
+      }
+      if (grow) m = mt;
+      const float mb = (m == -INFINITY) ? 0.f : m;
+      // P_t(j) as bf16 pairs over the first KT/2 columns of S_t. Packed in place:
+      // pair i lands in sv[i], whose own score was read by an earlier pair.
+      if constexpr (PACKED) {
+        const uint64_t sc2 = f32x2_pack(scale_log2, scale_log2), nm2 = f32x2_pack(-mb, -mb);
+        uint64_t acc[2] = {0ull, 0ull};
+#pragma unroll
+        for (int i = 0; i < KT / 2; ++i) {
+          const uint64_t y = f32x2_fma(f32x2_pack_bits(sv[2 * i], sv[2 * i + 1]), sc2, nm2);
+          const float a = ex2_approx(f32x2_lo(y)), b = ex2_approx(f32x2_hi(y));
+          acc[i & 1] = f32x2_add(acc[i & 1], f32x2_pack(a, b));
+          sv[i] = pack_bf16x2(a, b);
+        }
+        const uint64_t tt = f32x2_add(acc[0], acc[1]);
+        l += f32x2_lo(tt) + f32x2_hi(tt);
+      } else {
+        float rs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < KT / 2; ++i) {
+          const float a = ex2_approx(fmaf(__uint_as_float(sv[2 * i]), scale_log2, -mb));
+          const float b = ex2_approx(fmaf(__uint_as_float(sv[2 * i + 1]), scale_log2, -mb));
+          rs[i & 3] += a + b;
+          sv[i] = pack_bf16x2(a, b);
+        }
+        l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
+      }
+      tmem_st32(tS, reinterpret_cast<uint32_t(&)[32]>(sv[0]));
+      tmem_st32(tS + 32, reinterpret_cast<uint32_t(&)[32]>(sv[32]));
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    const bool go = live && ok && n_tiles > 0 && !*abort_flag;
+    if (__all_sync(0xffffffffu, go)) {
+      const int jl = n_tiles - 1;
+      if (__all_sync(0xffffffffu, mbar_wait(&o_done[t], jl & 1, err, kErrAttnWait))) {
+        tc_fence_after();
+        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+        const bool valid = gr < n_rows;
+        const int tok = qs + (valid ? gr / G : 0);
+        const int head = kvh * G + (valid ? gr % G : 0);
+        __nv_bfloat16* op = out + (int64_t)tok * out_stride + head * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(tO + c * 32, rr);
+          tmem_wait_ld();
+          if (valid) {
+            uint4* o4 = reinterpret_cast<uint4*>(op + c * 32);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              o4[e] = make_uint4(pack_bf16x2(__uint_as_float(rr[8 * e]) * inv, __uint_as_float(rr[8 * e + 1]) * inv),
+                                 pack_bf16x2(__uint_as_float(rr[8 * e + 2]) * inv, __uint_as_float(rr[8 * e + 3]) * inv),
+                                 pack_bf16x2(__uint_as_float(rr[8 * e + 4]) * inv, __uint_as_float(rr[8 * e + 5]) * inv),
+                                 pack_bf16x2(__uint_as_float(rr[8 * e + 6]) * inv, __uint_as_float(rr[8 * e + 7]) * inv));
+          }
+        }
+      }
+    } else if (live && n_tiles == 0 && gr < n_rows) {
+      __nv_bfloat16* op = out + (int64_t)(qs + gr / G) * out_stride + (kvh * G + gr % G) * D;
+      for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(op + c) = make_uint4(0, 0, 0, 0);
+    }
+    if (!ok) *abort_flag = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
 }  // namespace gsb
 
 using namespace gsb;
@@ -391,7 +732,7 @@ int64_t gsb_attn_packed(int64_t v) {
 void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                               const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
                               const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t num_q_heads,
-                              double scale, const at::Tensor& out, const at::Tensor& err) {
+                              double scale, const at::Tensor& out, const at::Tensor& err, int64_t rows_per_tile) {
   GSB_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16 &&
                 out.scalar_type() == at::kBFloat16,
             "attention_tc: bf16 tensors required");
@@ -411,8 +752,29 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
   CUtensorMap tk = make_tmap_bf16_2d(k_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   GSB_CHECK(n_work < 65536, "attention_tc: too many work tiles");
+  GSB_CHECK(rows_per_tile == 128 || rows_per_tile == 256, "attention_tc: rows_per_tile must be 128 or 256");
   dim3 grid(Hkv, n_work);
   const bool packed = g_attn_packed != 0;
+  if (rows_per_tile == 256) {
+    auto kp = (D == 128) ? (packed ? fa_pingpong_kernel<128, true> : fa_pingpong_kernel<128, false>)
+                         : (packed ? fa_pingpong_kernel<64, true> : fa_pingpong_kernel<64, false>);
+    const int smem_p = (D == 128) ? FaPPCfg<128>::SMEM : FaPPCfg<64>::SMEM;
+    static bool configured_p[4] = {false, false, false, false};
+    const int vp = (D == 128) * 2 + packed;
+    if (!configured_p[vp]) {
+      GSB_CUDA_CHECK(cudaFuncSetAttribute(kp, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_p));
+      configured_p[vp] = true;
+    }
+    kp<<<grid, 320, smem_p, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
+                                  block_table.data_ptr<int32_t>(), (int)block_table.stride(0), (int)k_cache.size(0),
+                                  q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
+                                  work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv,
+                                  (float)(scale * 1.4426950408889634),
+                                  reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
+                                  reinterpret_cast<uint32_t*>(err.data_ptr()));
+    GSB_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   auto kfn = (D == 128) ? (packed ? fa_prefill_kernel<128, 64, true> : fa_prefill_kernel<128, 64, false>)
                         : (packed ? fa_prefill_kernel<64, 64, true> : fa_prefill_kernel<64, 64, false>);
   const int smem = (D == 128) ? FaCfg<128, 64>::SMEM : FaCfg<64, 64>::SMEM;

@@ -588,10 +588,10 @@ class NativeGraniteSwitch:
     def _attention(self, b: StepBatch, q: torch.Tensor, kc, vc, attn: torch.Tensor, scale: float) -> None:
         R = self._region
         for plan in b.plans:
-            if plan.rows == 128:
+            if plan.rows in (128, 256):
                 with R("attn_prefill"):
                     A.prefill_attention_tc(q, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
-                                           plan.work_row0, self.num_q, scale, attn)
+                                           plan.work_row0, self.num_q, scale, attn, plan.rows)
             else:
                 with R("attn_decode" if plan.rows == 16 else "attn_prefill"):
                     A.paged_attention(q, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
@@ -659,7 +659,7 @@ class NativeGraniteSwitch:
         dec = [i for i, ql in enumerate(q_lens) if ql * g <= 16]
         pre = [i for i, ql in enumerate(q_lens) if ql * g > 16]
         plans = []
-        pre_rows = 128 if (self.head_dim in (64, 128) and self.use_tc_attention) else 64
+        pre_rows = A.TC_ROWS if (self.head_dim in (64, 128) and self.use_tc_attention) else 64
         for idx, rows in ((dec, 16), (pre, pre_rows)):
             if not idx:
                 continue

@@ -2,12 +2,17 @@
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
 from .._native import err_buffer, native
 
 NUM_SMS = 148
+
+#: rows per CTA of the tcgen05 prefill attention the engine uses: 128 (one query
+#: tile per CTA) or 256 (two query tiles per CTA sharing each K/V tile)
+TC_ROWS = int(os.environ.get("GSB_ATTN_TC_ROWS", "128"))
 
 
 def build_work(q_lens: list[int], group: int, rows_per_tile: int,
@@ -59,10 +64,12 @@ def paged_attention(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq,
 
 
 def prefill_attention_tc(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
-                         num_q_heads: int, scale: float, out):
-    """tcgen05 prefill attention; work tiles must be built with ``rows_per_tile=128``."""
+                         num_q_heads: int, scale: float, out, rows_per_tile: int = 128):
+    """tcgen05 prefill attention; the work tiles must be built with the same ``rows_per_tile``:
+    128 (one query tile per CTA, two CTAs per SM) or 256 (two query tiles per CTA sharing each
+    K/V tile, 128-key tiles, one CTA per SM)."""
     native().prefill_attention_tc(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
-                                  num_q_heads, float(scale), out, err_buffer(q.device))
+                                  num_q_heads, float(scale), out, err_buffer(q.device), int(rows_per_tile))
     return out
 
 

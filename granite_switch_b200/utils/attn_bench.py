@@ -61,17 +61,19 @@ def main():
     for name, q_lens, kv_lens in (("prefill_causal_4k", [4096], [4096]),
                                   ("prefill_8x512_over_3584", [512] * 8, [4096] * 8)):
         kc, vc, bt, q, out, qs, kvl = _setup(q_lens, kv_lens)
-        ws, wr = A.build_work(q_lens, hq // hkv, 128, kv_lens)
-        ws, wr = torch.tensor(ws, **i32), torch.tensor(wr, **i32)
         # causal FLOPs: each query attends to (ctx + its index + 1) keys; 4 flop per (q, k, d)
         pairs = sum(ql * (kl - ql) + ql * (ql + 1) // 2 for ql, kl in zip(q_lens, kv_lens))
         flops = 4.0 * pairs * hq * d
-        for packed in (0, 1):  # softmax on scalar / packed f32x2 arithmetic
-            old = _native.native().attn_packed(packed)
-            ms = _time(lambda: A.prefill_attention_tc(q, kc, vc, bt, qs, kvl, ws, wr, hq, 0.088, out), args.iters)
-            _native.native().attn_packed(old)
-            print(json.dumps({"case": name, "packed": packed, "ms": round(ms, 4),
-                              "tflops": round(flops / ms / 1e9, 1)}), flush=True)
+        for rows in (128, 256):  # one / two query tiles per CTA
+            ws, wr = A.build_work(q_lens, hq // hkv, rows, kv_lens)
+            ws, wr = torch.tensor(ws, **i32), torch.tensor(wr, **i32)
+            for packed in (0, 1):  # softmax on scalar / packed f32x2 arithmetic
+                old = _native.native().attn_packed(packed)
+                ms = _time(lambda: A.prefill_attention_tc(q, kc, vc, bt, qs, kvl, ws, wr, hq, 0.088, out, rows),
+                           args.iters)
+                _native.native().attn_packed(old)
+                print(json.dumps({"case": name, "rows": rows, "packed": packed, "ms": round(ms, 4),
+                                  "tflops": round(flops / ms / 1e9, 1)}), flush=True)
     q_lens, kv_lens = [1] * 128, [4200] * 128
     kc, vc, bt, q, out, qs, kvl = _setup(q_lens, kv_lens)
     ws, wr = A.build_work(q_lens, hq // hkv, 16)

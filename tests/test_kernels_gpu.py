@@ -182,10 +182,11 @@ def test_paged_attention(d, mode, nsplit):
     _check()
 
 
+@pytest.mark.parametrize("rows", [128, 256])
 @pytest.mark.parametrize("packed", [0, 1])
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("case", ["fresh", "cached_prefix", "mixed"])
-def test_prefill_attention_tcgen05(case, d, packed):
+def test_prefill_attention_tcgen05(case, d, packed, rows):
     from granite_switch_b200._native import native
     from granite_switch_b200.ops import attention as A
 
@@ -206,12 +207,12 @@ def test_prefill_attention_tcgen05(case, d, packed):
     qs = [0]
     for l in q_lens:
         qs.append(qs[-1] + l)
-    ws, wr = A.build_work(q_lens, g, 128)
+    ws, wr = A.build_work(q_lens, g, rows)
     dev = "cuda"
     A.prefill_attention_tc(q, kc, vc, bt, torch.tensor(qs, dtype=torch.int32, device=dev),
                            torch.tensor(kv_lens, dtype=torch.int32, device=dev),
                            torch.tensor(ws, dtype=torch.int32, device=dev),
-                           torch.tensor(wr, dtype=torch.int32, device=dev), hq, 0.088, out)
+                           torch.tensor(wr, dtype=torch.int32, device=dev), hq, 0.088, out, rows)
     native().attn_packed(old)
     ref = A.paged_attention_reference(q, kc, vc, bt, q_lens, kv_lens, hq, 0.088)
     err = (out.float() - ref).abs().max().item()
