@@ -43,7 +43,8 @@ struct FaCfg {
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = KT * D * 2;      // one of K or V
   static constexpr int STAGES = 2;
-  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + 512;
+  static constexpr int PT_CAP = 2048;             // page ids staged in shared memory (32k keys)
+  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + 512 + PT_CAP * 4;
   static constexpr int TMEM_COLS = (2 * KT + D) <= 256 ? 256 : 512;  // S0 | S1 | O
   static constexpr int S_COL0 = 0, S_COL1 = KT, O_COL = 2 * KT;
 };
@@ -80,6 +81,7 @@ __global__ void __launch_bounds__(192, 2)
   uint64_t* o_done = p_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* s_pages = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(k_full) + 512);  // [PT_CAP]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.x, w = blockIdx.y;
@@ -115,6 +117,10 @@ __global__ void __launch_bounds__(192, 2)
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
+  // page ids of the key range into shared memory: the producer then issues each
+  // tile's boxes without a dependent global read per page
+  const int n_pages = min((k_end + PAGE - 1) / PAGE, C::PT_CAP);
+  for (int i = threadIdx.x; i < n_pages; i += blockDim.x) s_pages[i] = checked_index(bt[i], num_blocks, err, kSiteTcPage);
   for (int c = threadIdx.x; c < BM * (D / 8); c += blockDim.x) {
     const int r = c / (D / 8), ch = c % (D / 8);
     const int gr = row0 + r;
@@ -138,13 +144,16 @@ __global__ void __launch_bounds__(192, 2)
   if (warp == 0) {
     // ---------------- K/V producer: K runs one tile ahead of V ----------------
     if (lane == 0 && n_tiles > 0) {
-      const int first_page = checked_index(bt[0], num_blocks, err, kSiteTcPage);
+      const int first_page = s_pages[0];
       auto load = [&](uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, int j) {
         mbar_arrive_expect_tx(bar, C::KV_BYTES);
-#pragma unroll 1
+#pragma unroll
         for (int p = 0; p < KT / PAGE; ++p) {
           const int key = j * KT + p * PAGE;
-          const int page = (key < k_end) ? checked_index(bt[key / PAGE], num_blocks, err, kSiteTcPage) : first_page;
+          const int pi = key / PAGE;
+          const int page = (key < k_end) ? (pi < n_pages ? s_pages[pi] : checked_index(bt[pi], num_blocks, err,
+                                                                                      kSiteTcPage))
+                                         : first_page;
           const int row = (page * Hkv + kvh) * PAGE;
 #pragma unroll
           for (int h = 0; h < D / 64; ++h) tma_load_2d(dst + h * (KT * 128) + p * PAGE * 128, tm, bar, h * 64, row);
@@ -393,7 +402,8 @@ struct FaPPCfg {
   static constexpr int Q_BYTES = BM * D * 2;  // one query tile
   static constexpr int KV_BYTES = KT * D * 2;  // one K (or V) tile
   static constexpr int STAGES = 2;
-  static constexpr int SMEM = 1024 + 2 * Q_BYTES + STAGES * 2 * KV_BYTES + 512;
+  static constexpr int PT_CAP = 4096;             // page ids staged in shared memory (64k keys)
+  static constexpr int SMEM = 1024 + 2 * Q_BYTES + STAGES * 2 * KV_BYTES + 512 + PT_CAP * 4;
   static constexpr int TMEM_COLS = 512;
   static constexpr int S_COL = 0;           // + t * KT
   static constexpr int O_COL = 2 * KT;      // + t * D
@@ -424,6 +434,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* o_done = p_full + 2;     // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* s_pages = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(k_full) + 512);  // [PT_CAP]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.x, w = blockIdx.y;
@@ -462,6 +473,8 @@ __global__ void __launch_bounds__(320, 1)
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
+  const int n_pages = min((k_end + PAGE - 1) / PAGE, C::PT_CAP);
+  for (int i = threadIdx.x; i < n_pages; i += blockDim.x) s_pages[i] = checked_index(bt[i], num_blocks, err, kSiteTcPage);
   for (int c = threadIdx.x; c < 2 * BM * (D / 8); c += blockDim.x) {
     const int rr = c / (D / 8), ch = c % (D / 8);
     const int t = rr / BM, r = rr % BM;
@@ -486,13 +499,16 @@ __global__ void __launch_bounds__(320, 1)
   if (warp == 0) {
     // ---------------- K/V producer: K runs one tile ahead of V ----------------
     if (lane == 0 && n_tiles > 0) {
-      const int first_page = checked_index(bt[0], num_blocks, err, kSiteTcPage);
+      const int first_page = s_pages[0];
       auto load = [&](uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, int j) {
         mbar_arrive_expect_tx(bar, C::KV_BYTES);
-#pragma unroll 1
+#pragma unroll
         for (int p = 0; p < KT / PAGE; ++p) {
           const int key = j * KT + p * PAGE;
-          const int page = (key < k_end) ? checked_index(bt[key / PAGE], num_blocks, err, kSiteTcPage) : first_page;
+          const int pi = key / PAGE;
+          const int page = (key < k_end) ? (pi < n_pages ? s_pages[pi] : checked_index(bt[pi], num_blocks, err,
+                                                                                      kSiteTcPage))
+                                         : first_page;
           const int row = (page * Hkv + kvh) * PAGE;
 #pragma unroll
           for (int h = 0; h < D / 64; ++h) tma_load_2d(dst + h * (KT * 128) + p * PAGE * 128, tm, bar, h * 64, row);
