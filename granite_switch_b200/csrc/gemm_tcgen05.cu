@@ -80,6 +80,13 @@ struct GemmEpiArgs {
 // tile of X belongs to one expert (tile_expert[mt]; -1 = no rows, skipped).
 struct GemmGroupArgs {
   const int32_t* tile_expert;  // null: plain GEMM
+  // split-K (decode-sized GEMMs with too few output tiles to fill the GPU): each
+  // output tile's K range is cut into `ksplit` equal parts computed by different
+  // CTAs; part p stores its fp32 partial sum at ws + p * M * N, and
+  // splitk_reduce_kernel adds the parts and applies the epilogue. The LoRA
+  // expand blocks run with the last part.
+  int ksplit;                  // 1: off
+  float* ws;                   // [ksplit, M, N] fp32
 };
 
 // A shrink tile is skipped when none of the adapters owning its columns has a
@@ -422,6 +429,9 @@ __global__ void __launch_bounds__(192, 1)
   const int n_tiles = N / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int main_blocks = K / C::BK;
+  const int ksplit = grp.ksplit > 1 ? grp.ksplit : 1;   // the host keeps main_blocks % ksplit == 0
+  const int num_work = num_tiles * ksplit;
+  const int part_blocks = main_blocks / ksplit;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -457,13 +467,15 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       uint32_t kb = 0;  // k-blocks issued by this CTA (ring position)
       bool stop = false;
-      for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x) {
+      for (int t = blockIdx.x; t < num_work && !stop; t += gridDim.x) {
         int mt, nt;
-        gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
+        const int part = t / num_tiles;
+        gemm_tile_coords(t - part * num_tiles, m_tiles, n_tiles, mt, nt);
         const int m0 = mt * C::BM, n0 = nt * BN;
         if (tile_skipped<BN, EPI>(epi, grp, mt, n0)) continue;
-        const LoraTile lt = lora_tile<SPLIT>(lora, mt, n0);
-        const int total = main_blocks + lt.blocks;
+        const LoraTile lt = (part == ksplit - 1) ? lora_tile<SPLIT>(lora, mt, n0) : LoraTile{0, 0, 0, 0};
+        const int kb0 = part * part_blocks;
+        const int total = part_blocks + lt.blocks;
         uint64_t rem = lt.amask;
         int a_bit = 0, rb = 0;
         for (int i = 0; i < total; ++i, ++kb) {
@@ -476,13 +488,13 @@ __global__ void __launch_bounds__(192, 1)
           }
           uint8_t* sa = smem + s * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
-          if (i < main_blocks) {
+          if (i < part_blocks) {
             mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
-            tma_load_2d(sa, &tm_a, &full_bar[s], i * C::BK, m0);
+            tma_load_2d(sa, &tm_a, &full_bar[s], (kb0 + i) * C::BK, m0);
             if (grp.tile_expert != nullptr)
-              tma_load_3d(sb, &tm_b, &full_bar[s], i * C::BK, n0, grp.tile_expert[mt]);
+              tma_load_3d(sb, &tm_b, &full_bar[s], (kb0 + i) * C::BK, n0, grp.tile_expert[mt]);
             else
-              tma_load_2d(sb, &tm_b, &full_bar[s], i * C::BK, n0);
+              tma_load_2d(sb, &tm_b, &full_bar[s], (kb0 + i) * C::BK, n0);
           } else {
             if (rb == 0) a_bit = __ffsll((long long)rem) - 1;
             const int kcol = a_bit * lora.rank_blocks * 32 + rb * 32;
@@ -513,12 +525,13 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t kb = 0;
       int ltile = 0;
       bool stop = false;
-      for (int t = blockIdx.x; t < num_tiles && !stop; t += gridDim.x) {
+      for (int t = blockIdx.x; t < num_work && !stop; t += gridDim.x) {
         int mt, nt;
-        gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
+        const int part = t / num_tiles;
+        gemm_tile_coords(t - part * num_tiles, m_tiles, n_tiles, mt, nt);
         if (tile_skipped<BN, EPI>(epi, grp, mt, nt * BN)) continue;
-        const LoraTile lt = lora_tile<SPLIT>(lora, mt, nt * BN);
-        const int total = main_blocks + lt.blocks;
+        const LoraTile lt = (part == ksplit - 1) ? lora_tile<SPLIT>(lora, mt, nt * BN) : LoraTile{0, 0, 0, 0};
+        const int total = part_blocks + lt.blocks;
         const int acc = ltile & 1;
         if (*abort_flag || !mbar_wait(&tempty_bar[acc], ((ltile >> 1) & 1) ^ 1, err, kErrGemmWait)) {
           *abort_flag = 1;
@@ -537,7 +550,7 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
           const uint32_t sb = sa + C::A_BYTES;
-          if (i < main_blocks) {
+          if (i < part_blocks) {
             const uint64_t ad = umma_desc_sw128(sa);
             const uint64_t bd = umma_desc_sw128(sb);
 #pragma unroll
@@ -569,9 +582,10 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int ltile = 0;
     int sbuf = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    for (int t = blockIdx.x; t < num_work; t += gridDim.x) {
       int mt, nt;
-      gemm_tile_coords(t, m_tiles, n_tiles, mt, nt);
+      const int part = t / num_tiles;
+      gemm_tile_coords(t - part * num_tiles, m_tiles, n_tiles, mt, nt);
       const int m0 = mt * C::BM, n0 = nt * BN;
       if (tile_skipped<BN, EPI>(epi, grp, mt, n0)) continue;
       const int acc = ltile & 1;
@@ -582,10 +596,18 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
       const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
-      if constexpr (epi_staged(EPI, BN))
+      if (ksplit > 1) {
+        // split-K part: fp32 partial sums; splitk_reduce_kernel applies the epilogue
+        GemmEpiArgs pe = epi;
+        pe.out = grp.ws + (int64_t)part * M * N;
+        pe.ldo = N;
+        pe.scale = 1.f;
+        epilogue_tile<BN, kEpiF32>(pe, tbase, row, M, n0);
+      } else if constexpr (epi_staged(EPI, BN)) {
         epilogue_tile_staged<BN, EPI>(epi, &tm_out, tbase, m0 + q * 32, M, n0, staging + q * 8192, sbuf);
-      else
+      } else {
         epilogue_tile<BN, EPI>(epi, tbase, row, M, n0);
+      }
       if (EPI == kEpiMultimemRed) __threadfence_system();  // this tile's reductions precede the next barrier
       // accumulator drained: hand the TMEM buffer back to the MMA warp
       tc_fence_before();
@@ -893,7 +915,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
     GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     configured = true;
   }
-  const int tiles = (N / BN) * ((M + C::BM - 1) / C::BM);
+  const int tiles = (N / BN) * ((M + C::BM - 1) / C::BM) * (grp.ksplit > 1 ? grp.ksplit : 1);
   const int grid = std::min(tiles, num_sms_for_current_device());
   kfn<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, err);
   GSB_CUDA_CHECK(cudaGetLastError());
@@ -985,6 +1007,75 @@ static void dispatch_epi(int epi_kind, const CUtensorMap& ta, const CUtensorMap&
   }
 }
 
+// Split-K finish: out = epilogue(sum over parts of ws[p]), with the epilogue
+// arithmetic of epilogue_tile (bf16 rounding of the projection before a
+// residual add; gate / up rounded to bf16 before SwiGLU, whose column tiles of
+// `swiglu_tile` hold the gate half then the up half). One thread per two columns.
+template <int EPI>
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int parts, int M, int N, float scale,
+                                     const __nv_bfloat16* __restrict__ res, int64_t ldr, void* __restrict__ out,
+                                     int64_t ldo, int swiglu_tile) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int half_n = N / 2;
+  if (idx >= (int64_t)M * half_n) return;
+  const int row = (int)(idx / half_n);
+  const int c = (int)(idx % half_n) * 2;
+  const int64_t plane = (int64_t)M * N;
+  auto sum2 = [&](int col, float& a0, float& a1) {
+    a0 = 0.f;
+    a1 = 0.f;
+    for (int p = 0; p < parts; ++p) {
+      const float2 v = *reinterpret_cast<const float2*>(ws + p * plane + (int64_t)row * N + col);
+      a0 += v.x;
+      a1 += v.y;
+    }
+  };
+  if (EPI == kEpiSwiGLU) {
+    const int t = c / swiglu_tile, j = c % swiglu_tile, h = swiglu_tile / 2;
+    if (j >= h) return;  // up columns are read by the thread of their gate columns
+    float g0, g1, u0, u1;
+    sum2(c, g0, g1);
+    sum2(c + h, u0, u1);
+    g0 = __bfloat162float(__float2bfloat16_rn(g0));
+    g1 = __bfloat162float(__float2bfloat16_rn(g1));
+    u0 = __bfloat162float(__float2bfloat16_rn(u0));
+    u1 = __bfloat162float(__float2bfloat16_rn(u1));
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(out) + (int64_t)row * ldo + t * h + j) =
+        pack_bf16x2(__fdividef(g0, 1.f + __expf(-g0)) * u0, __fdividef(g1, 1.f + __expf(-g1)) * u1);
+    return;
+  }
+  float a0, a1;
+  sum2(c, a0, a1);
+  if (EPI == kEpiF32) {
+    *reinterpret_cast<float2*>(reinterpret_cast<float*>(out) + (int64_t)row * ldo + c) = make_float2(a0 * scale,
+                                                                                                    a1 * scale);
+    return;
+  }
+  float v0 = a0 * scale, v1 = a1 * scale;
+  if (EPI == kEpiResAdd) {
+    const float2 r = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(res + (int64_t)row * ldr + c));
+    v0 = r.x + __bfloat162float(__float2bfloat16_rn(a0)) * scale;
+    v1 = r.y + __bfloat162float(__float2bfloat16_rn(a1)) * scale;
+  }
+  *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(out) + (int64_t)row * ldo + c) = pack_bf16x2(v0, v1);
+}
+
+// Split-K is used below this many output tiles (half the SMs); 0 turns it off.
+static int g_splitk_max_tiles = [] {
+  const char* v = getenv("GSB_GEMM_SPLITK_MAX_TILES");
+  return v != nullptr ? atoi(v) : 74;
+}();
+
+// Parts for a single-CTA GEMM of `tiles` output tiles and `kblocks` 64-deep K
+// blocks: the largest of 4 / 3 / 2 that divides kblocks, leaves at least four
+// blocks per part and keeps tiles * parts within one wave; 1 when none does.
+static int splitk_parts(int tiles, int kblocks, int nsms) {
+  if (tiles >= g_splitk_max_tiles) return 1;
+  for (int p = 4; p >= 2; --p)
+    if (kblocks % p == 0 && kblocks / p >= 4 && tiles * p <= nsms) return p;
+  return 1;
+}
+
 }  // namespace gsb
 
 // x [M, K] bf16, w [N, K] bf16 (both row-major, K contiguous).
@@ -1010,6 +1101,8 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
   GSB_CHECK(w.size(-1) == K, "K mismatch");
   GemmGroupArgs grp{};
   grp.tile_expert = nullptr;
+  grp.ksplit = 1;
+  grp.ws = nullptr;
   if (grouped) {
     GSB_CHECK(w.is_contiguous(), "grouped GEMM: w must be a contiguous [E, N, K] stack");
     GSB_CHECK(tile_expert->scalar_type() == at::kInt && tile_expert->numel() >= (M + 127) / 128,
@@ -1132,11 +1225,53 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     dispatch_epi_pair((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, errp, stream);
     return;
   }
+  // decode-sized GEMMs: split K when the output tiles alone would leave most SMs idle
+  const bool split_ok = !grouped && (epi_kind == kEpiStore || epi_kind == kEpiResAdd || epi_kind == kEpiSwiGLU ||
+                                     epi_kind == kEpiF32);
+  const int tiles = (int)(N / bn) * ((M + 127) / 128);
+  const int parts = split_ok ? splitk_parts(tiles, K / 64, num_sms_for_current_device()) : 1;
+  at::Tensor ws;
+  if (parts > 1) {
+    ws = at::empty({parts, M, N}, x.options().dtype(at::kFloat));
+    grp.ksplit = parts;
+    grp.ws = ws.data_ptr<float>();
+  }
   switch (bn) {
     case 64: dispatch_epi<64>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, errp, stream); break;
     case 128: dispatch_epi<128>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, errp, stream); break;
     case 256: dispatch_epi<256>((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, errp, stream); break;
   }
+  if (parts > 1) {
+    const int64_t threads = (int64_t)M * (N / 2);
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    const __nv_bfloat16* rp = epi.residual;
+    switch (epi_kind) {
+      case kEpiStore:
+        splitk_reduce_kernel<kEpiStore><<<blocks, 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
+                                                                   out.data_ptr(), out.stride(0), (int)bn);
+        break;
+      case kEpiResAdd:
+        splitk_reduce_kernel<kEpiResAdd><<<blocks, 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
+                                                                    out.data_ptr(), out.stride(0), (int)bn);
+        break;
+      case kEpiSwiGLU:
+        splitk_reduce_kernel<kEpiSwiGLU><<<blocks, 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
+                                                                    out.data_ptr(), out.stride(0), (int)bn);
+        break;
+      default:
+        splitk_reduce_kernel<kEpiF32><<<blocks, 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
+                                                                 out.data_ptr(), out.stride(0), (int)bn);
+    }
+    GSB_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+// Sets the largest output-tile count at which single-CTA GEMMs split K (0: never);
+// returns the previous value.
+int64_t gsb_gemm_splitk_max_tiles(int64_t v) {
+  const int64_t old = gsb::g_splitk_max_tiles;
+  if (v >= 0) gsb::g_splitk_max_tiles = (int)v;
+  return old;
 }
 
 // Sets the smallest M served by the CTA-pair kernel (negative: never); returns

@@ -69,3 +69,4 @@ void gsb_residual_axpy(const at::Tensor& h, const at::Tensor& y, double scale);
 void gsb_allreduce_ldreduce_p2p(int64_t mc_ptr, const at::Tensor& peer_ptrs, int64_t offset, int64_t nbytes,
                                 int64_t rank, int64_t tp);
 int64_t gsb_attn_packed(int64_t v);
+int64_t gsb_gemm_splitk_max_tiles(int64_t v);

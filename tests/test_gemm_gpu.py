@@ -361,3 +361,56 @@ def test_grouped_gemm(epi):
         else:
             ref = G.switched_gemm_reference(x[rows], w[ex])
         _close(out[rows], ref)
+
+
+class _SplitK:
+    """Temporarily set the output-tile count below which single-CTA GEMMs split K (0: never)."""
+
+    def __init__(self, v):
+        self.v = v
+
+    def __enter__(self):
+        from granite_switch_b200._native import native
+
+        self.old = native().gemm_splitk_max_tiles(self.v)
+
+    def __exit__(self, *a):
+        from granite_switch_b200._native import native
+
+        native().gemm_splitk_max_tiles(self.old)
+
+
+@pytest.mark.parametrize("epi", ["store", "resadd", "swiglu", "f32"])
+@pytest.mark.parametrize("m,k", [(1, 4096), (77, 12800), (200, 4096)])
+def test_split_k_decode_shapes(epi, m, k):
+    """Decode-sized GEMMs split K across CTAs (fp32 parts + reduce epilogue): equal to the
+    unsplit kernel and to the fp32 oracle, with the LoRA expand in the last part."""
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(7)
+    n, na, rank = 4096, 3, 32
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.02)
+    row_adapter = torch.randint(0, na + 1, (m,), device="cuda", dtype=torch.int32)
+    lb = _rand(n, na * rank, scale=0.05)
+    width = (2 if epi == "swiglu" else 1) * na * rank  # SwiGLU: gate and up shrink slices
+    cols = torch.arange(width, device="cuda")
+    keep = ((cols // rank) % na + 1).unsqueeze(0) == row_adapter.long().unsqueeze(1)
+    s = (_rand(m, width, scale=0.5).float() * keep).to(torch.bfloat16)
+    mask = _tile_mask(row_adapter, m)
+    res = _rand(m, n)
+    kind = {"store": G.EPI_STORE, "resadd": G.EPI_RESADD, "swiglu": G.EPI_SWIGLU, "f32": G.EPI_F32}[epi]
+    bn = 64 if epi != "swiglu" else 128
+    kw = dict(epi=kind, residual=res if epi == "resadd" else None, scale=0.5, s=s, lb=lb, tile_mask=mask,
+              rank=rank, num_adapters=na, slice_bounds=[0, n], bn=bn)
+    with _SplitK(74):
+        split = G.switched_gemm(x, w, **kw)
+    with _SplitK(0):
+        whole = G.switched_gemm(x, w, **kw)
+    ref = G.switched_gemm_reference(x, w, epi=kind, residual=kw["residual"], scale=0.5, s=s, lb=lb, rank=rank,
+                                    num_adapters=na, slice_bounds=[0, n], swiglu_tile=bn)
+    _close(split, ref)
+    _close(split, whole)
+    from granite_switch_b200._native import check_errors
+
+    check_errors(torch.device("cuda", 0))
