@@ -169,7 +169,7 @@ def test_pair_store_and_resadd(m):
     check_errors(x.device)
     _close(out, G.switched_gemm_reference(x, w))
     _close(res, G.switched_gemm_reference(x, w, epi=G.EPI_RESADD, residual=res_copy, scale=0.22))
-    with _PairMinM(-1):
+    with _PairMinM(-1), _SplitK(0):  # same accumulation order: no split of K on the single-CTA side
         single = G.switched_gemm(x, w, bn=256)
     assert torch.equal(out, single), "pair and single-CTA tiles must agree bit for bit"
 
