@@ -21,6 +21,7 @@
 // (reference: attention comes from vLLM's backends, called at
 // src/granite_switch/vllm/decoder/lora/decoder.py:146-174.)
 #include "common.cuh"
+#include <cstdlib>
 #include "tma_util.h"
 
 #include <ATen/ATen.h>
@@ -76,9 +77,18 @@ struct AttnCfg {
   static constexpr int Q_BYTES = ROWS * D * 2;
   // page ids of the CTA's key range, staged in shared memory once (past this
   // many pages the loop falls back to reading the block table in global memory)
-  static constexpr int PT_CAP = 2048;
+  // (the two-stage decode layout keeps 1024 so that three CTAs fit on an SM)
+  static constexpr int PT_CAP = (WARPS_M == 1 && STAGES == 2) ? 1024 : 2048;
   static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * TILE_BYTES + 256 + PT_CAP * 4;
 };
+
+// Decode layout (16-row tiles, head_dim 128): 3 stages and two CTAs per SM, or
+// 2 stages and three CTAs per SM (the same K/V bytes in flight per SM, more warps
+// to hide the latency of each tile's MMAs and softmax). Env GSB_ATTN_DECODE_STAGES.
+static int g_decode_stages = [] {
+  const char* e = std::getenv("GSB_ATTN_DECODE_STAGES");
+  return e ? std::atoi(e) : 3;
+}();
 
 template <int D, int WARPS_M, int KT, int STAGES>
 __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
@@ -436,6 +446,12 @@ static void launch_attn(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const
   GSB_CUDA_CHECK(cudaGetLastError());
 }
 
+int64_t gsb_attn_decode_stages(int64_t v) {
+  const int64_t old = g_decode_stages;
+  if (v == 2 || v == 3) g_decode_stages = (int)v;
+  return old;
+}
+
 // q: [T, >= Hq*D] bf16 (row stride q.stride(0)); caches [num_blocks, Hkv, 16, D];
 // block_table [S, max_blocks] int32; q_start [S+1] int32 (token offsets of each
 // request chunk in q); kv_len [S] int32 (cached + new keys); work_seq/work_row0
@@ -493,6 +509,7 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
   if (D == 128) {
     if (rows_per_tile == 128) GSB_ATTN(128, 8, 64, 2);
     else if (rows_per_tile == 64) GSB_ATTN(128, 4, 64, 2);
+    else if (g_decode_stages == 2) GSB_ATTN(128, 1, 64, 2);
     else GSB_ATTN(128, 1, 64, 3);
   } else if (D == 64) {
     if (rows_per_tile == 128) GSB_ATTN(64, 8, 64, 3);

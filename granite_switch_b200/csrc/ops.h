@@ -70,3 +70,4 @@ void gsb_allreduce_ldreduce_p2p(int64_t mc_ptr, const at::Tensor& peer_ptrs, int
                                 int64_t rank, int64_t tp);
 int64_t gsb_attn_packed(int64_t v);
 int64_t gsb_gemm_splitk_max_tiles(int64_t v);
+int64_t gsb_attn_decode_stages(int64_t v);

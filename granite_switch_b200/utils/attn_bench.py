@@ -78,10 +78,13 @@ def main():
     kc, vc, bt, q, out, qs, kvl = _setup(q_lens, kv_lens)
     ws, wr = A.build_work(q_lens, hq // hkv, 16)
     ws, wr = torch.tensor(ws, **i32), torch.tensor(wr, **i32)
-    ms = _time(lambda: A.paged_attention(q, kc, vc, bt, qs, kvl, ws, wr, 16, hq, 0.088, out, 1), args.iters)
     kv_bytes = 2 * sum(kv_lens) * hkv * d * 2
-    print(json.dumps({"case": "decode_128x4200", "ms": round(ms, 4), "gbs": round(kv_bytes / ms / 1e6, 1)}),
-          flush=True)
+    for stages in (3, 2):  # two CTAs per SM with 3 stages, or three with 2
+        old = _native.native().attn_decode_stages(stages)
+        ms = _time(lambda: A.paged_attention(q, kc, vc, bt, qs, kvl, ws, wr, 16, hq, 0.088, out, 1), args.iters)
+        _native.native().attn_decode_stages(old)
+        print(json.dumps({"case": "decode_128x4200", "stages": stages, "ms": round(ms, 4),
+                          "gbs": round(kv_bytes / ms / 1e6, 1)}), flush=True)
     _native.check_errors(torch.device("cuda", 0))
 
 

@@ -146,10 +146,14 @@ def _make_cache(lens, hkv, d, seed=0):
 
 
 @pytest.mark.parametrize("d", [64, 128])
-@pytest.mark.parametrize("mode", ["prefill", "prefill128", "decode"])
+@pytest.mark.parametrize("mode", ["prefill", "prefill128", "decode", "decode2"])
 @pytest.mark.parametrize("nsplit", [1, 3])
 def test_paged_attention(d, mode, nsplit):
+    from granite_switch_b200._native import native
     from granite_switch_b200.ops import attention as A
+
+    old_stages = native().attn_decode_stages(2 if mode == "decode2" else 3)
+    mode = "decode" if mode == "decode2" else mode
 
     hq, hkv = 8, 2
     g = hq // hkv
@@ -176,6 +180,7 @@ def test_paged_attention(d, mode, nsplit):
                       torch.tensor(kv_lens, dtype=torch.int32, device=dev),
                       torch.tensor(ws, dtype=torch.int32, device=dev), torch.tensor(wr, dtype=torch.int32, device=dev),
                       rows, hq, 0.125, out, nsplit, ws_o, ws_l)
+    native().attn_decode_stages(old_stages)
     ref = A.paged_attention_reference(q, kc, vc, bt, q_lens, kv_lens, hq, 0.125)
     err = (out.float() - ref).abs().max().item()
     assert err < 3e-2, err
