@@ -659,7 +659,8 @@ class NativeGraniteSwitch:
         dec = [i for i, ql in enumerate(q_lens) if ql * g <= 16]
         pre = [i for i, ql in enumerate(q_lens) if ql * g > 16]
         plans = []
-        pre_rows = A.TC_ROWS if (self.head_dim in (64, 128) and self.use_tc_attention) else 64
+        tc = self.head_dim in (64, 128) and self.use_tc_attention
+        pre_rows = A.tc_rows_for([q_lens[i] for i in pre], [kv_lens[i] for i in pre]) if tc and pre else 64
         for idx, rows in ((dec, 16), (pre, pre_rows)):
             if not idx:
                 continue

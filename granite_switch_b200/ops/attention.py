@@ -11,8 +11,25 @@ from .._native import err_buffer, native
 NUM_SMS = 148
 
 #: rows per CTA of the tcgen05 prefill attention the engine uses: 128 (one query
-#: tile per CTA) or 256 (two query tiles per CTA sharing each K/V tile)
-TC_ROWS = int(os.environ.get("GSB_ATTN_TC_ROWS", "128"))
+#: tile per CTA), 256 (two query tiles per CTA sharing each K/V tile) or 0 (chosen
+#: per step by :func:`tc_rows_for`)
+TC_ROWS = int(os.environ.get("GSB_ATTN_TC_ROWS", "0"))
+
+
+def tc_rows_for(q_lens: list[int], kv_lens: list[int]) -> int:
+    """Rows per CTA for a step's prefill chunks when ``TC_ROWS`` is 0.
+
+    256 when at least half of the prefill tokens are in long, mostly fresh chunks
+    (q_len >= 1024 over at most as many cached keys), else 128. Measured on B200
+    (d=128, 32/8 heads): fresh causal 4k runs at 825 vs 768 TFLOP/s with 256 rows
+    (16.5 vs 17.4 ms in an 8B step with two such prompts), while 8 chunks of 512
+    over 3.5k cached keys run at 759 vs 775 TFLOP/s.
+    """
+    if TC_ROWS:
+        return TC_ROWS
+    total = sum(q_lens)
+    long_fresh = sum(q for q, k in zip(q_lens, kv_lens) if q >= 1024 and k - q <= q)
+    return 256 if total and 2 * long_fresh >= total else 128
 
 
 def build_work(q_lens: list[int], group: int, rows_per_tile: int,

@@ -121,3 +121,13 @@ def test_routing_trace(tiny_dir, tmp_path):
     trace.flush()
     lines = open(path).read().splitlines()
     assert len(lines) == trace.step and json.loads(lines[0])["spans"]
+
+
+def test_prefill_layout_choice():
+    """Two query tiles per CTA only when long, mostly fresh chunks carry most prefill tokens."""
+    from granite_switch_b200.ops import attention as A
+
+    assert A.tc_rows_for([4096, 3968], [4096, 3968]) == 256
+    assert A.tc_rows_for([512] * 8, [4096] * 8) == 128
+    assert A.tc_rows_for([40, 60], [40, 60]) == 128
+    assert A.tc_rows_for([2048, 64], [2048, 9000]) == 256
