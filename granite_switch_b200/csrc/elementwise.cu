@@ -126,26 +126,36 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ldq,
   const int64_t slot = slots ? slots[t] : -1;
   const int nheads = Hq + Hkv;
   constexpr int HALF = D / 2;
-  // rotate q and k heads: thread handles a pair (i, i + D/2)
-  for (int idx = threadIdx.x; idx < nheads * HALF; idx += blockDim.x) {
-    const int h = idx / HALF;
-    const int i = idx % HALF;
+  constexpr int CH = HALF / 8;  // 8-element (16-byte) chunks per half
+  // rotate q and k heads: a thread handles 8 pairs (i, i + D/2) with 16-byte loads and stores
+  for (int idx = threadIdx.x; idx < nheads * CH; idx += blockDim.x) {
+    const int h = idx / CH;
+    const int i0 = (idx % CH) * 8;
     __nv_bfloat16* hp = row + h * D;
-    const float x1 = bf2f(hp[i]);
-    const float x2 = bf2f(hp[i + HALF]);
-    const float c = cs[i], s = cs[HALF + i];
-    // x*cos + rotate_half(x)*sin; cos/sin equal on both halves
-    const float y1 = x1 * c - x2 * s;
-    const float y2 = x2 * c + x1 * s;
-    const __nv_bfloat16 b1 = f2bf(y1), b2 = f2bf(y2);
-    hp[i] = b1;
-    hp[i + HALF] = b2;
+    const uint4 a = *reinterpret_cast<const uint4*>(hp + i0);
+    const uint4 b = *reinterpret_cast<const uint4*>(hp + HALF + i0);
+    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+    uint32_t ya[4], yb[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 x1 = unpack_bf16x2(av[j]), x2 = unpack_bf16x2(bv[j]);
+      const float c0 = cs[i0 + 2 * j], c1 = cs[i0 + 2 * j + 1];
+      const float s0 = cs[HALF + i0 + 2 * j], s1 = cs[HALF + i0 + 2 * j + 1];
+      // x*cos + rotate_half(x)*sin; cos/sin equal on both halves
+      const float y10 = x1.x * c0 - x2.x * s0, y11 = x1.y * c1 - x2.y * s1;
+      const float y20 = x2.x * c0 + x1.x * s0, y21 = x2.y * c1 + x1.y * s1;
+      ya[j] = pack_bf16x2(y10, y11);
+      yb[j] = pack_bf16x2(y20, y21);
+    }
+    const uint4 oa = make_uint4(ya[0], ya[1], ya[2], ya[3]), ob = make_uint4(yb[0], yb[1], yb[2], yb[3]);
+    *reinterpret_cast<uint4*>(hp + i0) = oa;
+    *reinterpret_cast<uint4*>(hp + HALF + i0) = ob;
     if (h >= Hq && slot >= 0 && slot < num_slots) {
       const int kh = h - Hq;
       const int64_t blk = slot / BS, off = slot % BS;
       __nv_bfloat16* kc = k_cache + ((blk * Hkv + kh) * BS + off) * D;
-      kc[i] = b1;
-      kc[i + HALF] = b2;
+      *reinterpret_cast<uint4*>(kc + i0) = oa;
+      *reinterpret_cast<uint4*>(kc + HALF + i0) = ob;
     }
   }
   if (slot >= 0 && slot < num_slots) {
@@ -268,6 +278,8 @@ void gsb_rope_kv(const at::Tensor& qkv, const at::Tensor& positions, const at::T
                  const c10::optional<at::Tensor>& slots, int64_t num_q_heads, int64_t num_kv_heads,
                  int64_t head_dim, const at::Tensor& err) {
   GSB_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.stride(1) == 1, "rope: bf16 qkv required");
+  GSB_CHECK(qkv.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(qkv.data_ptr()) & 15) == 0,
+            "rope: qkv rows must be 16-byte aligned");
   GSB_CHECK(positions.scalar_type() == at::kLong && cos_sin.scalar_type() == at::kFloat,
             "rope: int64 positions and fp32 cos_sin required");
   GSB_CHECK(qkv.size(1) >= (num_q_heads + 2 * num_kv_heads) * head_dim, "rope: qkv too narrow");
