@@ -75,3 +75,50 @@ def test_chatml_preserve_needs_thinking_off():
     conv2.build_prompt("ans")
     with pytest.raises(RuntimeError):
         conv2.record_answer(encode(tok, "Ten dollars."), adapter="ans")
+
+
+def _engine_with_template(tmp_path):
+    import torch
+
+    from granite_switch_b200.composer.compose import compose_checkpoint
+    from granite_switch_b200.composer.synthetic import base_config, random_base_state, synthetic_adapters
+    from granite_switch_b200.engine import LLM, EngineConfig
+
+    tok = make_tokenizer(granite_template("4.1"))
+    cfg = base_config("tiny", num_hidden_layers=2)
+    ads = synthetic_adapters(cfg, 2, 8, ("q", "k", "v", "o"), seed=1)
+    for a in ads:
+        a.invocation_tokens = encode(tok, HEADER["4.1"])
+    ids, setup = configure_tokenizer(tok, ads)
+    d = str(tmp_path / "conv")
+    config = compose_checkpoint(cfg, random_base_state(cfg), ads, d, dtype=torch.float32, control_token_ids=ids,
+                                default_substitute=setup.lora_substitute)
+    llm = LLM(d, device="cpu", engine_config=EngineConfig(max_num_seqs=2, max_num_batched_tokens=512,
+                                                          num_kv_blocks=256, max_model_len=2048))
+    return tok, config, llm
+
+
+def test_turn_two_prefix_reuse_by_policy(tmp_path):
+    """Turn 2 of an aLoRA conversation (reference: tests/integration/test_conversation_prefix_cache.py):
+    PRESERVE sends the turn-1 ids verbatim, so all of them are cache hits; RE_PREFILL re-renders the
+    history in base form and reuses the cache up to the turn-1 control token."""
+    from granite_switch_b200.engine import SamplingParams
+
+    tok, config, llm = _engine_with_template(tmp_path)
+    cached = {}
+    for policy in (KVHistoryPolicy.RE_PREFILL, KVHistoryPolicy.PRESERVE_MIXED_HISTORY):
+        llm.engine.blocks.reset_prefix_cache()
+        conv = Conversation(tok, policy, config)
+        conv.system("Answer from the document. The permit fee is ten dollars and renewals take a week.")
+        conv.user("What is the fee for a permit?")
+        p1 = conv.build_prompt("adapter_0")
+        out1 = llm.generate([list(p1)], SamplingParams(max_tokens=6))[0]
+        conv.record_answer(out1.output_ids, adapter="adapter_0")
+        conv.user("And how long does a renewal take?")
+        p2 = conv.build_prompt("adapter_0")
+        out2 = llm.generate([list(p2)], SamplingParams(max_tokens=2))[0]
+        cached[policy] = (out2.num_cached_tokens, len(p1), p1.index(config.adapter_token_ids[0]))
+    pre, pre_p1, _ = cached[KVHistoryPolicy.PRESERVE_MIXED_HISTORY]
+    re, _, ctrl_pos = cached[KVHistoryPolicy.RE_PREFILL]
+    assert pre >= 16 * (pre_p1 // 16)            # every full block of the sent turn-1 prompt
+    assert 16 * (ctrl_pos // 16) <= re < pre     # base-form history: hits stop at the old control token
