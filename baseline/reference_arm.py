@@ -84,6 +84,7 @@ def _run(args, emit, metric, world):
     seen = {}
     first_tok = {}
     ttfts = []
+    first_calls = set()
     counter = [0]
 
     def submit(conv, now):
@@ -93,6 +94,8 @@ def _run(args, emit, metric, world):
         sp = SamplingParams(max_tokens=conv.calls[conv.next_call].gen_len, temperature=0.0, ignore_eos=True)
         engine.add_request(rid, {"prompt_token_ids": prompt}, sp)
         live[rid] = (conv, prompt, now)
+        if conv.next_call == 0:
+            first_calls.add(rid)
 
     t0 = time.perf_counter()
     nxt = [0]
@@ -116,7 +119,7 @@ def _run(args, emit, metric, world):
             seen[o.request_id] = len(toks)
             if toks and o.request_id not in first_tok:
                 first_tok[o.request_id] = tnow
-                ttfts.append((tnow, tnow - sub))
+                ttfts.append((tnow, tnow - sub, o.request_id in first_calls))
             if o.finished:
                 seen.pop(o.request_id, None)
                 stats["prompt"] += len(prompt)
@@ -144,7 +147,8 @@ def _run(args, emit, metric, world):
     w1 = time.perf_counter()
     tok_after = stats["gen"]
     gen = tok_after - tok_before
-    win = [t for (ts, t) in ttfts if w0 <= ts <= w1]
+    win = [t for (ts, t, _) in ttfts if w0 <= ts <= w1]
+    win_first = [t for (ts, t, first) in ttfts if w0 <= ts <= w1 and first]
     dp, dc = stats["prompt"] - p0, stats["cached"] - c0
     hit = None
     try:  # vLLM's own prefix-cache counters, when this version exposes them
@@ -159,12 +163,17 @@ def _run(args, emit, metric, world):
           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
           "data": "synthetic (random prompts, random-init base and adapter weights)", "impl": "reference",
           "timing": "host clock (vLLM runs the model in its own engine process)",
-          "p50_ttft_s": round(statistics.median(win), 4) if win else None, "ttft_samples": len(win),
+          "p50_ttft_s": round(statistics.median(win), 4) if win else None,
+          "p90_ttft_s": round(sorted(win)[min(len(win) - 1, int(0.9 * len(win)))], 4) if win else None,
+          "ttft_samples": len(win),
+          "first_call_p50_ttft_s": round(statistics.median(win_first), 4) if win_first else None,
+          "first_call_ttft_samples": len(win_first),
           "prefix_hit_rate": round(dc / dp, 4) if dp else None, "vllm_prefix_cache_counters": hit,
           "config": {"model": f"{args.preset}-shape", "global_batch": args.max_num_seqs, "seq_len": args.context_len,
                      "parallelism": f"tp{world}", "adapters": "12 aLoRA r32 q/k/v/o",
                      "workload": f"poisson {args.rate}/s, {args.calls} chained calls, inv 16-64, gen 32-128",
-                     "mode": args.mode, "ramp_steps": ramp, "vllm": _vllm_version()}})
+                     "mode": args.mode, "scheduling_policy": "fcfs (vLLM default)", "ramp_steps": ramp,
+                     "vllm": _vllm_version()}})
 
 
 def _vllm_version():

@@ -56,9 +56,16 @@ def parse_args():
     p.add_argument("--mode", choices=["alora", "lora"], default="alora")
     p.add_argument("--no-fused-comm", dest="fused_comm", action="store_false",
                    help="use NCCL all-reduce instead of the fused GEMM+multimem collectives for TP")
+    p.add_argument("--scheduling-policy", choices=["cache_affinity", "fcfs"], default="cache_affinity",
+                   help="engine admission order (the reference arm's vLLM engine is FCFS)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-blocks", type=int, default=None)
     return p.parse_args()
+
+
+def _pct(xs, q):
+    s = sorted(xs)
+    return s[min(len(s) - 1, int(q * len(s)))]
 
 
 def emit(obj):
@@ -111,7 +118,8 @@ def run_native(args):
     config, base = model_config(args)
     ecfg = EngineConfig(max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
                         max_model_len=args.context_len + args.calls * 200 + 256, tensor_parallel_size=world,
-                        num_kv_blocks=args.kv_blocks, fused_tp_comm=args.fused_comm, seed=args.seed)
+                        num_kv_blocks=args.kv_blocks, fused_tp_comm=args.fused_comm, seed=args.seed,
+                        scheduling_policy=args.scheduling_policy)
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
               random_init=dict(lora_modules=("qkv", "o"), rank=32, seed=args.seed), tp_rank=rank, tp_group=group)
     eng = llm.engine
@@ -120,14 +128,15 @@ def run_native(args):
     convs = make_workload(wl)
     ctrl = config.adapter_token_ids
     by_req = {}
-    submit_times = {}
+    first_calls = set()  # request ids of conversations' first calls (cold contexts)
 
     def submit(conv, now):
         prompt = call_prompt(conv, ctrl, args.mode)
         gen = conv.calls[conv.next_call].gen_len
         r = eng.add_request(prompt, SamplingParams(max_tokens=gen, ignore_eos=True), arrival_time=now)
         by_req[r.request_id] = conv
-        submit_times[r.request_id] = now
+        if conv.next_call == 0:
+            first_calls.add(r.request_id)
 
     def on_finish(req):
         conv = by_req.pop(req.request_id)
@@ -204,13 +213,12 @@ def run_native(args):
     gen = eng.stats.generated_tokens - gen0
     launches = _native.launch_count() - launches0
     # TTFT of calls whose first token landed in the timed window
-    ttfts = []
-    for r in finished_log:
+    ttfts, first_ttfts = [], []
+    for r in finished_log + list(eng.scheduler.running):
         if r.first_token_time is not None and w0 <= r.first_token_time <= w1:
             ttfts.append(r.first_token_time - r.arrival_time)
-    for r in eng.scheduler.running:
-        if r.first_token_time is not None and w0 <= r.first_token_time <= w1:
-            ttfts.append(r.first_token_time - r.arrival_time)
+            if r.request_id in first_calls:
+                first_ttfts.append(r.first_token_time - r.arrival_time)
     dq, dh = eng.blocks.queries - q0, eng.blocks.hits - h0
     value = gen / (dev_ms / 1e3)
     e2e = gen / wall_s
@@ -224,7 +232,10 @@ def run_native(args):
             "dtype": "bf16", "data": "synthetic (random prompts, random-init base and adapter weights)",
             "impl": "native",
             "p50_ttft_s": round(statistics.median(ttfts), 4) if ttfts else None,
+            "p90_ttft_s": round(_pct(ttfts, 0.9), 4) if ttfts else None,
             "ttft_samples": len(ttfts),
+            "first_call_p50_ttft_s": round(statistics.median(first_ttfts), 4) if first_ttfts else None,
+            "first_call_ttft_samples": len(first_ttfts),
             "prefix_hit_rate": round(dh / dq, 4) if dq else None,
             "prefix_hit_rate_overall": round(eng.prefix_cache_hit_rate(), 4),
             "config": {"model": f"{args.preset}-shape" + (f"-L{args.layers}" if args.layers else ""),
@@ -232,6 +243,7 @@ def run_native(args):
                        "parallelism": f"tp{world}", "adapters": "12 aLoRA r32 q/k/v/o",
                        "workload": f"poisson {args.rate}/s, {args.calls} chained calls, inv 16-64, gen 32-128",
                        "mode": args.mode, "max_num_batched_tokens": args.max_num_batched_tokens,
+                       "scheduling_policy": args.scheduling_policy,
                        "ramp_steps": ramp, "l2": "inputs larger than L2 (each step streams all weights)",
                        "fused_comm": bool(getattr(llm.model, "comm", None) is not None)},
             "e2e": {"value": round(e2e, 2), "unit": "output tok/s", "h2d_bytes_per_step": (ex.h2d_bytes - h2d0) // args.steps,

@@ -94,6 +94,12 @@ class BlockManager:
         self.hits += hit * BLOCK_SIZE
         return hit * BLOCK_SIZE
 
+    def first_block_cached(self, token_ids: list[int]) -> bool:
+        """Whether the first full block of ``token_ids`` is in the prefix cache (one hash probe)."""
+        if not self.enable_prefix_caching or len(token_ids) <= BLOCK_SIZE:
+            return False
+        return chain_hashes(token_ids, 1)[0] in self.by_hash
+
     # ---------------------------------------------------------------- allocation
     def blocks_needed(self, req: Request, num_tokens: int) -> int:
         need = (num_tokens + BLOCK_SIZE - 1) // BLOCK_SIZE

@@ -37,6 +37,7 @@ class EngineConfig:
     dtype: str = "bfloat16"
     seed: int = 0
     fused_tp_comm: bool = False            # symmetric-memory fused GEMM + reduction kernels
+    scheduling_policy: str = "cache_affinity"  # or "fcfs" (admission order, see engine.scheduler)
 
 
 @dataclass
@@ -91,7 +92,8 @@ class LLMEngine:
         self.blocks = BlockManager(num_blocks, self.ecfg.enable_prefix_caching)
         self.router = HostRouter(config)
         self.scheduler = Scheduler(self.blocks, self.ecfg.max_num_seqs, self.ecfg.max_num_batched_tokens,
-                                   self.ecfg.enable_chunked_prefill, route_fn=self.router)
+                                   self.ecfg.enable_chunked_prefill, route_fn=self.router,
+                                   policy=self.ecfg.scheduling_policy)
         self.stats = EngineStats()
         self.requests: dict[str, Request] = {}
         self.eos = config.eos_token_id if isinstance(config.eos_token_id, int) else None
@@ -185,7 +187,7 @@ class LLMEngine:
     def metrics(self) -> dict:
         return {
             "num_requests_running": len(self.scheduler.running),
-            "num_requests_waiting": len(self.scheduler.waiting),
+            "num_requests_waiting": self.scheduler.num_waiting,
             "prefix_cache_queries_total": self.blocks.queries,
             "prefix_cache_hits_total": self.blocks.hits,
             "generation_tokens_total": self.stats.generated_tokens,

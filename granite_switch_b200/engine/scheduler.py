@@ -1,11 +1,25 @@
 """Continuous batching with chunked prefill (one token budget per step).
 
 Each step: running requests first (one decode token, or their next prefill
-chunk), then waiting requests in arrival order while the token budget, the
-sequence cap and free KV blocks allow. A new request first acquires its
-longest cached prefix. When a running request cannot get a block, the most
-recently admitted running request is preempted (its blocks are freed; it
-recomputes later, largely from the prefix cache).
+chunk), then waiting requests while the token budget, the sequence cap and
+free KV blocks allow. A new request first acquires its longest cached prefix.
+When a running request cannot get a block, the most recently admitted running
+request is preempted (its blocks are freed; it recomputes later, largely from
+the prefix cache).
+
+Admission order (``policy``):
+
+* ``"fcfs"``: arrival order (vLLM's default policy).
+* ``"cache_affinity"``: requests whose first KV block is in the prefix cache
+  when they arrive (the next call of a conversation, a preempted request, a
+  prompt sharing a cached system prompt) are admitted before cold ones, in
+  arrival order within each class. Under overload this finishes the
+  conversations whose context is resident instead of prefilling new contexts
+  that evict it, so each generated token costs less prefill; an idle or
+  lightly loaded server admits everything at once either way. This is the
+  longest-prefix-first idea of cache-aware schedulers reduced to one O(1)
+  probe per request at arrival, so scheduling cost does not grow with the
+  queue.
 """
 from __future__ import annotations
 
@@ -41,24 +55,38 @@ class SchedulerOutput:
         return all(c.num_tokens == 1 and not c.req.prefilling for c in self.chunks)
 
 
+POLICIES = ("fcfs", "cache_affinity")
+
+
 class Scheduler:
     def __init__(self, blocks: BlockManager, max_num_seqs: int = 256, max_num_batched_tokens: int = 8192,
-                 enable_chunked_prefill: bool = True, route_fn=None):
+                 enable_chunked_prefill: bool = True, route_fn=None, policy: str = "fcfs"):
+        if policy not in POLICIES:
+            raise ValueError(f"unknown scheduling policy {policy!r} (expected one of {POLICIES})")
+        self.policy = policy
         self.blocks = blocks
         self.max_num_seqs = max_num_seqs
         self.max_num_batched_tokens = max_num_batched_tokens
         self.chunked = enable_chunked_prefill
-        self.waiting: deque[Request] = deque()
+        self.waiting: deque[Request] = deque()  # cold requests (every request under "fcfs")
+        self.warm: deque[Request] = deque()     # "cache_affinity": first block cached at arrival
         self.running: list[Request] = []
         self.route_fn = route_fn  # (ids, carry) -> carry after ids
         self.num_preemptions = 0
 
     def add(self, req: Request) -> None:
         req.status = RequestStatus.WAITING
-        self.waiting.append(req)
+        if self.policy == "cache_affinity" and self.blocks.first_block_cached(req.prompt_ids):
+            self.warm.append(req)
+        else:
+            self.waiting.append(req)
+
+    @property
+    def num_waiting(self) -> int:
+        return len(self.waiting) + len(self.warm)
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.warm or self.running)
 
     def _preempt(self, req: Request, out: SchedulerOutput) -> None:
         self.running.remove(req)
@@ -67,7 +95,8 @@ class Scheduler:
         req.carry = 0
         req.matched = False
         req.status = RequestStatus.PREEMPTED
-        self.waiting.appendleft(req)
+        # resumes first: its computed blocks stay cached until evicted
+        (self.warm if self.policy == "cache_affinity" else self.waiting).appendleft(req)
         out.preempted.append(req)
         self.num_preemptions += 1
 
@@ -98,8 +127,11 @@ class Scheduler:
             budget -= n
             i += 1
         # ---- waiting requests
-        while self.waiting and budget > 0 and len(self.running) < self.max_num_seqs:
-            req = self.waiting[0]
+        while budget > 0 and len(self.running) < self.max_num_seqs:
+            queue = self.warm if self.warm else self.waiting
+            if not queue:
+                break
+            req = queue[0]
             if not req.matched:
                 req.matched = True
                 hit = self.blocks.match_prefix(req)
@@ -109,8 +141,8 @@ class Scheduler:
             remaining = req.num_tokens - req.num_computed
             n = min(remaining, budget) if self.chunked else remaining
             if n > budget or not self.blocks.allocate(req, req.num_computed + n):
-                break  # keep arrival order; retry next step
-            self.waiting.popleft()
+                break  # keep the admission order; retry next step
+            queue.popleft()
             req.status = RequestStatus.RUNNING
             self.running.append(req)
             out.chunks.append(ScheduledChunk(req, req.num_computed, n))
@@ -125,13 +157,10 @@ class Scheduler:
         self.blocks.free_request(req)
 
     def abort(self, request_id: str) -> bool:
-        for q in (self.running, self.waiting):
+        for q in (self.running, self.warm, self.waiting):
             for r in list(q):
                 if r.request_id == request_id:
-                    if r in self.running:
-                        self.running.remove(r)
-                    else:
-                        self.waiting.remove(r)
+                    q.remove(r)
                     self.blocks.free_request(r)
                     r.status = RequestStatus.FINISHED
                     r.finish_reason = "abort"

@@ -147,6 +147,8 @@ def main(argv=None):
     ap.add_argument("--tensor-parallel-size", type=int, default=1)
     ap.add_argument("--pipeline-parallel-size", type=int, default=1)
     ap.add_argument("--no-fused-tp-comm", action="store_true", help="reduce with NCCL only")
+    ap.add_argument("--scheduling-policy", choices=["cache_affinity", "fcfs"], default="cache_affinity",
+                    help="admission order: requests whose context is cached first, or arrival order")
     args = ap.parse_args(argv)
     import uvicorn
 
@@ -156,7 +158,8 @@ def main(argv=None):
     ecfg = EngineConfig(max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
                         max_model_len=args.max_model_len, gpu_memory_utilization=args.gpu_memory_utilization,
                         enable_prefix_caching=not args.no_prefix_caching, tensor_parallel_size=tp,
-                        pipeline_parallel_size=pp, fused_tp_comm=not args.no_fused_tp_comm)
+                        pipeline_parallel_size=pp, fused_tp_comm=not args.no_fused_tp_comm,
+                        scheduling_policy=args.scheduling_policy)
     sync = None
     if tp * pp > 1:
         # one process per GPU (torchrun); rank 0 serves HTTP and drives the others in lock step

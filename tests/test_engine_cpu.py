@@ -9,6 +9,7 @@ from granite_switch_b200.composer.synthetic import compose_synthetic
 from granite_switch_b200.engine import LLM, EngineConfig, SamplingParams
 from granite_switch_b200.engine.kv_cache import BlockManager, chain_hashes
 from granite_switch_b200.engine.request import Request
+from granite_switch_b200.engine.scheduler import Scheduler, SchedulerOutput
 from granite_switch_b200.models import GraniteSwitchForCausalLM
 
 
@@ -73,9 +74,11 @@ def test_prefix_cache_shared_across_adapters(tiny_dir):
     assert [first.output_ids] + [r.output_ids for r in rest] == ref
 
 
-def test_preemption_keeps_outputs(tiny_dir):
+@pytest.mark.parametrize("policy", ["fcfs", "cache_affinity"])
+def test_preemption_keeps_outputs(tiny_dir, policy):
     prompts = _prompts(tiny_dir, 6, seed=2, lo=40, hi=70)
-    ecfg = EngineConfig(max_num_seqs=6, max_num_batched_tokens=64, num_kv_blocks=14, max_model_len=256)
+    ecfg = EngineConfig(max_num_seqs=6, max_num_batched_tokens=64, num_kv_blocks=14, max_model_len=256,
+                        scheduling_policy=policy)
     llm = LLM(tiny_dir, device="cpu", engine_config=ecfg)
     outs = llm.generate(prompts, SamplingParams(max_tokens=8))
     assert llm.engine.scheduler.num_preemptions > 0
@@ -99,6 +102,58 @@ def test_block_manager_lru_and_hashes():
     r3 = Request([9] * 70)
     bm.match_prefix(r3)
     assert not bm.allocate(r3, 70)  # 5 blocks > 4
+
+
+def _cache_context(bm, ctx):
+    """Run one request over ``ctx`` through the block manager so its full blocks end up cached."""
+    r = Request(ctx + [1])
+    bm.match_prefix(r)
+    assert bm.allocate(r, len(r.prompt_ids))
+    r.num_computed = len(r.prompt_ids)
+    bm.register_full_blocks(r)
+    bm.free_request(r)
+
+
+@pytest.mark.parametrize("policy", ["fcfs", "cache_affinity"])
+def test_scheduling_policy_admission_order(policy):
+    """cache_affinity admits a request whose context is cached ahead of an older cold one;
+    fcfs keeps arrival order."""
+    bm = BlockManager(64)
+    ctx = list(range(100, 164))  # four full blocks
+    _cache_context(bm, ctx)
+    assert bm.first_block_cached(ctx + [2]) and not bm.first_block_cached(list(range(500, 540)))
+    sch = Scheduler(bm, max_num_seqs=1, max_num_batched_tokens=512, policy=policy)
+    cold, warm = Request(list(range(500, 540))), Request(ctx + [2, 3])
+    sch.add(cold)
+    sch.add(warm)
+    assert sch.num_waiting == 2
+    first = sch.schedule().chunks[0].req
+    assert first is (warm if policy == "cache_affinity" else cold)
+    assert first.num_cached_tokens == (64 if policy == "cache_affinity" else 0)
+    # the other request waits for a free sequence slot, then runs
+    sch.finish(first, "length")
+    assert sch.schedule().chunks[0].req is (cold if policy == "cache_affinity" else warm)
+    assert sch.num_waiting == 0
+
+
+def test_cache_affinity_preempted_and_abort():
+    bm = BlockManager(64)
+    sch = Scheduler(bm, max_num_seqs=2, max_num_batched_tokens=512, policy="cache_affinity")
+    a = Request(list(range(10, 50)))
+    sch.add(a)
+    assert sch.schedule().chunks[0].req is a
+    b = Request(list(range(60, 100)))
+    sch.add(b)  # cold, arrives while a runs
+    sch._preempt(a, SchedulerOutput())
+    assert sch.warm[0] is a  # a preempted request resumes before cold arrivals
+    assert [c.req for c in sch.schedule().chunks] == [a, b]
+    c = Request(list(range(10, 50)) + [5])
+    a.num_computed = 40  # a's prefill ran: its two full blocks are published
+    bm.register_full_blocks(a)
+    sch.add(c)
+    assert c in sch.warm and sch.abort(c.request_id) and c not in sch.warm
+    with pytest.raises(ValueError):
+        Scheduler(bm, policy="lifo")
 
 
 def test_routing_trace(tiny_dir, tmp_path):
