@@ -19,6 +19,13 @@ steps. ``e2e`` is the same metric measured by the host clock around the same
 K steps of the public engine API, whose every step copies its inputs from
 pinned host memory and reads the sampled ids back.
 
+The engine admits requests under its default ``cache_affinity`` policy:
+a call whose context is already in the prefix cache (a conversation's next
+call) is admitted before new conversations; ``--scheduling-policy fcfs``
+admits in arrival order, as the reference's vLLM engine does. The line
+reports p50 / p90 TTFT over every call whose first token landed in the timed
+window and, separately, the p50 TTFT of conversations' first calls.
+
 ``--impl reference`` runs the unmodified reference (granite-switch's vLLM
 plugin from baseline/_ref) on the same workload and prints the same line.
 """
