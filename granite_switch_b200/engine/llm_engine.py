@@ -38,6 +38,7 @@ class EngineConfig:
     seed: int = 0
     fused_tp_comm: bool = False            # symmetric-memory fused GEMM + reduction kernels
     scheduling_policy: str = "cache_affinity"  # or "fcfs" (admission order, see engine.scheduler)
+    max_wait_steps: int | None = None      # cache_affinity: steps before a cold request goes first
 
 
 @dataclass
@@ -93,7 +94,7 @@ class LLMEngine:
         self.router = HostRouter(config)
         self.scheduler = Scheduler(self.blocks, self.ecfg.max_num_seqs, self.ecfg.max_num_batched_tokens,
                                    self.ecfg.enable_chunked_prefill, route_fn=self.router,
-                                   policy=self.ecfg.scheduling_policy)
+                                   policy=self.ecfg.scheduling_policy, max_wait_steps=self.ecfg.max_wait_steps)
         self.stats = EngineStats()
         self.requests: dict[str, Request] = {}
         self.eos = config.eos_token_id if isinstance(config.eos_token_id, int) else None

@@ -41,6 +41,7 @@ class Request:
     eos_token_id: int | None = None
     output_ids: list[int] = field(default_factory=list)
     status: RequestStatus = RequestStatus.WAITING
+    enqueue_step: int = 0              # scheduler step at which it (re)entered a waiting queue
     num_computed: int = 0              # tokens whose KV is in the cache
     block_ids: list[int] = field(default_factory=list)
     block_hashes: list[int] = field(default_factory=list)  # chained hashes of full blocks

@@ -19,7 +19,10 @@ Admission order (``policy``):
   lightly loaded server admits everything at once either way. This is the
   longest-prefix-first idea of cache-aware schedulers reduced to one O(1)
   probe per request at arrival, so scheduling cost does not grow with the
-  queue.
+  queue. ``max_wait_steps`` bounds how long a cold request can be passed
+  over: once the oldest cold request has waited that many engine steps, it
+  is admitted ahead of warm ones. The bound counts steps, not seconds, so
+  every tensor-parallel rank takes the same decision.
 """
 from __future__ import annotations
 
@@ -60,7 +63,8 @@ POLICIES = ("fcfs", "cache_affinity")
 
 class Scheduler:
     def __init__(self, blocks: BlockManager, max_num_seqs: int = 256, max_num_batched_tokens: int = 8192,
-                 enable_chunked_prefill: bool = True, route_fn=None, policy: str = "fcfs"):
+                 enable_chunked_prefill: bool = True, route_fn=None, policy: str = "fcfs",
+                 max_wait_steps: int | None = None):
         if policy not in POLICIES:
             raise ValueError(f"unknown scheduling policy {policy!r} (expected one of {POLICIES})")
         self.policy = policy
@@ -73,9 +77,12 @@ class Scheduler:
         self.running: list[Request] = []
         self.route_fn = route_fn  # (ids, carry) -> carry after ids
         self.num_preemptions = 0
+        self.max_wait_steps = max_wait_steps
+        self.steps = 0
 
     def add(self, req: Request) -> None:
         req.status = RequestStatus.WAITING
+        req.enqueue_step = self.steps
         if self.policy == "cache_affinity" and self.blocks.first_block_cached(req.prompt_ids):
             self.warm.append(req)
         else:
@@ -100,7 +107,16 @@ class Scheduler:
         out.preempted.append(req)
         self.num_preemptions += 1
 
+    def _next_queue(self) -> deque:
+        if not self.warm:
+            return self.waiting
+        if (self.max_wait_steps is not None and self.waiting
+                and self.steps - self.waiting[0].enqueue_step >= self.max_wait_steps):
+            return self.waiting  # the oldest cold request has waited long enough
+        return self.warm
+
     def schedule(self) -> SchedulerOutput:
+        self.steps += 1
         out = SchedulerOutput()
         budget = self.max_num_batched_tokens
         scheduled = set()
@@ -128,7 +144,7 @@ class Scheduler:
             i += 1
         # ---- waiting requests
         while budget > 0 and len(self.running) < self.max_num_seqs:
-            queue = self.warm if self.warm else self.waiting
+            queue = self._next_queue()
             if not queue:
                 break
             req = queue[0]

@@ -136,6 +136,23 @@ def test_scheduling_policy_admission_order(policy):
     assert sch.num_waiting == 0
 
 
+def test_cache_affinity_max_wait_steps():
+    """A cold request passed over for max_wait_steps engine steps is admitted ahead of warm ones."""
+    bm = BlockManager(64)
+    ctx = list(range(100, 164))
+    _cache_context(bm, ctx)
+    sch = Scheduler(bm, max_num_seqs=1, max_num_batched_tokens=512, policy="cache_affinity", max_wait_steps=2)
+    cold = Request(list(range(500, 540)))
+    sch.add(cold)
+    order = []
+    for i in range(3):
+        sch.add(Request(ctx + [2, i]))  # a warm arrival every step
+        r = sch.schedule().chunks[0].req
+        order.append(r is cold)
+        sch.finish(r, "length")
+    assert order == [False, True, False]
+
+
 def test_cache_affinity_preempted_and_abort():
     bm = BlockManager(64)
     sch = Scheduler(bm, max_num_seqs=2, max_num_batched_tokens=512, policy="cache_affinity")
