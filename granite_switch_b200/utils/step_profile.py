@@ -1,7 +1,7 @@
 """Per-op device time of one representative engine step (CUDA events, no profiler).
 
 ``python -m granite_switch_b200.utils.step_profile [--preset granite-8b] [--prefill 4096 4096]
-[--decode 120 --decode-ctx 4400]``; under torchrun (one process per GPU) it
+[--prefill-ctx 0] [--decode 120 --decode-ctx 4400]``; under torchrun (one process per GPU) it
 runs the tensor-parallel model, with the fused NVSwitch collectives unless
 ``--no-fused-comm``.
 
@@ -53,8 +53,10 @@ class StepProfiler:
         return dict(out)
 
 
-def build_step(engine, prefill: list[int], decode: int, decode_ctx: int, vocab: int, seed: int = 0):
-    """Scheduler output with ``prefill`` chunks and ``decode`` single-token rows."""
+def build_step(engine, prefill: list[int], decode: int, decode_ctx: int, vocab: int, seed: int = 0,
+               prefill_ctx: int = 0):
+    """Scheduler output with ``prefill`` chunks (each after ``prefill_ctx`` cached tokens)
+    and ``decode`` single-token rows."""
     from ..engine.request import Request, SamplingParams
     from ..engine.scheduler import ScheduledChunk, SchedulerOutput
 
@@ -62,9 +64,10 @@ def build_step(engine, prefill: list[int], decode: int, decode_ctx: int, vocab: 
     bm = engine.blocks
     out = SchedulerOutput()
     for n in prefill:
-        r = Request(torch.randint(0, vocab, (n,), generator=g).tolist(), SamplingParams(max_tokens=8))
-        assert bm.allocate(r, n)
-        out.chunks.append(ScheduledChunk(r, 0, n))
+        r = Request(torch.randint(0, vocab, (prefill_ctx + n,), generator=g).tolist(), SamplingParams(max_tokens=8))
+        assert bm.allocate(r, prefill_ctx + n)
+        r.num_computed = prefill_ctx
+        out.chunks.append(ScheduledChunk(r, prefill_ctx, n))
     for _ in range(decode):
         r = Request(torch.randint(0, vocab, (decode_ctx,), generator=g).tolist(), SamplingParams(max_tokens=8))
         r.output_ids.append(1)
@@ -81,6 +84,7 @@ def main():
     p.add_argument("--prefill", type=int, nargs="*", default=[4096, 3968])
     p.add_argument("--decode", type=int, default=128)
     p.add_argument("--decode-ctx", type=int, default=4400)
+    p.add_argument("--prefill-ctx", type=int, default=0, help="cached tokens before each prefill chunk")
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--no-fused-comm", dest="fused", action="store_false")
@@ -112,14 +116,16 @@ def main():
     bargs = argparse.Namespace(preset=args.preset, layers=args.layers)
     config, base = bench.model_config(bargs)
     tokens = sum(args.prefill) + args.decode
-    need_blocks = sum((n + 15) // 16 for n in args.prefill) + args.decode * ((args.decode_ctx + 16) // 16) + 64
+    need_blocks = (sum((args.prefill_ctx + n + 15) // 16 for n in args.prefill)
+                   + args.decode * ((args.decode_ctx + 16) // 16) + 64)
     ecfg = EngineConfig(max_num_seqs=max(8, len(args.prefill) + args.decode), max_num_batched_tokens=tokens,
-                        max_model_len=max(args.prefill + [args.decode_ctx + 1]) + 16, tensor_parallel_size=world,
+                        max_model_len=max([args.prefill_ctx + n for n in args.prefill] + [args.decode_ctx + 1]) + 16,
+                        tensor_parallel_size=world,
                         num_kv_blocks=need_blocks, fused_tp_comm=args.fused)
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
               random_init=dict(lora_modules=tuple(args.lora), rank=32), tp_rank=rank, tp_group=group)
     eng = llm.engine
-    out = build_step(eng, args.prefill, args.decode, args.decode_ctx, base["vocab_size"])
+    out = build_step(eng, args.prefill, args.decode, args.decode_ctx, base["vocab_size"], prefill_ctx=args.prefill_ctx)
     ex = eng.executor
     model = llm.model
     for _ in range(args.warmup):
@@ -173,7 +179,8 @@ def main():
     if rank == 0:
         table = {k: dict(ms=round(v, 3), share=round(v / step_ms, 3)) for k, v in sorted(ops.items(), key=lambda kv: -kv[1])}
         print(json.dumps(dict(preset=args.preset, tp=world, fused_comm=bool(getattr(model, "comm", None)),
-                              tokens=tokens, prefill=args.prefill, decode=args.decode, decode_ctx=args.decode_ctx,
+                              tokens=tokens, prefill=args.prefill, prefill_ctx=args.prefill_ctx,
+                              decode=args.decode, decode_ctx=args.decode_ctx,
                               step_ms=round(plain, 3), step_ms_with_regions=round(step_ms, 3),
                               host_enqueue_ms=round(host_ms, 3), ops=table)), flush=True)
     if group is not None:
