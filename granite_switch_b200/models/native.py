@@ -660,7 +660,11 @@ class NativeGraniteSwitch:
         pre = [i for i, ql in enumerate(q_lens) if ql * g > 16]
         plans = []
         tc = self.head_dim in (64, 128) and self.use_tc_attention
-        pre_rows = A.tc_rows_for([q_lens[i] for i in pre], [kv_lens[i] for i in pre]) if tc and pre else 64
+        pre_q, pre_kv = [q_lens[i] for i in pre], [kv_lens[i] for i in pre]
+        # short chunks over long cached prefixes: split-KV layout (needs the split workspace)
+        pre_split = (A.split_prefill(pre_q, pre_kv, g, self.num_kv)
+                     if tc and pre and sum(q_lens) <= self.ws_tokens else 0)
+        pre_rows = 64 if pre_split or not (tc and pre) else A.tc_rows_for(pre_q, pre_kv)
         for idx, rows in ((dec, 16), (pre, pre_rows)):
             if not idx:
                 continue
@@ -669,7 +673,7 @@ class NativeGraniteSwitch:
             ws = [idx[t] for t in sw]
             n_ctas = len(ws) * self.num_kv
             max_kv = max(kv_lens[i] for i in idx)
-            ns = A.choose_splits(n_ctas, max_kv) if rows == 16 else 1
+            ns = A.choose_splits(n_ctas, max_kv) if rows == 16 else (pre_split or 1)
             tot = sum(q_lens)
             if ns > 1 and tot > self.ws_tokens:
                 ns = 1

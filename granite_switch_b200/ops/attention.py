@@ -32,6 +32,27 @@ def tc_rows_for(q_lens: list[int], kv_lens: list[int]) -> int:
     return 256 if total and 2 * long_fresh >= total else 128
 
 
+def split_prefill(q_lens: list[int], kv_lens: list[int], group: int, num_kv_heads: int,
+                  min_kv: int = 1024) -> int:
+    """Key-range splits for a step's prefill chunks, or 0 to keep the tcgen05 layout.
+
+    Short chunks after long cached prefixes (the next call of a conversation:
+    tens of new tokens over thousands of cached keys) give the tcgen05 kernel
+    a few 128-row tiles that each stream the whole prefix, leaving most SMs
+    idle: measured on B200 (8B shape, two 48-token chunks over 4.5k keys) at
+    95 us per layer, ~0.4 TB/s of K/V. When the tcgen05 grid would have fewer
+    CTAs than SMs and the longest context is at least ``min_kv`` keys, the
+    chunks take the 64-row split-KV layout of the paged kernel instead, with
+    the key range split as for decode (``choose_splits``).
+    """
+    if not q_lens or max(kv_lens) < min_kv:
+        return 0
+    if sum(-(-q * group // 128) for q in q_lens) * num_kv_heads >= NUM_SMS:
+        return 0
+    ns = choose_splits(sum(-(-q * group // 64) for q in q_lens) * num_kv_heads, max(kv_lens))
+    return ns if ns > 1 else 0
+
+
 def build_work(q_lens: list[int], group: int, rows_per_tile: int,
                kv_lens: list[int] | None = None) -> tuple[list[int], list[int]]:
     """(request, first row) per CTA tile; a request contributes ceil(q_len*G / rows) tiles.

@@ -146,7 +146,7 @@ def _make_cache(lens, hkv, d, seed=0):
 
 
 @pytest.mark.parametrize("d", [64, 128])
-@pytest.mark.parametrize("mode", ["prefill", "prefill128", "decode", "decode2"])
+@pytest.mark.parametrize("mode", ["prefill", "prefill128", "decode", "decode2", "short_after_long"])
 @pytest.mark.parametrize("nsplit", [1, 3])
 def test_paged_attention(d, mode, nsplit):
     from granite_switch_b200._native import native
@@ -161,6 +161,11 @@ def test_paged_attention(d, mode, nsplit):
         q_lens = [1, 1, 2, 1, 4]
         kv_lens = [1, 37, 300, 1025, 64]
         rows = 16
+    elif mode == "short_after_long":  # a conversation's next call: split-KV prefill layout
+        q_lens = [48, 40, 17]
+        kv_lens = [4548, 2100, 1040]
+        rows = 64
+        nsplit = 4 if nsplit > 1 else 1
     else:
         q_lens = [5, 64, 130, 1, 40]
         kv_lens = [5, 200, 130, 77, 1000]
