@@ -403,24 +403,47 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
   }
 }
 
-// Merge flash-decoding partials: out = sum_s 2^(lse_s - M) o_s / sum_s 2^(lse_s - M).
+// Merge flash-decoding partials: out = sum_s 2^(lse_s - M) o_s / sum_s 2^(lse_s - M),
+// for the (token, head) rows owned by this call's work tiles only. The plans of
+// one engine step (decode rows, prefill chunks) write disjoint rows of the same
+// output and share the split workspaces, so a merge must leave every other
+// row untouched. Block (tile w, KV head); one thread per column.
 template <int D>
 __global__ void attn_merge_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, int nsplit,
-                                  int T, int Hq, __nv_bfloat16* __restrict__ out, int64_t out_stride) {
-  const int tok = blockIdx.x, head = blockIdx.y;
-  float m = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) m = fmaxf(m, ws_lse[((int64_t)s * T + tok) * Hq + head]);
-  for (int col = threadIdx.x; col < D; col += blockDim.x) {
-    float acc = 0.f, den = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float l = ws_lse[((int64_t)s * T + tok) * Hq + head];
-      if (l == -INFINITY) continue;
-      const float wgt = exp2f(l - m);
-      acc += wgt * ws_o[(((int64_t)s * T + tok) * Hq + head) * D + col];
-      den += wgt;
+                                  int T, int Hq, int Hkv, const int32_t* __restrict__ q_start,
+                                  const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0,
+                                  int rows_per_tile, __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+  const int w = blockIdx.x, kvh = blockIdx.y;
+  const int G = Hq / Hkv;
+  const int seq = work_seq[w], row0 = work_row0[w];
+  const int qs = q_start[seq];
+  const int r_end = min(row0 + rows_per_tile, (q_start[seq + 1] - qs) * G);
+  for (int gr = row0; gr < r_end; ++gr) {
+    const int tok = qs + gr / G, head = kvh * G + gr % G;
+    if (tok >= T) break;
+    float m = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) m = fmaxf(m, ws_lse[((int64_t)s * T + tok) * Hq + head]);
+    for (int col = threadIdx.x; col < D; col += blockDim.x) {
+      float acc = 0.f, den = 0.f;
+      for (int s = 0; s < nsplit; ++s) {
+        const float l = ws_lse[((int64_t)s * T + tok) * Hq + head];
+        if (l == -INFINITY) continue;
+        const float wgt = exp2f(l - m);
+        acc += wgt * ws_o[(((int64_t)s * T + tok) * Hq + head) * D + col];
+        den += wgt;
+      }
+      out[(int64_t)tok * out_stride + head * D + col] = f2bf(den > 0.f ? acc / den : 0.f);
     }
-    out[(int64_t)tok * out_stride + head * D + col] = f2bf(den > 0.f ? acc / den : 0.f);
   }
+}
+
+template <int D>
+static void launch_merge(int n_work, int Hkv, cudaStream_t st, const float* wso, const float* wsl, int nsplit, int T,
+                         int Hq, const int32_t* q_start, const int32_t* work_seq, const int32_t* work_row0,
+                         int rows_per_tile, void* out, int64_t out_stride) {
+  attn_merge_kernel<D><<<dim3(n_work, Hkv), D, 0, st>>>(wso, wsl, nsplit, T, Hq, Hkv, q_start, work_seq, work_row0,
+                                                        rows_per_tile, reinterpret_cast<__nv_bfloat16*>(out),
+                                                        out_stride);
 }
 
 }  // namespace gsb
@@ -524,13 +547,9 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
   }
 #undef GSB_ATTN
   if (nsplit > 1) {
-    dim3 g2(T, Hq);
-    if (D == 128)
-      attn_merge_kernel<128><<<g2, 128, 0, st>>>(wso, wsl, (int)nsplit, T, Hq,
-                                                 reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0));
-    else
-      attn_merge_kernel<64><<<g2, 64, 0, st>>>(wso, wsl, (int)nsplit, T, Hq,
-                                               reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0));
+    auto merge = (D == 128) ? launch_merge<128> : launch_merge<64>;
+    merge(n_work, Hkv, st, wso, wsl, (int)nsplit, T, Hq, q_start.data_ptr<int32_t>(), work_seq.data_ptr<int32_t>(),
+          work_row0.data_ptr<int32_t>(), (int)rows_per_tile, out.data_ptr(), out.stride(0));
     GSB_CUDA_CHECK(cudaGetLastError());
   }
 }
@@ -618,8 +637,7 @@ static void launch_decode(dim3 grid, cudaStream_t st, const CUtensorMap& tk, con
       work_seq, work_row0, Hq, Hkv, scale_log2, reinterpret_cast<__nv_bfloat16*>(out), out_stride, wso, wsl, nsplit,
       T, err);
   if (nsplit > 1)
-    attn_merge_kernel<D><<<dim3(T, Hq), D, 0, st>>>(wso, wsl, nsplit, T, Hq, reinterpret_cast<__nv_bfloat16*>(out),
-                                                    out_stride);
+    launch_merge<D>((int)grid.x, Hkv, st, wso, wsl, nsplit, T, Hq, q_start, work_seq, work_row0, 16, out, out_stride);
 }
 
 }  // namespace noalloc

@@ -192,6 +192,42 @@ def test_paged_attention(d, mode, nsplit):
     _check()
 
 
+@pytest.mark.parametrize("dec_split", [1, 3])
+def test_step_plans_share_output_and_workspace(dec_split):
+    """The two attention plans of one engine step (decode rows, then short prefill chunks over
+    long cached prefixes with split keys) write disjoint rows of one output and share the split
+    workspaces: each split merge must touch only its own plan's rows."""
+    from granite_switch_b200.ops import attention as A
+
+    hq, hkv, d = 8, 2, 128
+    g = hq // hkv
+    q_lens = [1, 1, 48, 2, 40]
+    kv_lens = [300, 2100, 4548, 700, 1500]
+    kc, vc, bt = _make_cache(kv_lens, hkv, d, seed=5)
+    T = sum(q_lens)
+    q = torch.randn(T, (hq + 2 * hkv) * d, device="cuda").bfloat16()
+    out = torch.zeros(T, hq * d, device="cuda").bfloat16()
+    qs = [0]
+    for n in q_lens:
+        qs.append(qs[-1] + n)
+    dev = "cuda"
+    # unwritten workspace entries read as NaN
+    ws_o = torch.full((4 * T * hq * d,), float("nan"), device=dev)
+    ws_l = torch.full((4 * T * hq,), float("nan"), device=dev)
+    dec = [i for i, n in enumerate(q_lens) if n * g <= 16]
+    pre = [i for i, n in enumerate(q_lens) if n * g > 16]
+    for idx, rows, ns in ((dec, 16, dec_split), (pre, 64, 4)):
+        sw, wr = A.build_work([q_lens[i] for i in idx], g, rows)
+        A.paged_attention(q, kc, vc, bt, torch.tensor(qs, dtype=torch.int32, device=dev),
+                          torch.tensor(kv_lens, dtype=torch.int32, device=dev),
+                          torch.tensor([idx[t] for t in sw], dtype=torch.int32, device=dev),
+                          torch.tensor(wr, dtype=torch.int32, device=dev), rows, hq, 0.125, out, ns, ws_o, ws_l)
+    ref = A.paged_attention_reference(q, kc, vc, bt, q_lens, kv_lens, hq, 0.125)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 3e-2, err
+    _check()
+
+
 @pytest.mark.parametrize("rows", [128, 256])
 @pytest.mark.parametrize("packed", [0, 1])
 @pytest.mark.parametrize("d", [64, 128])
