@@ -407,43 +407,53 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
 // for the (token, head) rows owned by this call's work tiles only. The plans of
 // one engine step (decode rows, prefill chunks) write disjoint rows of the same
 // output and share the split workspaces, so a merge must leave every other
-// row untouched. Block (tile w, KV head); one thread per column.
+// row untouched. Block (tile w, KV head, group of 8 tile rows); one warp per
+// row, each lane D/32 columns (coalesced 128-byte reads of every split).
 template <int D>
-__global__ void attn_merge_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_lse, int nsplit,
-                                  int T, int Hq, int Hkv, const int32_t* __restrict__ q_start,
-                                  const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0,
-                                  int rows_per_tile, __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+__global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict__ ws_o,
+                                                         const float* __restrict__ ws_lse, int nsplit, int T, int Hq,
+                                                         int Hkv, const int32_t* __restrict__ q_start,
+                                                         const int32_t* __restrict__ work_seq,
+                                                         const int32_t* __restrict__ work_row0, int rows_per_tile,
+                                                         __nv_bfloat16* __restrict__ out, int64_t out_stride) {
   const int w = blockIdx.x, kvh = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.z * 8 + warp;
   const int G = Hq / Hkv;
   const int seq = work_seq[w], row0 = work_row0[w];
   const int qs = q_start[seq];
-  const int r_end = min(row0 + rows_per_tile, (q_start[seq + 1] - qs) * G);
-  for (int gr = row0; gr < r_end; ++gr) {
-    const int tok = qs + gr / G, head = kvh * G + gr % G;
-    if (tok >= T) break;
-    float m = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) m = fmaxf(m, ws_lse[((int64_t)s * T + tok) * Hq + head]);
-    for (int col = threadIdx.x; col < D; col += blockDim.x) {
-      float acc = 0.f, den = 0.f;
-      for (int s = 0; s < nsplit; ++s) {
-        const float l = ws_lse[((int64_t)s * T + tok) * Hq + head];
-        if (l == -INFINITY) continue;
-        const float wgt = exp2f(l - m);
-        acc += wgt * ws_o[(((int64_t)s * T + tok) * Hq + head) * D + col];
-        den += wgt;
-      }
-      out[(int64_t)tok * out_stride + head * D + col] = f2bf(den > 0.f ? acc / den : 0.f);
-    }
+  const int gr = row0 + r;
+  if (r >= rows_per_tile || gr >= (q_start[seq + 1] - qs) * G) return;
+  const int tok = qs + gr / G, head = kvh * G + gr % G;
+  if (tok >= T) return;
+  const int64_t row = (int64_t)tok * Hq + head, split_stride = (int64_t)T * Hq;
+  float m = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) m = fmaxf(m, ws_lse[s * split_stride + row]);
+  float acc[D / 32];
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) acc[c] = 0.f;
+  float den = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float l = ws_lse[s * split_stride + row];
+    if (l == -INFINITY) continue;
+    const float wgt = exp2f(l - m);
+    const float* o = ws_o + (s * split_stride + row) * D;
+#pragma unroll
+    for (int c = 0; c < D / 32; ++c) acc[c] += wgt * o[lane + 32 * c];
+    den += wgt;
   }
+  __nv_bfloat16* op = out + (int64_t)tok * out_stride + head * D;
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) op[lane + 32 * c] = f2bf(den > 0.f ? acc[c] / den : 0.f);
 }
 
 template <int D>
 static void launch_merge(int n_work, int Hkv, cudaStream_t st, const float* wso, const float* wsl, int nsplit, int T,
                          int Hq, const int32_t* q_start, const int32_t* work_seq, const int32_t* work_row0,
                          int rows_per_tile, void* out, int64_t out_stride) {
-  attn_merge_kernel<D><<<dim3(n_work, Hkv), D, 0, st>>>(wso, wsl, nsplit, T, Hq, Hkv, q_start, work_seq, work_row0,
-                                                        rows_per_tile, reinterpret_cast<__nv_bfloat16*>(out),
-                                                        out_stride);
+  attn_merge_kernel<D><<<dim3(n_work, Hkv, (rows_per_tile + 7) / 8), 256, 0, st>>>(
+      wso, wsl, nsplit, T, Hq, Hkv, q_start, work_seq, work_row0, rows_per_tile, reinterpret_cast<__nv_bfloat16*>(out),
+      out_stride);
 }
 
 }  // namespace gsb
