@@ -456,6 +456,13 @@ static void launch_merge(int n_work, int Hkv, cudaStream_t st, const float* wso,
       out_stride);
 }
 
+void launch_attn_merge(int D, int n_work, int Hkv, cudaStream_t st, const float* wso, const float* wsl, int nsplit,
+                       int T, int Hq, const int32_t* q_start, const int32_t* work_seq, const int32_t* work_row0,
+                       int rows_per_tile, void* out, int64_t out_stride) {
+  auto merge = (D == 128) ? launch_merge<128> : launch_merge<64>;
+  merge(n_work, Hkv, st, wso, wsl, nsplit, T, Hq, q_start, work_seq, work_row0, rows_per_tile, out, out_stride);
+}
+
 }  // namespace gsb
 
 using namespace gsb;

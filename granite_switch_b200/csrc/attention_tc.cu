@@ -63,6 +63,7 @@ __global__ void __launch_bounds__(192, 2)
                              const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
                              const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0, int Hq,
                              int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out, int64_t out_stride,
+                             float* __restrict__ ws_o, float* __restrict__ ws_lse, int nsplit, int T,
                              uint32_t* err) {
   using C = FaCfg<D, KT_>;
   constexpr int KT = C::KT, BM = C::BM, PAGE = C::PAGE;
@@ -95,8 +96,14 @@ __global__ void __launch_bounds__(192, 2)
   const int n_rows = q_len * G;
   const int32_t* bt = block_table + (int64_t)seq * bt_stride;
   const int last_row = min(row0 + BM, n_rows) - 1;
-  const int k_end = max(0, min(kv_len, ctx + last_row / G + 1));
-  const int n_tiles = (k_end + KT - 1) / KT;
+  // keys [k_begin, k_end): split blockIdx.z of the tile's causal key range,
+  // whole 64-key tiles per split (nsplit 1: the whole range)
+  const int split = blockIdx.z;
+  const int k_limit = max(0, min(kv_len, ctx + last_row / G + 1));
+  const int per_split = ((k_limit + nsplit - 1) / nsplit + KT - 1) / KT * KT;
+  const int k_begin = min(k_limit, split * per_split);
+  const int k_end = min(k_limit, k_begin + per_split);
+  const int n_tiles = (k_end - k_begin + KT - 1) / KT;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
@@ -119,8 +126,10 @@ __global__ void __launch_bounds__(192, 2)
   }
   // page ids of the key range into shared memory: the producer then issues each
   // tile's boxes without a dependent global read per page
-  const int n_pages = min((k_end + PAGE - 1) / PAGE, C::PT_CAP);
-  for (int i = threadIdx.x; i < n_pages; i += blockDim.x) s_pages[i] = checked_index(bt[i], num_blocks, err, kSiteTcPage);
+  const int pg0 = k_begin / PAGE;
+  const int n_pages = max(0, min((k_end + PAGE - 1) / PAGE - pg0, C::PT_CAP));
+  for (int i = threadIdx.x; i < n_pages; i += blockDim.x)
+    s_pages[i] = checked_index(bt[pg0 + i], num_blocks, err, kSiteTcPage);
   for (int c = threadIdx.x; c < BM * (D / 8); c += blockDim.x) {
     const int r = c / (D / 8), ch = c % (D / 8);
     const int gr = row0 + r;
@@ -149,9 +158,9 @@ __global__ void __launch_bounds__(192, 2)
         mbar_arrive_expect_tx(bar, C::KV_BYTES);
 #pragma unroll
         for (int p = 0; p < KT / PAGE; ++p) {
-          const int key = j * KT + p * PAGE;
-          const int pi = key / PAGE;
-          const int page = (key < k_end) ? (pi < n_pages ? s_pages[pi] : checked_index(bt[pi], num_blocks, err,
+          const int key = k_begin + j * KT + p * PAGE;
+          const int pi = key / PAGE - pg0;
+          const int page = (key < k_end) ? (pi < n_pages ? s_pages[pi] : checked_index(bt[pg0 + pi], num_blocks, err,
                                                                                       kSiteTcPage))
                                          : first_page;
           const int row = (page * Hkv + kvh) * PAGE;
@@ -262,7 +271,7 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
       for (int c = 0; c < KT / 32; ++c) tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t(&)[32]>(sv[c * 32]));
       tmem_wait_ld();
-      const int kbase = j * KT;
+      const int kbase = k_begin + j * KT;
       if (__any_sync(0xffffffffu, kbase + KT - 1 > pos || kbase + KT > k_end)) {
 #pragma unroll
         for (int i = 0; i < KT; ++i) {
@@ -345,12 +354,24 @@ __global__ void __launch_bounds__(192, 2)
         const int head = kvh * G + (valid ? gr % G : 0);
         __nv_bfloat16* op = out + (int64_t)tok * out_stride + head * D;
         const uint32_t tO = tmem + lane_base + C::O_COL;
+        // split partial: normalised fp32 O and the row's log2-sum-exp, merged
+        // afterwards (m lags the row maximum by at most 2^8, l matches it)
+        const int64_t ws_row = ((int64_t)split * T + tok) * Hq + head;
+        if (nsplit > 1 && valid) ws_lse[ws_row] = (l > 0.f) ? m + log2f(l) : -INFINITY;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t rr[32];
           tmem_ld32(tO + c * 32, rr);
           tmem_wait_ld();
-          if (valid) {
+          if (nsplit > 1) {
+            if (valid) {
+              float4* w4 = reinterpret_cast<float4*>(ws_o + ws_row * D + c * 32);
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                w4[e] = make_float4(__uint_as_float(rr[4 * e]) * inv, __uint_as_float(rr[4 * e + 1]) * inv,
+                                    __uint_as_float(rr[4 * e + 2]) * inv, __uint_as_float(rr[4 * e + 3]) * inv);
+            }
+          } else if (valid) {
             uint4* o4 = reinterpret_cast<uint4*>(op + c * 32);
 #pragma unroll
             for (int e = 0; e < 4; ++e)
@@ -364,8 +385,12 @@ __global__ void __launch_bounds__(192, 2)
         *abort_flag = 1;
       }
     } else if (n_tiles == 0 && gr < n_rows) {
-      __nv_bfloat16* op = out + (int64_t)(qs + gr / G) * out_stride + (kvh * G + gr % G) * D;
-      for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(op + c) = make_uint4(0, 0, 0, 0);
+      if (nsplit > 1) {
+        ws_lse[((int64_t)split * T + qs + gr / G) * Hq + kvh * G + gr % G] = -INFINITY;  // empty split
+      } else {
+        __nv_bfloat16* op = out + (int64_t)(qs + gr / G) * out_stride + (kvh * G + gr % G) * D;
+        for (int c = 0; c < D; c += 8) *reinterpret_cast<uint4*>(op + c) = make_uint4(0, 0, 0, 0);
+      }
     }
     if (!ok) *abort_flag = 1;
   }
@@ -744,11 +769,15 @@ int64_t gsb_attn_packed(int64_t v) {
   return old;
 }
 
-// Same metadata contract as gsb_paged_attention (rows_per_tile = 128), no key split.
+// Same metadata contract as gsb_paged_attention (rows_per_tile = 128 or 256).
+// nsplit > 1 (128-row tiles only) splits each tile's key range over CTAs, as the
+// paged kernel's flash-decoding split, with the same workspaces and merge.
 void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                               const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
                               const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t num_q_heads,
-                              double scale, const at::Tensor& out, const at::Tensor& err, int64_t rows_per_tile) {
+                              double scale, const at::Tensor& out, const at::Tensor& err, int64_t rows_per_tile,
+                              int64_t nsplit, const c10::optional<at::Tensor>& ws_o,
+                              const c10::optional<at::Tensor>& ws_lse) {
   GSB_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16 &&
                 out.scalar_type() == at::kBFloat16,
             "attention_tc: bf16 tensors required");
@@ -769,6 +798,20 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
   CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   GSB_CHECK(n_work < 65536, "attention_tc: too many work tiles");
   GSB_CHECK(rows_per_tile == 128 || rows_per_tile == 256, "attention_tc: rows_per_tile must be 128 or 256");
+  GSB_CHECK(nsplit >= 1 && nsplit <= 64 && (nsplit == 1 || rows_per_tile == 128),
+            "attention_tc: nsplit must be in [1, 64], and 1 with 256-row tiles");
+  const int T = (int)q.size(0);
+  float* wso = nullptr;
+  float* wsl = nullptr;
+  if (nsplit > 1) {
+    GSB_CHECK(ws_o.has_value() && ws_lse.has_value() && ws_o->scalar_type() == at::kFloat &&
+                  ws_lse->scalar_type() == at::kFloat && ws_o->is_contiguous() && ws_lse->is_contiguous(),
+              "attention_tc: contiguous fp32 workspaces required for nsplit > 1");
+    GSB_CHECK(ws_o->numel() >= nsplit * (int64_t)T * Hq * D && ws_lse->numel() >= nsplit * (int64_t)T * Hq,
+              "attention_tc: workspaces too small");
+    wso = ws_o->data_ptr<float>();
+    wsl = ws_lse->data_ptr<float>();
+  }
   dim3 grid(Hkv, n_work);
   const bool packed = g_attn_packed != 0;
   if (rows_per_tile == 256) {
@@ -800,12 +843,16 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
     GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[variant] = true;
   }
-  kfn<<<grid, 192, smem, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
-                                  block_table.data_ptr<int32_t>(), (int)block_table.stride(0), (int)k_cache.size(0),
-                                  q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
-                                  work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv,
-                                  (float)(scale * 1.4426950408889634),
-                                  reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
-                                  reinterpret_cast<uint32_t*>(err.data_ptr()));
+  kfn<<<dim3(Hkv, n_work, (unsigned)nsplit), 192, smem, st>>>(
+      tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), block_table.data_ptr<int32_t>(),
+      (int)block_table.stride(0), (int)k_cache.size(0), q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
+      work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv, (float)(scale * 1.4426950408889634),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), wso, wsl, (int)nsplit, T,
+      reinterpret_cast<uint32_t*>(err.data_ptr()));
   GSB_CUDA_CHECK(cudaGetLastError());
+  if (nsplit > 1) {
+    launch_attn_merge(D, n_work, Hkv, st, wso, wsl, (int)nsplit, T, Hq, q_start.data_ptr<int32_t>(),
+                      work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), 128, out.data_ptr(), out.stride(0));
+    GSB_CUDA_CHECK(cudaGetLastError());
+  }
 }

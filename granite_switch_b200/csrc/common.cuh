@@ -435,4 +435,10 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int M, int N) {
   return umma_idesc_bf16(M, N) | (1u << 16);
 }
 
+// Merge of split-KV attention partials (attention.cu) for the rows of the given
+// work tiles: ws_o [nsplit][T][Hq][D] normalised fp32, ws_lse [nsplit][T][Hq] log2.
+void launch_attn_merge(int D, int n_work, int Hkv, cudaStream_t st, const float* wso, const float* wsl, int nsplit,
+                       int T, int Hq, const int32_t* q_start, const int32_t* work_seq, const int32_t* work_row0,
+                       int rows_per_tile, void* out, int64_t out_stride);
+
 }  // namespace gsb

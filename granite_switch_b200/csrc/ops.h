@@ -45,7 +45,9 @@ void gsb_sample(const at::Tensor& logits, const at::Tensor& temperature, const a
 void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                               const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
                               const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t num_q_heads,
-                              double scale, const at::Tensor& out, const at::Tensor& err, int64_t rows_per_tile);
+                              double scale, const at::Tensor& out, const at::Tensor& err, int64_t rows_per_tile,
+                              int64_t nsplit, const c10::optional<at::Tensor>& ws_o,
+                              const c10::optional<at::Tensor>& ws_lse);
 void gsb_peer_barrier(const at::Tensor& pad_ptrs_dev, int64_t rank, int64_t tp, int64_t epoch, int64_t budget_ns,
                       const at::Tensor& err);
 void gsb_multimem_allreduce_bf16(int64_t mc_ptr, int64_t nbytes, int64_t rank, int64_t tp, const at::Tensor& like);

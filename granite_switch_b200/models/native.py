@@ -591,7 +591,8 @@ class NativeGraniteSwitch:
             if plan.rows in (128, 256):
                 with R("attn_prefill"):
                     A.prefill_attention_tc(q, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
-                                           plan.work_row0, self.num_q, scale, attn, plan.rows)
+                                           plan.work_row0, self.num_q, scale, attn, plan.rows, plan.nsplit,
+                                           self.ws_o, self.ws_lse)
             else:
                 with R("attn_decode" if plan.rows == 16 else "attn_prefill"):
                     A.paged_attention(q, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
@@ -664,7 +665,7 @@ class NativeGraniteSwitch:
         # short chunks over long cached prefixes: split-KV layout (needs the split workspace)
         pre_split = (A.split_prefill(pre_q, pre_kv, g, self.num_kv)
                      if tc and pre and sum(q_lens) <= self.ws_tokens else 0)
-        pre_rows = 64 if pre_split or not (tc and pre) else A.tc_rows_for(pre_q, pre_kv)
+        pre_rows = 128 if pre_split else (A.tc_rows_for(pre_q, pre_kv) if tc and pre else 64)
         for idx, rows in ((dec, 16), (pre, pre_rows)):
             if not idx:
                 continue

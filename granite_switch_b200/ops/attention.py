@@ -34,22 +34,22 @@ def tc_rows_for(q_lens: list[int], kv_lens: list[int]) -> int:
 
 def split_prefill(q_lens: list[int], kv_lens: list[int], group: int, num_kv_heads: int,
                   min_kv: int = 1024) -> int:
-    """Key-range splits for a step's prefill chunks, or 0 to keep the tcgen05 layout.
+    """Key-range splits for a step's tcgen05 prefill tiles (128 rows), or 0 for none.
 
     Short chunks after long cached prefixes (the next call of a conversation:
     tens of new tokens over thousands of cached keys) give the tcgen05 kernel
     a few 128-row tiles that each stream the whole prefix, leaving most SMs
     idle: measured on B200 (8B shape, two 48-token chunks over 4.5k keys) at
-    95 us per layer, ~0.4 TB/s of K/V. When the tcgen05 grid would have fewer
-    CTAs than SMs and the longest context is at least ``min_kv`` keys, the
-    chunks take the 64-row split-KV layout of the paged kernel instead, with
-    the key range split as for decode (``choose_splits``).
+    95 us per layer. When the grid would have fewer CTAs than SMs and the
+    longest context is at least ``min_kv`` keys, each tile's key range is
+    split over CTAs as for decode (``choose_splits``) and the partials merged.
     """
     if not q_lens or max(kv_lens) < min_kv:
         return 0
-    if sum(-(-q * group // 128) for q in q_lens) * num_kv_heads >= NUM_SMS:
+    n_ctas = sum(-(-q * group // 128) for q in q_lens) * num_kv_heads
+    if n_ctas >= NUM_SMS:
         return 0
-    ns = choose_splits(sum(-(-q * group // 64) for q in q_lens) * num_kv_heads, max(kv_lens))
+    ns = choose_splits(n_ctas, max(kv_lens))
     return ns if ns > 1 else 0
 
 
@@ -102,12 +102,16 @@ def paged_attention(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq,
 
 
 def prefill_attention_tc(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
-                         num_q_heads: int, scale: float, out, rows_per_tile: int = 128):
+                         num_q_heads: int, scale: float, out, rows_per_tile: int = 128, nsplit: int = 1,
+                         ws_o=None, ws_lse=None):
     """tcgen05 prefill attention; the work tiles must be built with the same ``rows_per_tile``:
     128 (one query tile per CTA, two CTAs per SM) or 256 (two query tiles per CTA sharing each
-    K/V tile, 128-key tiles, one CTA per SM)."""
+    K/V tile, 128-key tiles, one CTA per SM). ``nsplit > 1`` (128-row tiles) splits every
+    tile's key range over CTAs and merges the partials, with the fp32 workspaces of
+    :func:`paged_attention`; only the work tiles' own output rows are written."""
     native().prefill_attention_tc(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
-                                  num_q_heads, float(scale), out, err_buffer(q.device), int(rows_per_tile))
+                                  num_q_heads, float(scale), out, err_buffer(q.device), int(rows_per_tile),
+                                  int(nsplit), ws_o, ws_lse)
     return out
 
 

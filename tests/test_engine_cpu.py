@@ -206,24 +206,25 @@ def test_prefill_layout_choice():
 
 
 def test_short_chunks_over_long_prefix_split_kv():
-    """Short prefill chunks after long cached prefixes take the 64-row split-KV layout;
-    fresh or many chunks keep the tcgen05 layout."""
+    """Short prefill chunks after long cached prefixes split each tcgen05 tile's key range;
+    fresh or many chunks keep one CTA per tile."""
     import types
 
     from granite_switch_b200.models.native import NativeGraniteSwitch
     from granite_switch_b200.ops import attention as A
 
-    assert A.split_prefill([48, 48], [4548, 4548], 4, 8) == 4    # 48 CTAs of 64 rows -> 4 splits
-    assert A.split_prefill([4096], [4096], 4, 8) == 0            # 1024 tcgen05 CTAs
+    assert A.split_prefill([48, 48], [4548, 4548], 4, 8) == 5    # 32 CTAs of 128 rows -> 5 splits
+    assert A.split_prefill([4096], [4096], 4, 8) == 0            # 1024 CTAs
     assert A.split_prefill([48, 48], [300, 500], 4, 8) == 0      # short contexts
-    assert A.split_prefill([48, 48, 300], [4548, 4548, 300], 4, 8) == 0  # 200 CTAs without splits
+    assert A.split_prefill([48, 48, 300], [4548, 4548, 300], 4, 8) == 2  # 112 CTAs
+    assert A.split_prefill([300] * 3, [4548] * 3, 4, 8) == 0     # 240 CTAs
     m = types.SimpleNamespace(num_q=32, num_kv=8, head_dim=128, use_tc_attention=True, ws_tokens=512)
     q = [48, 48] + [1] * 126
     kv = [4548, 4548] + [4500] * 126
     plans = NativeGraniteSwitch.attention_plans(m, q, kv)
-    assert [(p[2], p[3]) for p in plans] == [(16, 1), (64, 4)]
-    assert sorted(set(plans[1][0])) == [0, 1] and len(plans[1][0]) == 6  # 3 tiles of 64 rows each
+    assert [(p[2], p[3]) for p in plans] == [(16, 1), (128, 5)]
+    assert sorted(plans[1][0]) == [0, 0, 1, 1]  # two 128-row tiles per chunk
     plans = NativeGraniteSwitch.attention_plans(m, [4096] + [1] * 127, [4096] + [4500] * 127)
     assert plans[1][2] == 256 and plans[1][3] == 1
-    m.ws_tokens = 128  # the split workspace cannot hold the step: tcgen05 layout
+    m.ws_tokens = 128  # the split workspace cannot hold the step: no split
     assert NativeGraniteSwitch.attention_plans(m, q, kv)[1][2:] == (128, 1)

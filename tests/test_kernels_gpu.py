@@ -192,8 +192,9 @@ def test_paged_attention(d, mode, nsplit):
     _check()
 
 
+@pytest.mark.parametrize("pre_rows", [64, 128])
 @pytest.mark.parametrize("dec_split", [1, 3])
-def test_step_plans_share_output_and_workspace(dec_split):
+def test_step_plans_share_output_and_workspace(dec_split, pre_rows):
     """The two attention plans of one engine step (decode rows, then short prefill chunks over
     long cached prefixes with split keys) write disjoint rows of one output and share the split
     workspaces: each split merge must touch only its own plan's rows."""
@@ -216,23 +217,27 @@ def test_step_plans_share_output_and_workspace(dec_split):
     ws_l = torch.full((4 * T * hq,), float("nan"), device=dev)
     dec = [i for i, n in enumerate(q_lens) if n * g <= 16]
     pre = [i for i, n in enumerate(q_lens) if n * g > 16]
-    for idx, rows, ns in ((dec, 16, dec_split), (pre, 64, 4)):
+    for idx, rows, ns in ((dec, 16, dec_split), (pre, pre_rows, 4)):
         sw, wr = A.build_work([q_lens[i] for i in idx], g, rows)
-        A.paged_attention(q, kc, vc, bt, torch.tensor(qs, dtype=torch.int32, device=dev),
-                          torch.tensor(kv_lens, dtype=torch.int32, device=dev),
-                          torch.tensor([idx[t] for t in sw], dtype=torch.int32, device=dev),
-                          torch.tensor(wr, dtype=torch.int32, device=dev), rows, hq, 0.125, out, ns, ws_o, ws_l)
+        args = (q, kc, vc, bt, torch.tensor(qs, dtype=torch.int32, device=dev),
+                torch.tensor(kv_lens, dtype=torch.int32, device=dev),
+                torch.tensor([idx[t] for t in sw], dtype=torch.int32, device=dev),
+                torch.tensor(wr, dtype=torch.int32, device=dev))
+        if rows == 128:  # tcgen05 prefill with split keys
+            A.prefill_attention_tc(*args, hq, 0.125, out, rows, ns, ws_o, ws_l)
+        else:
+            A.paged_attention(*args, rows, hq, 0.125, out, ns, ws_o, ws_l)
     ref = A.paged_attention_reference(q, kc, vc, bt, q_lens, kv_lens, hq, 0.125)
     err = (out.float() - ref).abs().max().item()
     assert err < 3e-2, err
     _check()
 
 
-@pytest.mark.parametrize("rows", [128, 256])
+@pytest.mark.parametrize("rows,nsplit", [(128, 1), (128, 3), (256, 1)])
 @pytest.mark.parametrize("packed", [0, 1])
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("case", ["fresh", "cached_prefix", "mixed"])
-def test_prefill_attention_tcgen05(case, d, packed, rows):
+def test_prefill_attention_tcgen05(case, d, packed, rows, nsplit):
     from granite_switch_b200._native import native
     from granite_switch_b200.ops import attention as A
 
@@ -255,10 +260,13 @@ def test_prefill_attention_tcgen05(case, d, packed, rows):
         qs.append(qs[-1] + l)
     ws, wr = A.build_work(q_lens, g, rows)
     dev = "cuda"
+    # key-split partials; unwritten workspace entries read as NaN
+    ws_o = torch.full((nsplit * T * hq * d,), float("nan"), device=dev)
+    ws_l = torch.full((nsplit * T * hq,), float("nan"), device=dev)
     A.prefill_attention_tc(q, kc, vc, bt, torch.tensor(qs, dtype=torch.int32, device=dev),
                            torch.tensor(kv_lens, dtype=torch.int32, device=dev),
                            torch.tensor(ws, dtype=torch.int32, device=dev),
-                           torch.tensor(wr, dtype=torch.int32, device=dev), hq, 0.088, out, rows)
+                           torch.tensor(wr, dtype=torch.int32, device=dev), hq, 0.088, out, rows, nsplit, ws_o, ws_l)
     native().attn_packed(old)
     ref = A.paged_attention_reference(q, kc, vc, bt, q_lens, kv_lens, hq, 0.088)
     err = (out.float() - ref).abs().max().item()
