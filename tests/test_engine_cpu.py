@@ -228,3 +228,14 @@ def test_short_chunks_over_long_prefix_split_kv():
     assert plans[1][2] == 256 and plans[1][3] == 1
     m.ws_tokens = 128  # the split workspace cannot hold the step: no split
     assert NativeGraniteSwitch.attention_plans(m, q, kv)[1][2:] == (128, 1)
+
+
+def test_pick_bn_policy():
+    """GEMM N-tile choice: widest filling tile for large M, 128 for two row tiles, narrowest
+    filling tile for one row tile and for the LoRA shrink."""
+    from granite_switch_b200.ops.gemm import pick_bn
+
+    assert pick_bn(8192, 6144) == 256
+    assert pick_bn(222, 6144) == 128 and pick_bn(222, 4096) == 128
+    assert pick_bn(100, 6144) == 64 and pick_bn(300, 4096) == 64
+    assert pick_bn(222, 384, (128, 64), two_tile_bn=None) == 64
