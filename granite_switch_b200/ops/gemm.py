@@ -36,8 +36,8 @@ def pick_bn(m: int, n: int, candidates=(256, 128, 64), two_tile_bn: int | None =
     ok = [bn for bn in candidates if n % bn == 0]
     if not ok:
         raise ValueError(f"N={n} is not a multiple of 64")
-    if m_tiles == 2 and two_tile_bn in ok:
-        return two_tile_bn
+    if m_tiles == 2 and two_tile_bn in ok and (n // two_tile_bn) * m_tiles >= 64:
+        return two_tile_bn  # as measured: at least 64 output tiles (split-K fills the rest)
     for bn in ok:
         if (n // bn) * m_tiles >= 148:
             return bn

@@ -239,3 +239,4 @@ def test_pick_bn_policy():
     assert pick_bn(222, 6144) == 128 and pick_bn(222, 4096) == 128
     assert pick_bn(100, 6144) == 64 and pick_bn(300, 4096) == 64
     assert pick_bn(222, 384, (128, 64), two_tile_bn=None) == 64
+    assert pick_bn(222, 768) == 64  # a tensor-parallel shard: too few 128-wide tiles
