@@ -27,46 +27,25 @@ class NativeExtensionMissing(RuntimeError):
     pass
 
 
-class _Counted:
-    """Proxy over the extension that counts op calls (one call = one or two kernel launches).
-
-    ``launch_count()`` lets benchmarks report how many native kernels ran in a
-    timed region.
-    """
-
-    def __init__(self, mod):
-        self._mod = mod
-        self._fns = {}
-
-    def __getattr__(self, name):
-        fn = self._fns.get(name)
-        if fn is None:
-            raw = getattr(self._mod, name)
-
-            def fn(*a, _raw=raw, **k):
-                global _LAUNCHES
-                _LAUNCHES += 1
-                return _raw(*a, **k)
-
-            self._fns[name] = fn
-        return fn
-
-
-_LAUNCHES = 0
+_REPLAYED = 0  # kernels run by CUDA-graph replays (the extension counts host launches)
 
 
 def launch_count() -> int:
-    return _LAUNCHES
+    """Kernels this extension launched so far: every launch it issued from the host
+    (counted in the extension, one per launch configuration, split-K reduces and
+    split-KV merges included) plus the kernels of CUDA-graph replays reported
+    through :func:`add_launches`. 0 before the extension is loaded."""
+    return (int(_C.kernel_launches()) if _C is not None else 0) + _REPLAYED
 
 
 def add_launches(n: int) -> None:
     """Account for ``n`` kernel launches issued by a CUDA-graph replay."""
-    global _LAUNCHES
-    _LAUNCHES += n
+    global _REPLAYED
+    _REPLAYED += n
 
 
 def native():
-    """Return the loaded extension (through the counting proxy), importing it on first use."""
+    """Return the loaded extension, importing it on first use."""
     global _C
     if _C is None:
         with _lock:
@@ -78,7 +57,7 @@ def native():
                         "granite_switch_b200._C is not built; run "
                         "`python setup.py build_ext --inplace` in the repository root"
                     ) from e
-                _C = _Counted(mod)
+                _C = mod
     return _C
 
 

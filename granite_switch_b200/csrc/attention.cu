@@ -451,7 +451,7 @@ template <int D>
 static void launch_merge(int n_work, int Hkv, cudaStream_t st, const float* wso, const float* wsl, int nsplit, int T,
                          int Hq, const int32_t* q_start, const int32_t* work_seq, const int32_t* work_row0,
                          int rows_per_tile, void* out, int64_t out_stride) {
-  attn_merge_kernel<D><<<dim3(n_work, Hkv, (rows_per_tile + 7) / 8), 256, 0, st>>>(
+  attn_merge_kernel<D><<<(::gsb::count_launch(), dim3(n_work, Hkv, (rows_per_tile + 7) / 8)), 256, 0, st>>>(
       wso, wsl, nsplit, T, Hq, Hkv, q_start, work_seq, work_row0, rows_per_tile, reinterpret_cast<__nv_bfloat16*>(out),
       out_stride);
 }
@@ -480,7 +480,7 @@ static void launch_attn(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const
     GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured = true;
   }
-  kfn<<<grid, C::THREADS, C::SMEM, st>>>(
+  kfn<<<(::gsb::count_launch(), grid), C::THREADS, C::SMEM, st>>>(
       tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), bt.data_ptr<int32_t>(),
       (int)bt.stride(0), num_blocks, q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
       work_seq.data_ptr<int32_t>(),
@@ -649,7 +649,7 @@ static void launch_decode(dim3 grid, cudaStream_t st, const CUtensorMap& tk, con
                           float scale_log2, void* out, int64_t out_stride, float* wso, float* wsl, int nsplit, int T,
                           uint32_t* err) {
   using C = AttnCfg<D, 1, 64, ST>;
-  paged_attn_kernel<D, 1, 64, ST><<<grid, C::THREADS, C::SMEM, st>>>(
+  paged_attn_kernel<D, 1, 64, ST><<<(::gsb::count_launch(), grid), C::THREADS, C::SMEM, st>>>(
       tk, tv, reinterpret_cast<const __nv_bfloat16*>(q), q_stride, bt, (int)bt_stride, num_blocks, q_start, kv_len,
       work_seq, work_row0, Hq, Hkv, scale_log2, reinterpret_cast<__nv_bfloat16*>(out), out_stride, wso, wsl, nsplit,
       T, err);
@@ -712,7 +712,7 @@ extern "C" int gsb_decode_attention_noalloc(const void* q, int64_t q_stride, con
     float* wsl = (nsplit > 1) ? scratch + lse_off : nullptr;
     if (nsplit > 1) {
       const int64_t n = (int64_t)nsplit * T * Hq;
-      fill_neg_inf_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 148), 256, 0, stream>>>(wsl, n);
+      fill_neg_inf_kernel<<<(::gsb::count_launch(), (unsigned)std::min<int64_t>((n + 255) / 256, 148)), 256, 0, stream>>>(wsl, n);
     }
     const float scale_log2 = (float)(scale * 1.4426950408889634);
     const dim3 grid(num_work, Hkv, nsplit);

@@ -824,7 +824,7 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
       GSB_CUDA_CHECK(cudaFuncSetAttribute(kp, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_p));
       configured_p[vp] = true;
     }
-    kp<<<grid, 320, smem_p, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
+    kp<<<(::gsb::count_launch(), grid), 320, smem_p, st>>>(tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
                                   block_table.data_ptr<int32_t>(), (int)block_table.stride(0), (int)k_cache.size(0),
                                   q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
                                   work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv,
@@ -843,7 +843,7 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
     GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured[variant] = true;
   }
-  kfn<<<dim3(Hkv, n_work, (unsigned)nsplit), 192, smem, st>>>(
+  kfn<<<(::gsb::count_launch(), dim3(Hkv, n_work, (unsigned)nsplit)), 192, smem, st>>>(
       tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), block_table.data_ptr<int32_t>(),
       (int)block_table.stride(0), (int)k_cache.size(0), q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
       work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv, (float)(scale * 1.4426950408889634),

@@ -6,7 +6,17 @@
 
 #include "ops.h"
 
+#include <atomic>
+
+namespace gsb {
+static std::atomic<int64_t> g_kernel_launches{0};
+void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace gsb
+
+static int64_t gsb_kernel_launches() { return gsb::g_kernel_launches.load(std::memory_order_relaxed); }
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("kernel_launches", &gsb_kernel_launches, "kernels launched by this extension since it was loaded");
   m.doc() = "granite_switch_b200 sm_100a kernels";
   m.def("switched_gemm", &gsb_switched_gemm, "tcgen05 GEMM with fused switched-LoRA expand");
   m.def("gemm_pair_min_m", &gsb_gemm_pair_min_m, "set the smallest M of the CTA-pair GEMM (returns the old value)");

@@ -167,7 +167,7 @@ void gsb_peer_barrier(const at::Tensor& pad_ptrs_dev, int64_t rank, int64_t tp, 
   GSB_CHECK(pad_ptrs_dev.is_cuda() && pad_ptrs_dev.numel() >= tp && tp >= 1 && tp <= 64, "barrier: bad pads");
   c10::cuda::CUDAGuard g(err.device());
   auto st = c10::cuda::getCurrentCUDAStream(err.device().index()).stream();
-  peer_barrier_kernel<<<1, 64, 0, st>>>(reinterpret_cast<const uint64_t*>(pad_ptrs_dev.data_ptr()), (int)rank,
+  peer_barrier_kernel<<<(::gsb::count_launch(), 1), 64, 0, st>>>(reinterpret_cast<const uint64_t*>(pad_ptrs_dev.data_ptr()), (int)rank,
                                         (int)tp, (uint32_t)epoch, (uint64_t)budget_ns,
                                         reinterpret_cast<uint32_t*>(err.data_ptr()));
   GSB_CUDA_CHECK(cudaGetLastError());
@@ -180,7 +180,7 @@ void gsb_multimem_allreduce_bf16(int64_t mc_ptr, int64_t nbytes, int64_t rank, i
   const int64_t n_vec = nbytes / 16;
   const int64_t per = (n_vec + tp - 1) / tp;
   const int blocks = (int)std::min<int64_t>(std::max<int64_t>(1, (per + 255) / 256), 132);
-  multimem_allreduce_bf16_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<uint8_t*>(mc_ptr), n_vec, (int)rank,
+  multimem_allreduce_bf16_kernel<<<(::gsb::count_launch(), blocks), 256, 0, st>>>(reinterpret_cast<uint8_t*>(mc_ptr), n_vec, (int)rank,
                                                           (int)tp);
   GSB_CUDA_CHECK(cudaGetLastError());
 }
@@ -196,7 +196,7 @@ void gsb_allreduce_ldreduce_p2p(int64_t mc_ptr, const at::Tensor& peer_ptrs, int
   const int64_t n_vec = nbytes / 16;
   const int64_t per = (n_vec + tp - 1) / tp;
   const int blocks = (int)std::min<int64_t>(std::max<int64_t>(1, (per + 255) / 256), 148);
-  allreduce_ldreduce_p2p_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<const uint8_t*>(mc_ptr),
+  allreduce_ldreduce_p2p_kernel<<<(::gsb::count_launch(), blocks), 256, 0, st>>>(reinterpret_cast<const uint8_t*>(mc_ptr),
                                                          reinterpret_cast<const uint64_t*>(peer_ptrs.data_ptr()),
                                                          offset, n_vec, (int)rank, (int)tp);
   GSB_CUDA_CHECK(cudaGetLastError());
@@ -217,8 +217,8 @@ void gsb_rmsnorm_residual_from(const at::Tensor& y, const at::Tensor& h, const a
   auto* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   auto* xp = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
   const int vpt = (H / 8 + 255) / 256;
-  if (vpt <= 1) rmsnorm_residual_from_kernel<1><<<T, 256, 0, st>>>(yp, hp, wp, xp, H, (float)eps);
-  else if (vpt <= 2) rmsnorm_residual_from_kernel<2><<<T, 256, 0, st>>>(yp, hp, wp, xp, H, (float)eps);
-  else rmsnorm_residual_from_kernel<4><<<T, 256, 0, st>>>(yp, hp, wp, xp, H, (float)eps);
+  if (vpt <= 1) rmsnorm_residual_from_kernel<1><<<(::gsb::count_launch(), T), 256, 0, st>>>(yp, hp, wp, xp, H, (float)eps);
+  else if (vpt <= 2) rmsnorm_residual_from_kernel<2><<<(::gsb::count_launch(), T), 256, 0, st>>>(yp, hp, wp, xp, H, (float)eps);
+  else rmsnorm_residual_from_kernel<4><<<(::gsb::count_launch(), T), 256, 0, st>>>(yp, hp, wp, xp, H, (float)eps);
   GSB_CUDA_CHECK(cudaGetLastError());
 }

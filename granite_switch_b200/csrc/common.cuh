@@ -435,6 +435,12 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int M, int N) {
   return umma_idesc_bf16(M, N) | (1u << 16);
 }
 
+// Host-side count of kernel launches issued by this extension (bindings.cpp):
+// every launch configuration evaluates it once, so benchmarks can report how
+// many of the extension's kernels a timed region launched (CUDA-graph captures
+// count once, at capture).
+void count_launch();
+
 // Merge of split-KV attention partials (attention.cu) for the rows of the given
 // work tiles: ws_o [nsplit][T][Hq][D] normalised fp32, ws_lse [nsplit][T][Hq] log2.
 void launch_attn_merge(int D, int n_work, int Hkv, cudaStream_t st, const float* wso, const float* wsl, int nsplit,

@@ -241,14 +241,14 @@ void gsb_rmsnorm(const at::Tensor& x, const at::Tensor& w, const at::Tensor& out
   auto* op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   auto st = cur_stream(x);
   if (vpt <= 1)
-    rmsnorm_kernel<1><<<n, threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
+    rmsnorm_kernel<1><<<(::gsb::count_launch(), n), threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
   else if (vpt <= 2)
-    rmsnorm_kernel<2><<<n, threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
+    rmsnorm_kernel<2><<<(::gsb::count_launch(), n), threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
   else if (vpt <= 4)
-    rmsnorm_kernel<4><<<n, threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
+    rmsnorm_kernel<4><<<(::gsb::count_launch(), n), threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
   else {
     GSB_CHECK(vpt <= 8, "rmsnorm: H too large");
-    rmsnorm_kernel<8><<<n, threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
+    rmsnorm_kernel<8><<<(::gsb::count_launch(), n), threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
   }
   GSB_CUDA_CHECK(cudaGetLastError());
 }
@@ -266,7 +266,7 @@ void gsb_embed(const at::Tensor& ids, const at::Tensor& table, const c10::option
   c10::cuda::CUDAGuard g(ids.device());
   const int64_t* lp = lut.has_value() ? lut->data_ptr<int64_t>() : nullptr;
   const int64_t ls = lut.has_value() ? lut->numel() : 0;
-  embed_kernel<<<T, 128, 0, cur_stream(ids)>>>(
+  embed_kernel<<<(::gsb::count_launch(), T), 128, 0, cur_stream(ids)>>>(
       ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), lp, ls,
       table.size(0), (float)mult, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H,
       reinterpret_cast<uint32_t*>(err.data_ptr()));
@@ -309,17 +309,17 @@ void gsb_rope_kv(const at::Tensor& qkv, const at::Tensor& positions, const at::T
   const int threads = 256;
   switch (head_dim) {
     case 64:
-      rope_kv_kernel<64><<<T, threads, 0, st>>>(qp, qkv.stride(0), positions.data_ptr<int64_t>(),
+      rope_kv_kernel<64><<<(::gsb::count_launch(), T), threads, 0, st>>>(qp, qkv.stride(0), positions.data_ptr<int64_t>(),
                                                 cos_sin.data_ptr<float>(), (int)cos_sin.size(0), kc, vc,
                                                 sp, (int)num_q_heads, (int)num_kv_heads, BS, num_slots, ep);
       break;
     case 128:
-      rope_kv_kernel<128><<<T, threads, 0, st>>>(qp, qkv.stride(0), positions.data_ptr<int64_t>(),
+      rope_kv_kernel<128><<<(::gsb::count_launch(), T), threads, 0, st>>>(qp, qkv.stride(0), positions.data_ptr<int64_t>(),
                                                  cos_sin.data_ptr<float>(), (int)cos_sin.size(0), kc, vc,
                                                  sp, (int)num_q_heads, (int)num_kv_heads, BS, num_slots, ep);
       break;
     case 16:
-      rope_kv_kernel<16><<<T, threads, 0, st>>>(qp, qkv.stride(0), positions.data_ptr<int64_t>(),
+      rope_kv_kernel<16><<<(::gsb::count_launch(), T), threads, 0, st>>>(qp, qkv.stride(0), positions.data_ptr<int64_t>(),
                                                 cos_sin.data_ptr<float>(), (int)cos_sin.size(0), kc, vc,
                                                 sp, (int)num_q_heads, (int)num_kv_heads, BS, num_slots, ep);
       break;
@@ -335,7 +335,7 @@ void gsb_argmax(const at::Tensor& logits, const at::Tensor& out) {
   const int B = (int)logits.size(0);
   if (B == 0) return;
   c10::cuda::CUDAGuard g(logits.device());
-  argmax_kernel<<<B, 512, 0, cur_stream(logits)>>>(logits.data_ptr<float>(), logits.stride(0),
+  argmax_kernel<<<(::gsb::count_launch(), B), 512, 0, cur_stream(logits)>>>(logits.data_ptr<float>(), logits.stride(0),
                                                    (int)logits.size(1), out.data_ptr<int64_t>());
   GSB_CUDA_CHECK(cudaGetLastError());
 }
@@ -362,7 +362,7 @@ void gsb_residual_axpy(const at::Tensor& h, const at::Tensor& y, double scale) {
   const int T = (int)h.size(0);
   if (T == 0) return;
   c10::cuda::CUDAGuard g(h.device());
-  residual_axpy_kernel<<<T, 256, 0, cur_stream(h)>>>(reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), h.stride(0),
+  residual_axpy_kernel<<<(::gsb::count_launch(), T), 256, 0, cur_stream(h)>>>(reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), h.stride(0),
                                                      reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
                                                      (int)h.size(1), (float)scale);
   GSB_CUDA_CHECK(cudaGetLastError());

@@ -917,7 +917,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   }
   const int tiles = (N / BN) * ((M + C::BM - 1) / C::BM) * (grp.ksplit > 1 ? grp.ksplit : 1);
   const int grid = std::min(tiles, num_sms_for_current_device());
-  kfn<<<grid, 192, C::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, err);
+  kfn<<<(::gsb::count_launch(), grid), 192, C::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, to, M, N, K, lora, epi, grp, err);
   GSB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -957,7 +957,7 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   const int clusters = pair_max_clusters<EPI, SPLIT>();  // also sets the shared-memory attribute
   const int tiles = (N / PairCfg::BN) * ((M + 255) / 256);
   const int grid = 2 * std::min(tiles, clusters);
-  kfn<<<grid, 192, PairCfg::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err);
+  kfn<<<(::gsb::count_launch(), grid), 192, PairCfg::SMEM_BYTES, stream>>>(ta, tb, ts, tlb, to, M, N, K, lora, epi, err);
   GSB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -1247,19 +1247,19 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     const __nv_bfloat16* rp = epi.residual;
     switch (epi_kind) {
       case kEpiStore:
-        splitk_reduce_kernel<kEpiStore><<<blocks, 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
+        splitk_reduce_kernel<kEpiStore><<<(::gsb::count_launch(), blocks), 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
                                                                    out.data_ptr(), out.stride(0), (int)bn);
         break;
       case kEpiResAdd:
-        splitk_reduce_kernel<kEpiResAdd><<<blocks, 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
+        splitk_reduce_kernel<kEpiResAdd><<<(::gsb::count_launch(), blocks), 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
                                                                     out.data_ptr(), out.stride(0), (int)bn);
         break;
       case kEpiSwiGLU:
-        splitk_reduce_kernel<kEpiSwiGLU><<<blocks, 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
+        splitk_reduce_kernel<kEpiSwiGLU><<<(::gsb::count_launch(), blocks), 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
                                                                     out.data_ptr(), out.stride(0), (int)bn);
         break;
       default:
-        splitk_reduce_kernel<kEpiF32><<<blocks, 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
+        splitk_reduce_kernel<kEpiF32><<<(::gsb::count_launch(), blocks), 256, 0, stream>>>(grp.ws, parts, M, N, epi.scale, rp, epi.ldr,
                                                                  out.data_ptr(), out.stride(0), (int)bn);
     }
     GSB_CUDA_CHECK(cudaGetLastError());

@@ -211,12 +211,12 @@ void gsb_moe_route(const at::Tensor& logits, int64_t num_experts, int64_t top_k,
   auto st = moe_stream(logits);
   if (T > 0) {
     const int threads = 256;
-    moe_topk_kernel<<<(T * 32 + threads - 1) / threads, threads, 0, st>>>(
+    moe_topk_kernel<<<(::gsb::count_launch(), (T * 32 + threads - 1) / threads), threads, 0, st>>>(
         logits.data_ptr<float>(), logits.stride(0), T, E, K, ids.data_ptr<int32_t>(), wts.data_ptr<float>(),
         counts.data_ptr<int32_t>());
     GSB_CUDA_CHECK(cudaGetLastError());
   }
-  moe_plan_kernel<<<1, 256, 0, st>>>(counts.data_ptr<int32_t>(), offsets.data_ptr<int32_t>(),
+  moe_plan_kernel<<<(::gsb::count_launch(), 1), 256, 0, st>>>(counts.data_ptr<int32_t>(), offsets.data_ptr<int32_t>(),
                                      cursor.data_ptr<int32_t>(), tile_expert.data_ptr<int32_t>(), E,
                                      (int)tile_expert.numel());
   GSB_CUDA_CHECK(cudaGetLastError());
@@ -233,7 +233,7 @@ void gsb_moe_scatter(const at::Tensor& x, const at::Tensor& ids, const at::Tenso
   c10::cuda::CUDAGuard g(x.device());
   const int threads = 256;
   const int64_t warps = (int64_t)T * K;
-  moe_scatter_kernel<<<(unsigned)((warps * 32 + threads - 1) / threads), threads, 0, moe_stream(x)>>>(
+  moe_scatter_kernel<<<(::gsb::count_launch(), (unsigned)((warps * 32 + threads - 1) / threads)), threads, 0, moe_stream(x)>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), T, K, H, ids.data_ptr<int32_t>(),
       offsets.data_ptr<int32_t>(), cursor.data_ptr<int32_t>(), slot.data_ptr<int32_t>(),
       reinterpret_cast<__nv_bfloat16*>(xp.data_ptr()), xp.stride(0));
@@ -255,7 +255,7 @@ void gsb_moe_scatter_slots(const at::Tensor& x, const at::Tensor& slot, int64_t 
   c10::cuda::CUDAGuard g(x.device());
   const int threads = 256;
   const int64_t warps = (int64_t)T * K;
-  moe_scatter_kernel<<<(unsigned)((warps * 32 + threads - 1) / threads), threads, 0, moe_stream(x)>>>(
+  moe_scatter_kernel<<<(::gsb::count_launch(), (unsigned)((warps * 32 + threads - 1) / threads)), threads, 0, moe_stream(x)>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), T, K, H, nullptr, nullptr, nullptr,
       slot.data_ptr<int32_t>(), reinterpret_cast<__nv_bfloat16*>(xp.data_ptr()), xp.stride(0));
   GSB_CUDA_CHECK(cudaGetLastError());
@@ -274,7 +274,7 @@ void gsb_moe_combine(const at::Tensor& yp, const at::Tensor& slot, const at::Ten
   c10::cuda::CUDAGuard g(out.device());
   const __nv_bfloat16* sp = shared ? reinterpret_cast<const __nv_bfloat16*>(shared->data_ptr()) : nullptr;
   const __nv_bfloat16* rp = residual ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
-  moe_combine_kernel<<<T, 256, 0, moe_stream(out)>>>(
+  moe_combine_kernel<<<(::gsb::count_launch(), T), 256, 0, moe_stream(out)>>>(
       reinterpret_cast<const __nv_bfloat16*>(yp.data_ptr()), yp.stride(0), slot.data_ptr<int32_t>(),
       wts.data_ptr<float>(), (int)top_k, H, sp, shared ? shared->stride(0) : 0, rp, residual ? residual->stride(0) : 0,
       (float)scale, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0));

@@ -88,7 +88,7 @@ void gsb_probe_verdict(const at::Tensor& hidden, const at::Tensor& rows, const a
   GSB_CHECK(verdict.size(1) >= L && verdict.stride(1) == 1, "probe_verdict: verdict too narrow");
   c10::cuda::CUDAGuard g(hidden.device());
   auto st = c10::cuda::getCurrentCUDAStream(hidden.device().index()).stream();
-  probe_verdict_kernel<<<n, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(hidden.data_ptr()),
+  probe_verdict_kernel<<<(::gsb::count_launch(), n), 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(hidden.data_ptr()),
                                           hidden.stride(0), rows.data_ptr<int32_t>(), slots.data_ptr<int32_t>(),
                                           out_rows.data_ptr<int32_t>(),
                                           reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
@@ -111,7 +111,7 @@ void gsb_probe_rewrite(const at::Tensor& logits, int64_t vocab_lo, const at::Ten
             "probe_rewrite: verdict too narrow");
   c10::cuda::CUDAGuard g(logits.device());
   auto st = c10::cuda::getCurrentCUDAStream(logits.device().index()).stream();
-  probe_rewrite_kernel<<<n, 256, 0, st>>>(logits.data_ptr<float>(), logits.stride(0), (int)logits.size(1), vocab_lo,
+  probe_rewrite_kernel<<<(::gsb::count_launch(), n), 256, 0, st>>>(logits.data_ptr<float>(), logits.stride(0), (int)logits.size(1), vocab_lo,
                                           out_rows.data_ptr<int32_t>(), slots.data_ptr<int32_t>(),
                                           labels.data_ptr<int32_t>(), (int)labels.size(1),
                                           verdict.data_ptr<float>(), (int)verdict.stride(0));

@@ -127,7 +127,7 @@ void gsb_routing(const at::Tensor& ids, const at::Tensor& seq_starts, const c10:
               "routing: kind_lut must be bool");
     kp = reinterpret_cast<const uint8_t*>(kind_lut->data_ptr());
   }
-  routing_kernel<256><<<S, 256, 0, st>>>(
+  routing_kernel<256><<<(::gsb::count_launch(), S), 256, 0, st>>>(
       ids.data_ptr<int64_t>(), seq_starts.data_ptr<int32_t>(),
       carry_in.has_value() ? carry_in->data_ptr<int32_t>() : nullptr, expert_tbl.data_ptr<int32_t>(),
       expert_tbl.numel(), lut.has_value() ? lut->data_ptr<int64_t>() : nullptr,

@@ -162,7 +162,7 @@ void gsb_sample(const at::Tensor& logits, const at::Tensor& temperature, const a
   if (B == 0) return;
   c10::cuda::CUDAGuard g(logits.device());
   auto st = c10::cuda::getCurrentCUDAStream(logits.device().index()).stream();
-  sample_kernel<512><<<B, 512, 0, st>>>(logits.data_ptr<float>(), logits.stride(0), (int)logits.size(1),
+  sample_kernel<512><<<(::gsb::count_launch(), B), 512, 0, st>>>(logits.data_ptr<float>(), logits.stride(0), (int)logits.size(1),
                                         temperature.data_ptr<float>(), top_k.data_ptr<int32_t>(),
                                         top_p.data_ptr<float>(), seeds.data_ptr<int64_t>(),
                                         offsets.data_ptr<int64_t>(), out.data_ptr<int64_t>());
