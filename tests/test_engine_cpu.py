@@ -240,3 +240,52 @@ def test_pick_bn_policy():
     assert pick_bn(100, 6144) == 64 and pick_bn(300, 4096) == 64
     assert pick_bn(222, 384, (128, 64), two_tile_bn=None) == 64
     assert pick_bn(222, 768) == 64  # a tensor-parallel shard: too few 128-wide tiles
+
+
+def test_cache_affinity_raises_hit_rate_under_overload():
+    """Chained calls under overload with a small KV cache: cache-affinity admission keeps the
+    running conversations' contexts resident, FCFS admission evicts them for new contexts.
+    The model is replaced by an executor that returns fixed tokens (scheduling only)."""
+    import types
+
+    from granite_switch_b200.engine.llm_engine import LLMEngine
+    from granite_switch_b200.engine.request import SamplingParams
+    from granite_switch_b200.utils.workload import WorkloadConfig, advance, call_prompt, make_workload
+
+    cfg = types.SimpleNamespace(num_adapters=0, adapter_token_ids=[], eos_token_id=None)
+
+    class _Exec:
+        def execute(self, out):
+            return [7 for c in out.chunks if c.needs_sample]
+
+    def run(policy):
+        eng = LLMEngine(cfg, _Exec(), 96, EngineConfig(max_num_seqs=4, max_num_batched_tokens=256,
+                                                       max_model_len=1024, scheduling_policy=policy))
+        convs = make_workload(WorkloadConfig(num_conversations=24, rate=float("inf"), context_len=160, calls=4,
+                                             inv_min=4, inv_max=8, gen_min=4, gen_max=8, vocab=1000, num_adapters=1,
+                                             seed=1))
+        by_req = {}
+
+        def submit(conv):
+            r = eng.add_request(call_prompt(conv, [999]), SamplingParams(max_tokens=conv.calls[conv.next_call].gen_len,
+                                                                        ignore_eos=True))
+            by_req[r.request_id] = conv
+
+        def on_finish(req):
+            conv = by_req.pop(req.request_id)
+            if advance(conv, req.prompt_ids, req.output_ids):
+                submit(conv)
+
+        eng.on_finish = on_finish
+        for c in convs:
+            submit(c)
+        steps = 0
+        while eng.has_unfinished() and steps < 5000:
+            eng.step()
+            steps += 1
+        assert not eng.has_unfinished()
+        assert all(c.next_call == 4 for c in convs)  # every call of every conversation ran
+        return eng.prefix_cache_hit_rate()
+
+    fcfs, affinity = run("fcfs"), run("cache_affinity")
+    assert affinity > fcfs + 0.2, (fcfs, affinity)
