@@ -149,8 +149,9 @@ def main(argv=None):
     ap.add_argument("--no-fused-tp-comm", action="store_true", help="reduce with NCCL only")
     ap.add_argument("--scheduling-policy", choices=["cache_affinity", "fcfs"], default="cache_affinity",
                     help="admission order: requests whose context is cached first, or arrival order")
-    ap.add_argument("--max-wait-steps", type=int, default=None,
-                    help="cache_affinity: engine steps after which a waiting cold request goes first")
+    ap.add_argument("--max-wait-steps", type=int, default=2000,
+                    help="cache_affinity: engine steps after which a waiting cold request goes first "
+                         "(bounds how long a new conversation waits under overload; negative: no bound)")
     args = ap.parse_args(argv)
     import uvicorn
 
@@ -161,7 +162,8 @@ def main(argv=None):
                         max_model_len=args.max_model_len, gpu_memory_utilization=args.gpu_memory_utilization,
                         enable_prefix_caching=not args.no_prefix_caching, tensor_parallel_size=tp,
                         pipeline_parallel_size=pp, fused_tp_comm=not args.no_fused_tp_comm,
-                        scheduling_policy=args.scheduling_policy, max_wait_steps=args.max_wait_steps)
+                        scheduling_policy=args.scheduling_policy,
+                        max_wait_steps=args.max_wait_steps if args.max_wait_steps >= 0 else None)
     sync = None
     if tp * pp > 1:
         # one process per GPU (torchrun); rank 0 serves HTTP and drives the others in lock step
