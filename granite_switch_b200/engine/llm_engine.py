@@ -22,6 +22,11 @@ from .request import Request, RequestOutput, SamplingParams
 from .scheduler import Scheduler
 
 
+# Engine steps a cold request may be passed over under cache-affinity admission
+# before it goes first (about a minute of 8B-shape steps on one B200).
+DEFAULT_MAX_WAIT_STEPS = 2000
+
+
 @dataclass
 class EngineConfig:
     max_num_seqs: int = 256
@@ -38,7 +43,8 @@ class EngineConfig:
     seed: int = 0
     fused_tp_comm: bool = False            # symmetric-memory fused GEMM + reduction kernels
     scheduling_policy: str = "cache_affinity"  # or "fcfs" (admission order, see engine.scheduler)
-    max_wait_steps: int | None = None      # cache_affinity: steps before a cold request goes first
+    max_wait_steps: int | None = DEFAULT_MAX_WAIT_STEPS  # cache_affinity: steps before a cold request
+    #                                                    goes first; None = unbounded
 
 
 @dataclass
@@ -301,4 +307,4 @@ class LLM:
         return [_to_output(r) for r in reqs]
 
 
-__all__ = ["LLM", "LLMEngine", "EngineConfig", "SamplingParams", "BLOCK_SIZE", "os"]
+__all__ = ["LLM", "LLMEngine", "EngineConfig", "SamplingParams", "BLOCK_SIZE", "DEFAULT_MAX_WAIT_STEPS", "os"]

@@ -18,6 +18,7 @@ import json
 import time
 import uuid
 
+from ..engine.llm_engine import DEFAULT_MAX_WAIT_STEPS
 from ..engine.request import SamplingParams
 from .async_engine import AsyncEngine
 
@@ -149,7 +150,7 @@ def main(argv=None):
     ap.add_argument("--no-fused-tp-comm", action="store_true", help="reduce with NCCL only")
     ap.add_argument("--scheduling-policy", choices=["cache_affinity", "fcfs"], default="cache_affinity",
                     help="admission order: requests whose context is cached first, or arrival order")
-    ap.add_argument("--max-wait-steps", type=int, default=2000,
+    ap.add_argument("--max-wait-steps", type=int, default=DEFAULT_MAX_WAIT_STEPS,
                     help="cache_affinity: engine steps after which a waiting cold request goes first "
                          "(bounds how long a new conversation waits under overload; negative: no bound)")
     args = ap.parse_args(argv)

@@ -17,6 +17,9 @@ owned). When the chosen replica has ``--max-inflight-skew`` more requests in
 flight than the least loaded one, the request goes to the least loaded one.
 A replica that refuses a connection is marked down and the request is retried
 on the next replica in hash order; a background task re-probes ``/health``.
+A request that reached a replica is never re-sent: a timeout answers 504 and a
+connection broken mid-request 502, and neither marks the replica down (it may
+still be generating, and one slow request says nothing about its health).
 
 ``python -m granite_switch_b200.server.router --backend http://127.0.0.1:8001
 --backend http://127.0.0.1:8002 [--port 8000]``
@@ -176,6 +179,7 @@ def build_router_app(router: Router, health_interval_s: float = 5.0):
     import aiohttp
     from fastapi import FastAPI, Request
     from fastapi.responses import JSONResponse, PlainTextResponse, Response, StreamingResponse
+    from starlette.background import BackgroundTask
 
     @contextlib.asynccontextmanager
     async def lifespan(app):
@@ -205,35 +209,57 @@ def build_router_app(router: Router, health_interval_s: float = 5.0):
             if i > 0:
                 router.failovers += 1
             router.inflight[backend] += 1
-            released = False
             try:
                 resp = await router.session.post(backend + path, data=raw, headers=headers)
-            except (aiohttp.ClientConnectionError, asyncio.TimeoutError) as e:
+            except aiohttp.ClientConnectorError as e:
+                # the connection was never made, so the replica never saw the request: try the next one
                 router.inflight[backend] -= 1
                 router.healthy[backend] = False
                 last_error = e
                 continue
+            except asyncio.TimeoutError:
+                # the replica may have accepted the request and still be generating; sending it
+                # elsewhere would run it twice, and one slow request says nothing about health
+                router.inflight[backend] -= 1
+                return JSONResponse({"error": {"message": f"replica {backend} timed out"}}, status_code=504)
+            except aiohttp.ClientError as e:
+                # the connection broke after the request went out: same reasoning as a timeout
+                router.inflight[backend] -= 1
+                return JSONResponse({"error": {"message": f"replica {backend} failed: {e}"}}, status_code=502)
             router.requests[backend] += 1
-            try:
-                if body.get("stream"):
-                    async def relay(resp=resp, backend=backend):
-                        try:
-                            async for chunk in resp.content.iter_chunked(STREAM_CHUNK):
-                                yield chunk
-                        finally:
-                            resp.release()
-                            router.inflight[backend] -= 1
+            done = False
 
-                    released = True  # the relay releases the response and the in-flight slot
+            def release(resp=resp, backend=backend):
+                # idempotent: reached from the relay's finally, the response's background task
+                # (which runs when the client disconnects before the relay starts) or the
+                # non-streaming path below
+                nonlocal done
+                if not done:
+                    done = True
+                    resp.release()
+                    router.inflight[backend] -= 1
+
+            if body.get("stream"):
+                async def relay(resp=resp, release=release):
+                    try:
+                        async for chunk in resp.content.iter_chunked(STREAM_CHUNK):
+                            yield chunk
+                    finally:
+                        release()
+
+                try:
                     return StreamingResponse(relay(), status_code=resp.status,
-                                             media_type=resp.headers.get("Content-Type", "text/event-stream"))
+                                             media_type=resp.headers.get("Content-Type", "text/event-stream"),
+                                             background=BackgroundTask(release))
+                except BaseException:
+                    release()
+                    raise
+            try:
                 data = await resp.read()
                 return Response(content=data, status_code=resp.status,
                                 media_type=resp.headers.get("Content-Type", "application/json"))
             finally:
-                if not released:
-                    resp.release()
-                    router.inflight[backend] -= 1
+                release()
         return JSONResponse({"error": {"message": f"no replica reachable: {last_error}"}}, status_code=503)
 
     @app.post("/v1/completions")

@@ -153,6 +153,35 @@ def test_cache_affinity_max_wait_steps():
     assert order == [False, True, False]
 
 
+def _starve(max_wait_steps, steps):
+    """Step a one-slot cache-affinity scheduler with a warm arrival every step; return the
+    step at which the single cold request was admitted (None if never)."""
+    bm = BlockManager(64)
+    ctx = list(range(100, 164))
+    _cache_context(bm, ctx)
+    sch = Scheduler(bm, max_num_seqs=1, max_num_batched_tokens=512, policy="cache_affinity",
+                    max_wait_steps=max_wait_steps)
+    cold = Request(list(range(500, 540)))
+    sch.add(cold)
+    for i in range(steps):
+        sch.add(Request(ctx + [2, i % 50]))  # the next call of a resident conversation
+        r = sch.schedule().chunks[0].req
+        sch.finish(r, "length")
+        if r is cold:
+            return i + 1
+    return None
+
+
+def test_cache_affinity_default_bound_prevents_starvation():
+    """A steady stream of warm calls starves a cold request forever without a bound; the
+    engine's default bound admits it after DEFAULT_MAX_WAIT_STEPS steps."""
+    from granite_switch_b200.engine import DEFAULT_MAX_WAIT_STEPS, EngineConfig
+
+    assert EngineConfig().max_wait_steps == DEFAULT_MAX_WAIT_STEPS
+    assert _starve(None, DEFAULT_MAX_WAIT_STEPS + 50) is None
+    assert _starve(EngineConfig().max_wait_steps, DEFAULT_MAX_WAIT_STEPS + 50) == DEFAULT_MAX_WAIT_STEPS
+
+
 def test_cache_affinity_preempted_and_abort():
     bm = BlockManager(64)
     sch = Scheduler(bm, max_num_seqs=2, max_num_batched_tokens=512, policy="cache_affinity")

@@ -4,6 +4,7 @@ The replicas here are small HTTP apps that report which replica served a call,
 so the routing logic is tested without models (the replica server itself is
 covered by test_server.py).
 """
+import asyncio
 import json
 import socket
 import threading
@@ -32,6 +33,8 @@ def _replica_app(name: str):
     async def serve(req: Request):
         body = await req.json()
         app.state.calls += 1
+        if body.get("sleep_s"):
+            await asyncio.sleep(body["sleep_s"])  # a slow generation
         if body.get("stream"):
             async def events():
                 for i in range(3):
@@ -163,3 +166,33 @@ def test_router_failover(replicas):
         assert router.failovers >= 1 and router.healthy[down.url] is False
         h = c.get("/health").json()
         assert h["status"] == "ok" and h["backends"][down.url] is False
+
+
+def test_router_timeout_is_not_failover(replicas):
+    """A replica that accepted the request but answers too slowly gets a 504: the request is
+    not re-sent to another replica (it would run twice) and the replica stays in rotation."""
+    from fastapi.testclient import TestClient
+
+    router = Router([r.url for r in replicas], timeout_s=0.5)
+    with TestClient(build_router_app(router, health_interval_s=0)) as c:
+        body = {"prompt": [7, 8, 9], "max_tokens": 2, "sleep_s": 2.0}
+        r = c.post("/v1/completions", json=body)
+        assert r.status_code == 504, r.text
+        assert sum(rep.app.state.calls for rep in replicas) == 1
+        assert router.failovers == 0 and all(router.healthy.values())
+        assert sum(router.inflight.values()) == 0
+
+
+def test_router_stream_released_without_iteration(replicas):
+    """The in-flight slot and the upstream response of a streaming call are released even when
+    the relay generator never runs (the client went away before the body was read)."""
+    from fastapi.testclient import TestClient
+
+    router = Router([r.url for r in replicas])
+    with TestClient(build_router_app(router, health_interval_s=0)) as c:
+        with c.stream("POST", "/v1/completions", json={"prompt": [1, 2], "max_tokens": 3, "stream": True}):
+            pass  # close without reading the body
+        deadline = time.time() + 5
+        while sum(router.inflight.values()) and time.time() < deadline:
+            time.sleep(0.05)
+        assert sum(router.inflight.values()) == 0
