@@ -10,7 +10,6 @@ other torchrun ranks wait. Prints the same JSON line as the native arm with
 from __future__ import annotations
 
 import os
-import statistics
 import sys
 import time
 import traceback
@@ -29,7 +28,7 @@ def _wait_for_rank0(flag):
         time.sleep(2)
 
 
-def run(args, emit, metric):
+def run(args, emit, metric, ref_path=REF):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     flag = f"/tmp/gs_ref_done_{os.environ.get('MASTER_PORT', 'x')}"
@@ -37,7 +36,7 @@ def run(args, emit, metric):
         _wait_for_rank0(flag)
         return
     try:
-        _run(args, emit, metric, world)
+        _run(args, emit, metric, world, ref_path)
     except Exception as e:  # the line must still be printed
         tb = traceback.format_exc().strip().splitlines()
         emit({"impl": "reference", "unavailable": f"{type(e).__name__}: {str(e)[:300]}",
@@ -47,11 +46,11 @@ def run(args, emit, metric):
             f.write("done")
 
 
-def _run(args, emit, metric, world):
+def _run(args, emit, metric, world, ref_path):
     for k in _TORCHRUN_VARS:
         os.environ.pop(k, None)
-    os.environ["PYTHONPATH"] = REF + os.pathsep + os.environ.get("PYTHONPATH", "")
-    sys.path.insert(0, REF)
+    os.environ["PYTHONPATH"] = ref_path + os.pathsep + os.environ.get("PYTHONPATH", "")
+    sys.path.insert(0, ref_path)
     sys.path.insert(0, ROOT)
     import torch
 
@@ -83,14 +82,18 @@ def _run(args, emit, metric, world):
     stats = {"gen": 0, "prompt": 0, "cached": 0}
     seen = {}
     first_tok = {}
-    ttfts = []
     first_calls = set()
     counter = [0]
+
+    from types import SimpleNamespace
+
+    submitted = {}  # rid -> record with arrival / first-token times (bench.ttft_summary)
 
     def submit(conv, now):
         prompt = call_prompt(conv, ctrl, args.mode)
         rid = f"r{counter[0]}"
         counter[0] += 1
+        submitted[rid] = SimpleNamespace(request_id=rid, arrival_time=now, first_token_time=None)
         sp = SamplingParams(max_tokens=conv.calls[conv.next_call].gen_len, temperature=0.0, ignore_eos=True)
         engine.add_request(rid, {"prompt_token_ids": prompt}, sp)
         live[rid] = (conv, prompt, now)
@@ -98,6 +101,7 @@ def _run(args, emit, metric, world):
             first_calls.add(rid)
 
     t0 = time.perf_counter()
+    t_start = t0
     nxt = [0]
 
     def step():
@@ -119,7 +123,7 @@ def _run(args, emit, metric, world):
             seen[o.request_id] = len(toks)
             if toks and o.request_id not in first_tok:
                 first_tok[o.request_id] = tnow
-                ttfts.append((tnow, tnow - sub, o.request_id in first_calls))
+                submitted[o.request_id].first_token_time = tnow
             if o.finished:
                 seen.pop(o.request_id, None)
                 stats["prompt"] += len(prompt)
@@ -147,8 +151,7 @@ def _run(args, emit, metric, world):
     w1 = time.perf_counter()
     tok_after = stats["gen"]
     gen = tok_after - tok_before
-    win = [t for (ts, t, _) in ttfts if w0 <= ts <= w1]
-    win_first = [t for (ts, t, first) in ttfts if w0 <= ts <= w1 and first]
+    ttft = bench.ttft_summary(list(submitted.values()), first_calls, t_start, w0, w1)
     dp, dc = stats["prompt"] - p0, stats["cached"] - c0
     hit = None
     try:  # vLLM's own prefix-cache counters, when this version exposes them
@@ -163,11 +166,7 @@ def _run(args, emit, metric, world):
           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
           "data": "synthetic (random prompts, random-init base and adapter weights)", "impl": "reference",
           "timing": "host clock (vLLM runs the model in its own engine process)",
-          "p50_ttft_s": round(statistics.median(win), 4) if win else None,
-          "p90_ttft_s": round(sorted(win)[min(len(win) - 1, int(0.9 * len(win)))], 4) if win else None,
-          "ttft_samples": len(win),
-          "first_call_p50_ttft_s": round(statistics.median(win_first), 4) if win_first else None,
-          "first_call_ttft_samples": len(win_first),
+          **ttft,
           "prefix_hit_rate": round(dc / dp, 4) if dp else None, "vllm_prefix_cache_counters": hit,
           "config": {"model": f"{args.preset}-shape", "global_batch": args.max_num_seqs, "seq_len": args.context_len,
                      "parallelism": f"tp{world}", "adapters": "12 aLoRA r32 q/k/v/o",

@@ -21,10 +21,15 @@ pinned host memory and reads the sampled ids back.
 
 The engine admits requests under its default ``cache_affinity`` policy:
 a call whose context is already in the prefix cache (a conversation's next
-call) is admitted before new conversations; ``--scheduling-policy fcfs``
-admits in arrival order, as the reference's vLLM engine does. The line
-reports p50 / p90 TTFT over every call whose first token landed in the timed
-window and, separately, the p50 TTFT of conversations' first calls.
+call) is admitted before new conversations, and a cold request waits at most
+``--max-wait-steps`` engine steps; ``--scheduling-policy fcfs`` admits in
+arrival order, as the reference's vLLM engine does. The line reports p50 / p90
+TTFT over every request that arrived since the ramp began, queue wait
+included (a request still waiting at the end counts at its wait so far), the
+p50 of conversations' first calls, the window's token mix (prefill tokens and
+decode rows per step, fraction of cold admissions) and the count of device
+errors (steps whose kernels reported a bounded wait that ran out or a bad
+index); the run exits non-zero if there was any.
 
 ``--impl reference`` runs the unmodified reference (granite-switch's vLLM
 plugin from baseline/_ref) on the same workload and prints the same line.
@@ -33,16 +38,15 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
-import statistics
 import sys
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
+DEFAULT_MAX_WAIT_STEPS = 2000  # the engine's default (engine.llm_engine.DEFAULT_MAX_WAIT_STEPS)
 METRIC = "output tok/s + p50 TTFT, multi-aLoRA 8B-shape, TP1/2/4/8; KV prefix-hit rate"
-BASELINE_VALUE = None  # BASELINE.md publishes no number for this workload on any B200
+BASELINE_VALUE = None  # the reference publishes no number for this workload on any B200
 
 
 def parse_args():
@@ -65,6 +69,8 @@ def parse_args():
                    help="use NCCL all-reduce instead of the fused GEMM+multimem collectives for TP")
     p.add_argument("--scheduling-policy", choices=["cache_affinity", "fcfs"], default="cache_affinity",
                    help="engine admission order (the reference arm's vLLM engine is FCFS)")
+    p.add_argument("--max-wait-steps", type=int, default=DEFAULT_MAX_WAIT_STEPS,
+                   help="cache_affinity: engine steps after which a waiting cold request goes first (negative: none)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-blocks", type=int, default=None)
     return p.parse_args()
@@ -126,7 +132,8 @@ def run_native(args):
     ecfg = EngineConfig(max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
                         max_model_len=args.context_len + args.calls * 200 + 256, tensor_parallel_size=world,
                         num_kv_blocks=args.kv_blocks, fused_tp_comm=args.fused_comm, seed=args.seed,
-                        scheduling_policy=args.scheduling_policy)
+                        scheduling_policy=args.scheduling_policy,
+                        max_wait_steps=args.max_wait_steps if args.max_wait_steps >= 0 else None)
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
               random_init=dict(lora_modules=("qkv", "o"), rank=32, seed=args.seed), tp_rank=rank, tp_group=group)
     eng = llm.engine
@@ -137,10 +144,13 @@ def run_native(args):
     by_req = {}
     first_calls = set()  # request ids of conversations' first calls (cold contexts)
 
+    submitted = []  # every request, for TTFT over all arrivals (queue wait included)
+
     def submit(conv, now):
         prompt = call_prompt(conv, ctrl, args.mode)
         gen = conv.calls[conv.next_call].gen_len
         r = eng.add_request(prompt, SamplingParams(max_tokens=gen, ignore_eos=True), arrival_time=now)
+        submitted.append(r)
         by_req[r.request_id] = conv
         if conv.next_call == 0:
             first_calls.add(r.request_id)
@@ -152,6 +162,7 @@ def run_native(args):
 
     eng.on_finish = on_finish
     t0 = time.perf_counter()
+    t_start = t0
     next_conv = 0
     arrived = torch.zeros(1, dtype=torch.long, device="cuda")
 
@@ -178,7 +189,11 @@ def run_native(args):
 
     def step():
         admit()
-        fin = eng_step()
+        try:
+            fin = eng_step()
+        except _native.DeviceError as e:  # the engine aborted that step's requests; counted below
+            print(f"rank {rank}: {e}", file=sys.stderr, flush=True)
+            fin = []
         finished_log.extend(fin)
         return fin
 
@@ -199,10 +214,11 @@ def run_native(args):
         dist.barrier(group=group)
     gen0 = eng.stats.generated_tokens
     q0, h0 = eng.blocks.queries, eng.blocks.hits
+    pf0, dr0 = eng.stats.prefill_tokens, eng.stats.decode_rows
+    adm0, cold0 = eng.scheduler.num_admitted, eng.scheduler.num_admitted_cold
     ex = eng.executor
     h2d0, d2h0 = ex.h2d_bytes, ex.d2h_bytes
     launches0 = _native.launch_count()
-    first_tok_before = {r.request_id for r in finished_log}
     start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank()) as clocks:
         torch.cuda.synchronize()
@@ -219,14 +235,10 @@ def run_native(args):
     wall_s = max_over_ranks(w1 - w0, group)
     gen = eng.stats.generated_tokens - gen0
     launches = _native.launch_count() - launches0
-    # TTFT of calls whose first token landed in the timed window
-    ttfts, first_ttfts = [], []
-    for r in finished_log + list(eng.scheduler.running):
-        if r.first_token_time is not None and w0 <= r.first_token_time <= w1:
-            ttfts.append(r.first_token_time - r.arrival_time)
-            if r.request_id in first_calls:
-                first_ttfts.append(r.first_token_time - r.arrival_time)
+    ttft = ttft_summary(submitted, first_calls, t_start, w0, w1)
     dq, dh = eng.blocks.queries - q0, eng.blocks.hits - h0
+    adm, cold = eng.scheduler.num_admitted - adm0, eng.scheduler.num_admitted_cold - cold0
+    device_errors = eng.stats.device_errors + _native.read_errors(torch.device("cuda", local_rank()))
     value = gen / (dev_ms / 1e3)
     e2e = gen / wall_s
     clk = clocks.summary()
@@ -238,11 +250,7 @@ def run_native(args):
             "vs_baseline": (round(value / BASELINE_VALUE, 4) if BASELINE_VALUE else None),
             "dtype": "bf16", "data": "synthetic (random prompts, random-init base and adapter weights)",
             "impl": "native",
-            "p50_ttft_s": round(statistics.median(ttfts), 4) if ttfts else None,
-            "p90_ttft_s": round(_pct(ttfts, 0.9), 4) if ttfts else None,
-            "ttft_samples": len(ttfts),
-            "first_call_p50_ttft_s": round(statistics.median(first_ttfts), 4) if first_ttfts else None,
-            "first_call_ttft_samples": len(first_ttfts),
+            **ttft,
             "prefix_hit_rate": round(dh / dq, 4) if dq else None,
             "prefix_hit_rate_overall": round(eng.prefix_cache_hit_rate(), 4),
             "config": {"model": f"{args.preset}-shape" + (f"-L{args.layers}" if args.layers else ""),
@@ -250,7 +258,7 @@ def run_native(args):
                        "parallelism": f"tp{world}", "adapters": "12 aLoRA r32 q/k/v/o",
                        "workload": f"poisson {args.rate}/s, {args.calls} chained calls, inv 16-64, gen 32-128",
                        "mode": args.mode, "max_num_batched_tokens": args.max_num_batched_tokens,
-                       "scheduling_policy": args.scheduling_policy,
+                       "scheduling_policy": args.scheduling_policy, "max_wait_steps": ecfg.max_wait_steps,
                        "ramp_steps": ramp, "l2": "inputs larger than L2 (each step streams all weights)",
                        "fused_comm": bool(getattr(llm.model, "comm", None) is not None)},
             "e2e": {"value": round(e2e, 2), "unit": "output tok/s", "h2d_bytes_per_step": (ex.h2d_bytes - h2d0) // args.steps,
@@ -259,24 +267,83 @@ def run_native(args):
             "clocks": clk,
             "kv_blocks": eng.blocks.num_blocks,
             "running_at_end": len(eng.scheduler.running),
+            "window_mix": {"prefill_tokens_per_step": round((eng.stats.prefill_tokens - pf0) / args.steps, 1),
+                           "decode_rows_per_step": round((eng.stats.decode_rows - dr0) / args.steps, 1),
+                           "admitted": adm, "cold_admission_fraction": round(cold / adm, 4) if adm else None},
+            "device_errors": device_errors,
         })
     if world > 1:
         dist.barrier(group=group)
         dist.destroy_process_group()
+    if device_errors:
+        raise SystemExit(f"{device_errors} device error(s) during the run")
+
+
+def ttft_summary(reqs, first_calls, t_start, w0, w1) -> dict:
+    """TTFT over every request that arrived from the start of the ramp to the end of the
+    timed window, queue wait included: a request with no first token by ``w1`` counts at
+    its wait so far (``waiting_at_end`` of them). Also the p50 of conversations' first calls
+    and, for comparison with window-only figures, TTFTs of first tokens inside [w0, w1]."""
+    all_t, first_t, win = [], [], []
+    waiting = 0
+    for r in reqs:
+        if r.arrival_time < t_start or r.arrival_time > w1:
+            continue
+        ft = r.first_token_time
+        if ft is not None and ft <= w1:
+            t = ft - r.arrival_time
+            if ft >= w0:
+                win.append(t)
+        else:
+            t = w1 - r.arrival_time
+            waiting += 1
+        all_t.append(t)
+        if r.request_id in first_calls:
+            first_t.append(t)
+
+    def p(xs, q):
+        return round(_pct(xs, q), 4) if xs else None
+
+    return {"p50_ttft_s": p(all_t, 0.5), "p90_ttft_s": p(all_t, 0.9), "ttft_samples": len(all_t),
+            "ttft_waiting_at_end": waiting, "ttft_scope": "every request arrived since the ramp began; "
+            "requests without a first token count at their wait so far",
+            "first_call_p50_ttft_s": p(first_t, 0.5), "first_call_ttft_samples": len(first_t),
+            "window_p50_ttft_s": p(win, 0.5), "window_ttft_samples": len(win)}
 
 
 # ----------------------------------------------------------------------------- reference arm
+def find_reference() -> tuple[str | None, list[str]]:
+    """Locate the installed reference package: the ``pip --target baseline/_ref`` layout
+    (``baseline/_ref/granite_switch``), a source tree (``baseline/_ref/src/granite_switch``)
+    or an installed distribution. Returns ``(directory to put on sys.path, paths checked)``."""
+    import importlib.util
+
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    checked = []
+    for root in (ref, os.path.join(ref, "src")):
+        pkg = os.path.join(root, "granite_switch", "__init__.py")
+        checked.append(pkg)
+        if os.path.isfile(pkg):
+            return root, checked
+    checked.append("importlib: granite_switch")
+    spec = importlib.util.find_spec("granite_switch")
+    if spec is not None and spec.origin:
+        return os.path.dirname(os.path.dirname(spec.origin)), checked
+    return None, checked
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
-    ref_dir = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_dir, "granite_switch")):
+    where, checked = find_reference()
+    if where is None:
         if rank == 0:
-            emit({"impl": "reference", "unavailable": "baseline/_ref is not installed"})
+            emit({"impl": "reference", "unavailable": "the reference package is not installed; checked: "
+                  + ", ".join(checked)})
         return
     sys.path.insert(0, os.path.join(ROOT, "baseline"))
     from reference_arm import run as ref_run  # baseline/reference_arm.py
 
-    ref_run(args, emit, METRIC)
+    ref_run(args, emit, METRIC, where)
 
 
 def main():

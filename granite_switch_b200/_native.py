@@ -101,21 +101,39 @@ def read_error_detail(device: torch.device, clear: bool = True) -> tuple[int, st
         buf.zero_()
     if not site:
         return w, None, None
-    return w, BAD_INDEX_SITES.get(site, f"site {site}"), idx
+    return w, site_name(site), idx
+
+
+class DeviceError(RuntimeError):
+    """Kernels of a step reported a bounded wait that ran out or a bad index.
+
+    ``word`` is the device error word (``ERR_*`` bits); ``site`` / ``index`` the
+    first bad index reported, if any. The outputs of that step are not to be
+    trusted: the engine aborts the requests the step carried.
+    """
+
+    def __init__(self, word: int, site: str | None = None, index: int | None = None):
+        self.word, self.site, self.index = int(word), site, index
+        super().__init__(describe_error(self.word, site, index))
+
+
+_ERR_NAMES = ((ERR_GEMM_WAIT, "gemm-wait-timeout"), (ERR_ATTN_WAIT, "attention-wait-timeout"),
+              (ERR_PEER_WAIT, "peer-wait-timeout"), (ERR_BAD_SHAPE, "bad-shape"),
+              (ERR_SHRINK_WAIT, "shrink-wait-timeout"))
+
+
+def describe_error(word: int, site: str | None = None, index: int | None = None) -> str:
+    names = [name for bit, name in _ERR_NAMES if word & bit] or ["unknown"]
+    where = f"; first bad index: {site} = {index}" if site else ""
+    return f"device kernels reported errors: {', '.join(names)} (0x{word:x}){where}"
+
+
+def site_name(code: int) -> str | None:
+    """Name of a bad-index site code (``err[1]``), or None for 0."""
+    return BAD_INDEX_SITES.get(code, f"site {code}") if code else None
 
 
 def check_errors(device: torch.device) -> None:
     val, site, idx = read_error_detail(device)
     if val:
-        names = []
-        for bit, name in (
-            (ERR_GEMM_WAIT, "gemm-wait-timeout"),
-            (ERR_ATTN_WAIT, "attention-wait-timeout"),
-            (ERR_PEER_WAIT, "peer-wait-timeout"),
-            (ERR_BAD_SHAPE, "bad-shape"),
-            (ERR_SHRINK_WAIT, "shrink-wait-timeout"),
-        ):
-            if val & bit:
-                names.append(name)
-        where = f"; first bad index: {site} = {idx}" if site else ""
-        raise RuntimeError(f"device kernels reported errors: {', '.join(names)} (0x{val:x}){where}")
+        raise DeviceError(val, site, idx)

@@ -26,7 +26,7 @@ import torch
 from ..checkpoint import save_state_dict
 from ..config import SWITCH_CACHE_LAYERS, GraniteSwitchConfig
 from ..routing.codebook import KerdockDGCodeGenerator
-from ..routing.probe_routing import build_adapter_kind_lut
+from ..routing.scan import probe_slot_mask
 from ..routing.token_exchange import build_control_to_substitute_lut, validate_control_lut
 from .arch import resolve_arch
 from .validators import audit_saved_checkpoint, validate_cross_stream_population, validate_parameters
@@ -209,7 +209,7 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
         lut = build_control_to_substitute_lut(config)
         validate_control_lut(lut, config)
         sd["model.switch.control_to_substitute_lut"] = lut
-        kind_lut = build_adapter_kind_lut(config)
+        kind_lut = probe_slot_mask(getattr(config, "adapter_kinds", None))
         if kind_lut is not None:
             sd["model.switch.adapter_kind_lut"] = kind_lut
     if config.tie_word_embeddings:

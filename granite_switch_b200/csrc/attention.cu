@@ -87,11 +87,8 @@ struct AttnCfg {
 // Both keep the same K/V bytes in flight per SM; the short layout has more warps
 // to hide each tile's MMA and softmax latency. Measured on B200 (128 requests x
 // 4.2k keys, d=128): 5.86 vs 5.05 TB/s, and 16.4 vs 19.0 ms of decode attention
-// in an 8B step. Env GSB_ATTN_DECODE_STAGES sets the start value.
-static int g_decode_stages = [] {
-  const char* e = std::getenv("GSB_ATTN_DECODE_STAGES");
-  return e ? std::atoi(e) : 2;
-}();
+// in an 8B step. attn_decode_stages() switches it at run time for A/B tests.
+static int g_decode_stages = 2;
 
 template <int D, int WARPS_M, int KT, int STAGES>
 __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
@@ -627,8 +624,15 @@ static int setup(int dev, float** scratch, char* msg, size_t len) {
     if (e != cudaSuccess || p == nullptr)
       return fail(msg, len, GSB_NOALLOC_ECUDA, "cudaGetSymbolAddress(scratch) failed on device %d: %s", dev,
                   cudaGetErrorString(e));
-    e = cudaFuncSetAttribute(paged_attn_kernel<128, 1, 64, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             AttnCfg<128, 1, 64, 3>::SMEM);
+    // both decode layouts of each head size (the one used follows attn_decode_stages())
+    e = cudaFuncSetAttribute(paged_attn_kernel<128, 1, 64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             AttnCfg<128, 1, 64, 2>::SMEM);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(paged_attn_kernel<128, 1, 64, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               AttnCfg<128, 1, 64, 3>::SMEM);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(paged_attn_kernel<64, 1, 64, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               AttnCfg<64, 1, 64, 4>::SMEM);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(paged_attn_kernel<64, 1, 64, 6>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                AttnCfg<64, 1, 64, 6>::SMEM);
@@ -716,14 +720,20 @@ extern "C" int gsb_decode_attention_noalloc(const void* q, int64_t q_stride, con
     }
     const float scale_log2 = (float)(scale * 1.4426950408889634);
     const dim3 grid(num_work, Hkv, nsplit);
-    if (D == 128)
-      launch_decode<128, 3>(grid, stream, tk, tv, q, q_stride, block_table, block_table_stride, (int)num_blocks,
-                            q_start, kv_len,
-                            work_seq, work_row0, Hq, Hkv, scale_log2, out, out_stride, wso, wsl, nsplit, T, err);
-    else
-      launch_decode<64, 6>(grid, stream, tk, tv, q, q_stride, block_table, block_table_stride, (int)num_blocks,
-                           q_start, kv_len,
-                           work_seq, work_row0, Hq, Hkv, scale_log2, out, out_stride, wso, wsl, nsplit, T, err);
+    // the same layout choice as gsb_paged_attention: short rings (default) or deep rings
+    const bool short_ring = g_decode_stages == 2;
+#define GSB_NOALLOC_DECODE(DD, ST)                                                                               \
+  launch_decode<DD, ST>(grid, stream, tk, tv, q, q_stride, block_table, block_table_stride, (int)num_blocks,    \
+                        q_start, kv_len, work_seq, work_row0, Hq, Hkv, scale_log2, out, out_stride, wso, wsl, \
+                        nsplit, T, err)
+    if (D == 128) {
+      if (short_ring) GSB_NOALLOC_DECODE(128, 2);
+      else GSB_NOALLOC_DECODE(128, 3);
+    } else {
+      if (short_ring) GSB_NOALLOC_DECODE(64, 4);
+      else GSB_NOALLOC_DECODE(64, 6);
+    }
+#undef GSB_NOALLOC_DECODE
   } catch (const std::exception& ex) {
     return fail(msg, msg_len, GSB_NOALLOC_EINVAL, "%s", ex.what());
   }

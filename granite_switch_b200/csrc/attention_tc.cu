@@ -755,13 +755,10 @@ __global__ void __launch_bounds__(320, 1)
 using namespace gsb;
 
 // Softmax arithmetic: 0 = scalar fp32, 1 = packed f32x2 scale-and-shift and row
-// sums (env GSB_ATTN_PACKED sets the start value). Taking a quarter of the
-// exponentials off MUFU with a polynomial was measured slower on B200 (530 vs
-// 518 TFLOP/s causal 4k), so the exponentials stay on ex2.approx.
-static int g_attn_packed = [] {
-  const char* e = std::getenv("GSB_ATTN_PACKED");
-  return e ? std::atoi(e) : 1;
-}();
+// sums (attn_packed() switches it at run time for A/B tests). Taking a quarter
+// of the exponentials off MUFU with a polynomial was measured slower on B200
+// (530 vs 518 TFLOP/s causal 4k), so the exponentials stay on ex2.approx.
+static int g_attn_packed = 1;
 
 int64_t gsb_attn_packed(int64_t v) {
   const int64_t old = g_attn_packed;

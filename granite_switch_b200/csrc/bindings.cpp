@@ -28,7 +28,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &gsb_sample, "temperature / top-k / top-p sampling (Gumbel-max, Philox)");
   m.def("prefill_attention_tc", &gsb_prefill_attention_tc, "tcgen05/TMEM prefill attention (128-row tiles)");
   m.def("peer_barrier", &gsb_peer_barrier, "bounded cross-rank barrier over P2P signal pads");
-  m.def("multimem_allreduce_bf16", &gsb_multimem_allreduce_bf16, "NVLS one-shot all-reduce (multimem)");
   m.def("rmsnorm_residual_from", &gsb_rmsnorm_residual_from, "h <- y; x <- rmsnorm(y); y <- 0");
   m.def("probe_verdict", &gsb_probe_verdict, "probe-head scores at marker rows");
   m.def("probe_rewrite", &gsb_probe_rewrite, "replace marker logit rows by the probe verdict");
@@ -41,7 +40,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_scatter_slots", &gsb_moe_scatter_slots, "MoE rows into the slots of an earlier scatter");
   m.def("moe_combine", &gsb_moe_combine, "MoE weighted sum of expert outputs (+ shared MLP, residual)");
   m.def("residual_axpy", &gsb_residual_axpy, "h <- h + y * scale");
-  m.def("allreduce_ldreduce_p2p", &gsb_allreduce_ldreduce_p2p,
-        "switch-summed slices written to every rank by P2P stores");
   m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode)");
 }

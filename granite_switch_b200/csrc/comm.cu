@@ -4,11 +4,6 @@
 //   signal pad (plain P2P st.release.sys) and waits, with a bounded spin, until
 //   all peers' epochs arrived in its own pad (ld.acquire.sys). A wait that runs
 //   out sets kErrPeerWait and returns; it never hangs.
-// * multimem_allreduce_bf16: one-shot all-reduce of a symmetric bf16 buffer
-//   through the NVSwitch: each rank reduces a 1/tp slice with
-//   multimem.ld_reduce (the switch sums every rank's copy) and multicasts the
-//   sum back with multimem.st, so every rank ends up with the full result
-//   (reduce-scatter + all-gather in one pass over NVLink).
 // * rmsnorm_residual_from: h <- y (the reduced residual stream), x <- RMSNorm(y),
 //   y <- 0 ready for the next accumulation - one pass over the row.
 // The fused row-parallel GEMM (gemm_tcgen05.cu, kEpiMultimemRed) pushes each
@@ -50,50 +45,6 @@ __global__ void peer_barrier_kernel(const uint64_t* __restrict__ pads, int rank,
       raise_error(err, kErrPeerWait);
       break;
     }
-  }
-  __threadfence_system();
-}
-
-__device__ __forceinline__ void multimem_ld_reduce_v4_bf16x2(const void* mc, uint32_t (&r)[4]) {
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.bf16x2 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "l"(mc)
-               : "memory");
-}
-__device__ __forceinline__ void multimem_st_v4(void* mc, const uint32_t (&r)[4]) {
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(mc), "r"(r[0]), "r"(r[1]),
-               "r"(r[2]), "r"(r[3])
-               : "memory");
-}
-
-// one-shot all-reduce over a multicast mapping: rank r reduces 16-byte vectors
-// [r*n/tp, (r+1)*n/tp) and stores the sums to every rank
-__global__ void multimem_allreduce_bf16_kernel(uint8_t* __restrict__ mc, int64_t n_vec, int rank, int tp) {
-  const int64_t per = (n_vec + tp - 1) / tp;
-  const int64_t lo = rank * per, hi = min(n_vec, lo + per);
-  for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hi; i += (int64_t)gridDim.x * blockDim.x) {
-    uint32_t r[4];
-    multimem_ld_reduce_v4_bf16x2(mc + i * 16, r);
-    multimem_st_v4(mc + i * 16, r);
-  }
-  __threadfence_system();  // the multicast stores precede the barrier that follows this kernel
-}
-
-// All-reduce whose result travels by plain peer stores: rank r sums its 1/tp
-// slice through the switch (multimem.ld_reduce) and writes the sums into every
-// rank's copy with ordinary P2P stores. Completion is then signalled by the P2P
-// barrier on the same path as the data (multicast stores followed by a P2P flag
-// were observed out of order by a reader that did not synchronise).
-__global__ void allreduce_ldreduce_p2p_kernel(const uint8_t* __restrict__ mc, const uint64_t* __restrict__ peers,
-                                              int64_t offset, int64_t n_vec, int rank, int tp) {
-  const int64_t per = (n_vec + tp - 1) / tp;
-  const int64_t lo = rank * per, hi = min(n_vec, lo + per);
-  for (int64_t i = lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < hi; i += (int64_t)gridDim.x * blockDim.x) {
-    uint32_t r[4];
-    multimem_ld_reduce_v4_bf16x2(mc + offset + i * 16, r);
-    const uint4 v = make_uint4(r[0], r[1], r[2], r[3]);
-    for (int p = 0; p < tp; ++p)
-      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(peers[p]) + offset + i * 16) = v;
   }
   __threadfence_system();
 }
@@ -170,35 +121,6 @@ void gsb_peer_barrier(const at::Tensor& pad_ptrs_dev, int64_t rank, int64_t tp, 
   peer_barrier_kernel<<<(::gsb::count_launch(), 1), 64, 0, st>>>(reinterpret_cast<const uint64_t*>(pad_ptrs_dev.data_ptr()), (int)rank,
                                         (int)tp, (uint32_t)epoch, (uint64_t)budget_ns,
                                         reinterpret_cast<uint32_t*>(err.data_ptr()));
-  GSB_CUDA_CHECK(cudaGetLastError());
-}
-
-void gsb_multimem_allreduce_bf16(int64_t mc_ptr, int64_t nbytes, int64_t rank, int64_t tp, const at::Tensor& like) {
-  GSB_CHECK(mc_ptr != 0 && nbytes % 16 == 0, "multimem all-reduce: multicast pointer and 16-byte size required");
-  c10::cuda::CUDAGuard g(like.device());
-  auto st = c10::cuda::getCurrentCUDAStream(like.device().index()).stream();
-  const int64_t n_vec = nbytes / 16;
-  const int64_t per = (n_vec + tp - 1) / tp;
-  const int blocks = (int)std::min<int64_t>(std::max<int64_t>(1, (per + 255) / 256), 132);
-  multimem_allreduce_bf16_kernel<<<(::gsb::count_launch(), blocks), 256, 0, st>>>(reinterpret_cast<uint8_t*>(mc_ptr), n_vec, (int)rank,
-                                                          (int)tp);
-  GSB_CUDA_CHECK(cudaGetLastError());
-}
-
-void gsb_allreduce_ldreduce_p2p(int64_t mc_ptr, const at::Tensor& peer_ptrs, int64_t offset, int64_t nbytes,
-                                int64_t rank, int64_t tp) {
-  GSB_CHECK(mc_ptr != 0 && nbytes % 16 == 0 && offset % 16 == 0,
-            "all-reduce: multicast pointer and 16-byte size/offset required");
-  GSB_CHECK(peer_ptrs.is_cuda() && peer_ptrs.scalar_type() == at::kLong && peer_ptrs.numel() >= tp,
-            "all-reduce: int64 device tensor of peer base pointers required");
-  c10::cuda::CUDAGuard g(peer_ptrs.device());
-  auto st = c10::cuda::getCurrentCUDAStream(peer_ptrs.device().index()).stream();
-  const int64_t n_vec = nbytes / 16;
-  const int64_t per = (n_vec + tp - 1) / tp;
-  const int blocks = (int)std::min<int64_t>(std::max<int64_t>(1, (per + 255) / 256), 148);
-  allreduce_ldreduce_p2p_kernel<<<(::gsb::count_launch(), blocks), 256, 0, st>>>(reinterpret_cast<const uint8_t*>(mc_ptr),
-                                                         reinterpret_cast<const uint64_t*>(peer_ptrs.data_ptr()),
-                                                         offset, n_vec, (int)rank, (int)tp);
   GSB_CUDA_CHECK(cudaGetLastError());
 }
 

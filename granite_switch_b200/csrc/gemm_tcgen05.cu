@@ -72,8 +72,6 @@ struct GemmEpiArgs {
   int mask_num_adapters;
   const uint64_t* skip_mask;   // kEpiMaskAdapter: adapters present per 128-row tile; tiles
                                // whose columns belong only to absent adapters are skipped
-  int diag;                    // pair kernel diagnostics (GSB_GEMM_DIAG): bit 0 skips the
-                               // epilogue stores, bit 1 re-reads K block 0 (L2-resident)
 };
 
 // Grouped mode (mixture-of-experts): W is a stack [E, N, K] and every 128-row
@@ -752,7 +750,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           const uint32_t fb = full_bar_leader + s * 8;
           if (i < main_blocks) {
             if (leader) mbar_arrive_expect_tx(&full_bar[s], 2 * C::STAGE_BYTES);
-            const int kx = (epi.diag & 2) ? 0 : i * C::BK;
+            const int kx = i * C::BK;
             tma_load_2d_pair(sa, &tm_a, fb, kx, m0);
             tma_load_2d_pair(sb, &tm_b, fb, kx, n0 + (int)rank * (BN / 2));
           } else {
@@ -860,12 +858,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
       tc_fence_after();
       const int row = mt * 2 * C::BM + (int)rank * C::BM + q * 32 + lane;
       const uint32_t tbase = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
-      if (!(epi.diag & 1)) {
-        if constexpr (epi_staged(EPI, BN))
-          epilogue_tile_staged<BN, EPI>(epi, &tm_out, tbase, row - lane, M, nt * BN, staging + q * 8192, sbuf);
-        else
-          epilogue_tile<BN, EPI>(epi, tbase, row, M, nt * BN);
-      }
+      if constexpr (epi_staged(EPI, BN))
+        epilogue_tile_staged<BN, EPI>(epi, &tm_out, tbase, row - lane, M, nt * BN, staging + q * 8192, sbuf);
+      else
+        epilogue_tile<BN, EPI>(epi, tbase, row, M, nt * BN);
       if (EPI == kEpiMultimemRed) __threadfence_system();
       tc_fence_before();
       __syncwarp();
@@ -975,15 +971,10 @@ static void dispatch_epi_pair(int epi_kind, const CUtensorMap& ta, const CUtenso
   }
 }
 
-// The pair kernel serves 256-wide tiles of large-M GEMMs: M >= the threshold
-// below (GSB_GEMM_PAIR_MIN_M, default 512; GSB_GEMM_PAIR=0 or a negative
-// threshold keeps every GEMM on the single-CTA kernel).
-static int g_pair_min_m = []() {
-  const char* off = getenv("GSB_GEMM_PAIR");
-  if (off != nullptr && off[0] == '0') return -1;
-  const char* v = getenv("GSB_GEMM_PAIR_MIN_M");
-  return v != nullptr ? atoi(v) : 512;
-}();
+// The pair kernel serves 256-wide tiles of large-M GEMMs: M >= this threshold
+// (gemm_pair_min_m() changes it at run time for A/B tests; a negative value
+// keeps every GEMM on the single-CTA kernel).
+static int g_pair_min_m = 512;
 
 static bool pair_enabled(int M, int bn, int epi_kind) {
   if (g_pair_min_m < 0 || bn != 256 || M < g_pair_min_m) return false;
@@ -1060,11 +1051,9 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int parts, in
   *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(out) + (int64_t)row * ldo + c) = pack_bf16x2(v0, v1);
 }
 
-// Split-K is used below this many output tiles (half the SMs); 0 turns it off.
-static int g_splitk_max_tiles = [] {
-  const char* v = getenv("GSB_GEMM_SPLITK_MAX_TILES");
-  return v != nullptr ? atoi(v) : 74;
-}();
+// Split-K is used below this many output tiles (half the SMs); 0 turns it off
+// (gemm_splitk_max_tiles() changes it at run time for A/B tests).
+static int g_splitk_max_tiles = 74;
 
 // Parts for a single-CTA GEMM of `tiles` output tiles and `kblocks` 64-deep K
 // blocks: the largest of 4 / 3 / 2 that divides kblocks, leaves at least four
@@ -1165,11 +1154,6 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     }
   }
   GemmEpiArgs epi{};
-  static const int diag = []() {
-    const char* v = getenv("GSB_GEMM_DIAG");
-    return v != nullptr ? atoi(v) : 0;
-  }();
-  epi.diag = diag;
   epi.out = (epi_kind == kEpiMultimemRed && mc_out != 0) ? reinterpret_cast<void*>(mc_out) : out.data_ptr();
   epi.ldo = out.stride(0);
   epi.scale = (float)scale;

@@ -50,7 +50,6 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
                               const c10::optional<at::Tensor>& ws_lse);
 void gsb_peer_barrier(const at::Tensor& pad_ptrs_dev, int64_t rank, int64_t tp, int64_t epoch, int64_t budget_ns,
                       const at::Tensor& err);
-void gsb_multimem_allreduce_bf16(int64_t mc_ptr, int64_t nbytes, int64_t rank, int64_t tp, const at::Tensor& like);
 void gsb_rmsnorm_residual_from(const at::Tensor& y, const at::Tensor& h, const at::Tensor& w, const at::Tensor& x,
                                double eps);
 void gsb_probe_verdict(const at::Tensor& hidden, const at::Tensor& rows, const at::Tensor& slots,
@@ -68,8 +67,6 @@ void gsb_moe_combine(const at::Tensor& yp, const at::Tensor& slot, const at::Ten
                      const c10::optional<at::Tensor>& shared, const c10::optional<at::Tensor>& residual, double scale,
                      const at::Tensor& out);
 void gsb_residual_axpy(const at::Tensor& h, const at::Tensor& y, double scale);
-void gsb_allreduce_ldreduce_p2p(int64_t mc_ptr, const at::Tensor& peer_ptrs, int64_t offset, int64_t nbytes,
-                                int64_t rank, int64_t tp);
 int64_t gsb_attn_packed(int64_t v);
 int64_t gsb_gemm_splitk_max_tiles(int64_t v);
 int64_t gsb_attn_decode_stages(int64_t v);

@@ -132,6 +132,9 @@ class NativeExecutor:
         self.h_bt = torch.zeros(s, self.max_blocks, dtype=torch.int32, **pin)
         self.h_rows = torch.empty(s, dtype=torch.long, **pin)
         self.h_out = torch.empty(s, dtype=torch.long, **pin)
+        # device error word (bits, bad-index site, index), read back with each step's ids
+        self.h_err = torch.zeros(3, dtype=torch.int32, **pin)
+        self.d_err = torch.zeros(3, dtype=torch.int32, device=model.device)
         dev = self.device
         self.d_i64 = torch.empty(3 * t, dtype=torch.long, device=dev)
         self.d_i32 = torch.empty(3 * s + 1, dtype=torch.int32, device=dev)
@@ -345,7 +348,12 @@ class NativeExecutor:
 
         hb, logits = self.compute_logits(out)
         nb = len(hb.rows)
-        if nb == 0:
+        if nb == 0:  # no row samples (prefill chunks only): still check the step's kernels
+            self._stage_error_word()
+            self.copy_event.record()
+            self.copy_event.synchronize()
+            self.d2h_bytes += 12
+            self._raise_device_error()
             return []
         toks = self.d_tokens[:nb]
         pipe = self.model.pipeline
@@ -357,11 +365,46 @@ class NativeExecutor:
                 sample(logits, params, [c.req for c in hb.chunks if c.needs_sample], out=toks)
         if pipe is not None:
             pipe.broadcast_tokens(toks)  # every stage's scheduler sees the sampled ids
+        self._stage_error_word()
         self.h_out[:nb].copy_(toks, non_blocking=True)
         self.copy_event.record()
         self.copy_event.synchronize()
-        self.d2h_bytes += 8 * nb
+        self.d2h_bytes += 8 * nb + 12
+        self._raise_device_error()
         return self.h_out[:nb].tolist()
+
+    def _stage_error_word(self) -> None:
+        """Queue the copy of the device error word next to the sampled ids.
+
+        Under tensor or pipeline parallelism the word is max-reduced over the
+        model's ranks first, so every rank sees a failure in the same step and
+        the ranks stay in lock step when the engine aborts that step.
+        """
+        from .._native import err_buffer
+
+        err = err_buffer(self.device)
+        self.d_err.copy_(err[:3])
+        group = None
+        if self.model.pipeline is not None:
+            group = torch.distributed.group.WORLD
+        elif self.tp_size > 1:
+            group = self.tp_group
+        if group is not None:
+            torch.distributed.all_reduce(self.d_err, op=torch.distributed.ReduceOp.MAX, group=group)
+        self.h_err.copy_(self.d_err, non_blocking=True)
+
+    def _raise_device_error(self) -> None:
+        """After the step's copies landed: raise :class:`DeviceError` if a kernel reported one
+        (and clear the device word, so the engine can go on with other requests)."""
+        word = int(self.h_err[0])
+        if not word:
+            return
+        from .._native import DeviceError, err_buffer, site_name
+
+        site, idx = int(self.h_err[1]), int(self.h_err[2])
+        err_buffer(self.device).zero_()
+        self.h_err.zero_()
+        raise DeviceError(word, site_name(site), idx if site else None)
 
 
 class ReferenceExecutor:

@@ -8,6 +8,7 @@ tokens) is identical on all ranks.
 """
 from __future__ import annotations
 
+import logging
 import os
 import time
 from dataclasses import dataclass, field
@@ -15,12 +16,15 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
+from .._native import DeviceError
 from ..config import GraniteSwitchConfig
 from ..routing.scan import expert_table
 from .kv_cache import BLOCK_SIZE, BlockManager
-from .request import Request, RequestOutput, SamplingParams
+from .request import Request, RequestOutput, RequestStatus, SamplingParams
 from .scheduler import Scheduler
 
+
+_log = logging.getLogger(__name__)
 
 # Engine steps a cold request may be passed over under cache-affinity admission
 # before it goes first (about a minute of 8B-shape steps on one B200).
@@ -55,6 +59,9 @@ class EngineStats:
     finished: int = 0
     ttfts: list = field(default_factory=list)
     latencies: list = field(default_factory=list)
+    device_errors: int = 0   # steps aborted because a kernel reported an error
+    prefill_tokens: int = 0  # tokens computed in prefill chunks (prompt tokens not served from cache)
+    decode_rows: int = 0     # single-token decode rows
 
 
 class HostRouter:
@@ -139,7 +146,16 @@ class LLMEngine:
             return []
         if self.health is not None:
             self.health.check()  # a dead peer is reported here, not inside a collective
-        tokens = self.executor.execute(out)
+        for c in out.chunks:
+            if c.num_tokens > 1 or c.req.prefilling:
+                self.stats.prefill_tokens += c.num_tokens
+            else:
+                self.stats.decode_rows += c.num_tokens
+        try:
+            tokens = self.executor.execute(out)
+        except DeviceError as e:
+            self._abort_step(out, e)
+            raise
         if self.health is not None:
             self.health.beat()
         now = time.perf_counter()
@@ -174,6 +190,28 @@ class LLMEngine:
                     self.on_finish(r)
         self.stats.steps += 1
         return finished
+
+    def _abort_step(self, out, err) -> None:
+        """A kernel of this step reported an error: its outputs cannot be trusted.
+
+        Every request the step carried is finished with reason ``"error"`` (its
+        blocks freed, never published), and the prefix cache is dropped: a bad
+        index is replaced by entry 0 on the device, so a cached page may have
+        been overwritten. Other waiting and running requests go on.
+        """
+        now = time.perf_counter()
+        self.stats.device_errors += 1
+        for c in out.chunks:
+            r = c.req
+            if r.status == RequestStatus.FINISHED:
+                continue
+            r.finish_time = now
+            self.scheduler.finish(r, "error")
+            self.requests.pop(r.request_id, None)
+        for r in list(self.scheduler.running):  # their pages are suspect too: recompute them
+            self.scheduler.preempt(r)
+        self.blocks.reset_prefix_cache()
+        _log.error("engine step aborted %d request(s): %s", len(out.chunks), err)
 
     def _stop_reason(self, r: Request, tok: int) -> str | None:
         sp = r.sampling

@@ -79,6 +79,8 @@ class Scheduler:
         self.num_preemptions = 0
         self.max_wait_steps = max_wait_steps
         self.steps = 0
+        self.num_admitted = 0       # requests admitted from the waiting queues (first admissions)
+        self.num_admitted_cold = 0  # ... of which no prompt block was found in the prefix cache
 
     def add(self, req: Request) -> None:
         req.status = RequestStatus.WAITING
@@ -95,7 +97,7 @@ class Scheduler:
     def has_work(self) -> bool:
         return bool(self.waiting or self.warm or self.running)
 
-    def _preempt(self, req: Request, out: SchedulerOutput) -> None:
+    def _preempt(self, req: Request, out: SchedulerOutput | None) -> None:
         self.running.remove(req)
         self.blocks.free_request(req)
         req.num_computed = 0
@@ -104,8 +106,14 @@ class Scheduler:
         req.status = RequestStatus.PREEMPTED
         # resumes first: its computed blocks stay cached until evicted
         (self.warm if self.policy == "cache_affinity" else self.waiting).appendleft(req)
-        out.preempted.append(req)
+        if out is not None:
+            out.preempted.append(req)
         self.num_preemptions += 1
+
+    def preempt(self, req: Request) -> None:
+        """Free a running request's blocks and queue it to recompute from its prompt and
+        generated tokens (ahead of other waiting requests)."""
+        self._preempt(req, None)
 
     def _next_queue(self) -> deque:
         if not self.warm:
@@ -153,6 +161,8 @@ class Scheduler:
                 hit = self.blocks.match_prefix(req)
                 req.num_computed = hit
                 req.num_cached_tokens = hit
+                self.num_admitted += 1
+                self.num_admitted_cold += int(hit == 0)
                 req.carry = self.route_fn(req.prompt_ids[:hit], 0) if (self.route_fn and hit) else 0
             remaining = req.num_tokens - req.num_computed
             n = min(remaining, budget) if self.chunked else remaining

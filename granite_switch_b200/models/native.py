@@ -108,8 +108,8 @@ class NativeGraniteSwitch:
         self.remaps: torch.Tensor | None = None
         self.comm = None  # optional fused-collective communicator
         self.prof = None  # optional per-op CUDA-event profiler (utils.step_profile.StepProfiler)
-        # prefill attention on tcgen05 (head_dim 64 / 128); GSB_ATTN_TC=0 selects the mma.sync kernel
-        self.use_tc_attention = os.environ.get("GSB_ATTN_TC", "1") != "0"
+        # prefill attention on tcgen05 (head_dim 64 / 128); False selects the mma.sync kernel (A/B tests)
+        self.use_tc_attention = True
         self.err = err_buffer(device)
         na = config.num_adapters
         self.num_adapters = na

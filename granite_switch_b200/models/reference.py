@@ -26,8 +26,7 @@ from torch.nn import functional as F
 
 from ..config import SWITCH_CACHE_LAYERS, GraniteSwitchConfig
 from ..routing.codebook import KerdockDGCodeGenerator
-from ..routing.probe_routing import build_adapter_kind_lut, split_adapter_indices
-from ..routing.scan import expert_table, route_sequence
+from ..routing.scan import expert_table, probe_slot_mask, route_sequence, split_probe_stream
 from ..routing.token_exchange import apply_token_exchange, build_control_to_substitute_lut
 from .layers import (
     MergedSwitchedLoRALinear,
@@ -86,7 +85,7 @@ class GraniteSwitchRouter(nn.Module):
             self.register_buffer("control_to_substitute_lut", lut, persistent=True)
         else:
             self.control_to_substitute_lut = None
-        kind = build_adapter_kind_lut(config)
+        kind = probe_slot_mask(getattr(config, "adapter_kinds", None))
         if kind is not None:
             self.register_buffer("adapter_kind_lut", kind, persistent=True)
         else:
@@ -118,7 +117,7 @@ class GraniteSwitchRouter(nn.Module):
         return out, modified, new_carry
 
     def split_indices(self, adapter_indices: torch.Tensor):
-        return split_adapter_indices(self.adapter_kind_lut, adapter_indices)
+        return split_probe_stream(adapter_indices, self.adapter_kind_lut)
 
 
 class SwitchedProbeHead(nn.Module):

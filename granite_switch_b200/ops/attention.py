@@ -2,7 +2,6 @@
 from __future__ import annotations
 
 import math
-import os
 
 import torch
 
@@ -12,8 +11,8 @@ NUM_SMS = 148
 
 #: rows per CTA of the tcgen05 prefill attention the engine uses: 128 (one query
 #: tile per CTA), 256 (two query tiles per CTA sharing each K/V tile) or 0 (chosen
-#: per step by :func:`tc_rows_for`)
-TC_ROWS = int(os.environ.get("GSB_ATTN_TC_ROWS", "0"))
+#: per step by :func:`tc_rows_for`); A/B tests assign it
+TC_ROWS = 0
 
 
 def tc_rows_for(q_lens: list[int], kv_lens: list[int]) -> int:

@@ -21,14 +21,14 @@ the NCCL all-reduce path. Buffers come from ``torch.distributed._symmetric_memor
 """
 from __future__ import annotations
 
-import os
-
 import torch
 
 from .._native import err_buffer, native
 from ..ops import gemm as G
 
 BARRIER_BUDGET_NS = 5_000_000_000
+# largest step (rows) whose reduction rides in the GEMM epilogue, per TP size (default 256)
+RED_MAX_TOKENS = {2: 1 << 20, 4: 1024}
 
 
 def _multicast_supported(device: torch.device) -> bool:
@@ -41,7 +41,7 @@ def _multicast_supported(device: torch.device) -> bool:
 
 
 class FusedTPComm:
-    def __init__(self, group, device: torch.device, max_tokens: int, hidden: int):
+    def __init__(self, group, device: torch.device, max_tokens: int, hidden: int, red_max_tokens: int | None = None):
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
 
@@ -65,14 +65,7 @@ class FusedTPComm:
         self.epoch = 0
         # rows up to which the reduction rides in the GEMM epilogue (see row_parallel);
         # from the collective sweep: always at TP=2, small steps only at TP=4 / 8
-        default = {2: 1 << 20, 4: 1024}.get(self.world, 256)
-        self.red_max_tokens = int(os.environ.get("GSB_TP_RED_MAX_TOKENS", str(default)))
-        # large steps reduce through NCCL; GSB_TP_SWITCH_ALLREDUCE=1 selects the switch
-        # all-reduce kernel instead (under investigation, see the TP self-check)
-        self.switch_allreduce = os.environ.get("GSB_TP_SWITCH_ALLREDUCE", "0") == "1"
-        # diagnostics: compare every switch all-reduce with NCCL on a copy of the partial
-        self.debug_compare = os.environ.get("GSB_TP_DEBUG_COMPARE", "0") == "1"
-        self.calls = 0
+        self.red_max_tokens = red_max_tokens if red_max_tokens is not None else RED_MAX_TOKENS.get(self.world, 256)
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
 
@@ -109,33 +102,8 @@ class FusedTPComm:
                 model._proj(pl, x, y, epi=G.EPI_RESADD, residual=resid, scale=mult)
             else:
                 model._proj(pl, x, y, epi=G.EPI_STORE, scale=mult)
-            if self.switch_allreduce:
-                chk = y.clone() if self.debug_compare else None
-                self.barrier()
-                native().allreduce_ldreduce_p2p(self.mc, self.y_ptrs, b * self.max_tokens * self.hidden * 2,
-                                                m * self.hidden * 2, self.rank, self.world)
-                self.barrier()
-                if chk is not None:
-                    self._compare(y, chk, b)
-            else:
-                torch.distributed.all_reduce(y, group=self.group)
+            torch.distributed.all_reduce(y, group=self.group)
         return y
-
-    def _compare(self, y: torch.Tensor, partial: torch.Tensor, b: int) -> None:
-        """Diagnostics: this rank's switch all-reduce result vs NCCL's sum of the same
-        partials, and this rank's result vs rank 0's (every rank must hold the same sum)."""
-        import torch.distributed as dist
-
-        dist.all_reduce(partial, group=self.group)
-        d = (y.float() - partial.float()).abs()
-        bad = (d > 1e-2 * partial.float().abs().amax() + 1e-3).nonzero()
-        y0 = y.clone()
-        dist.broadcast(y0, src=dist.get_global_rank(self.group, 0), group=self.group)
-        first = bad[0].tolist() if len(bad) else None
-        print(f"[tp-compare] rank {self.rank} call {self.calls} buf {b} m {y.shape[0]} "
-              f"max_diff_vs_nccl {float(d.max()):.4g} bad {len(bad)} first {first} "
-              f"max_diff_vs_rank0 {float((y.float() - y0.float()).abs().max()):.4g}", flush=True)
-        self.calls += 1
 
     def finish(self, y: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor, x: torch.Tensor, eps: float) -> None:
         """``h <- y; x <- RMSNorm(y) * norm_w; y <- 0``."""

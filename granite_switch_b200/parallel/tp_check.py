@@ -36,7 +36,7 @@ def _config():
     return GraniteSwitchConfig(**cfg)
 
 
-def _run(config, device, tp, rank, group, fused, red_max_tokens=None):
+def _run(config, device, tp, rank, group, fused, red_max_tokens=None, lora=("qkv", "o")):
     from ..engine import EngineConfig
     from ..engine.executor import NativeExecutor
     from ..engine.kv_cache import BlockManager
@@ -45,7 +45,6 @@ def _run(config, device, tp, rank, group, fused, red_max_tokens=None):
     from ..engine.scheduler import Scheduler
     from ..models.native import NativeGraniteSwitch
 
-    lora = tuple(x for x in os.environ.get("GSB_TPCHECK_LORA", "qkv,o").split(",") if x)
     m = NativeGraniteSwitch.from_random(config, device, max_tokens=512, num_kv_blocks=256,
                                         lora_modules=lora, rank=16, seed=7, tp_rank=rank, tp_size=tp,
                                         tp_group=group, max_seqs=16)
@@ -101,24 +100,14 @@ def _check_primitives(device, group, rank, world) -> dict:
     want = part.clone()
     dist.all_reduce(want, group=group)
     mc0 = comm.mc
-    for name in ("plain_store+allreduce", "gemm_store+allreduce", "gemm_multimem_red"):
-        y = comm.y[0, :m]
-        y.zero_()
-        torch.cuda.synchronize()
-        dist.barrier(group=group)
-        if name == "plain_store+allreduce":
-            y.copy_(part)
-        elif name == "gemm_store+allreduce":
-            G.switched_gemm(x, w, y)
-        else:
-            G.switched_gemm(x, w, y, epi=G.EPI_MULTIMEM_RED, mc_out=mc0)
-        comm.barrier()
-        if name != "gemm_multimem_red":
-            native().allreduce_ldreduce_p2p(mc0, comm.y_ptrs, 0, m * h * 2, rank, world)
-            comm.barrier()
-        torch.cuda.synchronize()
-        err = ((y.float() - want.float()).abs().max() / want.float().abs().max()).item()
-        out[name] = round(err, 5)
+    y = comm.y[0, :m]
+    y.zero_()
+    torch.cuda.synchronize()
+    dist.barrier(group=group)
+    G.switched_gemm(x, w, y, epi=G.EPI_MULTIMEM_RED, mc_out=mc0)
+    comm.barrier()
+    torch.cuda.synchronize()
+    out["gemm_multimem_red"] = round(((y.float() - want.float()).abs().max() / want.float().abs().max()).item(), 5)
     # the model's sequence: three projections back to back through row_parallel + finish
     # (alternating buffers, rank 0 folds in the residual), no host synchronisation
     class _M:
@@ -145,7 +134,13 @@ def _check_primitives(device, group, rank, world) -> dict:
     return out
 
 
-def main() -> int:
+def main(argv=None) -> int:
+    import argparse
+
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--lora", default="qkv,o", help="comma-separated LoRA modules of the check model")
+    args = ap.parse_args(argv)
+    lora = tuple(x for x in args.lora.split(",") if x)
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -159,18 +154,18 @@ def main() -> int:
         print(json.dumps({"primitives": prim}), flush=True)
     dist.barrier()
     results = {}
-    nccl = _run(config, device, world, rank, group, fused=False)
+    nccl = _run(config, device, world, rank, group, fused=False, lora=lora)
     results["nccl"] = nccl
     dist.barrier()
-    fused = _run(config, device, world, rank, group, fused=True)
+    fused = _run(config, device, world, rank, group, fused=True, lora=lora)
     results["fused"] = fused
     dist.barrier()
     # every reduction on the large-step path (partial stored, NCCL all-reduce)
-    results["fused_allreduce"] = _run(config, device, world, rank, group, fused=True, red_max_tokens=0)
+    results["fused_allreduce"] = _run(config, device, world, rank, group, fused=True, red_max_tokens=0, lora=lora)
     dist.barrier()
     ok = True
     if rank == 0:
-        ref, _ = _run(config, device, 1, 0, None, fused=False)
+        ref, _ = _run(config, device, 1, 0, None, fused=False, lora=lora)
         for mode, res in results.items():
             if res is None:
                 print(json.dumps({"mode": mode, "skipped": "no NVLS multicast support"}), flush=True)

@@ -112,20 +112,6 @@ def main() -> int:
                     G.switched_gemm(y, wq, qkv)
                 y.zero_()  # the consumer clears the buffer before its next use
 
-            def fused_ar(col=False):
-                # GEMM stores the partial locally, then the switch all-reduce between two barriers
-                b = comm.turn
-                comm.turn ^= 1
-                y = comm.y[b, :m]
-                mc = comm.mc + b * comm.max_tokens * comm.hidden * 2
-                G.switched_gemm(x, w, y, scale=1.0)
-                comm.barrier()
-                native().allreduce_ldreduce_p2p(comm.mc, comm.y_ptrs, b * comm.max_tokens * comm.hidden * 2,
-                                                m * H * 2, comm.rank, comm.world)
-                comm.barrier()
-                if col:
-                    G.switched_gemm(y, wq, qkv)
-
             def baseline(col=False):
                 torch.matmul(x, w.t(), out=ybase)
                 dist.all_reduce(ybase, group=group)
@@ -135,9 +121,8 @@ def main() -> int:
             flops = 2.0 * m * k * H
             bytes_link = 2.0 * (world - 1) / world * m * H * 2
             res = {}
-            for tag, fn in (("fused", lambda: fused()), ("fused_ar", lambda: fused_ar()),
-                            ("baseline", lambda: baseline()), ("fused+col", lambda: fused(True)),
-                            ("fused_ar+col", lambda: fused_ar(True)), ("baseline+col", lambda: baseline(True))):
+            for tag, fn in (("fused", lambda: fused()), ("baseline", lambda: baseline()),
+                            ("fused+col", lambda: fused(True)), ("baseline+col", lambda: baseline(True))):
                 ms = _time(fn, args.iters, group)
                 fl = flops + (2.0 * m * H * (QKV // world) if tag.endswith("+col") else 0.0)
                 roof_ms = max(fl / (peak * 1e9), bytes_link / (LINK_GBS * 1e6))

@@ -33,6 +33,33 @@ def expert_table(adapter_token_ids: list[int], num_adapters: int, vocab_hint: in
     return tbl
 
 
+def probe_slot_mask(adapter_kinds) -> torch.Tensor | None:
+    """Which expert ids belong to probe slots: ``bool[len(adapter_kinds) + 1]`` (entry 0 is
+    the base), or ``None`` when no slot is a probe.
+
+    This is the persisted ``model.switch.adapter_kind_lut`` buffer of composed
+    checkpoints. The native routing kernel reads the same mask (its ``kind_lut``).
+    """
+    kinds = list(adapter_kinds or [])
+    if "probe" not in kinds:
+        return None
+    return torch.tensor([False] + [kind == "probe" for kind in kinds], dtype=torch.bool)
+
+
+def split_probe_stream(adapter_index: torch.Tensor, mask: torch.Tensor | None):
+    """``(lora_index, probe_index)`` from the routed expert ids.
+
+    A token routed to a probe slot runs no LoRA delta (its LoRA index is 0) and
+    carries the slot in the probe stream; every other token keeps its expert in
+    the LoRA stream and 0 in the probe stream. Same rule as the routing kernel
+    (csrc/routing.cu); reference behaviour: src/granite_switch/probe_routing.py:36-58.
+    """
+    if mask is None:
+        return adapter_index, torch.zeros_like(adapter_index)
+    sel = mask.to(adapter_index.device)[adapter_index].to(adapter_index.dtype)
+    return adapter_index * (1 - sel), adapter_index * sel
+
+
 def route_sequence(token_ids: list[int] | torch.Tensor, table: torch.Tensor, carry: int = 0) -> tuple[torch.Tensor, int]:
     """Route one request chunk. Returns ``(adapter_index[int64], new_carry)``."""
     ids = torch.as_tensor(token_ids, dtype=torch.long)

@@ -12,6 +12,7 @@ import threading
 import time
 from dataclasses import dataclass, field
 
+from .._native import DeviceError
 from ..engine.request import Request, SamplingParams
 
 
@@ -118,7 +119,12 @@ def follow(engine, group) -> None:
         if p["stop"]:
             return
         if p["step"]:
-            engine.step()
+            try:
+                engine.step()
+            except DeviceError:
+                # every rank sees the same (max-reduced) error word and aborts the same
+                # step; rank 0 then publishes the aborts of its remaining requests
+                pass
 
 
 class AsyncEngine:

@@ -2,7 +2,8 @@
 
 ``python -m granite_switch_b200.utils.kernel_cases <case>`` with case in
 gemm, gemm_pair, gemm_single, cublas, swiglu, attn_prefill64, moe, probe, decode_gemm, attn_prefill, attn_decode, rmsnorm, rope, embed,
-routing, sample (or ``all``). Pair it with ``ncu -k regex:<kernel> -c 1``.
+routing, sample (or ``all``). Pair it with ``ncu --clock-control none -k regex:<kernel> -c 1`` (without
+``--clock-control none`` ncu locks the GPU clocks).
 """
 import sys
 

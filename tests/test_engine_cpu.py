@@ -318,3 +318,49 @@ def test_cache_affinity_raises_hit_rate_under_overload():
 
     fcfs, affinity = run("fcfs"), run("cache_affinity")
     assert affinity > fcfs + 0.2, (fcfs, affinity)
+
+
+def test_device_error_aborts_the_step(tiny_dir):
+    """A kernel error reported in a step (here: the executor's error word, faked) aborts the
+    requests that step carried, drops the prefix cache and re-raises; the engine then keeps
+    serving the other requests, whose outputs still match plain generate."""
+    from granite_switch_b200._native import ERR_ATTN_WAIT, DeviceError
+
+    prompts = _prompts(tiny_dir, 4, seed=3)
+    ecfg = EngineConfig(max_num_seqs=2, max_num_batched_tokens=1024, num_kv_blocks=64, max_model_len=256)
+    llm = LLM(tiny_dir, device="cpu", engine_config=ecfg)
+    eng = llm.engine
+    real = eng.executor.execute
+    calls = {"n": 0}
+
+    def flaky(out):
+        calls["n"] += 1
+        if calls["n"] == 3:  # third step: the kernels report an attention wait that ran out
+            raise DeviceError(ERR_ATTN_WAIT, "attention page id", 7)
+        return real(out)
+
+    eng.executor.execute = flaky
+    reqs = [eng.add_request(p, SamplingParams(max_tokens=6)) for p in prompts]
+    errors = []
+    while eng.has_unfinished():
+        try:
+            eng.step()
+        except DeviceError as e:
+            errors.append(e)
+    assert len(errors) == 1 and "attention-wait-timeout" in str(errors[0]) and "attention page id = 7" in str(errors[0])
+    assert eng.stats.device_errors == 1
+    failed = [r for r in reqs if r.finish_reason == "error"]
+    ok = [r for r in reqs if r.finish_reason == "length"]
+    assert failed and ok and len(failed) + len(ok) == len(reqs)
+    ref = _ref_generate(tiny_dir, [r.prompt_ids for r in ok], 6)
+    assert [r.output_ids for r in ok] == ref
+
+
+def test_executor_error_word_check():
+    """The executor turns a nonzero error word into DeviceError with the site decoded."""
+    from granite_switch_b200._native import ERR_BAD_SHAPE, DeviceError, describe_error, site_name
+
+    assert site_name(0) is None and site_name(3) == "KV slot"
+    e = DeviceError(ERR_BAD_SHAPE, site_name(3), 99)
+    assert "bad-shape" in str(e) and "KV slot = 99" in str(e) and e.word == ERR_BAD_SHAPE
+    assert describe_error(0x3).count("timeout") == 2

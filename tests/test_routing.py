@@ -6,12 +6,12 @@ import torch
 
 from granite_switch_b200.routing import (
     apply_token_exchange,
-    build_adapter_kind_lut,
     build_control_to_substitute_lut,
     expert_table,
+    probe_slot_mask,
     route_flat,
     route_sequence,
-    split_adapter_indices,
+    split_probe_stream,
 )
 from granite_switch_b200.routing.codebook import KerdockDGCodeGenerator, verify_coherence
 from granite_switch_b200.routing.coded_switch import coded_switch_route
@@ -113,8 +113,10 @@ def test_token_exchange_and_probe_split():
     assert lut.numel() == 52 and lut[50] == 7 and lut[51] == 8 and lut[3] == -1
     ids = torch.tensor([[1, 50, 2, 51, 60]])
     assert apply_token_exchange(lut, ids).tolist() == [[1, 7, 2, 8, 60]]
-    kind = build_adapter_kind_lut(_Cfg)
-    lora, probe = split_adapter_indices(kind, torch.tensor([0, 1, 2, 1]))
+    kind = probe_slot_mask(_Cfg.adapter_kinds)
+    assert kind.tolist() == [False, False, True]
+    assert probe_slot_mask(["lora", "lora"]) is None
+    lora, probe = split_probe_stream(torch.tensor([0, 1, 2, 1]), kind)
     assert lora.tolist() == [0, 1, 0, 1] and probe.tolist() == [0, 0, 2, 0]
 
 
