@@ -56,7 +56,9 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--list-adapters", action="store_true")
     p.add_argument("--debug-fields", action="store_true")
     p.add_argument("--create-ioyaml", action="store_true")
-    p.add_argument("--dtype", default="bfloat16", choices=["bfloat16", "float16", "float32"])
+    p.add_argument("--dtype", default=None, choices=["bfloat16", "float16", "float32"],
+                   help="weight dtype of the composed checkpoint (default: the base config's dtype, else float32, "
+                        "as the reference's composer)")
     p.add_argument("--enable-audio", action="store_true")
     p.add_argument("--asr-model", default=None)
     p.add_argument("--asr-revision", default=None)
@@ -112,6 +114,9 @@ def _probe_adapter(found, tokenizer) -> AdapterSpec:
                        probe_weight=sd.get("weight"), probe_bias=sd.get("bias"), source=found.path)
 
 
+_TOKENIZER_FILES = ("tokenizer.json", "tokenizer_config.json", "vocab.json", "tokenizer.model")
+
+
 def compose_main(argv=None) -> int:
     args = build_argparser().parse_args(argv)
     base_path = _resolve_local(args.base_model) if not args.list_adapters else args.base_model
@@ -125,12 +130,14 @@ def compose_main(argv=None) -> int:
         return 0
     t0 = time.time()
     tokenizer = None
-    try:
-        from transformers import AutoTokenizer
+    # a directory without tokenizer files would give an empty placeholder tokenizer
+    if any(os.path.exists(os.path.join(base_path, f)) for f in _TOKENIZER_FILES):
+        try:
+            from transformers import AutoTokenizer
 
-        tokenizer = AutoTokenizer.from_pretrained(base_path)
-    except Exception:
-        tokenizer = None
+            tokenizer = AutoTokenizer.from_pretrained(base_path)
+        except Exception:
+            tokenizer = None
     adapters: list[AdapterSpec] = []
     for f in found:
         if f.kind == "probe":
@@ -175,13 +182,16 @@ def compose_main(argv=None) -> int:
                      asr_chunk_overlap_s=args.asr_chunk_overlap_s, asr_self_chunks=args.asr_self_chunks)
         if args.bundle_asr:
             extra["asr_bundled_path"] = "asr"
-    dtype = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}[args.dtype]
+    dtype_name = args.dtype or str(base_cfg.get("torch_dtype") or base_cfg.get("dtype") or "float32")
+    dtype = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}[
+        dtype_name.replace("torch.", "")]
     config = compose_checkpoint(base_cfg, base_sd, adapters, args.output, dtype=dtype,
                                 base_reset=args.base_reset_token, base_model_name=args.base_model,
                                 ms_code_m=args.ms_code_m or 6, ms_memory_gain=args.ms_memory_gain or 28.0,
                                 switch_head_dim=args.switch_head_dim or 32, extra_config=extra,
                                 control_token_ids=ctrl_ids, reserved_output_row=reserved_row,
-                                default_substitute=default_sub, extra_token_ids=extra_ids)
+                                default_substitute=default_sub, extra_token_ids=extra_ids,
+                                vocab_size=len(tokenizer) if tokenizer is not None else None)
     if tokenizer is not None:
         tokenizer.save_pretrained(args.output)
     io_dir = os.path.join(args.output, "io_configs")

@@ -80,9 +80,13 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
                        switch_head_dim: int = 32, extra_config: dict | None = None,
                        max_shard_bytes: int = 5 * 1024 ** 3,
                        control_token_ids: list[int] | None = None,
-                       extra_token_ids: list[int] | None = None) -> GraniteSwitchConfig:
+                       extra_token_ids: list[int] | None = None,
+                       vocab_size: int | None = None) -> GraniteSwitchConfig:
     """``extra_token_ids``: other added tokens that need an embedding row and a
-    never-emitted output row (the audio marker), like the control tokens."""
+    never-emitted output row (the audio marker), like the control tokens.
+    ``vocab_size``: rows of the composed embedding (the tokenizer's length after
+    the control tokens were added, as the reference's resize does; rows past it
+    are dropped); by default the base rows, grown to cover the added ids."""
     na = len(adapters)
     cfg = dict(base_config)
     base_vocab = int(cfg["vocab_size"])
@@ -128,6 +132,10 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
             subs.append(default_substitute if default_substitute is not None else 0)
     extra_ids = [int(t) for t in (extra_token_ids or [])]
     new_vocab = max([base_vocab] + [t + 1 for t in ctrl_ids + extra_ids])
+    if vocab_size is not None:
+        if vocab_size < max([0] + [t + 1 for t in ctrl_ids + extra_ids]):
+            raise ValueError(f"vocab_size {vocab_size} does not cover the added token ids")
+        new_vocab = int(vocab_size)
     ranks = [a.max_rank() if a.kind == "lora" else 1 for a in adapters]
     max_rank = max(ranks) if ranks else 8
     kinds = [a.kind for a in adapters]
@@ -185,7 +193,7 @@ def compose_checkpoint(base_config: dict, base_state: dict[str, torch.Tensor], a
         if new_vocab > t.shape[0]:
             t = torch.cat([t, t[reserved:reserved + 1].expand(new_vocab - t.shape[0], -1).clone()], 0)
         else:
-            t = t.clone()
+            t = t[:new_vocab].clone()
         if ctrl_ids or extra_ids:
             t[torch.tensor(ctrl_ids + extra_ids, dtype=torch.long)] = t[reserved].clone()
         sd[key] = t

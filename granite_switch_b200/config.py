@@ -113,6 +113,16 @@ class GraniteSwitchConfig:
         extra = dict(kwargs)
         for k, v in _BASE_DEFAULTS.items():
             setattr(self, k, extra.pop(k, v))
+        # transformers 5 serialises RoPE as ``rope_parameters`` and the dtype as
+        # ``dtype`` (the reference's composer writes these); both stay in the
+        # extra keys so they round-trip
+        rp = extra.get("rope_parameters")
+        if isinstance(rp, dict) and "rope_theta" not in kwargs and rp.get("rope_theta") is not None:
+            self.rope_theta = float(rp["rope_theta"])
+            if rp.get("rope_type") not in (None, "default") and self.rope_scaling is None:
+                self.rope_scaling = {k: v for k, v in rp.items() if k != "rope_theta"}
+        if extra.get("dtype") is not None and "torch_dtype" not in kwargs:
+            self.torch_dtype = str(extra["dtype"]).replace("torch.", "")
         # derived / placeholder values that the reference's parent class provides
         if self.attention_multiplier is None:
             hd = self.head_dim or (self.hidden_size // self.num_attention_heads)

@@ -20,6 +20,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "granite_switch_b200 sm_100a kernels";
   m.def("switched_gemm", &gsb_switched_gemm, "tcgen05 GEMM with fused switched-LoRA expand");
   m.def("gemm_pair_min_m", &gsb_gemm_pair_min_m, "set the smallest M of the CTA-pair GEMM (returns the old value)");
+  m.def("gemm_decode_max_m", &gsb_gemm_decode_max_m,
+        "set the largest M of the operand-swapped decode GEMM (0: off; -1 reads; returns the old value)");
   m.def("rmsnorm", &gsb_rmsnorm, "RMSNorm (optionally gathering rows)");
   m.def("embed", &gsb_embed, "embedding gather with token exchange and multiplier");
   m.def("rope_kv", &gsb_rope_kv, "RoPE on q/k fused with the paged KV-cache write");

@@ -1,0 +1,508 @@
+// Decode-sized switched-LoRA GEMMs (M <= 256 tokens) on tcgen05.
+//
+// A decode step multiplies a few hundred token rows by every weight matrix:
+// the work is a stream of weight bytes with almost no reuse, so the kernel is
+// laid out to read each weight byte once, with every SM streaming its share:
+//
+// * Operands swapped: the MMA's 128-row side (M) is a tile of 128 weight rows
+//   and its N side is all Mp tokens (M rounded up to 16, at most 256), so
+//   D^T[128 weight rows, Mp tokens] = W_tile . X^T accumulates in TMEM. One
+//   weight tile is read once for every token, whatever M is.
+// * Split-K over a thread-block cluster: the ks CTAs of a cluster share one
+//   weight tile and take contiguous K ranges, so n_tiles * ks CTAs fill the
+//   SMs. Each CTA drains its fp32 partial from TMEM into its own shared
+//   memory (token-major), then after a cluster barrier every CTA sums a
+//   slice of the tokens over all ks partials through distributed shared
+//   memory (ld.shared::cluster, fixed order, so the result is deterministic)
+//   and applies the epilogue. No global workspace, no second kernel.
+// * The LoRA expand rides in the same accumulator: for every adapter present
+//   among the step's tokens, rank/32 extra K blocks multiply B_a (weight rows
+//   x rank, the A operand) by the masked shrink output S (tokens x rank, the
+//   B operand; zero on tokens of other adapters). Those blocks are spread over
+//   the cluster's CTAs round-robin.
+// * Epilogues: store, residual add, SwiGLU (a tile holds 64 gate rows and the
+//   matching 64 up rows, loaded as two TMA boxes), adapter mask (the LoRA
+//   shrink itself) and the NVSwitch multicast reduction for tensor parallelism.
+//   Rounding follows the general kernel (gemm_tcgen05.cu) bit for bit.
+//
+// Warp roles (192 threads): warp 0 issues TMA loads into a ring of stages,
+// warp 1 owns TMEM and issues tcgen05.mma from one thread, warps 2..5 drain
+// TMEM; all six warps run the cluster reduction and the epilogue. Every wait
+// is bounded; a CTA that gives up still arrives at both cluster barriers, so
+// its peers never wait on it. TMA loads are plain single-CTA copies from this
+// GPU's memory (no multicast).
+#include "common.cuh"
+#include "gemm_common.cuh"
+#include "tma_util.h"
+
+#include <algorithm>
+
+namespace gsb {
+namespace dec {
+
+constexpr int BW = 128;      // weight rows per tile (the MMA's M)
+constexpr int BK = 64;       // K per main block
+constexpr int THREADS = 192;
+constexpr int MAX_KS = 8;    // portable cluster size
+
+template <int MPMAX>
+struct Cfg {
+  static constexpr int A_BYTES = BW * BK * 2;       // 16 KB of W per stage
+  static constexpr int B_BYTES = MPMAX * BK * 2;    // the k block of every token
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (MPMAX == 256) ? 4 : 6;
+  static constexpr int RING = STAGES * STAGE_BYTES;
+  static constexpr int P_STRIDE = BW;               // fp32 per token row of the partial
+  static constexpr int P_BYTES = MPMAX * P_STRIDE * 4;
+  static_assert(P_BYTES <= RING, "the partial reuses the operand ring");
+  static constexpr int BAR_OFF = RING;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+};
+
+struct Params {
+  int M, N, K, Mp;
+  int ks;            // K parts per tile = cluster size
+  int kblocks;       // K / 64
+  float scale;
+  void* out;
+  int64_t ldo;
+  const __nv_bfloat16* residual;
+  int64_t ldr;
+  int swiglu_half;   // kEpiSwiGLU: gate (then up) rows per interleave tile
+  int lora;
+  int rank_blocks;
+  int num_adapters;
+  int num_slices;
+  int slice_bounds[5];
+  const uint64_t* tile_mask;  // adapters present per 128-token tile (expand, or shrink tiles to skip)
+  const int32_t* row_adapter;
+  int mask_rank, mask_num_adapters;
+};
+
+__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Adapters (bits) present among all M tokens.
+__device__ __forceinline__ uint64_t present_adapters(const Params& p) {
+  if (p.tile_mask == nullptr) return (p.num_adapters >= 64) ? ~0ull : ((1ull << p.num_adapters) - 1);
+  uint64_t m = 0;
+  for (int t = 0; t < (p.M + 127) / 128; ++t) m |= p.tile_mask[t];
+  return m;
+}
+
+// Shrink (kEpiMaskAdapter): the tile's columns belong to adapters none of whose
+// tokens is in the step, so nothing reads them; the tile is skipped.
+__device__ __forceinline__ bool shrink_skipped(const Params& p, int n0) {
+  if (p.tile_mask == nullptr) return false;
+  uint64_t need = 0;
+  for (int c = 0; c < BW && n0 + c < p.N; c += p.mask_rank)
+    need |= 1ull << (((n0 + c) / p.mask_rank) % p.mask_num_adapters);
+  return (present_adapters(p) & need) == 0;
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue8(const Params& p, int m, int col, const float (&v)[8], const float (&u)[8]) {
+  if (EPI == kEpiSwiGLU) {
+    uint32_t pk[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // gate / up rounded to bf16 first, as the unfused path stores them
+      const float g0 = bf16r(v[2 * j]), g1 = bf16r(v[2 * j + 1]);
+      const float u0 = bf16r(u[2 * j]), u1 = bf16r(u[2 * j + 1]);
+      pk[j] = pack_bf16x2(__fdividef(g0, 1.f + __expf(-g0)) * u0, __fdividef(g1, 1.f + __expf(-g1)) * u1);
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)m * p.ldo + col) =
+        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    return;
+  }
+  float o[8];
+  const bool has_res = (EPI == kEpiResAdd) || (EPI == kEpiMultimemRed && p.residual != nullptr);
+  if (has_res) {
+    const uint4 r4 = *reinterpret_cast<const uint4*>(p.residual + (int64_t)m * p.ldr + col);
+    const uint32_t rr[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      // the projection is rounded to bf16 before the residual add
+      const float2 f = unpack_bf16x2(rr[j]);
+      o[2 * j] = f.x + bf16r(v[2 * j]) * p.scale;
+      o[2 * j + 1] = f.y + bf16r(v[2 * j + 1]) * p.scale;
+    }
+  } else if (EPI == kEpiMultimemRed) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = bf16r(v[j]) * p.scale;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = v[j] * p.scale;
+    if (EPI == kEpiMaskAdapter) {
+      const int ra = p.row_adapter[m];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (((col + j) / p.mask_rank) % p.mask_num_adapters + 1 != ra) o[j] = 0.f;
+    }
+  }
+  const uint4 pk = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                              pack_bf16x2(o[6], o[7]));
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)m * p.ldo + col;
+  if (EPI == kEpiMultimemRed)
+    multimem_red_add_v4_bf16x2(dst, pk.x, pk.y, pk.z, pk.w);
+  else
+    *reinterpret_cast<uint4*>(dst) = pk;
+}
+
+template <int MPMAX, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    decode_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                       const __grid_constant__ CUtensorMap tm_lb, const __grid_constant__ CUtensorMap tm_s,
+                       const Params p, uint32_t* err) {
+  using C = Cfg<MPMAX>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
+  uint64_t* empty_bar = full_bar + C::STAGES;
+  uint64_t* tfull_bar = empty_bar + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ks = p.ks;
+  const int part = ks > 1 ? (int)cluster_ctarank() : 0;
+  const int tile = blockIdx.x / ks;
+  const int n0 = tile * BW;  // first row of the tile in the (packed) weight
+  if (EPI == kEpiMaskAdapter && shrink_skipped(p, n0)) return;  // the whole cluster skips alike
+
+  // this CTA's blocks: a contiguous K range, then every ks-th LoRA block
+  const int kb_lo = part * p.kblocks / ks, kb_hi = (part + 1) * p.kblocks / ks;
+  const int n_main = kb_hi - kb_lo;
+  uint64_t amask = 0;
+  int s_base = 0;
+  if (EPI != kEpiMaskAdapter && p.lora) {
+    amask = present_adapters(p);
+    int sl = 0;
+    for (int i = 0; i < p.num_slices; ++i)
+      if (n0 >= p.slice_bounds[i]) sl = i;
+    s_base = sl * p.num_adapters * p.rank_blocks * 32;
+  }
+  const int n_lora_all = __popcll(amask) * p.rank_blocks;
+  const int n_lora = n_lora_all > part ? (n_lora_all - part + ks - 1) / ks : 0;
+  const int total = n_main + n_lora;
+  const int tcols = p.Mp <= 32 ? 32 : (p.Mp <= 64 ? 64 : (p.Mp <= 128 ? 128 : 256));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(tfull_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_x);
+    if (n_lora) {
+      tma_prefetch_desc(&tm_lb);
+      tma_prefetch_desc(&tm_s);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, tcols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  uint32_t issued = 0;  // producer: loads issued (for the drain on the error path)
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      for (int i = 0; i < total; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (*abort_flag || !mbar_wait(&empty_bar[s], ph ^ 1, err, kErrGemmWait)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* sa = smem + s * C::STAGE_BYTES;
+        uint8_t* sb = sa + C::A_BYTES;
+        if (i < n_main) {
+          const int kx = (kb_lo + i) * BK;
+          mbar_arrive_expect_tx(&full_bar[s], C::A_BYTES + p.Mp * BK * 2);
+          if (EPI == kEpiSwiGLU) {
+            // out columns [64 tile, 64 tile + 64): their gate rows, then their up rows
+            const int o0 = tile * 64, it = o0 / p.swiglu_half, off = o0 % p.swiglu_half;
+            const int g0 = it * 2 * p.swiglu_half + off;
+            tma_load_2d(sa, &tm_w, &full_bar[s], kx, g0);
+            tma_load_2d(sa + 64 * 128, &tm_w, &full_bar[s], kx, g0 + p.swiglu_half);
+          } else {
+            tma_load_2d(sa, &tm_w, &full_bar[s], kx, n0);
+          }
+          tma_load_2d(sb, &tm_x, &full_bar[s], kx, 0);
+        } else {
+          const int j = part + (i - n_main) * ks;  // global LoRA block index
+          const int ai = j / p.rank_blocks, rb = j % p.rank_blocks;
+          uint64_t rem = amask;
+          for (int t = 0; t < ai; ++t) rem &= rem - 1;
+          const int a_bit = __ffsll((long long)rem) - 1;
+          const int kcol = a_bit * p.rank_blocks * 32 + rb * 32;
+          mbar_arrive_expect_tx(&full_bar[s], BW * 64 + p.Mp * 64);
+          tma_load_2d(sa, &tm_lb, &full_bar[s], kcol, n0);
+          tma_load_2d(sb, &tm_s, &full_bar[s], s_base + kcol, 0);
+        }
+        ++issued;
+      }
+      if (*abort_flag) {
+        // no TMA write may still be in flight into this CTA's shared memory at exit
+        const uint32_t first = issued > (uint32_t)C::STAGES ? issued - C::STAGES : 0;
+        for (uint32_t j = first; j < issued; ++j)
+          mbar_wait(&full_bar[j % C::STAGES], (j / C::STAGES) & 1, err, kErrGemmWait);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(BW, p.Mp);
+      bool ok = true;
+      for (int i = 0; i < total; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (*abort_flag || !mbar_wait(&full_bar[s], ph, err, kErrGemmWait)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
+        const uint32_t sb = sa + C::A_BYTES;
+        if (i < n_main) {
+          const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sb);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) umma_bf16(tmem_base, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0);
+        } else {
+          const uint64_t ad = umma_desc_sw64(sa), bd = umma_desc_sw64(sb);
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk) umma_bf16(tmem_base, ad + 2 * kk, bd + 2 * kk, idesc, 1);
+        }
+        umma_commit(&empty_bar[s]);
+      }
+      if (ok) umma_commit(tfull_bar);
+    }
+  } else {
+    // ---------------- TMEM drain: fp32 partial -> shared memory, token-major ----------------
+    const int q = warp & 3;  // the TMEM lane quarter this warp may read
+    if (!*abort_flag && mbar_wait(tfull_bar, 0, err, kErrGemmWait)) {
+      tc_fence_after();
+      float* P = reinterpret_cast<float*>(smem);
+      for (int c = 0; c < p.Mp; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + c + ((uint32_t)(q * 32) << 16), r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) P[(c + j) * C::P_STRIDE + q * 32 + lane] = __uint_as_float(r[j]);
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (ks > 1) cluster_sync();  // every CTA's partial is in its shared memory
+
+  // ---------------- cluster reduction + epilogue ----------------
+  if (!*abort_flag) {
+    const int rows_per = (p.M + ks - 1) / ks;
+    const int r0 = part * rows_per, r1 = min(p.M, r0 + rows_per);
+    const uint32_t pbase = smem_u32(smem);
+    constexpr int GROUPS = (EPI == kEpiSwiGLU) ? 8 : 16;  // 8-column groups per token row
+    const int n_items = max(0, r1 - r0) * GROUPS;
+    for (int it = threadIdx.x; it < n_items; it += THREADS) {
+      const int m = r0 + it / GROUPS;
+      const int c = (it % GROUPS) * 8;
+      float v[8], u[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = u[j] = 0.f;
+      const uint32_t local = pbase + (uint32_t)((m * C::P_STRIDE + c) * 4);
+#pragma unroll 1
+      for (int q = 0; q < ks; ++q) {  // fixed order: deterministic sums
+        const uint32_t src = ks > 1 ? mapa_shared(local, (uint32_t)q) : local;
+        const float4 a0 = ld_dsmem_f4(src), a1 = ld_dsmem_f4(src + 16);
+        v[0] += a0.x; v[1] += a0.y; v[2] += a0.z; v[3] += a0.w;
+        v[4] += a1.x; v[5] += a1.y; v[6] += a1.z; v[7] += a1.w;
+        if (EPI == kEpiSwiGLU) {
+          const float4 b0 = ld_dsmem_f4(src + 256), b1 = ld_dsmem_f4(src + 256 + 16);
+          u[0] += b0.x; u[1] += b0.y; u[2] += b0.z; u[3] += b0.w;
+          u[4] += b1.x; u[5] += b1.y; u[6] += b1.z; u[7] += b1.w;
+        }
+      }
+      if (EPI == kEpiSwiGLU) {
+        epilogue8<EPI>(p, m, tile * 64 + c, v, u);
+      } else if (n0 + c < p.N) {
+        epilogue8<EPI>(p, m, n0 + c, v, u);
+      }
+    }
+  }
+  if (ks > 1) cluster_sync();  // peers are done reading this CTA's partial
+  if (*abort_flag) {
+    // error path: MMAs and copies this CTA issued may still be in flight; give them
+    // time to finish before the tensor memory is released (bounded, ~1 ms)
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 1000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, tcols);
+  }
+}
+
+}  // namespace dec
+
+// Largest M served by the decode kernel (0 turns it off; gemm_decode_max_m()
+// changes it at run time for A/B tests).
+static int g_decode_max_m = 256;
+
+static int dec_num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  GSB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int n = 0;
+  GSB_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+template <int MPMAX, int EPI>
+static void launch_decode(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tlb,
+                          const CUtensorMap& ts, const dec::Params& p, int n_tiles, uint32_t* err,
+                          cudaStream_t stream) {
+  using C = dec::Cfg<MPMAX>;
+  auto kfn = dec::decode_gemm_kernel<MPMAX, EPI>;
+  static bool configured = false;  // per instantiation
+  if (!configured) {
+    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(n_tiles * p.ks), 1, 1);
+  cfg.blockDim = dim3(dec::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)p.ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.ks > 1 ? 1 : 0;
+  count_launch();
+  GSB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kfn, tw, tx, tlb, ts, p, err));
+}
+
+template <int MPMAX>
+static void dispatch_decode(int epi, const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tlb,
+                            const CUtensorMap& ts, const dec::Params& p, int n_tiles, uint32_t* err,
+                            cudaStream_t st) {
+  switch (epi) {
+    case kEpiStore: launch_decode<MPMAX, kEpiStore>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
+    case kEpiResAdd: launch_decode<MPMAX, kEpiResAdd>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
+    case kEpiSwiGLU: launch_decode<MPMAX, kEpiSwiGLU>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
+    case kEpiMaskAdapter: launch_decode<MPMAX, kEpiMaskAdapter>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
+    case kEpiMultimemRed: launch_decode<MPMAX, kEpiMultimemRed>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
+  }
+}
+
+// K parts per weight tile: the most that keep n_tiles * ks within one wave of
+// SMs, at most 8 (portable cluster) and at least four 64-deep K blocks per part.
+static int choose_ks(int n_tiles, int kblocks, int nsms) {
+  int ks = std::max(1, std::min(dec::MAX_KS, nsms / std::max(1, n_tiles)));
+  while (ks > 1 && kblocks / ks < 4) --ks;
+  return ks;
+}
+
+bool decode_gemm_try(const DecodeGemmArgs& a, uint32_t* err, cudaStream_t stream) {
+  const int epi = a.epi;
+  if (g_decode_max_m <= 0 || a.M < 1 || a.M > std::min(g_decode_max_m, 256)) return false;
+  if (!(epi == kEpiStore || epi == kEpiResAdd || epi == kEpiSwiGLU || epi == kEpiMaskAdapter ||
+        epi == kEpiMultimemRed))
+    return false;
+  if (a.K % 64 != 0 || a.N % 64 != 0) return false;
+  const bool lora = a.s != nullptr && a.lb != nullptr && a.num_adapters > 0 && epi != kEpiMaskAdapter;
+  if (epi == kEpiSwiGLU && (lora || a.swiglu_tile % 128 != 0 || a.N % a.swiglu_tile != 0)) return false;
+  if (epi == kEpiResAdd && a.residual == nullptr) return false;
+  if (lora) {
+    if (a.rank % 32 != 0 || a.num_adapters > 64 || a.num_slices < 1 || a.num_slices > 4) return false;
+    for (int i = 0; i < a.num_slices; ++i)
+      if (a.slice_bounds[i] % dec::BW != 0) return false;  // a weight tile lies in one slice
+  }
+  // 16-byte aligned rows for the vector epilogue
+  if ((a.ldo % 8) != 0 || (reinterpret_cast<uintptr_t>(a.out) & 15) != 0) return false;
+  if (a.residual != nullptr && ((a.ldr % 8) != 0 || (reinterpret_cast<uintptr_t>(a.residual) & 15) != 0))
+    return false;
+
+  dec::Params p{};
+  p.M = a.M;
+  p.N = a.N;
+  p.K = a.K;
+  p.Mp = (a.M + 15) / 16 * 16;
+  p.kblocks = a.K / 64;
+  p.scale = a.scale;
+  p.out = a.out;
+  p.ldo = a.ldo;
+  p.residual = reinterpret_cast<const __nv_bfloat16*>(a.residual);
+  p.ldr = a.ldr;
+  p.swiglu_half = a.swiglu_tile / 2;
+  const int n_tiles = (a.N + dec::BW - 1) / dec::BW;
+  p.ks = choose_ks(n_tiles, p.kblocks, dec_num_sms());
+  p.lora = lora ? 1 : 0;
+  p.tile_mask = nullptr;
+  if (lora) {
+    p.rank_blocks = a.rank / 32;
+    p.num_adapters = a.num_adapters;
+    p.num_slices = a.num_slices;
+    for (int i = 0; i <= a.num_slices; ++i) p.slice_bounds[i] = a.slice_bounds[i];
+    p.tile_mask = a.tile_mask;
+  }
+  if (epi == kEpiMaskAdapter) {
+    p.row_adapter = a.row_adapter;
+    p.mask_rank = a.mask_rank;
+    p.mask_num_adapters = a.mask_num_adapters;
+    p.tile_mask = a.skip_mask;
+  }
+  const uint32_t mp_box = (uint32_t)p.Mp;
+  const CUtensorMap tw = make_tmap_bf16_2d(a.w, (uint64_t)a.N, (uint64_t)a.K, (uint64_t)a.ldw, 64,
+                                           epi == kEpiSwiGLU ? 64u : 128u, CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMap tx = make_tmap_bf16_2d(a.x, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.ldx, 64, mp_box,
+                                           CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tlb = tw, ts = tx;
+  if (lora) {
+    tlb = make_tmap_bf16_2d(a.lb, (uint64_t)a.N, (uint64_t)a.num_adapters * a.rank, (uint64_t)a.ldlb, 32, 128,
+                            CU_TENSOR_MAP_SWIZZLE_64B);
+    ts = make_tmap_bf16_2d(a.s, (uint64_t)a.M, (uint64_t)a.s_cols, (uint64_t)a.lds, 32, mp_box,
+                           CU_TENSOR_MAP_SWIZZLE_64B);
+  }
+  if (p.Mp <= 128)
+    dispatch_decode<128>(epi, tw, tx, tlb, ts, p, n_tiles, err, stream);
+  else
+    dispatch_decode<256>(epi, tw, tx, tlb, ts, p, n_tiles, err, stream);
+  return true;
+}
+
+}  // namespace gsb
+
+// Sets the largest M served by the decode kernel (0: never); returns the previous value.
+int64_t gsb_gemm_decode_max_m(int64_t v) {
+  const int64_t old = gsb::g_decode_max_m;
+  if (v >= 0) gsb::g_decode_max_m = (int)v;
+  return old;
+}

@@ -21,6 +21,7 @@
 // Every TMA load is a plain single-CTA copy from this GPU's memory, so the
 // kernel is safe on every GPU count.
 #include "common.cuh"
+#include "gemm_common.cuh"
 #include "tma_util.h"
 
 #include <ATen/ATen.h>
@@ -31,25 +32,6 @@
 #include <cstdlib>
 
 namespace gsb {
-
-enum EpiKind : int {
-  kEpiStore = 0,     // out(bf16) = acc * scale
-  kEpiResAdd = 1,    // out(bf16) = residual + acc * scale  (out may alias residual)
-  kEpiSwiGLU = 2,    // out(bf16)[:, n/2] = silu(gate) * up, gate/up interleaved per tile
-  kEpiMaskAdapter = 3,  // shrink: keep column j only where row's adapter == (j/r)%NA+1
-  kEpiF32 = 4,       // out(fp32) = acc * scale
-  // out = multicast address of a symmetric bf16 buffer: every rank adds
-  // (residual +) acc * scale into all ranks' copies through NVSwitch
-  // (multimem.red), tile by tile as accumulators drain
-  kEpiMultimemRed = 5,
-};
-
-__device__ __forceinline__ void multimem_red_add_v4_bf16x2(void* mc, uint32_t a, uint32_t b, uint32_t c,
-                                                           uint32_t d) {
-  asm volatile("multimem.red.relaxed.sys.global.add.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(mc), "r"(a), "r"(b),
-               "r"(c), "r"(d)
-               : "memory");
-}
 
 struct GemmLoraArgs {
   int enabled;            // 0: plain GEMM
@@ -1200,11 +1182,48 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
     }
     GSB_CHECK(mask_rank > 0 && mask_num_adapters > 0, "mask_rank and mask_num_adapters required");
   }
+  uint32_t* errp = reinterpret_cast<uint32_t*>(err.data_ptr());
+  if (!grouped) {
+    // decode-sized GEMMs: operand-swapped kernel with a cluster split-K (gemm_decode.cu)
+    DecodeGemmArgs d{};
+    d.x = x.data_ptr();
+    d.ldx = x.stride(0);
+    d.w = w.data_ptr();
+    d.ldw = w.stride(0);
+    d.out = epi.out;
+    d.ldo = epi.ldo;
+    d.M = M;
+    d.N = N;
+    d.K = K;
+    d.epi = (int)epi_kind;
+    d.scale = epi.scale;
+    d.residual = epi.residual;
+    d.ldr = epi.ldr;
+    d.swiglu_tile = (int)bn;
+    if (lora.enabled) {
+      d.s = s->data_ptr();
+      d.lds = s->stride(0);
+      d.s_cols = (int)s->size(1);
+      d.lb = lb->data_ptr();
+      d.ldlb = lb->stride(0);
+      d.rank = (int)rank;
+      d.num_adapters = (int)num_adapters;
+      d.num_slices = lora.num_slices;
+      for (int i = 0; i <= lora.num_slices; ++i) d.slice_bounds[i] = lora.slice_bounds[i];
+      d.tile_mask = lora.tile_mask;
+    }
+    if (epi_kind == kEpiMaskAdapter) {
+      d.row_adapter = epi.row_adapter;
+      d.mask_rank = epi.mask_rank;
+      d.mask_num_adapters = epi.mask_num_adapters;
+      d.skip_mask = epi.skip_mask;
+    }
+    if (decode_gemm_try(d, errp, stream)) return;
+  }
   // staged epilogues store 32-row x 64-column boxes of the bf16 output by TMA
   CUtensorMap to = ta;
   if (epi_tma_store((int)epi_kind, pair ? 256 : (int)bn))
     to = make_tmap_bf16_2d(out.data_ptr(), M, out.size(1), out.stride(0), 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
-  uint32_t* errp = reinterpret_cast<uint32_t*>(err.data_ptr());
   if (pair) {
     dispatch_epi_pair((int)epi_kind, ta, tb, ts, tlb, to, M, N, K, lora, epi, errp, stream);
     return;

@@ -17,6 +17,7 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
                        const c10::optional<at::Tensor>& tile_expert);
 
 int64_t gsb_gemm_pair_min_m(int64_t m);
+int64_t gsb_gemm_decode_max_m(int64_t v);
 
 void gsb_rmsnorm(const at::Tensor& x, const at::Tensor& w, const at::Tensor& out,
                  const c10::optional<at::Tensor>& rows, double eps);

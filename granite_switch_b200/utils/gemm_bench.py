@@ -1,6 +1,7 @@
 """Switched-LoRA GEMM microbenchmark (the kernel sweep of the benchmark configs).
 
-``python -m granite_switch_b200.utils.gemm_bench [--quick] [--pair-min-m M]``
+``python -m granite_switch_b200.utils.gemm_bench [--quick] [--pair-min-m M]``, or
+``--decode M ...`` for the decode-sized 8B projections (:func:`decode_sweep`).
 
 For every point (M tokens, N x K, rank r, number of adapters) the per-token
 adapter ids are drawn uniformly over the adapters, then an activation mask
@@ -111,8 +112,101 @@ def run_point(m, n, k, rank, na, flush, dev, iters=20, compare_pair=False):
     return res
 
 
+DECODE_SHAPES = {  # 8B-shape projections: name -> (N, K, epilogue, LoRA on)
+    "qkv": (6144, 4096, "store", True),
+    "o": (4096, 4096, "resadd", True),
+    "gate_up": (25600, 4096, "swiglu", False),
+    "down": (4096, 12800, "resadd", False),
+}
+
+
+def _hbm_gbs() -> float:
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 6650.0  # earlier measurement on this pool, when the file is absent
+
+
+def decode_sweep(ms, iters: int = 50, rotate_bytes: int = 400 << 20) -> None:
+    """Decode-sized projections (the 8B shapes at M tokens, 12 adapters r32 where LoRA is on):
+    event-timed per call with enough weight copies rotated (``rotate_bytes`` in all, over three
+    times the 126 MB L2) that every call streams its weights from HBM, the operand-swapped decode kernel against the general kernel. Prints
+    microseconds and the weight bytes' fraction of the measured HBM copy bandwidth."""
+    dev = torch.device("cuda", 0)
+    nat = native()
+    hbm = _hbm_gbs()
+    na, rank = 12, 32
+    for m in ms:
+        for name, (n, k, epi, lora) in DECODE_SHAPES.items():
+            g = torch.Generator(device=dev).manual_seed(m)
+            copies = max(3, -(-rotate_bytes // (n * k * 2)))
+            ws = [(torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16() for _ in range(copies)]
+            x = torch.randn(m, k, device=dev, generator=g).bfloat16()
+            out = torch.empty(m, n // 2 if epi == "swiglu" else n, device=dev, dtype=torch.bfloat16)
+            kind = {"store": G.EPI_STORE, "resadd": G.EPI_RESADD, "swiglu": G.EPI_SWIGLU}[epi]
+            extra = {}
+            shrink = None
+            if lora:
+                slices = 3 if name == "qkv" else 1
+                ids = torch.randint(1, na + 1, (m,), device=dev, dtype=torch.int32, generator=g)
+                mask = torch.zeros((m + 127) // 128, dtype=torch.int64, device=dev)
+                for t in range(mask.numel()):
+                    bits = 0
+                    for a in ids[t * 128:(t + 1) * 128].unique().tolist():
+                        bits |= 1 << (a - 1)
+                    mask[t] = bits
+                a_all = (torch.randn(slices * na * rank, k, device=dev, generator=g) * 0.02).bfloat16()
+                s = torch.empty(m, a_all.shape[0], device=dev, dtype=torch.bfloat16)
+                lb = (torch.randn(n, na * rank, device=dev, generator=g) * 0.02).bfloat16()
+                bounds = [0, 4096, 5120, 6144] if name == "qkv" else [0, n]
+                extra = dict(s=s, lb=lb, tile_mask=mask, rank=rank, num_adapters=na, slice_bounds=bounds)
+
+                def shrink():
+                    G.lora_shrink(x, a_all, ids, rank, na, out=s, tile_mask=mask)
+            res = {}
+            parts = ["full", "base"] + (["shrink"] if lora else [])
+            for tag, dm in (("decode", 256), ("general", 0)):
+                old = nat.gemm_decode_max_m(dm)
+                for what in parts:
+                    i = [0]
+
+                    def call(what=what):
+                        w = ws[i[0] % copies]
+                        i[0] += 1
+                        if what == "shrink":
+                            shrink()
+                            return
+                        if what == "full" and shrink is not None:
+                            shrink()
+                        G.switched_gemm(x, w, out, epi=kind, residual=out if epi == "resadd" else None,
+                                        bn=128 if epi == "swiglu" else None, **(extra if what == "full" else {}))
+
+                    for _ in range(5):
+                        call()
+                    torch.cuda.synchronize()
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    for _ in range(iters):
+                        call()
+                    b.record()
+                    torch.cuda.synchronize()
+                    us = a.elapsed_time(b) / iters * 1e3
+                    gbs = n * k * 2 / (us * 1e-6) / 1e9
+                    res[f"{tag}_{what}"] = dict(us=round(us, 2), hbm_frac=round(gbs / hbm, 3))
+                nat.gemm_decode_max_m(old)
+            check_errors(dev)
+            print(json.dumps(dict(m=m, proj=name, n=n, k=k, lora=lora, **res)), flush=True)
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--decode", type=int, nargs="*", default=None,
+                   help="time the decode-sized 8B projections at these M instead of the sweep")
     p.add_argument("--quick", action="store_true", help="r=32, 12 adapters only")
     p.add_argument("--ms", type=int, nargs="*", default=None)
     p.add_argument("--pair-min-m", type=int, default=None, help="smallest M of the CTA-pair kernel (<0: off)")
@@ -121,6 +215,9 @@ def main():
     args = p.parse_args()
     dev = torch.device("cuda", 0)
     err_buffer(dev)
+    if args.decode is not None:
+        decode_sweep(args.decode or [222])
+        return
     nat = native()
     if args.pair_min_m is not None:
         nat.gemm_pair_min_m(args.pair_min_m)

@@ -48,11 +48,10 @@ if want("swiglu"):
     x = torch.randn(T, H, device=dev).bfloat16()
     w = (torch.randn(2 * I, H, device=dev) * 0.02).bfloat16()
     out = G.switched_gemm(x, w, epi=G.EPI_SWIGLU, bn=256)
-if want("decode_gemm"):
-    x = torch.randn(128, H, device=dev).bfloat16()
+if want("decode_gemm"):  # down projection of the headline decode step (222 tokens): the decode kernel
     w = (torch.randn(H, I, device=dev) * 0.02).bfloat16()
-    x2 = torch.randn(128, I, device=dev).bfloat16()
-    h = torch.randn(128, H, device=dev).bfloat16()
+    x2 = torch.randn(222, I, device=dev).bfloat16()
+    h = torch.randn(222, H, device=dev).bfloat16()
     G.switched_gemm(x2, w, h, epi=G.EPI_RESADD, residual=h, scale=0.5)
 if want("attn_prefill") or want("attn_decode"):
     hq, hkv, d = 32, 8, 128

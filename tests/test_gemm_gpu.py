@@ -363,6 +363,24 @@ def test_grouped_gemm(epi):
         _close(out[rows], ref)
 
 
+class _DecodeMaxM:
+    """Temporarily set the largest M of the operand-swapped decode kernel (0: off)."""
+
+    def __init__(self, v):
+        self.v = v
+
+    def __enter__(self):
+        from granite_switch_b200._native import native
+
+        self.old = native().gemm_decode_max_m(self.v)
+        return self
+
+    def __exit__(self, *a):
+        from granite_switch_b200._native import native
+
+        native().gemm_decode_max_m(self.old)
+
+
 class _SplitK:
     """Temporarily set the output-tile count below which single-CTA GEMMs split K (0: never)."""
 
@@ -403,14 +421,107 @@ def test_split_k_decode_shapes(epi, m, k):
     bn = 64 if epi != "swiglu" else 128
     kw = dict(epi=kind, residual=res if epi == "resadd" else None, scale=0.5, s=s, lb=lb, tile_mask=mask,
               rank=rank, num_adapters=na, slice_bounds=[0, n], bn=bn)
-    with _SplitK(74):
+    with _DecodeMaxM(0), _SplitK(74):  # the general kernel's split-K (decode kernel off)
         split = G.switched_gemm(x, w, **kw)
-    with _SplitK(0):
+    with _DecodeMaxM(0), _SplitK(0):
         whole = G.switched_gemm(x, w, **kw)
     ref = G.switched_gemm_reference(x, w, epi=kind, residual=kw["residual"], scale=0.5, s=s, lb=lb, rank=rank,
                                     num_adapters=na, slice_bounds=[0, n], swiglu_tile=bn)
     _close(split, ref)
     _close(split, whole)
+    from granite_switch_b200._native import check_errors
+
+    check_errors(torch.device("cuda", 0))
+
+
+def _masked_s(m, width, rank, na, row_adapter):
+    cols = torch.arange(width, device="cuda")
+    keep = ((cols // rank) % na + 1).unsqueeze(0) == row_adapter.long().unsqueeze(1)
+    return (_rand(m, width, scale=0.5).float() * keep).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("epi", ["store", "resadd", "swiglu"])
+@pytest.mark.parametrize("m", [1, 5, 77, 130, 222, 256])
+@pytest.mark.parametrize("n,k", [(512, 320), (4096, 4096), (1024, 12800)])
+def test_decode_gemm_epilogues(epi, m, n, k):
+    """Operand-swapped decode kernel (M <= 256; one CTA per 128 weight rows, K split over a
+    cluster and reduced through distributed shared memory): equal to the fp32 oracle and to
+    the general kernel, and bitwise deterministic."""
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(11)
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.02)
+    res = _rand(m, n)
+    kind = {"store": G.EPI_STORE, "resadd": G.EPI_RESADD, "swiglu": G.EPI_SWIGLU}[epi]
+    bn = 128 if epi == "swiglu" else None
+    out_cols = n // 2 if epi == "swiglu" else n
+
+    def run():
+        o = torch.empty(m, out_cols, device="cuda", dtype=torch.bfloat16)
+        if epi == "resadd":
+            o.copy_(res)
+        G.switched_gemm(x, w, o, epi=kind, residual=o if epi == "resadd" else None, scale=0.5, bn=bn)
+        return o
+
+    with _DecodeMaxM(256):
+        a = run()
+        b = run()
+    with _DecodeMaxM(0):
+        general = run()
+    ref = G.switched_gemm_reference(x, w, epi=kind, residual=res if epi == "resadd" else None, scale=0.5,
+                                    swiglu_tile=128)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    _close(a, ref)
+    _close(a, general)
+    from granite_switch_b200._native import check_errors
+
+    check_errors(torch.device("cuda", 0))
+
+
+@pytest.mark.parametrize("m", [3, 100, 222])
+@pytest.mark.parametrize("k", [512, 4096])
+def test_decode_gemm_lora_slices(m, k):
+    """qkv-shaped switched GEMM on the decode kernel: the shrink (adapter-mask epilogue, tiles of
+    absent adapters skipped) and the expand over three slices, LoRA blocks spread over the
+    cluster's K parts; against the oracle and the general kernel."""
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(12)
+    na, rank = 5, 32
+    bounds = [0, 1024, 1280, 1536]
+    n = bounds[-1]
+    x = _rand(m, k)
+    w = _rand(n, k, scale=0.02)
+    row_adapter = torch.randint(0, na + 1, (m,), device="cuda", dtype=torch.int32)
+    row_adapter[row_adapter == 2] = 3  # one adapter absent: its shrink tiles are skipped
+    width = 3 * na * rank
+    a_all = torch.zeros((width + 63) // 64 * 64, k, device="cuda", dtype=torch.bfloat16)
+    a_all[:width] = _rand(width, k, scale=0.02)
+    lb = _rand(n, na * rank, scale=0.05)
+    mask = _tile_mask(row_adapter, m)
+    s_ref = G.switched_gemm_reference(x, a_all, epi=G.EPI_MASK_ADAPTER, row_adapter=row_adapter,
+                                      mask_rank=rank, mask_num_adapters=na)
+    with _DecodeMaxM(256):
+        s = torch.full((m, a_all.shape[0]), float("nan"), device="cuda", dtype=torch.bfloat16)
+        G.lora_shrink(x, a_all, row_adapter, rank, na, out=s, tile_mask=mask)
+        out = G.switched_gemm(x, w, s=s, lb=lb, tile_mask=mask, rank=rank, num_adapters=na, slice_bounds=bounds)
+        out2 = G.switched_gemm(x, w, s=s, lb=lb, tile_mask=mask, rank=rank, num_adapters=na, slice_bounds=bounds)
+    present = [a for a in range(1, na + 1) if (row_adapter == a).any()]
+    for a in present:  # columns of present adapters are written for every token
+        for sl in range(3):
+            c0 = sl * na * rank + (a - 1) * rank
+            _close(s[:, c0:c0 + rank], s_ref[:, c0:c0 + rank])
+    ref = G.switched_gemm_reference(x, w, s=s_ref, lb=lb, rank=rank, num_adapters=na, slice_bounds=bounds)
+    with _DecodeMaxM(0):
+        s_gen = G.lora_shrink(x, a_all, row_adapter, rank, na, tile_mask=mask)
+        general = G.switched_gemm(x, w, s=s_gen, lb=lb, tile_mask=mask, rank=rank, num_adapters=na,
+                                  slice_bounds=bounds)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
+    _close(out, ref)
+    _close(out, general)
     from granite_switch_b200._native import check_errors
 
     check_errors(torch.device("cuda", 0))
