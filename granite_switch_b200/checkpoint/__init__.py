@@ -96,6 +96,46 @@ def load_state_dict(path: str, device: str = "cpu") -> dict[str, torch.Tensor]:
     return dict(iter_tensors(path, device))
 
 
+class LazyCheckpoint:
+    """Read-on-demand view of a composed checkpoint: ``ckpt[name]`` reads one tensor
+    from its shard (memory-mapped by safetensors), so a rank materialises only the
+    tensors it packs, one at a time, never the whole state dict. Every read is
+    recorded; :meth:`unread` lists the tensors nothing asked for (the load audit).
+    """
+
+    def __init__(self, path: str):
+        self.path = path
+        self._where: dict[str, str] = {}
+        for fname in checkpoint_files(path):
+            with safe_open(os.path.join(path, fname), framework="pt") as f:
+                for k in f.keys():
+                    self._where[k] = fname
+        self._open: dict[str, object] = {}
+        self.read: set[str] = set()
+
+    def __contains__(self, name: str) -> bool:
+        return name in self._where
+
+    def keys(self):
+        return self._where.keys()
+
+    def __getitem__(self, name: str) -> torch.Tensor:
+        fname = self._where.get(name)
+        if fname is None:
+            raise KeyError(f"tensor {name!r} is missing from the checkpoint at {self.path}")
+        h = self._open.get(fname)
+        if h is None:
+            h = self._open[fname] = safe_open(os.path.join(self.path, fname), framework="pt")
+        self.read.add(name)
+        return h.get_tensor(name)
+
+    def unread(self) -> list[str]:
+        return sorted(k for k in self._where if k not in self.read)
+
+    def close(self) -> None:
+        self._open.clear()
+
+
 def total_bytes(path: str) -> int:
     n = 0
     for fname in checkpoint_files(path):

@@ -40,29 +40,22 @@
 namespace gsb {
 namespace dec {
 
-constexpr int BW = 128;      // weight rows per tile (the MMA's M)
-constexpr int BK = 64;       // K per main block
+constexpr int BW = 128;        // weight rows per accumulator (the MMA's M)
+constexpr int BK = 64;         // K per main block
 constexpr int THREADS = 192;
-constexpr int MAX_KS = 8;    // portable cluster size
-
-template <int MPMAX>
-struct Cfg {
-  static constexpr int A_BYTES = BW * BK * 2;       // 16 KB of W per stage
-  static constexpr int B_BYTES = MPMAX * BK * 2;    // the k block of every token
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (MPMAX == 256) ? 4 : 6;
-  static constexpr int RING = STAGES * STAGE_BYTES;
-  static constexpr int P_STRIDE = BW;               // fp32 per token row of the partial
-  static constexpr int P_BYTES = MPMAX * P_STRIDE * 4;
-  static_assert(P_BYTES <= RING, "the partial reuses the operand ring");
-  static constexpr int BAR_OFF = RING;
-  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
-};
+constexpr int MAX_KS = 8;      // portable cluster size
+constexpr int MAX_STAGES = 8;
+constexpr int RING = 192 * 1024;                      // operand ring (the partial reuses it)
+constexpr int SMEM_BYTES = RING + 512 + 1024;         // + barriers + alignment
+constexpr int P_STRIDE = BW;                          // fp32 per token row of a drained partial
+static_assert(256 * P_STRIDE * 4 <= RING, "one accumulator's partial fits in the ring");
 
 struct Params {
-  int M, N, K, Mp;
+  int M, N, K, Mp, Mp_pad;
   int ks;            // K parts per tile = cluster size
   int kblocks;       // K / 64
+  int stages;        // ring stages (runtime: stage size follows Mp)
+  int stage_bytes;   // ACC * 16 KB of W, then the token rows of the k block
   float scale;
   void* out;
   int64_t ldo;
@@ -100,12 +93,21 @@ __device__ __forceinline__ uint64_t present_adapters(const Params& p) {
 
 // Shrink (kEpiMaskAdapter): the tile's columns belong to adapters none of whose
 // tokens is in the step, so nothing reads them; the tile is skipped.
-__device__ __forceinline__ bool shrink_skipped(const Params& p, int n0) {
+__device__ __forceinline__ bool shrink_skipped(const Params& p, int n0, int rows) {
   if (p.tile_mask == nullptr) return false;
   uint64_t need = 0;
-  for (int c = 0; c < BW && n0 + c < p.N; c += p.mask_rank)
+  for (int c = 0; c < rows && n0 + c < p.N; c += p.mask_rank)
     need |= 1ull << (((n0 + c) / p.mask_rank) % p.mask_num_adapters);
   return (present_adapters(p) & need) == 0;
+}
+
+// S column offset of the LoRA slice holding weight row `row` (a 128-row
+// accumulator lies within one slice; the host checks the bounds).
+__device__ __forceinline__ int slice_base(const Params& p, int row) {
+  int sl = 0;
+  for (int i = 0; i < p.num_slices; ++i)
+    if (row >= p.slice_bounds[i]) sl = i;
+  return sl * p.num_adapters * p.rank_blocks * 32;
 }
 
 template <int EPI>
@@ -157,46 +159,41 @@ __device__ __forceinline__ void epilogue8(const Params& p, int m, int col, const
     *reinterpret_cast<uint4*>(dst) = pk;
 }
 
-template <int MPMAX, int EPI>
+// ACC accumulators of 128 weight rows each share every token tile: a CTA owns
+// 128 * ACC weight rows, and the tokens' bytes it reads per weight byte drop by ACC.
+template <int ACC, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     decode_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                        const __grid_constant__ CUtensorMap tm_lb, const __grid_constant__ CUtensorMap tm_s,
                        const Params p, uint32_t* err) {
-  using C = Cfg<MPMAX>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::BAR_OFF);
-  uint64_t* empty_bar = full_bar + C::STAGES;
-  uint64_t* tfull_bar = empty_bar + C::STAGES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + RING);
+  uint64_t* empty_bar = full_bar + MAX_STAGES;
+  uint64_t* tfull_bar = empty_bar + MAX_STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tfull_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ks = p.ks;
+  const int ks = p.ks, stages = p.stages;
   const int part = ks > 1 ? (int)cluster_ctarank() : 0;
   const int tile = blockIdx.x / ks;
-  const int n0 = tile * BW;  // first row of the tile in the (packed) weight
-  if (EPI == kEpiMaskAdapter && shrink_skipped(p, n0)) return;  // the whole cluster skips alike
+  const int n0 = tile * BW * ACC;  // first row of the tile in the (packed) weight
+  if (EPI == kEpiMaskAdapter && shrink_skipped(p, n0, BW * ACC)) return;  // the whole cluster skips alike
 
   // this CTA's blocks: a contiguous K range, then every ks-th LoRA block
   const int kb_lo = part * p.kblocks / ks, kb_hi = (part + 1) * p.kblocks / ks;
   const int n_main = kb_hi - kb_lo;
-  uint64_t amask = 0;
-  int s_base = 0;
-  if (EPI != kEpiMaskAdapter && p.lora) {
-    amask = present_adapters(p);
-    int sl = 0;
-    for (int i = 0; i < p.num_slices; ++i)
-      if (n0 >= p.slice_bounds[i]) sl = i;
-    s_base = sl * p.num_adapters * p.rank_blocks * 32;
-  }
+  const uint64_t amask = (EPI != kEpiMaskAdapter && p.lora) ? present_adapters(p) : 0ull;
   const int n_lora_all = __popcll(amask) * p.rank_blocks;
   const int n_lora = n_lora_all > part ? (n_lora_all - part + ks - 1) / ks : 0;
   const int total = n_main + n_lora;
-  const int tcols = p.Mp <= 32 ? 32 : (p.Mp <= 64 ? 64 : (p.Mp <= 128 ? 128 : 256));
+  const int w_bytes = ACC * BW * BK * 2;
+  const int need_cols = ACC * p.Mp_pad;
+  const int tcols = need_cols <= 32 ? 32 : (need_cols <= 64 ? 64 : (need_cols <= 128 ? 128 : (need_cols <= 256 ? 256 : 512)));
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
@@ -221,30 +218,33 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  uint32_t issued = 0;  // producer: loads issued (for the drain on the error path)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
+      uint32_t issued = 0;
       for (int i = 0; i < total; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
+        const int s = i % stages;
+        const uint32_t ph = (i / stages) & 1;
         if (*abort_flag || !mbar_wait(&empty_bar[s], ph ^ 1, err, kErrGemmWait)) {
           *abort_flag = 1;
           break;
         }
-        uint8_t* sa = smem + s * C::STAGE_BYTES;
-        uint8_t* sb = sa + C::A_BYTES;
+        uint8_t* sa = smem + s * p.stage_bytes;
+        uint8_t* sb = sa + w_bytes;
         if (i < n_main) {
           const int kx = (kb_lo + i) * BK;
-          mbar_arrive_expect_tx(&full_bar[s], C::A_BYTES + p.Mp * BK * 2);
-          if (EPI == kEpiSwiGLU) {
-            // out columns [64 tile, 64 tile + 64): their gate rows, then their up rows
-            const int o0 = tile * 64, it = o0 / p.swiglu_half, off = o0 % p.swiglu_half;
-            const int g0 = it * 2 * p.swiglu_half + off;
-            tma_load_2d(sa, &tm_w, &full_bar[s], kx, g0);
-            tma_load_2d(sa + 64 * 128, &tm_w, &full_bar[s], kx, g0 + p.swiglu_half);
-          } else {
-            tma_load_2d(sa, &tm_w, &full_bar[s], kx, n0);
+          mbar_arrive_expect_tx(&full_bar[s], w_bytes + p.Mp * BK * 2);
+#pragma unroll
+          for (int a = 0; a < ACC; ++a) {
+            if (EPI == kEpiSwiGLU) {
+              // out columns [64 (ACC tile + a), +64): their gate rows, then their up rows
+              const int o0 = (tile * ACC + a) * 64, it = o0 / p.swiglu_half, off = o0 % p.swiglu_half;
+              const int g0 = it * 2 * p.swiglu_half + off;
+              tma_load_2d(sa + a * BW * 128, &tm_w, &full_bar[s], kx, g0);
+              tma_load_2d(sa + a * BW * 128 + 64 * 128, &tm_w, &full_bar[s], kx, g0 + p.swiglu_half);
+            } else {
+              tma_load_2d(sa + a * BW * 128, &tm_w, &full_bar[s], kx, n0 + a * BW);
+            }
           }
           tma_load_2d(sb, &tm_x, &full_bar[s], kx, 0);
         } else {
@@ -254,17 +254,20 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int t = 0; t < ai; ++t) rem &= rem - 1;
           const int a_bit = __ffsll((long long)rem) - 1;
           const int kcol = a_bit * p.rank_blocks * 32 + rb * 32;
-          mbar_arrive_expect_tx(&full_bar[s], BW * 64 + p.Mp * 64);
-          tma_load_2d(sa, &tm_lb, &full_bar[s], kcol, n0);
-          tma_load_2d(sb, &tm_s, &full_bar[s], s_base + kcol, 0);
+          mbar_arrive_expect_tx(&full_bar[s], ACC * (BW * 64 + p.Mp * 64));
+#pragma unroll
+          for (int a = 0; a < ACC; ++a) {
+            tma_load_2d(sa + a * BW * 64, &tm_lb, &full_bar[s], kcol, n0 + a * BW);
+            tma_load_2d(sb + a * p.Mp_pad * 64, &tm_s, &full_bar[s], slice_base(p, n0 + a * BW) + kcol, 0);
+          }
         }
         ++issued;
       }
       if (*abort_flag) {
         // no TMA write may still be in flight into this CTA's shared memory at exit
-        const uint32_t first = issued > (uint32_t)C::STAGES ? issued - C::STAGES : 0;
+        const uint32_t first = issued > (uint32_t)stages ? issued - stages : 0;
         for (uint32_t j = first; j < issued; ++j)
-          mbar_wait(&full_bar[j % C::STAGES], (j / C::STAGES) & 1, err, kErrGemmWait);
+          mbar_wait(&full_bar[j % stages], (j / stages) & 1, err, kErrGemmWait);
       }
     }
   } else if (warp == 1) {
@@ -273,84 +276,97 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t idesc = umma_idesc_bf16(BW, p.Mp);
       bool ok = true;
       for (int i = 0; i < total; ++i) {
-        const int s = i % C::STAGES;
-        const uint32_t ph = (i / C::STAGES) & 1;
+        const int s = i % stages;
+        const uint32_t ph = (i / stages) & 1;
         if (*abort_flag || !mbar_wait(&full_bar[s], ph, err, kErrGemmWait)) {
           *abort_flag = 1;
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
-        const uint32_t sb = sa + C::A_BYTES;
+        const uint32_t sa = smem_u32(smem + s * p.stage_bytes);
+        const uint32_t sb = sa + w_bytes;
         if (i < n_main) {
-          const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sb);
+          const uint64_t bd = umma_desc_sw128(sb);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) umma_bf16(tmem_base, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0);
+          for (int a = 0; a < ACC; ++a) {
+            const uint64_t ad = umma_desc_sw128(sa + a * BW * 128);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk)
+              umma_bf16(tmem_base + a * p.Mp_pad, ad + 2 * kk, bd + 2 * kk, idesc, (i | kk) != 0);
+          }
         } else {
-          const uint64_t ad = umma_desc_sw64(sa), bd = umma_desc_sw64(sb);
 #pragma unroll
-          for (int kk = 0; kk < 2; ++kk) umma_bf16(tmem_base, ad + 2 * kk, bd + 2 * kk, idesc, 1);
+          for (int a = 0; a < ACC; ++a) {
+            const uint64_t ad = umma_desc_sw64(sa + a * BW * 64), bd = umma_desc_sw64(sb + a * p.Mp_pad * 64);
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) umma_bf16(tmem_base + a * p.Mp_pad, ad + 2 * kk, bd + 2 * kk, idesc, 1);
+          }
         }
         umma_commit(&empty_bar[s]);
       }
       if (ok) umma_commit(tfull_bar);
     }
-  } else {
-    // ---------------- TMEM drain: fp32 partial -> shared memory, token-major ----------------
-    const int q = warp & 3;  // the TMEM lane quarter this warp may read
-    if (!*abort_flag && mbar_wait(tfull_bar, 0, err, kErrGemmWait)) {
-      tc_fence_after();
-      float* P = reinterpret_cast<float*>(smem);
+  }
+  // TMEM drain (warps 2..5), then the cluster reduction and epilogue (all warps), one
+  // accumulator at a time through the same shared-memory partial buffer
+  bool ready = false;
+  if (warp >= 2) {
+    ready = !*abort_flag && mbar_wait(tfull_bar, 0, err, kErrGemmWait);
+    if (!ready) *abort_flag = 1;
+    else tc_fence_after();
+  }
+  const uint32_t pbase = smem_u32(smem);
+  float* P = reinterpret_cast<float*>(smem);
+#pragma unroll 1
+  for (int a = 0; a < ACC; ++a) {
+    if (warp >= 2 && ready) {
+      const int q = warp & 3;  // the TMEM lane quarter this warp may read
       for (int c = 0; c < p.Mp; c += 32) {
         uint32_t r[32];
-        tmem_ld32(tmem_base + c + ((uint32_t)(q * 32) << 16), r);
+        tmem_ld32(tmem_base + a * p.Mp_pad + c + ((uint32_t)(q * 32) << 16), r);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) P[(c + j) * C::P_STRIDE + q * 32 + lane] = __uint_as_float(r[j]);
+        for (int j = 0; j < 32; ++j) P[(c + j) * P_STRIDE + q * 32 + lane] = __uint_as_float(r[j]);
       }
-    } else {
-      *abort_flag = 1;
     }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (ks > 1) cluster_sync();  // every CTA's partial is in its shared memory
-
-  // ---------------- cluster reduction + epilogue ----------------
-  if (!*abort_flag) {
-    const int rows_per = (p.M + ks - 1) / ks;
-    const int r0 = part * rows_per, r1 = min(p.M, r0 + rows_per);
-    const uint32_t pbase = smem_u32(smem);
-    constexpr int GROUPS = (EPI == kEpiSwiGLU) ? 8 : 16;  // 8-column groups per token row
-    const int n_items = max(0, r1 - r0) * GROUPS;
-    for (int it = threadIdx.x; it < n_items; it += THREADS) {
-      const int m = r0 + it / GROUPS;
-      const int c = (it % GROUPS) * 8;
-      float v[8], u[8];
+    __syncthreads();
+    if (ks > 1) cluster_sync();  // every CTA's partial of accumulator a is in its shared memory
+    if (!*abort_flag) {
+      const int rows_per = (p.M + ks - 1) / ks;
+      const int r0 = part * rows_per, r1 = min(p.M, r0 + rows_per);
+      constexpr int GROUPS = (EPI == kEpiSwiGLU) ? 8 : 16;  // 8-column groups per token row
+      const int n_items = max(0, r1 - r0) * GROUPS;
+      const int row0 = n0 + a * BW;
+      for (int it = threadIdx.x; it < n_items; it += THREADS) {
+        const int m = r0 + it / GROUPS;
+        const int c = (it % GROUPS) * 8;
+        float v[8], u[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = u[j] = 0.f;
-      const uint32_t local = pbase + (uint32_t)((m * C::P_STRIDE + c) * 4);
+        for (int j = 0; j < 8; ++j) v[j] = u[j] = 0.f;
+        const uint32_t local = pbase + (uint32_t)((m * P_STRIDE + c) * 4);
 #pragma unroll 1
-      for (int q = 0; q < ks; ++q) {  // fixed order: deterministic sums
-        const uint32_t src = ks > 1 ? mapa_shared(local, (uint32_t)q) : local;
-        const float4 a0 = ld_dsmem_f4(src), a1 = ld_dsmem_f4(src + 16);
-        v[0] += a0.x; v[1] += a0.y; v[2] += a0.z; v[3] += a0.w;
-        v[4] += a1.x; v[5] += a1.y; v[6] += a1.z; v[7] += a1.w;
+        for (int q = 0; q < ks; ++q) {  // fixed order: deterministic sums
+          const uint32_t src = ks > 1 ? mapa_shared(local, (uint32_t)q) : local;
+          const float4 a0 = ld_dsmem_f4(src), a1 = ld_dsmem_f4(src + 16);
+          v[0] += a0.x; v[1] += a0.y; v[2] += a0.z; v[3] += a0.w;
+          v[4] += a1.x; v[5] += a1.y; v[6] += a1.z; v[7] += a1.w;
+          if (EPI == kEpiSwiGLU) {
+            const float4 b0 = ld_dsmem_f4(src + 256), b1 = ld_dsmem_f4(src + 256 + 16);
+            u[0] += b0.x; u[1] += b0.y; u[2] += b0.z; u[3] += b0.w;
+            u[4] += b1.x; u[5] += b1.y; u[6] += b1.z; u[7] += b1.w;
+          }
+        }
         if (EPI == kEpiSwiGLU) {
-          const float4 b0 = ld_dsmem_f4(src + 256), b1 = ld_dsmem_f4(src + 256 + 16);
-          u[0] += b0.x; u[1] += b0.y; u[2] += b0.z; u[3] += b0.w;
-          u[4] += b1.x; u[5] += b1.y; u[6] += b1.z; u[7] += b1.w;
+          epilogue8<EPI>(p, m, (tile * ACC + a) * 64 + c, v, u);
+        } else if (row0 + c < p.N) {
+          epilogue8<EPI>(p, m, row0 + c, v, u);
         }
       }
-      if (EPI == kEpiSwiGLU) {
-        epilogue8<EPI>(p, m, tile * 64 + c, v, u);
-      } else if (n0 + c < p.N) {
-        epilogue8<EPI>(p, m, n0 + c, v, u);
-      }
     }
+    if (ks > 1) cluster_sync();  // peers are done reading this CTA's partial
+    __syncthreads();             // the partial buffer is rewritten for the next accumulator
   }
-  if (ks > 1) cluster_sync();  // peers are done reading this CTA's partial
   if (*abort_flag) {
     // error path: MMAs and copies this CTA issued may still be in flight; give them
     // time to finish before the tensor memory is released (bounded, ~1 ms)
@@ -382,21 +398,20 @@ static int dec_num_sms() {
   return n;
 }
 
-template <int MPMAX, int EPI>
+template <int ACC, int EPI>
 static void launch_decode(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tlb,
                           const CUtensorMap& ts, const dec::Params& p, int n_tiles, uint32_t* err,
                           cudaStream_t stream) {
-  using C = dec::Cfg<MPMAX>;
-  auto kfn = dec::decode_gemm_kernel<MPMAX, EPI>;
+  auto kfn = dec::decode_gemm_kernel<ACC, EPI>;
   static bool configured = false;  // per instantiation
   if (!configured) {
-    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(n_tiles * p.ks), 1, 1);
   cfg.blockDim = dim3(dec::THREADS, 1, 1);
-  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.dynamicSmemBytes = dec::SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -409,25 +424,77 @@ static void launch_decode(const CUtensorMap& tw, const CUtensorMap& tx, const CU
   GSB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kfn, tw, tx, tlb, ts, p, err));
 }
 
-template <int MPMAX>
+template <int ACC>
 static void dispatch_decode(int epi, const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& tlb,
                             const CUtensorMap& ts, const dec::Params& p, int n_tiles, uint32_t* err,
                             cudaStream_t st) {
   switch (epi) {
-    case kEpiStore: launch_decode<MPMAX, kEpiStore>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
-    case kEpiResAdd: launch_decode<MPMAX, kEpiResAdd>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
-    case kEpiSwiGLU: launch_decode<MPMAX, kEpiSwiGLU>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
-    case kEpiMaskAdapter: launch_decode<MPMAX, kEpiMaskAdapter>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
-    case kEpiMultimemRed: launch_decode<MPMAX, kEpiMultimemRed>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
+    case kEpiStore: launch_decode<ACC, kEpiStore>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
+    case kEpiResAdd: launch_decode<ACC, kEpiResAdd>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
+    case kEpiSwiGLU: launch_decode<ACC, kEpiSwiGLU>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
+    case kEpiMaskAdapter: launch_decode<ACC, kEpiMaskAdapter>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
+    case kEpiMultimemRed: launch_decode<ACC, kEpiMultimemRed>(tw, tx, tlb, ts, p, n_tiles, err, st); break;
   }
 }
 
-// K parts per weight tile: the most that keep n_tiles * ks within one wave of
-// SMs, at most 8 (portable cluster) and at least four 64-deep K blocks per part.
-static int choose_ks(int n_tiles, int kblocks, int nsms) {
-  int ks = std::max(1, std::min(dec::MAX_KS, nsms / std::max(1, n_tiles)));
-  while (ks > 1 && kblocks / ks < 4) --ks;
-  return ks;
+// Clusters of `ks` CTAs of the decode kernel that fit on the GPU at once (queried
+// once per device, accumulator count and cluster size; every epilogue variant
+// has the same shared memory and block size). Clusters must sit inside one GPC,
+// so large clusters leave SMs unused: on B200, 15 clusters of 8 fit (120 CTAs)
+// but 33 of 4 (132).
+template <int ACC>
+static int max_active_clusters(int ks) {
+  static int cached[64][dec::MAX_KS + 1] = {{0}};
+  int dev = 0;
+  GSB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 64 && cached[dev][ks]) return cached[dev][ks];
+  auto kfn = dec::decode_gemm_kernel<ACC, kEpiStore>;
+  GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::SMEM_BYTES));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(ks * dec_num_sms()), 1, 1);
+  cfg.blockDim = dim3(dec::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = dec::SMEM_BYTES;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)ks;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess || n <= 0) {
+    (void)cudaGetLastError();
+    n = dec_num_sms() / ks;
+  }
+  if (dev < 64) cached[dev][ks] = n;
+  return n;
+}
+
+// Split of a call over CTAs: `acc` accumulators (128 * acc weight rows per CTA)
+// and `ks` K parts per tile. Cost = waves of clusters x the bytes one CTA
+// streams (its weight rows plus the token rows it re-reads per K block); the
+// cheapest split wins. Every part keeps at least four 64-deep K blocks.
+struct DecodeSplit {
+  int acc, ks, n_tiles;
+};
+
+static DecodeSplit choose_split(int N, int Mp, int kblocks, bool two_ok) {
+  DecodeSplit best{1, 1, (N + dec::BW - 1) / dec::BW};
+  double best_cost = 1e300;
+  for (int acc = 1; acc <= (two_ok ? 2 : 1); ++acc) {
+    const int n_tiles = (N + dec::BW * acc - 1) / (dec::BW * acc);
+    for (int ks = 1; ks <= dec::MAX_KS; ++ks) {
+      if (ks > 1 && kblocks / ks < 4) break;
+      const int maxc = acc == 2 ? max_active_clusters<2>(ks) : max_active_clusters<1>(ks);
+      const int waves = (n_tiles + maxc - 1) / maxc;
+      const double cost = (double)waves * (double)(dec::BW * acc + Mp) * ((double)kblocks / ks);
+      if (cost < best_cost * 0.999) {
+        best_cost = cost;
+        best = DecodeSplit{acc, ks, n_tiles};
+      }
+    }
+  }
+  return best;
 }
 
 bool decode_gemm_try(const DecodeGemmArgs& a, uint32_t* err, cudaStream_t stream) {
@@ -455,6 +522,7 @@ bool decode_gemm_try(const DecodeGemmArgs& a, uint32_t* err, cudaStream_t stream
   p.N = a.N;
   p.K = a.K;
   p.Mp = (a.M + 15) / 16 * 16;
+  p.Mp_pad = (p.Mp + 31) / 32 * 32;
   p.kblocks = a.K / 64;
   p.scale = a.scale;
   p.out = a.out;
@@ -462,8 +530,14 @@ bool decode_gemm_try(const DecodeGemmArgs& a, uint32_t* err, cudaStream_t stream
   p.residual = reinterpret_cast<const __nv_bfloat16*>(a.residual);
   p.ldr = a.ldr;
   p.swiglu_half = a.swiglu_tile / 2;
-  const int n_tiles = (a.N + dec::BW - 1) / dec::BW;
-  p.ks = choose_ks(n_tiles, p.kblocks, dec_num_sms());
+  // one or two 128-row accumulators per CTA (two need Mp_pad <= 256 columns each, and
+  // for SwiGLU a whole number of 128-column output tiles)
+  const bool two_ok = 2 * p.Mp_pad <= 512 && (epi != kEpiSwiGLU || (a.N / 2) % 128 == 0);
+  const DecodeSplit sp = choose_split(a.N, p.Mp, p.kblocks, two_ok);
+  const int acc = sp.acc, n_tiles = sp.n_tiles;
+  p.ks = sp.ks;
+  p.stage_bytes = acc * dec::BW * dec::BK * 2 + (p.Mp_pad * dec::BK * 2 + 1023) / 1024 * 1024;
+  p.stages = std::min(dec::MAX_STAGES, dec::RING / p.stage_bytes);
   p.lora = lora ? 1 : 0;
   p.tile_mask = nullptr;
   if (lora) {
@@ -491,10 +565,10 @@ bool decode_gemm_try(const DecodeGemmArgs& a, uint32_t* err, cudaStream_t stream
     ts = make_tmap_bf16_2d(a.s, (uint64_t)a.M, (uint64_t)a.s_cols, (uint64_t)a.lds, 32, mp_box,
                            CU_TENSOR_MAP_SWIZZLE_64B);
   }
-  if (p.Mp <= 128)
-    dispatch_decode<128>(epi, tw, tx, tlb, ts, p, n_tiles, err, stream);
+  if (acc == 2)
+    dispatch_decode<2>(epi, tw, tx, tlb, ts, p, n_tiles, err, stream);
   else
-    dispatch_decode<256>(epi, tw, tx, tlb, ts, p, n_tiles, err, stream);
+    dispatch_decode<1>(epi, tw, tx, tlb, ts, p, n_tiles, err, stream);
   return true;
 }
 

@@ -275,12 +275,14 @@ class LLM:
             max_tokens = max(ecfg.max_num_batched_tokens, ecfg.max_num_seqs)
             nb = ecfg.num_kv_blocks or 64
             if path is not None:
-                from ..checkpoint import load_state_dict
+                from ..checkpoint import LazyCheckpoint
 
-                sd = load_state_dict(path)
-                nm = NativeGraniteSwitch.from_state_dict(config, sd, self.device, max_tokens, 1, tp_rank, tp,
+                # tensors are read one at a time from the memory-mapped shards, each rank
+                # keeping only its shard; the loader audits that none went unused
+                ckpt = LazyCheckpoint(path)
+                nm = NativeGraniteSwitch.from_state_dict(config, ckpt, self.device, max_tokens, 1, tp_rank, tp,
                                                          tp_group, ecfg.max_num_seqs, pipeline)
-                del sd
+                ckpt.close()
             else:
                 ri = dict(random_init or {})
                 nm = NativeGraniteSwitch.from_random(config, self.device, max_tokens, 1, tp_rank=tp_rank,

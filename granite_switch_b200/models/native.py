@@ -193,8 +193,17 @@ class NativeGraniteSwitch:
         With ``pipeline`` only this stage's decoder layers are read.
         """
         self = cls(config, device, max_tokens, num_kv_blocks, tp_rank, tp_size, tp_group, max_seqs, pipeline)
-        get = sd.__getitem__ if isinstance(sd, dict) else sd
-        has = (lambda k: k in sd) if isinstance(sd, dict) else (lambda k: True)
+        get = sd.__getitem__ if hasattr(sd, "__getitem__") else sd
+        if hasattr(sd, "__contains__"):
+            def has(k):
+                return k in sd
+        else:  # a bare getter: probe by reading
+            def has(k):
+                try:
+                    get(k)
+                    return True
+                except KeyError:
+                    return False
         na = config.num_adapters
         h, d = config.hidden_size, config.head_dim_eff
         q, kv = config.num_attention_heads * d, config.num_key_value_heads * d
@@ -246,6 +255,8 @@ class NativeGraniteSwitch:
         if has("model.switch.adapter_kind_lut"):
             self.kind_lut = get("model.switch.adapter_kind_lut").to(device, torch.bool)
         self._finish_weights(embed, get("model.norm.weight").to(device, torch.bfloat16), lm)
+        if hasattr(sd, "unread"):
+            audit_unread(config, sd.unread(), self.layer_lo, self.layer_hi)
         return self
 
     @classmethod
@@ -680,6 +691,34 @@ class NativeGraniteSwitch:
                 ns = 1
             plans.append((ws, wr, rows, ns))
         return plans
+
+
+def audit_unread(config: GraniteSwitchConfig, unread: list[str], layer_lo: int, layer_hi: int) -> None:
+    """Load audit: every checkpoint tensor must have been packed, except those this
+    runtime does not use by design. A leftover name means a layout this loader does
+    not understand (an unfused projection, a renamed module) whose weights would
+    otherwise be dropped silently (reference: src/granite_switch/vllm/decoder/interface.py:95-127
+    raises on unloaded parameters).
+
+    Unused by design: the Kerdock codebook (routing is the exact scan), the
+    all-zero cross-stream base weight of Shadow-Residual checkpoints, an LM head
+    equal to the tied embedding, and other pipeline stages' layers.
+    """
+    import re
+
+    bad = []
+    for k in unread:
+        if k == "model.switch.codebook" or k.endswith("cross_stream.base_layer.weight"):
+            continue
+        if k == "lm_head.weight" and config.tie_word_embeddings:
+            continue
+        m = re.match(r"model\.layers\.(\d+)\.", k)
+        if m and not (layer_lo <= int(m.group(1)) < layer_hi):
+            continue
+        bad.append(k)
+    if bad:
+        more = f" (+{len(bad) - 8} more)" if len(bad) > 8 else ""
+        raise ValueError(f"checkpoint tensors this loader does not use: {', '.join(bad[:8])}{more}")
 
 
 def split_layers(num_layers: int, stage: int, stages: int) -> tuple[int, int]:

@@ -134,7 +134,7 @@ def _hbm_gbs() -> float:
 
 def decode_sweep(ms, iters: int = 50, rotate_bytes: int = 400 << 20) -> None:
     """Decode-sized projections (the 8B shapes at M tokens, 12 adapters r32 where LoRA is on):
-    event-timed per call with enough weight copies rotated (``rotate_bytes`` in all, over three
+    device time per call from CUDA-graph replays of ``iters`` calls with enough weight copies rotated (``rotate_bytes`` in all, over three
     times the 126 MB L2) that every call streams its weights from HBM, the operand-swapped decode kernel against the general kernel. Prints
     microseconds and the weight bytes' fraction of the measured HBM copy bandwidth."""
     dev = torch.device("cuda", 0)
@@ -189,12 +189,20 @@ def decode_sweep(ms, iters: int = 50, rotate_bytes: int = 400 << 20) -> None:
                     for _ in range(5):
                         call()
                     torch.cuda.synchronize()
+                    # device time only: the calls are replayed from a CUDA graph, so host
+                    # launch cost (which the engine overlaps with earlier kernels) is excluded
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph):
+                        for _ in range(iters):
+                            call()
+                    graph.replay()
+                    torch.cuda.synchronize()
                     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     a.record()
-                    for _ in range(iters):
-                        call()
+                    graph.replay()
                     b.record()
                     torch.cuda.synchronize()
+                    del graph
                     us = a.elapsed_time(b) / iters * 1e3
                     gbs = n * k * 2 / (us * 1e-6) / 1e9
                     res[f"{tag}_{what}"] = dict(us=round(us, 2), hbm_frac=round(gbs / hbm, 3))
