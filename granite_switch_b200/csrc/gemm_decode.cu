@@ -35,7 +35,11 @@
 #include "gemm_common.cuh"
 #include "tma_util.h"
 
+#include <ATen/ATen.h>
+
 #include <algorithm>
+#include <utility>
+#include <vector>
 
 namespace gsb {
 namespace dec {
@@ -48,10 +52,17 @@ constexpr int MAX_STAGES = 8;
 constexpr int RING = 192 * 1024;                      // operand ring (the partial reuses it)
 constexpr int SMEM_BYTES = RING + 512 + 1024;         // + barriers + alignment
 constexpr int P_STRIDE = BW;                          // fp32 per token row of a drained partial
-static_assert(256 * P_STRIDE * 4 <= RING, "one accumulator's partial fits in the ring");
+// Tokens per CTA of a K-split cluster in the reduction: ceil(M / ks) rounded up to 32,
+// so every 32-column chunk of an accumulator belongs to one CTA. The receive buffer of
+// one accumulator is ks * rows_per rows of P_STRIDE fp32 (the host keeps it in the ring).
+__host__ __device__ constexpr int rows_per_part(int M, int ks) { return ((M + ks - 1) / ks + 31) / 32 * 32; }
+__host__ __device__ constexpr bool split_fits(int M, int ks) { return ks * rows_per_part(M, ks) * P_STRIDE * 4 <= RING; }
+static_assert(split_fits(256, 1) && split_fits(256, 2) && split_fits(256, 4) && split_fits(256, 8),
+              "power-of-two splits of 256 tokens fit the ring");
 
 struct Params {
   int M, N, K, Mp, Mp_pad;
+  int rows_per;  // rows_per_part(M, ks)
   int ks;            // K parts per tile = cluster size
   int kblocks;       // K / 64
   int stages;        // ring stages (runtime: stage size follows Mp)
@@ -70,7 +81,18 @@ struct Params {
   const uint64_t* tile_mask;  // adapters present per 128-token tile (expand, or shrink tiles to skip)
   const int32_t* row_adapter;
   int mask_rank, mask_num_adapters;
+  // optional phase timestamps (%globaltimer, ns) per CTA: [start, set-up done, first
+  // stage landed, accumulator ready, partials shared, epilogue done, end, reduction
+  // barrier passed, warp 2's partial pushed, every drain warp's partial pushed]
+  uint64_t* trace;
 };
+constexpr int TRACE_SLOTS = 16;
+
+__device__ __forceinline__ void trace_mark(const Params& p, int slot) {
+  if (p.trace != nullptr && threadIdx.x % 32 == 0)
+    atomicMax(reinterpret_cast<unsigned long long*>(p.trace + blockIdx.x * TRACE_SLOTS + slot),
+              (unsigned long long)globaltimer_ns());
+}
 
 __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
   float4 v;
@@ -79,6 +101,18 @@ __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
                : "r"(addr)
                : "memory");
   return v;
+}
+
+template <int OFF>
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0+%2], %1;" ::"r"(addr), "f"(v), "n"(OFF));
+}
+
+// r[j] -> the fp32 at byte addr + j * P_STRIDE * 4 of a cluster peer's shared memory
+// (one store per value, offsets folded into the instruction).
+template <int... J>
+__device__ __forceinline__ void push_rows32(uint32_t addr, const uint32_t (&r)[32], std::integer_sequence<int, J...>) {
+  (st_dsmem_f32<J * P_STRIDE * 4>(addr, __uint_as_float(r[J])), ...);
 }
 
 __device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
@@ -110,8 +144,25 @@ __device__ __forceinline__ int slice_base(const Params& p, int row) {
   return sl * p.num_adapters * p.rank_blocks * 32;
 }
 
+// Global inputs of an epilogue item (loaded ahead of the reduction, so their
+// latency overlaps it): the residual's 8 values and the row's adapter.
+struct EpiIn {
+  uint4 res;
+  int ra;
+};
+
 template <int EPI>
-__device__ __forceinline__ void epilogue8(const Params& p, int m, int col, const float (&v)[8], const float (&u)[8]) {
+__device__ __forceinline__ EpiIn epilogue_inputs(const Params& p, int m, int col) {
+  EpiIn in{make_uint4(0u, 0u, 0u, 0u), 0};
+  if (EPI == kEpiResAdd || (EPI == kEpiMultimemRed && p.residual != nullptr))
+    in.res = *reinterpret_cast<const uint4*>(p.residual + (int64_t)m * p.ldr + col);
+  if (EPI == kEpiMaskAdapter) in.ra = p.row_adapter[m];
+  return in;
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue8(const Params& p, int m, int col, const float (&v)[8], const float (&u)[8],
+                                          const EpiIn& in) {
   if (EPI == kEpiSwiGLU) {
     uint32_t pk[4];
 #pragma unroll
@@ -128,8 +179,7 @@ __device__ __forceinline__ void epilogue8(const Params& p, int m, int col, const
   float o[8];
   const bool has_res = (EPI == kEpiResAdd) || (EPI == kEpiMultimemRed && p.residual != nullptr);
   if (has_res) {
-    const uint4 r4 = *reinterpret_cast<const uint4*>(p.residual + (int64_t)m * p.ldr + col);
-    const uint32_t rr[4] = {r4.x, r4.y, r4.z, r4.w};
+    const uint32_t rr[4] = {in.res.x, in.res.y, in.res.z, in.res.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       // the projection is rounded to bf16 before the residual add
@@ -144,10 +194,11 @@ __device__ __forceinline__ void epilogue8(const Params& p, int m, int col, const
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j] = v[j] * p.scale;
     if (EPI == kEpiMaskAdapter) {
-      const int ra = p.row_adapter[m];
+      // the 8 columns share one adapter: mask_rank is a multiple of 8 (checked by the host)
+      if ((col / p.mask_rank) % p.mask_num_adapters + 1 != in.ra) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (((col + j) / p.mask_rank) % p.mask_num_adapters + 1 != ra) o[j] = 0.f;
+        for (int j = 0; j < 8; ++j) o[j] = 0.f;
+      }
     }
   }
   const uint4 pk = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
@@ -175,6 +226,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) trace_mark(p, 0);
   const int ks = p.ks, stages = p.stages;
   const int part = ks > 1 ? (int)cluster_ctarank() : 0;
   const int tile = blockIdx.x / ks;
@@ -217,6 +269,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (warp == 0) trace_mark(p, 1);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -283,6 +336,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = false;
           break;
         }
+        if (i == 0 && p.trace != nullptr)
+          p.trace[blockIdx.x * TRACE_SLOTS + 2] = globaltimer_ns();
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + s * p.stage_bytes);
         const uint32_t sb = sa + w_bytes;
@@ -308,64 +363,88 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (ok) umma_commit(tfull_bar);
     }
   }
-  // TMEM drain (warps 2..5), then the cluster reduction and epilogue (all warps), one
-  // accumulator at a time through the same shared-memory partial buffer
+  // Reduction over the cluster, one accumulator at a time. Token m belongs to CTA
+  // owner(m) = m / rows_per of the cluster. After every CTA's main loop is done (the
+  // shared-memory rings are free), the drain warps push their fp32 partial rows from
+  // TMEM straight into the owner's receive buffer R[part][m - owner's first row][128]
+  // with remote shared-memory stores, which need no round trip; after a second
+  // cluster barrier each CTA sums its rows over the ks parts from its own shared
+  // memory, in a fixed order (deterministic), and applies the epilogue.
   bool ready = false;
   if (warp >= 2) {
     ready = !*abort_flag && mbar_wait(tfull_bar, 0, err, kErrGemmWait);
     if (!ready) *abort_flag = 1;
     else tc_fence_after();
+    if (warp == 2) trace_mark(p, 3);
   }
-  const uint32_t pbase = smem_u32(smem);
-  float* P = reinterpret_cast<float*>(smem);
+  const int rows_per = p.rows_per;
+  const uint32_t rbase = smem_u32(smem);
+  const float* R = reinterpret_cast<const float*>(smem);
 #pragma unroll 1
   for (int a = 0; a < ACC; ++a) {
+    __syncthreads();
+    if (ks > 1) cluster_sync();  // a == 0: every main loop is done; a > 0: the last sums read R
+    if (warp == 2) trace_mark(p, 7);
     if (warp >= 2 && ready) {
       const int q = warp & 3;  // the TMEM lane quarter this warp may read
-      for (int c = 0; c < p.Mp; c += 32) {
+      const int n = q * 32 + lane;
+      // token m goes to row (part * rows_per + m - owner * rows_per) of CTA owner's R,
+      // owner = m / rows_per; rows_per is a multiple of 32, so one 32-token chunk has
+      // one owner and each value is one store at a fixed offset from the chunk's base
+      float* Rw = reinterpret_cast<float*>(smem);
+      for (int c = 0, owner = 0, oc = 0; c < p.M; c += 32) {
+        if (c - oc >= rows_per) {
+          ++owner;
+          oc += rows_per;
+        }
         uint32_t r[32];
         tmem_ld32(tmem_base + a * p.Mp_pad + c + ((uint32_t)(q * 32) << 16), r);
         tmem_wait_ld();
+        const int row = part * rows_per + c - oc;  // rows past M land in the owner's buffer, unread
+        if (ks > 1) {
+          push_rows32(mapa_shared(rbase + (uint32_t)(row * P_STRIDE + n) * 4u, (uint32_t)owner), r,
+                      std::make_integer_sequence<int, 32>{});
+        } else {
+          float* dst = Rw + row * P_STRIDE + n;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) P[(c + j) * P_STRIDE + q * 32 + lane] = __uint_as_float(r[j]);
+          for (int j = 0; j < 32; ++j) dst[j * P_STRIDE] = __uint_as_float(r[j]);
+        }
       }
+      if (warp == 2) trace_mark(p, 8);
+      trace_mark(p, 9);
     }
     __syncthreads();
-    if (ks > 1) cluster_sync();  // every CTA's partial of accumulator a is in its shared memory
+    if (ks > 1) cluster_sync();  // every partial row has landed in its owner's R
+    if (warp == 0) trace_mark(p, 4);
     if (!*abort_flag) {
-      const int rows_per = (p.M + ks - 1) / ks;
       const int r0 = part * rows_per, r1 = min(p.M, r0 + rows_per);
       constexpr int GROUPS = (EPI == kEpiSwiGLU) ? 8 : 16;  // 8-column groups per token row
       const int n_items = max(0, r1 - r0) * GROUPS;
       const int row0 = n0 + a * BW;
       for (int it = threadIdx.x; it < n_items; it += THREADS) {
-        const int m = r0 + it / GROUPS;
-        const int c = (it % GROUPS) * 8;
+        const int lm = it / GROUPS, c = (it % GROUPS) * 8, m = r0 + lm;
+        const int col = (EPI == kEpiSwiGLU) ? (tile * ACC + a) * 64 + c : row0 + c;
+        if (EPI != kEpiSwiGLU && col >= p.N) continue;
+        const EpiIn ein = epilogue_inputs<EPI>(p, m, col);
         float v[8], u[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[j] = u[j] = 0.f;
-        const uint32_t local = pbase + (uint32_t)((m * P_STRIDE + c) * 4);
 #pragma unroll 1
-        for (int q = 0; q < ks; ++q) {  // fixed order: deterministic sums
-          const uint32_t src = ks > 1 ? mapa_shared(local, (uint32_t)q) : local;
-          const float4 a0 = ld_dsmem_f4(src), a1 = ld_dsmem_f4(src + 16);
+        for (int q = 0; q < ks; ++q) {
+          const float* src = R + (q * rows_per + lm) * P_STRIDE + c;
+          const float4 a0 = *reinterpret_cast<const float4*>(src), a1 = *reinterpret_cast<const float4*>(src + 4);
           v[0] += a0.x; v[1] += a0.y; v[2] += a0.z; v[3] += a0.w;
           v[4] += a1.x; v[5] += a1.y; v[6] += a1.z; v[7] += a1.w;
           if (EPI == kEpiSwiGLU) {
-            const float4 b0 = ld_dsmem_f4(src + 256), b1 = ld_dsmem_f4(src + 256 + 16);
+            const float4 b0 = *reinterpret_cast<const float4*>(src + 64), b1 = *reinterpret_cast<const float4*>(src + 68);
             u[0] += b0.x; u[1] += b0.y; u[2] += b0.z; u[3] += b0.w;
             u[4] += b1.x; u[5] += b1.y; u[6] += b1.z; u[7] += b1.w;
           }
         }
-        if (EPI == kEpiSwiGLU) {
-          epilogue8<EPI>(p, m, (tile * ACC + a) * 64 + c, v, u);
-        } else if (row0 + c < p.N) {
-          epilogue8<EPI>(p, m, row0 + c, v, u);
-        }
+        epilogue8<EPI>(p, m, col, v, u, ein);
       }
     }
-    if (ks > 1) cluster_sync();  // peers are done reading this CTA's partial
-    __syncthreads();             // the partial buffer is rewritten for the next accumulator
+    trace_mark(p, 5);
   }
   if (*abort_flag) {
     // error path: MMAs and copies this CTA issued may still be in flight; give them
@@ -379,6 +458,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, tcols);
   }
+  if (warp == 0) trace_mark(p, 6);
 }
 
 }  // namespace dec
@@ -471,30 +551,43 @@ static int max_active_clusters(int ks) {
 }
 
 // Split of a call over CTAs: `acc` accumulators (128 * acc weight rows per CTA)
-// and `ks` K parts per tile. Cost = waves of clusters x the bytes one CTA
-// streams (its weight rows plus the token rows it re-reads per K block); the
-// cheapest split wins. Every part keeps at least four 64-deep K blocks.
+// and `ks` K parts per tile. At a few hundred tokens the tensor work per weight
+// byte matches the HBM stream, so every SM has to take part in one wave:
+// measured on B200 at M = 222, 96 CTAs with two accumulators ran the 4096-row
+// projections 1.3-1.7x slower than 128 CTAs with one, and a second wave of
+// clusters doubled the time. The rule: one accumulator and the largest K split
+// whose clusters all fit at once (at most one wave, at least four 64-deep K
+// blocks per part); when even an unsplit grid of one-accumulator tiles needs a
+// second wave, two accumulators per CTA if that fits one wave, else the general
+// kernel takes the call (acc = 0).
 struct DecodeSplit {
   int acc, ks, n_tiles;
 };
 
-static DecodeSplit choose_split(int N, int Mp, int kblocks, bool two_ok) {
-  DecodeSplit best{1, 1, (N + dec::BW - 1) / dec::BW};
-  double best_cost = 1e300;
-  for (int acc = 1; acc <= (two_ok ? 2 : 1); ++acc) {
-    const int n_tiles = (N + dec::BW * acc - 1) / (dec::BW * acc);
-    for (int ks = 1; ks <= dec::MAX_KS; ++ks) {
-      if (ks > 1 && kblocks / ks < 4) break;
-      const int maxc = acc == 2 ? max_active_clusters<2>(ks) : max_active_clusters<1>(ks);
-      const int waves = (n_tiles + maxc - 1) / maxc;
-      const double cost = (double)waves * (double)(dec::BW * acc + Mp) * ((double)kblocks / ks);
-      if (cost < best_cost * 0.999) {
-        best_cost = cost;
-        best = DecodeSplit{acc, ks, n_tiles};
-      }
-    }
+// A/B override of the split (gemm_decode_force_split): 0 keeps the rule above.
+static int g_force_acc = 0, g_force_ks = 0;
+// Phase trace buffer (gemm_decode_trace): uint64 [CTAs][16], or null.
+static uint64_t* g_trace = nullptr;
+
+static DecodeSplit choose_split(int N, int M, int kblocks, bool two_ok) {
+  if (g_force_acc > 0 && g_force_ks > 0 && (g_force_acc == 1 || two_ok)) {
+    int ks = std::min(g_force_ks, std::max(1, kblocks));
+    while (ks > 1 && !dec::split_fits(M, ks)) --ks;
+    return DecodeSplit{g_force_acc, ks, (N + dec::BW * g_force_acc - 1) / (dec::BW * g_force_acc)};
   }
-  return best;
+  const int nsms = dec_num_sms();
+  const int t1 = (N + dec::BW - 1) / dec::BW;
+  if (t1 <= max_active_clusters<1>(1)) {
+    int best = 1;
+    for (int ks = 2; ks <= dec::MAX_KS; ++ks) {
+      if (kblocks / ks < 4 || t1 * ks > nsms) break;
+      if (dec::split_fits(M, ks) && t1 <= max_active_clusters<1>(ks)) best = ks;
+    }
+    return DecodeSplit{1, best, t1};
+  }
+  const int t2 = (N + 2 * dec::BW - 1) / (2 * dec::BW);
+  if (two_ok && t2 <= max_active_clusters<2>(1)) return DecodeSplit{2, 1, t2};
+  return DecodeSplit{0, 0, 0};
 }
 
 bool decode_gemm_try(const DecodeGemmArgs& a, uint32_t* err, cudaStream_t stream) {
@@ -507,6 +600,7 @@ bool decode_gemm_try(const DecodeGemmArgs& a, uint32_t* err, cudaStream_t stream
   const bool lora = a.s != nullptr && a.lb != nullptr && a.num_adapters > 0 && epi != kEpiMaskAdapter;
   if (epi == kEpiSwiGLU && (lora || a.swiglu_tile % 128 != 0 || a.N % a.swiglu_tile != 0)) return false;
   if (epi == kEpiResAdd && a.residual == nullptr) return false;
+  if (epi == kEpiMaskAdapter && (a.mask_rank % 8 != 0 || a.mask_rank <= 0 || a.mask_num_adapters <= 0)) return false;
   if (lora) {
     if (a.rank % 32 != 0 || a.num_adapters > 64 || a.num_slices < 1 || a.num_slices > 4) return false;
     for (int i = 0; i < a.num_slices; ++i)
@@ -530,12 +624,15 @@ bool decode_gemm_try(const DecodeGemmArgs& a, uint32_t* err, cudaStream_t stream
   p.residual = reinterpret_cast<const __nv_bfloat16*>(a.residual);
   p.ldr = a.ldr;
   p.swiglu_half = a.swiglu_tile / 2;
+  p.trace = g_trace;
   // one or two 128-row accumulators per CTA (two need Mp_pad <= 256 columns each, and
   // for SwiGLU a whole number of 128-column output tiles)
   const bool two_ok = 2 * p.Mp_pad <= 512 && (epi != kEpiSwiGLU || (a.N / 2) % 128 == 0);
-  const DecodeSplit sp = choose_split(a.N, p.Mp, p.kblocks, two_ok);
+  const DecodeSplit sp = choose_split(a.N, a.M, p.kblocks, two_ok);
+  if (sp.acc == 0) return false;
   const int acc = sp.acc, n_tiles = sp.n_tiles;
   p.ks = sp.ks;
+  p.rows_per = dec::rows_per_part(p.M, p.ks);
   p.stage_bytes = acc * dec::BW * dec::BK * 2 + (p.Mp_pad * dec::BK * 2 + 1023) / 1024 * 1024;
   p.stages = std::min(dec::MAX_STAGES, dec::RING / p.stage_bytes);
   p.lora = lora ? 1 : 0;
@@ -573,6 +670,34 @@ bool decode_gemm_try(const DecodeGemmArgs& a, uint32_t* err, cudaStream_t stream
 }
 
 }  // namespace gsb
+
+// The split the decode kernel would use for an M x N x K call: {accumulators,
+// K parts, weight tiles, ring stages}, or {0, 0, 0, 0} when M is out of its range
+// (diagnostics and tests).
+std::vector<int64_t> gsb_gemm_decode_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t swiglu_tile) {
+  using namespace gsb;
+  if (M < 1 || M > std::min(g_decode_max_m, 256) || K % 64 != 0) return {0, 0, 0, 0};
+  const int Mp = (int)(M + 15) / 16 * 16, Mp_pad = (Mp + 31) / 32 * 32;
+  const bool two_ok = 2 * Mp_pad <= 512 && (epi != kEpiSwiGLU || (N / 2) % 128 == 0);
+  const DecodeSplit sp = choose_split((int)N, (int)M, (int)(K / 64), two_ok);
+  if (sp.acc == 0) return {0, 0, 0, 0};
+  const int stage_bytes = sp.acc * dec::BW * dec::BK * 2 + (Mp_pad * dec::BK * 2 + 1023) / 1024 * 1024;
+  (void)swiglu_tile;
+  return {sp.acc, sp.ks, sp.n_tiles, std::min(dec::MAX_STAGES, dec::RING / stage_bytes)};
+}
+
+// Forces the decode kernel's split (accumulators, K parts; 0, 0 restores the rule), for
+// A/B measurements.
+void gsb_gemm_decode_force_split(int64_t acc, int64_t ks) {
+  gsb::g_force_acc = (int)acc;
+  gsb::g_force_ks = (int)std::min<int64_t>(ks, gsb::dec::MAX_KS);
+}
+
+// Records per-CTA phase timestamps of the following decode-kernel launches into
+// `buf` (uint64, 16 per CTA, zeroed by the caller); an empty tensor stops.
+void gsb_gemm_decode_trace(const at::Tensor& buf) {
+  gsb::g_trace = buf.numel() ? reinterpret_cast<uint64_t*>(buf.data_ptr()) : nullptr;
+}
 
 // Sets the largest M served by the decode kernel (0: never); returns the previous value.
 int64_t gsb_gemm_decode_max_m(int64_t v) {

@@ -1,7 +1,7 @@
 """One launch of each native kernel on a representative shape, for profiler captures.
 
 ``python -m granite_switch_b200.utils.kernel_cases <case>`` with case in
-gemm, gemm_pair, gemm_single, cublas, swiglu, attn_prefill64, moe, probe, decode_gemm, attn_prefill, attn_decode, rmsnorm, rope, embed,
+gemm, gemm_pair, gemm_single, cublas, swiglu, attn_prefill64, moe, probe, decode_gemm, decode_shrink, attn_prefill, attn_decode, rmsnorm, rope, embed,
 routing, sample (or ``all``). Pair it with ``ncu --clock-control none -k regex:<kernel> -c 1`` (without
 ``--clock-control none`` ncu locks the GPU clocks).
 """
@@ -53,6 +53,12 @@ if want("decode_gemm"):  # down projection of the headline decode step (222 toke
     x2 = torch.randn(222, I, device=dev).bfloat16()
     h = torch.randn(222, H, device=dev).bfloat16()
     G.switched_gemm(x2, w, h, epi=G.EPI_RESADD, residual=h, scale=0.5)
+if want("decode_shrink"):  # LoRA shrink of o_proj in the headline decode step (222 tokens, 12 adapters r32)
+    xs = torch.randn(222, H, device=dev).bfloat16()
+    a_all = (torch.randn(12 * 32, H, device=dev) * 0.02).bfloat16()
+    ids = torch.randint(1, 13, (222,), device=dev, dtype=torch.int32)
+    s_out = torch.empty(222, 12 * 32, device=dev, dtype=torch.bfloat16)
+    G.lora_shrink(xs, a_all, ids, 32, 12, out=s_out)
 if want("attn_prefill") or want("attn_decode"):
     hq, hkv, d = 32, 8, 128
     def setup(q_lens, kv_lens):
