@@ -72,7 +72,8 @@ def _run(args, emit, metric, world, ref_path):
     llm = LLM(model=ckpt, skip_tokenizer_init=True, tensor_parallel_size=world, enable_prefix_caching=True,
               max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
               max_model_len=args.context_len + args.calls * 200 + 256, dtype="bfloat16",
-              gpu_memory_utilization=0.88, seed=args.seed)
+              gpu_memory_utilization=0.88, seed=args.seed,
+              kv_cache_dtype="auto" if getattr(args, "kv_cache_dtype", "bfloat16") == "bfloat16" else "fp8_e4m3")
     engine = llm.llm_engine
     wl = WorkloadConfig(num_conversations=args.conversations, rate=args.rate, context_len=args.context_len,
                         calls=args.calls, vocab=base["vocab_size"], num_adapters=12, seed=args.seed, mode=args.mode)
@@ -172,6 +173,7 @@ def _run(args, emit, metric, world, ref_path):
                      "parallelism": f"tp{world}", "adapters": "12 aLoRA r32 q/k/v/o",
                      "workload": f"poisson {args.rate}/s, {args.calls} chained calls, inv 16-64, gen 32-128",
                      "mode": args.mode, "scheduling_policy": "fcfs (vLLM default)", "ramp_steps": ramp,
+                     "kv_cache_dtype": getattr(args, "kv_cache_dtype", "bfloat16"),
                      "vllm": _vllm_version()}})
 
 

@@ -71,6 +71,8 @@ def parse_args():
                    help="engine admission order (the reference arm's vLLM engine is FCFS)")
     p.add_argument("--max-wait-steps", type=int, default=DEFAULT_MAX_WAIT_STEPS,
                    help="cache_affinity: engine steps after which a waiting cold request goes first (negative: none)")
+    p.add_argument("--kv-cache-dtype", choices=["bfloat16", "fp8_e4m3"], default="bfloat16",
+                   help="KV cache storage; the headline metric is defined on the bf16 cache")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-blocks", type=int, default=None)
     return p.parse_args()
@@ -133,7 +135,8 @@ def run_native(args):
                         max_model_len=args.context_len + args.calls * 200 + 256, tensor_parallel_size=world,
                         num_kv_blocks=args.kv_blocks, fused_tp_comm=args.fused_comm, seed=args.seed,
                         scheduling_policy=args.scheduling_policy,
-                        max_wait_steps=args.max_wait_steps if args.max_wait_steps >= 0 else None)
+                        max_wait_steps=args.max_wait_steps if args.max_wait_steps >= 0 else None,
+                        kv_cache_dtype=args.kv_cache_dtype)
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
               random_init=dict(lora_modules=("qkv", "o"), rank=32, seed=args.seed), tp_rank=rank, tp_group=group)
     eng = llm.engine
@@ -259,7 +262,7 @@ def run_native(args):
                        "workload": f"poisson {args.rate}/s, {args.calls} chained calls, inv 16-64, gen 32-128",
                        "mode": args.mode, "max_num_batched_tokens": args.max_num_batched_tokens,
                        "scheduling_policy": args.scheduling_policy, "max_wait_steps": ecfg.max_wait_steps,
-                       "ramp_steps": ramp, "l2": "inputs larger than L2 (each step streams all weights)",
+                       "kv_cache_dtype": args.kv_cache_dtype, "ramp_steps": ramp, "l2": "inputs larger than L2 (each step streams all weights)",
                        "fused_comm": bool(getattr(llm.model, "comm", None) is not None)},
             "e2e": {"value": round(e2e, 2), "unit": "output tok/s", "h2d_bytes_per_step": (ex.h2d_bytes - h2d0) // args.steps,
                     "d2h_bytes_per_step": (ex.d2h_bytes - d2h0) // args.steps},

@@ -24,6 +24,9 @@
 #include <cstdlib>
 #include "tma_util.h"
 
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
@@ -64,22 +67,54 @@ __device__ __forceinline__ uint32_t sw(int r, int ch) {
   return (uint32_t)((ch >> 3) * (ROWS * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
+// fp8 pages (kv_fp8.cu): byte offset of 16-byte chunk `ch` of key row `key` in a
+// K tile of D-byte rows with the TMA swizzle of that row width (128 B: chunk ^
+// row % 8; 64 B: chunk ^ (row / 2) % 4).
+template <int D>
+__device__ __forceinline__ uint32_t sw8(int key, int ch) {
+  if (D == 128) return (uint32_t)(key * 128 + ((ch ^ (key & 7)) << 4));
+  return (uint32_t)(key * 64 + ((ch ^ ((key >> 1) & 3)) << 4));
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+// Two e4m3 values -> bf16x2 (exact: every e4m3 value is a bf16 value).
+__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint32_t pair) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(pair & 0xffffu), __NV_E4M3);
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+  return pack_bf16x2(f.x, f.y);
+}
+
 }  // namespace attn
 
-template <int D, int WARPS_M, int KT, int STAGES>
+template <int D, int WARPS_M, int KT, int STAGES, bool F8 = false>
 struct AttnCfg {
   static constexpr int WARPS = (WARPS_M == 1) ? 4 : WARPS_M;
   static constexpr int THREADS = WARPS * 32;
   static constexpr int ROWS = 16 * WARPS_M;
   static constexpr int WARPS_N = (WARPS_M == 1) ? 4 : 1;
   static constexpr int KPW = KT / WARPS_N;        // keys per warp per tile
-  static constexpr int TILE_BYTES = KT * D * 2;   // one of K or V
+  static constexpr int TILE_BYTES = KT * D * (F8 ? 1 : 2);  // one of K or V
+  // fp8: the tile's K then V scales, one 128-byte slot per page (a TMA destination in
+  // shared memory must start on a 128-byte boundary; a page's 16 scales use 64 bytes)
+  static constexpr int SC_SLOT = 128;
+  static constexpr int SC_BYTES = F8 ? 2 * (KT / 16) * SC_SLOT : 0;
+  static constexpr int TX_BYTES = 2 * TILE_BYTES + (F8 ? 2 * KT * 4 : 0);  // bytes the TMA loads land per stage
+  // stages start on 1024-byte boundaries: the swizzled TMA destinations of the K tiles
+  // must be aligned to the swizzle pattern (the fp8 scale arrays would break that)
+  static constexpr int STAGE_BYTES = (2 * TILE_BYTES + SC_BYTES + 1023) / 1024 * 1024;
+  static_assert(STAGE_BYTES % 1024 == 0 && TILE_BYTES % 1024 == 0, "stage alignment");
   static constexpr int Q_BYTES = ROWS * D * 2;
   // page ids of the CTA's key range, staged in shared memory once (past this
   // many pages the loop falls back to reading the block table in global memory)
   // (the short decode layouts keep 1024 so that three CTAs fit on an SM)
   static constexpr int PT_CAP = (WARPS_M == 1 && STAGES * TILE_BYTES <= 32768) ? 1024 : 2048;
-  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * 2 * TILE_BYTES + 256 + PT_CAP * 4;
+  static constexpr int SMEM = 1024 + Q_BYTES + STAGES * STAGE_BYTES + 256 + PT_CAP * 4;
+  // the decode layout merges its key-split warps through the stage ring
+  static_assert(WARPS_M != 1 || STAGES * STAGE_BYTES >= (WARPS_N * 16 * (2 + D)) * 4, "merge scratch");
+  static_assert(Q_BYTES % 1024 == 0, "the stage ring starts 1024-byte aligned");
 };
 
 // Decode layout (16-row tiles): 2 = short rings (2 stages at head_dim 128, 4 at
@@ -90,9 +125,14 @@ struct AttnCfg {
 // in an 8B step. attn_decode_stages() switches it at run time for A/B tests.
 static int g_decode_stages = 2;
 
-template <int D, int WARPS_M, int KT, int STAGES>
-__global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
+// F8: the cache is the fp8 layout of kv_fp8.cu (K [blocks, Hkv, 16, D] bytes, V
+// [blocks, Hkv, D, 16] bytes, fp32 scales [blocks, Hkv, 16] for each); fragments are
+// read as 32-bit words and converted to bf16 in registers, the K scales multiply the
+// scores and the V scales the probabilities.
+template <int D, int WARPS_M, int KT, int STAGES, bool F8 = false>
+__global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
     paged_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                      const __grid_constant__ CUtensorMap tm_ks, const __grid_constant__ CUtensorMap tm_vs,
                       const __nv_bfloat16* __restrict__ q, int64_t q_stride,
                       const int32_t* __restrict__ block_table, int bt_stride, int num_blocks,
                       const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
@@ -101,14 +141,14 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
                       int64_t out_stride, float* __restrict__ ws_o, float* __restrict__ ws_lse,
                       int nsplit, int T, uint32_t* err) {
   using namespace attn;
-  using C = AttnCfg<D, WARPS_M, KT, STAGES>;
+  using C = AttnCfg<D, WARPS_M, KT, STAGES, F8>;
   constexpr int ROWS = C::ROWS, WARPS_N = C::WARPS_N, KPW = C::KPW, NB = KPW / 8;
   constexpr int DC = D / 8, OB = D / 8, PAGES = KT / PAGE;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
-  uint8_t* sKV = smem + C::Q_BYTES;  // [STAGES][K tile | V tile]
-  uint64_t* full = reinterpret_cast<uint64_t*>(sKV + STAGES * 2 * C::TILE_BYTES);
+  uint8_t* sKV = smem + C::Q_BYTES;  // [STAGES][K tile | V tile (| K, V scales)]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sKV + STAGES * C::STAGE_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wm = (WARPS_M == 1) ? 0 : warp;
@@ -137,6 +177,10 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
     fence_barrier_init();
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
+    if (F8) {
+      tma_prefetch_desc(&tm_ks);
+      tma_prefetch_desc(&tm_vs);
+    }
   }
   // ---- page ids of [k_begin, k_end) into shared memory: the producer thread
   // then issues each tile's page loads without a dependent global read
@@ -161,10 +205,10 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
   const int first_page = checked_index(bt[0], num_blocks, err, kSitePage);
   auto issue = [&](int it) {
     const int s = it % STAGES;
-    uint8_t* dK = sKV + s * 2 * C::TILE_BYTES;
+    uint8_t* dK = sKV + s * C::STAGE_BYTES;
     uint8_t* dV = dK + C::TILE_BYTES;
     const int tile_start = k_begin + it * KT;
-    mbar_arrive_expect_tx(&full[s], 2 * C::TILE_BYTES);
+    mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
 #pragma unroll
     for (int p = 0; p < PAGES; ++p) {
       const int j = tile_start + p * PAGE;
@@ -175,10 +219,18 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
                                                                                   kSitePage))
                                    : first_page;
       const int row = (page * Hkv + kvh) * PAGE;
+      if (F8) {
+        uint8_t* dS = dV + C::TILE_BYTES;
+        tma_load_2d(dK + p * PAGE * D, &tm_k, &full[s], 0, row);
+        tma_load_2d(dV + p * PAGE * D, &tm_v, &full[s], 0, (page * Hkv + kvh) * D);
+        tma_load_2d(dS + p * C::SC_SLOT, &tm_ks, &full[s], 0, page * Hkv + kvh);
+        tma_load_2d(dS + (PAGES + p) * C::SC_SLOT, &tm_vs, &full[s], 0, page * Hkv + kvh);
+      } else {
 #pragma unroll
-      for (int h = 0; h < D / 64; ++h) {
-        tma_load_2d(dK + h * (KT * 128) + p * PAGE * 128, &tm_k, &full[s], h * 64, row);
-        tma_load_2d(dV + h * (KT * 128) + p * PAGE * 128, &tm_v, &full[s], h * 64, row);
+        for (int h = 0; h < D / 64; ++h) {
+          tma_load_2d(dK + h * (KT * 128) + p * PAGE * 128, &tm_k, &full[s], h * 64, row);
+          tma_load_2d(dV + h * (KT * 128) + p * PAGE * 128, &tm_v, &full[s], h * 64, row);
+        }
       }
     }
   };
@@ -219,8 +271,11 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
     }
     const bool landed = mbar_wait(&full[s], (it / STAGES) & 1, err, kErrAttnWait);
     const int tile_start = k_begin + it * KT;
-    const uint32_t kbase = smem_u32(sKV + s * 2 * C::TILE_BYTES);
+    const uint32_t kbase = smem_u32(sKV + s * C::STAGE_BYTES);
     const uint32_t vbase = kbase + C::TILE_BYTES;
+    // scale of tile key kt: slot kt / 16, entry kt % 16 (slots of C::SC_SLOT bytes)
+    const float* kss = reinterpret_cast<const float*>(sKV + s * C::STAGE_BYTES + 2 * C::TILE_BYTES);
+    const float* vss = kss + PAGES * (C::SC_SLOT / 4);
 
     float sacc[NB][4];
 #pragma unroll
@@ -229,12 +284,21 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
     for (int kk = 0; kk < D / 16; ++kk) {
 #pragma unroll
       for (int nb2 = 0; nb2 < NB / 2; ++nb2) {
-        const int key = wn * KPW + nb2 * 16 + (lane & 7) + ((lane >> 4) << 3);
-        const int ch = kk * 2 + ((lane >> 3) & 1);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kbase + sw<KT>(key, ch), b0, b1, b2, b3);
-        mma16816(sacc[2 * nb2], qf[kk], b0, b1);
-        mma16816(sacc[2 * nb2 + 1], qf[kk], b2, b3);
+        if (F8) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int key = wn * KPW + (2 * nb2 + h) * 8 + g;
+            const uint32_t wd = lds32(kbase + sw8<D>(key, kk) + 4 * t4);
+            mma16816(sacc[2 * nb2 + h], qf[kk], e4m3x2_to_bf16x2(wd), e4m3x2_to_bf16x2(wd >> 16));
+          }
+        } else {
+          const int key = wn * KPW + nb2 * 16 + (lane & 7) + ((lane >> 4) << 3);
+          const int ch = kk * 2 + ((lane >> 3) & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kbase + sw<KT>(key, ch), b0, b1, b2, b3);
+          mma16816(sacc[2 * nb2], qf[kk], b0, b1);
+          mma16816(sacc[2 * nb2 + 1], qf[kk], b2, b3);
+        }
       }
     }
     float mx[2] = {-INFINITY, -INFINITY};
@@ -242,9 +306,10 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
     for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int j = tile_start + wn * KPW + nb * 8 + 2 * t4 + (e & 1);
+        const int kt = wn * KPW + nb * 8 + 2 * t4 + (e & 1);
+        const int j = tile_start + kt;
         const int pos = (e < 2) ? posA : posB;
-        float v = sacc[nb][e] * scale_log2;
+        float v = sacc[nb][e] * (F8 ? kss[(kt >> 4) * (C::SC_SLOT / 4) + (kt & 15)] * scale_log2 : scale_log2);
         if (j >= k_end || j > pos) v = -INFINITY;
         sacc[nb][e] = v;
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
@@ -276,6 +341,15 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
       rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
       l_r[h] = l_r[h] * corr[h] + rs[h];
     }
+    if (F8) {  // the V scales fold into the probabilities (the row sums stay unscaled)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int kt = wn * KPW + nb * 8 + 2 * t4 + (e & 1);
+          sacc[nb][e] *= vss[(kt >> 4) * (C::SC_SLOT / 4) + (kt & 15)];
+        }
+    }
 #pragma unroll
     for (int i = 0; i < OB; ++i) {
       o[i][0] *= corr[0];
@@ -292,12 +366,22 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES>::THREADS)
       pa[3] = pack_bf16x2(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
 #pragma unroll
       for (int db = 0; db < D / 16; ++db) {
-        const int key = wn * KPW + kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
-        const int ch = db * 2 + (lane >> 4);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vbase + sw<KT>(key, ch), b0, b1, b2, b3);
-        mma16816(o[2 * db], pa, b0, b1);
-        mma16816(o[2 * db + 1], pa, b2, b3);
+        if (F8) {
+          // V^T page of the 16 keys: [D][16 bytes]; one word = keys 2t, 2t+1, 2t+8, 2t+9
+          const uint32_t pg = vbase + ((wn * KPW + kk * 16) / PAGE) * (PAGE * D);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t wd = lds32(pg + (db * 16 + h * 8 + g) * 16 + 4 * t4);
+            mma16816(o[2 * db + h], pa, e4m3x2_to_bf16x2(wd), e4m3x2_to_bf16x2(wd >> 16));
+          }
+        } else {
+          const int key = wn * KPW + kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+          const int ch = db * 2 + (lane >> 4);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vbase + sw<KT>(key, ch), b0, b1, b2, b3);
+          mma16816(o[2 * db], pa, b0, b1);
+          mma16816(o[2 * db + 1], pa, b2, b3);
+        }
       }
     }
     // every warp is done with stage s before it is refilled; a lost TMA
@@ -464,21 +548,22 @@ void launch_attn_merge(int D, int n_work, int Hkv, cudaStream_t st, const float*
 
 using namespace gsb;
 
-template <int D, int WM, int KT, int ST>
+template <int D, int WM, int KT, int ST, bool F8 = false>
 static void launch_attn(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const CUtensorMap& tv,
+                        const CUtensorMap& tks, const CUtensorMap& tvs,
                         const at::Tensor& q, const at::Tensor& bt, int num_blocks, const at::Tensor& q_start,
                         const at::Tensor& kv_len,
                         const at::Tensor& work_seq, const at::Tensor& work_row0, int Hq, int Hkv, float scale_log2,
                         const at::Tensor& out, float* wso, float* wsl, int nsplit, int T, uint32_t* err) {
-  using C = AttnCfg<D, WM, KT, ST>;
-  auto kfn = paged_attn_kernel<D, WM, KT, ST>;
+  using C = AttnCfg<D, WM, KT, ST, F8>;
+  auto kfn = paged_attn_kernel<D, WM, KT, ST, F8>;
   static bool configured = false;
   if (!configured) {
     GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured = true;
   }
   kfn<<<(::gsb::count_launch(), grid), C::THREADS, C::SMEM, st>>>(
-      tk, tv, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), bt.data_ptr<int32_t>(),
+      tk, tv, tks, tvs, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), bt.data_ptr<int32_t>(),
       (int)bt.stride(0), num_blocks, q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
       work_seq.data_ptr<int32_t>(),
       work_row0.data_ptr<int32_t>(), Hq, Hkv, scale_log2, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
@@ -503,13 +588,28 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
                          const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t rows_per_tile,
                          int64_t num_q_heads, double scale, const at::Tensor& out, int64_t nsplit,
                          const c10::optional<at::Tensor>& ws_o, const c10::optional<at::Tensor>& ws_lse,
-                         const at::Tensor& err) {
-  GSB_CHECK(q.scalar_type() == at::kBFloat16 && k_cache.scalar_type() == at::kBFloat16 &&
-                out.scalar_type() == at::kBFloat16,
-            "attention: bf16 tensors required");
-  GSB_CHECK(k_cache.dim() == 4 && k_cache.size(2) == attn::PAGE && k_cache.is_contiguous() &&
-                v_cache.is_contiguous() && v_cache.sizes() == k_cache.sizes(),
-            "attention: caches must be contiguous [num_blocks, Hkv, 16, D]");
+                         const at::Tensor& err, const c10::optional<at::Tensor>& k_scale,
+                         const c10::optional<at::Tensor>& v_scale) {
+  const bool f8 = k_cache.scalar_type() == at::kByte;
+  GSB_CHECK(q.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16 &&
+                (k_cache.scalar_type() == at::kBFloat16 || f8) && v_cache.scalar_type() == k_cache.scalar_type(),
+            "attention: bf16 q/out and a bf16 or fp8 (uint8) cache required");
+  if (f8) {
+    GSB_CHECK(k_cache.dim() == 4 && k_cache.size(2) == attn::PAGE && k_cache.is_contiguous() &&
+                  v_cache.is_contiguous() && v_cache.dim() == 4 && v_cache.size(0) == k_cache.size(0) &&
+                  v_cache.size(1) == k_cache.size(1) && v_cache.size(2) == k_cache.size(3) &&
+                  v_cache.size(3) == attn::PAGE,
+              "attention: fp8 caches must be K [num_blocks, Hkv, 16, D] and V [num_blocks, Hkv, D, 16]");
+    GSB_CHECK(k_scale.has_value() && v_scale.has_value() && k_scale->scalar_type() == at::kFloat &&
+                  v_scale->scalar_type() == at::kFloat && k_scale->is_contiguous() && v_scale->is_contiguous() &&
+                  k_scale->numel() == k_cache.size(0) * k_cache.size(1) * attn::PAGE &&
+                  v_scale->numel() == k_scale->numel(),
+              "attention: fp8 caches need fp32 scales [num_blocks, Hkv, 16]");
+  } else {
+    GSB_CHECK(k_cache.dim() == 4 && k_cache.size(2) == attn::PAGE && k_cache.is_contiguous() &&
+                  v_cache.is_contiguous() && v_cache.sizes() == k_cache.sizes(),
+              "attention: caches must be contiguous [num_blocks, Hkv, 16, D]");
+  }
   GSB_CHECK(block_table.scalar_type() == at::kInt && q_start.scalar_type() == at::kInt &&
                 kv_len.scalar_type() == at::kInt && work_seq.scalar_type() == at::kInt &&
                 work_row0.scalar_type() == at::kInt,
@@ -537,16 +637,44 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
   GSB_CHECK(page_rows < (int64_t(1) << 31), "attention: cache too large for 32-bit TMA coordinates");
   c10::cuda::CUDAGuard guard(q.device());
   auto st = c10::cuda::getCurrentCUDAStream(q.device().index()).stream();
-  CUtensorMap tk = make_tmap_bf16_2d(k_cache.data_ptr(), page_rows, D, D, 64, attn::PAGE, CU_TENSOR_MAP_SWIZZLE_128B);
-  CUtensorMap tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, attn::PAGE, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tk, tv, tks, tvs;
+  if (f8) {
+    const CUtensorMapSwizzle swz = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    tk = make_tmap_2d(k_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, page_rows, D, D, D, attn::PAGE, swz);
+    tv = make_tmap_2d(v_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k_cache.size(0) * Hkv * D,
+                      attn::PAGE, attn::PAGE, attn::PAGE, D, CU_TENSOR_MAP_SWIZZLE_NONE);
+    tks = make_tmap_2d(k_scale->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)k_cache.size(0) * Hkv,
+                       attn::PAGE, attn::PAGE, attn::PAGE, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+    tvs = make_tmap_2d(v_scale->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)k_cache.size(0) * Hkv,
+                       attn::PAGE, attn::PAGE, attn::PAGE, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  } else {
+    tk = make_tmap_bf16_2d(k_cache.data_ptr(), page_rows, D, D, 64, attn::PAGE, CU_TENSOR_MAP_SWIZZLE_128B);
+    tv = make_tmap_bf16_2d(v_cache.data_ptr(), page_rows, D, D, 64, attn::PAGE, CU_TENSOR_MAP_SWIZZLE_128B);
+    tks = tk;
+    tvs = tv;
+  }
   uint32_t* ep = reinterpret_cast<uint32_t*>(err.data_ptr());
   const float scale_log2 = (float)(scale * 1.4426950408889634);
   dim3 grid(n_work, Hkv, (unsigned)nsplit);
 #define GSB_ATTN(DD, WM, KT, ST)                                                                              \
-  launch_attn<DD, WM, KT, ST>(grid, st, tk, tv, q, block_table, (int)k_cache.size(0), q_start, kv_len, work_seq, \
-                              work_row0, Hq, Hkv, \
+  launch_attn<DD, WM, KT, ST>(grid, st, tk, tv, tks, tvs, q, block_table, (int)k_cache.size(0), q_start, kv_len, \
+                              work_seq, work_row0, Hq, Hkv, \
                               scale_log2, out, wso, wsl, (int)nsplit, T, ep)
-  if (D == 128) {
+#define GSB_ATTN8(DD, WM, KT, ST)                                                                             \
+  launch_attn<DD, WM, KT, ST, true>(grid, st, tk, tv, tks, tvs, q, block_table, (int)k_cache.size(0), q_start,  \
+                                    kv_len, work_seq, work_row0, Hq, Hkv, scale_log2, out, wso, wsl, (int)nsplit, \
+                                    T, ep)
+  // fp8 pages are half the bytes, so the rings hold twice as many tiles for the same bytes in flight
+  // (decode: three CTAs per SM, as the bf16 short-ring layout)
+  if (f8 && D == 128) {
+    if (rows_per_tile == 128) GSB_ATTN8(128, 8, 64, 4);
+    else if (rows_per_tile == 64) GSB_ATTN8(128, 4, 64, 4);
+    else GSB_ATTN8(128, 1, 64, 3);
+  } else if (f8 && D == 64) {
+    if (rows_per_tile == 128) GSB_ATTN8(64, 8, 64, 6);
+    else if (rows_per_tile == 64) GSB_ATTN8(64, 4, 64, 6);
+    else GSB_ATTN8(64, 1, 64, 6);
+  } else if (D == 128) {
     if (rows_per_tile == 128) GSB_ATTN(128, 8, 64, 2);
     else if (rows_per_tile == 64) GSB_ATTN(128, 4, 64, 2);
     else if (g_decode_stages == 2) GSB_ATTN(128, 1, 64, 2);
@@ -560,6 +688,7 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
     GSB_CHECK(false, "attention: head_dim must be 64 or 128, got ", D);
   }
 #undef GSB_ATTN
+#undef GSB_ATTN8
   if (nsplit > 1) {
     auto merge = (D == 128) ? launch_merge<128> : launch_merge<64>;
     merge(n_work, Hkv, st, wso, wsl, (int)nsplit, T, Hq, q_start.data_ptr<int32_t>(), work_seq.data_ptr<int32_t>(),
@@ -654,7 +783,7 @@ static void launch_decode(dim3 grid, cudaStream_t st, const CUtensorMap& tk, con
                           uint32_t* err) {
   using C = AttnCfg<D, 1, 64, ST>;
   paged_attn_kernel<D, 1, 64, ST><<<(::gsb::count_launch(), grid), C::THREADS, C::SMEM, st>>>(
-      tk, tv, reinterpret_cast<const __nv_bfloat16*>(q), q_stride, bt, (int)bt_stride, num_blocks, q_start, kv_len,
+      tk, tv, tk, tv, reinterpret_cast<const __nv_bfloat16*>(q), q_stride, bt, (int)bt_stride, num_blocks, q_start, kv_len,
       work_seq, work_row0, Hq, Hkv, scale_log2, reinterpret_cast<__nv_bfloat16*>(out), out_stride, wso, wsl, nsplit,
       T, err);
   if (nsplit > 1)

@@ -20,6 +20,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "granite_switch_b200 sm_100a kernels";
   m.def("switched_gemm", &gsb_switched_gemm, "tcgen05 GEMM with fused switched-LoRA expand");
   m.def("gemm_pair_min_m", &gsb_gemm_pair_min_m, "set the smallest M of the CTA-pair GEMM (returns the old value)");
+  m.def("gemm_decode_plan", &gsb_gemm_decode_plan,
+        "decode-kernel split for (M, N, K, epilogue, swiglu tile): [accumulators, K parts, tiles, stages]");
+  m.def("gemm_decode_force_split", &gsb_gemm_decode_force_split,
+        "force the decode kernel's (accumulators, K parts) for A/B tests; (0, 0) restores the rule");
+  m.def("gemm_decode_trace", &gsb_gemm_decode_trace,
+        "record per-CTA phase timestamps of later decode-GEMM launches into a uint64 [CTAs, 8] tensor");
   m.def("gemm_decode_max_m", &gsb_gemm_decode_max_m,
         "set the largest M of the operand-swapped decode GEMM (0: off; -1 reads; returns the old value)");
   m.def("rmsnorm", &gsb_rmsnorm, "RMSNorm (optionally gathering rows)");
@@ -42,5 +48,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_scatter_slots", &gsb_moe_scatter_slots, "MoE rows into the slots of an earlier scatter");
   m.def("moe_combine", &gsb_moe_combine, "MoE weighted sum of expert outputs (+ shared MLP, residual)");
   m.def("residual_axpy", &gsb_residual_axpy, "h <- h + y * scale");
-  m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode)");
+  m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode; bf16 or fp8 cache)");
+  m.def("kv_write_fp8", &gsb_kv_write_fp8, "quantised (e4m3, per-row scale) write of a step's K/V into the fp8 cache");
 }

@@ -18,6 +18,12 @@ void gsb_switched_gemm(const at::Tensor& x, const at::Tensor& w, const at::Tenso
 
 int64_t gsb_gemm_pair_min_m(int64_t m);
 int64_t gsb_gemm_decode_max_m(int64_t v);
+void gsb_gemm_decode_force_split(int64_t acc, int64_t ks);
+void gsb_gemm_decode_trace(const at::Tensor& buf);
+void gsb_kv_write_fp8(const at::Tensor& qkv, const at::Tensor& slots, const at::Tensor& k8, const at::Tensor& v8,
+                      const at::Tensor& k_scale, const at::Tensor& v_scale, int64_t num_q_heads,
+                      int64_t num_kv_heads, int64_t head_dim, const at::Tensor& err);
+std::vector<int64_t> gsb_gemm_decode_plan(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t swiglu_tile);
 
 void gsb_rmsnorm(const at::Tensor& x, const at::Tensor& w, const at::Tensor& out,
                  const c10::optional<at::Tensor>& rows, double eps);
@@ -40,7 +46,8 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
                          const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t rows_per_tile,
                          int64_t num_q_heads, double scale, const at::Tensor& out, int64_t nsplit,
                          const c10::optional<at::Tensor>& ws_o, const c10::optional<at::Tensor>& ws_lse,
-                         const at::Tensor& err);
+                         const at::Tensor& err, const c10::optional<at::Tensor>& k_scale,
+                         const c10::optional<at::Tensor>& v_scale);
 void gsb_sample(const at::Tensor& logits, const at::Tensor& temperature, const at::Tensor& top_k,
                 const at::Tensor& top_p, const at::Tensor& seeds, const at::Tensor& offsets, const at::Tensor& out);
 void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,

@@ -73,6 +73,25 @@ inline CUtensorMap make_tmap_bf16_2d(const void* ptr, uint64_t rows, uint64_t co
   return m;
 }
 
+// 2-D tensor map of any element type (uint8 fp8 bytes, fp32 scales): [rows, cols]
+// with the given row stride in elements; box [box_rows, box_cols].
+inline CUtensorMap make_tmap_2d(const void* ptr, CUtensorMapDataType dtype, uint32_t elem_bytes, uint64_t rows,
+                                uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows,
+                                CUtensorMapSwizzle swizzle) {
+  GSB_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
+  GSB_CHECK((row_stride_elems * elem_bytes) % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride_elems * elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = tma_encode_fn()(&m, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  GSB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r, " rows=", rows, " cols=", cols);
+  return m;
+}
+
 // 3-D bf16 tensor map over a stack of row-major matrices [planes, rows, cols]
 // (contiguous); box [1, box_rows, box_cols].
 inline CUtensorMap make_tmap_bf16_3d(const void* ptr, uint64_t planes, uint64_t rows, uint64_t cols,

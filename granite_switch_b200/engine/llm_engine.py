@@ -49,6 +49,7 @@ class EngineConfig:
     scheduling_policy: str = "cache_affinity"  # or "fcfs" (admission order, see engine.scheduler)
     max_wait_steps: int | None = DEFAULT_MAX_WAIT_STEPS  # cache_affinity: steps before a cold request
     #                                                    goes first; None = unbounded
+    kv_cache_dtype: str = "bfloat16"       # or "fp8_e4m3": e4m3 K/V with a per-(token, KV head) scale
 
 
 @dataclass
@@ -288,10 +289,13 @@ class LLM:
                 nm = NativeGraniteSwitch.from_random(config, self.device, max_tokens, 1, tp_rank=tp_rank,
                                                      tp_size=tp, tp_group=tp_group, max_seqs=ecfg.max_num_seqs,
                                                      pipeline=pipeline, **ri)
+            if ecfg.kv_cache_dtype not in ("bfloat16", "fp8_e4m3"):
+                raise ValueError(f"kv_cache_dtype must be 'bfloat16' or 'fp8_e4m3', got {ecfg.kv_cache_dtype!r}")
+            nm.kv_fp8 = ecfg.kv_cache_dtype == "fp8_e4m3"
             if ecfg.num_kv_blocks is None:
                 torch.cuda.synchronize()
                 nb = default_num_kv_blocks(0, config, tp, ecfg.gpu_memory_utilization, self.device,
-                                           num_layers=nm.num_layers)
+                                           num_layers=nm.num_layers, kv_fp8=nm.kv_fp8)
             nm.num_kv_blocks = nb
             nm._alloc_buffers()
             self.model = nm

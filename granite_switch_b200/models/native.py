@@ -107,6 +107,8 @@ class NativeGraniteSwitch:
         self.layers: list[LayerWeights] = []
         self.remaps: torch.Tensor | None = None
         self.comm = None  # optional fused-collective communicator
+        # KV cache storage: bf16, or e4m3 with a per-(token, KV head) scale (kv_fp8.cu)
+        self.kv_fp8 = False
         self.prof = None  # optional per-op CUDA-event profiler (utils.step_profile.StepProfiler)
         # prefill attention on tcgen05 (head_dim 64 / 128); False selects the mma.sync kernel (A/B tests)
         self.use_tc_attention = True
@@ -333,8 +335,16 @@ class NativeGraniteSwitch:
         # one extra block past the managed ones: a scratch page for padding rows of
         # CUDA-graph decode steps (the block manager never hands it out)
         self.scratch_block = self.num_kv_blocks
-        self.kv_cache = torch.zeros(self.num_layers, 2, self.num_kv_blocks + 1, self.num_kv, 16, self.head_dim,
-                                    dtype=bf, device=dev)
+        if self.kv_fp8:
+            # [layer, K | V, block, head, ...]: K pages [16, D] bytes, V pages transposed [D, 16]
+            self.kv_cache = torch.zeros(self.num_layers, 2, self.num_kv_blocks + 1, self.num_kv, 16, self.head_dim,
+                                        dtype=torch.uint8, device=dev)
+            self.kv_scale = torch.ones(self.num_layers, 2, self.num_kv_blocks + 1, self.num_kv, 16,
+                                       dtype=torch.float32, device=dev)
+        else:
+            self.kv_cache = torch.zeros(self.num_layers, 2, self.num_kv_blocks + 1, self.num_kv, 16, self.head_dim,
+                                        dtype=bf, device=dev)
+            self.kv_scale = None
         self.h = torch.empty(t, self.hidden, dtype=bf, device=dev)
         self.h2 = torch.empty(t, self.hidden, dtype=bf, device=dev) if self.tp_size > 1 else None
         self.x = torch.empty(t, self.hidden, dtype=bf, device=dev)
@@ -388,7 +398,27 @@ class NativeGraniteSwitch:
         self.ws_tokens = min(t, 4 * self.max_seqs)
 
     def kv_cache_bytes(self) -> int:
-        return self.kv_cache.numel() * self.kv_cache.element_size()
+        n = self.kv_cache.numel() * self.kv_cache.element_size()
+        if self.kv_scale is not None:
+            n += self.kv_scale.numel() * 4
+        return n
+
+    def _layer_cache(self, li: int):
+        """``(k_cache, v_cache, k_scale, v_scale)`` views of layer ``li`` (scales None for bf16)."""
+        kc, vc = self.kv_cache[li, 0], self.kv_cache[li, 1]
+        if not self.kv_fp8:
+            return kc, vc, None, None
+        nb = kc.shape[0]
+        return kc, vc.view(nb, self.num_kv, self.head_dim, 16), self.kv_scale[li, 0], self.kv_scale[li, 1]
+
+    def _rope_and_cache(self, b, qkv, li: int) -> None:
+        """RoPE on q / k and the write of the step's K / V into layer ``li``'s cache."""
+        kc, vc, ks, vs = self._layer_cache(li)
+        if self.kv_fp8:
+            E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim)
+            A.kv_write_fp8(qkv, b.slots, kc, vc, ks, vs, self.num_q, self.num_kv, self.head_dim)
+        else:
+            E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
 
     def _region(self, name: str):
         return self.prof.region(name) if self.prof is not None else contextlib.nullcontext()
@@ -551,10 +581,9 @@ class NativeGraniteSwitch:
                         E.rmsnorm(h, lw.in_norm, cfg.rms_norm_eps, out=x)
                 with R("qkv"):
                     self._proj(lw.qkv, x, qkv)
-                kc, vc = self.kv_cache[li, 0], self.kv_cache[li, 1]
                 with R("rope+kv"):
-                    E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
-                self._attention(b, qkv, kc, vc, attn, scale)
+                    self._rope_and_cache(b, qkv, li)
+                self._attention(b, qkv, li, attn, scale)
                 if comm is not None:
                     with R("o+reduce"):
                         y = comm.row_parallel(self, lw.o, attn, h, mult)
@@ -596,8 +625,9 @@ class NativeGraniteSwitch:
             native().probe_rewrite(logits, self.lm_vocab_lo, outj, slots, self.probe_labels, self.verdict)
         return logits
 
-    def _attention(self, b: StepBatch, q: torch.Tensor, kc, vc, attn: torch.Tensor, scale: float) -> None:
+    def _attention(self, b: StepBatch, q: torch.Tensor, li: int, attn: torch.Tensor, scale: float) -> None:
         R = self._region
+        kc, vc, ks, vs = self._layer_cache(li)
         for plan in b.plans:
             if plan.rows in (128, 256):
                 with R("attn_prefill"):
@@ -608,7 +638,7 @@ class NativeGraniteSwitch:
                 with R("attn_decode" if plan.rows == 16 else "attn_prefill"):
                     A.paged_attention(q, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
                                       plan.work_row0, plan.rows, self.num_q, scale, attn, plan.nsplit,
-                                      self.ws_o, self.ws_lse)
+                                      self.ws_o, self.ws_lse, ks, vs)
 
     def _forward_dual(self, b: StepBatch, h, x, qkv, attn, act, mult: float, scale: float) -> None:
         """Shadow Residual layers (reference: src/granite_switch/vllm/decoder/shadow_residual/decoder.py:88-364).
@@ -631,15 +661,14 @@ class NativeGraniteSwitch:
         eps = cfg.rms_norm_eps
         hb2 = self.hbase2[:t] if self.hbase2 is not None else None
         for li, lw in enumerate(self.layers):
-            kc, vc = self.kv_cache[li, 0], self.kv_cache[li, 1]
             # base stream: q, k, v without LoRA; k/v go to the cache
             with R("rmsnorm"):
                 E.rmsnorm(hb, lw.in_norm, eps, out=x)
             with R("qkv"):
                 self._proj(lw.qkv, x, qkv, lora=False)
             with R("rope+kv"):
-                E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
-            self._attention(b, qkv, kc, vc, attn, scale)
+                self._rope_and_cache(b, qkv, li)
+            self._attention(b, qkv, li, attn, scale)
             with R("o"):
                 self._row_parallel(lw.o, attn, hb, mult, lora=False, partial=hb2)
             # adapter stream: switched Q only, same base K/V
@@ -649,7 +678,7 @@ class NativeGraniteSwitch:
                 self._proj(lw.qkv, x, qa, n_rows=q_n)
             with R("rope+kv"):
                 E.rope_kv(qa, b.positions, self.cos_sin, self.num_q, 0, self.head_dim)
-            self._attention(b, qa, kc, vc, attn, scale)
+            self._attention(b, qa, li, attn, scale)
             with R("o"):
                 self._row_parallel(lw.o, attn, h, mult)
             # MLPs: base stream first (its output feeds the cross stream; with
@@ -671,7 +700,8 @@ class NativeGraniteSwitch:
         dec = [i for i, ql in enumerate(q_lens) if ql * g <= 16]
         pre = [i for i, ql in enumerate(q_lens) if ql * g > 16]
         plans = []
-        tc = self.head_dim in (64, 128) and self.use_tc_attention
+        # the tcgen05 prefill kernel reads bf16 pages; an fp8 cache takes the mma.sync layouts
+        tc = self.head_dim in (64, 128) and self.use_tc_attention and not self.kv_fp8
         pre_q, pre_kv = [q_lens[i] for i in pre], [kv_lens[i] for i in pre]
         # short chunks over long cached prefixes: split-KV layout (needs the split workspace)
         pre_split = (A.split_prefill(pre_q, pre_kv, g, self.num_kv)
@@ -730,11 +760,13 @@ def split_layers(num_layers: int, stage: int, stages: int) -> tuple[int, int]:
 
 def default_num_kv_blocks(model_bytes: int, cfg: GraniteSwitchConfig, tp_size: int, mem_fraction: float = 0.85,
                           device=None, reserve_bytes: int = 6 << 30, cap_blocks: int | None = None,
-                          num_layers: int | None = None) -> int:
+                          num_layers: int | None = None, kv_fp8: bool = False) -> int:
     free, total = torch.cuda.mem_get_info(device)
     d = cfg.head_dim_eff
     kv_heads = max(1, cfg.num_key_value_heads // tp_size)
-    per_block = (num_layers or cfg.num_decoder_layers) * 2 * kv_heads * 16 * d * 2
+    # bytes per 16-token block over all layers: bf16 K and V, or e4m3 K and V plus fp32 row scales
+    per_row = d + 4 if kv_fp8 else 2 * d
+    per_block = (num_layers or cfg.num_decoder_layers) * 2 * kv_heads * 16 * per_row
     budget = int(total * mem_fraction) - (total - free) - reserve_bytes
     n = max(64, budget // per_block)
     if cap_blocks is not None:

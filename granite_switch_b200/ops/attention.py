@@ -93,11 +93,37 @@ def choose_splits(n_ctas: int, max_kv: int, min_keys_per_split: int = 512) -> in
 
 def paged_attention(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
                     rows_per_tile: int, num_q_heads: int, scale: float, out, nsplit: int = 1,
-                    ws_o=None, ws_lse=None):
+                    ws_o=None, ws_lse=None, k_scale=None, v_scale=None):
+    """bf16 cache: ``k_cache``/``v_cache`` ``[blocks, Hkv, 16, D]``. fp8 cache (uint8, the
+    layout of :func:`kv_write_fp8`): K ``[blocks, Hkv, 16, D]``, V ``[blocks, Hkv, D, 16]``,
+    with fp32 ``k_scale``/``v_scale`` ``[blocks, Hkv, 16]``."""
     native().paged_attention(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,
                              rows_per_tile, num_q_heads, float(scale), out, nsplit, ws_o, ws_lse,
-                             err_buffer(q.device))
+                             err_buffer(q.device), k_scale, v_scale)
     return out
+
+
+def _perm16():
+    """Stored position of each element of a 16-element group in the fp8 cache."""
+    return [((i >> 1) << 2) + (i & 1) if i < 8 else (((i - 8) >> 1) << 2) + 2 + (i & 1) for i in range(16)]
+
+
+def kv_write_fp8(qkv, slots, k8, v8, k_scale, v_scale, num_q_heads: int, num_kv_heads: int, head_dim: int):
+    """Quantise a step's (already rotated) K and V rows of ``qkv`` into the fp8 cache: one fp32
+    scale per (token, KV head) row, ``max|x| / 448``, and e4m3 values. K is stored
+    ``[blocks, Hkv, 16, D]`` and V transposed ``[blocks, Hkv, D, 16]``, both with each
+    16-element group in the order 0 1 8 9 2 3 10 11 4 5 12 13 6 7 14 15."""
+    native().kv_write_fp8(qkv, slots, k8, v8, k_scale, v_scale, num_q_heads, num_kv_heads, head_dim,
+                          err_buffer(qkv.device))
+
+
+def dequantize_fp8_cache(k8, v8, k_scale, v_scale):
+    """fp32 ``[blocks, Hkv, 16, D]`` K and V from the fp8 cache (test oracle, reads the stored order)."""
+    perm = torch.tensor(_perm16(), device=k8.device)
+    nb, hkv, page, d = k8.shape
+    kf = k8.view(torch.float8_e4m3fn).float().view(nb, hkv, page, d // 16, 16)[..., perm].reshape(nb, hkv, page, d)
+    vf = v8.view(torch.float8_e4m3fn).float()[..., perm].transpose(2, 3)  # [nb, hkv, 16, d]
+    return kf * k_scale.unsqueeze(-1), vf * v_scale.unsqueeze(-1)
 
 
 def prefill_attention_tc(q, k_cache, v_cache, block_table, q_start, kv_len, work_seq, work_row0,

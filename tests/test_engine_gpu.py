@@ -244,3 +244,70 @@ def test_native_moe_matches_reference(moe_dir, budget):
     assert total == 20
     assert worst < 0.05, worst
     assert agree >= total - 1
+
+
+def test_fp8_kv_cache_engine_close_to_bf16():
+    """The engine with an fp8 (e4m3, per-row scale) KV cache: over a prefill step and two decode
+    steps of a tiny random model (prefill chunks, a prefix-cache hit, decode rows), the logits
+    stay within a few percent of the bf16 cache's and most greedy tokens agree (both runs are fed
+    the bf16 run's tokens)."""
+    import torch
+
+    from granite_switch_b200.composer.synthetic import base_config
+    from granite_switch_b200.config import GraniteSwitchConfig
+    from granite_switch_b200.engine import EngineConfig
+    from granite_switch_b200.engine.executor import NativeExecutor
+    from granite_switch_b200.engine.kv_cache import BlockManager
+    from granite_switch_b200.engine.llm_engine import HostRouter
+    from granite_switch_b200.engine.request import Request, SamplingParams
+    from granite_switch_b200.engine.scheduler import Scheduler
+    from granite_switch_b200.models.native import NativeGraniteSwitch
+
+    base = base_config("tiny")
+    na, v = 3, base["vocab_size"]
+    cfg = dict(base)
+    cfg.update(num_adapters=na, adapter_token_ids=list(range(v, v + na)), adapter_substitute_token_ids=[1] * na,
+               adapter_ranks=[8] * na, max_lora_rank=8, lora_target_modules=["qkv_proj", "o_proj"],
+               num_hidden_layers=base["num_hidden_layers"] + 2, vocab_size=v + na)
+    config = GraniteSwitchConfig(**cfg)
+    dev = torch.device("cuda", 0)
+    ctx = [int(t) for t in torch.randint(5, 900, (300,), generator=torch.Generator().manual_seed(0))]
+    results, forced = {}, []
+    for fp8 in (False, True):
+        m = NativeGraniteSwitch.from_random(config, dev, max_tokens=1024, num_kv_blocks=128, lora_modules=("qkv", "o"),
+                                            rank=8, seed=3, max_seqs=8)
+        m.kv_fp8 = fp8
+        m._alloc_buffers()
+        ex = NativeExecutor(m, 1024)
+        bm = BlockManager(128)
+        router = HostRouter(config)
+        sch = Scheduler(bm, 8, 1024, True, route_fn=router)
+        for ids in (ctx + [v, 9, 10], ctx + [v + 1, 11], [3, 4, 5, v + 2] * 20):
+            sch.add(Request(ids, SamplingParams(max_tokens=3)))
+        outs = []
+        for step in range(3):
+            out = sch.schedule()
+            _, logits = ex.compute_logits(out)
+            outs.append(logits.float().cpu())
+            # both runs feed the bf16 run's greedy tokens: the random model's logits are
+            # nearly flat, and one flipped argmax would change every later step's input
+            if not fp8:
+                forced.append(logits.argmax(-1).tolist())
+            toks = forced[step]
+            j = 0
+            for c in out.chunks:
+                r = c.req
+                r.carry = router(r.all_ids[c.start:c.start + c.num_tokens], r.carry)
+                r.num_computed = c.start + c.num_tokens
+                bm.register_full_blocks(r)
+                if c.needs_sample:
+                    r.output_ids.append(toks[j])
+                    j += 1
+        results[fp8] = outs
+    for a, b in zip(results[False], results[True]):
+        assert a.shape == b.shape
+        assert (a - b).abs().max() <= 0.05 * a.abs().max(), float((a - b).abs().max())
+        assert (a.argmax(-1) == b.argmax(-1)).float().mean() >= 0.66
+    from granite_switch_b200._native import check_errors
+
+    check_errors(dev)

@@ -312,3 +312,92 @@ def test_bad_indices_reported_not_faulted():
     w, site, idx = read_error_detail(dev)
     assert w & 8 and site == "tcgen05 attention page id" and idx >= n_ok
     assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_kv_write_fp8_roundtrip(d):
+    """fp8 cache write: every (token, KV head) row is stored as e4m3 with scale max|x| / 448;
+    dequantised it is within e4m3's rounding of the bf16 row (half an ulp of a 3-bit mantissa,
+    plus the subnormal step)."""
+    from granite_switch_b200.ops import attention as A
+
+    hq, hkv, t, nb = 8, 2, 50, 16
+    qkv = (torch.randn(t, (hq + 2 * hkv) * d, device="cuda") * torch.rand(t, 1, device="cuda") * 8).bfloat16()
+    slots = torch.randperm(nb * 16, device="cuda")[:t]
+    k8 = torch.zeros(nb, hkv, 16, d, dtype=torch.uint8, device="cuda")
+    v8 = torch.zeros(nb, hkv, d, 16, dtype=torch.uint8, device="cuda")
+    ks = torch.ones(nb, hkv, 16, device="cuda")
+    vs = torch.ones(nb, hkv, 16, device="cuda")
+    A.kv_write_fp8(qkv, slots, k8, v8, ks, vs, hq, hkv, d)
+    kf, vf = A.dequantize_fp8_cache(k8, v8, ks, vs)
+    blk, off = slots // 16, slots % 16
+    k = qkv[:, hq * d:(hq + hkv) * d].float().view(t, hkv, d)
+    v = qkv[:, (hq + hkv) * d:].float().view(t, hkv, d)
+    for x, deq, sc in ((k, kf, ks), (v, vf, vs)):
+        got = deq[blk, :, off]  # [t, hkv, d]
+        scale = sc[blk, :, off].unsqueeze(-1)
+        amax = x.abs().amax(-1, keepdim=True)
+        torch.testing.assert_close(scale, torch.where(amax > 0, amax / 448, torch.ones_like(amax)))
+        bound = 0.0625 * x.abs() + scale * 2.0 ** -9 + 1e-7
+        assert ((got - x).abs() <= bound).all()
+    _check()
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("mode", ["decode", "prefill", "prefill128", "short_after_long"])
+@pytest.mark.parametrize("nsplit", [1, 3])
+@pytest.mark.parametrize("hq", [8, 4])
+def test_paged_attention_fp8(d, mode, nsplit, hq):
+    """Paged attention over the fp8 cache (every mma.sync layout, split keys, GQA groups of 4
+    and 2) against the fp32 oracle on the dequantised cache: the kernel's only extra error is
+    bf16 rounding."""
+    from granite_switch_b200.ops import attention as A
+
+    hkv = 2
+    g = hq // hkv
+    if mode == "decode":
+        q_lens, kv_lens, rows = [1, 1, 2, 1, 4], [1, 37, 300, 1025, 64], 16
+    elif mode == "short_after_long":
+        q_lens, kv_lens, rows = [48, 40, 17], [4548, 2100, 1040], 64
+        nsplit = 4 if nsplit > 1 else 1
+    else:
+        q_lens, kv_lens = [5, 64, 130, 1, 40], [5, 200, 130, 77, 1000]
+        rows = 128 if mode == "prefill128" else 64
+    nb = sum((n + 15) // 16 for n in kv_lens) + 4
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    # fill every page through the write kernel: random K/V rows at every slot
+    slots_all = torch.arange(nb * 16, device="cuda")
+    src = torch.randn(nb * 16, (hq + 2 * hkv) * d, device="cuda", generator=gen).bfloat16()
+    k8 = torch.zeros(nb, hkv, 16, d, dtype=torch.uint8, device="cuda")
+    v8 = torch.zeros(nb, hkv, d, 16, dtype=torch.uint8, device="cuda")
+    ks = torch.ones(nb, hkv, 16, device="cuda")
+    vs = torch.ones(nb, hkv, 16, device="cuda")
+    A.kv_write_fp8(src, slots_all, k8, v8, ks, vs, hq, hkv, d)
+    kf, vf = A.dequantize_fp8_cache(k8, v8, ks, vs)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(1))
+    maxb = max((n + 15) // 16 for n in kv_lens)
+    bt = torch.zeros(len(kv_lens), maxb, dtype=torch.int32)
+    p = 0
+    for i, n in enumerate(kv_lens):
+        for j in range((n + 15) // 16):
+            bt[i, j] = perm[p]
+            p += 1
+    bt = bt.cuda()
+    T = sum(q_lens)
+    q = torch.randn(T, (hq + 2 * hkv) * d, device="cuda", generator=gen).bfloat16()
+    out = torch.zeros(T, hq * d, device="cuda").bfloat16()
+    qs = [0]
+    for n in q_lens:
+        qs.append(qs[-1] + n)
+    ws, wr = A.build_work(q_lens, g, rows)
+    ws_o = torch.empty(nsplit * T * hq * d, device="cuda")
+    ws_l = torch.empty(nsplit * T * hq, device="cuda")
+    A.paged_attention(q, k8, v8, bt, torch.tensor(qs, dtype=torch.int32, device="cuda"),
+                      torch.tensor(kv_lens, dtype=torch.int32, device="cuda"),
+                      torch.tensor(ws, dtype=torch.int32, device="cuda"),
+                      torch.tensor(wr, dtype=torch.int32, device="cuda"), rows, hq, 0.125, out, nsplit, ws_o, ws_l,
+                      ks, vs)
+    ref = A.paged_attention_reference(q, kf, vf, bt, q_lens, kv_lens, hq, 0.125)
+    err = (out.float() - ref).abs().max().item()
+    assert err < 3e-2, err
+    _check()
