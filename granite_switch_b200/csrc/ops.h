@@ -20,6 +20,12 @@ int64_t gsb_gemm_pair_min_m(int64_t m);
 int64_t gsb_gemm_decode_max_m(int64_t v);
 void gsb_gemm_decode_force_split(int64_t acc, int64_t ks);
 void gsb_gemm_decode_trace(const at::Tensor& buf);
+void gsb_quantize_fp8_rows(const at::Tensor& x, const at::Tensor& x8, const at::Tensor& sfa, const at::Tensor& err);
+void gsb_fp8_gemm(const at::Tensor& x8, const at::Tensor& sfa, const at::Tensor& w8, const at::Tensor& sfb,
+                  const at::Tensor& out, int64_t epi, double scale, const c10::optional<at::Tensor>& residual,
+                  const c10::optional<at::Tensor>& s, const c10::optional<at::Tensor>& lb,
+                  const c10::optional<at::Tensor>& tile_mask, int64_t rank, int64_t num_adapters,
+                  std::vector<int64_t> slice_bounds, const at::Tensor& err);
 void gsb_kv_write_fp8(const at::Tensor& qkv, const at::Tensor& slots, const at::Tensor& k8, const at::Tensor& v8,
                       const at::Tensor& k_scale, const at::Tensor& v_scale, int64_t num_q_heads,
                       int64_t num_kv_heads, int64_t head_dim, const at::Tensor& err);

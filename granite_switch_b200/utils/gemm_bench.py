@@ -14,7 +14,22 @@ warm-up and an L2 flush (a 256 MB write) before every launch:
 * ``base``    - the same tcgen05 GEMM with no adapters,
 * ``cublas``  - ``torch.matmul`` of the base weight (the library bar).
 
-TFLOP/s count the base product only (2 M N K), so the three columns compare
+With ``--fp8`` (block-scaled e4m3 base weight, 1x128 activation and 128x128
+weight scales, LoRA in bf16; :mod:`ops.gemm_fp8`):
+
+* ``fp8_native`` - activation quantiser + bf16 LoRA shrink + fp8 GEMM with the
+  bf16 expand fused (what an fp8 projection costs),
+* ``fp8_base``   - the fp8 GEMM alone on pre-quantised operands, no adapters.
+
+With ``--reference`` the reference's own switched projection runs beside them
+(``reference``): one cuBLAS GEMM of ``x`` against ``[W; A_1..A_n]`` and the
+reference's Triton expand kernel (``switch_lora_expand`` from the installed
+reference package, reference: src/granite_switch/vllm/core/lora.py:540-566 and
+src/granite_switch/kernels/switch_lora_kernel.py:414-458), with its kernel
+metadata (kernel-local ids, 32-row tile bitmasks, per-slice shrink columns, rank
+tiers 16..512, rank 8 promoted to 16) built here as its layer builds it.
+
+TFLOP/s count the base product only (2 M N K), so the columns compare
 directly. One JSON line per point on stdout.
 """
 from __future__ import annotations
@@ -79,7 +94,52 @@ def make_case(m, n, k, rank, na, dev, seed=0):
     return dict(x=x, w=w, ids=ids, a_all=a_all, lb=lb, mask=mask.to(dev), rank=rp, na=na)
 
 
-def run_point(m, n, k, rank, na, flush, dev, iters=20, compare_pair=False):
+def _reference_kernels():
+    """The reference's Triton switched-LoRA module from ``baseline/_ref`` (None if absent)."""
+    import importlib
+    import os
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    for base in (os.path.join(root, "baseline", "_ref"), os.path.join(root, "baseline", "_ref", "src")):
+        if os.path.isfile(os.path.join(base, "granite_switch", "kernels", "switch_lora_kernel.py")):
+            if base not in sys.path:
+                sys.path.insert(0, base)
+            return importlib.import_module("granite_switch.kernels.switch_lora_kernel")
+    return None
+
+
+def reference_case(c, n, k, rank, ref):
+    """The reference layer's operands for one point: W_ext (base rows, then every adapter's
+    A rows), the packed B of the rank tier, kernel-local ids, the 32-row tile bitmask and
+    the per-slice shrink column table (one slice)."""
+    r = ref.promote_rank(rank)
+    na, dev = c["na"], c["x"].device
+    g = torch.Generator(device=dev).manual_seed(1)
+    a = (torch.randn(na, 1, r, k, device=dev, generator=g) * 0.02).bfloat16()
+    w_ext = ref.build_w_ext(c["w"], {r: a})
+    lb = (torch.randn(na, n, r, device=dev, generator=g) * 0.02).bfloat16().contiguous()
+    ids = c["ids"].long()
+    bm = ref.get_switch_lora_expand_config()["block_m"]
+    tiles = (ids.shape[0] + bm - 1) // bm
+    bits = torch.zeros(tiles, dtype=torch.int64)
+    ids_h = ids.cpu()
+    for t in range(tiles):
+        v = 0
+        for x in ids_h[t * bm:(t + 1) * bm].unique().tolist():
+            if x > 0:
+                v |= 1 << (x - 1)
+        bits[t] = v if v < (1 << 63) else v - (1 << 64)
+    tiers = list(ref.SUPPORTED_RANKS)
+    na_t = tuple(na if t == r else 0 for t in tiers)
+    col_r = torch.tensor([[n for _ in tiers]], dtype=torch.int32, device=dev)  # tier r's block starts at N
+    block_n = ref.get_switch_lora_expand_config()["block_n"]
+    tile_slice = torch.zeros((n + block_n - 1) // block_n, dtype=torch.int32, device=dev)
+    return dict(w_ext=w_ext, lb=lb, ids=ids, bits=bits.to(dev), na=na_t, col_r=col_r, tile_slice=tile_slice,
+                block_n=block_n)
+
+
+def run_point(m, n, k, rank, na, flush, dev, iters=20, compare_pair=False, fp8=False, ref=None):
     c = make_case(m, n, k, rank, na, dev)
     x, w = c["x"], c["w"]
     out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
@@ -101,6 +161,32 @@ def run_point(m, n, k, rank, na, flush, dev, iters=20, compare_pair=False):
     if compare_pair:  # same point on the CTA-pair and the single-CTA kernel, interleaved
         fns = [("native_pair", native_fn, 1), ("native_single", native_fn, -1), ("base_pair", base_fn, 1),
                ("base_single", base_fn, -1), ("cublas", cublas_fn, None)]
+    if fp8:
+        from ..ops import gemm_fp8 as F
+
+        x8, sfa = F.quantize_rows_fp8(x)
+        w8, sfb = F.quantize_weight_fp8(w)
+
+        def fp8_native_fn():
+            F.quantize_rows_fp8(x, x8, sfa)
+            G.lora_shrink(x, c["a_all"], c["ids"], c["rank"], c["na"], out=s, tile_mask=c["mask"])
+            F.fp8_gemm(x8, sfa, w8, sfb, out, s=s, lb=c["lb"], tile_mask=c["mask"], rank=c["rank"],
+                       num_adapters=c["na"])
+
+        def fp8_base_fn():
+            F.fp8_gemm(x8, sfa, w8, sfb, out)
+
+        fns += [("fp8_native", fp8_native_fn, None), ("fp8_base", fp8_base_fn, None)]
+    if ref is not None:
+        rc = reference_case(c, n, k, rank, ref)
+        x_ext = torch.empty(m, rc["w_ext"].shape[0], dtype=torch.bfloat16, device=dev)
+
+        def reference_fn():
+            torch.mm(x, rc["w_ext"].t(), out=x_ext)
+            ref.switch_lora_expand(x_ext, rc["ids"], rc["bits"], rc["lb"], rc["tile_slice"], rc["col_r"], rc["na"],
+                                   1, rc["block_n"], n)
+
+        fns.append(("reference", reference_fn, None))
     nat = native()
     for name, fn, pair in fns:
         old = nat.gemm_pair_min_m(pair) if pair is not None else None
@@ -220,6 +306,10 @@ def main():
     p.add_argument("--pair-min-m", type=int, default=None, help="smallest M of the CTA-pair kernel (<0: off)")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--compare-pair", action="store_true", help="time CTA-pair and single-CTA tiles side by side")
+    p.add_argument("--fp8", action="store_true", help="also time the block-scaled fp8 GEMM")
+    p.add_argument("--reference", action="store_true",
+                   help="also time the reference's switched projection (cuBLAS + its Triton expand)")
+    p.add_argument("--shapes", nargs="*", default=None, help="N x K pairs as NxK (default: the three 8B shapes)")
     args = p.parse_args()
     dev = torch.device("cuda", 0)
     err_buffer(dev)
@@ -232,11 +322,15 @@ def main():
     flush = _flush_buffer(dev)
     ranks = [32] if args.quick else RANKS
     adapters = [12] if args.quick else ADAPTERS
+    shapes = [tuple(int(v) for v in sh.split("x")) for sh in args.shapes] if args.shapes else SHAPES
+    ref = _reference_kernels() if args.reference else None
+    if args.reference and ref is None:
+        print(json.dumps({"reference": "unavailable: the reference package is not installed under baseline/_ref"}))
     for m in args.ms or MS:
-        for n, k in SHAPES:
+        for n, k in shapes:
             for r in ranks:
                 for na in adapters:
-                    res = run_point(m, n, k, r, na, flush, dev, args.iters, args.compare_pair)
+                    res = run_point(m, n, k, r, na, flush, dev, args.iters, args.compare_pair, args.fp8, ref)
                     print(json.dumps(dict(m=m, n=n, k=k, rank=r, adapters=na, **res)), flush=True)
 
 
