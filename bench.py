@@ -73,6 +73,8 @@ def parse_args():
                    help="cache_affinity: engine steps after which a waiting cold request goes first (negative: none)")
     p.add_argument("--kv-cache-dtype", choices=["bfloat16", "fp8_e4m3"], default="bfloat16",
                    help="KV cache storage; the headline metric is defined on the bf16 cache")
+    p.add_argument("--no-async", dest="async_scheduling", action="store_false",
+                   help="blocking engine steps (read each step's ids before scheduling the next)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-blocks", type=int, default=None)
     return p.parse_args()
@@ -129,6 +131,9 @@ def run_native(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank()))
         group = dist.group.WORLD
+        # host-side agreement (arrivals) over gloo: a broadcast on the GPU stream plus a host
+        # read would wait for the step just launched and serialise the pipelined steps
+        cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
     _native.native()
     config, base = model_config(args)
     ecfg = EngineConfig(max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
@@ -136,7 +141,7 @@ def run_native(args):
                         num_kv_blocks=args.kv_blocks, fused_tp_comm=args.fused_comm, seed=args.seed,
                         scheduling_policy=args.scheduling_policy,
                         max_wait_steps=args.max_wait_steps if args.max_wait_steps >= 0 else None,
-                        kv_cache_dtype=args.kv_cache_dtype)
+                        kv_cache_dtype=args.kv_cache_dtype, async_scheduling=args.async_scheduling)
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
               random_init=dict(lora_modules=("qkv", "o"), rank=32, seed=args.seed), tp_rank=rank, tp_group=group)
     eng = llm.engine
@@ -167,7 +172,7 @@ def run_native(args):
     t0 = time.perf_counter()
     t_start = t0
     next_conv = 0
-    arrived = torch.zeros(1, dtype=torch.long, device="cuda")
+    arrived = torch.zeros(1, dtype=torch.long)
 
     def admit():
         nonlocal next_conv
@@ -181,7 +186,7 @@ def run_native(args):
             n += 1
         if world > 1:
             arrived.fill_(n)
-            dist.broadcast(arrived, src=0, group=group)
+            dist.broadcast(arrived, src=0, group=cpu_group)
             n = int(arrived.item())
         while next_conv < n:
             submit(convs[next_conv], time.perf_counter())
@@ -221,6 +226,7 @@ def run_native(args):
     adm0, cold0 = eng.scheduler.num_admitted, eng.scheduler.num_admitted_cold
     ex = eng.executor
     h2d0, d2h0 = ex.h2d_bytes, ex.d2h_bytes
+    host0 = (eng.stats.host_schedule_s, ex.host_stage_s, ex.host_enqueue_s, ex.host_wait_s, eng.stats.host_post_s)
     launches0 = _native.launch_count()
     start_ev, end_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank()) as clocks:
@@ -238,6 +244,9 @@ def run_native(args):
     wall_s = max_over_ranks(w1 - w0, group)
     gen = eng.stats.generated_tokens - gen0
     launches = _native.launch_count() - launches0
+    host1 = (eng.stats.host_schedule_s, ex.host_stage_s, ex.host_enqueue_s, ex.host_wait_s, eng.stats.host_post_s)
+    host_ms = {k: round((b - a) * 1e3 / args.steps, 3)
+               for k, a, b in zip(("schedule", "stage", "enqueue", "wait_for_gpu", "post"), host0, host1)}
     ttft = ttft_summary(submitted, first_calls, t_start, w0, w1)
     dq, dh = eng.blocks.queries - q0, eng.blocks.hits - h0
     adm, cold = eng.scheduler.num_admitted - adm0, eng.scheduler.num_admitted_cold - cold0
@@ -262,7 +271,8 @@ def run_native(args):
                        "workload": f"poisson {args.rate}/s, {args.calls} chained calls, inv 16-64, gen 32-128",
                        "mode": args.mode, "max_num_batched_tokens": args.max_num_batched_tokens,
                        "scheduling_policy": args.scheduling_policy, "max_wait_steps": ecfg.max_wait_steps,
-                       "kv_cache_dtype": args.kv_cache_dtype, "ramp_steps": ramp, "l2": "inputs larger than L2 (each step streams all weights)",
+                       "kv_cache_dtype": args.kv_cache_dtype, "async_scheduling": eng.async_steps,
+                       "ramp_steps": ramp, "l2": "inputs larger than L2 (each step streams all weights)",
                        "fused_comm": bool(getattr(llm.model, "comm", None) is not None)},
             "e2e": {"value": round(e2e, 2), "unit": "output tok/s", "h2d_bytes_per_step": (ex.h2d_bytes - h2d0) // args.steps,
                     "d2h_bytes_per_step": (ex.d2h_bytes - d2h0) // args.steps},
@@ -274,6 +284,9 @@ def run_native(args):
                            "decode_rows_per_step": round((eng.stats.decode_rows - dr0) / args.steps, 1),
                            "admitted": adm, "cold_admission_fraction": round(cold / adm, 4) if adm else None},
             "device_errors": device_errors,
+            # rank 0's host time per step by phase (wall clock): the GPU has no queued work
+            # during schedule, stage and post
+            "host_ms_per_step": host_ms,
         })
     if world > 1:
         dist.barrier(group=group)

@@ -60,6 +60,15 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// The same with f16 operands (the fp8 cache path: e4m3 -> f16 is one conversion).
+__device__ __forceinline__ void mma16816_f16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 // Byte offset of 16-byte chunk `ch` (of D/8) of row `r` in a tile stored as
 // [D/64 halves][ROWS][64 bf16] with the TMA 128-byte swizzle (chunk ^ row%8).
 template <int ROWS>
@@ -67,24 +76,26 @@ __device__ __forceinline__ uint32_t sw(int r, int ch) {
   return (uint32_t)((ch >> 3) * (ROWS * 128) + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
 }
 
-// fp8 pages (kv_fp8.cu): byte offset of 16-byte chunk `ch` of key row `key` in a
-// K tile of D-byte rows with the TMA swizzle of that row width (128 B: chunk ^
-// row % 8; 64 B: chunk ^ (row / 2) % 4).
-template <int D>
-__device__ __forceinline__ uint32_t sw8(int key, int ch) {
-  if (D == 128) return (uint32_t)(key * 128 + ((ch ^ (key & 7)) << 4));
-  return (uint32_t)(key * 64 + ((ch ^ ((key >> 1) & 3)) << 4));
-}
-__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
-  return v;
-}
-// Two e4m3 values -> bf16x2 (exact: every e4m3 value is a bf16 value).
-__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint32_t pair) {
+// fp8 pages (kv_fp8.cu): K tiles of D-byte rows keep the TMA swizzle of that row
+// width (128 B: 16-byte chunk ^ row % 8; 64 B: chunk ^ (row / 2) % 4), so a warp's 32
+// fragment words hit 32 banks.
+// Two e4m3 values (low 16 bits) -> f16x2: one conversion, exact (every e4m3 value is an
+// f16 value).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
   const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(pair & 0xffffu), __NV_E4M3);
-  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
-  return pack_bf16x2(f.x, f.y);
+  return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+// bf16x2 * s -> f16x2, saturating at the f16 range.
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2_scaled(uint32_t v, float s) {
+  const float2 f = unpack_bf16x2(v);
+  uint32_t r;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(f.y * s), "f"(f.x * s));
+  return r;
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 }  // namespace attn
@@ -127,8 +138,10 @@ static int g_decode_stages = 2;
 
 // F8: the cache is the fp8 layout of kv_fp8.cu (K [blocks, Hkv, 16, D] bytes, V
 // [blocks, Hkv, D, 16] bytes, fp32 scales [blocks, Hkv, 16] for each); fragments are
-// read as 32-bit words and converted to bf16 in registers, the K scales multiply the
-// scores and the V scales the probabilities.
+// read as 32-bit words and converted to f16 pairs in registers (one conversion per
+// pair; bf16 would take three), so these MMAs run on f16 operands: Q is converted
+// once per CTA with the softmax scale folded in (saturating at the f16 range), the K
+// scales multiply the scores, the V scales the probabilities, which are packed as f16.
 template <int D, int WARPS_M, int KT, int STAGES, bool F8 = false>
 __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
     paged_attn_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -222,7 +235,8 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
       if (F8) {
         uint8_t* dS = dV + C::TILE_BYTES;
         tma_load_2d(dK + p * PAGE * D, &tm_k, &full[s], 0, row);
-        tma_load_2d(dV + p * PAGE * D, &tm_v, &full[s], 0, (page * Hkv + kvh) * D);
+        // the transposed V page ([D][16] bytes) is contiguous: one box of D / 16 rows of 256 B
+        tma_load_2d(dV + p * PAGE * D, &tm_v, &full[s], 0, (page * Hkv + kvh) * (D / 16));
         tma_load_2d(dS + p * C::SC_SLOT, &tm_ks, &full[s], 0, page * Hkv + kvh);
         tma_load_2d(dS + (PAGES + p) * C::SC_SLOT, &tm_vs, &full[s], 0, page * Hkv + kvh);
       } else {
@@ -258,6 +272,10 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
     for (int kk = 0; kk < D / 16; ++kk) {
       const int ch = kk * 2 + (lane >> 4);
       ldsm_x4(smem_u32(sQ) + sw<ROWS>(r, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+      if (F8) {  // f16 operands with the softmax scale (log2 domain) folded into Q
+#pragma unroll
+        for (int e = 0; e < 4; ++e) qf[kk][e] = bf16x2_to_f16x2_scaled(qf[kk][e], scale_log2);
+      }
     }
   }
 
@@ -273,6 +291,10 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
     const int tile_start = k_begin + it * KT;
     const uint32_t kbase = smem_u32(sKV + s * C::STAGE_BYTES);
     const uint32_t vbase = kbase + C::TILE_BYTES;
+    // fp8 fragments are plain shared-memory loads (ordered after the barrier wait above,
+    // free to be scheduled ahead of the MMAs)
+    const uint8_t* kst = sKV + s * C::STAGE_BYTES;
+    const uint8_t* vst = kst + C::TILE_BYTES;
     // scale of tile key kt: slot kt / 16, entry kt % 16 (slots of C::SC_SLOT bytes)
     const float* kss = reinterpret_cast<const float*>(sKV + s * C::STAGE_BYTES + 2 * C::TILE_BYTES);
     const float* vss = kss + PAGES * (C::SC_SLOT / 4);
@@ -287,9 +309,12 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
         if (F8) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
+            // sw8: row `key` (key % 8 == g), 16-byte chunk kk ^ (swizzle of g): the chunk bits
+            // of the lane's base are g's, so the swizzled offset is one XOR with kk
             const int key = wn * KPW + (2 * nb2 + h) * 8 + g;
-            const uint32_t wd = lds32(kbase + sw8<D>(key, kk) + 4 * t4);
-            mma16816(sacc[2 * nb2 + h], qf[kk], e4m3x2_to_bf16x2(wd), e4m3x2_to_bf16x2(wd >> 16));
+            const int off = (key * D + 4 * t4 + ((D == 128 ? g : (g >> 1) & 3) << 4)) ^ (kk << 4);
+            const uint32_t wd = *reinterpret_cast<const uint32_t*>(kst + off);
+            mma16816_f16(sacc[2 * nb2 + h], qf[kk], e4m3x2_to_f16x2(wd), e4m3x2_to_f16x2(wd >> 16));
           }
         } else {
           const int key = wn * KPW + nb2 * 16 + (lane & 7) + ((lane >> 4) << 3);
@@ -309,7 +334,7 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
         const int kt = wn * KPW + nb * 8 + 2 * t4 + (e & 1);
         const int j = tile_start + kt;
         const int pos = (e < 2) ? posA : posB;
-        float v = sacc[nb][e] * (F8 ? kss[(kt >> 4) * (C::SC_SLOT / 4) + (kt & 15)] * scale_log2 : scale_log2);
+        float v = sacc[nb][e] * (F8 ? kss[(kt >> 4) * (C::SC_SLOT / 4) + (kt & 15)] : scale_log2);
         if (j >= k_end || j > pos) v = -INFINITY;
         sacc[nb][e] = v;
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
@@ -350,29 +375,40 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
           sacc[nb][e] *= vss[(kt >> 4) * (C::SC_SLOT / 4) + (kt & 15)];
         }
     }
+    // rescale O only when some row's running max grew in this tile (after the first
+    // tiles of a long context it rarely does); warp-uniform, so the MMAs stay converged
+    if (__any_sync(0xffffffffu, corr[0] != 1.f || corr[1] != 1.f)) {
 #pragma unroll
-    for (int i = 0; i < OB; ++i) {
-      o[i][0] *= corr[0];
-      o[i][1] *= corr[0];
-      o[i][2] *= corr[1];
-      o[i][3] *= corr[1];
+      for (int i = 0; i < OB; ++i) {
+        o[i][0] *= corr[0];
+        o[i][1] *= corr[0];
+        o[i][2] *= corr[1];
+        o[i][3] *= corr[1];
+      }
     }
 #pragma unroll
     for (int kk = 0; kk < KPW / 16; ++kk) {
       uint32_t pa[4];
-      pa[0] = pack_bf16x2(sacc[2 * kk][0], sacc[2 * kk][1]);
-      pa[1] = pack_bf16x2(sacc[2 * kk][2], sacc[2 * kk][3]);
-      pa[2] = pack_bf16x2(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
-      pa[3] = pack_bf16x2(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
+      if (F8) {
+        pa[0] = pack_f16x2(sacc[2 * kk][0], sacc[2 * kk][1]);
+        pa[1] = pack_f16x2(sacc[2 * kk][2], sacc[2 * kk][3]);
+        pa[2] = pack_f16x2(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+        pa[3] = pack_f16x2(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
+      } else {
+        pa[0] = pack_bf16x2(sacc[2 * kk][0], sacc[2 * kk][1]);
+        pa[1] = pack_bf16x2(sacc[2 * kk][2], sacc[2 * kk][3]);
+        pa[2] = pack_bf16x2(sacc[2 * kk + 1][0], sacc[2 * kk + 1][1]);
+        pa[3] = pack_bf16x2(sacc[2 * kk + 1][2], sacc[2 * kk + 1][3]);
+      }
 #pragma unroll
       for (int db = 0; db < D / 16; ++db) {
         if (F8) {
           // V^T page of the 16 keys: [D][16 bytes]; one word = keys 2t, 2t+1, 2t+8, 2t+9
-          const uint32_t pg = vbase + ((wn * KPW + kk * 16) / PAGE) * (PAGE * D);
+          const uint8_t* pg = vst + ((wn * KPW + kk * 16) / PAGE) * (PAGE * D) + g * 16 + 4 * t4;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const uint32_t wd = lds32(pg + (db * 16 + h * 8 + g) * 16 + 4 * t4);
-            mma16816(o[2 * db + h], pa, e4m3x2_to_bf16x2(wd), e4m3x2_to_bf16x2(wd >> 16));
+            const uint32_t wd = *reinterpret_cast<const uint32_t*>(pg + (db * 16 + h * 8) * 16);
+            mma16816_f16(o[2 * db + h], pa, e4m3x2_to_f16x2(wd), e4m3x2_to_f16x2(wd >> 16));
           }
         } else {
           const int key = wn * KPW + kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
@@ -641,8 +677,9 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
   if (f8) {
     const CUtensorMapSwizzle swz = D == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     tk = make_tmap_2d(k_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, page_rows, D, D, D, attn::PAGE, swz);
-    tv = make_tmap_2d(v_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k_cache.size(0) * Hkv * D,
-                      attn::PAGE, attn::PAGE, attn::PAGE, D, CU_TENSOR_MAP_SWIZZLE_NONE);
+    // V pages ([D][16] bytes, contiguous) as rows of 256 bytes: D / 16 rows per page
+    tv = make_tmap_2d(v_cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1,
+                      (uint64_t)k_cache.size(0) * Hkv * (D / 16), 256, 256, 256, D / 16, CU_TENSOR_MAP_SWIZZLE_NONE);
     tks = make_tmap_2d(k_scale->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)k_cache.size(0) * Hkv,
                        attn::PAGE, attn::PAGE, attn::PAGE, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
     tvs = make_tmap_2d(v_scale->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)k_cache.size(0) * Hkv,

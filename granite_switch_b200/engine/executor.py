@@ -12,6 +12,7 @@ prefix caching and chunked prefill are checked against plain ``generate``).
 from __future__ import annotations
 
 import math
+import time
 
 import numpy as np
 import torch
@@ -78,13 +79,22 @@ class HostBatch:
         ids = np.empty(t, np.int64)
         blocks = []
         width = 1
+        fb_dst, fb_src = [], []
         for i, c in enumerate(chunks):
             r = c.req
             end = c.start + c.num_tokens
             ids[cu[i]:cu[i + 1]] = _req_tokens(r, end)[c.start:end]
+            if r.pending >= 0:  # its last sampled token is still on the device
+                pos = len(r.prompt_ids) + r.pending
+                if c.start <= pos < end:
+                    fb_dst.append(int(cu[i]) + pos - c.start)
+                    fb_src.append(r.pending_row)
             bl = _req_blocks(r)
             blocks.append(bl)
             width = max(width, bl[1])
+        # token rows whose id is the previous step's sample: (row in this step, row of that step's samples)
+        self.fb_dst = np.asarray(fb_dst, np.int64)
+        self.fb_src = np.asarray(fb_src, np.int64)
         bt = np.zeros((s, width), np.int32)
         for i, (bl, ln) in enumerate(blocks):
             bt[i, :ln] = bl[:ln]
@@ -101,6 +111,13 @@ class HostBatch:
 
 
 GRAPH_BUCKETS = (8, 16, 32, 64, 128, 256, 512)
+
+
+class StepHandle:
+    """A launched step: its sampled ids land in buffer ``buf`` (``nb`` rows) when ``event`` completes."""
+
+    def __init__(self, out: SchedulerOutput, nb: int, buf: int, event, tokens=None):
+        self.out, self.nb, self.buf, self.event, self.tokens = out, nb, buf, event, tokens
 
 
 class _DecodeGraph:
@@ -131,10 +148,12 @@ class NativeExecutor:
         self.h_i32 = torch.empty(3 * s + 1, dtype=torch.int32, **pin)     # starts | carry | kv_lens
         self.h_bt = torch.zeros(s, self.max_blocks, dtype=torch.int32, **pin)
         self.h_rows = torch.empty(s, dtype=torch.long, **pin)
-        self.h_out = torch.empty(s, dtype=torch.long, **pin)
-        # device error word (bits, bad-index site, index), read back with each step's ids
-        self.h_err = torch.zeros(3, dtype=torch.int32, **pin)
+        # sampled ids and the device error word (bits, bad-index site, index) of the last two
+        # launched steps: a step's inputs may take the previous step's ids on the device
+        self.h_out = torch.empty(2, s, dtype=torch.long, **pin)
+        self.h_err = torch.zeros(2, 3, dtype=torch.int32, **pin)
         self.d_err = torch.zeros(3, dtype=torch.int32, device=model.device)
+        self.h_fb = torch.empty(2, s, dtype=torch.long, **pin)
         dev = self.device
         self.d_i64 = torch.empty(3 * t, dtype=torch.long, device=dev)
         self.d_i32 = torch.empty(3 * s + 1, dtype=torch.int32, device=dev)
@@ -142,11 +161,14 @@ class NativeExecutor:
         self.d_rows = torch.empty(s, dtype=torch.long, device=dev)
         self.d_work = torch.empty(4, 4 * t + 4 * s, dtype=torch.int32, device=dev)
         self.h_work = torch.empty(4, 4 * t + 4 * s, dtype=torch.int32, **pin)
-        self.d_tokens = torch.empty(s, dtype=torch.long, device=dev)
+        self.d_tokens = torch.empty(2, s, dtype=torch.long, device=dev)
+        self.d_fb = torch.empty(2, s, dtype=torch.long, device=dev)
+        self.buf = 0           # buffer of the next launched step
+        self.prev_buf = None   # buffer of the last launched step (source of fed-back ids)
         # numpy views of the pinned staging buffers (same memory)
         self.np_i64, self.np_i32 = self.h_i64.numpy(), self.h_i32.numpy()
         self.np_bt, self.np_rows, self.np_work = self.h_bt.numpy(), self.h_rows.numpy(), self.h_work.numpy()
-        self.copy_event = torch.cuda.Event()
+        self.copy_events = (torch.cuda.Event(), torch.cuda.Event())
         self.h2d_event = torch.cuda.Event()
         self.h2d_pending = False
         self.h2d_bytes = 0
@@ -157,6 +179,10 @@ class NativeExecutor:
         self.nvtx = False          # NVTX range per step (regions: model.prof = NvtxRanges())
         self.graphs: dict[int, _DecodeGraph] = {}
         self.graph_replays = 0
+        # host seconds: staging inputs, enqueueing the forward, waiting for the step's results
+        self.host_stage_s = 0.0
+        self.host_enqueue_s = 0.0
+        self.host_wait_s = 0.0
 
     # ------------------------------------------------------------------ CUDA graphs
     def _graph_bucket(self, out: SchedulerOutput) -> int | None:
@@ -198,9 +224,25 @@ class NativeExecutor:
         self.d_i32[: 3 * p + 1].copy_(self.h_i32[: 3 * p + 1], non_blocking=True)
         self.d_bt[:p].copy_(self.h_bt[:p], non_blocking=True)
         self.d_rows[:p].copy_(self.h_rows[:p], non_blocking=True)
+        self._feed_back(hb, self.d_i64[:s])
         self.h2d_event.record()
         self.h2d_pending = True
         self.h2d_bytes += 8 * 3 * p + 4 * (3 * p + 1) + 4 * p * self.max_blocks + 8 * p
+
+    def _feed_back(self, hb: HostBatch, ids: torch.Tensor) -> None:
+        """Rows whose token was sampled by the previous (still running) step take it from that
+        step's device buffer: one H2D copy of the row pairs and one gather."""
+        n = len(hb.fb_dst)
+        if n == 0:
+            return
+        if self.prev_buf is None:
+            raise RuntimeError("a step feeds back sampled ids but no step was launched before it")
+        hf = self.h_fb.numpy()
+        hf[0, :n] = hb.fb_dst
+        hf[1, :n] = hb.fb_src
+        self.d_fb[:, :n].copy_(self.h_fb[:, :n], non_blocking=True)
+        ids.index_copy_(0, self.d_fb[0, :n], self.d_tokens[self.prev_buf].index_select(0, self.d_fb[1, :n]))
+        self.h2d_bytes += 16 * n
 
     def _graph_batch(self, p: int, work):
         from ..models.native import AttnPlan, StepBatch
@@ -274,6 +316,7 @@ class NativeExecutor:
         nw = max((len(p[0]) for p in plans_host), default=0)
         if plans_host:
             self.d_work[: 2 * len(plans_host), :nw].copy_(self.h_work[: 2 * len(plans_host), :nw], non_blocking=True)
+        self._feed_back(hb, self.d_i64[:t])
         self.h2d_event.record()
         self.h2d_pending = True
         self.h2d_bytes += 8 * 3 * t + 4 * (3 * s + 1) + 4 * s * width + 8 * nb + 4 * 2 * len(plans_host) * nw
@@ -318,9 +361,16 @@ class NativeExecutor:
         with nvtx_range(f"step {len(hb.ids)} tokens", self.nvtx):
             p = self._graph_bucket(out)
             if p is not None:
+                t0 = time.perf_counter()
                 logits = self._run_graph(hb, p)
+                self.host_enqueue_s += time.perf_counter() - t0
             else:
-                logits = self.model.forward(self._stage(hb))
+                t0 = time.perf_counter()
+                batch = self._stage(hb)
+                t1 = time.perf_counter()
+                logits = self.model.forward(batch)
+                self.host_stage_s += t1 - t0
+                self.host_enqueue_s += time.perf_counter() - t1
                 if not len(hb.rows):
                     logits = None
             if self.routing_trace is not None:
@@ -343,37 +393,48 @@ class NativeExecutor:
         rec["spans"] = [(int(hb.starts[i]), int(hb.starts[i + 1])) for i in range(len(hb.chunks))]
 
     def execute(self, out: SchedulerOutput) -> list[int]:
+        """Run one step and return its sampled ids (blocking)."""
+        return self.collect(self.launch(out))
+
+    def launch(self, out: SchedulerOutput) -> StepHandle:
+        """Stage and enqueue one step (forward, sampling, copies of the ids and the error word)
+        without waiting for it. Rows whose input is the previous launched step's sample read it
+        on the device (``HostBatch.fb_dst``)."""
         from ..ops import elementwise as E
         from .sampling import sample
 
         hb, logits = self.compute_logits(out)
         nb = len(hb.rows)
-        if nb == 0:  # no row samples (prefill chunks only): still check the step's kernels
-            self._stage_error_word()
-            self.copy_event.record()
-            self.copy_event.synchronize()
-            self.d2h_bytes += 12
-            self._raise_device_error()
-            return []
-        toks = self.d_tokens[:nb]
-        pipe = self.model.pipeline
-        if pipe is None or self.model.last_stage:
-            params = [c.req.sampling for c in hb.chunks if c.needs_sample]
-            if all(p.greedy for p in params):
-                E.argmax(logits, out=toks)
-            else:
-                sample(logits, params, [c.req for c in hb.chunks if c.needs_sample], out=toks)
-        if pipe is not None:
-            pipe.broadcast_tokens(toks)  # every stage's scheduler sees the sampled ids
-        self._stage_error_word()
-        self.h_out[:nb].copy_(toks, non_blocking=True)
-        self.copy_event.record()
-        self.copy_event.synchronize()
+        buf = self.buf
+        toks = self.d_tokens[buf, :nb]
+        if nb:
+            pipe = self.model.pipeline
+            if pipe is None or self.model.last_stage:
+                params = [c.req.sampling for c in hb.chunks if c.needs_sample]
+                if all(p.greedy for p in params):
+                    E.argmax(logits, out=toks)
+                else:
+                    sample(logits, params, [c.req for c in hb.chunks if c.needs_sample], out=toks)
+            if pipe is not None:
+                pipe.broadcast_tokens(toks)  # every stage's scheduler sees the sampled ids
+        self._stage_error_word(buf)
+        if nb:
+            self.h_out[buf, :nb].copy_(toks, non_blocking=True)
+        ev = self.copy_events[buf]
+        ev.record()
         self.d2h_bytes += 8 * nb + 12
-        self._raise_device_error()
-        return self.h_out[:nb].tolist()
+        self.prev_buf, self.buf = buf, buf ^ 1
+        return StepHandle(out, nb, buf, ev)
 
-    def _stage_error_word(self) -> None:
+    def collect(self, h: StepHandle) -> list[int]:
+        """Wait for a launched step's ids (raises :class:`DeviceError` if a kernel reported one)."""
+        t0 = time.perf_counter()
+        h.event.synchronize()
+        self.host_wait_s += time.perf_counter() - t0
+        self._raise_device_error(h.buf)
+        return self.h_out[h.buf, :h.nb].tolist()
+
+    def _stage_error_word(self, buf: int) -> None:
         """Queue the copy of the device error word next to the sampled ids.
 
         Under tensor or pipeline parallelism the word is max-reduced over the
@@ -391,17 +452,17 @@ class NativeExecutor:
             group = self.tp_group
         if group is not None:
             torch.distributed.all_reduce(self.d_err, op=torch.distributed.ReduceOp.MAX, group=group)
-        self.h_err.copy_(self.d_err, non_blocking=True)
+        self.h_err[buf].copy_(self.d_err, non_blocking=True)
 
-    def _raise_device_error(self) -> None:
+    def _raise_device_error(self, buf: int) -> None:
         """After the step's copies landed: raise :class:`DeviceError` if a kernel reported one
         (and clear the device word, so the engine can go on with other requests)."""
-        word = int(self.h_err[0])
+        word = int(self.h_err[buf, 0])
         if not word:
             return
         from .._native import DeviceError, err_buffer, site_name
 
-        site, idx = int(self.h_err[1]), int(self.h_err[2])
+        site, idx = int(self.h_err[buf, 1]), int(self.h_err[buf, 2])
         err_buffer(self.device).zero_()
         self.h_err.zero_()
         raise DeviceError(word, site_name(site), idx if site else None)
@@ -421,6 +482,16 @@ class ReferenceExecutor:
         self.table = sw._table if sw is not None else None
         self.h2d_bytes = self.d2h_bytes = 0
         self.routing_trace = None
+        self.last_tokens = np.zeros(0, np.int64)  # the last launched step's sampled ids
+
+    def launch(self, out: SchedulerOutput) -> StepHandle:
+        """Run the step now (CPU); rows fed back from the previous step read its ids here."""
+        toks = self.execute(out)
+        self.last_tokens = np.asarray(toks, np.int64)
+        return StepHandle(out, len(toks), 0, None, toks)
+
+    def collect(self, h: StepHandle) -> list[int]:
+        return h.tokens
 
     @torch.no_grad()
     def execute(self, out: SchedulerOutput) -> list[int]:
@@ -442,6 +513,8 @@ class ReferenceExecutor:
 
         cfg = self.cfg
         hb = HostBatch(out)
+        if len(hb.fb_dst):
+            hb.ids[hb.fb_dst] = self.last_tokens[hb.fb_src]
         ids = torch.from_numpy(hb.ids)
         if self.table is not None:
             idx, _ = route_flat(ids, hb.starts.tolist(), hb.carry.tolist(), self.table)

@@ -42,7 +42,7 @@ class EngineConfig:
     enable_chunked_prefill: bool = True
     tensor_parallel_size: int = 1
     pipeline_parallel_size: int = 1
-    use_cuda_graphs: bool = False
+    use_cuda_graphs: bool = True           # decode-only steps on one GPU replay a captured graph
     dtype: str = "bfloat16"
     seed: int = 0
     fused_tp_comm: bool = False            # symmetric-memory fused GEMM + reduction kernels
@@ -50,6 +50,9 @@ class EngineConfig:
     max_wait_steps: int | None = DEFAULT_MAX_WAIT_STEPS  # cache_affinity: steps before a cold request
     #                                                    goes first; None = unbounded
     kv_cache_dtype: str = "bfloat16"       # or "fp8_e4m3": e4m3 K/V with a per-(token, KV head) scale
+    # launch step i+1 before reading step i's sampled ids (they reach step i+1's inputs on
+    # the device), so scheduling and bookkeeping overlap the GPU
+    async_scheduling: bool = True
 
 
 @dataclass
@@ -63,6 +66,9 @@ class EngineStats:
     device_errors: int = 0   # steps aborted because a kernel reported an error
     prefill_tokens: int = 0  # tokens computed in prefill chunks (prompt tokens not served from cache)
     decode_rows: int = 0     # single-token decode rows
+    # host seconds per phase (the GPU idles during schedule / stage / post unless work is queued)
+    host_schedule_s: float = 0.0
+    host_post_s: float = 0.0
 
 
 class HostRouter:
@@ -114,6 +120,11 @@ class LLMEngine:
         self.eos = config.eos_token_id if isinstance(config.eos_token_id, int) else None
         self.on_finish = None  # optional callback(req)
         self.health = None     # optional parallel.health.Heartbeat (multi-rank)
+        # async steps need an executor that launches without waiting, and no probe
+        # control tokens (a probe marker is found from the sampled row's token id on the host)
+        self.async_steps = (self.ecfg.async_scheduling and hasattr(executor, "launch")
+                            and not (getattr(config, "probe_control_token_ids", None) or []))
+        self._inflight = None  # StepHandle of the launched step whose ids are not read yet
 
     # -------------------------------------------------------------- requests
     def add_request(self, prompt_ids: list[int], sampling: SamplingParams | None = None,
@@ -135,14 +146,22 @@ class LLMEngine:
         return req
 
     def abort_request(self, request_id: str) -> bool:
-        return self.scheduler.abort(request_id)
+        r = self.requests.get(request_id)
+        ok = self.scheduler.abort(request_id)
+        if ok and r is not None:
+            r.drop_pending()  # a token of the running step is discarded with the request
+        return ok
 
     def has_unfinished(self) -> bool:
-        return self.scheduler.has_work()
+        return self.scheduler.has_work() or self._inflight is not None
 
     # -------------------------------------------------------------- step
     def step(self) -> list[Request]:
+        if self.async_steps:
+            return self._step_async()
+        t0 = time.perf_counter()
         out = self.scheduler.schedule()
+        self.stats.host_schedule_s += time.perf_counter() - t0
         if not out.chunks:
             return []
         if self.health is not None:
@@ -160,6 +179,7 @@ class LLMEngine:
         if self.health is not None:
             self.health.beat()
         now = time.perf_counter()
+        t_post = now
         finished = []
         j = 0
         for c in out.chunks:
@@ -190,9 +210,117 @@ class LLMEngine:
                 if self.on_finish is not None:
                     self.on_finish(r)
         self.stats.steps += 1
+        self.stats.host_post_s += time.perf_counter() - t_post
         return finished
 
-    def _abort_step(self, out, err) -> None:
+    def _count_mix(self, out) -> None:
+        for c in out.chunks:
+            if c.num_tokens > 1 or c.req.prefilling:
+                self.stats.prefill_tokens += c.num_tokens
+            else:
+                self.stats.decode_rows += c.num_tokens
+
+    def _step_async(self) -> list[Request]:
+        """One pipelined step: finish the bookkeeping of the running step that needs no
+        sampled values (positions, routing carry, published blocks, a placeholder per
+        sampled row), schedule and launch the next step (its decode rows take the running
+        step's ids on the device), then wait for the running step's ids and resolve them
+        (stop checks, finished requests). A request whose last token stops it was scheduled
+        once more; that row's result is dropped. Returns the requests finished by the
+        step whose ids were resolved."""
+        inflight = self._inflight  # the launched step's handle, or None
+        t0 = time.perf_counter()
+        sampled = self._advance(inflight) if inflight is not None else None
+        out = self.scheduler.schedule()
+        self.stats.host_schedule_s += time.perf_counter() - t0
+        handle = None
+        if out.chunks:
+            if self.health is not None:
+                self.health.check()
+            self._count_mix(out)
+            try:
+                handle = self.executor.launch(out)
+            except DeviceError as e:
+                self._inflight = None
+                self._abort_step(out, e, extra=inflight.out if inflight is not None else None)
+                raise
+        finished = []
+        if inflight is not None:
+            try:
+                toks = self.executor.collect(inflight)
+            except DeviceError as e:
+                self._inflight = None
+                if handle is not None:
+                    try:
+                        self.executor.collect(handle)  # drain it; its ids are discarded
+                    except DeviceError:
+                        pass
+                self._abort_step(inflight.out, e, extra=out)
+                raise
+            if self.health is not None:
+                self.health.beat()
+            t_post = time.perf_counter()
+            finished = self._resolve(sampled, toks)
+            self.stats.host_post_s += time.perf_counter() - t_post
+            self.stats.steps += 1
+        self._inflight = handle
+        return finished
+
+    def _advance(self, handle) -> list:
+        """Bookkeeping of a launched step that needs no sampled value; appends a placeholder
+        for every sampled row and returns them, ``(request, output index, row)``, for
+        :meth:`_resolve`."""
+        sampled = []
+        row = 0
+        for c in handle.out.chunks:
+            r = c.req
+            ns = c.needs_sample
+            if r.status == RequestStatus.FINISHED:
+                row += ns
+                continue
+            end = c.start + c.num_tokens
+            toks = r._np_tok[c.start:end] if r._np_tok_n >= end else r.all_ids[c.start:end]
+            r.carry = self.router(toks, r.carry)
+            r.num_computed = end
+            self.blocks.register_full_blocks(r)
+            if ns:
+                r.set_pending(row)
+                sampled.append((r, r.pending, row))
+                if len(r.output_ids) >= r.sampling.max_tokens:
+                    r.finishing = True
+                row += 1
+        return sampled
+
+    def _resolve(self, sampled, toks) -> list[Request]:
+        now = time.perf_counter()
+        finished = []
+        for r, idx, row in sampled:
+            if r.status == RequestStatus.FINISHED or r.pending != idx:
+                continue  # aborted while its step ran
+            tok = int(toks[row])
+            r.resolve_pending(tok)
+            self.stats.generated_tokens += 1
+            if r.first_token_time is None:
+                r.first_token_time = now
+            reason = self._stop_reason(r, tok)
+            if reason:
+                self._finish(r, reason, now)
+                finished.append(r)
+        return finished
+
+    def _finish(self, r: Request, reason: str, now: float) -> None:
+        r.finish_time = now
+        r.finishing = False
+        self.scheduler.finish(r, reason)
+        self.stats.finished += 1
+        if r.ttft() is not None:
+            self.stats.ttfts.append(r.ttft())
+        self.stats.latencies.append(r.finish_time - r.arrival_time)
+        self.requests.pop(r.request_id, None)
+        if self.on_finish is not None:
+            self.on_finish(r)
+
+    def _abort_step(self, out, err, extra=None) -> None:
         """A kernel of this step reported an error: its outputs cannot be trusted.
 
         Every request the step carried is finished with reason ``"error"`` (its
@@ -202,17 +330,20 @@ class LLMEngine:
         """
         now = time.perf_counter()
         self.stats.device_errors += 1
-        for c in out.chunks:
+        chunks = list(out.chunks) + (list(extra.chunks) if extra is not None else [])
+        for c in chunks:
             r = c.req
             if r.status == RequestStatus.FINISHED:
                 continue
+            r.drop_pending()
+            r.finishing = False
             r.finish_time = now
             self.scheduler.finish(r, "error")
             self.requests.pop(r.request_id, None)
         for r in list(self.scheduler.running):  # their pages are suspect too: recompute them
             self.scheduler.preempt(r)
         self.blocks.reset_prefix_cache()
-        _log.error("engine step aborted %d request(s): %s", len(out.chunks), err)
+        _log.error("engine step aborted %d request(s): %s", len(chunks), err)
 
     def _stop_reason(self, r: Request, tok: int) -> str | None:
         sp = r.sampling

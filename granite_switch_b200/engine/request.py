@@ -32,6 +32,9 @@ class RequestStatus(enum.Enum):
     FINISHED = 3
 
 
+PENDING_TOKEN = -1  # placeholder id of a sampled token not yet copied to the host
+
+
 @dataclass
 class Request:
     prompt_ids: list[int]
@@ -49,6 +52,12 @@ class Request:
     num_cached_tokens: int = 0         # prefix-cache hit at admission
     carry: int = 0                     # routing carry after num_computed tokens
     matched: bool = False              # prefix cache consulted for the current admission
+    # async steps: index in output_ids of a sampled token whose value is still on the
+    # device (PENDING_TOKEN there), its row in that step's sampled-token buffer, and
+    # whether that token completes max_tokens (then the request is not scheduled again)
+    pending: int = -1
+    pending_row: int = -1
+    finishing: bool = False
     first_token_time: float | None = None
     finish_time: float | None = None
     finish_reason: str | None = None
@@ -84,6 +93,33 @@ class Request:
     @property
     def num_tokens(self) -> int:
         return len(self.prompt_ids) + len(self.output_ids)
+
+    def set_pending(self, row: int) -> None:
+        """Append a sampled token whose value is still on the device (row ``row`` of its step)."""
+        self.output_ids.append(PENDING_TOKEN)
+        self.pending = len(self.output_ids) - 1
+        self.pending_row = row
+
+    def resolve_pending(self, tok: int) -> None:
+        """Write the pending token's value here and into the maintained id mirrors."""
+        i = self.pending
+        if i < 0:
+            return
+        self.output_ids[i] = tok
+        j = len(self.prompt_ids) + i
+        if self._all is not None and len(self._all) > j:
+            self._all[j] = tok
+        if self._np_tok is not None and self._np_tok_n > j:
+            self._np_tok[j] = tok
+        self.pending = self.pending_row = -1
+
+    def drop_pending(self) -> None:
+        """Forget a pending token (the request was aborted while its step ran)."""
+        if self.pending < 0:
+            return
+        del self.output_ids[self.pending:]
+        self._np_tok_n = min(self._np_tok_n, len(self.prompt_ids) + len(self.output_ids))
+        self.pending = self.pending_row = -1
 
     @property
     def prefilling(self) -> bool:

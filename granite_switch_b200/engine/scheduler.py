@@ -132,6 +132,9 @@ class Scheduler:
         i = 0
         while i < len(self.running) and budget > 0:
             req = self.running[i]
+            if req.finishing:  # its last token is still on the device
+                i += 1
+                continue
             remaining = req.num_tokens - req.num_computed
             n = min(remaining, budget) if self.chunked else remaining
             if n <= 0 or n > budget:
@@ -180,6 +183,10 @@ class Scheduler:
         req.finish_reason = reason
         if req in self.running:
             self.running.remove(req)
+        else:  # preempted while its last step ran (async steps)
+            for q in (self.warm, self.waiting):
+                if req in q:
+                    q.remove(req)
         self.blocks.free_request(req)
 
     def abort(self, request_id: str) -> bool:

@@ -48,7 +48,7 @@ def _run(config, device, steps_out, tp_rank=0, tp=1, tp_group=None, pipeline=Non
         hb, logits = ex.compute_logits(out)
         if logits is not None:
             logits_seen.append(logits.float().cpu())
-        toks = ex.d_tokens[: len(hb.rows)]
+        toks = ex.d_tokens[0, : len(hb.rows)]
         if logits is not None:
             toks.copy_(logits.argmax(dim=-1))
         if pipeline is not None:

@@ -7,8 +7,10 @@ Run under torchrun, one process per GPU::
 Every rank builds the same seeded random model, keeps its shard, runs one
 prefill step and two decode steps through the native executor, and gathers
 the logits: over NCCL, with the fused reductions, and with every fused
-reduction on the large-step path. Rank 0 also builds the unsharded model alone and compares. Prints
-one JSON line per checked mode on rank 0 and exits non-zero on a mismatch.
+reduction on the large-step path. Rank 0 also builds the unsharded model alone and compares. With
+``--engine`` every rank also serves prompts through the engine with pipelined and with blocking
+steps (NCCL and fused reductions) and requires identical greedy tokens. Prints one JSON line per
+checked mode on rank 0 and exits non-zero on a mismatch.
 """
 from __future__ import annotations
 
@@ -134,11 +136,36 @@ def _check_primitives(device, group, rank, world) -> dict:
     return out
 
 
+def _engine_tokens(config, device, world, rank, group, async_on: bool, fused: bool, lora) -> list[list[int]]:
+    """Greedy tokens of the serving engine (``LLM``) on this rank's shard: chunked prefill,
+    decode rows and, with ``async_on``, pipelined steps whose decode inputs are fed back on
+    the device."""
+    from ..engine import LLM, EngineConfig, SamplingParams
+
+    ecfg = EngineConfig(max_num_seqs=6, max_num_batched_tokens=96, num_kv_blocks=256, max_model_len=512,
+                        tensor_parallel_size=world, fused_tp_comm=fused, async_scheduling=async_on)
+    llm = LLM(config, device=str(device), engine_config=ecfg,
+              random_init=dict(lora_modules=lora, rank=16, seed=7), tp_rank=rank, tp_group=group)
+    assert llm.engine.async_steps == async_on
+    g = torch.Generator().manual_seed(5)
+    v = config.vocab_size - config.num_adapters
+    prompts = []
+    for i in range(8):
+        n = int(torch.randint(20, 120, (1,), generator=g))
+        ids = torch.randint(5, v, (n,), generator=g).tolist()
+        ids.insert(n // 2, config.adapter_token_ids[i % config.num_adapters])
+        prompts.append(ids)
+    outs = llm.generate(prompts, SamplingParams(max_tokens=10))
+    return [o.output_ids for o in outs]
+
+
 def main(argv=None) -> int:
     import argparse
 
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--lora", default="qkv,o", help="comma-separated LoRA modules of the check model")
+    ap.add_argument("--engine", action="store_true",
+                    help="also compare the serving engine's pipelined steps with blocking steps (greedy tokens)")
     args = ap.parse_args(argv)
     lora = tuple(x for x in args.lora.split(",") if x)
     rank = int(os.environ["RANK"])
@@ -178,6 +205,17 @@ def main(argv=None) -> int:
             ok &= good
             print(json.dumps({"mode": mode, "tp": world, "max_rel_err": round(worst, 5), "argmax_agree": agree,
                               "rows": total, "device_errors": errs, "ok": good}), flush=True)
+    if args.engine:
+        for fused in (False, True):
+            sync_t = _engine_tokens(config, device, world, rank, group, False, fused, lora)
+            dist.barrier()
+            async_t = _engine_tokens(config, device, world, rank, group, True, fused, lora)
+            dist.barrier()
+            same = sync_t == async_t and all(len(t) == 10 for t in async_t)
+            ok &= same
+            if rank == 0:
+                print(json.dumps({"mode": "engine_async_vs_sync", "tp": world, "fused": fused, "ok": same}),
+                      flush=True)
     flag = torch.tensor([1 if ok else 0], device=device)
     dist.broadcast(flag, 0)
     dist.barrier()

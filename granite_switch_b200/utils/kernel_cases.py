@@ -1,8 +1,8 @@
 """One launch of each native kernel on a representative shape, for profiler captures.
 
 ``python -m granite_switch_b200.utils.kernel_cases <case>`` with case in
-gemm, gemm_pair, gemm_single, cublas, swiglu, attn_prefill64, moe, probe, decode_gemm, decode_shrink, attn_prefill, attn_decode, rmsnorm, rope, embed,
-routing, sample (or ``all``). Pair it with ``ncu --clock-control none -k regex:<kernel> -c 1`` (without
+gemm, gemm_pair, gemm_single, cublas, swiglu, attn_prefill64, moe, probe, decode_gemm, decode_shrink, fp8_gemm,
+fp8_quant, attn_prefill, attn_decode, attn_decode_fp8, rmsnorm, rope, embed, routing, sample (or ``all``). Pair it with ``ncu --clock-control none -k regex:<kernel> -c 1`` (without
 ``--clock-control none`` ncu locks the GPU clocks).
 """
 import sys
@@ -53,13 +53,20 @@ if want("decode_gemm"):  # down projection of the headline decode step (222 toke
     x2 = torch.randn(222, I, device=dev).bfloat16()
     h = torch.randn(222, H, device=dev).bfloat16()
     G.switched_gemm(x2, w, h, epi=G.EPI_RESADD, residual=h, scale=0.5)
+if want("fp8_gemm") or want("fp8_quant"):  # block-scaled fp8 GEMM, 4096 x 12800 x 4096 (and its activation quantiser)
+    from granite_switch_b200.ops import gemm_fp8 as F
+    xq = torch.randn(T, H, device=dev).bfloat16()
+    x8, sfa = F.quantize_rows_fp8(xq)
+    if want("fp8_gemm"):
+        w8, sfb = F.quantize_weight_fp8((torch.randn(I, H, device=dev) * 0.02).bfloat16())
+        out8 = F.fp8_gemm(x8, sfa, w8, sfb)
 if want("decode_shrink"):  # LoRA shrink of o_proj in the headline decode step (222 tokens, 12 adapters r32)
     xs = torch.randn(222, H, device=dev).bfloat16()
     a_all = (torch.randn(12 * 32, H, device=dev) * 0.02).bfloat16()
     ids = torch.randint(1, 13, (222,), device=dev, dtype=torch.int32)
     s_out = torch.empty(222, 12 * 32, device=dev, dtype=torch.bfloat16)
     G.lora_shrink(xs, a_all, ids, 32, 12, out=s_out)
-if want("attn_prefill") or want("attn_decode"):
+if want("attn_prefill") or want("attn_decode") or want("attn_decode_fp8"):
     hq, hkv, d = 32, 8, 128
     def setup(q_lens, kv_lens):
         nblk = sum((l + 15)//16 for l in kv_lens) + 4
@@ -83,6 +90,13 @@ if want("attn_prefill") or want("attn_decode"):
         q_lens = [1] * 128; kv = [4200] * 128; kc, vc, bt, q, out, qs, kvl = setup(q_lens, kv)
         ws, wr = [torch.tensor(v, dtype=torch.int32, device=dev) for v in A.build_work(q_lens, 4, 16)]
         A.paged_attention(q, kc, vc, bt, qs, kvl, ws, wr, 16, hq, 0.088, out, 1)
+    if want("attn_decode_fp8"):  # the same decode step over the fp8 (e4m3) cache
+        q_lens = [1] * 128; kv = [4200] * 128; kc, vc, bt, q, out, qs, kvl = setup(q_lens, kv)
+        k8 = torch.randint(0, 126, kc.shape, dtype=torch.uint8, device=dev)  # finite e4m3 bytes
+        v8 = torch.randint(0, 126, (kc.shape[0], hkv, d, 16), dtype=torch.uint8, device=dev)
+        ks = torch.full(kc.shape[:3], 0.01, device=dev); vs = torch.full_like(ks, 0.01)
+        ws, wr = [torch.tensor(v, dtype=torch.int32, device=dev) for v in A.build_work(q_lens, 4, 16)]
+        A.paged_attention(q, k8, v8, bt, qs, kvl, ws, wr, 16, hq, 0.088, out, 1, k_scale=ks, v_scale=vs)
 if want("attn_prefill64"):  # tcgen05 prefill attention, head_dim 64 (3B shape: 32 q / 8 kv heads)
     hq, hkv, d = 32, 8, 64
     q_lens = [2048, 2048]

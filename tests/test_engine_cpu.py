@@ -364,3 +364,53 @@ def test_executor_error_word_check():
     e = DeviceError(ERR_BAD_SHAPE, site_name(3), 99)
     assert "bad-shape" in str(e) and "KV slot = 99" in str(e) and e.word == ERR_BAD_SHAPE
     assert describe_error(0x3).count("timeout") == 2
+
+
+@pytest.mark.parametrize("budget,blocks", [(64, 14), (1024, 64)])
+def test_async_steps_match_sync(tiny_dir, budget, blocks):
+    """Pipelined steps (step i+1 launched before step i's ids are read, decode rows fed on the
+    device) give the same outputs as blocking steps: chunked prefill, preemption under a small
+    KV cache, per-request max_tokens, stop tokens taken from the sync run, and seeded
+    temperature sampling."""
+    prompts = _prompts(tiny_dir, 6, seed=4, lo=30, hi=70)
+
+    def run(async_on, params):
+        ecfg = EngineConfig(max_num_seqs=4, max_num_batched_tokens=budget, num_kv_blocks=blocks, max_model_len=256,
+                            async_scheduling=async_on)
+        llm = LLM(tiny_dir, device="cpu", engine_config=ecfg)
+        assert llm.engine.async_steps == async_on
+        outs = llm.generate(prompts, params)
+        return [o.output_ids for o in outs], [o.finish_reason for o in outs], llm.engine
+
+    greedy = [SamplingParams(max_tokens=3 + i) for i in range(len(prompts))]
+    ref_ids, _, _ = run(False, greedy)
+    # stop on a token the sync run produced mid-sequence
+    stop = [SamplingParams(max_tokens=8, stop_token_ids=(ids[2],)) for ids in ref_ids]
+    sampled = [SamplingParams(max_tokens=6, temperature=0.8, seed=11 + i) for i in range(len(prompts))]
+    for params in (greedy, stop, sampled):
+        a_ids, a_reason, eng = run(True, params)
+        s_ids, s_reason, _ = run(False, params)
+        assert a_ids == s_ids and a_reason == s_reason
+        assert not eng.has_unfinished() and eng._inflight is None
+        assert all(t >= 0 for ids in a_ids for t in ids)
+
+
+def test_async_abort_while_running(tiny_dir):
+    """A request aborted while a step that carries it is in flight gets no token from that
+    step; the others match blocking steps."""
+    prompts = _prompts(tiny_dir, 3, seed=5)
+    ecfg = EngineConfig(max_num_seqs=3, max_num_batched_tokens=1024, num_kv_blocks=64, max_model_len=256)
+    llm = LLM(tiny_dir, device="cpu", engine_config=ecfg)
+    eng = llm.engine
+    reqs = [eng.add_request(p, SamplingParams(max_tokens=6)) for p in prompts]
+    eng.step()
+    eng.step()
+    assert eng._inflight is not None and any(c.req is reqs[0] for c in eng._inflight.out.chunks)
+    n = len(reqs[0].output_ids)
+    assert eng.abort_request(reqs[0].request_id)
+    while eng.has_unfinished():
+        eng.step()
+    ref = _ref_generate(tiny_dir, prompts[1:], 6)
+    assert [r.output_ids for r in reqs[1:]] == ref
+    assert reqs[0].finish_reason == "abort" and len(reqs[0].output_ids) == n
+    assert all(t >= 0 for t in reqs[0].output_ids)

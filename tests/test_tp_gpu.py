@@ -40,11 +40,12 @@ def test_tp2_matches_tp1():
     env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29531", "-m",
-           "granite_switch_b200.parallel.tp_check"]
+           "granite_switch_b200.parallel.tp_check", "--engine"]
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)
     print(r.stdout[-4000:], r.stderr[-4000:])
     assert r.returncode == 0, r.stderr[-2000:]
     assert '"mode": "nccl"' in r.stdout
+    assert '"mode": "engine_async_vs_sync"' in r.stdout
 
 
 @pytest.mark.multigpu
