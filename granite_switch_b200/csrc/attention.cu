@@ -79,11 +79,14 @@ __device__ __forceinline__ uint32_t sw(int r, int ch) {
 // fp8 pages (kv_fp8.cu): K tiles of D-byte rows keep the TMA swizzle of that row
 // width (128 B: 16-byte chunk ^ row % 8; 64 B: chunk ^ (row / 2) % 4), so a warp's 32
 // fragment words hit 32 banks.
-// Two e4m3 values (low 16 bits) -> f16x2: one conversion, exact (every e4m3 value is an
-// f16 value).
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t pair) {
-  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(pair & 0xffffu), __NV_E4M3);
-  return (uint32_t)h.x | ((uint32_t)h.y << 16);
+// e4m3 -> f16 is exact (every e4m3 value is an f16 value).
+// Four e4m3 values (one 32-bit word) -> two f16x2: the word's 16-bit halves are split by
+// a register move, so the pair costs two conversions and nothing else.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
 }
 // bf16x2 * s -> f16x2, saturating at the f16 range.
 __device__ __forceinline__ uint32_t bf16x2_to_f16x2_scaled(uint32_t v, float s) {
@@ -117,6 +120,7 @@ struct AttnCfg {
   // must be aligned to the swizzle pattern (the fp8 scale arrays would break that)
   static constexpr int STAGE_BYTES = (2 * TILE_BYTES + SC_BYTES + 1023) / 1024 * 1024;
   static_assert(STAGE_BYTES % 1024 == 0 && TILE_BYTES % 1024 == 0, "stage alignment");
+  static_assert(TX_BYTES % (KT / 16) == 0, "every page's producer expects the same bytes");
   static constexpr int Q_BYTES = ROWS * D * 2;
   // page ids of the CTA's key range, staged in shared memory once (past this
   // many pages the loop falls back to reading the block table in global memory)
@@ -186,7 +190,7 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
   const int n_tiles = (k_end > k_begin) ? (k_end - k_begin + KT - 1) / KT : 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], PAGES);  // one arrival per page's producer
     fence_barrier_init();
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
@@ -214,16 +218,17 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
   cp_commit();
   __syncthreads();  // barrier init visible
 
-  // producer: one thread issues every box of a key tile
+  // producers: lane 0 of warp p issues page p of every key tile (one arrival with that
+  // page's bytes each), so no warp carries the whole tile's copy issue
+  static_assert(PAGES <= C::WARPS, "one producer warp per page");
   const int first_page = checked_index(bt[0], num_blocks, err, kSitePage);
-  auto issue = [&](int it) {
+  auto issue = [&](int it, int p) {
     const int s = it % STAGES;
     uint8_t* dK = sKV + s * C::STAGE_BYTES;
     uint8_t* dV = dK + C::TILE_BYTES;
     const int tile_start = k_begin + it * KT;
-    mbar_arrive_expect_tx(&full[s], C::TX_BYTES);
-#pragma unroll
-    for (int p = 0; p < PAGES; ++p) {
+    mbar_arrive_expect_tx(&full[s], C::TX_BYTES / PAGES);
+    {
       const int j = tile_start + p * PAGE;
       // pages past the key range still load a valid page (masked later) so no
       // uninitialised smem (possibly NaN) ever meets a zero probability
@@ -248,9 +253,10 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
       }
     }
   };
-  int issued = 0;  // tiles whose loads were issued (thread 0 only)
-  if (threadIdx.x == 0) {
-    for (int it = 0; it < min(n_tiles, STAGES - 1); ++it) issue(it);
+  const bool producer = lane == 0 && warp < PAGES;
+  int issued = 0;  // tiles whose loads were issued (the same on every producer)
+  if (producer) {
+    for (int it = 0; it < min(n_tiles, STAGES - 1); ++it) issue(it, warp);
     issued = min(n_tiles, STAGES - 1);
   }
 
@@ -283,8 +289,8 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
   int consumed = 0;
   for (int it = 0; it < n_tiles; ++it) {
     const int s = it % STAGES;
-    if (threadIdx.x == 0 && it + STAGES - 1 < n_tiles) {
-      issue(it + STAGES - 1);
+    if (producer && it + STAGES - 1 < n_tiles) {
+      issue(it + STAGES - 1, warp);
       issued = it + STAGES;
     }
     const bool landed = mbar_wait(&full[s], (it / STAGES) & 1, err, kErrAttnWait);
@@ -313,8 +319,9 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
             // of the lane's base are g's, so the swizzled offset is one XOR with kk
             const int key = wn * KPW + (2 * nb2 + h) * 8 + g;
             const int off = (key * D + 4 * t4 + ((D == 128 ? g : (g >> 1) & 3) << 4)) ^ (kk << 4);
-            const uint32_t wd = *reinterpret_cast<const uint32_t*>(kst + off);
-            mma16816_f16(sacc[2 * nb2 + h], qf[kk], e4m3x2_to_f16x2(wd), e4m3x2_to_f16x2(wd >> 16));
+            uint32_t b0, b1;
+            e4m3x4_to_f16x2x2(*reinterpret_cast<const uint32_t*>(kst + off), b0, b1);
+            mma16816_f16(sacc[2 * nb2 + h], qf[kk], b0, b1);
           }
         } else {
           const int key = wn * KPW + nb2 * 16 + (lane & 7) + ((lane >> 4) << 3);
@@ -327,6 +334,9 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
       }
     }
     float mx[2] = {-INFINITY, -INFINITY};
+    // a tile inside both the key range and every row's causal limit needs no mask
+    // (CTA-uniform: the first row of the CTA has the smallest position)
+    const bool edge = tile_start + KT > min(k_end, ctx + row0 / G + 1);
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll
@@ -335,7 +345,7 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
         const int j = tile_start + kt;
         const int pos = (e < 2) ? posA : posB;
         float v = sacc[nb][e] * (F8 ? kss[(kt >> 4) * (C::SC_SLOT / 4) + (kt & 15)] : scale_log2);
-        if (j >= k_end || j > pos) v = -INFINITY;
+        if (edge && (j >= k_end || j > pos)) v = -INFINITY;
         sacc[nb][e] = v;
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
@@ -407,8 +417,9 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
           const uint8_t* pg = vst + ((wn * KPW + kk * 16) / PAGE) * (PAGE * D) + g * 16 + 4 * t4;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const uint32_t wd = *reinterpret_cast<const uint32_t*>(pg + (db * 16 + h * 8) * 16);
-            mma16816_f16(o[2 * db + h], pa, e4m3x2_to_f16x2(wd), e4m3x2_to_f16x2(wd >> 16));
+            uint32_t b0, b1;
+            e4m3x4_to_f16x2x2(*reinterpret_cast<const uint32_t*>(pg + (db * 16 + h * 8) * 16), b0, b1);
+            mma16816_f16(o[2 * db + h], pa, b0, b1);
           }
         } else {
           const int key = wn * KPW + kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
