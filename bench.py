@@ -73,6 +73,10 @@ def parse_args():
                    help="cache_affinity: engine steps after which a waiting cold request goes first (negative: none)")
     p.add_argument("--kv-cache-dtype", choices=["bfloat16", "fp8_e4m3"], default="bfloat16",
                    help="KV cache storage; the headline metric is defined on the bf16 cache")
+    p.add_argument("--pp", type=int, default=1,
+                   help="pipeline stages (the GPUs are split into pp stages of gpus / pp tensor-parallel ranks)")
+    p.add_argument("--no-pp-microbatches", dest="pp_microbatches", action="store_false",
+                   help="pipeline parallelism: run each step whole instead of as two micro-batches")
     p.add_argument("--no-async", dest="async_scheduling", action="store_false",
                    help="blocking engine steps (read each step's ids before scheduling the next)")
     p.add_argument("--seed", type=int, default=0)
@@ -134,16 +138,26 @@ def run_native(args):
         # host-side agreement (arrivals) over gloo: a broadcast on the GPU stream plus a host
         # read would wait for the step just launched and serialise the pipelined steps
         cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
+    if world % args.pp:
+        raise SystemExit(f"--pp {args.pp} does not divide {world} GPUs")
+    tp = world // args.pp
+    tp_rank, tp_group, pipe = rank, group, None
+    if args.pp > 1:
+        from granite_switch_b200.parallel.pipeline import init_parallel_groups
+
+        tp_rank, tp_group, pipe = init_parallel_groups(tp, args.pp)
     _native.native()
     config, base = model_config(args)
     ecfg = EngineConfig(max_num_seqs=args.max_num_seqs, max_num_batched_tokens=args.max_num_batched_tokens,
-                        max_model_len=args.context_len + args.calls * 200 + 256, tensor_parallel_size=world,
+                        max_model_len=args.context_len + args.calls * 200 + 256, tensor_parallel_size=tp,
+                        pipeline_parallel_size=args.pp, pipeline_microbatches=args.pp_microbatches,
                         num_kv_blocks=args.kv_blocks, fused_tp_comm=args.fused_comm, seed=args.seed,
                         scheduling_policy=args.scheduling_policy,
                         max_wait_steps=args.max_wait_steps if args.max_wait_steps >= 0 else None,
                         kv_cache_dtype=args.kv_cache_dtype, async_scheduling=args.async_scheduling)
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
-              random_init=dict(lora_modules=("qkv", "o"), rank=32, seed=args.seed), tp_rank=rank, tp_group=group)
+              random_init=dict(lora_modules=("qkv", "o"), rank=32, seed=args.seed), tp_rank=tp_rank, tp_group=tp_group,
+              pipeline=pipe)
     eng = llm.engine
     wl = WorkloadConfig(num_conversations=args.conversations, rate=args.rate, context_len=args.context_len,
                         calls=args.calls, vocab=base["vocab_size"], num_adapters=12, seed=args.seed, mode=args.mode)
@@ -267,7 +281,9 @@ def run_native(args):
             "prefix_hit_rate_overall": round(eng.prefix_cache_hit_rate(), 4),
             "config": {"model": f"{args.preset}-shape" + (f"-L{args.layers}" if args.layers else ""),
                        "global_batch": args.max_num_seqs, "seq_len": args.context_len,
-                       "parallelism": f"tp{world}", "adapters": "12 aLoRA r32 q/k/v/o",
+                       "parallelism": f"tp{tp}" + (f"pp{args.pp}" + ("" if args.pp_microbatches else " (whole steps)")
+                                                    if args.pp > 1 else ""),
+                       "adapters": "12 aLoRA r32 q/k/v/o",
                        "workload": f"poisson {args.rate}/s, {args.calls} chained calls, inv 16-64, gen 32-128",
                        "mode": args.mode, "max_num_batched_tokens": args.max_num_batched_tokens,
                        "scheduling_policy": args.scheduling_policy, "max_wait_steps": ecfg.max_wait_steps,

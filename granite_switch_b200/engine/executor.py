@@ -137,7 +137,8 @@ class NativeExecutor:
     (routing, every layer, LM head) is one graph launch. Other steps run eagerly.
     """
 
-    def __init__(self, model, max_model_len: int, tp_group=None, tp_size: int = 1, use_cuda_graphs: bool = False):
+    def __init__(self, model, max_model_len: int, tp_group=None, tp_size: int = 1, use_cuda_graphs: bool = False,
+                 pp_microbatches: bool = True):
         self.model = model
         self.device = model.device
         self.tp_group, self.tp_size = tp_group, tp_size
@@ -175,6 +176,8 @@ class NativeExecutor:
         self.d2h_bytes = 0
         self.gather_buf = None
         self.use_cuda_graphs = bool(use_cuda_graphs) and tp_size == 1 and model.pipeline is None
+        # pipeline parallelism: a step of two or more sequences runs as two micro-batches
+        self.pp_microbatches = bool(pp_microbatches) and model.pipeline is not None
         self.routing_trace = None  # utils.tracing.RoutingTrace: per-step routing records
         self.nvtx = False          # NVTX range per step (regions: model.prof = NvtxRanges())
         self.graphs: dict[int, _DecodeGraph] = {}
@@ -360,6 +363,9 @@ class NativeExecutor:
         hb = HostBatch(out)
         with nvtx_range(f"step {len(hb.ids)} tokens", self.nvtx):
             p = self._graph_bucket(out)
+            parts = self._pp_parts(out) if p is None else None
+            if parts is not None:
+                return hb, self._forward_parts(parts)
             if p is not None:
                 t0 = time.perf_counter()
                 logits = self._run_graph(hb, p)
@@ -378,6 +384,39 @@ class NativeExecutor:
             if logits is None:
                 return hb, None
             return hb, self._gather_logits(logits)
+
+    def _pp_parts(self, out: SchedulerOutput):
+        """Two micro-batches of about half the step's tokens each (whole sequences), so that
+        stage s + 1 runs the first while stage s runs the second; None when the step is not
+        split (no pipeline, one sequence, probe steps, routing trace on)."""
+        m = self.model
+        if not self.pp_microbatches or m.probe_w is not None or self.routing_trace is not None or len(out.chunks) < 2:
+            return None
+        total, acc, k = out.num_tokens, 0, 0
+        for k, c in enumerate(out.chunks):
+            acc += c.num_tokens
+            if 2 * acc >= total:
+                break
+        k = min(max(k + 1, 1), len(out.chunks) - 1)
+        return [SchedulerOutput(chunks=out.chunks[:k]), SchedulerOutput(chunks=out.chunks[k:])]
+
+    def _forward_parts(self, parts) -> torch.Tensor | None:
+        """Run the micro-batches in order on this stage's stream. Each hands its hidden state
+        to the next stage as soon as its layers finish, so the stages overlap; the last stage
+        keeps each part's logits (the next part's forward rewrites the logits buffer) and
+        returns them in the step's row order."""
+        outs = []
+        for part in parts:
+            hbp = HostBatch(part)
+            t0 = time.perf_counter()
+            batch = self._stage(hbp)
+            t1 = time.perf_counter()
+            lg = self.model.forward(batch)
+            self.host_stage_s += t1 - t0
+            self.host_enqueue_s += time.perf_counter() - t1
+            if lg is not None and len(hbp.rows):
+                outs.append(self._gather_logits(lg).clone())
+        return torch.cat(outs) if outs else None
 
     def _trace(self, hb: HostBatch) -> None:
         """Record this step's routing from the model's static buffers (valid after a graph replay too)."""

@@ -53,6 +53,8 @@ class EngineConfig:
     # launch step i+1 before reading step i's sampled ids (they reach step i+1's inputs on
     # the device), so scheduling and bookkeeping overlap the GPU
     async_scheduling: bool = True
+    # pipeline parallelism: run each step as two micro-batches so consecutive stages overlap
+    pipeline_microbatches: bool = True
 
 
 @dataclass
@@ -430,7 +432,8 @@ class LLM:
             nm.num_kv_blocks = nb
             nm._alloc_buffers()
             self.model = nm
-            executor = NativeExecutor(nm, ecfg.max_model_len, tp_group, tp, ecfg.use_cuda_graphs)
+            executor = NativeExecutor(nm, ecfg.max_model_len, tp_group, tp, ecfg.use_cuda_graphs,
+                                      ecfg.pipeline_microbatches)
             if ecfg.fused_tp_comm and tp > 1 and pipeline is None:
                 from ..parallel.fused import attach_fused_comm
 

@@ -148,6 +148,10 @@ def main(argv=None):
     ap.add_argument("--tensor-parallel-size", type=int, default=1)
     ap.add_argument("--pipeline-parallel-size", type=int, default=1)
     ap.add_argument("--no-fused-tp-comm", action="store_true", help="reduce with NCCL only")
+    ap.add_argument("--kv-cache-dtype", choices=["auto", "bfloat16", "fp8", "fp8_e4m3"], default="auto",
+                    help="KV cache storage: bf16 (auto) or e4m3 with a per-(token, KV head) scale")
+    ap.add_argument("--no-async-scheduling", action="store_true",
+                    help="read each step's sampled ids before scheduling the next")
     ap.add_argument("--scheduling-policy", choices=["cache_affinity", "fcfs"], default="cache_affinity",
                     help="admission order: requests whose context is cached first, or arrival order")
     ap.add_argument("--max-wait-steps", type=int, default=DEFAULT_MAX_WAIT_STEPS,
@@ -164,7 +168,9 @@ def main(argv=None):
                         enable_prefix_caching=not args.no_prefix_caching, tensor_parallel_size=tp,
                         pipeline_parallel_size=pp, fused_tp_comm=not args.no_fused_tp_comm,
                         scheduling_policy=args.scheduling_policy,
-                        max_wait_steps=args.max_wait_steps if args.max_wait_steps >= 0 else None)
+                        max_wait_steps=args.max_wait_steps if args.max_wait_steps >= 0 else None,
+                        kv_cache_dtype="fp8_e4m3" if args.kv_cache_dtype.startswith("fp8") else "bfloat16",
+                        async_scheduling=not args.no_async_scheduling)
     sync = None
     if tp * pp > 1:
         # one process per GPU (torchrun); rank 0 serves HTTP and drives the others in lock step

@@ -4,7 +4,10 @@
 line per case: tcgen05 prefill attention on a fresh causal 4k prompt and on 8
 chunks of 512 new tokens over 3.5k cached tokens (TFLOP/s, causal FLOPs
 counted once), and decode attention for 128 requests x 4.2k cached tokens
-(GB/s of K/V read). 32 query / 8 KV heads, head_dim 128 (Granite-8B shape).
+(GB/s of K/V read): over the bf16 cache with two or three ring stages, and over the
+bf16 and fp8 caches with 1-3 key splits, L2 flushed (256 MB write) before each
+launch (``decode_split``). 32 query / 8 KV heads, head_dim 128 (Granite-8B shape).
+``--decode-only`` skips the prefill cases.
 """
 from __future__ import annotations
 
@@ -51,15 +54,35 @@ def _time(fn, iters: int) -> float:
     return a.elapsed_time(b) / iters
 
 
+def _time_flushed(fn, iters: int, flush: torch.Tensor) -> float:
+    """Median event-timed launch with the L2 flushed before each."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    ts.sort()
+    return ts[len(ts) // 2]
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--decode-only", action="store_true")
     args = p.parse_args()
     _native.native()
     hq, hkv, d = 32, 8, 128
     i32 = dict(dtype=torch.int32, device="cuda")
-    for name, q_lens, kv_lens in (("prefill_causal_4k", [4096], [4096]),
-                                  ("prefill_8x512_over_3584", [512] * 8, [4096] * 8)):
+    prefill_cases = () if args.decode_only else (("prefill_causal_4k", [4096], [4096]),
+                                                 ("prefill_8x512_over_3584", [512] * 8, [4096] * 8))
+    for name, q_lens, kv_lens in prefill_cases:
         kc, vc, bt, q, out, qs, kvl = _setup(q_lens, kv_lens)
         # causal FLOPs: each query attends to (ctx + its index + 1) keys; 4 flop per (q, k, d)
         pairs = sum(ql * (kl - ql) + ql * (ql + 1) // 2 for ql, kl in zip(q_lens, kv_lens))
@@ -85,6 +108,24 @@ def main():
         _native.native().attn_decode_stages(old)
         print(json.dumps({"case": "decode_128x4200", "stages": stages, "ms": round(ms, 4),
                           "gbs": round(kv_bytes / ms / 1e6, 1)}), flush=True)
+    # bf16 and fp8 caches, key splits 1-3, L2 flushed before each launch
+    dev = "cuda"
+    nblk = kc.shape[0]
+    k8 = torch.randint(0, 126, kc.shape, dtype=torch.uint8, device=dev)  # finite e4m3 bytes
+    v8 = torch.randint(0, 126, (nblk, hkv, d, 16), dtype=torch.uint8, device=dev)
+    ks = torch.full(kc.shape[:3], 0.01, device=dev)
+    vs = torch.full_like(ks, 0.01)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    b = len(q_lens)
+    for ns in (1, 2, 3):
+        wso = torch.empty(ns, b, hq, d, device=dev)
+        wsl = torch.empty(ns, b, hq, device=dev)
+        for cache, kk, vv, sk, sv, per in (("bf16", kc, vc, None, None, 2), ("fp8", k8, v8, ks, vs, 1)):
+            ms = _time_flushed(lambda: A.paged_attention(q, kk, vv, bt, qs, kvl, ws, wr, 16, hq, 0.088, out, ns,
+                                                         wso, wsl, k_scale=sk, v_scale=sv), args.iters, flush)
+            nbytes = 2 * sum(kv_lens) * hkv * d * per
+            print(json.dumps({"case": "decode_split", "cache": cache, "nsplit": ns, "ms": round(ms, 4),
+                              "kv_tbs": round(nbytes / ms / 1e9, 2)}), flush=True)
     _native.check_errors(torch.device("cuda", 0))
 
 

@@ -414,3 +414,25 @@ def test_async_abort_while_running(tiny_dir):
     assert [r.output_ids for r in reqs[1:]] == ref
     assert reqs[0].finish_reason == "abort" and len(reqs[0].output_ids) == n
     assert all(t >= 0 for t in reqs[0].output_ids)
+
+
+def test_pp_microbatch_split():
+    """A pipelined step splits into two micro-batches of whole sequences holding about half
+    the tokens each; no split with one sequence, probes or a routing trace."""
+    import types
+
+    from granite_switch_b200.engine.executor import NativeExecutor
+    from granite_switch_b200.engine.request import Request
+    from granite_switch_b200.engine.scheduler import ScheduledChunk, SchedulerOutput
+
+    ex = types.SimpleNamespace(pp_microbatches=True, routing_trace=None, model=types.SimpleNamespace(probe_w=None))
+
+    def out(sizes):
+        return SchedulerOutput(chunks=[ScheduledChunk(Request(list(range(n + 1))), 0, n) for n in sizes])
+
+    for sizes, k in (([1, 1], 1), ([100, 1, 1, 1], 1), ([1, 1, 1, 100], 3), ([10, 10, 10, 10], 2), ([5, 50, 5], 2)):
+        parts = NativeExecutor._pp_parts(ex, out(sizes))
+        assert [len(p.chunks) for p in parts] == [k, len(sizes) - k], (sizes, [len(p.chunks) for p in parts])
+    assert NativeExecutor._pp_parts(ex, out([64])) is None
+    ex.model.probe_w = object()
+    assert NativeExecutor._pp_parts(ex, out([8, 8])) is None
