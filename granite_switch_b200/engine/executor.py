@@ -12,6 +12,7 @@ prefix caching and chunked prefill are checked against plain ``generate``).
 from __future__ import annotations
 
 import math
+import types
 import time
 
 import numpy as np
@@ -145,33 +146,29 @@ class NativeExecutor:
         self.max_blocks = (max_model_len + BLOCK_SIZE - 1) // BLOCK_SIZE
         t, s = model.max_tokens, model.max_seqs
         pin = dict(pin_memory=True)
-        self.h_i64 = torch.empty(3 * t, dtype=torch.long, **pin)          # ids | positions | slots
-        self.h_i32 = torch.empty(3 * s + 1, dtype=torch.int32, **pin)     # starts | carry | kv_lens
-        self.h_bt = torch.zeros(s, self.max_blocks, dtype=torch.int32, **pin)
-        self.h_rows = torch.empty(s, dtype=torch.long, **pin)
+        # pinned staging, two sets: a pipelined step stages its second micro-batch while the
+        # first one's copies may still wait behind the previous step on the stream
+        self._staging = [self._make_staging(t, s) for _ in range(2 if model.pipeline is not None else 1)]
         # sampled ids and the device error word (bits, bad-index site, index) of the last two
         # launched steps: a step's inputs may take the previous step's ids on the device
         self.h_out = torch.empty(2, s, dtype=torch.long, **pin)
         self.h_err = torch.zeros(2, 3, dtype=torch.int32, **pin)
         self.d_err = torch.zeros(3, dtype=torch.int32, device=model.device)
-        self.h_fb = torch.empty(2, s, dtype=torch.long, **pin)
+
         dev = self.device
         self.d_i64 = torch.empty(3 * t, dtype=torch.long, device=dev)
         self.d_i32 = torch.empty(3 * s + 1, dtype=torch.int32, device=dev)
         self.d_bt = torch.zeros(s, self.max_blocks, dtype=torch.int32, device=dev)
         self.d_rows = torch.empty(s, dtype=torch.long, device=dev)
         self.d_work = torch.empty(4, 4 * t + 4 * s, dtype=torch.int32, device=dev)
-        self.h_work = torch.empty(4, 4 * t + 4 * s, dtype=torch.int32, **pin)
+
         self.d_tokens = torch.empty(2, s, dtype=torch.long, device=dev)
         self.d_fb = torch.empty(2, s, dtype=torch.long, device=dev)
         self.buf = 0           # buffer of the next launched step
         self.prev_buf = None   # buffer of the last launched step (source of fed-back ids)
-        # numpy views of the pinned staging buffers (same memory)
-        self.np_i64, self.np_i32 = self.h_i64.numpy(), self.h_i32.numpy()
-        self.np_bt, self.np_rows, self.np_work = self.h_bt.numpy(), self.h_rows.numpy(), self.h_work.numpy()
+        self._use_staging(0)
         self.copy_events = (torch.cuda.Event(), torch.cuda.Event())
-        self.h2d_event = torch.cuda.Event()
-        self.h2d_pending = False
+
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.gather_buf = None
@@ -187,6 +184,33 @@ class NativeExecutor:
         self.host_enqueue_s = 0.0
         self.host_wait_s = 0.0
 
+    def _make_staging(self, t: int, s: int):
+        pin = dict(pin_memory=True)
+        st = types.SimpleNamespace(
+            h_i64=torch.empty(3 * t, dtype=torch.long, **pin),          # ids | positions | slots
+            h_i32=torch.empty(3 * s + 1, dtype=torch.int32, **pin),     # starts | carry | kv_lens
+            h_bt=torch.zeros(s, self.max_blocks, dtype=torch.int32, **pin),
+            h_rows=torch.empty(s, dtype=torch.long, **pin),
+            h_fb=torch.empty(2, s, dtype=torch.long, **pin),
+            h_work=torch.empty(4, 4 * t + 4 * s, dtype=torch.int32, **pin),
+            h2d_event=torch.cuda.Event(), h2d_pending=False)
+        # numpy views of the pinned buffers (same memory)
+        st.np_i64, st.np_i32 = st.h_i64.numpy(), st.h_i32.numpy()
+        st.np_bt, st.np_rows, st.np_work = st.h_bt.numpy(), st.h_rows.numpy(), st.h_work.numpy()
+        return st
+
+    def _use_staging(self, slot: int) -> None:
+        """Point the staging attributes at pinned set ``slot`` (its copy event travels with it)."""
+        if getattr(self, "_slot", None) is not None:
+            cur = self._staging[self._slot]
+            cur.h2d_pending = self.h2d_pending
+        st = self._staging[slot]
+        self._slot = slot
+        for k in ("h_i64", "h_i32", "h_bt", "h_rows", "h_fb", "h_work", "np_i64", "np_i32", "np_bt", "np_rows",
+                  "np_work", "h2d_event"):
+            setattr(self, k, getattr(st, k))
+        self.h2d_pending = st.h2d_pending
+
     # ------------------------------------------------------------------ CUDA graphs
     def _graph_bucket(self, out: SchedulerOutput) -> int | None:
         if not self.use_cuda_graphs or not out.is_decode_only:
@@ -201,6 +225,8 @@ class NativeExecutor:
         """Stage a decode step padded to ``p`` rows at the fixed offsets the graphs read."""
         s = len(hb.ids)
         m = self.model
+        if self._slot != 0:
+            self._use_staging(0)
         if self.h2d_pending:
             self.h2d_event.synchronize()
         i64, i32 = self.np_i64, self.np_i32
@@ -284,8 +310,11 @@ class NativeExecutor:
         self.graph_replays += 1
         return g.logits[: len(hb.rows)]
 
-    def _stage(self, hb: HostBatch):
+    def _stage(self, hb: HostBatch, slot: int = 0):
         from ..models.native import AttnPlan, StepBatch
+
+        if slot != self._slot:
+            self._use_staging(slot)
 
         t, s = len(hb.ids), len(hb.starts) - 1
         m = self.model
@@ -385,12 +414,18 @@ class NativeExecutor:
                 return hb, None
             return hb, self._gather_logits(logits)
 
+    # smallest step split into micro-batches: below it the projections stream their weights
+    # (bandwidth-bound), and two micro-batches would read every weight twice per stage
+    PP_SPLIT_MIN_TOKENS = 1024
+
     def _pp_parts(self, out: SchedulerOutput):
         """Two micro-batches of about half the step's tokens each (whole sequences), so that
         stage s + 1 runs the first while stage s runs the second; None when the step is not
-        split (no pipeline, one sequence, probe steps, routing trace on)."""
+        split (no pipeline, one sequence, fewer than ``PP_SPLIT_MIN_TOKENS`` tokens, probe
+        steps, routing trace on)."""
         m = self.model
-        if not self.pp_microbatches or m.probe_w is not None or self.routing_trace is not None or len(out.chunks) < 2:
+        if (not self.pp_microbatches or m.probe_w is not None or self.routing_trace is not None
+                or len(out.chunks) < 2 or out.num_tokens < self.PP_SPLIT_MIN_TOKENS):
             return None
         total, acc, k = out.num_tokens, 0, 0
         for k, c in enumerate(out.chunks):
@@ -406,10 +441,10 @@ class NativeExecutor:
         keeps each part's logits (the next part's forward rewrites the logits buffer) and
         returns them in the step's row order."""
         outs = []
-        for part in parts:
+        for i, part in enumerate(parts):
             hbp = HostBatch(part)
             t0 = time.perf_counter()
-            batch = self._stage(hbp)
+            batch = self._stage(hbp, slot=i)
             t1 = time.perf_counter()
             lg = self.model.forward(batch)
             self.host_stage_s += t1 - t0

@@ -6,7 +6,8 @@ Run under torchrun, one process per GPU::
 
 World = tp * pp. Every rank builds the same seeded random model and keeps its
 stage's layers (and its TP shard); three engine steps (a prefill step and two
-decode steps, greedy) run through the native executor, the last stage's TP
+decode steps, greedy, each split into two micro-batches) run through the
+native executor, the last stage's TP
 rank 0 gathers the logits and compares them with the unsharded model run
 alone on its GPU. Prints one JSON line and exits non-zero on a mismatch.
 """
@@ -34,6 +35,7 @@ def _run(config, device, steps_out, tp_rank=0, tp=1, tp_group=None, pipeline=Non
                                         lora_modules=("qkv", "o"), rank=16, seed=7, tp_rank=tp_rank, tp_size=tp,
                                         tp_group=tp_group, max_seqs=16, pipeline=pipeline)
     ex = NativeExecutor(m, 1024, tp_group, tp)
+    ex.PP_SPLIT_MIN_TOKENS = 0  # the check's steps are small: split them all into micro-batches
     bm = BlockManager(256)
     router = HostRouter(config)
     sch = Scheduler(bm, 8, 512, True, route_fn=router)

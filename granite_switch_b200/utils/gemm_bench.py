@@ -310,7 +310,11 @@ def main():
     p.add_argument("--reference", action="store_true",
                    help="also time the reference's switched projection (cuBLAS + its Triton expand)")
     p.add_argument("--shapes", nargs="*", default=None, help="N x K pairs as NxK (default: the three 8B shapes)")
+    p.add_argument("--small-shrink-max-m", type=int, default=None,
+                   help="largest M whose LoRA shrink runs on CUDA cores (A/B of the crossover)")
     args = p.parse_args()
+    if args.small_shrink_max_m is not None:
+        G.SMALL_SHRINK_MAX_M = args.small_shrink_max_m
     dev = torch.device("cuda", 0)
     err_buffer(dev)
     if args.decode is not None:

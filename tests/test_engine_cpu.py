@@ -425,7 +425,8 @@ def test_pp_microbatch_split():
     from granite_switch_b200.engine.request import Request
     from granite_switch_b200.engine.scheduler import ScheduledChunk, SchedulerOutput
 
-    ex = types.SimpleNamespace(pp_microbatches=True, routing_trace=None, model=types.SimpleNamespace(probe_w=None))
+    ex = types.SimpleNamespace(pp_microbatches=True, routing_trace=None, model=types.SimpleNamespace(probe_w=None),
+                               PP_SPLIT_MIN_TOKENS=2)
 
     def out(sizes):
         return SchedulerOutput(chunks=[ScheduledChunk(Request(list(range(n + 1))), 0, n) for n in sizes])
@@ -434,5 +435,8 @@ def test_pp_microbatch_split():
         parts = NativeExecutor._pp_parts(ex, out(sizes))
         assert [len(p.chunks) for p in parts] == [k, len(sizes) - k], (sizes, [len(p.chunks) for p in parts])
     assert NativeExecutor._pp_parts(ex, out([64])) is None
+    ex.PP_SPLIT_MIN_TOKENS = 1024
+    assert NativeExecutor._pp_parts(ex, out([500, 500])) is None  # weight-bound: run whole
+    assert NativeExecutor._pp_parts(ex, out([600, 600])) is not None
     ex.model.probe_w = object()
     assert NativeExecutor._pp_parts(ex, out([8, 8])) is None
