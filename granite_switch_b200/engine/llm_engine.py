@@ -231,27 +231,33 @@ class LLMEngine:
         once more; that row's result is dropped. Returns the requests finished by the
         step whose ids were resolved."""
         inflight = self._inflight  # the launched step's handle, or None
+        self._inflight = None       # owned by this call from here on
         t0 = time.perf_counter()
         sampled = self._advance(inflight) if inflight is not None else None
-        out = self.scheduler.schedule()
-        self.stats.host_schedule_s += time.perf_counter() - t0
         handle = None
-        if out.chunks:
-            if self.health is not None:
-                self.health.check()
-            self._count_mix(out)
-            try:
+        out = None
+        try:
+            out = self.scheduler.schedule()
+            self.stats.host_schedule_s += time.perf_counter() - t0
+            if out.chunks:
+                if self.health is not None:
+                    self.health.check()
+                self._count_mix(out)
                 handle = self.executor.launch(out)
-            except DeviceError as e:
-                self._inflight = None
-                self._abort_step(out, e, extra=inflight.out if inflight is not None else None)
-                raise
+        except DeviceError as e:
+            self._abort_step(out, e, extra=inflight.out if inflight is not None else None)
+            raise
+        except BaseException:
+            # the running step was advanced above: resolve it now so no step is lost or
+            # advanced twice; the step that failed to launch is scheduled again next time
+            if inflight is not None:
+                self._resolve(sampled, self.executor.collect(inflight))
+            raise
         finished = []
         if inflight is not None:
             try:
                 toks = self.executor.collect(inflight)
             except DeviceError as e:
-                self._inflight = None
                 if handle is not None:
                     try:
                         self.executor.collect(handle)  # drain it; its ids are discarded
@@ -332,7 +338,7 @@ class LLMEngine:
         """
         now = time.perf_counter()
         self.stats.device_errors += 1
-        chunks = list(out.chunks) + (list(extra.chunks) if extra is not None else [])
+        chunks = (list(out.chunks) if out is not None else []) + (list(extra.chunks) if extra is not None else [])
         for c in chunks:
             r = c.req
             if r.status == RequestStatus.FINISHED:

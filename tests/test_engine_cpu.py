@@ -440,3 +440,32 @@ def test_pp_microbatch_split():
     assert NativeExecutor._pp_parts(ex, out([600, 600])) is not None
     ex.model.probe_w = object()
     assert NativeExecutor._pp_parts(ex, out([8, 8])) is None
+
+
+def test_async_launch_failure_loses_no_step(tiny_dir):
+    """A launch that raises (not a device error) leaves the engine consistent: the running
+    step's ids are still resolved, the step that failed to launch runs again on the next
+    call, and every output matches plain generate."""
+    prompts = _prompts(tiny_dir, 3, seed=6)
+    ecfg = EngineConfig(max_num_seqs=3, max_num_batched_tokens=1024, num_kv_blocks=64, max_model_len=256)
+    llm = LLM(tiny_dir, device="cpu", engine_config=ecfg)
+    eng = llm.engine
+    real = eng.executor.launch
+    calls = {"n": 0}
+
+    def flaky(out):
+        calls["n"] += 1
+        if calls["n"] == 3:
+            raise RuntimeError("launch failed")
+        return real(out)
+
+    eng.executor.launch = flaky
+    reqs = [eng.add_request(p, SamplingParams(max_tokens=6)) for p in prompts]
+    failures = 0
+    while eng.has_unfinished():
+        try:
+            eng.step()
+        except RuntimeError:
+            failures += 1
+    assert failures == 1
+    assert [r.output_ids for r in reqs] == _ref_generate(tiny_dir, prompts, 6)
