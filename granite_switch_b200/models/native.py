@@ -704,9 +704,12 @@ class NativeGraniteSwitch:
         tc = self.head_dim in (64, 128) and self.use_tc_attention and not self.kv_fp8
         pre_q, pre_kv = [q_lens[i] for i in pre], [kv_lens[i] for i in pre]
         # short chunks over long cached prefixes: split-KV layout (needs the split workspace)
-        pre_split = (A.split_prefill(pre_q, pre_kv, g, self.num_kv)
-                     if tc and pre and sum(q_lens) <= self.ws_tokens else 0)
-        pre_rows = 128 if pre_split else (A.tc_rows_for(pre_q, pre_kv) if tc and pre else 64)
+        pre_split = (A.split_prefill(pre_q, pre_kv, g, self.num_kv, rows=128 if tc else 64)
+                     if pre and sum(q_lens) <= self.ws_tokens else 0)
+        if tc:
+            pre_rows = 128 if pre_split else (A.tc_rows_for(pre_q, pre_kv) if pre else 64)
+        else:
+            pre_rows = 64
         for idx, rows in ((dec, 16), (pre, pre_rows)):
             if not idx:
                 continue

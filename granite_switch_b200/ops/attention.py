@@ -32,8 +32,9 @@ def tc_rows_for(q_lens: list[int], kv_lens: list[int]) -> int:
 
 
 def split_prefill(q_lens: list[int], kv_lens: list[int], group: int, num_kv_heads: int,
-                  min_kv: int = 1024) -> int:
-    """Key-range splits for a step's tcgen05 prefill tiles (128 rows), or 0 for none.
+                  min_kv: int = 1024, rows: int = 128) -> int:
+    """Key-range splits for a step's prefill tiles of ``rows`` rows (128: tcgen05; 64: the
+    mma.sync layout, which an fp8 cache uses), or 0 for none.
 
     Short chunks after long cached prefixes (the next call of a conversation:
     tens of new tokens over thousands of cached keys) give the tcgen05 kernel
@@ -45,7 +46,7 @@ def split_prefill(q_lens: list[int], kv_lens: list[int], group: int, num_kv_head
     """
     if not q_lens or max(kv_lens) < min_kv:
         return 0
-    n_ctas = sum(-(-q * group // 128) for q in q_lens) * num_kv_heads
+    n_ctas = sum(-(-q * group // rows) for q in q_lens) * num_kv_heads
     if n_ctas >= NUM_SMS:
         return 0
     ns = choose_splits(n_ctas, max(kv_lens))

@@ -89,6 +89,7 @@ def main():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--no-fused-comm", dest="fused", action="store_false")
     p.add_argument("--lora", nargs="*", default=["qkv", "o"], help="projections with adapters")
+    p.add_argument("--kv-cache-dtype", choices=["bfloat16", "fp8_e4m3"], default="bfloat16")
     args = p.parse_args()
 
     import torch.distributed as dist
@@ -121,7 +122,7 @@ def main():
     ecfg = EngineConfig(max_num_seqs=max(8, len(args.prefill) + args.decode), max_num_batched_tokens=tokens,
                         max_model_len=max([args.prefill_ctx + n for n in args.prefill] + [args.decode_ctx + 1]) + 16,
                         tensor_parallel_size=world,
-                        num_kv_blocks=need_blocks, fused_tp_comm=args.fused)
+                        num_kv_blocks=need_blocks, fused_tp_comm=args.fused, kv_cache_dtype=args.kv_cache_dtype)
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
               random_init=dict(lora_modules=tuple(args.lora), rank=32), tp_rank=rank, tp_group=group)
     eng = llm.engine

@@ -247,6 +247,7 @@ def test_short_chunks_over_long_prefix_split_kv():
     assert A.split_prefill([48, 48], [300, 500], 4, 8) == 0      # short contexts
     assert A.split_prefill([48, 48, 300], [4548, 4548, 300], 4, 8) == 2  # 112 CTAs
     assert A.split_prefill([300] * 3, [4548] * 3, 4, 8) == 0     # 240 CTAs
+    assert A.split_prefill([48, 48], [4548, 4548], 4, 8, rows=64) == 4  # 48 CTAs of 64 rows (fp8 cache)
     m = types.SimpleNamespace(num_q=32, num_kv=8, head_dim=128, use_tc_attention=True, ws_tokens=512, kv_fp8=False)
     q = [48, 48] + [1] * 126
     kv = [4548, 4548] + [4500] * 126
