@@ -49,6 +49,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &gsb_moe_combine, "MoE weighted sum of expert outputs (+ shared MLP, residual)");
   m.def("residual_axpy", &gsb_residual_axpy, "h <- h + y * scale");
   m.def("paged_attention", &gsb_paged_attention, "paged causal GQA attention (prefill + decode; bf16 or fp8 cache)");
+  m.def("lora_shrink_small", &gsb_lora_shrink_small,
+        "masked LoRA shrink for a few tokens on CUDA cores (each row's own adapter columns only)");
   m.def("quantize_fp8_rows", &gsb_quantize_fp8_rows,
         "bf16 rows -> e4m3 bytes with one power-of-two scale per (row, 128-K block), as scale atoms");
   m.def("fp8_gemm", &gsb_fp8_gemm, "block-scaled fp8 tcgen05 GEMM with the bf16 switched-LoRA expand fused");

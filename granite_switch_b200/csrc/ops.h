@@ -20,6 +20,8 @@ int64_t gsb_gemm_pair_min_m(int64_t m);
 int64_t gsb_gemm_decode_max_m(int64_t v);
 void gsb_gemm_decode_force_split(int64_t acc, int64_t ks);
 void gsb_gemm_decode_trace(const at::Tensor& buf);
+void gsb_lora_shrink_small(const at::Tensor& x, const at::Tensor& a_all, const at::Tensor& row_adapter,
+                           const at::Tensor& s, int64_t rank, int64_t num_adapters);
 void gsb_quantize_fp8_rows(const at::Tensor& x, const at::Tensor& x8, const at::Tensor& sfa, const at::Tensor& err);
 void gsb_fp8_gemm(const at::Tensor& x8, const at::Tensor& sfa, const at::Tensor& w8, const at::Tensor& sfb,
                   const at::Tensor& out, int64_t epi, double scale, const c10::optional<at::Tensor>& residual,

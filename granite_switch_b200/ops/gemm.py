@@ -89,6 +89,9 @@ def switched_gemm(
     return out
 
 
+SMALL_SHRINK_MAX_M = 96  # up to this many tokens the shrink runs on CUDA cores (lora_small.cu)
+
+
 def lora_shrink(x: torch.Tensor, a_all: torch.Tensor, row_adapter: torch.Tensor, rank: int,
                 num_adapters: int, out: torch.Tensor | None = None,
                 tile_mask: torch.Tensor | None = None) -> torch.Tensor:
@@ -96,10 +99,17 @@ def lora_shrink(x: torch.Tensor, a_all: torch.Tensor, row_adapter: torch.Tensor,
 
     With ``tile_mask`` (adapters present per 128-row tile) only the column
     blocks of present adapters are computed; the expand reads nothing else.
+    Up to ``SMALL_SHRINK_MAX_M`` tokens each row's own columns are computed on
+    CUDA cores instead (the tensor-core kernel's fixed cost dominates there).
     """
     n = a_all.shape[0]
     if n % 64:
         raise ValueError(f"a_all must have a multiple of 64 rows (pad with zeros), got {n}")
+    if x.shape[0] <= SMALL_SHRINK_MAX_M:
+        if out is None:
+            out = torch.empty(x.shape[0], n, dtype=torch.bfloat16, device=x.device)
+        native().lora_shrink_small(x, a_all, row_adapter, out, rank, num_adapters)
+        return out
     bn = pick_bn(x.shape[0], n, (128, 64), two_tile_bn=None)
     if bn > rank * num_adapters:
         bn = 64

@@ -525,3 +525,35 @@ def test_decode_gemm_lora_slices(m, k):
     from granite_switch_b200._native import check_errors
 
     check_errors(torch.device("cuda", 0))
+
+
+@pytest.mark.parametrize("m", [1, 5, 96])
+@pytest.mark.parametrize("rank,na,slices", [(32, 12, 3), (8, 3, 3), (16, 5, 1)])
+def test_small_shrink_matches_masked_gemm(m, rank, na, slices):
+    """The CUDA-core shrink for a few tokens writes what the tensor-core kernel's adapter-mask
+    epilogue writes: each row's own adapter columns in every slice (A padded with zero rows,
+    so a last partial slice exists when na * rank does not divide 64), zeros elsewhere and for
+    base rows."""
+    from granite_switch_b200._native import native
+    from granite_switch_b200.ops import gemm as G
+
+    torch.manual_seed(m + rank)
+    k = 1024
+    width = slices * na * rank
+    n = (width + 63) // 64 * 64
+    x = _rand(m, k)
+    a_all = torch.zeros(n, k, device="cuda", dtype=torch.bfloat16)
+    a_all[:width] = _rand(width, k, scale=0.05)
+    ra = torch.randint(0, na + 1, (m,), device="cuda", dtype=torch.int32)
+    s = torch.full((m, n), 7.0, device="cuda", dtype=torch.bfloat16)  # every column must be written
+    native().lora_shrink_small(x, a_all, ra, s, rank, na)
+    ref = G.switched_gemm_reference(x, a_all, epi=G.EPI_MASK_ADAPTER, row_adapter=ra, mask_rank=rank,
+                                    mask_num_adapters=na)
+    tc = G.switched_gemm(x, a_all, epi=G.EPI_MASK_ADAPTER, row_adapter=ra, mask_rank=rank, mask_num_adapters=na,
+                         bn=64)
+    torch.cuda.synchronize()
+    _close(s, ref)
+    _close(s, tc)
+    cols = torch.arange(n, device="cuda")
+    keep = ((cols // rank) % na + 1).unsqueeze(0) == ra.long().unsqueeze(1)
+    assert (s.float()[~keep] == 0).all()  # other adapters' and base rows' columns written as zeros
