@@ -7,7 +7,10 @@ counted once), and decode attention for 128 requests x 4.2k cached tokens
 (GB/s of K/V read): over the bf16 cache with two or three ring stages, and over the
 bf16 and fp8 caches with 1-3 key splits, L2 flushed (256 MB write) before each
 launch (``decode_split``). 32 query / 8 KV heads, head_dim 128 (Granite-8B shape).
-``--decode-only`` skips the prefill cases.
+``--decode-only`` skips the prefill cases. ``--library`` also times FlashInfer's
+Blackwell attention (the trtllm-gen paged decode and context kernels vLLM serves with on
+B200) on the same caches, shapes and flush rule, and reports its largest difference from
+this package's output.
 """
 from __future__ import annotations
 
@@ -76,6 +79,7 @@ def main():
     p = argparse.ArgumentParser(description=__doc__)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--decode-only", action="store_true")
+    p.add_argument("--library", action="store_true", help="also time FlashInfer's trtllm-gen kernels")
     args = p.parse_args()
     _native.native()
     hq, hkv, d = 32, 8, 128
@@ -97,6 +101,8 @@ def main():
                 _native.native().attn_packed(old)
                 print(json.dumps({"case": name, "rows": rows, "packed": packed, "ms": round(ms, 4),
                                   "tflops": round(flops / ms / 1e9, 1)}), flush=True)
+        if args.library:
+            _library_prefill(name, q, kc, vc, bt, q_lens, kv_lens, hq, d, out, flops, args.iters)
     q_lens, kv_lens = [1] * 128, [4200] * 128
     kc, vc, bt, q, out, qs, kvl = _setup(q_lens, kv_lens)
     ws, wr = A.build_work(q_lens, hq // hkv, 16)
@@ -126,7 +132,76 @@ def main():
             nbytes = 2 * sum(kv_lens) * hkv * d * per
             print(json.dumps({"case": "decode_split", "cache": cache, "nsplit": ns, "ms": round(ms, 4),
                               "kv_tbs": round(nbytes / ms / 1e9, 2)}), flush=True)
+    if args.library:
+        A.paged_attention(q, kc, vc, bt, qs, kvl, ws, wr, 16, hq, 0.088, out, 1)
+        _library_decode(q, kc, vc, bt, kv_lens, hq, d, out, 2 * sum(kv_lens) * hkv * d * 2, args.iters, flush)
     _native.check_errors(torch.device("cuda", 0))
+
+
+_WORKSPACE = None
+
+
+def _workspace():
+    global _WORKSPACE
+    if _WORKSPACE is None:
+        _WORKSPACE = torch.zeros(256 << 20, dtype=torch.uint8, device="cuda")
+    return _WORKSPACE
+
+
+def _library_decode(q, kc, vc, bt, kv_lens, hq, d, ours, kv_bytes, iters, flush):
+    """FlashInfer trtllm-gen paged decode over the same bf16 pages ([pages, Hkv, 16, D], its
+    HND layout), L2 flushed before each launch like ``decode_split``."""
+    try:
+        from flashinfer.decode import trtllm_batch_decode_with_kv_cache
+
+        b = len(kv_lens)
+        qq = q[:, :hq * d].reshape(b, hq, d).contiguous()
+        seq = torch.tensor(kv_lens, dtype=torch.int32, device="cuda")
+        out = torch.empty(b, hq, d, dtype=torch.bfloat16, device="cuda")
+
+        def run():
+            trtllm_batch_decode_with_kv_cache(qq, (kc, vc), _workspace(), bt, seq, max(kv_lens), bmm1_scale=0.088,
+                                              bmm2_scale=1.0, out=out, kv_layout="HND")
+
+        ms = _time_flushed(run, iters, flush)
+        diff = (out.reshape(b, hq * d).float() - ours[:b].float()).abs().max().item()
+        print(json.dumps({"case": "decode_split", "cache": "bf16", "impl": "flashinfer-trtllm-gen",
+                          "ms": round(ms, 4), "kv_tbs": round(kv_bytes / ms / 1e9, 2),
+                          "max_abs_diff_vs_native": round(diff, 4)}), flush=True)
+    except Exception as e:  # the library is optional: report, do not fail the sweep
+        print(json.dumps({"case": "decode_split", "impl": "flashinfer-trtllm-gen",
+                          "unavailable": f"{type(e).__name__}: {e}"[:300]}), flush=True)
+
+
+def _library_prefill(name, q, kc, vc, bt, q_lens, kv_lens, hq, d, ours, flops, iters):
+    """FlashInfer trtllm-gen paged causal context attention on the same pages and queries."""
+    try:
+        from flashinfer.prefill import trtllm_batch_context_with_kv_cache
+
+        t = sum(q_lens)
+        qq = q[:, :hq * d].reshape(t, hq, d).contiguous()
+        i32 = dict(dtype=torch.int32, device="cuda")
+        cq, ck = [0], [0]
+        for ql, kl in zip(q_lens, kv_lens):
+            cq.append(cq[-1] + ql)
+            ck.append(ck[-1] + kl)
+        seq = torch.tensor(kv_lens, **i32)
+        cq, ck = torch.tensor(cq, **i32), torch.tensor(ck, **i32)
+        out = torch.empty(t, hq, d, dtype=torch.bfloat16, device="cuda")
+
+        def run():
+            trtllm_batch_context_with_kv_cache(qq, (kc, vc), _workspace(), bt, seq, max(q_lens), max(kv_lens), 0.088,
+                                               1.0, len(q_lens), cq, ck, out=out, kv_layout="HND", causal=True)
+
+        ms = _time(run, iters)
+        # this package's output of the last timed configuration holds the same values
+        diff = (out.reshape(t, hq * d).float() - ours[:t].float()).abs().max().item()
+        print(json.dumps({"case": name, "impl": "flashinfer-trtllm-gen", "ms": round(ms, 4),
+                          "tflops": round(flops / ms / 1e9, 1), "max_abs_diff_vs_native": round(diff, 4)}),
+              flush=True)
+    except Exception as e:
+        print(json.dumps({"case": name, "impl": "flashinfer-trtllm-gen",
+                          "unavailable": f"{type(e).__name__}: {e}"[:300]}), flush=True)
 
 
 if __name__ == "__main__":
