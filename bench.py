@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Headline benchmark: multi-aLoRA serving throughput on the Granite-8B shape.
 
-Metric: output tok/s + p50 TTFT for the multi-adapter
+Metric (the headline benchmark): output tok/s + p50 TTFT for the multi-adapter
 Granite-8B-shape workload (40 layers, d_model 4096, 32 q / 8 kv heads,
 head_dim 128, FFN 12800, vocab 49152, random init; 12 aLoRA adapters of rank 32
 on q/k/v/o), with the KV prefix-hit rate. Conversations arrive by a Poisson

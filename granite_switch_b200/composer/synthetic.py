@@ -12,13 +12,13 @@ import torch
 from .compose import AdapterSpec, compose_checkpoint
 
 PRESETS = {
-    # CPU fp32 tiny model
+    # benchmark config 1: CPU fp32 tiny model
     "tiny": dict(vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
                  num_attention_heads=4, num_key_value_heads=2, head_dim=64, rope_theta=10000.0),
-    # Granite-3B-shape
+    # benchmark config 2: Granite-3B-shape
     "granite-3b": dict(vocab_size=49152, hidden_size=2048, intermediate_size=8192, num_hidden_layers=40,
                        num_attention_heads=32, num_key_value_heads=8, head_dim=64, rope_theta=10000.0),
-    # Granite-8B-shape
+    # benchmark config 3: Granite-8B-shape
     "granite-8b": dict(vocab_size=49152, hidden_size=4096, intermediate_size=12800, num_hidden_layers=40,
                        num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=10000.0),
     # unit-test shapes

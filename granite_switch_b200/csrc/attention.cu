@@ -158,6 +158,7 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
                       int64_t out_stride, float* __restrict__ ws_o, float* __restrict__ ws_lse,
                       int nsplit, int T, uint32_t* err) {
   using namespace attn;
+  griddep_launch();  // a GEMM launched as a dependent may start its set-up
   using C = AttnCfg<D, WARPS_M, KT, STAGES, F8>;
   constexpr int ROWS = C::ROWS, WARPS_N = C::WARPS_N, KPW = C::KPW, NB = KPW / 8;
   constexpr int DC = D / 8, OB = D / 8, PAGES = KT / PAGE;
@@ -544,6 +545,7 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(const float* __restrict
                                                          const int32_t* __restrict__ work_seq,
                                                          const int32_t* __restrict__ work_row0, int rows_per_tile,
                                                          __nv_bfloat16* __restrict__ out, int64_t out_stride) {
+  griddep_launch();  // a GEMM launched as a dependent may start its set-up
   const int w = blockIdx.x, kvh = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.z * 8 + warp;

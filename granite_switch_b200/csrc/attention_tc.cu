@@ -68,6 +68,7 @@ __global__ void __launch_bounds__(192, 2)
   using C = FaCfg<D, KT_>;
   constexpr int KT = C::KT, BM = C::BM, PAGE = C::PAGE;
   static_assert(KT == 64, "the P store below writes 32 TMEM columns (64 keys)");
+  griddep_launch();  // a GEMM launched as a dependent may start its set-up
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;
@@ -445,6 +446,7 @@ __global__ void __launch_bounds__(320, 1)
                        uint32_t* err) {
   using C = FaPPCfg<D>;
   constexpr int KT = C::KT, BM = C::BM, PAGE = C::PAGE, ST = C::STAGES;
+  griddep_launch();  // a GEMM launched as a dependent may start its set-up
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* sQ = smem;                               // [2][D/64][BM][64]

@@ -11,12 +11,18 @@
 namespace gsb {
 static std::atomic<int64_t> g_kernel_launches{0};
 void count_launch() { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+static std::atomic<bool> g_pdl{false};
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
 }  // namespace gsb
+
+static bool gsb_set_pdl(bool on) { return gsb::g_pdl.exchange(on); }
 
 static int64_t gsb_kernel_launches() { return gsb::g_kernel_launches.load(std::memory_order_relaxed); }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kernel_launches", &gsb_kernel_launches, "kernels launched by this extension since it was loaded");
+  m.def("set_pdl", &gsb_set_pdl,
+        "launch the GEMMs as programmatic dependents of the kernel before them (returns the old setting)");
   m.doc() = "granite_switch_b200 sm_100a kernels";
   m.def("switched_gemm", &gsb_switched_gemm, "tcgen05 GEMM with fused switched-LoRA expand");
   m.def("gemm_pair_min_m", &gsb_gemm_pair_min_m, "set the smallest M of the CTA-pair GEMM (returns the old value)");
@@ -25,7 +31,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_decode_force_split", &gsb_gemm_decode_force_split,
         "force the decode kernel's (accumulators, K parts) for A/B tests; (0, 0) restores the rule");
   m.def("gemm_decode_trace", &gsb_gemm_decode_trace,
-        "record per-CTA phase timestamps of later decode-GEMM launches into a uint64 [CTAs, 8] tensor");
+        "record per-CTA phase timestamps of later decode-GEMM launches into a uint64 [CTAs, 16] tensor");
   m.def("gemm_decode_max_m", &gsb_gemm_decode_max_m,
         "set the largest M of the operand-swapped decode GEMM (0: off; -1 reads; returns the old value)");
   m.def("rmsnorm", &gsb_rmsnorm, "RMSNorm (optionally gathering rows)");

@@ -37,6 +37,17 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may start while the kernel before it in the
+// stream still runs: griddep_wait() blocks the calling thread until that kernel
+// has completed and its writes are visible (a no-op for a kernel launched
+// without the attribute), so whatever comes before it may touch only constant
+// data (weights) and the CTA's own shared and tensor memory. griddep_launch()
+// lets such a dependent start once every CTA of this grid has issued it (or
+// exited); it changes nothing for dependents launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void raise_error(uint32_t* err, uint32_t bits) {
   if (err != nullptr) atomicOr(err, bits);
 }
@@ -440,6 +451,10 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int M, int N) {
 // many of the extension's kernels a timed region launched (CUDA-graph captures
 // count once, at capture).
 void count_launch();
+
+// Whether kernels that support it are launched as programmatic dependents of the
+// kernel before them (griddep_wait / griddep_launch); set_pdl() in bindings.cpp.
+bool pdl_enabled();
 
 // Merge of split-KV attention partials (attention.cu) for the rows of the given
 // work tiles: ws_o [nsplit][T][Hq][D] normalised fp32, ws_lse [nsplit][T][Hq] log2.

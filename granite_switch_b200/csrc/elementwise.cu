@@ -22,6 +22,7 @@ template <int VPT>
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                int64_t ldo, const int64_t* __restrict__ rows, int H, float eps) {
+  griddep_launch();  // a GEMM launched as this kernel's dependent may start its set-up
   const int r = blockIdx.x;
   const int64_t src = rows ? rows[r] : r;
   const uint4* xv = reinterpret_cast<const uint4*>(x + src * ldx);

@@ -25,6 +25,11 @@
 //   shrink itself) and the NVSwitch multicast reduction for tensor parallelism.
 //   Rounding follows the general kernel (gemm_tcgen05.cu) bit for bit.
 //
+// Launched as a programmatic dependent of the kernel before it (when enabled), a
+// CTA sets up its barriers and TMEM and puts its first stages' weight tiles in
+// flight while that kernel finishes, then waits for it (griddepcontrol.wait)
+// before it touches the step's activations.
+//
 // Warp roles (192 threads): warp 0 issues TMA loads into a ring of stages,
 // warp 1 owns TMEM and issues tcgen05.mma from one thread, warps 2..5 drain
 // TMEM; all six warps run the cluster reduction and the epilogue. Every wait
@@ -231,15 +236,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int part = ks > 1 ? (int)cluster_ctarank() : 0;
   const int tile = blockIdx.x / ks;
   const int n0 = tile * BW * ACC;  // first row of the tile in the (packed) weight
-  if (EPI == kEpiMaskAdapter && shrink_skipped(p, n0, BW * ACC)) return;  // the whole cluster skips alike
+  if (EPI == kEpiMaskAdapter) {
+    // the skip test reads the step's adapter masks, which an earlier kernel writes
+    griddep_wait();
+    if (shrink_skipped(p, n0, BW * ACC)) return;  // the whole cluster skips alike
+  }
 
-  // this CTA's blocks: a contiguous K range, then every ks-th LoRA block
+  // this CTA's blocks: a contiguous K range, then every ks-th LoRA block (their count
+  // depends on the step's adapters, read after the dependency wait below)
   const int kb_lo = part * p.kblocks / ks, kb_hi = (part + 1) * p.kblocks / ks;
   const int n_main = kb_hi - kb_lo;
-  const uint64_t amask = (EPI != kEpiMaskAdapter && p.lora) ? present_adapters(p) : 0ull;
-  const int n_lora_all = __popcll(amask) * p.rank_blocks;
-  const int n_lora = n_lora_all > part ? (n_lora_all - part + ks - 1) / ks : 0;
-  const int total = n_main + n_lora;
   const int w_bytes = ACC * BW * BK * 2;
   const int need_cols = ACC * p.Mp_pad;
   const int tcols = need_cols <= 32 ? 32 : (need_cols <= 64 ? 64 : (need_cols <= 128 ? 128 : (need_cols <= 256 ? 256 : 512)));
@@ -256,7 +262,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_w);
     tma_prefetch_desc(&tm_x);
-    if (n_lora) {
+    if (p.lora) {
       tma_prefetch_desc(&tm_lb);
       tma_prefetch_desc(&tm_s);
     }
@@ -270,12 +276,50 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   if (warp == 0) trace_mark(p, 1);
+  // The next kernel may start its own set-up now; it waits for this grid's end before
+  // it reads anything this grid writes.
+  griddep_launch();
+
+  // main block i's weight tiles into stage s (the stage's barrier expects them and
+  // the block's token tile)
+  auto load_w_main = [&](int i, int s) {
+    uint8_t* sa = smem + s * p.stage_bytes;
+    const int kx = (kb_lo + i) * BK;
+    mbar_arrive_expect_tx(&full_bar[s], w_bytes + p.Mp * BK * 2);
+#pragma unroll
+    for (int a = 0; a < ACC; ++a) {
+      if (EPI == kEpiSwiGLU) {
+        // out columns [64 (ACC tile + a), +64): their gate rows, then their up rows
+        const int o0 = (tile * ACC + a) * 64, it = o0 / p.swiglu_half, off = o0 % p.swiglu_half;
+        const int g0 = it * 2 * p.swiglu_half + off;
+        tma_load_2d(sa + a * BW * 128, &tm_w, &full_bar[s], kx, g0);
+        tma_load_2d(sa + a * BW * 128 + 64 * 128, &tm_w, &full_bar[s], kx, g0 + p.swiglu_half);
+      } else {
+        tma_load_2d(sa + a * BW * 128, &tm_w, &full_bar[s], kx, n0 + a * BW);
+      }
+    }
+  };
+  auto load_x_main = [&](int i, int s) {
+    tma_load_2d(smem + s * p.stage_bytes + w_bytes, &tm_x, &full_bar[s], (kb_lo + i) * BK, 0);
+  };
+  // Weights are constant: the producer puts the weight tiles of its first ring's worth
+  // of main blocks in flight before it waits for the previous kernel (launched as its
+  // programmatic dependent, this kernel may start while that one still runs). Every
+  // thread waits before it reads the step's activations or adapter masks.
+  const int prefetch = (warp == 0 && lane == 0) ? min(stages, n_main) : 0;
+  for (int i = 0; i < prefetch; ++i) load_w_main(i, i);  // fresh ring: no empty-slot wait
+  griddep_wait();
+  const uint64_t amask = (EPI != kEpiMaskAdapter && p.lora) ? present_adapters(p) : 0ull;
+  const int n_lora_all = __popcll(amask) * p.rank_blocks;
+  const int n_lora = n_lora_all > part ? (n_lora_all - part + ks - 1) / ks : 0;
+  const int total = n_main + n_lora;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      uint32_t issued = 0;
-      for (int i = 0; i < total; ++i) {
+      for (int i = 0; i < prefetch; ++i) load_x_main(i, i);
+      uint32_t issued = (uint32_t)prefetch;
+      for (int i = prefetch; i < total; ++i) {
         const int s = i % stages;
         const uint32_t ph = (i / stages) & 1;
         if (*abort_flag || !mbar_wait(&empty_bar[s], ph ^ 1, err, kErrGemmWait)) {
@@ -285,21 +329,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint8_t* sa = smem + s * p.stage_bytes;
         uint8_t* sb = sa + w_bytes;
         if (i < n_main) {
-          const int kx = (kb_lo + i) * BK;
-          mbar_arrive_expect_tx(&full_bar[s], w_bytes + p.Mp * BK * 2);
-#pragma unroll
-          for (int a = 0; a < ACC; ++a) {
-            if (EPI == kEpiSwiGLU) {
-              // out columns [64 (ACC tile + a), +64): their gate rows, then their up rows
-              const int o0 = (tile * ACC + a) * 64, it = o0 / p.swiglu_half, off = o0 % p.swiglu_half;
-              const int g0 = it * 2 * p.swiglu_half + off;
-              tma_load_2d(sa + a * BW * 128, &tm_w, &full_bar[s], kx, g0);
-              tma_load_2d(sa + a * BW * 128 + 64 * 128, &tm_w, &full_bar[s], kx, g0 + p.swiglu_half);
-            } else {
-              tma_load_2d(sa + a * BW * 128, &tm_w, &full_bar[s], kx, n0 + a * BW);
-            }
-          }
-          tma_load_2d(sb, &tm_x, &full_bar[s], kx, 0);
+          load_w_main(i, s);
+          load_x_main(i, s);
         } else {
           const int j = part + (i - n_main) * ks;  // global LoRA block index
           const int ai = j / p.rank_blocks, rb = j % p.rank_blocks;
@@ -493,13 +524,24 @@ static void launch_decode(const CUtensorMap& tw, const CUtensorMap& tx, const CU
   cfg.blockDim = dim3(dec::THREADS, 1, 1);
   cfg.dynamicSmemBytes = dec::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)p.ks;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[2];
+  unsigned n_attr = 0;
+  if (p.ks > 1) {
+    attr[n_attr].id = cudaLaunchAttributeClusterDimension;
+    attr[n_attr].val.clusterDim.x = (unsigned)p.ks;
+    attr[n_attr].val.clusterDim.y = 1;
+    attr[n_attr].val.clusterDim.z = 1;
+    ++n_attr;
+  }
+  // a programmatic dependent of the previous kernel (not while tracing: the caller
+  // zeroes the trace buffer with a kernel that an early start would race)
+  if (pdl_enabled() && p.trace == nullptr) {
+    attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
+    ++n_attr;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = p.ks > 1 ? 1 : 0;
+  cfg.numAttrs = n_attr;
   count_launch();
   GSB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kfn, tw, tx, tlb, ts, p, err));
 }

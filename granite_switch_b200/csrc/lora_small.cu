@@ -34,6 +34,7 @@ __global__ void __launch_bounds__(SHRINK_THREADS)
                              int64_t lda, const int32_t* __restrict__ row_adapter, __nv_bfloat16* __restrict__ s,
                              int64_t lds, int K, int rank, int num_adapters, int n_cols) {
   __shared__ float part[SHRINK_THREADS / 32][SHRINK_ROWS];
+  griddep_launch();  // the projection GEMM (this kernel's dependent) may start its set-up
   const int m = blockIdx.x, sl = blockIdx.y, z = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cols = num_adapters * rank;  // columns of one slice

@@ -16,7 +16,7 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
-from .._native import DeviceError
+from .._native import DeviceError, native
 from ..config import GraniteSwitchConfig
 from ..routing.scan import expert_table
 from .kv_cache import BLOCK_SIZE, BlockManager
@@ -55,6 +55,9 @@ class EngineConfig:
     async_scheduling: bool = True
     # pipeline parallelism: run each step as two micro-batches so consecutive stages overlap
     pipeline_microbatches: bool = True
+    # launch the decode-sized GEMMs as programmatic dependents of the kernel before them:
+    # they set up and start streaming weights while that kernel finishes (process-wide)
+    programmatic_launch: bool = True
 
 
 @dataclass
@@ -431,6 +434,7 @@ class LLM:
             if ecfg.kv_cache_dtype not in ("bfloat16", "fp8_e4m3"):
                 raise ValueError(f"kv_cache_dtype must be 'bfloat16' or 'fp8_e4m3', got {ecfg.kv_cache_dtype!r}")
             nm.kv_fp8 = ecfg.kv_cache_dtype == "fp8_e4m3"
+            native().set_pdl(bool(ecfg.programmatic_launch))
             if ecfg.num_kv_blocks is None:
                 torch.cuda.synchronize()
                 nb = default_num_kv_blocks(0, config, tp, ecfg.gpu_memory_utilization, self.device,

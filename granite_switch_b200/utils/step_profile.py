@@ -90,6 +90,8 @@ def main():
     p.add_argument("--no-fused-comm", dest="fused", action="store_false")
     p.add_argument("--lora", nargs="*", default=["qkv", "o"], help="projections with adapters")
     p.add_argument("--kv-cache-dtype", choices=["bfloat16", "fp8_e4m3"], default="bfloat16")
+    p.add_argument("--no-pdl", dest="pdl", action="store_false",
+                   help="launch the GEMMs in plain stream order (not as programmatic dependents)")
     args = p.parse_args()
 
     import torch.distributed as dist
@@ -123,6 +125,7 @@ def main():
                         max_model_len=max([args.prefill_ctx + n for n in args.prefill] + [args.decode_ctx + 1]) + 16,
                         tensor_parallel_size=world,
                         num_kv_blocks=need_blocks, fused_tp_comm=args.fused, kv_cache_dtype=args.kv_cache_dtype)
+    ecfg.programmatic_launch = args.pdl
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
               random_init=dict(lora_modules=tuple(args.lora), rank=32), tp_rank=rank, tp_group=group)
     eng = llm.engine
@@ -181,7 +184,7 @@ def main():
         table = {k: dict(ms=round(v, 3), share=round(v / step_ms, 3)) for k, v in sorted(ops.items(), key=lambda kv: -kv[1])}
         print(json.dumps(dict(preset=args.preset, tp=world, fused_comm=bool(getattr(model, "comm", None)),
                               tokens=tokens, prefill=args.prefill, prefill_ctx=args.prefill_ctx,
-                              decode=args.decode, decode_ctx=args.decode_ctx,
+                              decode=args.decode, decode_ctx=args.decode_ctx, pdl=args.pdl,
                               step_ms=round(plain, 3), step_ms_with_regions=round(step_ms, 3),
                               host_enqueue_ms=round(host_ms, 3), ops=table)), flush=True)
     if group is not None:

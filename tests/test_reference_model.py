@@ -1,4 +1,4 @@
-"""Composer + checkpoint + HF-style model on CPU (BASELINE config 1 and friends)."""
+"""Composer + checkpoint + HF-style model on CPU (benchmark config 1 and friends)."""
 import json
 import os
 
@@ -70,7 +70,7 @@ def _alora_batch(cfg, idx_json, seed=0, batch=4, seq=128):
 
 
 def test_config1_pre_invocation_equals_base(tiny_dir):
-    """logits and KV before the invocation equal the base model's."""
+    """Benchmark config 1: logits and KV before the invocation equal the base model's."""
     cfg = GraniteSwitchConfig.from_pretrained(tiny_dir)
     idx = json.load(open(os.path.join(tiny_dir, "adapter_index.json")))
     m = GraniteSwitchForCausalLM.from_pretrained(tiny_dir).eval()
