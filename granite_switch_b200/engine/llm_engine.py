@@ -58,6 +58,9 @@ class EngineConfig:
     # launch the decode-sized GEMMs as programmatic dependents of the kernel before them:
     # they set up and start streaming weights while that kernel finishes (process-wide)
     programmatic_launch: bool = True
+    # a step with decode rows and prefill chunks runs the prefill attention on a second
+    # stream beside the decode attention
+    overlap_attention: bool = True
 
 
 @dataclass
@@ -435,6 +438,7 @@ class LLM:
                 raise ValueError(f"kv_cache_dtype must be 'bfloat16' or 'fp8_e4m3', got {ecfg.kv_cache_dtype!r}")
             nm.kv_fp8 = ecfg.kv_cache_dtype == "fp8_e4m3"
             native().set_pdl(bool(ecfg.programmatic_launch))
+            nm.overlap_attention = bool(ecfg.overlap_attention)
             if ecfg.num_kv_blocks is None:
                 torch.cuda.synchronize()
                 nb = default_num_kv_blocks(0, config, tp, ecfg.gpu_memory_utilization, self.device,

@@ -112,6 +112,10 @@ class NativeGraniteSwitch:
         self.prof = None  # optional per-op CUDA-event profiler (utils.step_profile.StepProfiler)
         # prefill attention on tcgen05 (head_dim 64 / 128); False selects the mma.sync kernel (A/B tests)
         self.use_tc_attention = True
+        # a step with both decode rows and prefill chunks runs the prefill attention on a
+        # second stream, beside the decode attention (set by the engine)
+        self.overlap_attention = False
+        self._side_stream = None
         self.err = err_buffer(device)
         na = config.num_adapters
         self.num_adapters = na
@@ -626,9 +630,29 @@ class NativeGraniteSwitch:
         return logits
 
     def _attention(self, b: StepBatch, q: torch.Tensor, li: int, attn: torch.Tensor, scale: float) -> None:
+        """A step's attention plans. With ``overlap_attention`` and both a decode and a
+        prefill plan, the prefill plan (a few CTAs over long key ranges: latency bound)
+        runs on a side stream while the decode plan streams the decode rows' pages on the
+        current one; the plans write disjoint rows of ``attn`` and of the split
+        workspaces, and the current stream waits for the side stream before going on."""
+        if self.overlap_attention and len(b.plans) == 2 and self.prof is None:
+            main = torch.cuda.current_stream(self.device)
+            if self._side_stream is None:
+                self._side_stream = torch.cuda.Stream(device=self.device)
+            side = self._side_stream
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                self._run_plans(b, q, li, attn, scale, b.plans[1:])
+            self._run_plans(b, q, li, attn, scale, b.plans[:1])
+            main.wait_stream(side)
+            return
+        self._run_plans(b, q, li, attn, scale, b.plans)
+
+    def _run_plans(self, b: StepBatch, q: torch.Tensor, li: int, attn: torch.Tensor, scale: float,
+                   plans) -> None:
         R = self._region
         kc, vc, ks, vs = self._layer_cache(li)
-        for plan in b.plans:
+        for plan in plans:
             if plan.rows in (128, 256):
                 with R("attn_prefill"):
                     A.prefill_attention_tc(q, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,

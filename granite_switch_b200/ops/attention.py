@@ -31,6 +31,12 @@ def tc_rows_for(q_lens: list[int], kv_lens: list[int]) -> int:
     return 256 if total and 2 * long_fresh >= total else 128
 
 
+# CTAs a split prefill grid aims at, and the fewest keys a split may hold (A/B knobs of
+# split_prefill; the engine uses the defaults).
+PREFILL_SPLIT_CTAS = NUM_SMS
+PREFILL_MIN_KEYS_PER_SPLIT = 512
+
+
 def split_prefill(q_lens: list[int], kv_lens: list[int], group: int, num_kv_heads: int,
                   min_kv: int = 1024, rows: int = 128) -> int:
     """Key-range splits for a step's prefill tiles of ``rows`` rows (128: tcgen05; 64: the
@@ -49,7 +55,7 @@ def split_prefill(q_lens: list[int], kv_lens: list[int], group: int, num_kv_head
     n_ctas = sum(-(-q * group // rows) for q in q_lens) * num_kv_heads
     if n_ctas >= NUM_SMS:
         return 0
-    ns = choose_splits(n_ctas, max(kv_lens))
+    ns = choose_splits(n_ctas, max(kv_lens), PREFILL_MIN_KEYS_PER_SPLIT, PREFILL_SPLIT_CTAS)
     return ns if ns > 1 else 0
 
 
@@ -78,7 +84,7 @@ def build_work(q_lens: list[int], group: int, rows_per_tile: int,
     return seqs, rows
 
 
-def choose_splits(n_ctas: int, max_kv: int, min_keys_per_split: int = 512) -> int:
+def choose_splits(n_ctas: int, max_kv: int, min_keys_per_split: int = 512, target: int = NUM_SMS) -> int:
     """Flash-decoding split count: split the key range only while there are fewer
     (request, KV head) CTAs than SMs, aiming at one CTA per SM, never below 512
     keys per split. Measured on B200 (d=128, 32 q / 8 kv heads): at 256 or more
@@ -87,7 +93,7 @@ def choose_splits(n_ctas: int, max_kv: int, min_keys_per_split: int = 512) -> in
     """
     if n_ctas >= NUM_SMS:
         return 1
-    want = max(1, (NUM_SMS + n_ctas - 1) // max(n_ctas, 1))
+    want = max(1, (target + n_ctas - 1) // max(n_ctas, 1))
     cap = max(1, max_kv // min_keys_per_split)
     return int(max(1, min(want, cap, 32)))
 

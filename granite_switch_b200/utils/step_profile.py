@@ -90,6 +90,12 @@ def main():
     p.add_argument("--no-fused-comm", dest="fused", action="store_false")
     p.add_argument("--lora", nargs="*", default=["qkv", "o"], help="projections with adapters")
     p.add_argument("--kv-cache-dtype", choices=["bfloat16", "fp8_e4m3"], default="bfloat16")
+    p.add_argument("--prefill-split-ctas", type=int, default=None,
+                   help="CTAs a split prefill grid aims at (A/B of ops.attention.PREFILL_SPLIT_CTAS)")
+    p.add_argument("--prefill-min-keys", type=int, default=None,
+                   help="fewest keys per prefill split (A/B of ops.attention.PREFILL_MIN_KEYS_PER_SPLIT)")
+    p.add_argument("--no-attn-overlap", dest="attn_overlap", action="store_false",
+                   help="run a mixed step's prefill attention after its decode attention, on one stream")
     p.add_argument("--no-pdl", dest="pdl", action="store_false",
                    help="launch the GEMMs in plain stream order (not as programmatic dependents)")
     args = p.parse_args()
@@ -126,6 +132,13 @@ def main():
                         tensor_parallel_size=world,
                         num_kv_blocks=need_blocks, fused_tp_comm=args.fused, kv_cache_dtype=args.kv_cache_dtype)
     ecfg.programmatic_launch = args.pdl
+    ecfg.overlap_attention = args.attn_overlap
+    from ..ops import attention as A
+
+    if args.prefill_split_ctas:
+        A.PREFILL_SPLIT_CTAS = args.prefill_split_ctas
+    if args.prefill_min_keys:
+        A.PREFILL_MIN_KEYS_PER_SPLIT = args.prefill_min_keys
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
               random_init=dict(lora_modules=tuple(args.lora), rank=32), tp_rank=rank, tp_group=group)
     eng = llm.engine
@@ -185,6 +198,8 @@ def main():
         print(json.dumps(dict(preset=args.preset, tp=world, fused_comm=bool(getattr(model, "comm", None)),
                               tokens=tokens, prefill=args.prefill, prefill_ctx=args.prefill_ctx,
                               decode=args.decode, decode_ctx=args.decode_ctx, pdl=args.pdl,
+                              attn_overlap=args.attn_overlap, prefill_split_ctas=A.PREFILL_SPLIT_CTAS,
+                              prefill_min_keys=A.PREFILL_MIN_KEYS_PER_SPLIT,
                               step_ms=round(plain, 3), step_ms_with_regions=round(step_ms, 3),
                               host_enqueue_ms=round(host_ms, 3), ops=table)), flush=True)
     if group is not None:

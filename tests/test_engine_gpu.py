@@ -311,3 +311,58 @@ def test_fp8_kv_cache_engine_close_to_bf16():
     from granite_switch_b200._native import check_errors
 
     check_errors(dev)
+
+
+def test_overlapped_attention_plans_match_serial(tiny_dir):
+    """Steps with decode rows and prefill chunks give bit-identical logits whether the
+    prefill attention runs on a side stream beside the decode attention or after it."""
+    from granite_switch_b200.checkpoint import load_state_dict
+    from granite_switch_b200.config import GraniteSwitchConfig
+    from granite_switch_b200.engine.executor import NativeExecutor
+    from granite_switch_b200.engine.kv_cache import BlockManager
+    from granite_switch_b200.engine.llm_engine import HostRouter
+    from granite_switch_b200.engine.request import Request, SamplingParams
+    from granite_switch_b200.engine.scheduler import Scheduler
+    from granite_switch_b200.models.native import NativeGraniteSwitch
+    from granite_switch_b200._native import check_errors
+
+    cfg = GraniteSwitchConfig.from_pretrained(tiny_dir)
+    dev = torch.device("cuda")
+    nb = 128
+    nm = NativeGraniteSwitch.from_state_dict(cfg, load_state_dict(tiny_dir), dev, max_tokens=2048,
+                                             num_kv_blocks=nb, max_seqs=16)
+    nat = NativeExecutor(nm, 1024)
+    bm = BlockManager(nb)
+    router = HostRouter(cfg)
+    sch = Scheduler(bm, 8, 64, True, route_fn=router)
+    for p in _prompts(tiny_dir, 6, seed=3):
+        sch.add(Request(p, SamplingParams(max_tokens=6)))
+    mixed = steps = 0
+    while sch.has_work() and steps < 200:
+        out = sch.schedule()
+        nm.overlap_attention = False
+        _, serial = nat.compute_logits(out)
+        serial = serial.clone() if serial is not None else None  # None: no row samples this step
+        nm.overlap_attention = True
+        _, overlapped = nat.compute_logits(out)
+        torch.cuda.synchronize()
+        assert (serial is None) == (overlapped is None)
+        if serial is not None:
+            assert torch.equal(serial, overlapped)
+        q_lens = [c.num_tokens for c in out.chunks]
+        g = cfg.num_attention_heads // cfg.num_key_value_heads
+        mixed += int(any(q * g <= 16 for q in q_lens) and any(q * g > 16 for q in q_lens))
+        j = 0
+        for c in out.chunks:
+            r = c.req
+            r.carry = router(r.all_ids[c.start:c.start + c.num_tokens], r.carry)
+            r.num_computed = c.start + c.num_tokens
+            bm.register_full_blocks(r)
+            if c.needs_sample:
+                r.output_ids.append(int(serial[j].argmax()))
+                j += 1
+                if len(r.output_ids) >= r.sampling.max_tokens:
+                    sch.finish(r, "length")
+        steps += 1
+    check_errors(dev)
+    assert mixed > 0  # some steps had both plans
