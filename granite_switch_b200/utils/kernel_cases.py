@@ -1,7 +1,7 @@
 """One launch of each native kernel on a representative shape, for profiler captures.
 
 ``python -m granite_switch_b200.utils.kernel_cases <case>`` with case in
-gemm, gemm_pair, gemm_single, cublas, swiglu, attn_prefill64, moe, probe, decode_gemm, decode_shrink, fp8_gemm,
+gemm, gemm_pair, gemm_single, cublas, swiglu, attn_prefill64, moe, probe, decode_gemm, decode_shrink, lora_small, fp8_gemm,
 fp8_quant, attn_prefill, attn_decode, attn_decode_fp8, rmsnorm, rope, embed, routing, sample (or ``all``). Pair it with ``ncu --clock-control none -k regex:<kernel> -c 1`` (without
 ``--clock-control none`` ncu locks the GPU clocks).
 """
@@ -65,6 +65,12 @@ if want("decode_shrink"):  # LoRA shrink of o_proj in the headline decode step (
     a_all = (torch.randn(12 * 32, H, device=dev) * 0.02).bfloat16()
     ids = torch.randint(1, 13, (222,), device=dev, dtype=torch.int32)
     s_out = torch.empty(222, 12 * 32, device=dev, dtype=torch.bfloat16)
+    G.lora_shrink(xs, a_all, ids, 32, 12, out=s_out)
+if want("lora_small"):  # CUDA-core LoRA shrink of qkv at a 64-token decode step (3 slices, 12 adapters r32)
+    xs = torch.randn(64, H, device=dev).bfloat16()
+    a_all = (torch.randn(3 * 12 * 32, H, device=dev) * 0.02).bfloat16()
+    ids = torch.randint(0, 13, (64,), device=dev, dtype=torch.int32)
+    s_out = torch.empty(64, 3 * 12 * 32, device=dev, dtype=torch.bfloat16)
     G.lora_shrink(xs, a_all, ids, 32, 12, out=s_out)
 if want("attn_prefill") or want("attn_decode") or want("attn_decode_fp8"):
     hq, hkv, d = 32, 8, 128

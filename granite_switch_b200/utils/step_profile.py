@@ -96,6 +96,8 @@ def main():
                    help="fewest keys per prefill split (A/B of ops.attention.PREFILL_MIN_KEYS_PER_SPLIT)")
     p.add_argument("--no-attn-overlap", dest="attn_overlap", action="store_false",
                    help="run a mixed step's prefill attention after its decode attention, on one stream")
+    p.add_argument("--small-shrink-max-m", type=int, default=None,
+                   help="largest token count whose LoRA shrink runs on CUDA cores (A/B of ops.gemm.SMALL_SHRINK_MAX_M)")
     p.add_argument("--no-pdl", dest="pdl", action="store_false",
                    help="launch the GEMMs in plain stream order (not as programmatic dependents)")
     args = p.parse_args()
@@ -135,6 +137,10 @@ def main():
     ecfg.overlap_attention = args.attn_overlap
     from ..ops import attention as A
 
+    from ..ops import gemm as G
+
+    if args.small_shrink_max_m is not None:
+        G.SMALL_SHRINK_MAX_M = args.small_shrink_max_m
     if args.prefill_split_ctas:
         A.PREFILL_SPLIT_CTAS = args.prefill_split_ctas
     if args.prefill_min_keys:
@@ -199,7 +205,7 @@ def main():
                               tokens=tokens, prefill=args.prefill, prefill_ctx=args.prefill_ctx,
                               decode=args.decode, decode_ctx=args.decode_ctx, pdl=args.pdl,
                               attn_overlap=args.attn_overlap, prefill_split_ctas=A.PREFILL_SPLIT_CTAS,
-                              prefill_min_keys=A.PREFILL_MIN_KEYS_PER_SPLIT,
+                              prefill_min_keys=A.PREFILL_MIN_KEYS_PER_SPLIT, small_shrink_max_m=G.SMALL_SHRINK_MAX_M,
                               step_ms=round(plain, 3), step_ms_with_regions=round(step_ms, 3),
                               host_enqueue_ms=round(host_ms, 3), ops=table)), flush=True)
     if group is not None:
