@@ -98,6 +98,8 @@ def main():
                    help="run a mixed step's prefill attention after its decode attention, on one stream")
     p.add_argument("--small-shrink-max-m", type=int, default=None,
                    help="largest token count whose LoRA shrink runs on CUDA cores (A/B of ops.gemm.SMALL_SHRINK_MAX_M)")
+    p.add_argument("--decode-split-ctas", type=int, default=None,
+                   help="CTAs a split decode grid aims at (A/B of ops.attention.DECODE_SPLIT_CTAS)")
     p.add_argument("--no-pdl", dest="pdl", action="store_false",
                    help="launch the GEMMs in plain stream order (not as programmatic dependents)")
     args = p.parse_args()
@@ -141,6 +143,8 @@ def main():
 
     if args.small_shrink_max_m is not None:
         G.SMALL_SHRINK_MAX_M = args.small_shrink_max_m
+    if args.decode_split_ctas:
+        A.DECODE_SPLIT_CTAS = args.decode_split_ctas
     if args.prefill_split_ctas:
         A.PREFILL_SPLIT_CTAS = args.prefill_split_ctas
     if args.prefill_min_keys:
@@ -206,6 +210,7 @@ def main():
                               decode=args.decode, decode_ctx=args.decode_ctx, pdl=args.pdl,
                               attn_overlap=args.attn_overlap, prefill_split_ctas=A.PREFILL_SPLIT_CTAS,
                               prefill_min_keys=A.PREFILL_MIN_KEYS_PER_SPLIT, small_shrink_max_m=G.SMALL_SHRINK_MAX_M,
+                              decode_split_ctas=A.DECODE_SPLIT_CTAS,
                               step_ms=round(plain, 3), step_ms_with_regions=round(step_ms, 3),
                               host_enqueue_ms=round(host_ms, 3), ops=table)), flush=True)
     if group is not None:
