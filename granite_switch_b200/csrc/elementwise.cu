@@ -23,6 +23,7 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
                                int64_t ldo, const int64_t* __restrict__ rows, int H, float eps) {
   griddep_launch();  // a GEMM launched as this kernel's dependent may start its set-up
+  griddep_wait();    // launched as a dependent itself: x is the previous kernel's output
   const int r = blockIdx.x;
   const int64_t src = rows ? rows[r] : r;
   const uint4* xv = reinterpret_cast<const uint4*>(x + src * ldx);
@@ -116,6 +117,7 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ldq,
                                __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache,
                                const int64_t* __restrict__ slots, int Hq, int Hkv, int BS,
                                int64_t num_slots, uint32_t* err) {
+  griddep_wait();  // launched as a dependent of the projection that writes qkv
   const int t = blockIdx.x;
   int64_t pos = positions[t];
   if (pos < 0 || pos >= max_pos) {
@@ -242,14 +244,14 @@ void gsb_rmsnorm(const at::Tensor& x, const at::Tensor& w, const at::Tensor& out
   auto* op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   auto st = cur_stream(x);
   if (vpt <= 1)
-    rmsnorm_kernel<1><<<(::gsb::count_launch(), n), threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
+    launch_dependent(rmsnorm_kernel<1>, dim3(n), dim3(threads), 0, st, xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
   else if (vpt <= 2)
-    rmsnorm_kernel<2><<<(::gsb::count_launch(), n), threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
+    launch_dependent(rmsnorm_kernel<2>, dim3(n), dim3(threads), 0, st, xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
   else if (vpt <= 4)
-    rmsnorm_kernel<4><<<(::gsb::count_launch(), n), threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
+    launch_dependent(rmsnorm_kernel<4>, dim3(n), dim3(threads), 0, st, xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
   else {
     GSB_CHECK(vpt <= 8, "rmsnorm: H too large");
-    rmsnorm_kernel<8><<<(::gsb::count_launch(), n), threads, 0, st>>>(xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
+    launch_dependent(rmsnorm_kernel<8>, dim3(n), dim3(threads), 0, st, xp, x.stride(0), wp, op, out.stride(0), rp, H, (float)eps);
   }
   GSB_CUDA_CHECK(cudaGetLastError());
 }
@@ -310,17 +312,17 @@ void gsb_rope_kv(const at::Tensor& qkv, const at::Tensor& positions, const at::T
   const int threads = 256;
   switch (head_dim) {
     case 64:
-      rope_kv_kernel<64><<<(::gsb::count_launch(), T), threads, 0, st>>>(qp, qkv.stride(0), positions.data_ptr<int64_t>(),
+      launch_dependent(rope_kv_kernel<64>, dim3(T), dim3(threads), 0, st, qp, qkv.stride(0), positions.data_ptr<int64_t>(),
                                                 cos_sin.data_ptr<float>(), (int)cos_sin.size(0), kc, vc,
                                                 sp, (int)num_q_heads, (int)num_kv_heads, BS, num_slots, ep);
       break;
     case 128:
-      rope_kv_kernel<128><<<(::gsb::count_launch(), T), threads, 0, st>>>(qp, qkv.stride(0), positions.data_ptr<int64_t>(),
+      launch_dependent(rope_kv_kernel<128>, dim3(T), dim3(threads), 0, st, qp, qkv.stride(0), positions.data_ptr<int64_t>(),
                                                  cos_sin.data_ptr<float>(), (int)cos_sin.size(0), kc, vc,
                                                  sp, (int)num_q_heads, (int)num_kv_heads, BS, num_slots, ep);
       break;
     case 16:
-      rope_kv_kernel<16><<<(::gsb::count_launch(), T), threads, 0, st>>>(qp, qkv.stride(0), positions.data_ptr<int64_t>(),
+      launch_dependent(rope_kv_kernel<16>, dim3(T), dim3(threads), 0, st, qp, qkv.stride(0), positions.data_ptr<int64_t>(),
                                                 cos_sin.data_ptr<float>(), (int)cos_sin.size(0), kc, vc,
                                                 sp, (int)num_q_heads, (int)num_kv_heads, BS, num_slots, ep);
       break;

@@ -35,6 +35,7 @@ __global__ void __launch_bounds__(SHRINK_THREADS)
                              int64_t lds, int K, int rank, int num_adapters, int n_cols) {
   __shared__ float part[SHRINK_THREADS / 32][SHRINK_ROWS];
   griddep_launch();  // the projection GEMM (this kernel's dependent) may start its set-up
+  griddep_wait();    // launched as a dependent itself: x is the previous kernel's output
   const int m = blockIdx.x, sl = blockIdx.y, z = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cols = num_adapters * rank;  // columns of one slice
@@ -125,8 +126,9 @@ void gsb_lora_shrink_small(const at::Tensor& x, const at::Tensor& a_all, const a
   c10::cuda::CUDAGuard g(x.device());
   auto st = c10::cuda::getCurrentCUDAStream(x.device().index()).stream();
   const dim3 grid((unsigned)M, (unsigned)num_slices, (unsigned)((rank + SHRINK_ROWS - 1) / SHRINK_ROWS));
-  lora_shrink_small_kernel<<<(::gsb::count_launch(), grid), SHRINK_THREADS, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+  launch_dependent(
+      lora_shrink_small_kernel, grid, dim3(SHRINK_THREADS), 0, st, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+      x.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(a_all.data_ptr()), a_all.stride(0), row_adapter.data_ptr<int32_t>(),
       reinterpret_cast<__nv_bfloat16*>(s.data_ptr()), s.stride(0), K, (int)rank, (int)num_adapters, n);
   GSB_CUDA_CHECK(cudaGetLastError());

@@ -9,6 +9,7 @@
 
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 namespace gsb {
 
@@ -38,6 +39,30 @@ inline std::string gsb_str(const Ts&... vs) {
     cudaError_t _e = (expr);                                                  \
     GSB_CHECK(_e == cudaSuccess, "CUDA error ", cudaGetErrorString(_e), " in " #expr); \
   } while (0)
+
+bool pdl_enabled();
+void count_launch();
+
+// Launches `kernel` as a programmatic dependent of the kernel before it in `st` when
+// programmatic launch is enabled: it may start while that kernel finishes, so it must
+// execute griddepcontrol.wait (griddep_wait) before it reads anything an earlier kernel
+// writes or writes anything an earlier kernel reads.
+template <typename... KArgs, typename... Args>
+inline void launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                             Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  count_launch();
+  GSB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 inline PFN_cuTensorMapEncodeTiled_v12000 tma_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = []() {
