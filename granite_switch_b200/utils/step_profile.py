@@ -100,6 +100,8 @@ def main():
                    help="largest token count whose LoRA shrink runs on CUDA cores (A/B of ops.gemm.SMALL_SHRINK_MAX_M)")
     p.add_argument("--decode-split-ctas", type=int, default=None,
                    help="CTAs a split decode grid aims at (A/B of ops.attention.DECODE_SPLIT_CTAS)")
+    p.add_argument("--attn-decode-stages", type=int, default=None, choices=[2, 3],
+                   help="decode attention layout: 2 = short rings, three CTAs per SM; 3 = deep rings, two")
     p.add_argument("--no-pdl", dest="pdl", action="store_false",
                    help="launch the GEMMs in plain stream order (not as programmatic dependents)")
     args = p.parse_args()
@@ -143,6 +145,8 @@ def main():
 
     if args.small_shrink_max_m is not None:
         G.SMALL_SHRINK_MAX_M = args.small_shrink_max_m
+    if args.attn_decode_stages:
+        _native.native().attn_decode_stages(args.attn_decode_stages)
     if args.decode_split_ctas:
         A.DECODE_SPLIT_CTAS = args.decode_split_ctas
     if args.prefill_split_ctas:
@@ -211,6 +215,7 @@ def main():
                               attn_overlap=args.attn_overlap, prefill_split_ctas=A.PREFILL_SPLIT_CTAS,
                               prefill_min_keys=A.PREFILL_MIN_KEYS_PER_SPLIT, small_shrink_max_m=G.SMALL_SHRINK_MAX_M,
                               decode_split_ctas=A.DECODE_SPLIT_CTAS,
+                              attn_decode_stages=_native.native().attn_decode_stages(-1),
                               step_ms=round(plain, 3), step_ms_with_regions=round(step_ms, 3),
                               host_enqueue_ms=round(host_ms, 3), ops=table)), flush=True)
     if group is not None:
