@@ -248,11 +248,16 @@ def test_short_chunks_over_long_prefix_split_kv():
     assert A.split_prefill([48, 48, 300], [4548, 4548, 300], 4, 8) == 2  # 112 CTAs
     assert A.split_prefill([300] * 3, [4548] * 3, 4, 8) == 0     # 240 CTAs
     assert A.split_prefill([48, 48], [4548, 4548], 4, 8, rows=64) == 4  # 48 CTAs of 64 rows (fp8 cache)
+    assert A.choose_splits(1024, 4200) == 2    # decode: 128 requests x 8 KV heads
+    assert A.choose_splits(2048, 4200) == 1    # enough CTAs without a split
+    assert A.choose_splits(64, 8192) == 16     # a small batch: capped at 512 keys per split
+    assert A.choose_splits(64, 300) == 1       # short contexts never split
     m = types.SimpleNamespace(num_q=32, num_kv=8, head_dim=128, use_tc_attention=True, ws_tokens=512, kv_fp8=False)
     q = [48, 48] + [1] * 126
     kv = [4548, 4548] + [4500] * 126
     plans = NativeGraniteSwitch.attention_plans(m, q, kv)
-    assert [(p[2], p[3]) for p in plans] == [(16, 1), (128, 5)]
+    # decode rows: 126 x 8 KV heads = 1,008 CTAs, under the 1,536 a split grid aims at -> 2 splits
+    assert [(p[2], p[3]) for p in plans] == [(16, 2), (128, 5)]
     assert sorted(plans[1][0]) == [0, 0, 1, 1]  # two 128-row tiles per chunk
     plans = NativeGraniteSwitch.attention_plans(m, [4096] + [1] * 127, [4096] + [4500] * 127)
     assert plans[1][2] == 256 and plans[1][3] == 1
