@@ -532,6 +532,293 @@ __global__ void __launch_bounds__(AttnCfg<D, WARPS_M, KT, STAGES, F8>::THREADS)
   }
 }
 
+// Transpose of an 8x8 b16 matrix across the warp: a lane holds row lane / 4, columns
+// 2 (lane % 4) and 2 (lane % 4) + 1 before and after.
+__device__ __forceinline__ uint32_t attn_movmatrix_t(uint32_t v) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(v));
+  return r;
+}
+
+// Decode attention over the fp8 cache with the keys on the MMA's 16-row side: S^T =
+// K Q^T and O^T = V^T P^T on m16n8k16 (f16 operands, fp32 accumulators), for work tiles
+// of at most 8 query rows (rows_per_tile 8: one decode token's query heads of a KV head,
+// or two tokens' at 4 heads per KV head). The row-major layout (paged_attn_kernel,
+// 16 query rows as M) spends three quarters of its MMAs, exponentials and softmax
+// arithmetic on padding rows when a KV head has 4 query heads; here the 8 query
+// columns carry 4 of them, so the tensor and softmax work per key halves while every
+// K / V byte is still converted once. The stored fp8 layouts fit as they are: a K row's
+// 32-bit word at 4 t holds head dims {2t, 2t+1, 2t+8, 2t+9} of its 16-wide group, the
+// A fragment of a 16-key x 16-dim block, and the transposed V page row d holds keys in
+// the same order, the A fragment of V^T. The probabilities leave the S^T accumulators
+// as the B operand of the second MMA through two movmatrix transposes per 16 keys.
+// Four warps take 16 keys (one page) of every 64-key tile each and merge their softmax
+// states at the end, as the row-major decode layout does; the stage ring, page-id
+// staging and TMA issue are the same.
+template <int D, int STAGES>
+__global__ void __launch_bounds__(128)
+    paged_attn_fp8t_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                           const __grid_constant__ CUtensorMap tm_ks, const __grid_constant__ CUtensorMap tm_vs,
+                           const __nv_bfloat16* __restrict__ q, int64_t q_stride,
+                           const int32_t* __restrict__ block_table, int bt_stride, int num_blocks,
+                           const int32_t* __restrict__ q_start, const int32_t* __restrict__ kv_len_arr,
+                           const int32_t* __restrict__ work_seq, const int32_t* __restrict__ work_row0,
+                           int Hq, int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out,
+                           int64_t out_stride, float* __restrict__ ws_o, float* __restrict__ ws_lse,
+                           int nsplit, int T, uint32_t* err) {
+  using namespace attn;
+  griddep_launch();  // a GEMM launched as a dependent may start its set-up
+  using C = AttnCfg<D, 1, 64, STAGES, true>;
+  constexpr int KT = 64, PAGES = KT / PAGE, NQ = 8, DB = D / 16;
+  static_assert(C::WARPS == 4 && C::KPW == PAGE, "one 16-key page per warp and tile");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* sKV = smem + C::Q_BYTES;  // [STAGES][K tile | V tile | K, V scales]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sKV + STAGES * C::STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int w = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int seq = work_seq[w];
+  const int row0 = work_row0[w];
+  const int G = Hq / Hkv;
+  const int qs = q_start[seq];
+  const int q_len = q_start[seq + 1] - qs;
+  const int kv_len = kv_len_arr[seq];
+  const int ctx = kv_len - q_len;
+  const int n_rows = q_len * G;
+  const int32_t* bt = block_table + (int64_t)seq * bt_stride;
+
+  const int last_row = min(row0 + NQ, n_rows) - 1;
+  const int k_limit = max(0, min(kv_len, ctx + last_row / G + 1));
+  int per_split = (k_limit + nsplit - 1) / nsplit;
+  per_split = (per_split + KT - 1) / KT * KT;
+  const int k_begin = split * per_split;
+  const int k_end = min(k_limit, k_begin + per_split);
+  const int n_tiles = (k_end > k_begin) ? (k_end - k_begin + KT - 1) / KT : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], PAGES);  // one arrival per page's producer
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_ks);
+    tma_prefetch_desc(&tm_vs);
+  }
+  int32_t* s_pages = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full) + 256);
+  const int pg0 = k_begin / PAGE;
+  const int n_cached = (n_tiles > 0) ? min((k_end + PAGE - 1) / PAGE - pg0, C::PT_CAP) : 0;
+  for (int i = threadIdx.x; i < n_cached; i += C::THREADS) s_pages[i] = checked_index(bt[pg0 + i], num_blocks, err, kSitePage);
+  __syncthreads();  // barrier init and page ids visible
+
+  const int first_page = checked_index(bt[0], num_blocks, err, kSitePage);
+  auto issue = [&](int it, int p) {
+    const int s = it % STAGES;
+    uint8_t* dK = sKV + s * C::STAGE_BYTES;
+    uint8_t* dV = dK + C::TILE_BYTES;
+    uint8_t* dS = dV + C::TILE_BYTES;
+    mbar_arrive_expect_tx(&full[s], C::TX_BYTES / PAGES);
+    const int j = k_begin + it * KT + p * PAGE;
+    // pages past the key range still load a valid page (masked later)
+    const int pi = j / PAGE - pg0;
+    const int page = (j < k_end) ? (pi < n_cached ? s_pages[pi] : checked_index(bt[j / PAGE], num_blocks, err,
+                                                                                kSitePage))
+                                 : first_page;
+    tma_load_2d(dK + p * PAGE * D, &tm_k, &full[s], 0, (page * Hkv + kvh) * PAGE);
+    tma_load_2d(dV + p * PAGE * D, &tm_v, &full[s], 0, (page * Hkv + kvh) * (D / 16));
+    tma_load_2d(dS + p * C::SC_SLOT, &tm_ks, &full[s], 0, page * Hkv + kvh);
+    tma_load_2d(dS + (PAGES + p) * C::SC_SLOT, &tm_vs, &full[s], 0, page * Hkv + kvh);
+  };
+  const bool producer = lane == 0;  // lane 0 of warp p issues page p of every tile
+  int issued = 0;
+  if (producer) {
+    for (int it = 0; it < min(n_tiles, STAGES - 1); ++it) issue(it, warp);
+    issued = min(n_tiles, STAGES - 1);
+  }
+
+  // B fragments of Q^T (query column g of this tile, f16 with the softmax scale folded in):
+  // dims 16 kk + 2 t, +1 and 16 kk + 2 t + 8, +9; zero for columns past the tile's rows
+  uint32_t qb[DB][2];
+  {
+    const int r = row0 + g;
+    const bool valid = g < NQ && r < n_rows;
+    const __nv_bfloat16* src = q + (int64_t)(qs + (valid ? r / G : 0)) * q_stride + (kvh * G + (valid ? r % G : 0)) * D;
+#pragma unroll
+    for (int kk = 0; kk < DB; ++kk) {
+      const uint32_t lo = valid ? *reinterpret_cast<const uint32_t*>(src + 16 * kk + 2 * t4) : 0u;
+      const uint32_t hi = valid ? *reinterpret_cast<const uint32_t*>(src + 16 * kk + 2 * t4 + 8) : 0u;
+      qb[kk][0] = bf16x2_to_f16x2_scaled(lo, scale_log2);
+      qb[kk][1] = bf16x2_to_f16x2_scaled(hi, scale_log2);
+    }
+  }
+  // this thread's two query columns: 2 t and 2 t + 1 of the tile; their positions
+  int pos[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) pos[e] = ctx + (row0 + 2 * t4 + e) / G;
+
+  float o[DB][4];  // O^T: rows d = 16 db + g (+ 8), columns 2 t, 2 t + 1
+#pragma unroll
+  for (int i = 0; i < DB; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_c[2] = {-INFINITY, -INFINITY}, l_c[2] = {0.f, 0.f};
+  const int key_lo = warp * PAGE + g;  // this thread's keys in the tile: key_lo, key_lo + 8
+  // K word of key key_lo in 16-dim group kk: row key_lo, 16-byte chunk swizzled as
+  // kv_fp8.cu stores it; key_lo + 8 has the same swizzle
+  const int k_off = key_lo * D + 4 * t4 + ((D == 128 ? g : (g >> 1) & 3) << 4);
+
+  bool ok = true;
+  int consumed = 0;
+  for (int it = 0; it < n_tiles; ++it) {
+    const int s = it % STAGES;
+    if (producer && it + STAGES - 1 < n_tiles) {
+      issue(it + STAGES - 1, warp);
+      issued = it + STAGES;
+    }
+    const bool landed = mbar_wait(&full[s], (it / STAGES) & 1, err, kErrAttnWait);
+    const int tile_start = k_begin + it * KT;
+    const uint8_t* kst = sKV + s * C::STAGE_BYTES;
+    const uint8_t* vst = kst + C::TILE_BYTES;
+    const float* kss = reinterpret_cast<const float*>(kst + 2 * C::TILE_BYTES);
+    const float* vss = kss + PAGES * (C::SC_SLOT / 4);
+
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};  // S^T: keys key_lo (0, 1), key_lo + 8 (2, 3)
+#pragma unroll
+    for (int kk = 0; kk < DB; ++kk) {
+      uint32_t a[4];
+      const int off = k_off ^ (kk << 4);
+      e4m3x4_to_f16x2x2(*reinterpret_cast<const uint32_t*>(kst + off), a[0], a[2]);
+      e4m3x4_to_f16x2x2(*reinterpret_cast<const uint32_t*>(kst + off + 8 * D), a[1], a[3]);
+      mma16816_f16(sc, a, qb[kk][0], qb[kk][1]);
+    }
+    // K scales (the softmax scale is in Q), masks on edge tiles only
+    const float ks_lo = kss[warp * (C::SC_SLOT / 4) + g], ks_hi = kss[warp * (C::SC_SLOT / 4) + g + 8];
+    const bool edge = tile_start + KT > min(k_end, ctx + row0 / G + 1);
+    float mx[2];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = tile_start + key_lo + (e >> 1) * 8;
+      float v = sc[e] * ((e < 2) ? ks_lo : ks_hi);
+      if (edge && (j >= k_end || j > pos[e & 1])) v = -INFINITY;
+      sc[e] = v;
+    }
+    mx[0] = fmaxf(sc[0], sc[2]);
+    mx[1] = fmaxf(sc[1], sc[3]);
+    float corr[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 4));
+      mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 8));
+      mx[e] = fmaxf(mx[e], __shfl_xor_sync(0xffffffffu, mx[e], 16));
+      const float mnew = fmaxf(m_c[e], mx[e]);
+      corr[e] = (mnew == -INFINITY) ? 1.f : exp2f(m_c[e] - mnew);
+      m_c[e] = mnew;
+    }
+    float rs[2];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float mm = m_c[e & 1];
+      sc[e] = (mm == -INFINITY) ? 0.f : exp2f(sc[e] - mm);
+    }
+    rs[0] = sc[0] + sc[2];
+    rs[1] = sc[1] + sc[3];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      rs[e] += __shfl_xor_sync(0xffffffffu, rs[e], 4);
+      rs[e] += __shfl_xor_sync(0xffffffffu, rs[e], 8);
+      rs[e] += __shfl_xor_sync(0xffffffffu, rs[e], 16);
+      l_c[e] = l_c[e] * corr[e] + rs[e];
+    }
+    // the V scales fold into the probabilities (the sums stay unscaled)
+    const float vs_lo = vss[warp * (C::SC_SLOT / 4) + g], vs_hi = vss[warp * (C::SC_SLOT / 4) + g + 8];
+    const uint32_t pb0 = attn_movmatrix_t(pack_f16x2(sc[0] * vs_lo, sc[1] * vs_lo));  // keys 2 t, 2 t + 1
+    const uint32_t pb1 = attn_movmatrix_t(pack_f16x2(sc[2] * vs_hi, sc[3] * vs_hi));  // keys 2 t + 8, + 9
+    if (__any_sync(0xffffffffu, corr[0] != 1.f || corr[1] != 1.f)) {
+#pragma unroll
+      for (int i = 0; i < DB; ++i) {
+        o[i][0] *= corr[0];
+        o[i][1] *= corr[1];
+        o[i][2] *= corr[0];
+        o[i][3] *= corr[1];
+      }
+    }
+    // V^T page of this warp's 16 keys: [D][16 bytes], row d's word at 4 t = keys 2t, 2t+1, 2t+8, 2t+9
+    const uint8_t* vp = vst + warp * (PAGE * D) + g * 16 + 4 * t4;
+#pragma unroll
+    for (int db = 0; db < DB; ++db) {
+      uint32_t a[4];
+      e4m3x4_to_f16x2x2(*reinterpret_cast<const uint32_t*>(vp + db * 256), a[0], a[2]);
+      e4m3x4_to_f16x2x2(*reinterpret_cast<const uint32_t*>(vp + db * 256 + 128), a[1], a[3]);
+      mma16816_f16(o[db], a, pb0, pb1);
+    }
+    // every warp is done with stage s before it is refilled
+    if (!__syncthreads_and(landed)) {
+      ok = false;
+      break;
+    }
+    consumed = it + 1;
+  }
+  if (!ok) {
+    if (threadIdx.x == 0)
+      for (int it = consumed; it < issued; ++it)
+        mbar_wait(&full[it % STAGES], (it / STAGES) & 1, err, kErrAttnWait);
+    __syncthreads();
+    return;
+  }
+
+  // ---- merge the four warps' key slices (the ring is free: every tile was consumed)
+  float* sm = reinterpret_cast<float*>(sKV);
+  float* sl = sm + 4 * NQ;
+  float* so = sl + 4 * NQ;  // [4 warps][NQ columns][D]
+  if (g == 0) {
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      sm[warp * NQ + 2 * t4 + e] = m_c[e];
+      sl[warp * NQ + 2 * t4 + e] = l_c[e];
+    }
+  }
+  __syncthreads();
+  float my[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) m = fmaxf(m, sm[k * NQ + 2 * t4 + e]);
+    my[e] = (m_c[e] == -INFINITY) ? 0.f : exp2f(m_c[e] - m);
+  }
+#pragma unroll
+  for (int db = 0; db < DB; ++db) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int col = 2 * t4 + (e & 1), d = 16 * db + g + (e >> 1) * 8;
+      so[(warp * NQ + col) * D + d] = o[db][e] * my[e & 1];
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < NQ * D; idx += C::THREADS) {
+    const int r = idx / D, col = idx % D;
+    const int gr = row0 + r;
+    if (gr >= n_rows) continue;
+    float acc = 0.f, m = -INFINITY, l = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      acc += so[(k * NQ + r) * D + col];
+      m = fmaxf(m, sm[k * NQ + r]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float mk = sm[k * NQ + r];
+      l += (mk == -INFINITY) ? 0.f : sl[k * NQ + r] * exp2f(mk - m);
+    }
+    const int tok = qs + gr / G, head = kvh * G + gr % G;
+    const float val = (l > 0.f) ? acc / l : 0.f;
+    if (nsplit == 1) {
+      out[(int64_t)tok * out_stride + head * D + col] = f2bf(val);
+    } else {
+      ws_o[(((int64_t)split * T + tok) * Hq + head) * D + col] = val;
+      if (col == 0) ws_lse[((int64_t)split * T + tok) * Hq + head] = (l > 0.f) ? (m + log2f(l)) : -INFINITY;
+    }
+  }
+}
+
 // Merge flash-decoding partials: out = sum_s 2^(lse_s - M) o_s / sum_s 2^(lse_s - M),
 // for the (token, head) rows owned by this call's work tiles only. The plans of
 // one engine step (decode rows, prefill chunks) write disjoint rows of the same
@@ -620,6 +907,28 @@ static void launch_attn(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const
   GSB_CUDA_CHECK(cudaGetLastError());
 }
 
+template <int D, int ST>
+static void launch_attn_fp8t(dim3 grid, cudaStream_t st, const CUtensorMap& tk, const CUtensorMap& tv,
+                             const CUtensorMap& tks, const CUtensorMap& tvs, const at::Tensor& q, const at::Tensor& bt,
+                             int num_blocks, const at::Tensor& q_start, const at::Tensor& kv_len,
+                             const at::Tensor& work_seq, const at::Tensor& work_row0, int Hq, int Hkv,
+                             float scale_log2, const at::Tensor& out, float* wso, float* wsl, int nsplit, int T,
+                             uint32_t* err) {
+  using C = AttnCfg<D, 1, 64, ST, true>;
+  auto kfn = paged_attn_fp8t_kernel<D, ST>;
+  static bool configured = false;
+  if (!configured) {
+    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured = true;
+  }
+  kfn<<<(::gsb::count_launch(), grid), C::THREADS, C::SMEM, st>>>(
+      tk, tv, tks, tvs, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), bt.data_ptr<int32_t>(),
+      (int)bt.stride(0), num_blocks, q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
+      work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv, scale_log2,
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), wso, wsl, nsplit, T, err);
+  GSB_CUDA_CHECK(cudaGetLastError());
+}
+
 int64_t gsb_attn_decode_stages(int64_t v) {
   const int64_t old = g_decode_stages;
   if (v == 2 || v == 3) g_decode_stages = (int)v;
@@ -630,8 +939,9 @@ int64_t gsb_attn_decode_stages(int64_t v) {
 // block_table [S, max_blocks] int32; q_start [S+1] int32 (token offsets of each
 // request chunk in q); kv_len [S] int32 (cached + new keys); work_seq/work_row0
 // [n_work] int32: the (request, first row) of each CTA tile. rows_per_tile
-// selects the layout: 128 (prefill, 8 warps), 64 (prefill, 4 warps) or 16
-// (decode, warps split keys). out [T, Hq*D] bf16.
+// selects the layout: 128 (prefill, 8 warps), 64 (prefill, 4 warps), 16
+// (decode, warps split keys) or, over an fp8 cache only, 8 (decode with the keys on
+// the MMA's row side, tiles of at most 8 rows). out [T, Hq*D] bf16.
 void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                          const at::Tensor& block_table, const at::Tensor& q_start, const at::Tensor& kv_len,
                          const at::Tensor& work_seq, const at::Tensor& work_row0, int64_t rows_per_tile,
@@ -716,7 +1026,17 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
                                     T, ep)
   // fp8 pages are half the bytes, so the rings hold twice as many tiles for the same bytes in flight
   // (decode: three CTAs per SM, as the bf16 short-ring layout)
-  if (f8 && D == 128) {
+  GSB_CHECK(rows_per_tile != 8 || f8, "attention: 8-row decode tiles read the fp8 cache only");
+  if (f8 && rows_per_tile == 8) {
+    if (D == 128)
+      launch_attn_fp8t<128, 3>(grid, st, tk, tv, tks, tvs, q, block_table, (int)k_cache.size(0), q_start, kv_len,
+                               work_seq, work_row0, Hq, Hkv, scale_log2, out, wso, wsl, (int)nsplit, T, ep);
+    else if (D == 64)
+      launch_attn_fp8t<64, 6>(grid, st, tk, tv, tks, tvs, q, block_table, (int)k_cache.size(0), q_start, kv_len,
+                              work_seq, work_row0, Hq, Hkv, scale_log2, out, wso, wsl, (int)nsplit, T, ep);
+    else
+      GSB_CHECK(false, "attention: head_dim must be 64 or 128, got ", D);
+  } else if (f8 && D == 128) {
     if (rows_per_tile == 128) GSB_ATTN8(128, 8, 64, 4);
     else if (rows_per_tile == 64) GSB_ATTN8(128, 4, 64, 4);
     else GSB_ATTN8(128, 1, 64, 3);

@@ -280,7 +280,8 @@ class NativeExecutor:
                          slots=self.d_i64[2 * p:3 * p], seq_starts=self.d_i32[: p + 1],
                          carry_in=self.d_i32[p + 1:2 * p + 1], kv_lens=self.d_i32[2 * p + 1:3 * p + 1],
                          block_table=self.d_bt[:p], logit_rows=self.d_rows[:p],
-                         plans=[AttnPlan(work[0], work[1], 16, work[2])])
+                         plans=[AttnPlan(work[0], work[1], self.model.fp8_decode_rows if self.model.kv_fp8 else 16,
+                                         work[2])])
 
     def _run_graph(self, hb: HostBatch, p: int) -> torch.Tensor:
         from .. import _native
@@ -290,7 +291,7 @@ class NativeExecutor:
         g = self.graphs.get(p)
         if g is None:
             m = self.model
-            ws, wr = A.build_work([1] * p, m.num_q // m.num_kv, 16)
+            ws, wr = A.build_work([1] * p, m.num_q // m.num_kv, m.fp8_decode_rows if m.kv_fp8 else 16)
             ns = A.choose_splits(p * m.num_kv, self.max_blocks * BLOCK_SIZE)
             if ns > 1 and p > m.ws_tokens:
                 ns = 1

@@ -116,6 +116,8 @@ class NativeGraniteSwitch:
         # second stream, beside the decode attention (set by the engine)
         self.overlap_attention = False
         self._side_stream = None
+        # decode tile rows over an fp8 cache: 8 (keys on the MMA's row side) or 16 (row-major)
+        self.fp8_decode_rows = 8
         self.err = err_buffer(device)
         na = config.num_adapters
         self.num_adapters = na
@@ -659,7 +661,7 @@ class NativeGraniteSwitch:
                                            plan.work_row0, self.num_q, scale, attn, plan.rows, plan.nsplit,
                                            self.ws_o, self.ws_lse)
             else:
-                with R("attn_decode" if plan.rows == 16 else "attn_prefill"):
+                with R("attn_decode" if plan.rows in (8, 16) else "attn_prefill"):
                     A.paged_attention(q, kc, vc, b.block_table, b.seq_starts, b.kv_lens, plan.work_seq,
                                       plan.work_row0, plan.rows, self.num_q, scale, attn, plan.nsplit,
                                       self.ws_o, self.ws_lse, ks, vs)
@@ -734,7 +736,10 @@ class NativeGraniteSwitch:
             pre_rows = 128 if pre_split else (A.tc_rows_for(pre_q, pre_kv) if pre else 64)
         else:
             pre_rows = 64
-        for idx, rows in ((dec, 16), (pre, pre_rows)):
+        # decode rows over an fp8 cache: 8-row tiles with the keys on the MMA's row side
+        # (fp8_decode_rows = 16 selects the row-major layout, for A/B runs)
+        dec_rows = getattr(self, "fp8_decode_rows", 8) if self.kv_fp8 else 16
+        for idx, rows in ((dec, dec_rows), (pre, pre_rows)):
             if not idx:
                 continue
             sub_q = [q_lens[i] for i in idx]
@@ -742,7 +747,7 @@ class NativeGraniteSwitch:
             ws = [idx[t] for t in sw]
             n_ctas = len(ws) * self.num_kv
             max_kv = max(kv_lens[i] for i in idx)
-            ns = A.choose_splits(n_ctas, max_kv) if rows == 16 else (pre_split or 1)
+            ns = A.choose_splits(n_ctas, max_kv) if rows == dec_rows else (pre_split or 1)
             tot = sum(q_lens)
             if ns > 1 and tot > self.ws_tokens:
                 ns = 1

@@ -102,6 +102,8 @@ def main():
                    help="CTAs a split decode grid aims at (A/B of ops.attention.DECODE_SPLIT_CTAS)")
     p.add_argument("--attn-decode-stages", type=int, default=None, choices=[2, 3],
                    help="decode attention layout: 2 = short rings, three CTAs per SM; 3 = deep rings, two")
+    p.add_argument("--fp8-decode-rows", type=int, default=8, choices=[8, 16],
+                   help="decode tile rows over an fp8 cache: 8 (keys on the MMA's row side) or 16 (row-major)")
     p.add_argument("--no-pdl", dest="pdl", action="store_false",
                    help="launch the GEMMs in plain stream order (not as programmatic dependents)")
     args = p.parse_args()
@@ -156,6 +158,7 @@ def main():
     llm = LLM(config, device=f"cuda:{local_rank()}", engine_config=ecfg,
               random_init=dict(lora_modules=tuple(args.lora), rank=32), tp_rank=rank, tp_group=group)
     eng = llm.engine
+    llm.model.fp8_decode_rows = args.fp8_decode_rows
     out = build_step(eng, args.prefill, args.decode, args.decode_ctx, base["vocab_size"], prefill_ctx=args.prefill_ctx)
     ex = eng.executor
     model = llm.model
@@ -216,6 +219,7 @@ def main():
                               prefill_min_keys=A.PREFILL_MIN_KEYS_PER_SPLIT, small_shrink_max_m=G.SMALL_SHRINK_MAX_M,
                               decode_split_ctas=A.DECODE_SPLIT_CTAS,
                               attn_decode_stages=_native.native().attn_decode_stages(-1),
+                              kv_cache_dtype=args.kv_cache_dtype, fp8_decode_rows=args.fp8_decode_rows,
                               step_ms=round(plain, 3), step_ms_with_regions=round(step_ms, 3),
                               host_enqueue_ms=round(host_ms, 3), ops=table)), flush=True)
     if group is not None:

@@ -344,19 +344,20 @@ def test_kv_write_fp8_roundtrip(d):
 
 
 @pytest.mark.parametrize("d", [64, 128])
-@pytest.mark.parametrize("mode", ["decode", "prefill", "prefill128", "short_after_long"])
+@pytest.mark.parametrize("mode", ["decode", "decode8", "prefill", "prefill128", "short_after_long"])
 @pytest.mark.parametrize("nsplit", [1, 3])
 @pytest.mark.parametrize("hq", [8, 4])
 def test_paged_attention_fp8(d, mode, nsplit, hq):
-    """Paged attention over the fp8 cache (every mma.sync layout, split keys, GQA groups of 4
-    and 2) against the fp32 oracle on the dequantised cache: the kernel's only extra error is
-    bf16 rounding."""
+    """Paged attention over the fp8 cache (every mma.sync layout, including the 8-row decode
+    tiles with the keys on the MMA's row side; split keys, GQA groups of 4 and 2) against the
+    fp32 oracle on the dequantised cache: the kernel's only extra error is bf16 rounding."""
     from granite_switch_b200.ops import attention as A
 
     hkv = 2
     g = hq // hkv
-    if mode == "decode":
-        q_lens, kv_lens, rows = [1, 1, 2, 1, 4], [1, 37, 300, 1025, 64], 16
+    if mode in ("decode", "decode8"):
+        # decode8: a 4-token request at 4 heads per KV head spans two 8-row tiles
+        q_lens, kv_lens, rows = [1, 1, 2, 1, 4], [1, 37, 300, 1025, 64], (16 if mode == "decode" else 8)
     elif mode == "short_after_long":
         q_lens, kv_lens, rows = [48, 40, 17], [4548, 2100, 1040], 64
         nsplit = 4 if nsplit > 1 else 1
