@@ -555,6 +555,17 @@ __device__ __forceinline__ uint32_t attn_movmatrix_t(uint32_t v) {
 // Four warps take 16 keys (one page) of every 64-key tile each and merge their softmax
 // states at the end, as the row-major decode layout does; the stage ring, page-id
 // staging and TMA issue are the same.
+// Shared memory of paged_attn_fp8t_kernel: the stage ring, the barriers and the page ids
+// (no Q tile: Q goes from global memory straight into registers), kept small so that
+// four CTAs (3 stages) or five (2 stages, then registers limit) share an SM: the kernel
+// is bound by latency, not bandwidth, and needs the warps.
+template <int D, int STAGES>
+struct Fp8tCfg {
+  using A = AttnCfg<D, 1, 64, STAGES, true>;
+  static constexpr int PT_CAP = 512;  // page ids staged per CTA (8,192 keys; beyond, global reads)
+  static constexpr int SMEM = 1024 + STAGES * A::STAGE_BYTES + 256 + PT_CAP * 4;
+};
+
 template <int D, int STAGES>
 __global__ void __launch_bounds__(128)
     paged_attn_fp8t_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
@@ -569,11 +580,12 @@ __global__ void __launch_bounds__(128)
   using namespace attn;
   griddep_launch();  // a GEMM launched as a dependent may start its set-up
   using C = AttnCfg<D, 1, 64, STAGES, true>;
-  constexpr int KT = 64, PAGES = KT / PAGE, NQ = 8, DB = D / 16;
+  constexpr int KT = 64, PAGES = KT / PAGE, NQ = 8, DB = D / 16, PT_CAP = Fp8tCfg<D, STAGES>::PT_CAP;
   static_assert(C::WARPS == 4 && C::KPW == PAGE, "one 16-key page per warp and tile");
+  static_assert(STAGES * C::STAGE_BYTES >= (4 * NQ * (2 + D)) * 4, "merge scratch fits the ring");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* sKV = smem + C::Q_BYTES;  // [STAGES][K tile | V tile | K, V scales]
+  uint8_t* sKV = smem;  // [STAGES][K tile | V tile | K, V scales]
   uint64_t* full = reinterpret_cast<uint64_t*>(sKV + STAGES * C::STAGE_BYTES);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -607,7 +619,7 @@ __global__ void __launch_bounds__(128)
   }
   int32_t* s_pages = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full) + 256);
   const int pg0 = k_begin / PAGE;
-  const int n_cached = (n_tiles > 0) ? min((k_end + PAGE - 1) / PAGE - pg0, C::PT_CAP) : 0;
+  const int n_cached = (n_tiles > 0) ? min((k_end + PAGE - 1) / PAGE - pg0, PT_CAP) : 0;
   for (int i = threadIdx.x; i < n_cached; i += C::THREADS) s_pages[i] = checked_index(bt[pg0 + i], num_blocks, err, kSitePage);
   __syncthreads();  // barrier init and page ids visible
 
@@ -915,18 +927,31 @@ static void launch_attn_fp8t(dim3 grid, cudaStream_t st, const CUtensorMap& tk, 
                              float scale_log2, const at::Tensor& out, float* wso, float* wsl, int nsplit, int T,
                              uint32_t* err) {
   using C = AttnCfg<D, 1, 64, ST, true>;
+  constexpr int SMEM = Fp8tCfg<D, ST>::SMEM;
   auto kfn = paged_attn_fp8t_kernel<D, ST>;
   static bool configured = false;
   if (!configured) {
-    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    GSB_CUDA_CHECK(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     configured = true;
   }
-  kfn<<<(::gsb::count_launch(), grid), C::THREADS, C::SMEM, st>>>(
+  kfn<<<(::gsb::count_launch(), grid), C::THREADS, SMEM, st>>>(
       tk, tv, tks, tvs, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), bt.data_ptr<int32_t>(),
       (int)bt.stride(0), num_blocks, q_start.data_ptr<int32_t>(), kv_len.data_ptr<int32_t>(),
       work_seq.data_ptr<int32_t>(), work_row0.data_ptr<int32_t>(), Hq, Hkv, scale_log2,
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), wso, wsl, nsplit, T, err);
   GSB_CUDA_CHECK(cudaGetLastError());
+}
+
+// Stages of the fp8 decode kernel with 8-row tiles: 2 (five CTAs per SM) or 3 (four).
+// Measured on B200 (d=128, 8B decode step of 128 rows over 4.5k keys, CUDA-graph
+// replay): 13.7 vs 14.1 ms; the kernel needs warps to hide its conversion and MMA
+// latencies more than it needs a deeper ring. attn_fp8t_stages() switches it at run
+// time for A/B tests.
+static int g_fp8t_stages = 2;
+int64_t gsb_attn_fp8t_stages(int64_t v) {
+  const int64_t old = g_fp8t_stages;
+  if (v == 2 || v == 3) g_fp8t_stages = (int)v;
+  return old;
 }
 
 int64_t gsb_attn_decode_stages(int64_t v) {
@@ -1028,12 +1053,17 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
   // (decode: three CTAs per SM, as the bf16 short-ring layout)
   GSB_CHECK(rows_per_tile != 8 || f8, "attention: 8-row decode tiles read the fp8 cache only");
   if (f8 && rows_per_tile == 8) {
-    if (D == 128)
-      launch_attn_fp8t<128, 3>(grid, st, tk, tv, tks, tvs, q, block_table, (int)k_cache.size(0), q_start, kv_len,
-                               work_seq, work_row0, Hq, Hkv, scale_log2, out, wso, wsl, (int)nsplit, T, ep);
+#define GSB_ATTN8T(DD, ST)                                                                                  \
+  launch_attn_fp8t<DD, ST>(grid, st, tk, tv, tks, tvs, q, block_table, (int)k_cache.size(0), q_start, kv_len,   \
+                           work_seq, work_row0, Hq, Hkv, scale_log2, out, wso, wsl, (int)nsplit, T, ep)
+    if (D == 128 && g_fp8t_stages == 3)
+      GSB_ATTN8T(128, 3);
+    else if (D == 128)
+      GSB_ATTN8T(128, 2);
+    else if (D == 64 && g_fp8t_stages == 3)
+      GSB_ATTN8T(64, 6);
     else if (D == 64)
-      launch_attn_fp8t<64, 6>(grid, st, tk, tv, tks, tvs, q, block_table, (int)k_cache.size(0), q_start, kv_len,
-                              work_seq, work_row0, Hq, Hkv, scale_log2, out, wso, wsl, (int)nsplit, T, ep);
+      GSB_ATTN8T(64, 4);
     else
       GSB_CHECK(false, "attention: head_dim must be 64 or 128, got ", D);
   } else if (f8 && D == 128) {
@@ -1059,6 +1089,7 @@ void gsb_paged_attention(const at::Tensor& q, const at::Tensor& k_cache, const a
   }
 #undef GSB_ATTN
 #undef GSB_ATTN8
+#undef GSB_ATTN8T
   if (nsplit > 1) {
     auto merge = (D == 128) ? launch_merge<128> : launch_merge<64>;
     merge(n_work, Hkv, st, wso, wsl, (int)nsplit, T, Hq, q_start.data_ptr<int32_t>(), work_seq.data_ptr<int32_t>(),

@@ -49,6 +49,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_scatter", &gsb_moe_scatter, "MoE token rows into their experts' segments");
   m.def("gemm_splitk_max_tiles", &gsb_gemm_splitk_max_tiles,
         "single-CTA GEMMs with fewer output tiles split K (0: never; -1 reads)");
+  m.def("attn_fp8t_stages", &gsb_attn_fp8t_stages,
+        "stages of the fp8 decode kernel with 8-row tiles: 3 (four CTAs per SM) or 2 (five); other values read");
   m.def("attn_decode_stages", &gsb_attn_decode_stages, "decode attention layout: 2 = short rings, three CTAs per SM; 3 = deep rings, two (other values read)");
   m.def("attn_packed", &gsb_attn_packed, "prefill attention softmax on packed f32x2 math (0/1; -1 reads)");
   m.def("moe_scatter_slots", &gsb_moe_scatter_slots, "MoE rows into the slots of an earlier scatter");

@@ -85,4 +85,5 @@ void gsb_moe_combine(const at::Tensor& yp, const at::Tensor& slot, const at::Ten
 void gsb_residual_axpy(const at::Tensor& h, const at::Tensor& y, double scale);
 int64_t gsb_attn_packed(int64_t v);
 int64_t gsb_gemm_splitk_max_tiles(int64_t v);
+int64_t gsb_attn_fp8t_stages(int64_t v);
 int64_t gsb_attn_decode_stages(int64_t v);

@@ -132,14 +132,18 @@ def main():
             nbytes = 2 * sum(kv_lens) * hkv * d * per
             print(json.dumps({"case": "decode_split", "cache": cache, "nsplit": ns, "ms": round(ms, 4),
                               "kv_tbs": round(nbytes / ms / 1e9, 2)}), flush=True)
-        # fp8 cache, 8-row tiles with the keys on the MMA's row side
+        # fp8 cache, 8-row tiles with the keys on the MMA's row side (3 stages, four CTAs per
+        # SM, or 2 stages, five)
         ws8, wr8 = A.build_work(q_lens, hq // hkv, 8)
         ws8, wr8 = torch.tensor(ws8, **i32), torch.tensor(wr8, **i32)
-        ms = _time_flushed(lambda: A.paged_attention(q, k8, v8, bt, qs, kvl, ws8, wr8, 8, hq, 0.088, out, ns,
-                                                     wso, wsl, k_scale=ks, v_scale=vs), args.iters, flush)
-        nbytes = 2 * sum(kv_lens) * hkv * d
-        print(json.dumps({"case": "decode_split", "cache": "fp8", "rows": 8, "nsplit": ns, "ms": round(ms, 4),
-                          "kv_tbs": round(nbytes / ms / 1e9, 2)}), flush=True)
+        for st8 in (3, 2):
+            old = _native.native().attn_fp8t_stages(st8)
+            ms = _time_flushed(lambda: A.paged_attention(q, k8, v8, bt, qs, kvl, ws8, wr8, 8, hq, 0.088, out, ns,
+                                                         wso, wsl, k_scale=ks, v_scale=vs), args.iters, flush)
+            _native.native().attn_fp8t_stages(old)
+            nbytes = 2 * sum(kv_lens) * hkv * d
+            print(json.dumps({"case": "decode_split", "cache": "fp8", "rows": 8, "stages": st8, "nsplit": ns,
+                              "ms": round(ms, 4), "kv_tbs": round(nbytes / ms / 1e9, 2)}), flush=True)
     if args.library:
         A.paged_attention(q, kc, vc, bt, qs, kvl, ws, wr, 16, hq, 0.088, out, 1)
         _library_decode(q, kc, vc, bt, kv_lens, hq, d, out, 2 * sum(kv_lens) * hkv * d * 2, args.iters, flush)

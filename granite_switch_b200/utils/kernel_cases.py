@@ -2,7 +2,7 @@
 
 ``python -m granite_switch_b200.utils.kernel_cases <case>`` with case in
 gemm, gemm_pair, gemm_single, cublas, swiglu, attn_prefill64, moe, probe, decode_gemm, decode_shrink, lora_small, fp8_gemm,
-fp8_quant, attn_prefill, attn_decode, attn_decode_fp8, rmsnorm, rope, embed, routing, sample (or ``all``). Pair it with ``ncu --clock-control none -k regex:<kernel> -c 1`` (without
+fp8_quant, attn_prefill, attn_decode, attn_decode_fp8, attn_decode_fp8t, rmsnorm, rope, embed, routing, sample (or ``all``). Pair it with ``ncu --clock-control none -k regex:<kernel> -c 1`` (without
 ``--clock-control none`` ncu locks the GPU clocks).
 """
 import sys
@@ -72,7 +72,7 @@ if want("lora_small"):  # CUDA-core LoRA shrink of qkv at a 64-token decode step
     ids = torch.randint(0, 13, (64,), device=dev, dtype=torch.int32)
     s_out = torch.empty(64, 3 * 12 * 32, device=dev, dtype=torch.bfloat16)
     G.lora_shrink(xs, a_all, ids, 32, 12, out=s_out)
-if want("attn_prefill") or want("attn_decode") or want("attn_decode_fp8"):
+if want("attn_prefill") or want("attn_decode") or want("attn_decode_fp8") or want("attn_decode_fp8t"):
     hq, hkv, d = 32, 8, 128
     def setup(q_lens, kv_lens):
         nblk = sum((l + 15)//16 for l in kv_lens) + 4
@@ -103,6 +103,13 @@ if want("attn_prefill") or want("attn_decode") or want("attn_decode_fp8"):
         ks = torch.full(kc.shape[:3], 0.01, device=dev); vs = torch.full_like(ks, 0.01)
         ws, wr = [torch.tensor(v, dtype=torch.int32, device=dev) for v in A.build_work(q_lens, 4, 16)]
         A.paged_attention(q, k8, v8, bt, qs, kvl, ws, wr, 16, hq, 0.088, out, 1, k_scale=ks, v_scale=vs)
+    if want("attn_decode_fp8t"):  # the same over the fp8 cache with 8-row tiles (keys on the MMA's row side)
+        q_lens = [1] * 128; kv = [4200] * 128; kc, vc, bt, q, out, qs, kvl = setup(q_lens, kv)
+        k8 = torch.randint(0, 126, kc.shape, dtype=torch.uint8, device=dev)
+        v8 = torch.randint(0, 126, (kc.shape[0], hkv, d, 16), dtype=torch.uint8, device=dev)
+        ks = torch.full(kc.shape[:3], 0.01, device=dev); vs = torch.full_like(ks, 0.01)
+        ws, wr = [torch.tensor(v, dtype=torch.int32, device=dev) for v in A.build_work(q_lens, 4, 8)]
+        A.paged_attention(q, k8, v8, bt, qs, kvl, ws, wr, 8, hq, 0.088, out, 1, k_scale=ks, v_scale=vs)
 if want("attn_prefill64"):  # tcgen05 prefill attention, head_dim 64 (3B shape: 32 q / 8 kv heads)
     hq, hkv, d = 32, 8, 64
     q_lens = [2048, 2048]

@@ -104,6 +104,8 @@ def main():
                    help="decode attention layout: 2 = short rings, three CTAs per SM; 3 = deep rings, two")
     p.add_argument("--fp8-decode-rows", type=int, default=8, choices=[8, 16],
                    help="decode tile rows over an fp8 cache: 8 (keys on the MMA's row side) or 16 (row-major)")
+    p.add_argument("--attn-fp8t-stages", type=int, default=None, choices=[2, 3],
+                   help="stages of the fp8 decode kernel with 8-row tiles (3: four CTAs per SM, 2: five)")
     p.add_argument("--no-pdl", dest="pdl", action="store_false",
                    help="launch the GEMMs in plain stream order (not as programmatic dependents)")
     args = p.parse_args()
@@ -147,6 +149,8 @@ def main():
 
     if args.small_shrink_max_m is not None:
         G.SMALL_SHRINK_MAX_M = args.small_shrink_max_m
+    if args.attn_fp8t_stages:
+        _native.native().attn_fp8t_stages(args.attn_fp8t_stages)
     if args.attn_decode_stages:
         _native.native().attn_decode_stages(args.attn_decode_stages)
     if args.decode_split_ctas:
@@ -220,6 +224,7 @@ def main():
                               decode_split_ctas=A.DECODE_SPLIT_CTAS,
                               attn_decode_stages=_native.native().attn_decode_stages(-1),
                               kv_cache_dtype=args.kv_cache_dtype, fp8_decode_rows=args.fp8_decode_rows,
+                              attn_fp8t_stages=_native.native().attn_fp8t_stages(-1),
                               step_ms=round(plain, 3), step_ms_with_regions=round(step_ms, 3),
                               host_enqueue_ms=round(host_ms, 3), ops=table)), flush=True)
     if group is not None:
