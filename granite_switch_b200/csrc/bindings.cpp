@@ -41,7 +41,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("routing", &gsb_routing, "latest-wins routing, token exchange and LoRA tile metadata");
   m.def("sample", &gsb_sample, "temperature / top-k / top-p sampling (Gumbel-max, Philox)");
   m.def("prefill_attention_tc", &gsb_prefill_attention_tc, "tcgen05/TMEM prefill attention (128-row tiles)");
-  m.def("peer_barrier", &gsb_peer_barrier, "bounded cross-rank barrier over P2P signal pads");
+  m.def("peer_barrier", &gsb_peer_barrier,
+        "bounded cross-rank barrier over P2P signal pads; the epoch is an int32 counter on the device it advances");
   m.def("rmsnorm_residual_from", &gsb_rmsnorm_residual_from, "h <- y; x <- rmsnorm(y); y <- 0");
   m.def("probe_verdict", &gsb_probe_verdict, "probe-head scores at marker rows");
   m.def("probe_rewrite", &gsb_probe_rewrite, "replace marker logit rows by the probe verdict");

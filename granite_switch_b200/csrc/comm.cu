@@ -3,7 +3,10 @@
 // * peer_barrier: every rank stores an epoch into its slot of every peer's
 //   signal pad (plain P2P st.release.sys) and waits, with a bounded spin, until
 //   all peers' epochs arrived in its own pad (ld.acquire.sys). A wait that runs
-//   out sets kErrPeerWait and returns; it never hangs.
+//   out sets kErrPeerWait and returns; it never hangs. The epoch is a counter in
+//   this rank's device memory that every barrier advances, so barriers replayed
+//   from a CUDA graph and eager ones stay in one sequence (an epoch passed as a
+//   launch argument would be frozen into the graph at capture).
 // * rmsnorm_residual_from: h <- y (the reduced residual stream), x <- RMSNorm(y),
 //   y <- 0 ready for the next accumulation - one pass over the row.
 // The fused row-parallel GEMM (gemm_tcgen05.cu, kEpiMultimemRed) pushes each
@@ -31,22 +34,26 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 
 // signal pads: uint32 [tp] per rank; slot `src` of rank r's pad holds the last
 // epoch rank `src` announced to r.
-__global__ void peer_barrier_kernel(const uint64_t* __restrict__ pads, int rank, int tp, uint32_t epoch,
+__global__ void peer_barrier_kernel(const uint64_t* __restrict__ pads, int rank, int tp, uint32_t* __restrict__ ctr,
                                     uint64_t budget_ns, uint32_t* err) {
   const int p = threadIdx.x;
-  if (p >= tp) return;
-  __threadfence_system();  // this rank's earlier writes (incl. multimem) before the announce
-  uint32_t* peer_pad = reinterpret_cast<uint32_t*>(pads[p]);
-  st_release_sys(peer_pad + rank, epoch);
-  const uint32_t* mine = reinterpret_cast<const uint32_t*>(pads[rank]) + p;
-  const uint64_t t0 = globaltimer_ns();
-  while ((int32_t)(ld_acquire_sys(mine) - epoch) < 0) {
-    if (globaltimer_ns() - t0 > budget_ns) {
-      raise_error(err, kErrPeerWait);
-      break;
+  const uint32_t epoch = *ctr + 1;  // read by every thread before thread 0 advances it
+  if (p < tp) {
+    __threadfence_system();  // this rank's earlier writes (incl. multimem) before the announce
+    uint32_t* peer_pad = reinterpret_cast<uint32_t*>(pads[p]);
+    st_release_sys(peer_pad + rank, epoch);
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(pads[rank]) + p;
+    const uint64_t t0 = globaltimer_ns();
+    while ((int32_t)(ld_acquire_sys(mine) - epoch) < 0) {
+      if (globaltimer_ns() - t0 > budget_ns) {
+        raise_error(err, kErrPeerWait);
+        break;
+      }
     }
+    __threadfence_system();
   }
-  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) *ctr = epoch;
 }
 
 // h <- y; x <- rmsnorm(y) * w; y <- 0   (rows of H bf16, H % 8 == 0)
@@ -113,13 +120,15 @@ __global__ void rmsnorm_residual_from_kernel(__nv_bfloat16* __restrict__ y, __nv
 
 using namespace gsb;
 
-void gsb_peer_barrier(const at::Tensor& pad_ptrs_dev, int64_t rank, int64_t tp, int64_t epoch, int64_t budget_ns,
-                      const at::Tensor& err) {
+void gsb_peer_barrier(const at::Tensor& pad_ptrs_dev, int64_t rank, int64_t tp, const at::Tensor& epoch_ctr,
+                      int64_t budget_ns, const at::Tensor& err) {
   GSB_CHECK(pad_ptrs_dev.is_cuda() && pad_ptrs_dev.numel() >= tp && tp >= 1 && tp <= 64, "barrier: bad pads");
+  GSB_CHECK(epoch_ctr.is_cuda() && epoch_ctr.scalar_type() == at::kInt && epoch_ctr.numel() >= 1,
+            "barrier: the epoch counter is one int32 on the device");
   c10::cuda::CUDAGuard g(err.device());
   auto st = c10::cuda::getCurrentCUDAStream(err.device().index()).stream();
   peer_barrier_kernel<<<(::gsb::count_launch(), 1), 64, 0, st>>>(reinterpret_cast<const uint64_t*>(pad_ptrs_dev.data_ptr()), (int)rank,
-                                        (int)tp, (uint32_t)epoch, (uint64_t)budget_ns,
+                                        (int)tp, reinterpret_cast<uint32_t*>(epoch_ctr.data_ptr()), (uint64_t)budget_ns,
                                         reinterpret_cast<uint32_t*>(err.data_ptr()));
   GSB_CUDA_CHECK(cudaGetLastError());
 }

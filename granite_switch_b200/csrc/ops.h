@@ -64,7 +64,7 @@ void gsb_prefill_attention_tc(const at::Tensor& q, const at::Tensor& k_cache, co
                               double scale, const at::Tensor& out, const at::Tensor& err, int64_t rows_per_tile,
                               int64_t nsplit, const c10::optional<at::Tensor>& ws_o,
                               const c10::optional<at::Tensor>& ws_lse);
-void gsb_peer_barrier(const at::Tensor& pad_ptrs_dev, int64_t rank, int64_t tp, int64_t epoch, int64_t budget_ns,
+void gsb_peer_barrier(const at::Tensor& pad_ptrs_dev, int64_t rank, int64_t tp, const at::Tensor& epoch_ctr, int64_t budget_ns,
                       const at::Tensor& err);
 void gsb_rmsnorm_residual_from(const at::Tensor& y, const at::Tensor& h, const at::Tensor& w, const at::Tensor& x,
                                double eps);

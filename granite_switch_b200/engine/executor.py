@@ -131,11 +131,14 @@ class _DecodeGraph:
 class NativeExecutor:
     """Stages a scheduler step into persistent device buffers and runs the native model.
 
-    With ``use_cuda_graphs``, decode-only steps (every chunk one token) on one
-    GPU replay a CUDA graph captured per padded batch size (8, 16, ... up to
-    ``max_seqs``): the inputs are staged into the same device buffers, padding
-    rows point at a scratch KV page and are not sampled, and the whole forward
-    (routing, every layer, LM head) is one graph launch. Other steps run eagerly.
+    With ``use_cuda_graphs``, decode-only steps (every chunk one token) replay a
+    CUDA graph captured per padded batch size (8, 16, ... up to ``max_seqs``): the
+    inputs are staged into the same device buffers, padding rows point at a scratch
+    KV page and are not sampled, and the whole forward (routing, every layer, LM
+    head) is one graph launch. Under tensor parallelism a bucket is captured only
+    when every row-parallel reduction rides in the fused GEMM epilogue (the peer
+    barrier counts its epochs on the device); the logits all-gather runs after the
+    replay. Other steps, and pipeline-parallel ones, run eagerly.
     """
 
     def __init__(self, model, max_model_len: int, tp_group=None, tp_size: int = 1, use_cuda_graphs: bool = False,
@@ -172,7 +175,9 @@ class NativeExecutor:
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.gather_buf = None
-        self.use_cuda_graphs = bool(use_cuda_graphs) and tp_size == 1 and model.pipeline is None
+        # under tensor parallelism only steps whose reductions all ride in the fused GEMM
+        # epilogue are captured (no NCCL call inside a graph); see _graph_bucket
+        self.use_cuda_graphs = bool(use_cuda_graphs) and model.pipeline is None
         # pipeline parallelism: a step of two or more sequences runs as two micro-batches
         self.pp_microbatches = bool(pp_microbatches) and model.pipeline is not None
         self.routing_trace = None  # utils.tracing.RoutingTrace: per-step routing records
@@ -216,8 +221,15 @@ class NativeExecutor:
         if not self.use_cuda_graphs or not out.is_decode_only:
             return None
         n = len(out.chunks)
+        m = self.model
         for b in GRAPH_BUCKETS:
-            if n <= b <= self.model.max_seqs and b <= self.model.max_tokens:
+            if n <= b <= m.max_seqs and b <= m.max_tokens:
+                if self.tp_size > 1:
+                    # every row-parallel reduction must be the fused epilogue + device-counted
+                    # peer barrier, never an NCCL all-reduce
+                    comm = getattr(m, "comm", None)
+                    if comm is None or b > comm.red_max_tokens or getattr(m, "dual", False) or m.has_moe:
+                        return None
                 return b
         return None
 

@@ -42,7 +42,7 @@ class EngineConfig:
     enable_chunked_prefill: bool = True
     tensor_parallel_size: int = 1
     pipeline_parallel_size: int = 1
-    use_cuda_graphs: bool = True           # decode-only steps on one GPU replay a captured graph
+    use_cuda_graphs: bool = True           # decode-only steps replay a captured graph (TP: fused reductions only)
     dtype: str = "bfloat16"
     seed: int = 0
     fused_tp_comm: bool = False            # symmetric-memory fused GEMM + reduction kernels

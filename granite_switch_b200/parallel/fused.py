@@ -62,7 +62,9 @@ class FusedTPComm:
         self.pads.zero_()
         self.pad_handle = symm_mem.rendezvous(self.pads, group)
         self.pad_ptrs = torch.tensor(list(self.pad_handle.buffer_ptrs), dtype=torch.int64, device=device)
-        self.epoch = 0
+        # barrier epochs count on the device, so barriers replayed from a CUDA graph
+        # and eager ones advance one sequence
+        self.epoch_ctr = torch.zeros(1, dtype=torch.int32, device=device)
         # rows up to which the reduction rides in the GEMM epilogue (see row_parallel);
         # from the collective sweep: always at TP=2, small steps only at TP=4 / 8
         self.red_max_tokens = red_max_tokens if red_max_tokens is not None else RED_MAX_TOKENS.get(self.world, 256)
@@ -74,8 +76,8 @@ class FusedTPComm:
         return self.mc != 0
 
     def barrier(self, budget_ns: int = BARRIER_BUDGET_NS) -> None:
-        self.epoch += 1
-        native().peer_barrier(self.pad_ptrs, self.rank, self.world, self.epoch, budget_ns, err_buffer(self.device))
+        native().peer_barrier(self.pad_ptrs, self.rank, self.world, self.epoch_ctr, budget_ns,
+                              err_buffer(self.device))
 
     def row_parallel(self, model, pl, x: torch.Tensor, h: torch.Tensor, mult: float) -> torch.Tensor:
         """Reduce ``x @ W_shard^T * mult`` (+ ``h`` once) over the group into ``y``; returns ``y[:m]``.

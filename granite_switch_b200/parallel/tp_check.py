@@ -136,14 +136,18 @@ def _check_primitives(device, group, rank, world) -> dict:
     return out
 
 
-def _engine_tokens(config, device, world, rank, group, async_on: bool, fused: bool, lora) -> list[list[int]]:
+def _engine_tokens(config, device, world, rank, group, async_on: bool, fused: bool, lora,
+                   graphs: bool = False) -> tuple[list[list[int]], int]:
     """Greedy tokens of the serving engine (``LLM``) on this rank's shard: chunked prefill,
     decode rows and, with ``async_on``, pipelined steps whose decode inputs are fed back on
-    the device."""
+    the device; with ``graphs``, decode-only steps replayed from CUDA graphs where the
+    engine captures them (fused reductions). Returns the tokens and the graph replays (-1
+    when the fused reductions could not be attached)."""
     from ..engine import LLM, EngineConfig, SamplingParams
 
-    ecfg = EngineConfig(max_num_seqs=6, max_num_batched_tokens=96, num_kv_blocks=256, max_model_len=512,
-                        tensor_parallel_size=world, fused_tp_comm=fused, async_scheduling=async_on)
+    ecfg = EngineConfig(max_num_seqs=8, max_num_batched_tokens=96, num_kv_blocks=256, max_model_len=512,
+                        tensor_parallel_size=world, fused_tp_comm=fused, async_scheduling=async_on,
+                        use_cuda_graphs=graphs)
     llm = LLM(config, device=str(device), engine_config=ecfg,
               random_init=dict(lora_modules=lora, rank=16, seed=7), tp_rank=rank, tp_group=group)
     assert llm.engine.async_steps == async_on
@@ -156,7 +160,9 @@ def _engine_tokens(config, device, world, rank, group, async_on: bool, fused: bo
         ids.insert(n // 2, config.adapter_token_ids[i % config.num_adapters])
         prompts.append(ids)
     outs = llm.generate(prompts, SamplingParams(max_tokens=10))
-    return [o.output_ids for o in outs]
+    replays = int(getattr(llm.engine.executor, "graph_replays", 0))
+    fused_on = getattr(llm.model, "comm", None) is not None
+    return [o.output_ids for o in outs], (replays if fused_on else -1)
 
 
 def main(argv=None) -> int:
@@ -207,14 +213,19 @@ def main(argv=None) -> int:
                               "rows": total, "device_errors": errs, "ok": good}), flush=True)
     if args.engine:
         for fused in (False, True):
-            sync_t = _engine_tokens(config, device, world, rank, group, False, fused, lora)
+            # blocking, eager steps vs pipelined steps with decode graphs (captured only
+            # when every reduction is fused: with NCCL reductions the second run is eager too)
+            sync_t, _ = _engine_tokens(config, device, world, rank, group, False, fused, lora, graphs=False)
             dist.barrier()
-            async_t = _engine_tokens(config, device, world, rank, group, True, fused, lora)
+            async_t, replays = _engine_tokens(config, device, world, rank, group, True, fused, lora, graphs=True)
             dist.barrier()
             same = sync_t == async_t and all(len(t) == 10 for t in async_t)
+            if fused and replays >= 0:
+                same &= replays > 0  # with the fused reductions on, decode graphs were replayed
             ok &= same
             if rank == 0:
-                print(json.dumps({"mode": "engine_async_vs_sync", "tp": world, "fused": fused, "ok": same}),
+                print(json.dumps({"mode": "engine_async_vs_sync", "tp": world, "fused": fused, "ok": same,
+                                  "graph_replays": replays}),
                       flush=True)
     flag = torch.tensor([1 if ok else 0], device=device)
     dist.broadcast(flag, 0)

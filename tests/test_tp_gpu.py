@@ -25,9 +25,11 @@ def test_peer_barrier_times_out_with_status():
     read_errors(dev)
     pad = torch.zeros(64, dtype=torch.int32, device=dev)
     ptrs = torch.tensor([pad.data_ptr(), pad.data_ptr()], dtype=torch.int64, device=dev)
-    native().peer_barrier(ptrs, 0, 2, 1, 200_000_000, err_buffer(dev))  # 0.2 s budget
+    ctr = torch.zeros(1, dtype=torch.int32, device=dev)  # epoch 1 is announced, never answered
+    native().peer_barrier(ptrs, 0, 2, ctr, 200_000_000, err_buffer(dev))  # 0.2 s budget
     torch.cuda.synchronize()
     assert read_errors(dev) & ERR_PEER_WAIT
+    assert int(ctr.item()) == 1  # the device counter advanced
     # the context stays usable
     x = torch.ones(4, device=dev)
     assert float(x.sum()) == 4.0
