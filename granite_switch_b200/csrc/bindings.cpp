@@ -63,5 +63,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quantize_fp8_rows", &gsb_quantize_fp8_rows,
         "bf16 rows -> e4m3 bytes with one power-of-two scale per (row, 128-K block), as scale atoms");
   m.def("fp8_gemm", &gsb_fp8_gemm, "block-scaled fp8 tcgen05 GEMM with the bf16 switched-LoRA expand fused");
+  m.def("rope_kv_fp8", &gsb_rope_kv_fp8, "RoPE on q / k then the quantised fp8 K / V write, one launch");
   m.def("kv_write_fp8", &gsb_kv_write_fp8, "quantised (e4m3, per-row scale) write of a step's K/V into the fp8 cache");
 }

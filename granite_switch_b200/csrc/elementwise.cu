@@ -7,6 +7,7 @@
 // sampler as called from src/granite_switch/vllm/decoder/lora/decoder.py:136-215
 // and src/granite_switch/vllm/granite_switch_model.py:423-433.)
 #include "common.cuh"
+#include "rope.cuh"
 #include "tma_util.h"
 
 #include <ATen/ATen.h>
@@ -127,40 +128,10 @@ __global__ void rope_kv_kernel(__nv_bfloat16* __restrict__ qkv, int64_t ldq,
   const float* cs = cos_sin + pos * D;
   __nv_bfloat16* row = qkv + (int64_t)t * ldq;
   const int64_t slot = slots ? slots[t] : -1;
-  const int nheads = Hq + Hkv;
-  constexpr int HALF = D / 2;
-  constexpr int CH = HALF / 8;  // 8-element (16-byte) chunks per half
-  // rotate q and k heads: a thread handles 8 pairs (i, i + D/2) with 16-byte loads and stores
-  for (int idx = threadIdx.x; idx < nheads * CH; idx += blockDim.x) {
-    const int h = idx / CH;
-    const int i0 = (idx % CH) * 8;
-    __nv_bfloat16* hp = row + h * D;
-    const uint4 a = *reinterpret_cast<const uint4*>(hp + i0);
-    const uint4 b = *reinterpret_cast<const uint4*>(hp + HALF + i0);
-    const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
-    uint32_t ya[4], yb[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 x1 = unpack_bf16x2(av[j]), x2 = unpack_bf16x2(bv[j]);
-      const float c0 = cs[i0 + 2 * j], c1 = cs[i0 + 2 * j + 1];
-      const float s0 = cs[HALF + i0 + 2 * j], s1 = cs[HALF + i0 + 2 * j + 1];
-      // x*cos + rotate_half(x)*sin; cos/sin equal on both halves
-      const float y10 = x1.x * c0 - x2.x * s0, y11 = x1.y * c1 - x2.y * s1;
-      const float y20 = x2.x * c0 + x1.x * s0, y21 = x2.y * c1 + x1.y * s1;
-      ya[j] = pack_bf16x2(y10, y11);
-      yb[j] = pack_bf16x2(y20, y21);
-    }
-    const uint4 oa = make_uint4(ya[0], ya[1], ya[2], ya[3]), ob = make_uint4(yb[0], yb[1], yb[2], yb[3]);
-    *reinterpret_cast<uint4*>(hp + i0) = oa;
-    *reinterpret_cast<uint4*>(hp + HALF + i0) = ob;
-    if (h >= Hq && slot >= 0 && slot < num_slots) {
-      const int kh = h - Hq;
-      const int64_t blk = slot / BS, off = slot % BS;
-      __nv_bfloat16* kc = k_cache + ((blk * Hkv + kh) * BS + off) * D;
-      *reinterpret_cast<uint4*>(kc + i0) = oa;
-      *reinterpret_cast<uint4*>(kc + HALF + i0) = ob;
-    }
-  }
+  // rotate q and k heads; with a valid slot the rotated k heads also go to the cache
+  __nv_bfloat16* kc = nullptr;
+  if (slot >= 0 && slot < num_slots) kc = k_cache + ((slot / BS) * Hkv * BS + slot % BS) * D;
+  rope_rotate_row<D>(row, cs, Hq, Hkv, kc, (int64_t)BS * D);
   if (slot >= 0 && slot < num_slots) {
     const __nv_bfloat16* vrow = row + (Hq + Hkv) * D;
     const int64_t blk = slot / BS, off = slot % BS;

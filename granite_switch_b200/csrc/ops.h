@@ -28,6 +28,10 @@ void gsb_fp8_gemm(const at::Tensor& x8, const at::Tensor& sfa, const at::Tensor&
                   const c10::optional<at::Tensor>& s, const c10::optional<at::Tensor>& lb,
                   const c10::optional<at::Tensor>& tile_mask, int64_t rank, int64_t num_adapters,
                   std::vector<int64_t> slice_bounds, const at::Tensor& err);
+void gsb_rope_kv_fp8(const at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& cos_sin,
+                     const at::Tensor& slots, const at::Tensor& k8, const at::Tensor& v8, const at::Tensor& k_scale,
+                     const at::Tensor& v_scale, int64_t num_q_heads, int64_t num_kv_heads, int64_t head_dim,
+                     const at::Tensor& err);
 void gsb_kv_write_fp8(const at::Tensor& qkv, const at::Tensor& slots, const at::Tensor& k8, const at::Tensor& v8,
                       const at::Tensor& k_scale, const at::Tensor& v_scale, int64_t num_q_heads,
                       int64_t num_kv_heads, int64_t head_dim, const at::Tensor& err);

@@ -421,8 +421,8 @@ class NativeGraniteSwitch:
         """RoPE on q / k and the write of the step's K / V into layer ``li``'s cache."""
         kc, vc, ks, vs = self._layer_cache(li)
         if self.kv_fp8:
-            E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim)
-            A.kv_write_fp8(qkv, b.slots, kc, vc, ks, vs, self.num_q, self.num_kv, self.head_dim)
+            A.rope_kv_fp8(qkv, b.positions, self.cos_sin, b.slots, kc, vc, ks, vs, self.num_q, self.num_kv,
+                          self.head_dim)
         else:
             E.rope_kv(qkv, b.positions, self.cos_sin, self.num_q, self.num_kv, self.head_dim, kc, vc, b.slots)
 

@@ -133,6 +133,15 @@ def kv_write_fp8(qkv, slots, k8, v8, k_scale, v_scale, num_q_heads: int, num_kv_
                           err_buffer(qkv.device))
 
 
+def rope_kv_fp8(qkv, positions, cos_sin, slots, k8, v8, k_scale, v_scale, num_q_heads: int, num_kv_heads: int,
+                head_dim: int):
+    """RoPE on the step's q / k heads of ``qkv`` (in place), then the quantised write of its K / V
+    rows into the fp8 cache, in one launch: the result of ``elementwise.rope_kv`` (without a
+    cache) followed by :func:`kv_write_fp8`."""
+    native().rope_kv_fp8(qkv, positions, cos_sin, slots, k8, v8, k_scale, v_scale, num_q_heads, num_kv_heads,
+                         head_dim, err_buffer(qkv.device))
+
+
 def dequantize_fp8_cache(k8, v8, k_scale, v_scale):
     """fp32 ``[blocks, Hkv, 16, D]`` K and V from the fp8 cache (test oracle, reads the stored order)."""
     perm = torch.tensor(_perm16(), device=k8.device)

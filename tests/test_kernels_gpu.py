@@ -344,6 +344,39 @@ def test_kv_write_fp8_roundtrip(d):
 
 
 @pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("hq,hkv", [(8, 2), (32, 8), (4, 1)])
+def test_rope_kv_fp8_fused_matches_separate(d, hq, hkv):
+    """The fused RoPE + fp8 K/V write leaves qkv, the fp8 pages and the scales bit for bit as
+    RoPE followed by the separate quantised write does."""
+    from granite_switch_b200.ops import attention as A
+    from granite_switch_b200.ops import elementwise as E
+
+    t, nb, max_pos = 37, 12, 512
+    gen = torch.Generator(device="cuda").manual_seed(d + hq)
+    qkv = (torch.randn(t, (hq + 2 * hkv) * d, device="cuda", generator=gen) * 3).bfloat16()
+    pos = torch.randint(0, max_pos, (t,), device="cuda", generator=gen)
+    cos_sin = E.rope_cos_sin_table(max_pos, d, 10000.0, "cuda")
+    slots = torch.randperm(nb * 16, device="cuda", generator=gen)[:t]
+    outs = []
+    for fused in (False, True):
+        q = qkv.clone()
+        k8 = torch.zeros(nb, hkv, 16, d, dtype=torch.uint8, device="cuda")
+        v8 = torch.zeros(nb, hkv, d, 16, dtype=torch.uint8, device="cuda")
+        ks = torch.zeros(nb, hkv, 16, device="cuda")
+        vs = torch.zeros(nb, hkv, 16, device="cuda")
+        if fused:
+            A.rope_kv_fp8(q, pos, cos_sin, slots, k8, v8, ks, vs, hq, hkv, d)
+        else:
+            E.rope_kv(q, pos, cos_sin, hq, hkv, d)
+            A.kv_write_fp8(q, slots, k8, v8, ks, vs, hq, hkv, d)
+        outs.append((q, k8, v8, ks, vs))
+    torch.cuda.synchronize()
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+    _check()
+
+
+@pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("mode", ["decode", "decode8", "prefill", "prefill128", "short_after_long"])
 @pytest.mark.parametrize("nsplit", [1, 3])
 @pytest.mark.parametrize("hq", [8, 4])
