@@ -263,6 +263,12 @@ def test_short_chunks_over_long_prefix_split_kv():
     assert plans[1][2] == 256 and plans[1][3] == 1
     m.ws_tokens = 128  # the split workspace cannot hold the step: no split
     assert NativeGraniteSwitch.attention_plans(m, q, kv)[1][2:] == (128, 1)
+    # fp8 cache: decode rows in 8-row tiles (keys on the MMA's row side), prefill chunks on
+    # the 64-row mma.sync layout with its own key split
+    m.ws_tokens, m.kv_fp8 = 512, True
+    plans = NativeGraniteSwitch.attention_plans(m, q, kv)
+    assert [(p[2], p[3]) for p in plans] == [(8, 2), (64, 4)]
+    assert len(plans[0][0]) == 126  # one 8-row tile per decode request (4 query heads each)
 
 
 def test_pick_bn_policy():
@@ -475,3 +481,30 @@ def test_async_launch_failure_loses_no_step(tiny_dir):
             failures += 1
     assert failures == 1
     assert [r.output_ids for r in reqs] == _ref_generate(tiny_dir, prompts, 6)
+
+
+def test_graph_bucket_gating_under_tp():
+    """Decode-only steps take the smallest padded bucket; under tensor parallelism only
+    buckets whose reductions all ride in the fused epilogue (no NCCL inside a graph)."""
+    import types
+
+    from granite_switch_b200.engine.executor import NativeExecutor
+
+    def ex(tp, comm, max_seqs=256, dual=False, moe=False):
+        e = NativeExecutor.__new__(NativeExecutor)
+        e.use_cuda_graphs, e.tp_size = True, tp
+        e.model = types.SimpleNamespace(max_seqs=max_seqs, max_tokens=8192, comm=comm, dual=dual, has_moe=moe)
+        return e
+
+    def step(n, decode_only=True):
+        return types.SimpleNamespace(is_decode_only=decode_only, chunks=[None] * n)
+
+    fused = types.SimpleNamespace(red_max_tokens=256)
+    assert ex(1, None)._graph_bucket(step(100)) == 128
+    assert ex(1, None)._graph_bucket(step(100, decode_only=False)) is None
+    assert ex(1, None, max_seqs=64)._graph_bucket(step(100)) is None  # beyond the largest bucket that fits
+    assert ex(2, None)._graph_bucket(step(100)) is None                # NCCL reductions: eager
+    assert ex(8, fused)._graph_bucket(step(100)) == 128                # fused up to 256 rows
+    assert ex(8, fused)._graph_bucket(step(300)) is None               # bucket 512 would all-reduce over NCCL
+    assert ex(8, fused, dual=True)._graph_bucket(step(10)) is None     # Shadow-Residual reduces over NCCL
+    assert ex(8, fused, moe=True)._graph_bucket(step(10)) is None      # so do expert banks
